@@ -1,0 +1,222 @@
+"""ctypes binding of the deltaphase_b200 C ABI (include/deltaphase_b200.h).
+
+torch is used only for device memory, the current stream and dtype bookkeeping; every
+computation on the hot path runs in the CUDA library.  There is no CPU fallback: if
+the library is missing or a tensor is not on a CUDA device, these functions raise.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+import torch
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "lib", "libdeltaphase_b200.so")
+
+DP_F32, DP_BF16, DP_F16 = 0, 1, 2
+_DTYPE_CODES = {torch.float32: DP_F32, torch.bfloat16: DP_BF16, torch.float16: DP_F16}
+
+_P = ctypes.c_void_p
+_I = ctypes.c_int
+_I64P = ctypes.POINTER(ctypes.c_int64)
+_SIG = {
+    "dp_version": (ctypes.c_char_p, []),
+    "dp_last_error": (ctypes.c_char_p, []),
+    "dp_status_string": (ctypes.c_char_p, [_I]),
+    "dp_core_fwd": (_I, [_P, _P, _P, _P, _I, _I, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I64P, _P]),
+    "dp_core_decode": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _P, _I, _I, _I, _I, _I64P, _P]),
+    "dp_gram": (_I, [_P, _P, _I, _I, _P, _I, _I, _I, _P]),
+    "dp_laplace_fwd": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _P, _P, _P, _I, _I, _I, _I, _I,
+                            _I, _I64P, _P]),
+    "dp_ffn_fold": (_I, [_P, _P, _P, _P, _P, _I, _I, _P]),
+    "dp_ffn_workspace_size": (ctypes.c_size_t, [_I, _I, _I]),
+    "dp_ffn_fwd": (_I, [_P, _I, _P, _P, _P, _I, _I, _P, ctypes.c_size_t, _P]),
+}
+
+_lib = None
+_lock = threading.Lock()
+
+
+class DeltaPhaseCudaError(RuntimeError):
+    """A deltaphase_b200 entry point returned a non-zero status."""
+
+    def __init__(self, fn, status, msg):
+        super().__init__(f"{fn} failed with status {status}: {msg}")
+        self.status = status
+
+
+def lib():
+    """Load the CUDA library (raises if it has not been built)."""
+    global _lib
+    if _lib is None:
+        with _lock:
+            if _lib is None:
+                if not os.path.exists(LIB_PATH):
+                    raise RuntimeError(
+                        f"deltaphase_b200 CUDA library not found at {LIB_PATH}; build it with "
+                        "`python -m delta_phase_b200.build` (nvcc, sm_100a)")
+                L = ctypes.CDLL(LIB_PATH)
+                for name, (res, args) in _SIG.items():
+                    f = getattr(L, name)
+                    f.restype = res
+                    f.argtypes = args
+                _lib = L
+    return _lib
+
+
+def exported_symbols():
+    return list(_SIG)
+
+
+def version():
+    return lib().dp_version().decode()
+
+
+def library_available():
+    try:
+        lib()
+        return True
+    except (RuntimeError, OSError):
+        return False
+
+
+def _check(fn, status):
+    if status != 0:
+        L = lib()
+        msg = L.dp_last_error().decode()
+        if status == 1:
+            raise ValueError(f"{fn}: {msg}")
+        raise DeltaPhaseCudaError(fn, status, msg)
+
+
+def dtype_code(t: torch.Tensor) -> int:
+    try:
+        return _DTYPE_CODES[t.dtype]
+    except KeyError:
+        raise TypeError(f"unsupported dtype {t.dtype} (the CUDA path takes float32, bfloat16 "
+                        "or float16; float64 is not supported)") from None
+
+
+def require_cuda(*tensors):
+    dev = None
+    for t in tensors:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise RuntimeError("deltaphase_b200 kernels require CUDA tensors")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise RuntimeError("all tensors must be on the same CUDA device")
+    return dev
+
+
+def ptr(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def stream_of(device):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def strides_array(values):
+    arr = (ctypes.c_int64 * len(values))(*[int(x) for x in values])
+    return arr
+
+
+def seq_strides(t: torch.Tensor):
+    """(sb, sh, st) of a (B, H, L, C) view with unit channel stride."""
+    if t.dim() != 4:
+        raise ValueError("expected a 4-D (B, H, L, C) tensor")
+    if t.shape[-1] > 1 and t.stride(-1) != 1:
+        raise ValueError("the channel dimension must have unit stride")
+    return t.stride(0), t.stride(1), t.stride(2)
+
+
+def core_fwd(theta_k, theta_q, v, beta, chunk_size, state_in, out, state_out):
+    """dp_core_fwd on (B,H,L,D) views.  state_in/state_out are float32 views of the
+    interleaved complex64 state (B,H,Dv,D,2), contiguous."""
+    dev = require_cuda(theta_k, theta_q, v, beta, state_in, out, state_out)
+    B, H, L, D = theta_k.shape
+    Dv = v.shape[-1]
+    st = []
+    for t in (theta_k, theta_q, v):
+        st += seq_strides(t)
+    st += (beta.stride(0), beta.stride(1), beta.stride(2))
+    st += seq_strides(out)
+    arr = strides_array(st)
+    with torch.cuda.device(dev):
+        rc = lib().dp_core_fwd(ptr(theta_k), ptr(theta_q), ptr(v), ptr(beta), dtype_code(theta_k),
+                               dtype_code(beta), ptr(state_in), ptr(out), ptr(state_out), B, H, L, D,
+                               Dv, int(chunk_size), arr, stream_of(dev))
+    _check("dp_core_fwd", rc)
+
+
+def core_decode(state_in, state_out, theta_k, theta_q, v, beta, out):
+    """dp_core_decode; theta_k/theta_q (B,H,D), v (B,H,Dv), beta (B,H), out (B,H,Dv)."""
+    dev = require_cuda(state_in, state_out, theta_k, theta_q, v, beta, out)
+    B, H, D = theta_k.shape
+    Dv = v.shape[-1]
+    for t in (theta_k, theta_q, v, out):
+        if t.shape[-1] > 1 and t.stride(-1) != 1:
+            raise ValueError("the channel dimension must have unit stride")
+    st = []
+    for t in (theta_k, theta_q, v, beta, out):
+        st += (t.stride(0), t.stride(1))
+    with torch.cuda.device(dev):
+        rc = lib().dp_core_decode(ptr(state_in), ptr(state_out), ptr(theta_k), ptr(theta_q), ptr(v),
+                                  ptr(beta), dtype_code(theta_k), dtype_code(beta), ptr(out), B, H, D,
+                                  Dv, strides_array(st), stream_of(dev))
+    _check("dp_core_decode", rc)
+
+
+def gram(theta, beta, out):
+    dev = require_cuda(theta, beta, out)
+    N, C, D = theta.shape
+    with torch.cuda.device(dev):
+        rc = lib().dp_gram(ptr(theta), ptr(beta), dtype_code(theta), dtype_code(beta), ptr(out), N, C,
+                           D, stream_of(dev))
+    _check("dp_gram", rc)
+
+
+def laplace_fwd(theta_k, logmag_k, theta_q, logmag_q, v, log_decay, beta, chunk_size, state_in,
+                out, state_out):
+    dev = require_cuda(theta_k, logmag_k, theta_q, logmag_q, v, log_decay, beta, state_in, out,
+                       state_out)
+    B, H, L, D = theta_k.shape
+    Dv = v.shape[-1]
+    st = []
+    for t in (theta_k, logmag_k, theta_q, logmag_q, v, log_decay):
+        st += (0, 0, 0) if t is None else seq_strides(t)
+    st += (beta.stride(0), beta.stride(1), beta.stride(2))
+    st += seq_strides(out)
+    with torch.cuda.device(dev):
+        rc = lib().dp_laplace_fwd(ptr(theta_k), ptr(logmag_k), ptr(theta_q), ptr(logmag_q), ptr(v),
+                                  ptr(log_decay), ptr(beta), dtype_code(theta_k), dtype_code(beta),
+                                  ptr(state_in), ptr(out), ptr(state_out), B, H, L, D, Dv,
+                                  int(chunk_size), strides_array(st), stream_of(dev))
+    _check("dp_laplace_fwd", rc)
+
+
+def ffn_fold(logits, mats, banks, combine, F, d, nb):
+    dev = require_cuda(logits, mats, banks, combine, F)
+    with torch.cuda.device(dev):
+        rc = lib().dp_ffn_fold(ptr(logits), ptr(mats), ptr(banks), ptr(combine), ptr(F), d, nb,
+                               stream_of(dev))
+    _check("dp_ffn_fold", rc)
+
+
+def ffn_workspace_size(tokens, d, dtype):
+    return int(lib().dp_ffn_workspace_size(tokens, d, _DTYPE_CODES[dtype]))
+
+
+def ffn_fwd(x, dct, F, y, workspace):
+    dev = require_cuda(x, dct, F, y, workspace)
+    tokens, d = x.shape
+    with torch.cuda.device(dev):
+        rc = lib().dp_ffn_fwd(ptr(x), dtype_code(x), ptr(dct), ptr(F), ptr(y), tokens, d,
+                              ptr(workspace), workspace.numel() * workspace.element_size(),
+                              stream_of(dev))
+    _check("dp_ffn_fwd", rc)

@@ -1,0 +1,29 @@
+// dp_core_fwd: argument checks and kernel selection for the chunkwise core.
+#include "dp_common.cuh"
+
+namespace dp {
+int core_fwd_simt(const void *tk, const void *tq, const void *v, const void *beta, int in_dt,
+                  int beta_dt, const float *state_in, float *out, float *state_out, int B, int H,
+                  int L, int D, int Dv, const SeqStrides *s, cudaStream_t stream);
+}  // namespace dp
+
+extern "C" int dp_core_fwd(const void *theta_k, const void *theta_q, const void *v,
+                           const void *beta, int in_dtype, int beta_dtype, const float *state_in,
+                           float *out, float *state_out, int B, int H, int L, int D, int Dv,
+                           int chunk_size, const int64_t *strides, void *stream) {
+  using namespace dp;
+  DP_REQUIRE(B >= 0 && H >= 0 && L >= 0, DP_ERR_INVALID_ARGUMENT, "dp_core_fwd: negative size");
+  DP_REQUIRE(chunk_size >= 1, DP_ERR_INVALID_ARGUMENT, "dp_core_fwd: chunk_size must be >= 1");
+  DP_REQUIRE(D >= 1 && Dv >= 1, DP_ERR_INVALID_ARGUMENT, "dp_core_fwd: D and Dv must be >= 1");
+  DP_REQUIRE(D <= 128 && Dv <= 128, DP_ERR_UNSUPPORTED, "dp_core_fwd: D and Dv must be <= 128");
+  DP_REQUIRE(valid_dtype(in_dtype) && valid_dtype(beta_dtype), DP_ERR_INVALID_ARGUMENT,
+             "dp_core_fwd: bad dtype code");
+  if (B == 0 || H == 0) return DP_OK;
+  DP_REQUIRE(state_out && strides, DP_ERR_INVALID_ARGUMENT, "dp_core_fwd: null state_out/strides");
+  DP_REQUIRE(L == 0 || (theta_k && theta_q && v && beta && out), DP_ERR_INVALID_ARGUMENT,
+             "dp_core_fwd: null input pointer");
+  SeqStrides s[5];
+  for (int i = 0; i < 5; ++i) s[i] = SeqStrides{strides[3 * i], strides[3 * i + 1], strides[3 * i + 2]};
+  return core_fwd_simt(theta_k, theta_q, v, beta, in_dtype, beta_dtype, state_in, out, state_out,
+                       B, H, L, D, Dv, s, as_stream(stream));
+}

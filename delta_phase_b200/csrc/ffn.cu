@@ -1,0 +1,223 @@
+// Spectral Lerp FFN: parameter fold and forward.
+//
+// Reference: LearnableSubstrateLerpFFN.forward (delta_phase/layers.py:119-141) and the
+// bases of delta_phase/spectral.py:4-35, mcarbonell/delta-phase v1.3.0.
+//
+// Per branch b (FWHT, DCT-II, Haar) the reference computes h = M_b x, the multi-bank
+// activation a[k, i] = cos(h_i + phi1[k, i]) w1[k, i] + sin(h_i + phi2[k, i]) w2[k, i],
+// c = W_c a (shared combine) and M_b^T c, then mixes the branches with softmax router
+// weights.  By angle addition a[k, i] = alpha[k, i] cos h_i + gamma[k, i] sin h_i with
+//   alpha = w1 cos phi1 + w2 sin phi2,   gamma = w2 cos phi2 - w1 sin phi1,
+// so the whole FFN is linear in z = [cos h_b, sin h_b]_b (6d values per token):
+//   y = z F,  F[(2b+s) d + i, j] = w_b sum_m (sum_k coef_{b,s}[k, i] W_c[m, k d + i]) M_b[m, j].
+// dp_ffn_fold builds F once per parameter update (float64 accumulation); the forward
+// then needs 6d sincos and one (tokens x 6d) x (6d x d) GEMM per call -- half the
+// multiply-adds of the reference's three (tokens x nb d) x (nb d x d) combines at nb = 4,
+// and none of its six dense d x d transform GEMMs except the DCT.
+#include <cublas_v2.h>
+
+#include <array>
+
+#include "dp_common.cuh"
+
+namespace dp {
+namespace {
+
+// ---------------------------------------------------------------- fold
+constexpr int kFoldTile = 32;
+
+// grid (d/32, d/32, 6): z = 2*branch + s.  One thread per output, float64 accumulation.
+__global__ void __launch_bounds__(kFoldTile * 8)
+ffn_fold_kernel(const float *__restrict__ logits, const float *__restrict__ mats,
+                const float *__restrict__ banks, const float *__restrict__ combine,
+                float *__restrict__ F, int d, int nb) {
+  __shared__ double At[kFoldTile][kFoldTile + 1];  // Wt[m][i] tile (m along rows)
+  __shared__ double Bt[kFoldTile][kFoldTile + 1];  // M_b[m][j] tile
+  const int br = blockIdx.z >> 1, sc = blockIdx.z & 1;
+  const int i0 = blockIdx.y * kFoldTile, j0 = blockIdx.x * kFoldTile;
+  const int tx = threadIdx.x % kFoldTile, ty = threadIdx.x / kFoldTile;  // ty in [0, 8)
+  // router weight w_b = softmax(logits)_b
+  double lmax = fmax(fmax((double)logits[0], (double)logits[1]), (double)logits[2]);
+  double den = exp(logits[0] - lmax) + exp(logits[1] - lmax) + exp(logits[2] - lmax);
+  const double wb = exp(logits[br] - lmax) / den;
+  const float *Mb = mats + (size_t)br * d * d;
+  const float *phi1 = banks + ((size_t)br * 4 + 0) * nb * d;
+  const float *phi2 = banks + ((size_t)br * 4 + 1) * nb * d;
+  const float *w1 = banks + ((size_t)br * 4 + 2) * nb * d;
+  const float *w2 = banks + ((size_t)br * 4 + 3) * nb * d;
+  double acc[4] = {0, 0, 0, 0};
+  for (int m0 = 0; m0 < d; m0 += kFoldTile) {
+    for (int r = ty; r < kFoldTile; r += 8) {
+      const int m = m0 + r, i = i0 + tx;
+      double wt = 0.0, mv = 0.0;
+      if (m < d && i < d)
+      for (int k = 0; k < nb; ++k) {
+        const size_t ki = (size_t)k * d + i;
+        const double p1 = phi1[ki], p2 = phi2[ki], a1 = w1[ki], a2 = w2[ki];
+        const double coef = sc == 0 ? a1 * cos(p1) + a2 * sin(p2) : a2 * cos(p2) - a1 * sin(p1);
+        wt += coef * (double)combine[(size_t)m * nb * d + ki];
+      }
+      if (m < d && j0 + tx < d) mv = (double)Mb[(size_t)m * d + j0 + tx];
+      At[r][tx] = wt;
+      Bt[r][tx] = mv;
+    }
+    __syncthreads();
+#pragma unroll 8
+    for (int mm = 0; mm < kFoldTile; ++mm) {
+      const double bj = Bt[mm][tx];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) acc[q] += At[mm][ty + 8 * q] * bj;
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const int i = i0 + ty + 8 * q, j = j0 + tx;
+    if (i < d && j < d) F[((size_t)blockIdx.z * d + i) * d + j] = (float)(wb * acc[q]);
+  }
+}
+
+// ---------------------------------------------------------------- transforms
+// One CTA per token row; four d-float shared buffers; writes the 6d-value row of z.
+template <typename T>
+__global__ void __launch_bounds__(256)
+ffn_features_kernel(const T *__restrict__ x, const float *__restrict__ hdct, T *__restrict__ z, int d,
+                    int log2d) {
+  extern __shared__ float sm[];
+  float *a = sm;       // FWHT work vector
+  float *hb = a + d;   // Haar work vector
+  float *ho = hb + d;  // Haar output
+  float *tmp = ho + d; // Haar ping-pong buffer
+  const int tid = threadIdx.x, nt = blockDim.x;
+  const int64_t row = blockIdx.x;
+  const T *xr = x + row * d;
+  for (int i = tid; i < d; i += nt) {
+    const float xv = to_f32(xr[i]);
+    a[i] = xv;
+    hb[i] = xv;
+  }
+  __syncthreads();
+  // Sylvester FWHT in natural order: (H x)[i] = sum_j (-1)^{popcount(i & j)} x[j]
+  for (int len = 1; len < d; len <<= 1) {
+    for (int p = tid; p < d / 2; p += nt) {
+      const int i = (p / len) * 2 * len + (p % len);
+      const float u = a[i], w = a[i + len];
+      a[i] = u + w;
+      a[i + len] = u - w;
+    }
+    __syncthreads();
+  }
+  // the reference's recursive Haar: high[i] = (x[2i] - x[2i+1]) / sqrt2 on the
+  // current level, low = (x[:n/2] + x[n/2:]) / sqrt2 recursed (spectral.py:25-35)
+  const float r2 = 0.70710678118654752f;
+  float *src = hb, *dst = tmp;
+  for (int n = d; n > 1; n >>= 1) {
+    const int half = n >> 1;
+    for (int i = tid; i < half; i += nt) {
+      ho[half + i] = (src[2 * i] - src[2 * i + 1]) * r2;
+      dst[i] = (src[i] + src[i + half]) * r2;
+    }
+    __syncthreads();
+    float *t = src;
+    src = dst;
+    dst = t;
+  }
+  if (tid == 0) ho[0] = src[0];
+  __syncthreads();
+  const float inv_sqrt_d = rsqrtf((float)d);
+  T *zr = z + row * 6 * d;
+  const float *hd = hdct + row * d;
+  for (int i = tid; i < d; i += nt) {
+    float s, c;
+    sincosf(a[i] * inv_sqrt_d, &s, &c);
+    zr[i] = from_f32<T>(c);
+    zr[d + i] = from_f32<T>(s);
+    sincosf(hd[i], &s, &c);
+    zr[2 * d + i] = from_f32<T>(c);
+    zr[3 * d + i] = from_f32<T>(s);
+    sincosf(ho[i], &s, &c);
+    zr[4 * d + i] = from_f32<T>(c);
+    zr[5 * d + i] = from_f32<T>(s);
+  }
+}
+
+// ---------------------------------------------------------------- cuBLAS handles
+cublasHandle_t handle_for_device(int dev) {
+  static thread_local std::array<cublasHandle_t, 64> handles{};
+  if (dev < 0 || dev >= 64) return nullptr;
+  if (!handles[dev]) {
+    if (cublasCreate(&handles[dev]) != CUBLAS_STATUS_SUCCESS) handles[dev] = nullptr;
+  }
+  return handles[dev];
+}
+
+}  // namespace
+}  // namespace dp
+
+extern "C" int dp_ffn_fold(const float *logits, const float *mats, const float *banks,
+                           const float *combine, float *F, int d, int nb, void *stream) {
+  using namespace dp;
+  DP_REQUIRE(logits && mats && banks && combine && F, DP_ERR_INVALID_ARGUMENT, "dp_ffn_fold: null pointer");
+  DP_REQUIRE(d >= 1 && nb >= 1, DP_ERR_INVALID_ARGUMENT, "dp_ffn_fold: bad sizes");
+  const int nt = (d + kFoldTile - 1) / kFoldTile;
+  dim3 grid(nt, nt, 6);
+  ffn_fold_kernel<<<grid, kFoldTile * 8, 0, as_stream(stream)>>>(logits, mats, banks, combine, F, d, nb);
+  return check_launch("ffn_fold_kernel");
+}
+
+extern "C" size_t dp_ffn_workspace_size(int tokens, int d, int x_dtype) {
+  if (tokens <= 0 || d <= 0) return 0;
+  const size_t es = dp::dtype_size(x_dtype);
+  return (size_t)tokens * d * sizeof(float) + (size_t)tokens * 6 * d * es + 256;
+}
+
+extern "C" int dp_ffn_fwd(const void *x, int x_dtype, const void *dct, const void *F, void *y,
+                          int tokens, int d, void *workspace, size_t workspace_bytes, void *stream) {
+  using namespace dp;
+  DP_REQUIRE(tokens >= 0 && d >= 1, DP_ERR_INVALID_ARGUMENT, "dp_ffn_fwd: bad sizes");
+  DP_REQUIRE(x_dtype == DP_F32 || x_dtype == DP_BF16, DP_ERR_INVALID_ARGUMENT,
+             "dp_ffn_fwd: x dtype must be float32 or bfloat16");
+  DP_REQUIRE((d & (d - 1)) == 0 && d >= 8 && d <= 4096, DP_ERR_UNSUPPORTED,
+             "dp_ffn_fwd: d must be a power of two in [8, 4096]");
+  if (tokens == 0) return DP_OK;
+  DP_REQUIRE(x && dct && F && y && workspace, DP_ERR_INVALID_ARGUMENT, "dp_ffn_fwd: null pointer");
+  DP_REQUIRE(workspace_bytes >= dp_ffn_workspace_size(tokens, d, x_dtype), DP_ERR_WORKSPACE,
+             "dp_ffn_fwd: workspace too small");
+  DP_REQUIRE(reinterpret_cast<uintptr_t>(workspace) % 256 == 0, DP_ERR_MISALIGNED,
+             "dp_ffn_fwd: workspace must be 256-byte aligned");
+  cudaStream_t st = as_stream(stream);
+  int dev = 0;
+  cudaGetDevice(&dev);
+  cublasHandle_t hdl = handle_for_device(dev);
+  DP_REQUIRE(hdl != nullptr, DP_ERR_CUDA, "dp_ffn_fwd: cublasCreate failed");
+  cublasSetStream(hdl, st);
+  float *hdct = static_cast<float *>(workspace);
+  void *z = static_cast<char *>(workspace) + (size_t)tokens * d * sizeof(float);
+  const bool bf = x_dtype == DP_BF16;
+  const cudaDataType_t ab = bf ? CUDA_R_16BF : CUDA_R_32F;
+  const cublasComputeType_t ct = bf ? CUBLAS_COMPUTE_32F : CUBLAS_COMPUTE_32F_FAST_TF32;
+  const float one = 1.f, zero = 0.f;
+  // Hdct (tokens x d, row-major) = X Cdct^T  <=>  col-major Hdct^T (d x tokens) = Cdct^T(d x d) X^T
+  cublasStatus_t cs = cublasGemmEx(hdl, CUBLAS_OP_T, CUBLAS_OP_N, d, tokens, d, &one, dct, ab, d, x,
+                                   ab, d, &zero, hdct, CUDA_R_32F, d, ct, CUBLAS_GEMM_DEFAULT);
+  DP_REQUIRE(cs == CUBLAS_STATUS_SUCCESS, DP_ERR_CUDA, "dp_ffn_fwd: DCT GEMM failed");
+  int log2d = 0;
+  while ((1 << log2d) < d) ++log2d;
+  const size_t smem = 4 * (size_t)d * sizeof(float);
+  const int threads = d >= 256 ? 256 : d;
+  cudaFuncSetAttribute(ffn_features_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaFuncSetAttribute(ffn_features_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (bf)
+    ffn_features_kernel<__nv_bfloat16><<<tokens, threads, smem, st>>>(
+        static_cast<const __nv_bfloat16 *>(x), hdct, static_cast<__nv_bfloat16 *>(z), d, log2d);
+  else
+    ffn_features_kernel<float><<<tokens, threads, smem, st>>>(static_cast<const float *>(x), hdct,
+                                                               static_cast<float *>(z), d, log2d);
+  int rc = check_launch("ffn_features_kernel");
+  if (rc != DP_OK) return rc;
+  // Y (tokens x d) = Z (tokens x 6d) F (6d x d)  <=>  Y^T = F^T Z^T in column-major
+  cs = cublasGemmEx(hdl, CUBLAS_OP_N, CUBLAS_OP_N, d, tokens, 6 * d, &one, F, ab, d, z, ab, 6 * d,
+                    &zero, y, ab, d, ct, CUBLAS_GEMM_DEFAULT);
+  DP_REQUIRE(cs == CUBLAS_STATUS_SUCCESS, DP_ERR_CUDA, "dp_ffn_fwd: combine GEMM failed");
+  return DP_OK;
+}

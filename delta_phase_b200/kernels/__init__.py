@@ -1,0 +1,26 @@
+"""Fused B200 kernels and their functional API (drop-in for ``delta_phase.kernels``)."""
+from .chunk_delta import (
+    DeltaPhaseCudaFunction,
+    DeltaPhaseTritonFunction,
+    chunkwise_forward,
+    cuda_available,
+    decode_step,
+    delta_phase_chunkwise_fused,
+    gram_matrix_cuda,
+    gram_matrix_triton,
+    laplace_chunkwise,
+    triton_available,
+)
+
+__all__ = [
+    "delta_phase_chunkwise_fused",
+    "triton_available",
+    "DeltaPhaseTritonFunction",
+    "DeltaPhaseCudaFunction",
+    "cuda_available",
+    "chunkwise_forward",
+    "decode_step",
+    "gram_matrix_cuda",
+    "gram_matrix_triton",
+    "laplace_chunkwise",
+]

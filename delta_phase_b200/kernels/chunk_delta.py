@@ -1,0 +1,183 @@
+"""Functional chunkwise delta-rule core on the B200 CUDA kernels.
+
+Drop-in for ``delta_phase.kernels.triton_chunk_delta`` (mcarbonell/delta-phase v1.3.0):
+
+* :func:`delta_phase_chunkwise_fused` -- same signature and return contract as the
+  reference dispatcher (triton_chunk_delta.py:279-291) and ``_chunkwise_delta_reference``
+  (:211-252): ``(out (B,H,L,D) real, M (B,H,D,D) complex)``; ``L`` must be a multiple
+  of ``chunk_size`` (the reference's ``view`` raises RuntimeError otherwise);
+  ``initial_state`` is never modified.
+* :class:`DeltaPhaseCudaFunction` (alias ``DeltaPhaseTritonFunction``) -- the autograd
+  wrapper; like the reference's (:255-276) it is inference-only and its backward raises.
+* :func:`gram_matrix_cuda` (alias ``gram_matrix_triton``) -- the strictly-lower phasor
+  Gram of the archived Triton kernel (:32-122).
+* :func:`decode_step` -- the fused single-token state update (layers.py:279-285).
+* :func:`laplace_chunkwise` -- the LaplacePhaseCore chunk solve (layers.py:481-561).
+* :func:`triton_available` -- kept for API compatibility; True when the CUDA library
+  is loaded and a GPU is present (the kernels it reported on are replaced here).
+"""
+from __future__ import annotations
+
+import torch
+
+from .. import _capi
+
+
+def cuda_available() -> bool:
+    """True if the deltaphase_b200 library loads and a CUDA device is present."""
+    return torch.cuda.is_available() and _capi.library_available()
+
+
+def triton_available() -> bool:
+    """Reference name (triton_chunk_delta.py:21-23): reports whether the fused GPU path
+    can run.  Here that path is the sm_100a CUDA library, not Triton."""
+    return cuda_available()
+
+
+def _check_phase_inputs(theta_k, theta_q, v, beta):
+    if theta_k.dim() != 4 or theta_q.shape != theta_k.shape:
+        raise ValueError("theta_k and theta_q must both be (B, H, L, D)")
+    if v.dim() != 4 or v.shape[:3] != theta_k.shape[:3]:
+        raise ValueError("v must be (B, H, L, Dv)")
+    if beta.shape != theta_k.shape[:3]:
+        raise ValueError("beta must be (B, H, L)")
+    if theta_k.dtype == torch.float64 or v.dtype == torch.float64:
+        raise TypeError("float64 inputs are not supported by the CUDA path")
+    if not (theta_k.dtype == theta_q.dtype == v.dtype):
+        raise TypeError("theta_k, theta_q and v must share one dtype")
+
+
+def _complex_state_view(state, B, H, Dv, D, device):
+    """float32 (B,H,Dv,D,2) contiguous view of a complex64 state (copied if needed)."""
+    if state is None:
+        return None
+    if not torch.is_complex(state):
+        raise TypeError("the delta-rule state must be a complex tensor")
+    if state.dtype != torch.complex64:
+        raise TypeError("the CUDA path keeps the state in complex64")
+    if tuple(state.shape) != (B, H, Dv, D):
+        raise ValueError(f"state must be (B, H, Dv, D) = {(B, H, Dv, D)}, got {tuple(state.shape)}")
+    if state.device != device:
+        raise RuntimeError("state must be on the same device as the inputs")
+    return torch.view_as_real(state.contiguous())
+
+
+def chunkwise_forward(theta_k, theta_q, v, beta, chunk_size=64, initial_state=None, out=None):
+    """Run the CUDA chunkwise core; ragged L is allowed (tokens past L do not exist).
+
+    ``out`` may be a preallocated float32 (B, H, L, Dv) view (any strides with unit
+    channel stride), e.g. a (B, L, H, Dv) buffer transposed.  Returns ``(out, M)``.
+    """
+    _check_phase_inputs(theta_k, theta_q, v, beta)
+    _capi.require_cuda(theta_k, theta_q, v, beta)
+    B, H, L, D = theta_k.shape
+    Dv = v.shape[-1]
+    dev = theta_k.device
+    s_in = _complex_state_view(initial_state, B, H, Dv, D, dev)
+    if out is None:
+        out = torch.empty(B, H, L, Dv, device=dev, dtype=torch.float32)
+    M = torch.empty(B, H, Dv, D, device=dev, dtype=torch.complex64)
+    _capi.core_fwd(theta_k, theta_q, v, beta, chunk_size, s_in, out, torch.view_as_real(M))
+    return out, M
+
+
+class DeltaPhaseCudaFunction(torch.autograd.Function):
+    """Autograd wrapper of the fused forward.  Inference only, like the reference's
+    DeltaPhaseTritonFunction (triton_chunk_delta.py:255-276): backward raises."""
+
+    @staticmethod
+    def forward(ctx, theta_k, theta_q, v, beta, chunk_size=64, initial_state=None):
+        return chunkwise_forward(theta_k, theta_q, v, beta, chunk_size, initial_state)
+
+    @staticmethod
+    def backward(ctx, grad_out, grad_final_state):
+        raise NotImplementedError(
+            "The B200 delta-phase kernels are inference-only: no backward pass is built.")
+
+
+DeltaPhaseTritonFunction = DeltaPhaseCudaFunction
+
+
+def delta_phase_chunkwise_fused(theta_k, theta_q, v, beta, chunk_size=64, initial_state=None):
+    """Chunkwise complex delta-rule forward (reference: triton_chunk_delta.py:279-291).
+
+    theta_k, theta_q, v: (B, H, L, D) float32/bfloat16/float16 CUDA tensors; beta (B, H, L);
+    initial_state: (B, H, D, D) complex64 or None.  Returns ``(out (B,H,L,D) float32,
+    M (B,H,D,D) complex64)``.  L must be a multiple of chunk_size, as in the reference.
+    """
+    L = theta_k.shape[2]
+    if chunk_size < 1 or L % chunk_size != 0:
+        raise RuntimeError(
+            f"shape mismatch: L={L} is not a multiple of chunk_size={chunk_size}")
+    if torch.is_grad_enabled() and any(
+            t is not None and t.requires_grad for t in (theta_k, theta_q, v, beta, initial_state)):
+        return DeltaPhaseCudaFunction.apply(theta_k, theta_q, v, beta, chunk_size, initial_state)
+    with torch.no_grad():
+        return chunkwise_forward(theta_k, theta_q, v, beta, chunk_size, initial_state)
+
+
+def gram_matrix_cuda(theta_k: torch.Tensor, beta: torch.Tensor) -> torch.Tensor:
+    """Strictly-lower row-beta-scaled phasor Gram (N, C, C) float32
+    (contract of gram_matrix_reference, triton_chunk_delta.py:192-208)."""
+    if theta_k.dim() != 3 or beta.shape != theta_k.shape[:2]:
+        raise ValueError("theta_k must be (N, C, D) and beta (N, C)")
+    _capi.require_cuda(theta_k, beta)
+    th = theta_k.contiguous()
+    b = beta.contiguous()
+    N, C, _ = th.shape
+    out = torch.empty(N, C, C, device=th.device, dtype=torch.float32)
+    _capi.gram(th, b, out)
+    return out
+
+
+gram_matrix_triton = gram_matrix_cuda
+
+
+def decode_step(memory_state, theta_k, theta_q, v, beta, out=None, state_out=None):
+    """Fused decode step (layers.py:279-285).  memory_state (B,H,Dv,D) complex64;
+    theta_k/theta_q (B,H,D); v (B,H,Dv); beta (B,H).  Returns ``(out (B,H,Dv) float32,
+    new_state)``.  ``state_out=memory_state`` updates the state in place."""
+    B, H, D = theta_k.shape
+    Dv = v.shape[-1]
+    _capi.require_cuda(memory_state, theta_k, theta_q, v, beta)
+    s_in = _complex_state_view(memory_state, B, H, Dv, D, theta_k.device)
+    if state_out is None:
+        state_out = torch.empty(B, H, Dv, D, device=theta_k.device, dtype=torch.complex64)
+    elif state_out.dtype != torch.complex64 or not state_out.is_contiguous():
+        raise ValueError("state_out must be a contiguous complex64 tensor")
+    if out is None:
+        out = torch.empty(B, H, Dv, device=theta_k.device, dtype=torch.float32)
+    _capi.core_decode(s_in, torch.view_as_real(state_out), theta_k, theta_q, v, beta, out)
+    return out, state_out
+
+
+def laplace_chunkwise(theta_k, logmag_k, theta_q, logmag_q, v, log_decay, beta, chunk_size=32,
+                      initial_state=None, out=None):
+    """LaplacePhaseCore chunk solve (layers.py:481-561) on the CUDA kernel.
+
+    K = exp(logmag_k) e^{i theta_k}, Q = exp(logmag_q) e^{i theta_q} ((B,H,L,D); the
+    log-magnitudes may be None = unit phasors); log_decay (B,H,L,Dv) is log r per value
+    channel (clamped at -80 per step like the reference); beta (B,H,L).
+    Returns ``(out (B,H,L,Dv) float32, M (B,H,Dv,D) complex64)``.
+    """
+    B, H, L, D = theta_k.shape
+    Dv = v.shape[-1]
+    _capi.require_cuda(theta_k, theta_q, v, log_decay, beta)
+    for t in (logmag_k, logmag_q):
+        if t is not None and t.shape != theta_k.shape:
+            raise ValueError("log-magnitudes must match theta's shape")
+    if log_decay.shape != v.shape:
+        raise ValueError("log_decay must be (B, H, L, Dv)")
+    dt = theta_k.dtype
+    for t in (theta_q, v, log_decay, logmag_k, logmag_q):
+        if t is not None and t.dtype != dt:
+            raise TypeError("phase, magnitude, value and decay inputs must share one dtype")
+    if dt == torch.float64:
+        raise TypeError("float64 inputs are not supported by the CUDA path")
+    s_in = _complex_state_view(initial_state, B, H, Dv, D, theta_k.device)
+    if out is None:
+        out = torch.empty(B, H, L, Dv, device=theta_k.device, dtype=torch.float32)
+    M = torch.empty(B, H, Dv, D, device=theta_k.device, dtype=torch.complex64)
+    _capi.laplace_fwd(theta_k, logmag_k, theta_q, logmag_q, v, log_decay, beta, chunk_size, s_in,
+                      out, torch.view_as_real(M))
+    return out, M

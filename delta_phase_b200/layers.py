@@ -1,0 +1,281 @@
+"""Drop-in modules of the DeltaPhase hot path, running on the B200 CUDA kernels.
+
+Same class names, constructor arguments, parameter and buffer names as
+``delta_phase/layers.py`` (mcarbonell/delta-phase v1.3.0), so ``state_dict`` files
+load in both directions:
+
+* :class:`ShortCausalConv1D`            -- layers.py:60-88 (torch glue, unchanged math)
+* :class:`LearnableSubstrateLerpFFN`    -- layers.py:90-145 (CUDA: dp_ffn_fold/dp_ffn_fwd)
+* :class:`DeltaPhaseHolographicBlock`   -- layers.py:147-291 (CUDA: dp_core_fwd/dp_core_decode)
+* :class:`LaplacePhaseCore`             -- layers.py:422-583 (CUDA: dp_laplace_fwd)
+
+LayerNorms, the causal conv and the projections stay torch (cuBLAS) calls; the
+delta-rule core, its decode step and the spectral FFN run in the CUDA library, with no
+CPU fallback.  The modules are inference-only: the fused core has no backward.
+"""
+from __future__ import annotations
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from . import _capi
+from .kernels.chunk_delta import chunkwise_forward, decode_step, laplace_chunkwise
+from .spectral import create_dct2_matrix, create_haar_matrix, create_hadamard_matrix
+
+_BRANCHES = ("fwht", "dct", "haar")
+
+
+class ShortCausalConv1D(nn.Module):
+    """Depthwise causal conv (kernel_size 4) + SiLU + residual (layers.py:60-88)."""
+
+    def __init__(self, d_model: int, kernel_size: int = 4):
+        super().__init__()
+        self.kernel_size = kernel_size
+        self.conv = nn.Conv1d(d_model, d_model, kernel_size, padding=kernel_size - 1, groups=d_model)
+        self.act = nn.SiLU()
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        B, L, D = x.shape
+        conv_out = self.conv(x.transpose(1, 2))[:, :, :L].transpose(1, 2)
+        return x + self.act(conv_out)
+
+    def step(self, x_t: torch.Tensor, conv_state=None):
+        B, L, D = x_t.shape
+        if conv_state is None:
+            conv_state = torch.zeros(B, D, self.kernel_size - 1, device=x_t.device, dtype=x_t.dtype)
+        inputs = torch.cat([conv_state, x_t.transpose(1, 2)], dim=2)
+        new_conv_state = inputs[:, :, 1:]
+        conv_out = F.conv1d(inputs, self.conv.weight, self.conv.bias, groups=D)[:, :, -1:]
+        return x_t + self.act(conv_out.transpose(1, 2)), new_conv_state
+
+
+class LearnableSubstrateLerpFFN(nn.Module):
+    """Spectral Lerp FFN (layers.py:90-145) on the folded CUDA path.
+
+    The three branch activations are linear in z = [cos h_b, sin h_b] (angle addition),
+    so the parameters are folded once into F (6d x d, float64 accumulation) and each
+    call runs the fast transforms, 6d sincos per token and one GEMM.  F is rebuilt
+    whenever a parameter or buffer changes (tracked by tensor version counters).
+    """
+
+    def __init__(self, d_model: int, num_banks: int = 4):
+        super().__init__()
+        self.d_model = d_model
+        self.num_banks = num_banks
+        self.substrate_logits = nn.Parameter(torch.tensor([0.0, 0.0, 0.0]))
+        self.register_buffer("mat_fwht", create_hadamard_matrix(d_model))
+        self.register_buffer("mat_dct", create_dct2_matrix(d_model))
+        self.register_buffer("mat_haar", create_haar_matrix(d_model))
+        for b in _BRANCHES:
+            setattr(self, f"phi1_{b}", nn.Parameter(torch.zeros(num_banks, d_model)))
+            setattr(self, f"phi2_{b}", nn.Parameter(torch.zeros(num_banks, d_model)))
+            setattr(self, f"w1_{b}", nn.Parameter(torch.ones(num_banks, d_model)))
+            setattr(self, f"w2_{b}", nn.Parameter(torch.ones(num_banks, d_model)))
+        self.combine = nn.Linear(num_banks * d_model, d_model, bias=False)
+        self._fold_key = None
+        self._fold = {}
+
+    def _state_key(self):
+        ts = [self.substrate_logits, self.mat_fwht, self.mat_dct, self.mat_haar, self.combine.weight]
+        for b in _BRANCHES:
+            ts += [getattr(self, f"{n}_{b}") for n in ("phi1", "phi2", "w1", "w2")]
+        return tuple((t.data_ptr(), t._version, t.device) for t in ts)
+
+    @torch.no_grad()
+    def folded(self, dtype):
+        """F (6d x d) and the DCT matrix in ``dtype`` (float32 or bfloat16), cached."""
+        key = self._state_key()
+        if key != self._fold_key:
+            d, nb = self.d_model, self.num_banks
+            dev = self.mat_dct.device
+            f32 = lambda t: t.detach().to(device=dev, dtype=torch.float32).contiguous()  # noqa: E731
+            mats = torch.stack([f32(self.mat_fwht), f32(self.mat_dct), f32(self.mat_haar)])
+            banks = torch.stack([torch.stack([f32(getattr(self, f"{n}_{b}"))
+                                              for n in ("phi1", "phi2", "w1", "w2")])
+                                 for b in _BRANCHES])
+            Fm = torch.empty(6 * d, d, device=dev, dtype=torch.float32)
+            _capi.ffn_fold(f32(self.substrate_logits), mats, banks, f32(self.combine.weight), Fm, d, nb)
+            self._fold = {torch.float32: (Fm, f32(self.mat_dct))}
+            self._fold_key = key
+        if dtype not in self._fold:
+            Fm, dct = self._fold[torch.float32]
+            self._fold[dtype] = (Fm.to(dtype), dct.to(dtype))
+        return self._fold[dtype]
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if x.shape[-1] != self.d_model:
+            raise ValueError(f"expected last dim {self.d_model}, got {x.shape[-1]}")
+        if x.dtype == torch.float64:
+            raise TypeError("float64 inputs are not supported by the CUDA path")
+        _capi.require_cuda(x, self.mat_dct)
+        cdt = torch.bfloat16 if x.dtype == torch.bfloat16 else torch.float32
+        x2 = x.reshape(-1, self.d_model).to(cdt).contiguous()
+        Fm, dct = self.folded(cdt)
+        y = torch.empty_like(x2)
+        ws = torch.empty(_capi.ffn_workspace_size(x2.shape[0], self.d_model, cdt),
+                         device=x.device, dtype=torch.uint8)
+        _capi.ffn_fwd(x2, dct, Fm, y, ws)
+        return y.view(x.shape).to(x.dtype)
+
+    def get_substrate_probabilities(self):
+        probs = F.softmax(self.substrate_logits, dim=0)
+        return probs[0].item(), probs[1].item(), probs[2].item()
+
+
+class DeltaPhaseHolographicBlock(nn.Module):
+    """Chunkwise complex delta-phase memory block (layers.py:147-291)."""
+
+    def __init__(self, d_model: int, n_heads: int = 8, conv_kernel_size: int = 4,
+                 chunk_size: int = 64, num_banks: int = 4, beta_mode: str = "learned"):
+        super().__init__()
+        if beta_mode not in ("learned", "fixed"):
+            raise ValueError(f"beta_mode must be 'learned' or 'fixed', got {beta_mode!r}")
+        self.d_model = d_model
+        self.n_heads = n_heads
+        self.d_k = d_model // n_heads
+        self.inv_dk = 1.0 / float(self.d_k)
+        self.chunk_size = chunk_size
+        self.beta_mode = beta_mode
+        self.last_beta = None
+        self.norm1 = nn.LayerNorm(d_model)
+        self.norm2 = nn.LayerNorm(d_model)
+        self.norm_retrieved = nn.LayerNorm(d_model)
+        self.causal_conv = ShortCausalConv1D(d_model, kernel_size=conv_kernel_size)
+        self.w_k = nn.Linear(d_model, d_model)
+        self.w_q = nn.Linear(d_model, d_model)
+        self.w_v = nn.Linear(d_model, d_model)
+        self.w_beta = nn.Linear(d_model, n_heads)
+        self.out_proj = nn.Linear(d_model, d_model)
+        self.ffn = LearnableSubstrateLerpFFN(d_model, num_banks=num_banks)
+
+    def _beta(self, conv_x):
+        beta = 2.0 * torch.sigmoid(self.w_beta(conv_x))
+        if self.beta_mode == "fixed":
+            beta = torch.ones_like(beta)
+        return beta
+
+    def forward(self, x: torch.Tensor, memory_state=None):
+        res = x
+        conv_x = self.causal_conv(self.norm1(x))
+        B, L, D = conv_x.shape
+        H, dk = self.n_heads, self.d_k
+        # (B, L, H, dk) projections viewed as (B, H, L, dk): the kernel reads them in
+        # place, handles the ragged last chunk itself (no padding copy) and writes the
+        # retrieved values straight into the (B, L, H*dk) buffer the norm consumes.
+        tk = self.w_k(conv_x).view(B, L, H, dk).transpose(1, 2)
+        tq = self.w_q(conv_x).view(B, L, H, dk).transpose(1, 2)
+        v = self.w_v(conv_x).view(B, L, H, dk).transpose(1, 2)
+        beta = self._beta(conv_x).transpose(1, 2)
+        dt = torch.promote_types(torch.promote_types(tk.dtype, tq.dtype), v.dtype)
+        tk, tq, v = tk.to(dt), tq.to(dt), v.to(dt)
+        retrieved = torch.empty(B, L, D, device=x.device, dtype=torch.float32)
+        _, M_state = chunkwise_forward(tk, tq, v, beta, self.chunk_size, memory_state,
+                                       out=retrieved.view(B, L, H, dk).transpose(1, 2))
+        self.last_beta = beta.detach()
+        x = res + self.out_proj(self.norm_retrieved(retrieved))
+        x = x + self.ffn(self.norm2(x))
+        return x, M_state
+
+    def step(self, x_t: torch.Tensor, state=None):
+        """Single-token step (layers.py:246-291); returns ``(x, (conv_state, M))``."""
+        res = x_t
+        normed = self.norm1(x_t)
+        if state is None:
+            conv_state, memory_state = None, None
+        elif isinstance(state, tuple):
+            conv_state, memory_state = state
+        else:
+            conv_state, memory_state = None, state
+        conv_x, new_conv_state = self.causal_conv.step(normed, conv_state=conv_state)
+        B, L, D = conv_x.shape
+        H, dk = self.n_heads, self.d_k
+        tk = self.w_k(conv_x).view(B, H, dk)
+        tq = self.w_q(conv_x).view(B, H, dk)
+        v = self.w_v(conv_x).view(B, H, dk)
+        beta = self._beta(conv_x).view(B, H)
+        dt = torch.promote_types(torch.promote_types(tk.dtype, tq.dtype), v.dtype)
+        tk, tq, v = tk.to(dt), tq.to(dt), v.to(dt)
+        self.last_beta = beta.detach().unsqueeze(-1)
+        if memory_state is None:
+            memory_state = torch.zeros(B, H, dk, dk, dtype=torch.complex64, device=x_t.device)
+        out, memory_state = decode_step(memory_state, tk, tq, v, beta)
+        retrieved_norm = self.norm_retrieved(out.reshape(B, 1, D))
+        x = res + self.out_proj(retrieved_norm)
+        x = x + self.ffn(self.norm2(x))
+        return x, (new_conv_state, memory_state)
+
+
+class LaplacePhaseCore(nn.Module):
+    """Gated (Laplace) phase memory core (layers.py:422-583) on the CUDA kernel.
+
+    Recurrence: v_old = Re(M k^H)/d_k; M = diag(r_t) M + beta_t (v_t - v_old) k_t^T;
+    out_t = Re(M q^H)/d_k with K = r_k e^{i theta_k}, r_t = r_k (both from sigma_k).
+    """
+
+    LOG_FLOOR = -80.0
+
+    def __init__(self, d_model=64, n_heads=4, d_k=16, chunk_size=32):
+        super().__init__()
+        self.d_model = d_model
+        self.n_heads = n_heads
+        self.d_k = d_k
+        self.inv_dk = 1.0 / float(d_k)
+        self.chunk_size = int(chunk_size)
+        self.w_theta_k = nn.Linear(d_model, d_model, bias=False)
+        self.w_sigma_k = nn.Linear(d_model, d_model, bias=False)
+        self.w_theta_q = nn.Linear(d_model, d_model, bias=False)
+        self.w_sigma_q = nn.Linear(d_model, d_model, bias=False)
+        self.w_v = nn.Linear(d_model, d_model, bias=False)
+        self.w_beta = nn.Linear(d_model, n_heads, bias=False)
+
+    def _proj(self, x, time_scale):
+        """Real projections (layers.py:462-479 before the phasor is formed), float32."""
+        B, L, _ = x.shape
+        dt = 1.0 / float(time_scale)
+        if x.dtype == torch.float64:
+            raise TypeError("float64 inputs are not supported by the CUDA path")
+        hv = lambda y: y.view(B, L, self.n_heads, self.d_k).transpose(1, 2)  # noqa: E731
+        theta_k = hv(self.w_theta_k(x).float() * dt)
+        sigma_k = hv(-F.softplus(self.w_sigma_k(x).float()) * dt)
+        theta_q = hv(self.w_theta_q(x).float() * dt)
+        sigma_q = hv(-F.softplus(self.w_sigma_q(x).float()) * dt)
+        v = hv(self.w_v(x).float())
+        beta = (2.0 * torch.sigmoid(self.w_beta(x).float()) * dt).transpose(1, 2)
+        return theta_k, sigma_k, theta_q, sigma_q, v, beta
+
+    def _project(self, x: torch.Tensor, time_scale: float):
+        """Reference API (layers.py:462-479): returns (K, Q, v, beta, r_k)."""
+        theta_k, sigma_k, theta_q, sigma_q, v, beta = self._proj(x, time_scale)
+        r_k = torch.exp(sigma_k)
+        r_q = torch.exp(sigma_q)
+        K = torch.complex(r_k * torch.cos(theta_k), r_k * torch.sin(theta_k))
+        Q = torch.complex(r_q * torch.cos(theta_q), r_q * torch.sin(theta_q))
+        return K, Q, v, beta, r_k
+
+    def forward(self, x: torch.Tensor, memory_state=None, time_scale: float = 1.0):
+        theta_k, sigma_k, theta_q, sigma_q, v, beta = self._proj(x, time_scale)
+        B, H, L, dk = theta_k.shape
+        retrieved = torch.empty(B, L, H * dk, device=x.device, dtype=torch.float32)
+        _, M = laplace_chunkwise(theta_k, sigma_k, theta_q, sigma_q, v, sigma_k, beta,
+                                 self.chunk_size, memory_state,
+                                 out=retrieved.view(B, L, H, dk).transpose(1, 2))
+        return retrieved, M
+
+    def forward_sequential(self, x: torch.Tensor, memory_state=None, time_scale: float = 1.0):
+        """Literal token loop (layers.py:563-583), kept as the module's reference API for
+        equivalence tests; it is not used by ``forward``."""
+        K, Q, v, beta, r_k = self._project(x, time_scale)
+        B, H, L, dk = K.shape
+        M = (torch.zeros(B, H, dk, dk, dtype=torch.complex64, device=x.device)
+             if memory_state is None else memory_state)
+        outs = []
+        for t in range(L):
+            kt, qt, vt, bt = K[:, :, t], Q[:, :, t], v[:, :, t], beta[:, :, t]
+            v_old = torch.matmul(M, torch.conj(kt).unsqueeze(-1)).squeeze(-1).real * self.inv_dk
+            err = vt - v_old
+            M = M * r_k[:, :, t].unsqueeze(-1) + bt[..., None, None] * torch.matmul(
+                err.to(M.dtype).unsqueeze(-1), kt.unsqueeze(-2))
+            outs.append(torch.matmul(M, torch.conj(qt).unsqueeze(-1)).squeeze(-1).real * self.inv_dk)
+        retrieved = torch.stack(outs, 2).transpose(1, 2).reshape(B, L, self.d_model)
+        return retrieved, M

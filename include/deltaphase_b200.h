@@ -1,0 +1,165 @@
+/*
+ * deltaphase_b200.h -- C ABI of the B200 (sm_100a) DeltaPhase inference kernels.
+ *
+ * Every entry point takes plain device pointers, sizes, element strides and a
+ * cudaStream_t passed as `void *` (NULL = legacy default stream), launches
+ * asynchronously on that stream, allocates nothing and returns an int status
+ * (DP_OK = 0).  On failure dp_last_error() returns a message for the calling
+ * host thread.  No entry point synchronises the stream.
+ *
+ * Conventions shared by all entry points
+ *   - dtype codes: DP_F32, DP_BF16, DP_F16 for phase / value / beta / x inputs.
+ *   - Complex states (the reference's complex64 M of shape (B, H, Dv, D), row =
+ *     value channel, column = key channel) are passed as float pointers to the
+ *     interleaved (re, im) pairs, i.e. torch.view_as_real(M), contiguous.
+ *   - Strides are in elements.  Sequence tensors are addressed as
+ *     base + b*sb + h*sh + t*st + c with unit stride over the channel c, so the
+ *     (B, L, H, D) projection outputs of a block can be passed without a copy.
+ *
+ * Reference: mcarbonell/delta-phase v1.3.0 (pure PyTorch); each declaration
+ * names the reference interface it replaces.
+ */
+#ifndef DELTAPHASE_B200_H
+#define DELTAPHASE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define DP_API __attribute__((visibility("default")))
+#else
+#define DP_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum dp_dtype { DP_F32 = 0, DP_BF16 = 1, DP_F16 = 2 };
+
+enum dp_status {
+  DP_OK = 0,
+  DP_ERR_INVALID_ARGUMENT = 1, /* null pointer, negative size, bad dtype code  */
+  DP_ERR_UNSUPPORTED = 2,      /* shape outside the kernel's limits            */
+  DP_ERR_MISALIGNED = 3,       /* pointer/stride alignment a kernel requires   */
+  DP_ERR_CUDA = 4,             /* launch or runtime error reported by CUDA     */
+  DP_ERR_TIMEOUT = 5,          /* a device-side wait exceeded its bound        */
+  DP_ERR_WORKSPACE = 6         /* workspace too small                          */
+};
+
+/* Library version string, e.g. "deltaphase_b200 0.1.0 (sm_100a)". */
+DP_API const char *dp_version(void);
+/* Message of the last failed call made by this host thread ("" if none). */
+DP_API const char *dp_last_error(void);
+/* Name of a status code. */
+DP_API const char *dp_status_string(int status);
+
+/*
+ * Chunkwise complex delta-rule forward (inference).
+ * Replaces _chunkwise_delta_reference / delta_phase_chunkwise_fused
+ * (delta_phase/kernels/triton_chunk_delta.py:211-252, :279-291) and the core
+ * inlined in DeltaPhaseHolographicBlock.forward (delta_phase/layers.py:203-236).
+ *
+ *   theta_k, theta_q : (B, H, L, D)  phases, dtype in_dtype
+ *   v                : (B, H, L, Dv) values, dtype in_dtype
+ *   beta             : (B, H, L)     write strengths, dtype beta_dtype
+ *   state_in         : (B, H, Dv, D) complex64 initial state or NULL (= zero)
+ *   out              : (B, H, L, Dv) float32 retrieved values
+ *   state_out        : (B, H, Dv, D) complex64 final state (may equal state_in)
+ *   strides[15]      : {sb, sh, st} of theta_k, theta_q, v, beta, out (beta's
+ *                      st is its token stride)
+ * Any L >= 0 is accepted; the result equals the reference's chunkwise path for
+ * every chunk_size (>= 1) because it is the same recurrence -- the kernel picks
+ * its own internal chunking.  Limits: 1 <= D, Dv <= 128.
+ */
+DP_API int dp_core_fwd(const void *theta_k, const void *theta_q, const void *v, const void *beta,
+                int in_dtype, int beta_dtype, const float *state_in, float *out,
+                float *state_out, int B, int H, int L, int D, int Dv, int chunk_size,
+                const int64_t *strides, void *stream);
+
+/*
+ * Single-token decode step: v_old = Re(M conj(k))/D; M += beta (v - v_old) k^T;
+ * out = Re(M conj(q))/D (read after the update).
+ * Replaces the state update of DeltaPhaseHolographicBlock.step
+ * (delta_phase/layers.py:279-285) and the never-launched
+ * _triton_streaming_step_kernel (delta_phase/kernels/triton_chunk_delta.py:125-185).
+ *
+ *   state_in/state_out : (B, H, Dv, D) complex64; may alias (in-place update)
+ *   theta_k, theta_q   : (B, H, D);  v : (B, H, Dv);  beta : (B, H)
+ *   out                : (B, H, Dv) float32
+ *   strides[10]        : {sb, sh} of theta_k, theta_q, v, beta, out
+ */
+DP_API int dp_core_decode(const float *state_in, float *state_out, const void *theta_k,
+                   const void *theta_q, const void *v, const void *beta, int in_dtype,
+                   int beta_dtype, float *out, int B, int H, int D, int Dv,
+                   const int64_t *strides, void *stream);
+
+/*
+ * Strictly-lower, row-beta-scaled phasor Gram of N chunks:
+ *   G[n, m, j] = beta[n, m] * sum_d cos(theta[n,m,d] - theta[n,j,d]) / D  (m > j), else 0.
+ * Replaces gram_matrix_triton / _triton_fused_phase_gram_kernel
+ * (delta_phase/kernels/triton_chunk_delta.py:32-122); contract of
+ * gram_matrix_reference (:192-208).  theta (N, C, D), beta (N, C), out (N, C, C)
+ * float32, all contiguous.  Limits: C <= 256, D <= 256.
+ */
+DP_API int dp_gram(const void *theta, const void *beta, int in_dtype, int beta_dtype, float *out,
+            int N, int C, int D, void *stream);
+
+/*
+ * LaplacePhaseCore chunkwise forward with per-row decay.
+ * Replaces the chunk loop of LaplacePhaseCore.forward (delta_phase/layers.py:481-561),
+ * fed the outputs of _project (layers.py:462-479):
+ *   K = exp(logmag_k) e^{i theta_k},  Q = exp(logmag_q) e^{i theta_q},
+ *   r = exp(log_decay) per (token, value channel), clamped like the reference
+ *   (log r >= -80, layers.py:445,512).
+ * Recurrence: v_old = Re(M conj(k_t))/D (pre-decay); M = diag(r_t) M + beta_t (v_t - v_old) k_t^T;
+ * out_t = Re(M conj(q_t))/D.
+ *   theta_k, theta_q, logmag_k, logmag_q : (B, H, L, D) (logmag_* may be NULL = 0)
+ *   v, log_decay : (B, H, L, Dv);  beta : (B, H, L)
+ *   strides[24]  : {sb, sh, st} of theta_k, logmag_k, theta_q, logmag_q, v,
+ *                  log_decay, beta, out (entries of NULL tensors are ignored)
+ * Limits: 1 <= D, Dv <= 128.
+ */
+DP_API int dp_laplace_fwd(const void *theta_k, const void *logmag_k, const void *theta_q,
+                   const void *logmag_q, const void *v, const void *log_decay,
+                   const void *beta, int in_dtype, int beta_dtype, const float *state_in,
+                   float *out, float *state_out, int B, int H, int L, int D, int Dv,
+                   int chunk_size, const int64_t *strides, void *stream);
+
+/*
+ * Fold the spectral Lerp FFN parameters into one (6d x d) matrix.
+ * With a_b = cos(h_b + phi1_b) w1_b + sin(h_b + phi2_b) w2_b
+ *           = cos(h_b) alpha_b + sin(h_b) gamma_b   (angle addition), the FFN of
+ * LearnableSubstrateLerpFFN.forward (delta_phase/layers.py:119-141) is exactly
+ *   y = sum_b softmax(logits)_b (a_b W_c^T) M_b = z F,
+ *   z = [cos h_fwht, sin h_fwht, cos h_dct, sin h_dct, cos h_haar, sin h_haar],
+ *   F[(2b+s) d + i, j] = w_b sum_m (sum_k coef_{b,s}[k,i] W_c[m, k d + i]) M_b[m, j].
+ * Inputs (float32, contiguous): logits (3); mats (3, d, d) = mat_fwht, mat_dct,
+ * mat_haar; banks (3, 4, nb, d) = per branch {phi1, phi2, w1, w2}; combine
+ * (d, nb*d).  Output F (6d, d) float32.  Accumulates in float64.
+ */
+DP_API int dp_ffn_fold(const float *logits, const float *mats, const float *banks,
+                const float *combine, float *F, int d, int nb, void *stream);
+
+/* Workspace bytes dp_ffn_fwd needs for `tokens` rows of width d. */
+DP_API size_t dp_ffn_workspace_size(int tokens, int d, int x_dtype);
+
+/*
+ * Spectral Lerp FFN forward: h_b = M_b x via the fast transforms (Sylvester FWHT,
+ * the reference's recursive Haar) and one GEMM with the DCT-II matrix,
+ * z = [cos h_b, sin h_b]_b, y = z F (F from dp_ffn_fold).
+ * Replaces LearnableSubstrateLerpFFN.forward (delta_phase/layers.py:119-141) and the
+ * dense bases of delta_phase/spectral.py:4-35.
+ *   x, y (tokens, d), dct (d, d) = mat_dct, F (6d, d): all contiguous and of dtype
+ *   x_dtype (DP_F32: TF32 tensor-core GEMMs; DP_BF16: bf16 GEMMs), fp32 accumulation.
+ *   d a power of two, 8 <= d <= 4096.  workspace >= dp_ffn_workspace_size() bytes,
+ *   256-byte aligned.
+ */
+DP_API int dp_ffn_fwd(const void *x, int x_dtype, const void *dct, const void *F, void *y, int tokens,
+               int d, void *workspace, size_t workspace_bytes, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DELTAPHASE_B200_H */

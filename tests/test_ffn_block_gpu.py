@@ -1,0 +1,114 @@
+"""GPU parity of the spectral Lerp FFN (dp_ffn_fold + dp_ffn_fwd) and of the drop-in
+block forward/step against golden vectors from the reference and the fp64 oracle."""
+import numpy as np
+import pytest
+import torch
+
+import delta_phase_b200 as dp
+from oracle import spectral as ospec
+
+from helpers import TOL_BF16, TOL_F32, load_golden, rel_l2, round_bf16, to_dev
+
+pytestmark = pytest.mark.gpu
+
+
+def _ffn_from_golden(g, i):
+    p = f"c{i}_p_"
+    params = {k[len(p):]: g[k] for k in g.files if k.startswith(p)}
+    d = params["mat_dct"].shape[0]
+    ffn = dp.LearnableSubstrateLerpFFN(d, num_banks=int(g[f"c{i}_nb"])).cuda()
+    ffn.load_state_dict({k: torch.from_numpy(v).float() for k, v in params.items()})
+    return ffn, params
+
+
+def test_ffn_golden_fp32():
+    g = load_golden("ffn")
+    for i in range(int(g["n_cases"])):
+        ffn, _ = _ffn_from_golden(g, i)
+        with torch.no_grad():
+            y = ffn(to_dev(g[f"c{i}_x"].astype(np.float32)))
+        assert rel_l2(y, g[f"c{i}_y"]) < TOL_F32, i
+
+
+def test_ffn_config4_bf16_slice():
+    """d_model = 1024, nb = 4, bf16 activations, params ~ N(0, 0.02), router ~ N(0, 1)."""
+    torch.manual_seed(0)
+    d, nb, tokens = 1024, 4, 512
+    ffn = dp.LearnableSubstrateLerpFFN(d, nb).cuda()
+    with torch.no_grad():
+        for n, p in ffn.named_parameters():
+            p.copy_(torch.randn_like(p) * (1.0 if n == "substrate_logits" else 0.02))
+    x = torch.randn(tokens, d, device="cuda").to(torch.bfloat16)
+    with torch.no_grad():
+        y = ffn(x)
+    assert y.dtype == torch.bfloat16
+    params = {k: v.detach().cpu().numpy() for k, v in ffn.state_dict().items()}
+    ref = ospec.lerp_ffn(x.float().cpu().numpy(), params)
+    assert rel_l2(y.float(), ref) < TOL_BF16
+
+
+def test_ffn_refolds_after_parameter_update():
+    g = load_golden("ffn")
+    ffn, params = _ffn_from_golden(g, 0)
+    x = to_dev(g["c0_x"].astype(np.float32))
+    with torch.no_grad():
+        ffn(x)
+        ffn.substrate_logits.add_(0.5)
+        y = ffn(x)
+    params = {k: v.detach().cpu().numpy() for k, v in ffn.state_dict().items()}
+    assert rel_l2(y, ospec.lerp_ffn(g["c0_x"], params)) < TOL_F32
+
+
+def _block_from_golden(g, i):
+    p = f"c{i}_"
+    params = {k[len(p) + 2:]: g[k] for k in g.files if k.startswith(p + "p_")}
+    blk = dp.DeltaPhaseHolographicBlock(d_model=64, n_heads=4, chunk_size=int(g[p + "C"]),
+                                        beta_mode=str(g[p + "beta_mode"])).cuda().eval()
+    blk.load_state_dict({k: torch.from_numpy(v).float() for k, v in params.items()})
+    return blk
+
+
+def test_block_forward_and_step_golden():
+    g = load_golden("block")
+    for i in range(int(g["n_cases"])):
+        p = f"c{i}_"
+        blk = _block_from_golden(g, i)
+        x = to_dev(g[p + "x"].astype(np.float32))
+        with torch.no_grad():
+            out, M = blk(x)
+            st = None
+            outs = []
+            for t in range(x.shape[1]):
+                o, st = blk.step(x[:, t:t + 1], st)
+                outs.append(o)
+        assert rel_l2(out, g[p + "out"]) < TOL_F32, i
+        assert rel_l2(M, g[p + "M"]) < TOL_F32, i
+        assert rel_l2(torch.cat(outs, 1), g[p + "out_step"]) < TOL_F32, i
+        assert rel_l2(st[1], g[p + "M_step"]) < TOL_F32, i
+        assert blk.last_beta.shape[:2] == (2, 4)
+
+
+def test_block_bf16_autocast_runs():
+    g = load_golden("block")
+    blk = _block_from_golden(g, 0)
+    x = to_dev(g["c0_x"].astype(np.float32))
+    with torch.no_grad():
+        ref, _ = blk(x)
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            out, M = blk(x)
+    assert torch.isfinite(out.float()).all()
+    assert rel_l2(out.float(), ref) < 5e-2
+
+
+def test_model_prefill_then_decode():
+    cfg = dp.DeltaPhaseConfig(dim=128, n_heads=2, n_layers=2, vocab_size=500, chunk_size=32)
+    torch.manual_seed(0)
+    model = dp.DeltaPhaseModel(cfg).cuda().eval()
+    ids = torch.randint(0, 500, (2, 40), device="cuda")
+    with torch.no_grad():
+        logits = model(ids)
+        st = None
+        for t in range(40):
+            lt, st = model.step(ids[:, t:t + 1], st)
+    assert logits.shape == (2, 40, 500)
+    assert rel_l2(lt[:, 0], logits[:, -1]) < TOL_F32
