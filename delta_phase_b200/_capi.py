@@ -25,6 +25,7 @@ _SIG = {
     "dp_version": (ctypes.c_char_p, []),
     "dp_last_error": (ctypes.c_char_p, []),
     "dp_status_string": (ctypes.c_char_p, [_I]),
+    "dp_device_error": (_I, [_I]),
     "dp_core_fwd": (_I, [_P, _P, _P, _P, _I, _I, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I64P, _P]),
     "dp_core_decode": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _P, _I, _I, _I, _I, _I64P, _P]),
     "dp_gram": (_I, [_P, _P, _I, _I, _P, _I, _I, _I, _P]),
@@ -72,6 +73,12 @@ def exported_symbols():
 
 def version():
     return lib().dp_version().decode()
+
+
+def device_error(clear=True):
+    """Synchronise the current device and return (optionally clear) the device-side
+    error word: 0, or 5 (DP_ERR_TIMEOUT) if a kernel's bounded wait expired."""
+    return int(lib().dp_device_error(1 if clear else 0))
 
 
 def library_available():

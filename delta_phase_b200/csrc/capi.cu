@@ -5,6 +5,22 @@ namespace dp {
 
 static thread_local std::string g_last_error;
 
+// Device-side error word: kernels record DP_ERR_TIMEOUT here when a bounded wait
+// expires (one word per device, read and cleared by dp_device_error).
+__device__ int g_device_error;
+
+int *device_error_ptr() {
+  static int *ptrs[64] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  if (!ptrs[dev]) {
+    void *p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_device_error) != cudaSuccess) return nullptr;
+    ptrs[dev] = static_cast<int *>(p);
+  }
+  return ptrs[dev];
+}
+
 int set_error(int status, const std::string &msg) {
   g_last_error = msg;
   return status;
@@ -25,6 +41,17 @@ extern "C" {
 const char *dp_version(void) { return "deltaphase_b200 0.1.0 (sm_100a)"; }
 
 const char *dp_last_error(void) { return dp::g_last_error.c_str(); }
+
+int dp_device_error(int clear) {
+  int v = 0;
+  if (cudaDeviceSynchronize() != cudaSuccess) return -1;
+  if (cudaMemcpyFromSymbol(&v, dp::g_device_error, sizeof(int)) != cudaSuccess) return -1;
+  if (clear && v != 0) {
+    const int zero = 0;
+    if (cudaMemcpyToSymbol(dp::g_device_error, &zero, sizeof(int)) != cudaSuccess) return -1;
+  }
+  return v;
+}
 
 const char *dp_status_string(int status) {
   switch (status) {

@@ -2,6 +2,11 @@
 #include "dp_common.cuh"
 
 namespace dp {
+bool core_tc_supported(const void *tk, const void *tq, const void *v, int in_dt, const float *out,
+                       int D, int Dv, const SeqStrides *s);
+int core_fwd_tc(const void *tk, const void *tq, const void *v, const void *beta, int beta_dt,
+                const float *state_in, float *out, float *state_out, int B, int H, int L,
+                const SeqStrides *s, cudaStream_t stream);
 int core_fwd_simt(const void *tk, const void *tq, const void *v, const void *beta, int in_dt,
                   int beta_dt, const float *state_in, float *out, float *state_out, int B, int H,
                   int L, int D, int Dv, const SeqStrides *s, cudaStream_t stream);
@@ -24,6 +29,9 @@ extern "C" int dp_core_fwd(const void *theta_k, const void *theta_q, const void 
              "dp_core_fwd: null input pointer");
   SeqStrides s[5];
   for (int i = 0; i < 5; ++i) s[i] = SeqStrides{strides[3 * i], strides[3 * i + 1], strides[3 * i + 2]};
+  if (core_tc_supported(theta_k, theta_q, v, in_dtype, out, D, Dv, s))
+    return core_fwd_tc(theta_k, theta_q, v, beta, beta_dtype, state_in, out, state_out, B, H, L, s,
+                       as_stream(stream));
   return core_fwd_simt(theta_k, theta_q, v, beta, in_dtype, beta_dtype, state_in, out, state_out,
                        B, H, L, D, Dv, s, as_stream(stream));
 }

@@ -53,6 +53,10 @@ DP_API const char *dp_version(void);
 DP_API const char *dp_last_error(void);
 /* Name of a status code. */
 DP_API const char *dp_status_string(int status);
+/* Synchronises the current device and returns the device-side error word (0, or
+ * DP_ERR_TIMEOUT if a kernel's bounded wait expired since the last clear); clears it
+ * when `clear` is non-zero.  Returns -1 if the CUDA runtime reports an error. */
+DP_API int dp_device_error(int clear);
 
 /*
  * Chunkwise complex delta-rule forward (inference).

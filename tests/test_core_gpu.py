@@ -174,3 +174,8 @@ def test_gram_golden(N, C, D):
     G = dp.gram_matrix_cuda(to_dev(g[f"theta{i}"]), to_dev(g[f"beta{i}"]))
     assert float((G.cpu() - torch.from_numpy(g[f"gram{i}"]).float()).abs().max()) < 1e-3
     assert float(torch.triu(G, 0).abs().max()) == 0.0
+
+
+def test_no_device_side_timeouts_recorded():
+    from delta_phase_b200 import _capi
+    assert _capi.device_error(clear=True) == 0
