@@ -29,6 +29,7 @@ _SIG = {
     "dp_core_fwd": (_I, [_P, _P, _P, _P, _I, _I, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I64P, _P]),
     "dp_core_decode": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _P, _I, _I, _I, _I, _I64P, _P]),
     "dp_gram": (_I, [_P, _P, _I, _I, _P, _I, _I, _I, _P]),
+    "dp_phasor": (_I, [_P, _I, ctypes.c_int64, _P, _P]),
     "dp_laplace_fwd": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _P, _P, _P, _I, _I, _I, _I, _I,
                             _I, _I64P, _P]),
     "dp_ffn_fold": (_I, [_P, _P, _P, _P, _P, _I, _I, _P]),
@@ -186,6 +187,16 @@ def gram(theta, beta, out):
         rc = lib().dp_gram(ptr(theta), ptr(beta), dtype_code(theta), dtype_code(beta), ptr(out), N, C,
                            D, stream_of(dev))
     _check("dp_gram", rc)
+
+
+def phasor(theta, out):
+    """dp_phasor: out (complex64, same shape as theta) = exp(i theta)."""
+    dev = require_cuda(theta, out)
+    th = theta.contiguous()
+    with torch.cuda.device(dev):
+        rc = lib().dp_phasor(ptr(th), dtype_code(th), th.numel(), ptr(torch.view_as_real(out)),
+                             stream_of(dev))
+    _check("dp_phasor", rc)
 
 
 def laplace_fwd(theta_k, logmag_k, theta_q, logmag_q, v, log_decay, beta, chunk_size, state_in,

@@ -50,9 +50,13 @@ constexpr int OFF_U = OFF_TP + 16 * RG_64;       // U, 64 x 64
 constexpr int OFF_S0 = OFF_U + 8 * RG_64;        // S^T bf16, 128 x 64
 constexpr int OFF_STAGE = OFF_S0 + 16 * RG_64;   // 2 x {theta_k, theta_q, v} raw rows
 constexpr int STAGE_BYTES = 3 * kC * 128;
-constexpr int OFF_AF = OFF_STAGE + 2 * STAGE_BYTES;  // A (64 x 64 fp32)
-constexpr int OFF_BETA = OFF_AF + kC * kC * 4;
-constexpr int OFF_BAR = OFF_BETA + kC * 4;
+constexpr int LDA = 68;                              // padded fp32 row stride (bank spread)
+constexpr int OFF_AT = OFF_STAGE + 2 * STAGE_BYTES;  // A^T (64 x 64 fp32): At[k][i] = A[i][k]
+constexpr int OFF_TF = OFF_AT + kC * LDA * 4;        // T = (I + A)^-1, fp32, diagonal blocks
+constexpr int LDY = 36;
+constexpr int OFF_Y = OFF_TF + kC * LDA * 4;         // Y = A[32:, :32] T[:32, :32] (32 x 32)
+constexpr int OFF_BETA = OFF_Y + 32 * LDY * 4;
+constexpr int OFF_BAR = OFF_BETA + 2 * kC * 4;  // beta: two chunk slots
 constexpr int SMEM_BYTES = OFF_BAR + 64;
 
 // tensor-memory columns
@@ -68,7 +72,7 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
 }
 
 // sin/cos of a phase: reduce to [-pi, pi] (x - 2 pi round(x / 2 pi), 2 pi split in two
-// parts), then the hardware approximation; far below bf16 resolution.
+// parts), then the hardware approximation; the error is far below bf16 resolution.
 __device__ __forceinline__ void fast_sincos(float x, float *s, float *c) {
   const float k = rintf(x * 0.15915494309189535f);
   float r = fmaf(-k, 6.28318548202514648f, x);
@@ -122,8 +126,10 @@ __global__ void __launch_bounds__(kThreads, 1) core_tc_kernel(TcArgs a) {
   uint8_t *tp = smem + OFF_TP;
   uint8_t *ub = smem + OFF_U;
   uint8_t *s0 = smem + OFF_S0;
-  float *af = reinterpret_cast<float *>(smem + OFF_AF);
-  float *bs = reinterpret_cast<float *>(smem + OFF_BETA);
+  float *at = reinterpret_cast<float *>(smem + OFF_AT);
+  float *tf = reinterpret_cast<float *>(smem + OFF_TF);
+  float *ys = reinterpret_cast<float *>(smem + OFF_Y);
+  float *bs2 = reinterpret_cast<float *>(smem + OFF_BETA);
   uint64_t *mma_bar = reinterpret_cast<uint64_t *>(smem + OFF_BAR);
   uint64_t *load_bar = mma_bar + 1;  // [2]
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mma_bar + 3);
@@ -156,6 +162,10 @@ __global__ void __launch_bounds__(kThreads, 1) core_tc_kernel(TcArgs a) {
     }
   }
 
+  // the upper-right 32 x 32 block of bT (rows 0..31, columns 32..63 of TP) is zero
+  for (int i = tid; i < 32 * 4; i += kThreads)
+    *reinterpret_cast<uint4 *>(tp + cm_off(i >> 2, 32 + 8 * (i & 3), RG_64)) = make_uint4(0, 0, 0, 0);
+
   // state^T (feature j = lane row, value channel o = column) -> TMEM
   {
     const int j = warp * 32 + lane;
@@ -173,6 +183,11 @@ __global__ void __launch_bounds__(kThreads, 1) core_tc_kernel(TcArgs a) {
   tc_fence_before();
   __syncthreads();
 
+  // beta of chunk 0 (later chunks are prefetched one chunk ahead)
+  if (tid < kC)
+    bs2[tid] = (tid < L) ? load_beta(a.beta, a.beta_dt, b * a.s_b.b + h * a.s_b.h + (int64_t)tid * a.s_b.t) : 0.f;
+  __syncthreads();
+
   uint32_t mma_phase = 0;
   bool failed = false, mma_pending = false;
   int issued = min(nchunks, 2), consumed = 0;  // chunk loads issued / waited for (uniform)
@@ -183,57 +198,65 @@ __global__ void __launch_bounds__(kThreads, 1) core_tc_kernel(TcArgs a) {
     const int nvalid = min(kC, L - t0);
     const int st = c & 1;
     uint8_t *stage = smem + OFF_STAGE + st * STAGE_BYTES;
+    float *bs = bs2 + st * kC;
 
     // ---- phase 0: inputs of this chunk
     bool ok = mbar_wait(&load_bar[st], (uint32_t)((c >> 1) & 1), kTimeoutNs);
     if (__syncthreads_or(!ok)) { failed = true; break; }
     consumed = c + 1;
 
-    // ---- phase 1: phasors (bf16) into the operand tiles, values, beta
+    // ---- phase 1: phasors (bf16) into the operand tiles, values, beta.  Work item
+    //      p = tid + 128 r covers token row p / 8 and channels 8 (p % 8) .. + 7, so a
+    //      warp reads 512 contiguous bytes of the staged rows per step.
     {
-      const int t = tid >> 1, hh = tid & 1;
-      const bool valid = t < nvalid;
-      const __nv_bfloat16 *rk = reinterpret_cast<const __nv_bfloat16 *>(stage + t * 128);
-      const __nv_bfloat16 *rq = reinterpret_cast<const __nv_bfloat16 *>(stage + kC * 128 + t * 128);
-#pragma unroll 2
-      for (int gg = 0; gg < 8; ++gg) {
-        const int g = 8 * hh + gg;  // feature group: channels 4g .. 4g+3
-        uint4 kw = make_uint4(0, 0, 0, 0), qw = make_uint4(0, 0, 0, 0);
-        if (valid) {
-          float s0_, c0_, s1_, c1_, s2_, c2_, s3_, c3_;
-          const uint2 kraw = *reinterpret_cast<const uint2 *>(rk + 4 * g);
-          const __nv_bfloat162 k01 = *reinterpret_cast<const __nv_bfloat162 *>(&kraw.x);
-          const __nv_bfloat162 k23 = *reinterpret_cast<const __nv_bfloat162 *>(&kraw.y);
-          fast_sincos(__low2float(k01), &s0_, &c0_);
-          fast_sincos(__high2float(k01), &s1_, &c1_);
-          fast_sincos(__low2float(k23), &s2_, &c2_);
-          fast_sincos(__high2float(k23), &s3_, &c3_);
-          kw = make_uint4(pack_bf16(c0_, s0_), pack_bf16(c1_, s1_), pack_bf16(c2_, s2_), pack_bf16(c3_, s3_));
-          const uint2 qraw = *reinterpret_cast<const uint2 *>(rq + 4 * g);
-          const __nv_bfloat162 q01 = *reinterpret_cast<const __nv_bfloat162 *>(&qraw.x);
-          const __nv_bfloat162 q23 = *reinterpret_cast<const __nv_bfloat162 *>(&qraw.y);
-          fast_sincos(__low2float(q01), &s0_, &c0_);
-          fast_sincos(__high2float(q01), &s1_, &c1_);
-          fast_sincos(__low2float(q23), &s2_, &c2_);
-          fast_sincos(__high2float(q23), &s3_, &c3_);
-          qw = make_uint4(pack_bf16(c0_, s0_), pack_bf16(c1_, s1_), pack_bf16(c2_, s2_), pack_bf16(c3_, s3_));
-        }
-        *reinterpret_cast<uint4 *>(kvq + cm_off(t, 8 * g, RG_KVQ)) = kw;
-        *reinterpret_cast<uint4 *>(kvq + cm_off(64 + t, 8 * g, RG_KVQ)) = qw;
-        *reinterpret_cast<uint4 *>(wq + cm_off(64 + t, 8 * g, RG_WQ)) = qw;
-      }
-      const uint8_t *rv = stage + 2 * kC * 128 + t * 128;
+      // beta of the next chunk: issue the load now, store it after the phasor work
+      float bnext = 0.f;
+      if (tid < kC && t0 + kC + tid < L)
+        bnext = load_beta(a.beta, a.beta_dt, b * a.s_b.b + h * a.s_b.h + (int64_t)(t0 + kC + tid) * a.s_b.t);
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int vg = 4 * hh + i;  // value channels 8 vg .. 8 vg + 7
-        uint4 w = valid ? *reinterpret_cast<const uint4 *>(rv + vg * 16) : make_uint4(0, 0, 0, 0);
-        *reinterpret_cast<uint4 *>(kvq + cm_off(t, 128 + 8 * vg, RG_KVQ)) = w;
+      for (int r = 0; r < 4; ++r) {
+        const int p = tid + kThreads * r;
+        const int t = p >> 3, sg = p & 7;
+        uint4 kraw = make_uint4(0, 0, 0, 0), qraw = kraw, vraw = kraw;
+        const bool valid = t < nvalid;
+        if (valid) {
+          kraw = *reinterpret_cast<const uint4 *>(stage + t * 128 + sg * 16);
+          qraw = *reinterpret_cast<const uint4 *>(stage + kC * 128 + t * 128 + sg * 16);
+          vraw = *reinterpret_cast<const uint4 *>(stage + 2 * kC * 128 + t * 128 + sg * 16);
+        }
+        const uint32_t kr[4] = {kraw.x, kraw.y, kraw.z, kraw.w};
+        const uint32_t qr[4] = {qraw.x, qraw.y, qraw.z, qraw.w};
+        uint32_t kw[8], qw[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          float s0_, c0_, s1_, c1_;
+          const __nv_bfloat162 kk2 = *reinterpret_cast<const __nv_bfloat162 *>(&kr[i]);
+          fast_sincos(__low2float(kk2), &s0_, &c0_);
+          fast_sincos(__high2float(kk2), &s1_, &c1_);
+          kw[2 * i] = pack_bf16(c0_, s0_);
+          kw[2 * i + 1] = pack_bf16(c1_, s1_);
+          const __nv_bfloat162 qq2 = *reinterpret_cast<const __nv_bfloat162 *>(&qr[i]);
+          fast_sincos(__low2float(qq2), &s0_, &c0_);
+          fast_sincos(__high2float(qq2), &s1_, &c1_);
+          qw[2 * i] = pack_bf16(c0_, s0_);
+          qw[2 * i + 1] = pack_bf16(c1_, s1_);
+        }
+        if (!valid) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) kw[i] = qw[i] = 0u;
+        }
+        // channels 8 sg .. 8 sg + 7 -> features 16 sg .. 16 sg + 15 (two core-matrix columns)
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          const uint4 kv = make_uint4(kw[4 * half], kw[4 * half + 1], kw[4 * half + 2], kw[4 * half + 3]);
+          const uint4 qv = make_uint4(qw[4 * half], qw[4 * half + 1], qw[4 * half + 2], qw[4 * half + 3]);
+          *reinterpret_cast<uint4 *>(kvq + cm_off(t, 16 * sg + 8 * half, RG_KVQ)) = kv;
+          *reinterpret_cast<uint4 *>(kvq + cm_off(64 + t, 16 * sg + 8 * half, RG_KVQ)) = qv;
+          *reinterpret_cast<uint4 *>(wq + cm_off(64 + t, 16 * sg + 8 * half, RG_WQ)) = qv;
+        }
+        *reinterpret_cast<uint4 *>(kvq + cm_off(t, 128 + 8 * sg, RG_KVQ)) = vraw;
       }
-      if (tid < kC)
-        bs[tid] = (tid < nvalid)
-                      ? load_beta(a.beta, a.beta_dt,
-                                  b * a.s_b.b + h * a.s_b.h + (int64_t)(t0 + tid) * a.s_b.t)
-                      : 0.f;
+      if (tid < kC) bs2[(st ^ 1) * kC + tid] = bnext;
     }
     fence_proxy_async_smem();
     __syncthreads();
@@ -260,70 +283,121 @@ __global__ void __launch_bounds__(kThreads, 1) core_tc_kernel(TcArgs a) {
     if (__syncthreads_or(!ok)) { failed = mma_pending = true; break; }
     tc_fence_after();
 
-    // ---- phase 3: A (fp32, rows 0..63) and P = tril(Q K^T) (bf16, rows 64..127 of TP)
-    {
-      const int row = warp * 32 + lane;  // TMEM lane
-      if (warp < 2) {
-        const int t = row;
+    // ---- phase 3: A^T from the (exactly symmetric) Gram rows:  At[k][i] = beta_k G[k][i] / 64
+    //      for i > k (row k of TMEM is thread k of warps 0, 1)
+    if (warp < 2) {
+      const int k = warp * 32 + lane;
+      const float bk = bs[k] * inv64;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          float g[16];
-          tmem_ld16(tmem + lane_base + COL_D1 + 16 * q, g);
-          tmem_ld_wait();
+      for (int q = 0; q < 4; ++q) {
+        float g[16];
+        tmem_ld16(tmem + lane_base + COL_D1 + 16 * q, g);
+        tmem_ld_wait();
 #pragma unroll
-          for (int i = 0; i < 16; i += 4) {
-            const int s = 16 * q + i;
-            float4 w;
-            w.x = (s + 0 < t) ? g[i + 0] * inv64 * bs[s + 0] : 0.f;
-            w.y = (s + 1 < t) ? g[i + 1] * inv64 * bs[s + 1] : 0.f;
-            w.z = (s + 2 < t) ? g[i + 2] * inv64 * bs[s + 2] : 0.f;
-            w.w = (s + 3 < t) ? g[i + 3] * inv64 * bs[s + 3] : 0.f;
-            *reinterpret_cast<float4 *>(af + t * kC + s) = w;
-          }
-        }
-      } else {
-        const int t = row - 64;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          float p[16];
-          tmem_ld16(tmem + lane_base + COL_D1 + 16 * q, p);
-          tmem_ld_wait();
-#pragma unroll
-          for (int half = 0; half < 2; ++half) {
-            const int s = 16 * q + 8 * half;
-            uint4 w;
-            w.x = pack_bf16(s + 0 <= t ? p[8 * half + 0] : 0.f, s + 1 <= t ? p[8 * half + 1] : 0.f);
-            w.y = pack_bf16(s + 2 <= t ? p[8 * half + 2] : 0.f, s + 3 <= t ? p[8 * half + 3] : 0.f);
-            w.z = pack_bf16(s + 4 <= t ? p[8 * half + 4] : 0.f, s + 5 <= t ? p[8 * half + 5] : 0.f);
-            w.w = pack_bf16(s + 6 <= t ? p[8 * half + 6] : 0.f, s + 7 <= t ? p[8 * half + 7] : 0.f);
-            *reinterpret_cast<uint4 *>(tp + cm_off(64 + t, s, RG_64)) = w;
-          }
+        for (int i = 0; i < 16; i += 4) {
+          const int c0 = 16 * q + i;
+          float4 w;
+          w.x = (c0 + 0 > k) ? g[i + 0] * bk : 0.f;
+          w.y = (c0 + 1 > k) ? g[i + 1] * bk : 0.f;
+          w.z = (c0 + 2 > k) ? g[i + 2] * bk : 0.f;
+          w.w = (c0 + 3 > k) ? g[i + 3] * bk : 0.f;
+          *reinterpret_cast<float4 *>(at + k * LDA + c0) = w;
         }
       }
     }
     tc_fence_before();
     __syncthreads();
 
-    // ---- phase 4: T = (I + A)^-1 by forward substitution (thread j owns column j);
-    //      bT = diag(beta) T -> rows 0..63 of TP
-    if (tid < kC) {
-      const int j = tid;
-      float col[kC];
+    // ---- phase 4a: warps 0, 1 invert the 32 x 32 diagonal blocks of (I + A) by
+    //      right-looking substitution (lane = column, the column lives in registers);
+    //      warps 2, 3 meanwhile convert P = tril(Q K^T) to bf16 (rows 64..127 of TP).
+    if (warp < 2) {
+      const int o = warp * 32;  // block offset
+      float col[32];
 #pragma unroll
-      for (int i = 0; i < kC; ++i) {
-        float acc0 = (i == j) ? 1.f : 0.f, acc1 = 0.f;
-        const float *ar = af + i * kC;
+      for (int i = 0; i < 32; ++i) col[i] = (i == lane) ? 1.f : 0.f;
 #pragma unroll
-        for (int k = 0; k + 1 < i; k += 2) {
-          acc0 = fmaf(-ar[k], col[k], acc0);
-          acc1 = fmaf(-ar[k + 1], col[k + 1], acc1);
+      for (int k = 0; k < 31; ++k) {
+        const float tk = col[k];
+        const float *ak = at + (o + k) * LDA + o;  // At[o+k][o+i] = A[o+i][o+k]
+#pragma unroll
+        for (int i4 = ((k + 1) & ~3); i4 < 32; i4 += 4) {
+          const float4 av = *reinterpret_cast<const float4 *>(ak + i4);
+          if (i4 + 0 > k) col[i4 + 0] = fmaf(-av.x, tk, col[i4 + 0]);
+          if (i4 + 1 > k) col[i4 + 1] = fmaf(-av.y, tk, col[i4 + 1]);
+          if (i4 + 2 > k) col[i4 + 2] = fmaf(-av.z, tk, col[i4 + 2]);
+          if (i4 + 3 > k) col[i4 + 3] = fmaf(-av.w, tk, col[i4 + 3]);
         }
-        if (i & 1) acc0 = fmaf(-ar[i - 1], col[i - 1], acc0);
-        col[i] = acc0 + acc1;
       }
 #pragma unroll
-      for (int i = 0; i < kC; ++i)
-        *reinterpret_cast<__nv_bfloat16 *>(tp + cm_off(i, j, RG_64)) = __float2bfloat16_rn(bs[i] * col[i]);
+      for (int i = 0; i < 32; ++i) {
+        tf[(o + i) * LDA + o + lane] = col[i];
+        *reinterpret_cast<__nv_bfloat16 *>(tp + cm_off(o + i, o + lane, RG_64)) =
+            __float2bfloat16_rn(bs[o + i] * col[i]);
+      }
+    } else {
+      const int t = warp * 32 + lane - 64;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float p[16];
+        tmem_ld16(tmem + lane_base + COL_D1 + 16 * q, p);
+        tmem_ld_wait();
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          const int sidx = 16 * q + 8 * half;
+          uint4 w;
+          w.x = pack_bf16(sidx + 0 <= t ? p[8 * half + 0] : 0.f, sidx + 1 <= t ? p[8 * half + 1] : 0.f);
+          w.y = pack_bf16(sidx + 2 <= t ? p[8 * half + 2] : 0.f, sidx + 3 <= t ? p[8 * half + 3] : 0.f);
+          w.z = pack_bf16(sidx + 4 <= t ? p[8 * half + 4] : 0.f, sidx + 5 <= t ? p[8 * half + 5] : 0.f);
+          w.w = pack_bf16(sidx + 6 <= t ? p[8 * half + 6] : 0.f, sidx + 7 <= t ? p[8 * half + 7] : 0.f);
+          *reinterpret_cast<uint4 *>(tp + cm_off(64 + t, sidx, RG_64)) = w;
+        }
+      }
+    }
+    tc_fence_before();
+    __syncthreads();
+
+    // ---- phase 4b: Y = A[32:64, 0:32] T00   (thread: column j, rows 8 ib .. 8 ib + 7)
+    {
+      const int j = lane, ib = warp;
+      float y[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll 8
+      for (int k = 0; k < 32; ++k) {
+        const float tkj = tf[k * LDA + j];
+        const float4 a0 = *reinterpret_cast<const float4 *>(at + k * LDA + 32 + 8 * ib);
+        const float4 a1 = *reinterpret_cast<const float4 *>(at + k * LDA + 36 + 8 * ib);
+        y[0] = fmaf(a0.x, tkj, y[0]); y[1] = fmaf(a0.y, tkj, y[1]);
+        y[2] = fmaf(a0.z, tkj, y[2]); y[3] = fmaf(a0.w, tkj, y[3]);
+        y[4] = fmaf(a1.x, tkj, y[4]); y[5] = fmaf(a1.y, tkj, y[5]);
+        y[6] = fmaf(a1.z, tkj, y[6]); y[7] = fmaf(a1.w, tkj, y[7]);
+      }
+#pragma unroll
+      for (int r = 0; r < 8; ++r) ys[(8 * ib + r) * LDY + j] = y[r];
+    }
+    __syncthreads();
+
+    // ---- phase 4c: T[32:64, 0:32] = -T11 Y, scaled by beta -> bf16 rows 32..63 of TP
+    {
+      const int j = lane, ib = warp;
+      float x[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll 4
+      for (int m = 0; m < 32; m += 4) {
+        const float y0 = ys[(m + 0) * LDY + j], y1 = ys[(m + 1) * LDY + j];
+        const float y2 = ys[(m + 2) * LDY + j], y3 = ys[(m + 3) * LDY + j];
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+          const float4 t4 = *reinterpret_cast<const float4 *>(tf + (32 + 8 * ib + r) * LDA + 32 + m);
+          x[r] = fmaf(t4.x, y0, x[r]);
+          x[r] = fmaf(t4.y, y1, x[r]);
+          x[r] = fmaf(t4.z, y2, x[r]);
+          x[r] = fmaf(t4.w, y3, x[r]);
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        const int i = 32 + 8 * ib + r;
+        *reinterpret_cast<__nv_bfloat16 *>(tp + cm_off(i, j, RG_64)) = __float2bfloat16_rn(-bs[i] * x[r]);
+      }
     }
     fence_proxy_async_smem();
     __syncthreads();
@@ -344,8 +418,7 @@ __global__ void __launch_bounds__(kThreads, 1) core_tc_kernel(TcArgs a) {
     if (__syncthreads_or(!ok)) { failed = mma_pending = true; break; }
     tc_fence_after();
 
-    // ---- phase 6: W = bT K (bf16, rows 0..63 of WQ), keep bT V in registers; S^T -> bf16
-    float ut[64];
+    // ---- phase 6: W = bT K (bf16, rows 0..63 of WQ); S^T -> bf16 (bT V stays in TMEM)
     if (warp < 2) {
       const int t = warp * 32 + lane;
 #pragma unroll
@@ -362,14 +435,6 @@ __global__ void __launch_bounds__(kThreads, 1) core_tc_kernel(TcArgs a) {
           pk.w = pack_bf16(w[8 * half + 6], w[8 * half + 7]);
           *reinterpret_cast<uint4 *>(wq + cm_off(t, 16 * q + 8 * half, RG_WQ)) = pk;
         }
-      }
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        float w[16];
-        tmem_ld16(tmem + lane_base + COL_D2 + 128 + 16 * q, w);
-        tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 16; ++i) ut[16 * q + i] = w[i];
       }
     }
     {
@@ -414,17 +479,19 @@ __global__ void __launch_bounds__(kThreads, 1) core_tc_kernel(TcArgs a) {
       const int t = warp * 32 + lane;
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
-        float ws[16];
+        float ws[16], ut[16];
         tmem_ld16(tmem + lane_base + COL_DC + 16 * q, ws);
+        tmem_ld16(tmem + lane_base + COL_D2 + 128 + 16 * q, ut);
         tmem_ld_wait();
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
           const int o = 16 * q + 8 * half;
+          const int u = 8 * half;
           uint4 pk;
-          pk.x = pack_bf16(ut[o + 0] - ws[8 * half + 0] * inv64, ut[o + 1] - ws[8 * half + 1] * inv64);
-          pk.y = pack_bf16(ut[o + 2] - ws[8 * half + 2] * inv64, ut[o + 3] - ws[8 * half + 3] * inv64);
-          pk.z = pack_bf16(ut[o + 4] - ws[8 * half + 4] * inv64, ut[o + 5] - ws[8 * half + 5] * inv64);
-          pk.w = pack_bf16(ut[o + 6] - ws[8 * half + 6] * inv64, ut[o + 7] - ws[8 * half + 7] * inv64);
+          pk.x = pack_bf16(ut[u + 0] - ws[u + 0] * inv64, ut[u + 1] - ws[u + 1] * inv64);
+          pk.y = pack_bf16(ut[u + 2] - ws[u + 2] * inv64, ut[u + 3] - ws[u + 3] * inv64);
+          pk.z = pack_bf16(ut[u + 4] - ws[u + 4] * inv64, ut[u + 5] - ws[u + 5] * inv64);
+          pk.w = pack_bf16(ut[u + 6] - ws[u + 6] * inv64, ut[u + 7] - ws[u + 7] * inv64);
           *reinterpret_cast<uint4 *>(ub + cm_off(t, o, RG_64)) = pk;
         }
       }

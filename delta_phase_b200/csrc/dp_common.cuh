@@ -66,6 +66,33 @@ __device__ __forceinline__ void phase_sincos(T th, float *s, float *c) {
   sincosf(to_f32(th), s, c);
 }
 
+// sin and cos of x on the FMA pipe (no special-function unit): Cody-Waite reduction
+// x = k pi/2 + r, |r| <= pi/4 (pi/2 split in a float head and tail), Taylor series of
+// sin (to r^7) and cos (to r^8) on the reduced argument, quadrant fix-up from k mod 4.
+// Truncation error < 4e-7 on |r| <= pi/4; max abs error ~2e-6 for |x| <= 20 (the
+// reduction's rounding grows with |x|).
+__device__ __forceinline__ void poly_sincos(float x, float *s_out, float *c_out) {
+  const float kf = fmaf(x, 0.63661977236758134f, 12582912.0f);  // 1.5 * 2^23 rounds k
+  const float k = kf - 12582912.0f;
+  const int q = __float_as_int(kf);
+  float r = fmaf(-k, 1.5707963705062866f, x);
+  r = fmaf(-k, -4.371138828673793e-08f, r);
+  const float r2 = r * r;
+  float ps = fmaf(r2, -1.9841270113829523e-04f, 8.3333337679505348e-03f);
+  ps = fmaf(r2, ps, -0.16666667163372040f);
+  const float sn = fmaf(r * r2, ps, r);
+  float pc = fmaf(r2, 2.4801587642286904e-05f, -1.3888889225199819e-03f);
+  pc = fmaf(r2, pc, 4.1666667908430100e-02f);
+  pc = fmaf(r2, pc, -0.5f);
+  const float cs = fmaf(r2, pc, 1.0f);
+  const bool swap = q & 1;
+  float so = swap ? cs : sn, co = swap ? sn : cs;
+  so = __uint_as_float(__float_as_uint(so) ^ (((unsigned)q & 2u) << 30));
+  co = __uint_as_float(__float_as_uint(co) ^ (((unsigned)(q + 1) & 2u) << 30));
+  *s_out = so;
+  *c_out = co;
+}
+
 struct SeqStrides {  // element strides of a (B, H, L, C) tensor with unit channel stride
   int64_t b, h, t;
 };

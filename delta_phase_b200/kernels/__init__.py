@@ -9,6 +9,7 @@ from .chunk_delta import (
     gram_matrix_cuda,
     gram_matrix_triton,
     laplace_chunkwise,
+    phasor,
     triton_available,
 )
 
@@ -23,4 +24,5 @@ __all__ = [
     "gram_matrix_cuda",
     "gram_matrix_triton",
     "laplace_chunkwise",
+    "phasor",
 ]

@@ -23,6 +23,16 @@ import torch
 from .. import _capi
 
 
+def phasor(theta: torch.Tensor) -> torch.Tensor:
+    """exp(i theta) as complex64 (layers.py:203-206 / triton_chunk_delta.py:220-221)."""
+    _capi.require_cuda(theta)
+    if theta.dtype == torch.float64:
+        raise TypeError("float64 inputs are not supported by the CUDA path")
+    out = torch.empty(theta.shape, device=theta.device, dtype=torch.complex64)
+    _capi.phasor(theta, out)
+    return out
+
+
 def cuda_available() -> bool:
     """True if the deltaphase_b200 library loads and a CUDA device is present."""
     return torch.cuda.is_available() and _capi.library_available()

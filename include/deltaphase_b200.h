@@ -82,6 +82,16 @@ DP_API int dp_core_fwd(const void *theta_k, const void *theta_q, const void *v, 
                 const int64_t *strides, void *stream);
 
 /*
+ * Phasors e^{i theta} = cos theta + i sin theta of n phases, written as interleaved
+ * complex64 (out[2i] = cos, out[2i+1] = sin).  The elementwise step of
+ * DeltaPhaseHolographicBlock.forward/step (delta_phase/layers.py:203-206, 275-278) and
+ * of _chunkwise_delta_reference (delta_phase/kernels/triton_chunk_delta.py:220-221);
+ * the fused kernels compute the same values in registers.  Max abs error ~2e-6 for
+ * |theta| <= 20 (FMA-pipe Cody-Waite reduction + Taylor series).
+ */
+DP_API int dp_phasor(const void *theta, int dtype, int64_t n, float *out, void *stream);
+
+/*
  * Single-token decode step: v_old = Re(M conj(k))/D; M += beta (v - v_old) k^T;
  * out = Re(M conj(q))/D (read after the update).
  * Replaces the state update of DeltaPhaseHolographicBlock.step

@@ -179,3 +179,15 @@ def test_gram_golden(N, C, D):
 def test_no_device_side_timeouts_recorded():
     from delta_phase_b200 import _capi
     assert _capi.device_error(clear=True) == 0
+
+
+def test_phasor_matches_cuda_sincos():
+    """The FMA-pipe sin/cos (Cody-Waite + Taylor) against CUDA's own sin/cos."""
+    from delta_phase_b200.kernels import phasor
+    x = torch.linspace(-20, 20, 400001, device="cuda")
+    z = phasor(x)
+    assert float((z.real - torch.cos(x)).abs().max()) < 4e-6
+    assert float((z.imag - torch.sin(x)).abs().max()) < 4e-6
+    xb = (torch.rand(1 << 16, device="cuda") * 2 * np.pi).to(torch.bfloat16)
+    zb = phasor(xb)
+    assert float((zb.real - torch.cos(xb.float())).abs().max()) < 1e-6
