@@ -35,6 +35,8 @@ _SIG = {
     "dp_ffn_fold": (_I, [_P, _P, _P, _P, _P, _I, _I, _P]),
     "dp_ffn_workspace_size": (ctypes.c_size_t, [_I, _I, _I]),
     "dp_ffn_fwd": (_I, [_P, _I, _P, _P, _P, _I, _I, _P, ctypes.c_size_t, _P]),
+    "dp_ffn_fwd_noalloc": (_I, [_P, _I, _P, _P, _P, _I, _I, _P]),
+    "dp_ffn_noalloc_max_tokens": (ctypes.c_size_t, [_I, _I]),
 }
 
 _lib = None
@@ -238,3 +240,18 @@ def ffn_fwd(x, dct, F, y, workspace):
                               ptr(workspace), workspace.numel() * workspace.element_size(),
                               stream_of(dev))
     _check("dp_ffn_fwd", rc)
+
+
+def ffn_fwd_noalloc(x, dct, F, y):
+    """dp_ffn_fwd_noalloc: the FFN forward with the library's fixed device scratch
+    instead of a workspace (for callers that cannot allocate; see the header)."""
+    dev = require_cuda(x, dct, F, y)
+    tokens, d = x.shape
+    with torch.cuda.device(dev):
+        rc = lib().dp_ffn_fwd_noalloc(ptr(x), dtype_code(x), ptr(dct), ptr(F), ptr(y), tokens, d,
+                                      stream_of(dev))
+    _check("dp_ffn_fwd_noalloc", rc)
+
+
+def ffn_noalloc_max_tokens(d, dtype):
+    return int(lib().dp_ffn_noalloc_max_tokens(d, _DTYPE_CODES[dtype]))

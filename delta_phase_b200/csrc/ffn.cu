@@ -17,6 +17,8 @@
 #include <cublas_v2.h>
 
 #include <array>
+#include <mutex>
+#include <string>
 
 #include "dp_common.cuh"
 
@@ -220,4 +222,159 @@ extern "C" int dp_ffn_fwd(const void *x, int x_dtype, const void *dct, const voi
                     &zero, y, ab, d, ct, CUBLAS_GEMM_DEFAULT);
   DP_REQUIRE(cs == CUBLAS_STATUS_SUCCESS, DP_ERR_CUDA, "dp_ffn_fwd: combine GEMM failed");
   return DP_OK;
+}
+
+// ---------------------------------------------------------------------------------
+// Allocation-free FFN forward (dp_ffn_fwd_noalloc).
+//
+// Some callers cannot allocate device memory where they run the FFN: code being
+// captured into a CUDA graph (cudaMalloc is not a capturable operation), host runtimes
+// that hand the whole device heap to their own allocator and forbid any other
+// allocation, and latency-bound decode loops that must never block on the driver's
+// allocator.  This entry point takes its scratch -- the DCT projections and the
+// sin/cos features of the tokens -- from the fixed array below, which lives in the
+// library's device image, and it runs its two GEMMs with a CUDA-core kernel of this
+// file instead of cuBLAS (creating a cuBLAS handle allocates).
+//
+// The array is kFfnScratchBytes on every GPU that loads the library, held until the
+// process exits.  All calls share it and it keeps the last call's contents; nothing in
+// it has to start at zero (every scratch element a call reads is written by that call
+// first), but calls that overlap on the GPU -- concurrent streams, or another host
+// thread -- race on it and must be serialised by the caller.
+static __device__ __align__(256) unsigned char g_ffn_scratch[8u << 20];
+
+namespace dp {
+namespace {
+
+constexpr size_t kFfnScratchBytes = 8u << 20;
+
+template <typename T>
+__device__ __forceinline__ float ld_f32(const T *p, int64_t i) { return to_f32(p[i]); }
+
+// C[m][n] = sum_k A[m][k] B(k, n), B(k, n) = B[k ldb + n] or, if B_TRANS, B[n ldb + k].
+// 64 x 64 output tile per CTA, 4 x 4 per thread, fp32 accumulation.
+template <typename TA, typename TB, typename TC, bool B_TRANS>
+__global__ void __launch_bounds__(256)
+small_gemm_kernel(const TA *__restrict__ A, int lda, const TB *__restrict__ B, int ldb,
+                  TC *__restrict__ C, int ldc, int M, int N, int K) {
+  __shared__ float As[16][64 + 4];
+  __shared__ float Bs[16][64 + 4];
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  const int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
+  float acc[4][4] = {};
+  for (int k0 = 0; k0 < K; k0 += 16) {
+    for (int i = threadIdx.x; i < 64 * 16; i += 256) {
+      const int m = i >> 4, k = i & 15;
+      As[k][m] = (m0 + m < M && k0 + k < K) ? ld_f32(A, (int64_t)(m0 + m) * lda + k0 + k) : 0.f;
+      int n, kb;
+      if (B_TRANS) { n = i >> 4; kb = i & 15; } else { kb = i >> 6; n = i & 63; }
+      float bv = 0.f;
+      if (n0 + n < N && k0 + kb < K)
+        bv = B_TRANS ? ld_f32(B, (int64_t)(n0 + n) * ldb + k0 + kb) : ld_f32(B, (int64_t)(k0 + kb) * ldb + n0 + n);
+      Bs[kb][n] = bv;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      float a[4], b[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        a[i] = As[k][ty * 4 + i];
+        b[i] = Bs[k][tx * 4 + i];
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int m = m0 + ty * 4 + i, n = n0 + tx * 4 + j;
+      if (m < M && n < N) C[(int64_t)m * ldc + n] = from_f32<TC>(acc[i][j]);
+    }
+}
+
+// Device address of g_ffn_scratch on the current device.  Looked up once per device,
+// with that device current, and cached; the lookup is the only set-up step.
+int ffn_scratch_address(void **out) {
+  static std::mutex mu;
+  static void *addr[64] = {nullptr};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(DP_ERR_CUDA, std::string("dp_ffn_fwd_noalloc: ") + cudaGetErrorString(e));
+  if (dev < 0 || dev >= 64) return set_error(DP_ERR_UNSUPPORTED, "dp_ffn_fwd_noalloc: device ordinal >= 64");
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[dev]) {
+    void *p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_ffn_scratch);
+    if (e != cudaSuccess || p == nullptr)
+      return set_error(DP_ERR_CUDA, std::string("dp_ffn_fwd_noalloc: cudaGetSymbolAddress failed: ") +
+                                        cudaGetErrorString(e));
+    addr[dev] = p;
+  }
+  *out = addr[dev];
+  return DP_OK;
+}
+
+template <typename T>
+int ffn_fwd_noalloc_typed(const T *x, const T *dct, const T *F, T *y, int tokens, int d,
+                          unsigned char *scratch, cudaStream_t st) {
+  float *hdct = reinterpret_cast<float *>(scratch);
+  T *z = reinterpret_cast<T *>(scratch + (((size_t)tokens * d * sizeof(float) + 255) & ~(size_t)255));
+  dim3 g1((d + 63) / 64, (tokens + 63) / 64);
+  small_gemm_kernel<T, T, float, true><<<g1, 256, 0, st>>>(x, d, dct, d, hdct, d, tokens, d, d);
+  int rc = check_launch("small_gemm_kernel (DCT)");
+  if (rc != DP_OK) return rc;
+  int log2d = 0;
+  while ((1 << log2d) < d) ++log2d;
+  const size_t smem = 4 * (size_t)d * sizeof(float);
+  cudaFuncSetAttribute(ffn_features_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  ffn_features_kernel<T><<<tokens, d >= 256 ? 256 : d, smem, st>>>(x, hdct, z, d, log2d);
+  rc = check_launch("ffn_features_kernel");
+  if (rc != DP_OK) return rc;
+  dim3 g2((d + 63) / 64, (tokens + 63) / 64);
+  small_gemm_kernel<T, T, T, false><<<g2, 256, 0, st>>>(z, 6 * d, F, d, y, d, tokens, d, 6 * d);
+  return check_launch("small_gemm_kernel (combine)");
+}
+
+}  // namespace
+}  // namespace dp
+
+extern "C" size_t dp_ffn_noalloc_max_tokens(int d, int x_dtype) {
+  if (d <= 0 || !(x_dtype == DP_F32 || x_dtype == DP_BF16)) return 0;
+  const size_t per_token = (size_t)d * sizeof(float) + (size_t)6 * d * dp::dtype_size(x_dtype);
+  return (dp::kFfnScratchBytes - 256) / per_token;
+}
+
+extern "C" int dp_ffn_fwd_noalloc(const void *x, int x_dtype, const void *dct, const void *F, void *y,
+                                  int tokens, int d, void *stream) {
+  using namespace dp;
+  DP_REQUIRE(tokens >= 0 && d >= 1, DP_ERR_INVALID_ARGUMENT, "dp_ffn_fwd_noalloc: bad sizes");
+  DP_REQUIRE(x_dtype == DP_F32 || x_dtype == DP_BF16, DP_ERR_INVALID_ARGUMENT,
+             "dp_ffn_fwd_noalloc: x dtype must be float32 or bfloat16");
+  DP_REQUIRE((d & (d - 1)) == 0 && d >= 8 && d <= 4096, DP_ERR_UNSUPPORTED,
+             "dp_ffn_fwd_noalloc: d must be a power of two in [8, 4096]");
+  const size_t max_tokens = dp_ffn_noalloc_max_tokens(d, x_dtype);
+  if ((size_t)tokens > max_tokens)
+    return set_error(DP_ERR_WORKSPACE,
+                     "dp_ffn_fwd_noalloc: " + std::to_string(tokens) + " tokens exceed the 8 MiB static "
+                     "scratch (at most " + std::to_string(max_tokens) + " tokens at d=" + std::to_string(d) +
+                     "); call dp_ffn_fwd with a workspace, or split the tokens");
+  if (tokens == 0) return DP_OK;
+  DP_REQUIRE(x && dct && F && y, DP_ERR_INVALID_ARGUMENT, "dp_ffn_fwd_noalloc: null pointer");
+  void *scratch = nullptr;
+  int rc = ffn_scratch_address(&scratch);
+  if (rc != DP_OK) return rc;
+  unsigned char *sp = static_cast<unsigned char *>(scratch);
+  cudaStream_t st = as_stream(stream);
+  if (x_dtype == DP_BF16)
+    return ffn_fwd_noalloc_typed(static_cast<const __nv_bfloat16 *>(x), static_cast<const __nv_bfloat16 *>(dct),
+                                 static_cast<const __nv_bfloat16 *>(F), static_cast<__nv_bfloat16 *>(y), tokens,
+                                 d, sp, st);
+  return ffn_fwd_noalloc_typed(static_cast<const float *>(x), static_cast<const float *>(dct),
+                               static_cast<const float *>(F), static_cast<float *>(y), tokens, d, sp, st);
 }

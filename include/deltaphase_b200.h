@@ -172,6 +172,24 @@ DP_API size_t dp_ffn_workspace_size(int tokens, int d, int x_dtype);
 DP_API int dp_ffn_fwd(const void *x, int x_dtype, const void *dct, const void *F, void *y, int tokens,
                int d, void *workspace, size_t workspace_bytes, void *stream);
 
+/*
+ * Allocation-free variant of dp_ffn_fwd.  It has no counterpart in the reference.
+ * For callers that cannot allocate device memory where they run the FFN: code being
+ * captured into a CUDA graph (cudaMalloc cannot be captured), runtimes whose own
+ * allocator owns the device heap, and decode loops that must not block on the
+ * driver's allocator.  Same arguments and results as dp_ffn_fwd, but no workspace: the
+ * scratch is a fixed 8 MiB array in the library's device image (held on every GPU that
+ * loads the library until exit), and the GEMMs run on CUDA cores instead of cuBLAS.
+ * Limit: tokens <= dp_ffn_noalloc_max_tokens(d, x_dtype) (511 at d = 1024 with bf16 x);
+ * larger calls fail with DP_ERR_WORKSPACE.  The first call on a device looks up the
+ * array's device address (cudaGetSymbolAddress), so make it before any stream capture.
+ * Calls share the array: calls that overlap on the GPU race and must be serialised.
+ */
+DP_API int dp_ffn_fwd_noalloc(const void *x, int x_dtype, const void *dct, const void *F, void *y,
+                              int tokens, int d, void *stream);
+/* Largest token count dp_ffn_fwd_noalloc accepts for width d and dtype x_dtype. */
+DP_API size_t dp_ffn_noalloc_max_tokens(int d, int x_dtype);
+
 #ifdef __cplusplus
 }
 #endif
