@@ -7,21 +7,23 @@
 // Real form (see core_simt.cu): per chunk of 64 tokens with key features K (64 x 128,
 // interleaved cos/sin), query features Q, values V, write strengths beta and the state
 // S (64 x 128, fp32, kept transposed in tensor memory for the whole sequence):
-//   G1:  [K; Q] K^T           -> K K^T (Gram) and Q K^T            (TMEM, fp32)
-//        A = strict_lower(K K^T / 64) diag(beta);  T = (I + A)^-1  (CUDA cores, fp32)
-//   G2:  [bT; P] [K | V]      -> bT K and bT V,   bT = diag(beta) T,  P = tril(Q K^T)
-//   G3:  [W; Q] S^T           -> W S^T, Q S^T,    W = bT K
-//        U = bT V - W S^T / 64                                    (the delta-rule writes)
-//   G4:  S^T += K^T U         (state update, accumulated in TMEM)
-//   G5:  Q S^T += P U   ->  64 * output rows of the chunk
-// All five products are tcgen05.mma (kind::f16, bf16 operands from shared memory,
-// fp32 accumulators in tensor memory) issued by one thread.  Operand tiles use the
-// SWIZZLE_NONE core-matrix layout (8 rows x 16 bytes per core matrix), so the same
-// buffer serves as a K-major or MN-major operand by swapping the two stride fields:
-// K is read as A (G1), B (G1), B (G2) and A^T (G4) without copies.
+//   A = strict_lower(K K^T / 64) diag(beta),  bT = diag(beta) (I + A)^-1
+//   W = bT K,  Ut = bT V,  P = tril(Q K^T)            (independent of the state)
+//   U = Ut - W S^T / 64;  O = (Q S^T + P U) / 64;  S^T += K^T U   (the state chain)
 //
-// One CTA of 128 threads per (batch, head); inputs stream in with bulk async copies
-// (cp.async.bulk + mbarrier, two stages ahead); every wait is bounded.
+// Two warp-specialised roles share one CTA per (batch, head):
+//   * prep (8 warps) computes the state-independent work of chunk c+1 while
+//   * chain (4 warps) runs the recurrence of chunk c.
+// Prep: phasors (bf16) from bulk-copied inputs; G1 = [K; Q] K^T (tcgen05, M=128);
+// A and P from the Gram rows; T = (I + A)^-1 in fp32 (16 x 16 diagonal blocks by
+// right-looking substitution, two block-merge levels); G2 = bT [K | V] (M=64); W to
+// shared memory.  Chain: S^T -> bf16; G3 = W S^T and Q S^T (M=64); U; G4 S^T += K^T U
+// (M=128, accumulated in TMEM) and G5 Q S^T += P U (M=64); outputs.  Buffers the
+// chain reads are double-buffered; hand-off uses mbarriers (ready / free per slot).
+// Operand tiles use the SWIZZLE_NONE core-matrix layout (8 rows x 16 bytes), so one
+// buffer is a K-major or MN-major operand by swapping the two descriptor strides: K is
+// read as A and B of G1, B of G2 and A^T of G4 without copies.  M=64 accumulators put
+// row m in TMEM lane (m % 16) + 32 (m / 16).  Every wait is bounded.
 #include "dp_common.cuh"
 #include "tc_ptx.cuh"
 
@@ -36,31 +38,44 @@ using namespace ptx;
 constexpr int kC = 64;     // tokens per chunk
 constexpr int kF = 128;    // key features (2 * d_k)
 constexpr int kDv = 64;    // value channels
-constexpr int kThreads = 128;
+constexpr int kPrepThreads = 256;   // warps 0..7
+constexpr int kChainThreads = 128;  // warps 8..11
+constexpr int kThreads = kPrepThreads + kChainThreads;
+constexpr int BAR_PREP = 1, BAR_CHAIN = 2;
 constexpr uint64_t kTimeoutNs = 2000000000ull;  // 2 s per wait
 
-// shared-memory map (bytes)
-constexpr int RG_KVQ = 24 * 128;                 // row group: 16 feature groups + 8 value groups
-constexpr int OFF_KVQ = 0;                       // [K | V] rows 0..63, [Q] rows 64..127
-constexpr int OFF_WQ = OFF_KVQ + 16 * RG_KVQ;    // [W; Q], 128 x 128
-constexpr int RG_WQ = 16 * 128;
-constexpr int OFF_TP = OFF_WQ + 16 * RG_WQ;      // [bT; P], 128 x 64
+// shared-memory map (bytes).  bf16 tiles: row group (8 rows) of a 128- or 64-wide tile.
+constexpr int RG_KQ = 16 * 128;
 constexpr int RG_64 = 8 * 128;
-constexpr int OFF_U = OFF_TP + 16 * RG_64;       // U, 64 x 64
-constexpr int OFF_S0 = OFF_U + 8 * RG_64;        // S^T bf16, 128 x 64
-constexpr int OFF_STAGE = OFF_S0 + 16 * RG_64;   // 2 x {theta_k, theta_q, v} raw rows
+constexpr int KQ_BYTES = 16 * RG_KQ;                 // rows 0..63 K, rows 64..127 Q
+constexpr int W_BYTES = 8 * RG_KQ;
+constexpr int P_BYTES = 8 * RG_64;
+constexpr int OFF_KQ = 0;                            // [2 slots]
+constexpr int OFF_W = OFF_KQ + 2 * KQ_BYTES;         // [2 slots]
+constexpr int OFF_P = OFF_W + 2 * W_BYTES;           // [2 slots]
+constexpr int OFF_V = OFF_P + 2 * P_BYTES;           // prep only
+constexpr int OFF_T = OFF_V + 8 * RG_64;             // bT bf16, prep only
+constexpr int OFF_U = OFF_T + 8 * RG_64;             // chain only
+constexpr int OFF_S0 = OFF_U + 8 * RG_64;            // S^T bf16 (128 x 64), chain only
+constexpr int OFF_STAGE = OFF_S0 + 16 * RG_64;       // raw theta_k, theta_q, v rows of a chunk
 constexpr int STAGE_BYTES = 3 * kC * 128;
-constexpr int LDA = 68;                              // padded fp32 row stride (bank spread)
-constexpr int OFF_AT = OFF_STAGE + 2 * STAGE_BYTES;  // A^T (64 x 64 fp32): At[k][i] = A[i][k]
-constexpr int OFF_TF = OFF_AT + kC * LDA * 4;        // T = (I + A)^-1, fp32, diagonal blocks
-constexpr int LDY = 36;
-constexpr int OFF_Y = OFF_TF + kC * LDA * 4;         // Y = A[32:, :32] T[:32, :32] (32 x 32)
-constexpr int OFF_BETA = OFF_Y + 32 * LDY * 4;
-constexpr int OFF_BAR = OFF_BETA + 2 * kC * 4;  // beta: two chunk slots
-constexpr int SMEM_BYTES = OFF_BAR + 64;
+constexpr int LDA = 68;                              // padded fp32 row stride
+constexpr int OFF_AT = OFF_STAGE + STAGE_BYTES;      // A^T fp32: At[k][i] = A[i][k]
+constexpr int OFF_TF = OFF_AT + kC * LDA * 4;        // T = (I + A)^-1 fp32
+constexpr int LDZ = 36;
+constexpr int OFF_Z = OFF_TF + kC * LDA * 4;         // block-merge scratch fp32 (32 x LDZ)
+constexpr int OFF_BETA = OFF_Z + 32 * LDZ * 4;       // beta, 2 chunk slots
+constexpr int OFF_BAR = OFF_BETA + 2 * kC * 4;
+constexpr int SMEM_BYTES = OFF_BAR + 128;
 
-// tensor-memory columns
-constexpr uint32_t COL_S = 0, COL_D1 = 64, COL_D2 = 128, COL_DC = 320, TMEM_COLS = 512;
+// tensor-memory columns (fp32)
+constexpr uint32_t COL_S = 0;      // S^T, M = 128 (lane = feature)
+constexpr uint32_t COL_D1 = 64;    // [K;Q] K^T, M = 128 (prep)
+constexpr uint32_t COL_D2W = 128;  // bT K, M = 64 (prep)
+constexpr uint32_t COL_DU = 256;   // bT V, M = 64, 2 slots (prep writes, chain reads)
+constexpr uint32_t COL_DCA = 384;  // W S^T, M = 64 (chain)
+constexpr uint32_t COL_DCB = 448;  // Q S^T + P U, M = 64 (chain)
+constexpr uint32_t TMEM_COLS = 512;
 
 __device__ __forceinline__ uint32_t cm_off(int r, int k, int rg) {
   return (uint32_t)((r >> 3) * rg + (k >> 3) * 128 + (r & 7) * 16 + (k & 7) * 2);
@@ -71,10 +86,11 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
   return *reinterpret_cast<uint32_t *>(&h);
 }
 
-// sin/cos of a phase: reduce to [-pi, pi] (x - 2 pi round(x / 2 pi), 2 pi split in two
-// parts), then the hardware approximation; the error is far below bf16 resolution.
+// sin/cos of a phase: reduce to [-pi, pi] (x - 2 pi round(x / 2 pi), with the rounding
+// done on the FMA pipe by the 1.5 * 2^23 trick and 2 pi split in two parts), then the
+// hardware approximation; the error is far below bf16 resolution.
 __device__ __forceinline__ void fast_sincos(float x, float *s, float *c) {
-  const float k = rintf(x * 0.15915494309189535f);
+  const float k = fmaf(x, 0.15915494309189535f, 12582912.0f) - 12582912.0f;
   float r = fmaf(-k, 6.28318548202514648f, x);
   r = fmaf(-k, -1.7484556e-07f, r);
   __sincosf(r, s, c);
@@ -98,8 +114,8 @@ struct TcArgs {
   int *err;
 };
 
-// Issue the bulk copies of chunk `c0` (rows [c0, c0 + n)) of one (b, h) into a stage.
-// Executed by one full warp; lane 0 registers the expected bytes first.
+// Bulk copies of chunk rows [c0, c0 + n) of one (b, h) into the stage (one full warp;
+// lane 0 registers the expected bytes first).
 __device__ __forceinline__ void issue_chunk_loads(const TcArgs &a, int b, int h, int c0, int n,
                                                   uint8_t *stage, uint64_t *bar, int lane) {
   if (lane == 0) mbar_arrive_expect_tx(bar, (uint32_t)(3 * n * 128));
@@ -119,106 +135,68 @@ __device__ __forceinline__ void issue_chunk_loads(const TcArgs &a, int b, int h,
   }
 }
 
-__global__ void __launch_bounds__(kThreads, 1) core_tc_kernel(TcArgs a) {
-  extern __shared__ __align__(1024) uint8_t smem[];
-  uint8_t *kvq = smem + OFF_KVQ;
-  uint8_t *wq = smem + OFF_WQ;
-  uint8_t *tp = smem + OFF_TP;
-  uint8_t *ub = smem + OFF_U;
-  uint8_t *s0 = smem + OFF_S0;
+struct Bars {
+  uint64_t load, prep_mma, chain_mma, ready[2], free_[2];
+};
+
+// ------------------------------------------------------------------------------ prep
+// Returns false if a bounded wait expired (after letting its own copies / MMAs land).
+__device__ bool prep_role(const TcArgs &a, uint8_t *smem, Bars *bars, uint32_t tmem, int b, int h,
+                          int nchunks) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int q = warp & 3, hf = warp >> 2;  // TMEM lane quarter, column half
+  const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+  const int L = a.L;
+  uint8_t *stage = smem + OFF_STAGE;
+  uint8_t *vb = smem + OFF_V;
+  uint8_t *tb = smem + OFF_T;
   float *at = reinterpret_cast<float *>(smem + OFF_AT);
   float *tf = reinterpret_cast<float *>(smem + OFF_TF);
-  float *ys = reinterpret_cast<float *>(smem + OFF_Y);
+  float *zs = reinterpret_cast<float *>(smem + OFF_Z);
   float *bs2 = reinterpret_cast<float *>(smem + OFF_BETA);
-  uint64_t *mma_bar = reinterpret_cast<uint64_t *>(smem + OFF_BAR);
-  uint64_t *load_bar = mma_bar + 1;  // [2]
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mma_bar + 3);
-
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int bh = blockIdx.x, b = bh / a.H, h = bh % a.H;
-  const int L = a.L;
-  const int nchunks = (L + kC - 1) / kC;
-
-  if (tid == 0) {
-    mbar_init(mma_bar, 1);
-    mbar_init(&load_bar[0], 1);
-    mbar_init(&load_bar[1], 1);
-    fence_mbar_init();
-  }
-  if (warp == 0) {
-    tmem_alloc(tmem_slot, TMEM_COLS);
-    tmem_relinquish();
-  }
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-  const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-
-  // prefetch the first two chunks
-  if (warp == 3) {
-    for (int c = 0; c < 2 && c < nchunks; ++c) {
-      const int n = min(kC, L - c * kC);
-      issue_chunk_loads(a, b, h, c * kC, n, smem + OFF_STAGE + c * STAGE_BYTES, &load_bar[c], lane);
-    }
-  }
-
-  // the upper-right 32 x 32 block of bT (rows 0..31, columns 32..63 of TP) is zero
-  for (int i = tid; i < 32 * 4; i += kThreads)
-    *reinterpret_cast<uint4 *>(tp + cm_off(i >> 2, 32 + 8 * (i & 3), RG_64)) = make_uint4(0, 0, 0, 0);
-
-  // state^T (feature j = lane row, value channel o = column) -> TMEM
-  {
-    const int j = warp * 32 + lane;
-    const int64_t base = (int64_t)bh * kDv * kF;
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      float vals[16];
-#pragma unroll
-      for (int i = 0; i < 16; ++i)
-        vals[i] = a.state_in ? a.state_in[base + (int64_t)(16 * q + i) * kF + j] : 0.f;
-      tmem_st16(tmem + lane_base + COL_S + 16 * q, vals);
-    }
-    tmem_st_wait();
-  }
-  tc_fence_before();
-  __syncthreads();
-
-  // beta of chunk 0 (later chunks are prefetched one chunk ahead)
-  if (tid < kC)
-    bs2[tid] = (tid < L) ? load_beta(a.beta, a.beta_dt, b * a.s_b.b + h * a.s_b.h + (int64_t)tid * a.s_b.t) : 0.f;
-  __syncthreads();
-
-  uint32_t mma_phase = 0;
-  bool failed = false, mma_pending = false;
-  int issued = min(nchunks, 2), consumed = 0;  // chunk loads issued / waited for (uniform)
   const float inv64 = 1.0f / 64.0f;
 
-  for (int c = 0; c < nchunks && !failed; ++c) {
-    const int t0 = c * kC;
-    const int nvalid = min(kC, L - t0);
-    const int st = c & 1;
-    uint8_t *stage = smem + OFF_STAGE + st * STAGE_BYTES;
-    float *bs = bs2 + st * kC;
+  int issued = 0, consumed = 0;
+  uint32_t pm_phase = 0;
+  bool mma_pending = false, ok = true;
+  if (nchunks > 0) {
+    if (warp == 0) issue_chunk_loads(a, b, h, 0, min(kC, L), stage, &bars->load, lane);
+    issued = 1;
+  }
+  if (tid < kC)
+    bs2[tid] = (tid < L) ? load_beta(a.beta, a.beta_dt, b * a.s_b.b + h * a.s_b.h + (int64_t)tid * a.s_b.t) : 0.f;
+  group_sync(BAR_PREP, kPrepThreads);
 
-    // ---- phase 0: inputs of this chunk
-    bool ok = mbar_wait(&load_bar[st], (uint32_t)((c >> 1) & 1), kTimeoutNs);
-    if (__syncthreads_or(!ok)) { failed = true; break; }
+  for (int c = 0; c < nchunks; ++c) {
+    const int slot = c & 1, t0 = c * kC, nvalid = min(kC, L - t0);
+    uint8_t *kq = smem + OFF_KQ + slot * KQ_BYTES;
+    uint8_t *wb = smem + OFF_W + slot * W_BYTES;
+    uint8_t *pb = smem + OFF_P + slot * P_BYTES;
+    const float *bs = bs2 + slot * kC;
+
+    // the chain must be done with this slot (chunk c - 2)
+    // one thread polls the mbarriers; the others wait in the hardware barrier
+    if (tid == 0) {
+      if (c >= 2) ok = mbar_wait(&bars->free_[slot], (uint32_t)(((c - 2) >> 1) & 1), kTimeoutNs);
+      if (ok) ok = mbar_wait(&bars->load, (uint32_t)(c & 1), kTimeoutNs);
+    }
+    if (group_any(!ok, BAR_PREP, kPrepThreads)) { ok = false; break; }
     consumed = c + 1;
 
-    // ---- phase 1: phasors (bf16) into the operand tiles, values, beta.  Work item
-    //      p = tid + 128 r covers token row p / 8 and channels 8 (p % 8) .. + 7, so a
-    //      warp reads 512 contiguous bytes of the staged rows per step.
+    // ---- P1: phasors (bf16) -> K, Q tiles; values -> V tile; beta of the next chunk.
+    //      Warp w covers token rows 8w .. 8w+7, lane l = 8a + b: row 8w + b, channel
+    //      segment (a + 2b + 4r) % 8 in pass r.  Each load from the staged rows then hits
+    //      every 16-byte bank group 4 times (segment), and so does each store into the
+    //      core-matrix tiles (row % 8): both are conflict-free 512-byte accesses.
     {
-      // beta of the next chunk: issue the load now, store it after the phasor work
       float bnext = 0.f;
       if (tid < kC && t0 + kC + tid < L)
         bnext = load_beta(a.beta, a.beta_dt, b * a.s_b.b + h * a.s_b.h + (int64_t)(t0 + kC + tid) * a.s_b.t);
 #pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        const int p = tid + kThreads * r;
-        const int t = p >> 3, sg = p & 7;
-        uint4 kraw = make_uint4(0, 0, 0, 0), qraw = kraw, vraw = kraw;
+      for (int r = 0; r < 2; ++r) {
+        const int t = 8 * warp + (lane & 7), sg = ((lane >> 3) + 2 * (lane & 7) + 4 * r) & 7;
         const bool valid = t < nvalid;
+        uint4 kraw = make_uint4(0, 0, 0, 0), qraw = kraw, vraw = kraw;
         if (valid) {
           kraw = *reinterpret_cast<const uint4 *>(stage + t * 128 + sg * 16);
           qraw = *reinterpret_cast<const uint4 *>(stage + kC * 128 + t * 128 + sg * 16);
@@ -245,323 +223,451 @@ __global__ void __launch_bounds__(kThreads, 1) core_tc_kernel(TcArgs a) {
 #pragma unroll
           for (int i = 0; i < 8; ++i) kw[i] = qw[i] = 0u;
         }
-        // channels 8 sg .. 8 sg + 7 -> features 16 sg .. 16 sg + 15 (two core-matrix columns)
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
-          const uint4 kv = make_uint4(kw[4 * half], kw[4 * half + 1], kw[4 * half + 2], kw[4 * half + 3]);
-          const uint4 qv = make_uint4(qw[4 * half], qw[4 * half + 1], qw[4 * half + 2], qw[4 * half + 3]);
-          *reinterpret_cast<uint4 *>(kvq + cm_off(t, 16 * sg + 8 * half, RG_KVQ)) = kv;
-          *reinterpret_cast<uint4 *>(kvq + cm_off(64 + t, 16 * sg + 8 * half, RG_KVQ)) = qv;
-          *reinterpret_cast<uint4 *>(wq + cm_off(64 + t, 16 * sg + 8 * half, RG_WQ)) = qv;
+          *reinterpret_cast<uint4 *>(kq + cm_off(t, 16 * sg + 8 * half, RG_KQ)) =
+              make_uint4(kw[4 * half], kw[4 * half + 1], kw[4 * half + 2], kw[4 * half + 3]);
+          *reinterpret_cast<uint4 *>(kq + cm_off(64 + t, 16 * sg + 8 * half, RG_KQ)) =
+              make_uint4(qw[4 * half], qw[4 * half + 1], qw[4 * half + 2], qw[4 * half + 3]);
         }
-        *reinterpret_cast<uint4 *>(kvq + cm_off(t, 128 + 8 * sg, RG_KVQ)) = vraw;
+        *reinterpret_cast<uint4 *>(vb + cm_off(t, 8 * sg, RG_64)) = vraw;
       }
-      if (tid < kC) bs2[(st ^ 1) * kC + tid] = bnext;
+      if (tid < kC) bs2[(slot ^ 1) * kC + tid] = bnext;
     }
     fence_proxy_async_smem();
-    __syncthreads();
+    group_sync(BAR_PREP, kPrepThreads);
 
-    // ---- phase 2: stage `st` is free again -> prefetch chunk c+2; G1 = [K; Q] K^T
-    if (c + 2 < nchunks) {
-      if (warp == 3) {
-        const int n = min(kC, L - (c + 2) * kC);
-        issue_chunk_loads(a, b, h, (c + 2) * kC, n, stage, &load_bar[st], lane);
-      }
-      issued = c + 3;
+    // ---- P2: the stage is free -> next chunk's loads; G1 = [K; Q] K^T  (M=128, N=64)
+    if (c + 1 < nchunks) {
+      if (warp == 0) issue_chunk_loads(a, b, h, t0 + kC, min(kC, L - t0 - kC), stage, &bars->load, lane);
+      issued = c + 2;
     }
     if (tid == 0) {
       tc_fence_after();
-      const uint32_t sa = smem_u32(kvq);
+      const uint32_t sa = smem_u32(kq);
 #pragma unroll
       for (int kk = 0; kk < 8; ++kk)
-        mma_f16_ss(tmem + COL_D1, make_desc(sa + kk * 256, 128, RG_KVQ),
-                   make_desc(sa + kk * 256, 128, RG_KVQ), idesc_bf16(128, 64, false, false), kk > 0);
-      mma_commit(mma_bar);
+        mma_f16_ss(tmem + COL_D1, make_desc(sa + kk * 256, 128, RG_KQ), make_desc(sa + kk * 256, 128, RG_KQ),
+                   idesc_bf16(128, 64, false, false), kk > 0);
+      mma_commit(&bars->prep_mma);
     }
-    ok = mbar_wait(mma_bar, mma_phase, kTimeoutNs);
-    mma_phase ^= 1;
-    if (__syncthreads_or(!ok)) { failed = mma_pending = true; break; }
+    mma_pending = true;
+    if (tid == 0) ok = mbar_wait(&bars->prep_mma, pm_phase, kTimeoutNs);
+    if (group_any(!ok, BAR_PREP, kPrepThreads)) { ok = false; break; }
+    pm_phase ^= 1;
+    mma_pending = false;
     tc_fence_after();
 
-    // ---- phase 3: A^T from the (exactly symmetric) Gram rows:  At[k][i] = beta_k G[k][i] / 64
-    //      for i > k (row k of TMEM is thread k of warps 0, 1)
-    if (warp < 2) {
-      const int k = warp * 32 + lane;
+    // ---- P3: A^T from the (exactly symmetric) Gram rows, At[k][i] = beta_k G[k][i] / 64
+    //      for i > k (quarters 0, 1); P = tril(Q K^T) in bf16 (quarters 2, 3).
+    //      Warp half hf takes columns 32 hf .. 32 hf + 31.
+    if (q < 2) {
+      const int k = q * 32 + lane;
       const float bk = bs[k] * inv64;
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
+      for (int u = 0; u < 2; ++u) {
         float g[16];
-        tmem_ld16(tmem + lane_base + COL_D1 + 16 * q, g);
+        const int c0 = 32 * hf + 16 * u;
+        tmem_ld16(tmem + lane_base + COL_D1 + c0, g);
         tmem_ld_wait();
 #pragma unroll
         for (int i = 0; i < 16; i += 4) {
-          const int c0 = 16 * q + i;
           float4 w;
-          w.x = (c0 + 0 > k) ? g[i + 0] * bk : 0.f;
-          w.y = (c0 + 1 > k) ? g[i + 1] * bk : 0.f;
-          w.z = (c0 + 2 > k) ? g[i + 2] * bk : 0.f;
-          w.w = (c0 + 3 > k) ? g[i + 3] * bk : 0.f;
-          *reinterpret_cast<float4 *>(at + k * LDA + c0) = w;
+          w.x = (c0 + i + 0 > k) ? g[i + 0] * bk : 0.f;
+          w.y = (c0 + i + 1 > k) ? g[i + 1] * bk : 0.f;
+          w.z = (c0 + i + 2 > k) ? g[i + 2] * bk : 0.f;
+          w.w = (c0 + i + 3 > k) ? g[i + 3] * bk : 0.f;
+          *reinterpret_cast<float4 *>(at + k * LDA + c0 + i) = w;
         }
-      }
-    }
-    tc_fence_before();
-    __syncthreads();
-
-    // ---- phase 4a: warps 0, 1 invert the 32 x 32 diagonal blocks of (I + A) by
-    //      right-looking substitution (lane = column, the column lives in registers);
-    //      warps 2, 3 meanwhile convert P = tril(Q K^T) to bf16 (rows 64..127 of TP).
-    if (warp < 2) {
-      const int o = warp * 32;  // block offset
-      float col[32];
-#pragma unroll
-      for (int i = 0; i < 32; ++i) col[i] = (i == lane) ? 1.f : 0.f;
-#pragma unroll
-      for (int k = 0; k < 31; ++k) {
-        const float tk = col[k];
-        const float *ak = at + (o + k) * LDA + o;  // At[o+k][o+i] = A[o+i][o+k]
-#pragma unroll
-        for (int i4 = ((k + 1) & ~3); i4 < 32; i4 += 4) {
-          const float4 av = *reinterpret_cast<const float4 *>(ak + i4);
-          if (i4 + 0 > k) col[i4 + 0] = fmaf(-av.x, tk, col[i4 + 0]);
-          if (i4 + 1 > k) col[i4 + 1] = fmaf(-av.y, tk, col[i4 + 1]);
-          if (i4 + 2 > k) col[i4 + 2] = fmaf(-av.z, tk, col[i4 + 2]);
-          if (i4 + 3 > k) col[i4 + 3] = fmaf(-av.w, tk, col[i4 + 3]);
-        }
-      }
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        tf[(o + i) * LDA + o + lane] = col[i];
-        *reinterpret_cast<__nv_bfloat16 *>(tp + cm_off(o + i, o + lane, RG_64)) =
-            __float2bfloat16_rn(bs[o + i] * col[i]);
       }
     } else {
-      const int t = warp * 32 + lane - 64;
+      const int t = (q - 2) * 32 + lane;
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
+      for (int u = 0; u < 2; ++u) {
         float p[16];
-        tmem_ld16(tmem + lane_base + COL_D1 + 16 * q, p);
+        const int c0 = 32 * hf + 16 * u;
+        tmem_ld16(tmem + lane_base + COL_D1 + c0, p);
         tmem_ld_wait();
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
-          const int sidx = 16 * q + 8 * half;
+          const int s = c0 + 8 * half;
+          const float *pp = p + 8 * half;
           uint4 w;
-          w.x = pack_bf16(sidx + 0 <= t ? p[8 * half + 0] : 0.f, sidx + 1 <= t ? p[8 * half + 1] : 0.f);
-          w.y = pack_bf16(sidx + 2 <= t ? p[8 * half + 2] : 0.f, sidx + 3 <= t ? p[8 * half + 3] : 0.f);
-          w.z = pack_bf16(sidx + 4 <= t ? p[8 * half + 4] : 0.f, sidx + 5 <= t ? p[8 * half + 5] : 0.f);
-          w.w = pack_bf16(sidx + 6 <= t ? p[8 * half + 6] : 0.f, sidx + 7 <= t ? p[8 * half + 7] : 0.f);
-          *reinterpret_cast<uint4 *>(tp + cm_off(64 + t, sidx, RG_64)) = w;
+          w.x = pack_bf16(s + 0 <= t ? pp[0] : 0.f, s + 1 <= t ? pp[1] : 0.f);
+          w.y = pack_bf16(s + 2 <= t ? pp[2] : 0.f, s + 3 <= t ? pp[3] : 0.f);
+          w.z = pack_bf16(s + 4 <= t ? pp[4] : 0.f, s + 5 <= t ? pp[5] : 0.f);
+          w.w = pack_bf16(s + 6 <= t ? pp[6] : 0.f, s + 7 <= t ? pp[7] : 0.f);
+          *reinterpret_cast<uint4 *>(pb + cm_off(t, s, RG_64)) = w;
         }
       }
     }
     tc_fence_before();
-    __syncthreads();
+    group_sync(BAR_PREP, kPrepThreads);
 
-    // ---- phase 4b: Y = A[32:64, 0:32] T00   (thread: column j, rows 8 ib .. 8 ib + 7)
+    // ---- P4a: 16 x 16 diagonal blocks of (I + A)^-1, right-looking substitution with
+    //      the column in registers (threads 0..63: block tid / 16, column tid % 16)
+    if (tid < 64) {
+      const int o = 16 * (tid >> 4), col = tid & 15;
+      float cl[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) cl[i] = (i == col) ? 1.f : 0.f;
+#pragma unroll
+      for (int k = 0; k < 15; ++k) {
+        const float tk = cl[k];
+        const float *ak = at + (o + k) * LDA + o;
+#pragma unroll
+        for (int i4 = ((k + 1) & ~3); i4 < 16; i4 += 4) {
+          const float4 av = *reinterpret_cast<const float4 *>(ak + i4);
+          if (i4 + 0 > k) cl[i4 + 0] = fmaf(-av.x, tk, cl[i4 + 0]);
+          if (i4 + 1 > k) cl[i4 + 1] = fmaf(-av.y, tk, cl[i4 + 1]);
+          if (i4 + 2 > k) cl[i4 + 2] = fmaf(-av.z, tk, cl[i4 + 2]);
+          if (i4 + 3 > k) cl[i4 + 3] = fmaf(-av.w, tk, cl[i4 + 3]);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 16; ++i) tf[(o + i) * LDA + o + col] = cl[i];
+    }
+    group_sync(BAR_PREP, kPrepThreads);
+
+    // ---- P4b: 16 -> 32 merge for the block pairs (0,1), (2,3):  Z = A[16+i][k] T[k][j],
+    //      then T[16+i][j] = -T11 Z.  Thread: pair tid / 128, row i = (tid / 8) % 16,
+    //      columns 2 (tid % 8) .. + 1.
     {
-      const int j = lane, ib = warp;
-      float y[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      const int pr = tid >> 7, i = (tid >> 3) & 15, j0 = 2 * (tid & 7), o = 32 * pr;
+      float z0 = 0.f, z1 = 0.f;
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        const float av = at[(o + k) * LDA + o + 16 + i];
+        const float2 tv = *reinterpret_cast<const float2 *>(tf + (o + k) * LDA + o + j0);
+        z0 = fmaf(av, tv.x, z0);
+        z1 = fmaf(av, tv.y, z1);
+      }
+      *reinterpret_cast<float2 *>(zs + (16 * pr + i) * LDZ + j0) = make_float2(z0, z1);
+      group_sync(BAR_PREP, kPrepThreads);
+      float x0 = 0.f, x1 = 0.f;
+      const float *trow = tf + (o + 16 + i) * LDA + o + 16;
+#pragma unroll
+      for (int m = 0; m < 16; m += 4) {
+        const float4 t4 = *reinterpret_cast<const float4 *>(trow + m);
+        const float2 y0 = *reinterpret_cast<const float2 *>(zs + (16 * pr + m + 0) * LDZ + j0);
+        const float2 y1 = *reinterpret_cast<const float2 *>(zs + (16 * pr + m + 1) * LDZ + j0);
+        const float2 y2 = *reinterpret_cast<const float2 *>(zs + (16 * pr + m + 2) * LDZ + j0);
+        const float2 y3 = *reinterpret_cast<const float2 *>(zs + (16 * pr + m + 3) * LDZ + j0);
+        x0 = fmaf(t4.x, y0.x, x0); x1 = fmaf(t4.x, y0.y, x1);
+        x0 = fmaf(t4.y, y1.x, x0); x1 = fmaf(t4.y, y1.y, x1);
+        x0 = fmaf(t4.z, y2.x, x0); x1 = fmaf(t4.z, y2.y, x1);
+        x0 = fmaf(t4.w, y3.x, x0); x1 = fmaf(t4.w, y3.y, x1);
+      }
+      *reinterpret_cast<float2 *>(tf + (o + 16 + i) * LDA + o + j0) = make_float2(-x0, -x1);
+    }
+    group_sync(BAR_PREP, kPrepThreads);
+
+    // ---- P4c: 32 -> 64 merge, Y = A[32+i][k] T[k][j] (k < 32), then T[32+i][j] = -T11 Y.
+    //      Thread: rows 2 (tid / 16) .. + 1, columns 2 (tid % 16) .. + 1.
+    {
+      const int i0 = 2 * (tid >> 4), j0 = 2 * (tid & 15);
+      float y00 = 0.f, y01 = 0.f, y10 = 0.f, y11 = 0.f;
 #pragma unroll 8
       for (int k = 0; k < 32; ++k) {
-        const float tkj = tf[k * LDA + j];
-        const float4 a0 = *reinterpret_cast<const float4 *>(at + k * LDA + 32 + 8 * ib);
-        const float4 a1 = *reinterpret_cast<const float4 *>(at + k * LDA + 36 + 8 * ib);
-        y[0] = fmaf(a0.x, tkj, y[0]); y[1] = fmaf(a0.y, tkj, y[1]);
-        y[2] = fmaf(a0.z, tkj, y[2]); y[3] = fmaf(a0.w, tkj, y[3]);
-        y[4] = fmaf(a1.x, tkj, y[4]); y[5] = fmaf(a1.y, tkj, y[5]);
-        y[6] = fmaf(a1.z, tkj, y[6]); y[7] = fmaf(a1.w, tkj, y[7]);
+        const float2 av = *reinterpret_cast<const float2 *>(at + k * LDA + 32 + i0);
+        const float2 tv = *reinterpret_cast<const float2 *>(tf + k * LDA + j0);
+        y00 = fmaf(av.x, tv.x, y00); y01 = fmaf(av.x, tv.y, y01);
+        y10 = fmaf(av.y, tv.x, y10); y11 = fmaf(av.y, tv.y, y11);
       }
-#pragma unroll
-      for (int r = 0; r < 8; ++r) ys[(8 * ib + r) * LDY + j] = y[r];
-    }
-    __syncthreads();
-
-    // ---- phase 4c: T[32:64, 0:32] = -T11 Y, scaled by beta -> bf16 rows 32..63 of TP
-    {
-      const int j = lane, ib = warp;
-      float x[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-#pragma unroll 4
+      *reinterpret_cast<float2 *>(zs + i0 * LDZ + j0) = make_float2(y00, y01);
+      *reinterpret_cast<float2 *>(zs + (i0 + 1) * LDZ + j0) = make_float2(y10, y11);
+      group_sync(BAR_PREP, kPrepThreads);
+      float x00 = 0.f, x01 = 0.f, x10 = 0.f, x11 = 0.f;
+      const float *r0 = tf + (32 + i0) * LDA + 32, *r1 = r0 + LDA;
+#pragma unroll 2
       for (int m = 0; m < 32; m += 4) {
-        const float y0 = ys[(m + 0) * LDY + j], y1 = ys[(m + 1) * LDY + j];
-        const float y2 = ys[(m + 2) * LDY + j], y3 = ys[(m + 3) * LDY + j];
+        const float4 a0 = *reinterpret_cast<const float4 *>(r0 + m);
+        const float4 a1 = *reinterpret_cast<const float4 *>(r1 + m);
+        const float av0[4] = {a0.x, a0.y, a0.z, a0.w}, av1[4] = {a1.x, a1.y, a1.z, a1.w};
 #pragma unroll
-        for (int r = 0; r < 8; ++r) {
-          const float4 t4 = *reinterpret_cast<const float4 *>(tf + (32 + 8 * ib + r) * LDA + 32 + m);
-          x[r] = fmaf(t4.x, y0, x[r]);
-          x[r] = fmaf(t4.y, y1, x[r]);
-          x[r] = fmaf(t4.z, y2, x[r]);
-          x[r] = fmaf(t4.w, y3, x[r]);
+        for (int u = 0; u < 4; ++u) {
+          const float2 yv = *reinterpret_cast<const float2 *>(zs + (m + u) * LDZ + j0);
+          x00 = fmaf(av0[u], yv.x, x00); x01 = fmaf(av0[u], yv.y, x01);
+          x10 = fmaf(av1[u], yv.x, x10); x11 = fmaf(av1[u], yv.y, x11);
         }
       }
-#pragma unroll
-      for (int r = 0; r < 8; ++r) {
-        const int i = 32 + 8 * ib + r;
-        *reinterpret_cast<__nv_bfloat16 *>(tp + cm_off(i, j, RG_64)) = __float2bfloat16_rn(-bs[i] * x[r]);
-      }
+      *reinterpret_cast<float2 *>(tf + (32 + i0) * LDA + j0) = make_float2(-x00, -x01);
+      *reinterpret_cast<float2 *>(tf + (33 + i0) * LDA + j0) = make_float2(-x10, -x11);
     }
-    fence_proxy_async_smem();
-    __syncthreads();
+    group_sync(BAR_PREP, kPrepThreads);
 
-    // ---- phase 5: G2 = [bT; P] [K | V]  (N = 192)
-    if (tid == 0) {
-      tc_fence_after();
-      const uint32_t sa = smem_u32(tp), sb = smem_u32(kvq);
-#pragma unroll
-      for (int kk = 0; kk < 4; ++kk)
-        mma_f16_ss(tmem + COL_D2, make_desc(sa + kk * 256, 128, RG_64),
-                   make_desc(sb + kk * 2 * RG_KVQ, RG_KVQ, 128), idesc_bf16(128, 192, false, true),
-                   kk > 0);
-      mma_commit(mma_bar);
-    }
-    ok = mbar_wait(mma_bar, mma_phase, kTimeoutNs);
-    mma_phase ^= 1;
-    if (__syncthreads_or(!ok)) { failed = mma_pending = true; break; }
-    tc_fence_after();
-
-    // ---- phase 6: W = bT K (bf16, rows 0..63 of WQ); S^T -> bf16 (bT V stays in TMEM)
-    if (warp < 2) {
-      const int t = warp * 32 + lane;
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        float w[16];
-        tmem_ld16(tmem + lane_base + COL_D2 + 16 * q, w);
-        tmem_ld_wait();
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          uint4 pk;
-          pk.x = pack_bf16(w[8 * half + 0], w[8 * half + 1]);
-          pk.y = pack_bf16(w[8 * half + 2], w[8 * half + 3]);
-          pk.z = pack_bf16(w[8 * half + 4], w[8 * half + 5]);
-          pk.w = pack_bf16(w[8 * half + 6], w[8 * half + 7]);
-          *reinterpret_cast<uint4 *>(wq + cm_off(t, 16 * q + 8 * half, RG_WQ)) = pk;
-        }
-      }
-    }
+    // ---- P4d: bT = diag(beta) T -> bf16 (row i = tid / 4, columns 16 (tid % 4) .. + 15)
     {
-      const int j = warp * 32 + lane;
+      const int i = tid >> 2, c0 = 16 * (tid & 3);
+      const float bi = bs[i];
+      const float *tr = tf + i * LDA + c0;
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        float sv[16];
-        tmem_ld16(tmem + lane_base + COL_S + 16 * q, sv);
+      for (int half = 0; half < 2; ++half) {
+        const float4 x0 = *reinterpret_cast<const float4 *>(tr + 8 * half);
+        const float4 x1 = *reinterpret_cast<const float4 *>(tr + 8 * half + 4);
+        *reinterpret_cast<uint4 *>(tb + cm_off(i, c0 + 8 * half, RG_64)) =
+            make_uint4(pack_bf16(bi * x0.x, bi * x0.y), pack_bf16(bi * x0.z, bi * x0.w),
+                       pack_bf16(bi * x1.x, bi * x1.y), pack_bf16(bi * x1.z, bi * x1.w));
+      }
+    }
+    fence_proxy_async_smem();
+    group_sync(BAR_PREP, kPrepThreads);
+
+    // ---- P5: G2 = bT [K | V]  (M=64; N=128 -> D2W, N=64 -> DU[slot])
+    if (tid == 0) {
+      tc_fence_after();
+      const uint32_t sa = smem_u32(tb), sk = smem_u32(kq), sv = smem_u32(vb);
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        const uint64_t ad = make_desc(sa + kk * 256, 128, RG_64);
+        mma_f16_ss(tmem + COL_D2W, ad, make_desc(sk + kk * 2 * RG_KQ, RG_KQ, 128),
+                   idesc_bf16(64, 128, false, true), kk > 0);
+        mma_f16_ss(tmem + COL_DU + 64 * slot, ad, make_desc(sv + kk * 2 * RG_64, RG_64, 128),
+                   idesc_bf16(64, 64, false, true), kk > 0);
+      }
+      mma_commit(&bars->prep_mma);
+    }
+    mma_pending = true;
+    if (tid == 0) ok = mbar_wait(&bars->prep_mma, pm_phase, kTimeoutNs);
+    if (group_any(!ok, BAR_PREP, kPrepThreads)) { ok = false; break; }
+    pm_phase ^= 1;
+    mma_pending = false;
+    tc_fence_after();
+
+    // ---- P6: W = bT K (M=64 rows in lanes < 16 of each quarter) -> bf16 tile
+    {
+      const int t = 16 * q + lane;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        float w[16];
+        const int c0 = 64 * hf + 16 * u;
+        tmem_ld16(tmem + lane_base + COL_D2W + c0, w);
         tmem_ld_wait();
+        if (lane < 16) {
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          uint4 pk;
-          pk.x = pack_bf16(sv[8 * half + 0], sv[8 * half + 1]);
-          pk.y = pack_bf16(sv[8 * half + 2], sv[8 * half + 3]);
-          pk.z = pack_bf16(sv[8 * half + 4], sv[8 * half + 5]);
-          pk.w = pack_bf16(sv[8 * half + 6], sv[8 * half + 7]);
-          *reinterpret_cast<uint4 *>(s0 + cm_off(j, 16 * q + 8 * half, RG_64)) = pk;
+          for (int half = 0; half < 2; ++half) {
+            const float *ww = w + 8 * half;
+            *reinterpret_cast<uint4 *>(wb + cm_off(t, c0 + 8 * half, RG_KQ)) =
+                make_uint4(pack_bf16(ww[0], ww[1]), pack_bf16(ww[2], ww[3]), pack_bf16(ww[4], ww[5]),
+                           pack_bf16(ww[6], ww[7]));
+          }
         }
       }
     }
     fence_proxy_async_smem();
     tc_fence_before();
-    __syncthreads();
+    group_sync(BAR_PREP, kPrepThreads);
+    if (tid == 0) mbar_arrive(&bars->ready[slot]);
+  }
 
-    // ---- phase 7: G3 = [W; Q] S^T
+  if (!ok) {
+    // let this role's own copies and MMAs land before shared / tensor memory is released
     if (tid == 0) {
-      tc_fence_after();
-      const uint32_t sa = smem_u32(wq), sb = smem_u32(s0);
-#pragma unroll
-      for (int kk = 0; kk < 8; ++kk)
-        mma_f16_ss(tmem + COL_DC, make_desc(sa + kk * 256, 128, RG_WQ),
-                   make_desc(sb + kk * 2 * RG_64, RG_64, 128), idesc_bf16(128, 64, false, true), kk > 0);
-      mma_commit(mma_bar);
+      for (int k = consumed; k < issued; ++k) mbar_wait(&bars->load, (uint32_t)(k & 1), kTimeoutNs);
+      if (mma_pending) mbar_wait(&bars->prep_mma, pm_phase, kTimeoutNs);
     }
-    ok = mbar_wait(mma_bar, mma_phase, kTimeoutNs);
-    mma_phase ^= 1;
-    if (__syncthreads_or(!ok)) { failed = mma_pending = true; break; }
+  }
+  return ok;
+}
+
+// ------------------------------------------------------------------------------ chain
+__device__ bool chain_role(const TcArgs &a, uint8_t *smem, Bars *bars, uint32_t tmem, int bh, int b,
+                           int h, int nchunks) {
+  const int ctid = threadIdx.x - kPrepThreads, cw = ctid >> 5, lane = ctid & 31;
+  const uint32_t lane_base = (uint32_t)(cw * 32) << 16;
+  const int L = a.L;
+  uint8_t *ub = smem + OFF_U;
+  uint8_t *s0 = smem + OFF_S0;
+  const float inv64 = 1.0f / 64.0f;
+  const int j = cw * 32 + lane;  // feature row of S^T held by this thread
+  const int64_t sbase = (int64_t)bh * kDv * kF;
+
+  // initial state^T -> TMEM
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    float vals[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) vals[i] = a.state_in ? a.state_in[sbase + (int64_t)(16 * u + i) * kF + j] : 0.f;
+    tmem_st16(tmem + lane_base + COL_S + 16 * u, vals);
+  }
+  tmem_st_wait();
+  tc_fence_before();
+  group_sync(BAR_CHAIN, kChainThreads);
+
+  uint32_t cm_phase = 0;
+  bool ok = true, mma_pending = false;
+  for (int c = 0; c < nchunks; ++c) {
+    const int slot = c & 1, t0 = c * kC, nvalid = min(kC, L - t0);
+    uint8_t *kq = smem + OFF_KQ + slot * KQ_BYTES;
+    uint8_t *wb = smem + OFF_W + slot * W_BYTES;
+    uint8_t *pb = smem + OFF_P + slot * P_BYTES;
+
+    if (ctid == 0) ok = mbar_wait(&bars->ready[slot], (uint32_t)((c >> 1) & 1), kTimeoutNs);
+    if (group_any(!ok, BAR_CHAIN, kChainThreads)) { ok = false; break; }
     tc_fence_after();
 
-    // ---- phase 8: U = bT V - W S^T / 64 (bf16, for G4 / G5)
-    if (warp < 2) {
-      const int t = warp * 32 + lane;
+    // ---- C1: S^T (fp32, TMEM) -> bf16 operand tile
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
+    for (int u = 0; u < 4; ++u) {
+      float sv[16];
+      tmem_ld16(tmem + lane_base + COL_S + 16 * u, sv);
+      tmem_ld_wait();
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const float *ss = sv + 8 * half;
+        *reinterpret_cast<uint4 *>(s0 + cm_off(j, 16 * u + 8 * half, RG_64)) =
+            make_uint4(pack_bf16(ss[0], ss[1]), pack_bf16(ss[2], ss[3]), pack_bf16(ss[4], ss[5]),
+                       pack_bf16(ss[6], ss[7]));
+      }
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    group_sync(BAR_CHAIN, kChainThreads);
+
+    // ---- C2: G3 = W S^T -> DCA and Q S^T -> DCB  (M=64, N=64, K=128)
+    if (ctid == 0) {
+      tc_fence_after();
+      const uint32_t sw = smem_u32(wb), sq = smem_u32(kq) + 8 * RG_KQ, ss = smem_u32(s0);
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        const uint64_t bd = make_desc(ss + kk * 2 * RG_64, RG_64, 128);
+        mma_f16_ss(tmem + COL_DCA, make_desc(sw + kk * 256, 128, RG_KQ), bd, idesc_bf16(64, 64, false, true), kk > 0);
+        mma_f16_ss(tmem + COL_DCB, make_desc(sq + kk * 256, 128, RG_KQ), bd, idesc_bf16(64, 64, false, true), kk > 0);
+      }
+      mma_commit(&bars->chain_mma);
+    }
+    mma_pending = true;
+    if (ctid == 0) ok = mbar_wait(&bars->chain_mma, cm_phase, kTimeoutNs);
+    if (group_any(!ok, BAR_CHAIN, kChainThreads)) { ok = false; break; }
+    cm_phase ^= 1;
+    mma_pending = false;
+    tc_fence_after();
+
+    // ---- C3: U = bT V - W S^T / 64 -> bf16 (M=64 rows: lanes < 16 of each quarter)
+    {
+      const int t = 16 * cw + lane;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
         float ws[16], ut[16];
-        tmem_ld16(tmem + lane_base + COL_DC + 16 * q, ws);
-        tmem_ld16(tmem + lane_base + COL_D2 + 128 + 16 * q, ut);
+        tmem_ld16(tmem + lane_base + COL_DCA + 16 * u, ws);
+        tmem_ld16(tmem + lane_base + COL_DU + 64 * slot + 16 * u, ut);
         tmem_ld_wait();
+        if (lane < 16) {
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          const int o = 16 * q + 8 * half;
-          const int u = 8 * half;
-          uint4 pk;
-          pk.x = pack_bf16(ut[u + 0] - ws[u + 0] * inv64, ut[u + 1] - ws[u + 1] * inv64);
-          pk.y = pack_bf16(ut[u + 2] - ws[u + 2] * inv64, ut[u + 3] - ws[u + 3] * inv64);
-          pk.z = pack_bf16(ut[u + 4] - ws[u + 4] * inv64, ut[u + 5] - ws[u + 5] * inv64);
-          pk.w = pack_bf16(ut[u + 6] - ws[u + 6] * inv64, ut[u + 7] - ws[u + 7] * inv64);
-          *reinterpret_cast<uint4 *>(ub + cm_off(t, o, RG_64)) = pk;
+          for (int half = 0; half < 2; ++half) {
+            const int o = 8 * half;
+            *reinterpret_cast<uint4 *>(ub + cm_off(t, 16 * u + o, RG_64)) =
+                make_uint4(pack_bf16(ut[o] - ws[o] * inv64, ut[o + 1] - ws[o + 1] * inv64),
+                           pack_bf16(ut[o + 2] - ws[o + 2] * inv64, ut[o + 3] - ws[o + 3] * inv64),
+                           pack_bf16(ut[o + 4] - ws[o + 4] * inv64, ut[o + 5] - ws[o + 5] * inv64),
+                           pack_bf16(ut[o + 6] - ws[o + 6] * inv64, ut[o + 7] - ws[o + 7] * inv64));
+          }
         }
       }
     }
     fence_proxy_async_smem();
     tc_fence_before();
-    __syncthreads();
+    group_sync(BAR_CHAIN, kChainThreads);
 
-    // ---- phase 9: G4  S^T += K^T U ;  G5  D_C += [bT; P] U  (rows 64..127 become 64 O)
-    if (tid == 0) {
+    // ---- C4: G4 S^T += K^T U (M=128) and G5 DCB += P U (M=64)
+    if (ctid == 0) {
       tc_fence_after();
-      const uint32_t sk = smem_u32(kvq), su = smem_u32(ub), stp = smem_u32(tp);
+      const uint32_t sk = smem_u32(kq), su = smem_u32(ub), sp = smem_u32(pb);
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk)
-        mma_f16_ss(tmem + COL_S, make_desc(sk + kk * 2 * RG_KVQ, RG_KVQ, 128),
-                   make_desc(su + kk * 2 * RG_64, RG_64, 128), idesc_bf16(128, 64, true, true), 1u);
-#pragma unroll
-      for (int kk = 0; kk < 4; ++kk)
-        mma_f16_ss(tmem + COL_DC, make_desc(stp + kk * 256, 128, RG_64),
-                   make_desc(su + kk * 2 * RG_64, RG_64, 128), idesc_bf16(128, 64, false, true), 1u);
-      mma_commit(mma_bar);
+      for (int kk = 0; kk < 4; ++kk) {
+        const uint64_t ud = make_desc(su + kk * 2 * RG_64, RG_64, 128);
+        mma_f16_ss(tmem + COL_S, make_desc(sk + kk * 2 * RG_KQ, RG_KQ, 128), ud, idesc_bf16(128, 64, true, true), 1u);
+        mma_f16_ss(tmem + COL_DCB, make_desc(sp + kk * 256, 128, RG_64), ud, idesc_bf16(64, 64, false, true), 1u);
+      }
+      mma_commit(&bars->chain_mma);
     }
-    ok = mbar_wait(mma_bar, mma_phase, kTimeoutNs);
-    mma_phase ^= 1;
-    if (__syncthreads_or(!ok)) { failed = mma_pending = true; break; }
+    mma_pending = true;
+    if (ctid == 0) ok = mbar_wait(&bars->chain_mma, cm_phase, kTimeoutNs);
+    if (group_any(!ok, BAR_CHAIN, kChainThreads)) { ok = false; break; }
+    cm_phase ^= 1;
+    mma_pending = false;
     tc_fence_after();
+    if (ctid == 0) mbar_arrive(&bars->free_[slot]);  // K, Q, W, P, bT V of this slot are consumed
 
-    // ---- phase 10: outputs (rows 64..127 of D_C) / 64 -> global fp32
-    if (warp >= 2) {
-      const int t = warp * 32 + lane - 64;
+    // ---- C5: outputs O = DCB / 64 (M=64 rows: lanes < 16 of each quarter)
+    {
+      const int t = 16 * cw + lane;
       float *orow = a.out + b * a.s_out.b + h * a.s_out.h + (int64_t)(t0 + t) * a.s_out.t;
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
+      for (int u = 0; u < 4; ++u) {
         float o[16];
-        tmem_ld16(tmem + lane_base + COL_DC + 16 * q, o);
+        tmem_ld16(tmem + lane_base + COL_DCB + 16 * u, o);
         tmem_ld_wait();
-        if (t < nvalid) {
+        if (lane < 16 && t < nvalid) {
 #pragma unroll
           for (int i = 0; i < 16; i += 4)
-            *reinterpret_cast<float4 *>(orow + 16 * q + i) =
+            *reinterpret_cast<float4 *>(orow + 16 * u + i) =
                 make_float4(o[i] * inv64, o[i + 1] * inv64, o[i + 2] * inv64, o[i + 3] * inv64);
         }
       }
     }
     tc_fence_before();
-    __syncthreads();
   }
 
-  if (failed) {
-    if (tid == 0) atomicCAS(a.err, 0, DP_ERR_TIMEOUT);
-    // let copies and MMAs still in flight land before the shared / tensor memory is
-    // released (each wait bounded again)
-    for (int k = consumed; k < issued; ++k) mbar_wait(&load_bar[k & 1], (uint32_t)((k >> 1) & 1), kTimeoutNs);
-    if (mma_pending) mbar_wait(mma_bar, mma_phase ^ 1, kTimeoutNs);
-  } else {
+  if (ok) {
     // final state: TMEM S^T -> complex64 state (row o, interleaved column j)
     tc_fence_after();
-    const int j = warp * 32 + lane;
-    const int64_t base = (int64_t)bh * kDv * kF;
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
+    for (int u = 0; u < 4; ++u) {
       float sv[16];
-      tmem_ld16(tmem + lane_base + COL_S + 16 * q, sv);
+      tmem_ld16(tmem + lane_base + COL_S + 16 * u, sv);
       tmem_ld_wait();
 #pragma unroll
-      for (int i = 0; i < 16; ++i) a.state_out[base + (int64_t)(16 * q + i) * kF + j] = sv[i];
+      for (int i = 0; i < 16; ++i) a.state_out[sbase + (int64_t)(16 * u + i) * kF + j] = sv[i];
     }
+  } else if (mma_pending && ctid == 0) {
+    mbar_wait(&bars->chain_mma, cm_phase, kTimeoutNs);
   }
+  return ok;
+}
+
+__global__ void __launch_bounds__(kThreads, 1) core_tc_kernel(TcArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  Bars *bars = reinterpret_cast<Bars *>(smem + OFF_BAR);
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 1);
+  int *fail_flag = reinterpret_cast<int *>(tmem_slot + 1);
+  float *tf = reinterpret_cast<float *>(smem + OFF_TF);
+
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int bh = blockIdx.x, b = bh / a.H, h = bh % a.H;
+  const int nchunks = (a.L + kC - 1) / kC;
+
+  if (tid == 0) {
+    mbar_init(&bars->load, 1);
+    mbar_init(&bars->prep_mma, 1);
+    mbar_init(&bars->chain_mma, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars->ready[i], 1);
+      mbar_init(&bars->free_[i], 1);
+    }
+    *fail_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  // T's strictly upper blocks are never written: zero them once
+  for (int i = tid; i < kC * LDA; i += kThreads) tf[i] = 0.f;
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  bool ok;
+  if (tid < kPrepThreads)
+    ok = prep_role(a, smem, bars, tmem, b, h, nchunks);
+  else
+    ok = chain_role(a, smem, bars, tmem, bh, b, h, nchunks);
+  if (!ok) atomicExch(fail_flag, 1);
+
   tc_fence_before();
   __syncthreads();
+  if (tid == 0 && *fail_flag) atomicCAS(a.err, 0, DP_ERR_TIMEOUT);
   if (warp == 0) tmem_dealloc(tmem, TMEM_COLS);
 }
 
