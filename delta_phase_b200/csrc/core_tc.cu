@@ -102,6 +102,57 @@ __device__ __forceinline__ float load_beta(const void *p, int dt, int64_t i) {
   return __half2float(static_cast<const __half *>(p)[i]);
 }
 
+// Warp-level tf32 MMA (m16n8k8, fp32 accumulate) for the small block products of the
+// triangular inverse: operands straight from shared memory into registers, no tensor
+// memory round trip.  Fragment layout (g = lane / 4, c = lane % 4): A a0 (g, c),
+// a1 (g+8, c), a2 (g, c+4), a3 (g+8, c+4); B b0 (c, g), b1 (c+4, g); D d0 (g, 2c),
+// d1 (g, 2c+1), d2 (g+8, 2c), d3 (g+8, 2c+1).
+__device__ __forceinline__ uint32_t to_tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+
+__device__ __forceinline__ void mma_tf32_m16n8k8(float (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+
+// One warp: D[16 x 16] = X[16 x K] Y[K x 16], X(i, k) = x[i * xs_i + k * xs_k],
+// Y(k, j) = y[k * ys_k + j * ys_j] (fp32 in shared memory, tf32 products); D is
+// returned as two m16n8 fragments.
+template <int K>
+__device__ __forceinline__ void warp_gemm16(float (&d0)[4], float (&d1)[4], const float *x, int xs_i, int xs_k,
+                                            const float *y, int ys_k, int ys_j, int lane) {
+  const int g = lane >> 2, c = lane & 3;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) d0[i] = d1[i] = 0.f;
+#pragma unroll
+  for (int k0 = 0; k0 < K; k0 += 8) {
+    const uint32_t a[4] = {to_tf32(x[g * xs_i + (k0 + c) * xs_k]), to_tf32(x[(g + 8) * xs_i + (k0 + c) * xs_k]),
+                           to_tf32(x[g * xs_i + (k0 + c + 4) * xs_k]),
+                           to_tf32(x[(g + 8) * xs_i + (k0 + c + 4) * xs_k])};
+    const uint32_t b0[2] = {to_tf32(y[(k0 + c) * ys_k + g * ys_j]), to_tf32(y[(k0 + c + 4) * ys_k + g * ys_j])};
+    const uint32_t b1[2] = {to_tf32(y[(k0 + c) * ys_k + (g + 8) * ys_j]),
+                            to_tf32(y[(k0 + c + 4) * ys_k + (g + 8) * ys_j])};
+    mma_tf32_m16n8k8(d0, a, b0);
+    mma_tf32_m16n8k8(d1, a, b1);
+  }
+}
+
+// Stores a warp's 16 x 16 result (two m16n8 fragments) scaled by `sc` at out[i * ld + j].
+__device__ __forceinline__ void warp_store16(float *out, int ld, const float (&d0)[4], const float (&d1)[4], float sc,
+                                             int lane) {
+  const int g = lane >> 2, c = lane & 3;
+  *reinterpret_cast<float2 *>(out + g * ld + 2 * c) = make_float2(sc * d0[0], sc * d0[1]);
+  *reinterpret_cast<float2 *>(out + (g + 8) * ld + 2 * c) = make_float2(sc * d0[2], sc * d0[3]);
+  *reinterpret_cast<float2 *>(out + g * ld + 8 + 2 * c) = make_float2(sc * d1[0], sc * d1[1]);
+  *reinterpret_cast<float2 *>(out + (g + 8) * ld + 8 + 2 * c) = make_float2(sc * d1[2], sc * d1[3]);
+}
+
 struct TcArgs {
   const __nv_bfloat16 *tk, *tq, *v;
   const void *beta;
@@ -329,70 +380,33 @@ __device__ bool prep_role(const TcArgs &a, uint8_t *smem, Bars *bars, uint32_t t
     }
     group_sync(BAR_PREP, kPrepThreads);
 
-    // ---- P4b: 16 -> 32 merge for the block pairs (0,1), (2,3):  Z = A[16+i][k] T[k][j],
-    //      then T[16+i][j] = -T11 Z.  Thread: pair tid / 128, row i = (tid / 8) % 16,
-    //      columns 2 (tid % 8) .. + 1.
-    {
-      const int pr = tid >> 7, i = (tid >> 3) & 15, j0 = 2 * (tid & 7), o = 32 * pr;
-      float z0 = 0.f, z1 = 0.f;
-#pragma unroll
-      for (int k = 0; k < 16; ++k) {
-        const float av = at[(o + k) * LDA + o + 16 + i];
-        const float2 tv = *reinterpret_cast<const float2 *>(tf + (o + k) * LDA + o + j0);
-        z0 = fmaf(av, tv.x, z0);
-        z1 = fmaf(av, tv.y, z1);
-      }
-      *reinterpret_cast<float2 *>(zs + (16 * pr + i) * LDZ + j0) = make_float2(z0, z1);
-      group_sync(BAR_PREP, kPrepThreads);
-      float x0 = 0.f, x1 = 0.f;
-      const float *trow = tf + (o + 16 + i) * LDA + o + 16;
-#pragma unroll
-      for (int m = 0; m < 16; m += 4) {
-        const float4 t4 = *reinterpret_cast<const float4 *>(trow + m);
-        const float2 y0 = *reinterpret_cast<const float2 *>(zs + (16 * pr + m + 0) * LDZ + j0);
-        const float2 y1 = *reinterpret_cast<const float2 *>(zs + (16 * pr + m + 1) * LDZ + j0);
-        const float2 y2 = *reinterpret_cast<const float2 *>(zs + (16 * pr + m + 2) * LDZ + j0);
-        const float2 y3 = *reinterpret_cast<const float2 *>(zs + (16 * pr + m + 3) * LDZ + j0);
-        x0 = fmaf(t4.x, y0.x, x0); x1 = fmaf(t4.x, y0.y, x1);
-        x0 = fmaf(t4.y, y1.x, x0); x1 = fmaf(t4.y, y1.y, x1);
-        x0 = fmaf(t4.z, y2.x, x0); x1 = fmaf(t4.z, y2.y, x1);
-        x0 = fmaf(t4.w, y3.x, x0); x1 = fmaf(t4.w, y3.y, x1);
-      }
-      *reinterpret_cast<float2 *>(tf + (o + 16 + i) * LDA + o + j0) = make_float2(-x0, -x1);
+    // ---- P4b: 16 -> 32 merge for the block pairs (0,1), (2,3) on warps 0, 1 (tf32 mma):
+    //      Z = A[16+i][k] T[k][j], then T[16+i][j] = -T11 Z
+    if (warp < 2) {
+      const int o = 32 * warp;
+      float d0[4], d1[4];
+      warp_gemm16<16>(d0, d1, at + o * LDA + o + 16, 1, LDA, tf + o * LDA + o, LDA, 1, lane);
+      warp_store16(zs + 16 * warp * LDZ, LDZ, d0, d1, 1.f, lane);
+      __syncwarp();
+      warp_gemm16<16>(d0, d1, tf + (o + 16) * LDA + o + 16, LDA, 1, zs + 16 * warp * LDZ, LDZ, 1, lane);
+      warp_store16(tf + (o + 16) * LDA + o, LDA, d0, d1, -1.f, lane);
     }
     group_sync(BAR_PREP, kPrepThreads);
 
-    // ---- P4c: 32 -> 64 merge, Y = A[32+i][k] T[k][j] (k < 32), then T[32+i][j] = -T11 Y.
-    //      Thread: rows 2 (tid / 16) .. + 1, columns 2 (tid % 16) .. + 1.
-    {
-      const int i0 = 2 * (tid >> 4), j0 = 2 * (tid & 15);
-      float y00 = 0.f, y01 = 0.f, y10 = 0.f, y11 = 0.f;
-#pragma unroll 8
-      for (int k = 0; k < 32; ++k) {
-        const float2 av = *reinterpret_cast<const float2 *>(at + k * LDA + 32 + i0);
-        const float2 tv = *reinterpret_cast<const float2 *>(tf + k * LDA + j0);
-        y00 = fmaf(av.x, tv.x, y00); y01 = fmaf(av.x, tv.y, y01);
-        y10 = fmaf(av.y, tv.x, y10); y11 = fmaf(av.y, tv.y, y11);
-      }
-      *reinterpret_cast<float2 *>(zs + i0 * LDZ + j0) = make_float2(y00, y01);
-      *reinterpret_cast<float2 *>(zs + (i0 + 1) * LDZ + j0) = make_float2(y10, y11);
-      group_sync(BAR_PREP, kPrepThreads);
-      float x00 = 0.f, x01 = 0.f, x10 = 0.f, x11 = 0.f;
-      const float *r0 = tf + (32 + i0) * LDA + 32, *r1 = r0 + LDA;
-#pragma unroll 2
-      for (int m = 0; m < 32; m += 4) {
-        const float4 a0 = *reinterpret_cast<const float4 *>(r0 + m);
-        const float4 a1 = *reinterpret_cast<const float4 *>(r1 + m);
-        const float av0[4] = {a0.x, a0.y, a0.z, a0.w}, av1[4] = {a1.x, a1.y, a1.z, a1.w};
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const float2 yv = *reinterpret_cast<const float2 *>(zs + (m + u) * LDZ + j0);
-          x00 = fmaf(av0[u], yv.x, x00); x01 = fmaf(av0[u], yv.y, x01);
-          x10 = fmaf(av1[u], yv.x, x10); x11 = fmaf(av1[u], yv.y, x11);
-        }
-      }
-      *reinterpret_cast<float2 *>(tf + (32 + i0) * LDA + j0) = make_float2(-x00, -x01);
-      *reinterpret_cast<float2 *>(tf + (33 + i0) * LDA + j0) = make_float2(-x10, -x11);
+    // ---- P4c: 32 -> 64 merge on warps 0..3 (tf32 mma, one 16 x 16 tile each):
+    //      Y = A[32+i][k] T[k][j] (k < 32), then T[32+i][j] = -T11 Y
+    if (warp < 4) {
+      const int mi = 16 * (warp >> 1), nj = 16 * (warp & 1);
+      float d0[4], d1[4];
+      warp_gemm16<32>(d0, d1, at + 32 + mi, 1, LDA, tf + nj, LDA, 1, lane);
+      warp_store16(zs + mi * LDZ + nj, LDZ, d0, d1, 1.f, lane);
+    }
+    group_sync(BAR_PREP, kPrepThreads);
+    if (warp < 4) {
+      const int mi = 16 * (warp >> 1), nj = 16 * (warp & 1);
+      float d0[4], d1[4];
+      warp_gemm16<32>(d0, d1, tf + (32 + mi) * LDA + 32, LDA, 1, zs + nj, LDZ, 1, lane);
+      warp_store16(tf + (32 + mi) * LDA + nj, LDA, d0, d1, -1.f, lane);
     }
     group_sync(BAR_PREP, kPrepThreads);
 
