@@ -285,6 +285,182 @@ def run_core(args, world, rank, local):
     return line
 
 
+def _timed(step, steps, warmup, stream):
+    """Device time per step (ms) of `step` over `steps` iterations after `warmup`."""
+    import torch
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def _line(metric, value, unit, args, world, ms, config, **extra):
+    d = {"metric": metric, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
+         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)", "config": config}
+    d.update(extra)
+    return d
+
+
+def run_laplace(args, world, rank, local):
+    """LaplacePhaseCore chunk solve at B=4, H=16, L=32768, d_k=64 (gated decay:
+    log r = -softplus(N(0,1)), unit phasors, bf16 inputs)."""
+    import torch
+    import torch.nn.functional as F
+    from delta_phase_b200.kernels import laplace_chunkwise
+    dev = torch.device("cuda", local)
+    B, H, L, D = 4, 16, 32768, 64
+    g = torch.Generator(device=dev).manual_seed(2000 + rank)
+    bf = torch.bfloat16
+    tk = (torch.rand(B, H, L, D, device=dev, generator=g) * 2 * np.pi).to(bf)
+    tq = (torch.rand(B, H, L, D, device=dev, generator=g) * 2 * np.pi).to(bf)
+    v = torch.randn(B, H, L, D, device=dev, generator=g).to(bf)
+    logr = (-F.softplus(torch.randn(B, H, L, D, device=dev, generator=g))).to(bf)
+    beta = (2 * torch.sigmoid(torch.randn(B, H, L, device=dev, generator=g))).to(bf)
+    out = torch.empty(B, H, L, D, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    ms = _timed(lambda: laplace_chunkwise(tk, None, tq, None, v, logr, beta, 64, None, out),
+                args.steps, args.warmup, stream)
+    ms = max_over_ranks(ms, world)
+    alg = B * H * L * (4 * D * 2 + 2 + D * 4) + B * H * D * D * 8
+    peaks, _ = load_peaks()
+    line = _line("laplace-core tokens/s (B=4,H=16,L=32K,d_k=64)", world * B * L / (ms / 1e3), "tokens/s",
+                 args, world, ms, {"workload": "LaplacePhaseCore chunk solve, B=4,H=16,L=32768,d_k=64,C=64",
+                                   "global_batch": B * world, "seq_len": L},
+                 roofline={"bound": "hbm", "achieved": alg / (ms / 1e3) / 1e9, "peak": peaks["hbm_gbs"],
+                           "unit": "GB/s", "frac": alg / (ms / 1e3) / 1e9 / peaks["hbm_gbs"],
+                           "algorithmic_bytes_per_launch": alg})
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle import laplace as olap
+        rng = np.random.default_rng(0)
+        Ls, u = 2048, 2
+        K = np.exp(1j * rng.uniform(0, 2 * np.pi, (1, u, Ls, D))).astype(np.complex64)
+        Q = np.exp(1j * rng.uniform(0, 2 * np.pi, (1, u, Ls, D))).astype(np.complex64)
+        vv = rng.standard_normal((1, u, Ls, D)).astype(np.float32)
+        bb = (2 / (1 + np.exp(-rng.standard_normal((1, u, Ls))))).astype(np.float32)
+        rr = np.exp(-np.logaddexp(0, rng.standard_normal((1, u, Ls, D)))).astype(np.float32)
+        t0 = time.perf_counter()
+        olap.laplace_chunkwise(K, Q, vv, bb, rr, 64, None, dtype=np.float32)
+        secs = time.perf_counter() - t0
+        line["cpu_baseline"] = {"value": u * Ls / H / secs, "unit": "tokens/s", "cores": cpu_threads(),
+                                "kind": "port", "sample": f"{u} (b,h) units x L={Ls}, numpy float32 port of "
+                                "LaplacePhaseCore.forward's chunk loop; tokens/s = head-tokens / 16 / s"}
+    return line
+
+
+def run_ffn(args, world, rank, local):
+    """Spectral Lerp FFN on 16 x 4096 tokens, d_model = 1024, nb = 4, bf16 activations."""
+    import torch
+    from delta_phase_b200 import LearnableSubstrateLerpFFN
+    dev = torch.device("cuda", local)
+    tokens, d, nb = 16 * 4096, 1024, 4
+    torch.manual_seed(3000 + rank)
+    ffn = LearnableSubstrateLerpFFN(d, nb).to(dev)
+    with torch.no_grad():
+        for n, p in ffn.named_parameters():
+            p.copy_(torch.randn_like(p) * (1.0 if n == "substrate_logits" else 0.02))
+    x = torch.randn(tokens, d, device=dev).to(torch.bfloat16)
+    stream = torch.cuda.current_stream(dev)
+    with torch.no_grad():
+        ms = _timed(lambda: ffn(x), args.steps, args.warmup, stream)
+    ms = max_over_ranks(ms, world)
+    flops = tokens * (2 * 6 * d * d + 2 * d * d)  # folded combine GEMM + DCT-II GEMM
+    peaks, _ = load_peaks()
+    line = _line("lerp-ffn tokens/s (d=1024, nb=4)", world * tokens / (ms / 1e3), "tokens/s", args, world, ms,
+                 {"workload": "LearnableSubstrateLerpFFN forward, 65536 tokens, d=1024, nb=4, bf16",
+                  "global_batch": 16 * world, "seq_len": 4096},
+                 roofline={"bound": "tensor", "achieved": flops / (ms / 1e3) / 1e12,
+                           "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                           "frac": flops / (ms / 1e3) / 1e12 / peaks["bf16_tflops"],
+                           "flops_per_launch": flops,
+                           "note": "folded algorithm: 2*6d^2 + 2d^2 FLOP/token (the reference's own "
+                                   "algorithm needs 6*nb*d^2 + 12 d^2 = 37.7 MFLOP/token)"})
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle import spectral as ospec
+        params = {k: v.detach().float().cpu().numpy() for k, v in ffn.state_dict().items()}
+        xs = x[:512].float().cpu().numpy()
+        t0 = time.perf_counter()
+        ospec.lerp_ffn(xs, params, dtype=np.float32)
+        secs = time.perf_counter() - t0
+        line["cpu_baseline"] = {"value": 512 / secs, "unit": "tokens/s", "cores": cpu_threads(), "kind": "port",
+                                "sample": "512 tokens, numpy float32 port of LearnableSubstrateLerpFFN.forward"}
+    return line
+
+
+def run_decode(args, world, rank, local, B=64, H=16, D=64):
+    """Decode step on a (B, H, 64, 64) complex state, 256 steps captured in one CUDA graph."""
+    import torch
+    from delta_phase_b200.kernels import decode_step
+    dev = torch.device("cuda", local)
+    g = torch.Generator(device=dev).manual_seed(4000 + rank)
+    M = torch.randn(B, H, D, D, device=dev, dtype=torch.complex64, generator=g) * 0.1
+    n = 256
+    tk = torch.rand(n, B, H, D, device=dev, generator=g) * 2 * np.pi
+    tq = torch.rand(n, B, H, D, device=dev, generator=g) * 2 * np.pi
+    v = torch.randn(n, B, H, D, device=dev, generator=g)
+    beta = 2 * torch.sigmoid(torch.randn(n, B, H, device=dev, generator=g))
+    out = torch.empty(B, H, D, device=dev)
+    s = torch.cuda.Stream(dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(s):
+        for t in range(3):
+            decode_step(M, tk[t], tq[t], v[t], beta[t], out=out, state_out=M)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            for t in range(n):
+                decode_step(M, tk[t], tq[t], v[t], beta[t], out=out, state_out=M)
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream(dev)
+    ms = _timed(graph.replay, args.steps, args.warmup, stream) / n
+    ms = max_over_ranks(ms, world)
+    byt = B * H * (2 * D * D * 8 + 3 * D * 4 + 4 + D * 4)
+    peaks, _ = load_peaks()
+    return _line("decode step latency (B*H=%d, d_k=64)" % (B * H), ms, "ms/step", args, world, ms,
+                 {"workload": f"decode step, state ({B},{H},64,64) complex64, fp32 inputs, "
+                              f"{n} steps per CUDA graph", "global_batch": B * world},
+                 higher_is_better=False, gpu_launches=n * args.steps,
+                 roofline={"bound": "hbm", "achieved": byt / (ms / 1e3) / 1e9, "peak": peaks["hbm_gbs"],
+                           "unit": "GB/s", "frac": byt / (ms / 1e3) / 1e9 / peaks["hbm_gbs"],
+                           "algorithmic_bytes_per_launch": byt})
+
+
+def run_lm(args, world, rank, local):
+    """DeltaPhase LM, d_model 1024, 16 heads of 64, 12 layers, vocab 32000 (the d_model 768
+    configuration cannot be built by the reference): prefill 16 x 4096 tokens, then decode."""
+    import torch
+    from delta_phase_b200 import DeltaPhaseConfig, DeltaPhaseModel
+    dev = torch.device("cuda", local)
+    torch.manual_seed(5000 + rank)
+    cfg = DeltaPhaseConfig(dim=1024, n_heads=16, n_layers=12, vocab_size=32000, chunk_size=64)
+    model = DeltaPhaseModel(cfg).to(dev).eval()
+    B, L, ndec = 16, 4096, args.decode_steps
+    ids = torch.randint(0, 32000, (B, L), device=dev)
+    stream = torch.cuda.current_stream(dev)
+    with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+        pre_ms = _timed(lambda: model(ids), max(1, args.steps // 4), 1, stream)
+        _, states = model.forward_with_states(ids)
+        st = [(None, M) for M in states]
+        nxt = ids[:, -1:]
+
+        def dec():
+            nonlocal st
+            logits, st = model.step(nxt, st)
+        dec_ms = _timed(dec, ndec, 2, stream)
+    pre_ms = max_over_ranks(pre_ms, world)
+    dec_ms = max_over_ranks(dec_ms, world)
+    return _line("LM prefill tokens/s (12x1024, 16 heads, vocab 32000)", world * B * L / (pre_ms / 1e3),
+                 "tokens/s", args, world, pre_ms,
+                 {"workload": "DeltaPhaseModel prefill B=16 x L=4096 then decode, bf16 autocast",
+                  "global_batch": B * world, "seq_len": L, "model": "d1024-h16-l12"},
+                 decode={"ms_per_token": dec_ms, "steps": ndec, "batch": B})
+
+
 def run_reference(args, world, rank):
     """CPU arm: the numpy port of the reference chunkwise path on the host cores."""
     if rank != 0:
@@ -319,7 +495,8 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="core", choices=["core"])
+    ap.add_argument("--workload", default="core", choices=["core", "laplace", "ffn", "decode", "lm"])
+    ap.add_argument("--decode-steps", type=int, default=256)
     ap.add_argument("--cpu-units", type=int, default=16)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
@@ -333,7 +510,9 @@ def main():
             print(json.dumps(line), flush=True)
         return
     world, rank, local = dist_setup(args.gpus)
-    line = run_core(args, world, rank, local)
+    run = {"core": run_core, "laplace": run_laplace, "ffn": run_ffn, "decode": run_decode,
+           "lm": run_lm}[args.workload]
+    line = run(args, world, rank, local)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
