@@ -126,6 +126,74 @@ decode_kernel(const float *state_in, float *state_out, const void *__restrict__ 
   }
 }
 
+// Fast path for even D <= 64 (one float4 = two complex entries per lane and row) and
+// Dv <= 8 RPW: warp w owns rows w, w + 8, ...; all of its rows are loaded before any
+// reduction, so every lane keeps RPW independent 16-byte loads in flight.
+template <int RPW>
+__global__ void __launch_bounds__(kDecThreads)
+decode_rows_kernel(const float *state_in, float *state_out, const void *__restrict__ tk,
+                   const void *__restrict__ tq, const void *__restrict__ v,
+                   const void *__restrict__ beta, int in_dt, int beta_dt, float *__restrict__ out,
+                   int H, int D, int Dv, SeqStrides s_tk, SeqStrides s_tq, SeqStrides s_v, SeqStrides s_b,
+                   SeqStrides s_out) {
+  const int bh = blockIdx.x, b = bh / H, h = bh % H;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int npair = D >> 1, p = lane;
+  const bool active = p < npair;
+  // this lane's two key / query channels (2p, 2p+1)
+  float ck0 = 0.f, sk0 = 0.f, ck1 = 0.f, sk1 = 0.f, cq0 = 0.f, sq0 = 0.f, cq1 = 0.f, sq1 = 0.f;
+  if (active) {
+    sincosf(load_any(tk, in_dt, b * s_tk.b + h * s_tk.h + 2 * p), &sk0, &ck0);
+    sincosf(load_any(tk, in_dt, b * s_tk.b + h * s_tk.h + 2 * p + 1), &sk1, &ck1);
+    sincosf(load_any(tq, in_dt, b * s_tq.b + h * s_tq.h + 2 * p), &sq0, &cq0);
+    sincosf(load_any(tq, in_dt, b * s_tq.b + h * s_tq.h + 2 * p + 1), &sq1, &cq1);
+  }
+  const float inv_d = 1.0f / (float)D;
+  const float bt = load_any(beta, beta_dt, b * s_b.b + h * s_b.h);
+  const int64_t base = (int64_t)bh * Dv * 2 * D;
+  float4 m[RPW];
+  float vo[RPW];
+#pragma unroll
+  for (int r = 0; r < RPW; ++r) {
+    const int o = warp + 8 * r;
+    m[r] = make_float4(0.f, 0.f, 0.f, 0.f);
+    vo[r] = 0.f;
+    if (o < Dv) {
+      if (active) m[r] = reinterpret_cast<const float4 *>(state_in + base + (int64_t)o * 2 * D)[p];
+      vo[r] = load_any(v, in_dt, b * s_v.b + h * s_v.h + o);
+    }
+  }
+  float acc[RPW];
+#pragma unroll
+  for (int r = 0; r < RPW; ++r) acc[r] = m[r].x * ck0 + m[r].y * sk0 + m[r].z * ck1 + m[r].w * sk1;
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+    for (int r = 0; r < RPW; ++r) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], off);
+#pragma unroll
+  for (int r = 0; r < RPW; ++r) {
+    const float e = bt * (vo[r] - acc[r] * inv_d);
+    m[r].x = fmaf(e, ck0, m[r].x);
+    m[r].y = fmaf(e, sk0, m[r].y);
+    m[r].z = fmaf(e, ck1, m[r].z);
+    m[r].w = fmaf(e, sk1, m[r].w);
+    const int o = warp + 8 * r;
+    if (o < Dv && active) reinterpret_cast<float4 *>(state_out + base + (int64_t)o * 2 * D)[p] = m[r];
+    acc[r] = m[r].x * cq0 + m[r].y * sq0 + m[r].z * cq1 + m[r].w * sq1;
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+    for (int r = 0; r < RPW; ++r) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], off);
+  if (lane == 0) {
+#pragma unroll
+    for (int r = 0; r < RPW; ++r) {
+      const int o = warp + 8 * r;
+      if (o < Dv) out[b * s_out.b + h * s_out.h + o] = acc[r] * inv_d;
+    }
+  }
+}
+
 }  // namespace
 }  // namespace dp
 
@@ -147,7 +215,11 @@ extern "C" int dp_core_decode(const float *state_in, float *state_out, const voi
   const bool vec4 = (D % 2 == 0) && (reinterpret_cast<uintptr_t>(state_in) % 16 == 0) &&
                     (reinterpret_cast<uintptr_t>(state_out) % 16 == 0);
   const size_t smem = 4 * (size_t)D * sizeof(float);
-  if (vec4)
+  if (vec4 && D <= 64 && Dv <= 128) {
+    auto kern = Dv <= 64 ? decode_rows_kernel<8> : decode_rows_kernel<16>;
+    kern<<<B * H, kDecThreads, 0, as_stream(stream)>>>(state_in, state_out, theta_k, theta_q, v, beta, in_dtype,
+                                                       beta_dtype, out, H, D, Dv, s[0], s[1], s[2], s[3], s[4]);
+  } else if (vec4)
     decode_kernel<true><<<B * H, kDecThreads, smem, as_stream(stream)>>>(
         state_in, state_out, theta_k, theta_q, v, beta, in_dtype, beta_dtype, out, H, D, Dv, s[0],
         s[1], s[2], s[3], s[4]);
