@@ -176,6 +176,12 @@ laplace_simt_kernel(LapPtrs p, int in_dt, int beta_dt, const float *state_in, fl
 }
 
 }  // namespace
+
+bool laplace_tc_supported(const void *const *ptrs, int in_dt, const float *out, int D, int Dv,
+                          const SeqStrides *s);
+int laplace_fwd_tc(const void *const *ptrs, const void *beta, int beta_dt, const float *state_in, float *out,
+                   float *state_out, int B, int H, int L, const SeqStrides *s, cudaStream_t stream);
+
 }  // namespace dp
 
 extern "C" int dp_laplace_fwd(const void *theta_k, const void *logmag_k, const void *theta_q,
@@ -197,6 +203,12 @@ extern "C" int dp_laplace_fwd(const void *theta_k, const void *logmag_k, const v
   LapStrides st;
   for (int i = 0; i < 8; ++i) st.s[i] = SeqStrides{strides[3 * i], strides[3 * i + 1], strides[3 * i + 2]};
   LapPtrs p{theta_k, logmag_k, theta_q, logmag_q, v, log_decay, beta};
+  if (L > 0) {
+    const void *tc_ptrs[6] = {theta_k, logmag_k, theta_q, logmag_q, v, log_decay};
+    if (laplace_tc_supported(tc_ptrs, in_dtype, out, D, Dv, st.s))
+      return laplace_fwd_tc(tc_ptrs, beta, beta_dtype, state_in, out, state_out, B, H, L, st.s,
+                            as_stream(stream));
+  }
   const bool ci32 = lap_smem_floats(32, D, Dv) * sizeof(float) <= 200 * 1024;
   const size_t smem = lap_smem_floats(ci32 ? 32 : 16, D, Dv) * sizeof(float);
   DP_REQUIRE(smem <= 227 * 1024, DP_ERR_UNSUPPORTED, "dp_laplace_fwd: shape exceeds shared memory");

@@ -6,6 +6,7 @@ import pytest
 import torch
 
 import delta_phase_b200 as dp
+from delta_phase_b200 import _capi
 from oracle import laplace as olap
 
 from helpers import TOL_BF16, TOL_F32, load_golden, rel_l2, round_bf16, to_dev
@@ -83,3 +84,81 @@ def test_strong_decay_is_finite():
     assert torch.isfinite(out).all()
     assert rel_l2(out, ref_out) < TOL_F32
     assert rel_l2(M, ref_M) < TOL_F32
+
+
+def _lap_bf16_inputs(seed, B, H, L, D, with_mag, logr_fill=None):
+    rng = np.random.default_rng(seed)
+    tk = round_bf16(rng.uniform(0, 2 * np.pi, (B, H, L, D)))
+    tq = round_bf16(rng.uniform(0, 2 * np.pi, (B, H, L, D)))
+    mk = round_bf16(-np.logaddexp(0, rng.standard_normal((B, H, L, D))) * 0.3) if with_mag else None
+    mq = round_bf16(-np.logaddexp(0, rng.standard_normal((B, H, L, D))) * 0.3) if with_mag else None
+    v = round_bf16(rng.standard_normal((B, H, L, D)))
+    beta = round_bf16(2 / (1 + np.exp(-rng.standard_normal((B, H, L)))))
+    if logr_fill is None:
+        logr = round_bf16(-np.logaddexp(0, rng.standard_normal((B, H, L, D))))
+    else:
+        logr = np.full((B, H, L, D), logr_fill, np.float32)
+    return tk, mk, tq, mq, v, logr, beta
+
+
+def _lap_ref(tk, mk, tq, mq, v, logr, beta, M0=None):
+    K = np.exp((0 if mk is None else mk.astype(np.float64)) + 1j * tk.astype(np.float64))
+    Q = np.exp((0 if mq is None else mq.astype(np.float64)) + 1j * tq.astype(np.float64))
+    return olap.laplace_sequential(K, Q, v, beta, np.exp(logr.astype(np.float64)), M0)
+
+
+@pytest.mark.parametrize("B,H,L,with_mag,with_state,layout", [
+    (2, 3, 1, False, False, "bhld"),
+    (1, 2, 64, True, True, "bhld"),
+    (1, 2, 129, True, True, "blhd"),
+    (2, 2, 700, False, True, "blhd"),
+    (1, 1, 257, True, False, "bhld"),
+])
+def test_tensor_core_path(B, H, L, with_mag, with_state, layout):
+    """bf16, d_k = d_v = 64: the tcgen05 kernel.  Ragged tails, log-magnitudes, an
+    initial state and (B, L, H, D) strided views against the fp64 token loop."""
+    D = 64
+    tk, mk, tq, mq, v, logr, beta = _lap_bf16_inputs(B * 1000 + L, B, H, L, D, with_mag)
+    rng = np.random.default_rng(7)
+    M0 = ((rng.standard_normal((B, H, D, D)) + 1j * rng.standard_normal((B, H, D, D))) * 0.5
+          if with_state else None)
+
+    def dev(a):
+        if a is None:
+            return None
+        if layout == "blhd" and a.ndim == 4:
+            return to_dev(np.ascontiguousarray(a.transpose(0, 2, 1, 3)), torch.bfloat16).transpose(1, 2)
+        if layout == "blhd":
+            return to_dev(np.ascontiguousarray(a.transpose(0, 2, 1)), torch.bfloat16).transpose(1, 2)
+        return to_dev(a, torch.bfloat16)
+
+    M0d = to_dev(M0.astype(np.complex64)) if with_state else None
+    out, M = dp.laplace_chunkwise(dev(tk), dev(mk), dev(tq), dev(mq), dev(v), dev(logr), dev(beta), 64, M0d)
+    ref_out, ref_M = _lap_ref(tk, mk, tq, mq, v, logr, beta, M0)
+    assert rel_l2(out, ref_out) < TOL_BF16
+    assert rel_l2(M, ref_M) < TOL_BF16
+    assert _capi.device_error(clear=True) == 0
+
+
+def test_tensor_core_matches_fp32_path():
+    """The bf16 tcgen05 kernel and the fp32 CUDA-core kernel on the same values."""
+    B, H, L, D = 1, 2, 300, 64
+    tk, mk, tq, mq, v, logr, beta = _lap_bf16_inputs(5, B, H, L, D, True)
+    args = (tk, mk, tq, mq, v, logr)
+    out_tc, M_tc = dp.laplace_chunkwise(*[to_dev(a, torch.bfloat16) for a in args],
+                                        to_dev(beta, torch.bfloat16), 64)
+    out_f, M_f = dp.laplace_chunkwise(*[to_dev(a) for a in args], to_dev(beta), 64)
+    assert rel_l2(out_tc, out_f) < TOL_BF16
+    assert rel_l2(M_tc, M_f) < TOL_BF16
+
+
+def test_tensor_core_strong_decay_is_finite():
+    """log r = -5 per step (cumulative -320 per chunk) on the tcgen05 kernel."""
+    B, H, L, D = 1, 2, 200, 64
+    tk, mk, tq, mq, v, logr, beta = _lap_bf16_inputs(9, B, H, L, D, False, logr_fill=-5.0)
+    out, M = dp.laplace_chunkwise(*[to_dev(a, torch.bfloat16) if a is not None else None
+                                    for a in (tk, mk, tq, mq, v, logr, beta)], 64)
+    ref_out, ref_M = _lap_ref(tk, mk, tq, mq, v, logr, beta)
+    assert torch.isfinite(out).all() and torch.isfinite(torch.view_as_real(M)).all()
+    assert rel_l2(out, ref_out) < TOL_BF16
+    assert rel_l2(M, ref_M) < TOL_BF16
