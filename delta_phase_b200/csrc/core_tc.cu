@@ -102,24 +102,9 @@ __device__ __forceinline__ float load_beta(const void *p, int dt, int64_t i) {
   return __half2float(static_cast<const __half *>(p)[i]);
 }
 
-// Warp-level tf32 MMA (m16n8k8, fp32 accumulate) for the small block products of the
-// triangular inverse: operands straight from shared memory into registers, no tensor
-// memory round trip.  Fragment layout (g = lane / 4, c = lane % 4): A a0 (g, c),
-// a1 (g+8, c), a2 (g, c+4), a3 (g+8, c+4); B b0 (c, g), b1 (c+4, g); D d0 (g, 2c),
-// d1 (g, 2c+1), d2 (g+8, 2c), d3 (g+8, 2c+1).
-__device__ __forceinline__ uint32_t to_tf32(float x) {
-  uint32_t r;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-  return r;
-}
-
-__device__ __forceinline__ void mma_tf32_m16n8k8(float (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
-}
+// Warp-level tf32 MMA (to_tf32, mma_tf32_m16n8k8: tc_ptx.cuh) for the small block products of
+// the triangular inverse: operands straight from shared memory into registers, no tensor
+// memory round trip.
 
 // One warp: D[16 x 16] = X[16 x K] Y[K x 16], X(i, k) = x[i * xs_i + k * xs_k],
 // Y(k, j) = y[k * ys_k + j * ys_j] (fp32 in shared memory, tf32 products); D is

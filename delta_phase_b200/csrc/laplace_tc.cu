@@ -13,16 +13,25 @@
 //   out[m] = e^{Lam[m]} B0q[m] + sum_{s<=m} e^{Lam[m]-Lam[s]} beta_s e[s] h[s][m]
 //   S_end = e^{Lam[63]} S0 + sum_s e^{Lam[63]-Lam[s]} beta_s e[s] kap_s
 // with g = K K^T / D, h[s][m] = kap_s . xi_m / D, B0k = K S0^T / D, B0q = Q S0^T / D.
-// tcgen05 (bf16 operands, fp32 TMEM accumulators) computes [K;Q] K^T, [K;Q] S0^T and the
-// state update S^T += K^T W.  The per-channel triangular systems run on the CUDA cores in
-// four 16-token blocks: terms from earlier blocks go through a running accumulator
-//   F[s][o] = e^{Lam[16b-1][o] - Lam[s][o]} beta_s e[s][o]   (rescaled block to block),
-// so every decay factor that is formed is exp(non-positive) -- nothing can overflow --
-// while terms inside a block use exact exp(Lam[m-1] - Lam[s]).  After the last block F is
-// the state-update weight W.  The state decay e^{Lam[63]} is applied in TMEM.
 //
-// One CTA of 256 threads per (batch, head, half of the value channels); inputs stream in
-// two chunks ahead with bulk async copies; every wait is bounded.
+// tcgen05 (bf16 operands, fp32 TMEM accumulators) computes [K;Q] K^T, [K;Q] S0^T and the
+// state update S^T += K^T W.  The per-channel triangular systems are solved in four
+// 16-token blocks b with reference points Lref_b = Lam[16b - 1]:
+//   f[s] = e^{Lref_b - Lam[s]} beta_s e[s]          (s in block b, the block's own scale)
+//   e[m] = v[m] - e^{Lam[m-1]} B0k[m] - e^{Lam[m-1]-Lref_b} (X_b[m] + sum_{s<m in b} g[s][m] f[s])
+//   out[m] = e^{Lam[m]-Lref_b} (e^{Lref_b} B0q[m] + sum_{s<=m} h[s][m] F_b[s])
+// where X_b and the output sums run over earlier blocks' f, rescaled block to block by
+// rho_k = e^{Lref_{k+1} - Lref_k}: warp-level tf32 MMAs with the accumulator rescaled
+// between 16-token K segments.  Inside a block the solve is a plain forward substitution
+// (no exponentials in the loop).  The factorisation needs |Lam[m] - Lref_b| <= 64 inside
+// every block of the chunk, so every factor stays inside fp32 range; a chunk that breaks
+// this (a decay of more than e^-64 within 16 tokens) takes the exact path instead, which
+// forms every decay ratio as exp(difference) <= 1.
+//
+// One CTA of 256 threads per (batch, head, half of the value channels): rows of the state
+// do not interact, so the two halves run independently.  Phases stream in two chunks ahead
+// with bulk async copies; v, log-decay and beta are prefetched a chunk ahead in registers.
+// Every wait is bounded.
 #include "dp_common.cuh"
 #include "tc_ptx.cuh"
 
@@ -41,31 +50,36 @@ constexpr int kNo = 32;         // value channels per CTA
 constexpr int kThreads = 256;
 constexpr uint64_t kTimeoutNs = 2000000000ull;
 constexpr float kLogFloor = -80.0f;
+constexpr float kFastRange = 64.0f;  // max |Lam[m] - Lref_b| for the factorised solve
 
-// stage: theta_k, theta_q, logmag_k, logmag_q rows (128 B), v and log-decay half rows (64 B)
+// stage: theta_k, theta_q, logmag_k, logmag_q rows of a chunk (64 rows x 128 B each)
 constexpr int ST_TK = 0, ST_TQ = kC * 128, ST_MK = 2 * kC * 128, ST_MQ = 3 * kC * 128;
-constexpr int ST_V = 4 * kC * 128, ST_LR = ST_V + kC * 64;
-constexpr int STAGE_BYTES = ST_LR + kC * 64;
+constexpr int STAGE_BYTES = 4 * kC * 128;
 constexpr int RG_KQ = 16 * 128;
 constexpr int RG_32 = 4 * 128;
-constexpr int LDG = 65;   // fp32 64 x 64 matrices
-constexpr int LDO = 33;   // fp32 64 x 32 matrices
+constexpr int LDG = 72;   // g, h: [s][m] fp32
+constexpr int LDM = 72;   // channel-major per-(token, channel) arrays: [o][m] fp32
+constexpr int LDF = 40;   // F: [s][o] fp32
 
 constexpr int OFF_STAGE = 0;                                  // [2]
 constexpr int OFF_KQ = OFF_STAGE + 2 * STAGE_BYTES;          // [K; Q] bf16 128 x 128
 constexpr int OFF_S0 = OFF_KQ + 16 * RG_KQ;                  // S^T bf16 128 x 32
 constexpr int OFF_W = OFF_S0 + 16 * RG_32;                   // W bf16 64 x 32
-constexpr int OFF_G = OFF_W + 8 * RG_32;                     // g[s][m] fp32
-constexpr int OFF_H = OFF_G + kC * LDG * 4;                  // h[s][m] fp32
-constexpr int OFF_BK = OFF_H + kC * LDG * 4;                 // B0k[m][o] fp32
-constexpr int OFF_BQ = OFF_BK + kC * LDO * 4;                // B0q[m][o]
-constexpr int OFF_LAM = OFF_BQ + kC * LDO * 4;               // Lam[m][o]
-constexpr int OFF_E = OFF_LAM + kC * LDO * 4;                // e[m][o]
-constexpr int OFF_F = OFF_E + kC * LDO * 4;                  // F[s][o]
-constexpr int OFF_VF = OFF_F + kC * LDO * 4;                 // v[m][o] fp32
-constexpr int OFF_BETA = OFF_VF + kC * LDO * 4;
+constexpr int OFF_G = OFF_W + 8 * RG_32;                     // g[s][m]
+constexpr int OFF_H = OFF_G + kC * LDG * 4;                  // h[s][m]
+constexpr int OFF_VF = OFF_H + kC * LDG * 4;                 // v[o][m]
+constexpr int OFF_LAM = OFF_VF + kNo * LDM * 4;              // Lam[o][m]
+constexpr int OFF_EA = OFF_LAM + kNo * LDM * 4;              // e^{Lam[m]-Lref}[o][m]; e[o][m] (exact path)
+constexpr int OFF_BK = OFF_EA + kNo * LDM * 4;               // B0k[o][m]
+constexpr int OFF_BQ = OFF_BK + kNo * LDM * 4;               // B0q[o][m]
+constexpr int OFF_F = OFF_BQ + kNo * LDM * 4;                // F[s][o]
+constexpr int OFF_XB = OFF_F + kC * LDF * 4;                 // X of the next block [16][o]
+constexpr int OFF_EREF = OFF_XB + 16 * LDF * 4;              // e^{Lref_b}[b][o]
+constexpr int OFF_RHO = OFF_EREF + 4 * kNo * 4;              // rho_b[b][o]
+constexpr int OFF_BETA = OFF_RHO + 4 * kNo * 4;
 constexpr int OFF_BAR = OFF_BETA + kC * 4;
 constexpr int SMEM_BYTES = OFF_BAR + 64;
+static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 
 constexpr uint32_t COL_S = 0, COL_D1 = 32, COL_D3 = 96, TMEM_COLS = 128;
 
@@ -102,35 +116,46 @@ struct LapTcArgs {
   int *err;
 };
 
-// Bulk copies of chunk rows [c0, c0 + n) into a stage (one warp; lane 0 registers bytes).
-__device__ __forceinline__ void lap_issue_loads(const LapTcArgs &a, int b, int h, int oh, int c0, int n,
-                                                uint8_t *stage, uint64_t *bar, int lane) {
+// Bulk copies of the phase / log-magnitude rows [c0, c0 + n) into a stage (one warp).
+__device__ __forceinline__ void lap_issue_loads(const LapTcArgs &a, int b, int h, int c0, int n, uint8_t *stage,
+                                                uint64_t *bar, int lane) {
   const bool has_mk = a.mk != nullptr, has_mq = a.mq != nullptr;
-  const uint32_t bytes = (uint32_t)n * (128u * (2 + has_mk + has_mq) + 64u * 2);
+  const uint32_t bytes = (uint32_t)n * 128u * (2 + has_mk + has_mq);
   if (lane == 0) mbar_arrive_expect_tx(bar, bytes);
   __syncwarp();
-  const __nv_bfloat16 *src128[4] = {a.tk + b * a.s_tk.b + h * a.s_tk.h + (int64_t)c0 * a.s_tk.t,
-                                    a.tq + b * a.s_tq.b + h * a.s_tq.h + (int64_t)c0 * a.s_tq.t,
-                                    has_mk ? a.mk + b * a.s_mk.b + h * a.s_mk.h + (int64_t)c0 * a.s_mk.t : nullptr,
-                                    has_mq ? a.mq + b * a.s_mq.b + h * a.s_mq.h + (int64_t)c0 * a.s_mq.t : nullptr};
-  const int64_t st128[4] = {a.s_tk.t, a.s_tq.t, a.s_mk.t, a.s_mq.t};
-  const int off128[4] = {ST_TK, ST_TQ, ST_MK, ST_MQ};
+  const __nv_bfloat16 *src[4] = {a.tk + b * a.s_tk.b + h * a.s_tk.h + (int64_t)c0 * a.s_tk.t,
+                                 a.tq + b * a.s_tq.b + h * a.s_tq.h + (int64_t)c0 * a.s_tq.t,
+                                 has_mk ? a.mk + b * a.s_mk.b + h * a.s_mk.h + (int64_t)c0 * a.s_mk.t : nullptr,
+                                 has_mq ? a.mq + b * a.s_mq.b + h * a.s_mq.h + (int64_t)c0 * a.s_mq.t : nullptr};
+  const int64_t st[4] = {a.s_tk.t, a.s_tq.t, a.s_mk.t, a.s_mq.t};
+  const int off[4] = {ST_TK, ST_TQ, ST_MK, ST_MQ};
 #pragma unroll
   for (int x = 0; x < 4; ++x) {
-    if (!src128[x]) continue;
-    if (st128[x] == 64) {
-      if (lane == 0) bulk_g2s(stage + off128[x], src128[x], (uint32_t)(n * 128), bar);
+    if (!src[x]) continue;
+    if (st[x] == 64) {
+      if (lane == 0) bulk_g2s(stage + off[x], src[x], (uint32_t)(n * 128), bar);
     } else {
-      for (int t = lane; t < n; t += 32) bulk_g2s(stage + off128[x] + t * 128, src128[x] + t * st128[x], 128u, bar);
+      for (int t = lane; t < n; t += 32) bulk_g2s(stage + off[x] + t * 128, src[x] + t * st[x], 128u, bar);
     }
   }
-  const __nv_bfloat16 *src64[2] = {a.v + b * a.s_v.b + h * a.s_v.h + (int64_t)c0 * a.s_v.t + kNo * oh,
-                                   a.lr + b * a.s_lr.b + h * a.s_lr.h + (int64_t)c0 * a.s_lr.t + kNo * oh};
-  const int64_t st64[2] = {a.s_v.t, a.s_lr.t};
-  const int off64[2] = {ST_V, ST_LR};
-#pragma unroll
-  for (int x = 0; x < 2; ++x)
-    for (int t = lane; t < n; t += 32) bulk_g2s(stage + off64[x] + t * 64, src64[x] + t * st64[x], 64u, bar);
+}
+
+// Register prefetch of chunk c's v and log-decay slices (thread: token tid % 64, channels
+// 8 (tid / 64) .. + 7 of this CTA's half) and beta (threads 0..63).  Past the end: v = 0,
+// log r = 0, beta = 0 -- the reference's padding.
+__device__ __forceinline__ void prefetch_vlr(const LapTcArgs &a, int b, int h, int oh, int c, int tid, uint4 &pv,
+                                             uint4 &pl, float &pb) {
+  const int tt = tid & 63, q4 = tid >> 6, t = c * kC + tt;
+  pv = make_uint4(0, 0, 0, 0);
+  pl = pv;
+  pb = 0.f;
+  if (t < a.L) {
+    pv = __ldg(reinterpret_cast<const uint4 *>(a.v + b * a.s_v.b + h * a.s_v.h + (int64_t)t * a.s_v.t + kNo * oh + 8 * q4));
+    pl = __ldg(reinterpret_cast<const uint4 *>(a.lr + b * a.s_lr.b + h * a.s_lr.h + (int64_t)t * a.s_lr.t + kNo * oh +
+                                               8 * q4));
+  }
+  const int tb = c * kC + tid;
+  if (tid < kC && tb < a.L) pb = load_beta(a.beta, a.beta_dt, b * a.s_b.b + h * a.s_b.h + (int64_t)tb * a.s_b.t);
 }
 
 __global__ void __launch_bounds__(kThreads, 1) laplace_tc_kernel(LapTcArgs a) {
@@ -140,12 +165,15 @@ __global__ void __launch_bounds__(kThreads, 1) laplace_tc_kernel(LapTcArgs a) {
   uint8_t *wt = smem + OFF_W;
   float *gm = reinterpret_cast<float *>(smem + OFF_G);
   float *hm = reinterpret_cast<float *>(smem + OFF_H);
-  float *bk = reinterpret_cast<float *>(smem + OFF_BK);
-  float *bq = reinterpret_cast<float *>(smem + OFF_BQ);
-  float *lam = reinterpret_cast<float *>(smem + OFF_LAM);
-  float *ev = reinterpret_cast<float *>(smem + OFF_E);
+  float *vfT = reinterpret_cast<float *>(smem + OFF_VF);
+  float *lamT = reinterpret_cast<float *>(smem + OFF_LAM);
+  float *eaT = reinterpret_cast<float *>(smem + OFF_EA);
+  float *bkT = reinterpret_cast<float *>(smem + OFF_BK);
+  float *bqT = reinterpret_cast<float *>(smem + OFF_BQ);
   float *fv = reinterpret_cast<float *>(smem + OFF_F);
-  float *vf = reinterpret_cast<float *>(smem + OFF_VF);
+  float *xb = reinterpret_cast<float *>(smem + OFF_XB);
+  float *eref = reinterpret_cast<float *>(smem + OFF_EREF);
+  float *rho = reinterpret_cast<float *>(smem + OFF_RHO);
   float *bs = reinterpret_cast<float *>(smem + OFF_BETA);
   uint64_t *mma_bar = reinterpret_cast<uint64_t *>(smem + OFF_BAR);
   uint64_t *load_bar = mma_bar + 1;  // [2]
@@ -175,9 +203,11 @@ __global__ void __launch_bounds__(kThreads, 1) laplace_tc_kernel(LapTcArgs a) {
 
   if (warp == 0) {
     for (int c = 0; c < 2 && c < nchunks; ++c)
-      lap_issue_loads(a, b, h, oh, c * kC, min(kC, L - c * kC), smem + OFF_STAGE + c * STAGE_BYTES,
-                      &load_bar[c], lane);
+      lap_issue_loads(a, b, h, c * kC, min(kC, L - c * kC), smem + OFF_STAGE + c * STAGE_BYTES, &load_bar[c], lane);
   }
+  uint4 pv, pl;
+  float pb;
+  prefetch_vlr(a, b, h, oh, 0, tid, pv, pl, pb);
   // state^T of this CTA's 32 value channels -> TMEM (lane = feature j, column = o)
   const int64_t sbase = (int64_t)unit * kDv * kF;
   if (warp < 4) {
@@ -198,17 +228,17 @@ __global__ void __launch_bounds__(kThreads, 1) laplace_tc_kernel(LapTcArgs a) {
   uint32_t mma_phase = 0;
   bool ok = true, mma_pending = false;
   int issued = min(nchunks, 2), consumed = 0;
-  // solve layout: thread (o = tid / 8, j = tid % 8) owns tokens m = j, j + 8, ... of channel o
-  const int so = tid >> 3, sj = tid & 7;
+  const int g8 = lane >> 2, t4 = lane & 3;  // mma.sync fragment coordinates
 
   for (int c = 0; c < nchunks; ++c) {
     const int t0 = c * kC, nvalid = min(kC, L - t0), st = c & 1;
     uint8_t *stage = smem + OFF_STAGE + st * STAGE_BYTES;
+    float *obase = a.out + b * a.s_out.b + h * a.s_out.h + (int64_t)t0 * a.s_out.t + kNo * oh;
     if (tid == 0) ok = mbar_wait(&load_bar[st], (uint32_t)((c >> 1) & 1), kTimeoutNs);
     if (__syncthreads_or(!ok)) { ok = false; break; }
     consumed = c + 1;
 
-    // ---- L1: phasors (with magnitudes) -> [K; Q] bf16; v, beta, cumulative log-decay
+    // ---- L1: phasors (with magnitudes) -> [K; Q] bf16; v, log-decay, beta -> shared
     {
 #pragma unroll
       for (int r = 0; r < 2; ++r) {
@@ -253,28 +283,21 @@ __global__ void __launch_bounds__(kThreads, 1) laplace_tc_kernel(LapTcArgs a) {
               make_uint4(qw[4 * half], qw[4 * half + 1], qw[4 * half + 2], qw[4 * half + 3]);
         }
       }
-      // v and log-decay of this CTA's channels (fp32), beta
-      for (int i = tid; i < kC * kNo; i += kThreads) {
-        const int t = i >> 5, o = i & 31;
-        const bool valid = t < nvalid;
-        vf[t * LDO + o] = valid ? __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(stage + ST_V + t * 64)[o]) : 0.f;
-        lam[t * LDO + o] = valid ? fmaxf(__bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(stage + ST_LR + t * 64)[o]), kLogFloor) : 0.f;
+      {
+        const int tt = tid & 63, q4 = tid >> 6;
+        const uint32_t vw[4] = {pv.x, pv.y, pv.z, pv.w}, lw[4] = {pl.x, pl.y, pl.z, pl.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 vv = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&vw[i]));
+          const float2 ll = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&lw[i]));
+          vfT[(8 * q4 + 2 * i) * LDM + tt] = vv.x;
+          vfT[(8 * q4 + 2 * i + 1) * LDM + tt] = vv.y;
+          lamT[(8 * q4 + 2 * i) * LDM + tt] = fmaxf(ll.x, kLogFloor);
+          lamT[(8 * q4 + 2 * i + 1) * LDM + tt] = fmaxf(ll.y, kLogFloor);
+        }
+        if (tid < kC) bs[tid] = pb;
       }
-      if (tid < kC)
-        bs[tid] = tid < nvalid ? load_beta(a.beta, a.beta_dt, b * a.s_b.b + h * a.s_b.h + (int64_t)(t0 + tid) * a.s_b.t) : 0.f;
-    }
-    __syncthreads();
-    // cumulative log-decay along the chunk (one thread per channel) and the next loads
-    if (tid < kNo) {
-      float acc = 0.f;
-      for (int t = 0; t < kC; ++t) {
-        acc += lam[t * LDO + tid];
-        lam[t * LDO + tid] = acc;
-      }
-    }
-    if (c + 2 < nchunks) {
-      if (warp == 7) lap_issue_loads(a, b, h, oh, t0 + 2 * kC, min(kC, L - t0 - 2 * kC), stage, &load_bar[st], lane);
-      issued = c + 3;
+      if (c + 1 < nchunks) prefetch_vlr(a, b, h, oh, c + 1, tid, pv, pl, pb);
     }
     // ---- L2: S^T (TMEM fp32) -> bf16 operand (128 x 32), MN-major B of [K;Q] S0^T
     if (warp < 4) {
@@ -309,14 +332,54 @@ __global__ void __launch_bounds__(kThreads, 1) laplace_tc_kernel(LapTcArgs a) {
       mma_commit(mma_bar);
     }
     mma_pending = true;
+    if (c + 2 < nchunks) {
+      if (warp == 7) lap_issue_loads(a, b, h, t0 + 2 * kC, min(kC, L - t0 - 2 * kC), stage, &load_bar[st], lane);
+      issued = c + 3;
+    }
+    // ---- decay: cumulative log-decay, block-relative factors (overlaps the MMAs)
+    bool bad;
+    {
+      const int o = tid >> 3, p = tid & 7;  // channel o, tokens 8p .. 8p + 7
+      float *lo = lamT + o * LDM + 8 * p;
+      const float4 x0 = *reinterpret_cast<const float4 *>(lo), x1 = *reinterpret_cast<const float4 *>(lo + 4);
+      float l[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+      for (int i = 1; i < 8; ++i) l[i] += l[i - 1];
+      float tot = l[7];
+#pragma unroll
+      for (int d = 1; d < 8; d <<= 1) {
+        const float n = __shfl_up_sync(0xffffffffu, tot, d, 8);
+        if (p >= d) tot += n;
+      }
+      const float excl = tot - l[7];
+      const float excl_prev = __shfl_up_sync(0xffffffffu, excl, 1, 8);
+      const float lref = (p & 1) ? excl_prev : excl;  // Lam[16 (p / 2) - 1]
+      float e[8], dev = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        l[i] += excl;
+        const float d = l[i] - lref;
+        e[i] = __expf(d);
+        dev = fmaxf(dev, fabsf(d));
+      }
+      *reinterpret_cast<float4 *>(lo) = make_float4(l[0], l[1], l[2], l[3]);
+      *reinterpret_cast<float4 *>(lo + 4) = make_float4(l[4], l[5], l[6], l[7]);
+      float *eo = eaT + o * LDM + 8 * p;
+      *reinterpret_cast<float4 *>(eo) = make_float4(e[0], e[1], e[2], e[3]);
+      *reinterpret_cast<float4 *>(eo + 4) = make_float4(e[4], e[5], e[6], e[7]);
+      if (p & 1) rho[(p >> 1) * kNo + o] = e[7];
+      else eref[(p >> 1) * kNo + o] = __expf(lref);
+      bad = !(dev <= kFastRange);
+    }
     if (tid == 0) ok = mbar_wait(mma_bar, mma_phase, kTimeoutNs);
     if (__syncthreads_or(!ok)) { ok = false; break; }
     mma_phase ^= 1;
     mma_pending = false;
+    const bool fast = !__syncthreads_or(bad);
     tc_fence_after();
 
-    // ---- L4: g[s][m] = K K^T / D (rows 0..63), h[s][m] = kap_s . xi_m / D (rows 64..127
-    //      hold (Q K^T)[m][s]); B0k, B0q from [K;Q] S0^T.  Warps 0..3 and 4..7 split columns.
+    // ---- L4: g[s][m] = K K^T / D (rows 0..63, symmetric), h[s][m] = kap_s . xi_m / D
+    //      (rows 64..127 hold (Q K^T)[m][s]); B0k, B0q channel-major from [K;Q] S0^T.
     {
       const int row = 32 * q + lane, hf = warp >> 2;
 #pragma unroll
@@ -327,8 +390,8 @@ __global__ void __launch_bounds__(kThreads, 1) laplace_tc_kernel(LapTcArgs a) {
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           const int col = 32 * hf + 16 * u + i;
-          if (row < 64) gm[row * LDG + col] = d[i] * inv_d;        // g symmetric
-          else hm[col * LDG + (row - 64)] = d[i] * inv_d;           // h[s = col][m = row - 64]
+          if (row < 64) gm[col * LDG + row] = d[i] * inv_d;
+          else hm[col * LDG + (row - 64)] = d[i] * inv_d;
         }
       }
       float d[16];
@@ -337,45 +400,141 @@ __global__ void __launch_bounds__(kThreads, 1) laplace_tc_kernel(LapTcArgs a) {
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
         const int o = 16 * hf + i;
-        if (row < 64) bk[row * LDO + o] = d[i] * inv_d;
-        else bq[(row - 64) * LDO + o] = d[i] * inv_d;
+        if (row < 64) bkT[o * LDM + row] = d[i] * inv_d;
+        else bqT[o * LDM + (row - 64)] = d[i] * inv_d;
       }
     }
     tc_fence_before();
     __syncthreads();
 
-    // ---- L5: per-channel triangular solve and outputs, four 16-token blocks
-    {
-      const int o = so;
-      float *orow = a.out + b * a.s_out.b + h * a.s_out.h + (int64_t)t0 * a.s_out.t + kNo * oh + o;
+    const int so = tid >> 3, sj = tid & 7;  // solve layout: channel so, tokens m0 + sj, m0 + 8 + sj
+    if (fast) {
+      // ---- L5: factorised blocked solve; W written straight to its bf16 operand
+      const float l63 = lamT[so * LDM + 63];
       for (int blk = 0; blk < 4; ++blk) {
         const int m0 = 16 * blk;
-        const float lref = blk > 0 ? lam[(m0 - 1) * LDO + o] : 0.f;  // Lam[16 blk - 1]
-        // owned tokens of this block: m0 + sj, m0 + 8 + sj
+        {
+          const float er = eref[blk * kNo + so];
+          float R[2], A[2], Bt[2], y[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int m = m0 + 8 * u + sj;
+            const float ap = eaT[so * LDM + m];
+            const float am = (8 * u + sj == 0) ? 1.f : eaT[so * LDM + m - 1];
+            R[u] = fmaf(-er * am, bkT[so * LDM + m], vfT[so * LDM + m]);
+            A[u] = am;
+            Bt[u] = __fdividef(bs[m], ap);
+            y[u] = blk ? xb[(8 * u + sj) * LDF + so] : 0.f;
+          }
+#pragma unroll
+          for (int s8 = 0; s8 < 16; ++s8) {
+            const int uo = s8 >> 3;
+            const float f_own = Bt[uo] * fmaf(-A[uo], y[uo], R[uo]);
+            const float f = __shfl_sync(0xffffffffu, f_own, (lane & ~7) | (s8 & 7));
+#pragma unroll
+            for (int u = 0; u < 2; ++u)
+              if (8 * u + sj > s8) y[u] = fmaf(gm[(m0 + s8) * LDG + m0 + 8 * u + sj], f, y[u]);
+          }
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int m = m0 + 8 * u + sj;
+            const float e = fmaf(-A[u], y[u], R[u]);
+            fv[m * LDF + so] = Bt[u] * e;
+            const float w = __expf(l63 - lamT[so * LDM + m]) * bs[m] * e;
+            *reinterpret_cast<__nv_bfloat16 *>(wt + cm_off(m, so, RG_32)) = __float2bfloat16_rn(w);
+          }
+        }
+        __syncthreads();
+        if (blk < 3) {
+          // X of the next block: rows 16 (blk + 1) .., warps 0..3 one 8-channel tile each
+          if (warp < 4) {
+            const int n0 = 8 * warp, r0 = m0 + 16;
+            float acc[4] = {0.f, 0.f, 0.f, 0.f};
+            for (int seg = 0; seg <= blk; ++seg) {
+              if (seg > 0) {
+                const float ra = rho[(seg - 1) * kNo + n0 + 2 * t4], rb = rho[(seg - 1) * kNo + n0 + 2 * t4 + 1];
+                acc[0] *= ra; acc[1] *= rb; acc[2] *= ra; acc[3] *= rb;
+              }
+#pragma unroll
+              for (int k8 = 0; k8 < 2; ++k8) {
+                const int k0 = 16 * seg + 8 * k8;
+                const uint32_t af[4] = {to_tf32(gm[(k0 + t4) * LDG + r0 + g8]), to_tf32(gm[(k0 + t4) * LDG + r0 + g8 + 8]),
+                                        to_tf32(gm[(k0 + t4 + 4) * LDG + r0 + g8]),
+                                        to_tf32(gm[(k0 + t4 + 4) * LDG + r0 + g8 + 8])};
+                const uint32_t bf[2] = {to_tf32(fv[(k0 + t4) * LDF + n0 + g8]), to_tf32(fv[(k0 + t4 + 4) * LDF + n0 + g8])};
+                mma_tf32_m16n8k8(acc, af, bf);
+              }
+            }
+            const float ra = rho[blk * kNo + n0 + 2 * t4], rb = rho[blk * kNo + n0 + 2 * t4 + 1];
+            xb[g8 * LDF + n0 + 2 * t4] = acc[0] * ra;
+            xb[g8 * LDF + n0 + 2 * t4 + 1] = acc[1] * rb;
+            xb[(g8 + 8) * LDF + n0 + 2 * t4] = acc[2] * ra;
+            xb[(g8 + 8) * LDF + n0 + 2 * t4 + 1] = acc[3] * rb;
+          }
+          __syncthreads();
+        }
+      }
+      // ---- L5o: outputs, 16 tiles (4 blocks x 4 channel tiles) over 8 warps
+#pragma unroll 1
+      for (int rep = 0; rep < 2; ++rep) {
+        const int blk = rep == 0 ? (warp >> 2) : 3 - (warp >> 2);
+        const int n0 = 8 * (warp & 3), r0 = 16 * blk;
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int seg = 0; seg <= blk; ++seg) {
+          if (seg > 0) {
+            const float ra = rho[(seg - 1) * kNo + n0 + 2 * t4], rb = rho[(seg - 1) * kNo + n0 + 2 * t4 + 1];
+            acc[0] *= ra; acc[1] *= rb; acc[2] *= ra; acc[3] *= rb;
+          }
+#pragma unroll
+          for (int k8 = 0; k8 < 2; ++k8) {
+            const int k0 = 16 * seg + 8 * k8;
+            const int sa = k0 + t4, sb = k0 + t4 + 4, ma = r0 + g8, mb = r0 + g8 + 8;
+            const uint32_t af[4] = {to_tf32(sa <= ma ? hm[sa * LDG + ma] : 0.f), to_tf32(sa <= mb ? hm[sa * LDG + mb] : 0.f),
+                                    to_tf32(sb <= ma ? hm[sb * LDG + ma] : 0.f), to_tf32(sb <= mb ? hm[sb * LDG + mb] : 0.f)};
+            const uint32_t bf[2] = {to_tf32(fv[sa * LDF + n0 + g8]), to_tf32(fv[sb * LDF + n0 + g8])};
+            mma_tf32_m16n8k8(acc, af, bf);
+          }
+        }
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const int m = r0 + g8 + 8 * hh;
+          if (m < nvalid) {
+#pragma unroll
+            for (int cc = 0; cc < 2; ++cc) {
+              const int o = n0 + 2 * t4 + cc;
+              const float val = eaT[o * LDM + m] * fmaf(eref[blk * kNo + o], bqT[o * LDM + m], acc[2 * hh + cc]);
+              obase[(int64_t)m * a.s_out.t + o] = val;
+            }
+          }
+        }
+      }
+    } else {
+      // ---- L5x: exact path, every decay ratio formed as exp(difference) <= 1
+      float *ev = eaT;
+      const float *lo = lamT + so * LDM;
+      for (int blk = 0; blk < 4; ++blk) {
+        const int m0 = 16 * blk;
+        const float lref = blk > 0 ? lo[m0 - 1] : 0.f;
         float rhs[2], xo[2], lprev[2];
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
           const int m = m0 + 8 * u + sj;
-          const float lmm1 = m > 0 ? lam[(m - 1) * LDO + o] : 0.f;
+          const float lmm1 = m > 0 ? lo[m - 1] : 0.f;
           lprev[u] = lmm1;
-          // terms of earlier blocks through F (exp(<= 0) factors only)
           float xs = 0.f, xq = 0.f;
           for (int s = 0; s < m0; ++s) {
-            const float f = fv[s * LDO + o];
+            const float f = fv[s * LDF + so];
             xs = fmaf(gm[s * LDG + m], f, xs);
             xq = fmaf(hm[s * LDG + m], f, xq);
           }
-          rhs[u] = vf[m * LDO + o] - __expf(lmm1) * bk[m * LDO + o] - __expf(lmm1 - lref) * xs;
-          xo[u] = __expf(lam[m * LDO + o] - lref) * xq;
+          rhs[u] = vfT[so * LDM + m] - __expf(lmm1) * bkT[so * LDM + m] - __expf(lmm1 - lref) * xs;
+          xo[u] = __expf(lo[m] - lref) * xq;
         }
-        // in-block forward substitution (right-looking over s; owner of s = lane % 8)
 #pragma unroll
         for (int s8 = 0; s8 < 16; ++s8) {
           const int s = m0 + s8;
-          const int owner_u = s8 >> 3;
-          const float es_own = rhs[owner_u];
-          const float es = __shfl_sync(0xffffffffu, es_own, (lane & ~7) | (s8 & 7));
-          const float ls = lam[s * LDO + o];
+          const float es = __shfl_sync(0xffffffffu, rhs[s8 >> 3], (lane & ~7) | (s8 & 7));
+          const float ls = lo[s];
           const float bes = bs[s] * es;
 #pragma unroll
           for (int u = 0; u < 2; ++u) {
@@ -383,40 +542,37 @@ __global__ void __launch_bounds__(kThreads, 1) laplace_tc_kernel(LapTcArgs a) {
             if (m > s) rhs[u] -= __expf(lprev[u] - ls) * gm[s * LDG + m] * bes;
           }
         }
-        // e of the owned tokens; in-block output terms need e of the whole block
 #pragma unroll
-        for (int u = 0; u < 2; ++u) ev[(m0 + 8 * u + sj) * LDO + o] = rhs[u];
+        for (int u = 0; u < 2; ++u) ev[so * LDM + m0 + 8 * u + sj] = rhs[u];
         __syncwarp();
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
           const int m = m0 + 8 * u + sj;
-          const float lm = lam[m * LDO + o];
-          float acc = __expf(lm) * bq[m * LDO + o] + xo[u];
-          for (int s = m0; s <= m; ++s)
-            acc = fmaf(__expf(lm - lam[s * LDO + o]) * bs[s] * ev[s * LDO + o], hm[s * LDG + m], acc);
-          if (m < nvalid) orow[(int64_t)m * a.s_out.t] = acc;
+          const float lm = lo[m];
+          float acc = __expf(lm) * bqT[so * LDM + m] + xo[u];
+          for (int s = m0; s <= m; ++s) acc = fmaf(__expf(lm - lo[s]) * bs[s] * ev[so * LDM + s], hm[s * LDG + m], acc);
+          if (m < nvalid) obase[(int64_t)m * a.s_out.t + so] = acc;
         }
-        // F for the next block: rescale the old terms, add this block's
-        const float lend = lam[(m0 + 15) * LDO + o];
+        const float lend = lo[m0 + 15];
         const float scale = __expf(lend - lref);
-        for (int s = sj; s < m0; s += 8) fv[s * LDO + o] *= scale;
+        for (int s = sj; s < m0; s += 8) fv[s * LDF + so] *= scale;
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
           const int s = m0 + 8 * u + sj;
-          fv[s * LDO + o] = __expf(lend - lam[s * LDO + o]) * bs[s] * rhs[u];
+          fv[s * LDF + so] = __expf(lend - lo[s]) * bs[s] * rhs[u];
         }
         __syncwarp();
       }
-    }
-    __syncthreads();
-    // W = F (exp(Lam[63] - Lam[s]) beta_s e_s) -> bf16 (64 tokens x 32 channels)
-    {
-      const int s = tid >> 2, o0 = 8 * (tid & 3);
-      float w[8];
+      __syncthreads();
+      // W = F (= exp(Lam[63] - Lam[s]) beta_s e_s) -> bf16 (64 tokens x 32 channels)
+      {
+        const int s = tid >> 2, o0 = 8 * (tid & 3);
+        float w[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) w[i] = fv[s * LDO + o0 + i];
-      *reinterpret_cast<uint4 *>(wt + cm_off(s, o0, RG_32)) =
-          make_uint4(pack_bf16(w[0], w[1]), pack_bf16(w[2], w[3]), pack_bf16(w[4], w[5]), pack_bf16(w[6], w[7]));
+        for (int i = 0; i < 8; ++i) w[i] = fv[s * LDF + o0 + i];
+        *reinterpret_cast<uint4 *>(wt + cm_off(s, o0, RG_32)) =
+            make_uint4(pack_bf16(w[0], w[1]), pack_bf16(w[2], w[3]), pack_bf16(w[4], w[5]), pack_bf16(w[6], w[7]));
+      }
     }
     // state decay in TMEM:  S^T[j][o] *= exp(Lam[63][o])
     if (warp < 4) {
@@ -426,7 +582,7 @@ __global__ void __launch_bounds__(kThreads, 1) laplace_tc_kernel(LapTcArgs a) {
         tmem_ld16(tmem + lane_base + COL_S + 16 * u, sv);
         tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 16; ++i) sv[i] *= __expf(lam[63 * LDO + 16 * u + i]);
+        for (int i = 0; i < 16; ++i) sv[i] *= __expf(lamT[(16 * u + i) * LDM + 63]);
         tmem_st16(tmem + lane_base + COL_S + 16 * u, sv);
       }
       tmem_st_wait();
@@ -477,7 +633,8 @@ __global__ void __launch_bounds__(kThreads, 1) laplace_tc_kernel(LapTcArgs a) {
 
 }  // namespace
 
-// True if dp_laplace_fwd's arguments fit the tensor-core kernel.
+// True if dp_laplace_fwd's arguments fit the tensor-core kernel: bf16, d_k = d_v = 64,
+// 16-byte aligned inputs with strides in whole 16-byte units.
 bool laplace_tc_supported(const void *const *ptrs, int in_dt, const float *out, int D, int Dv,
                           const SeqStrides *s) {
   if (in_dt != DP_BF16 || D != 64 || Dv != 64) return false;

@@ -182,6 +182,25 @@ __device__ __forceinline__ void tmem_st_wait() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
+// ---------------------------------------------------------------- warp-level tf32 MMA
+// mma.sync m16n8k8 (fp32 accumulate) for small products whose operands sit in shared
+// memory.  Fragment layout (g = lane / 4, c = lane % 4): A a0 (g, c), a1 (g+8, c),
+// a2 (g, c+4), a3 (g+8, c+4); B b0 (c, g), b1 (c+4, g); D d0 (g, 2c), d1 (g, 2c+1),
+// d2 (g+8, 2c), d3 (g+8, 2c+1).
+__device__ __forceinline__ uint32_t to_tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+
+__device__ __forceinline__ void mma_tf32_m16n8k8(float (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+
 // ---------------------------------------------------------------- descriptors
 // Shared-memory matrix descriptor, SWIZZLE_NONE canonical layout: core matrices of
 // 8 rows x 16 bytes stored contiguously; `lbo` = byte distance between core matrices

@@ -162,3 +162,19 @@ def test_tensor_core_strong_decay_is_finite():
     assert torch.isfinite(out).all() and torch.isfinite(torch.view_as_real(M)).all()
     assert rel_l2(out, ref_out) < TOL_BF16
     assert rel_l2(M, ref_M) < TOL_BF16
+
+
+@pytest.mark.parametrize("fill", [-3.5, None])
+def test_tensor_core_large_factors_and_mixed_paths(fill):
+    """log r = -3.5 per step: block-relative factors up to e^56 on the factorised solve.
+    None: ordinary decay with a burst of log r = -6 over tokens 100..139, so some chunks
+    take the exact path and the others the factorised one."""
+    B, H, L, D = 1, 2, 320, 64
+    tk, mk, tq, mq, v, logr, beta = _lap_bf16_inputs(11, B, H, L, D, True, logr_fill=fill)
+    if fill is None:
+        logr[:, :, 100:140, :] = -6.0
+    out, M = dp.laplace_chunkwise(*[to_dev(a, torch.bfloat16) for a in (tk, mk, tq, mq, v, logr, beta)], 64)
+    ref_out, ref_M = _lap_ref(tk, mk, tq, mq, v, logr, beta)
+    assert torch.isfinite(out).all()
+    assert rel_l2(out, ref_out) < TOL_BF16
+    assert rel_l2(M, ref_M) < TOL_BF16
