@@ -225,9 +225,9 @@ __device__ bool prep_role(const TcArgs &a, uint8_t *smem, Bars *bars, uint32_t t
     //      every 16-byte bank group 4 times (segment), and so does each store into the
     //      core-matrix tiles (row % 8): both are conflict-free 512-byte accesses.
     {
-      float bnext = 0.f;
+      uint32_t bnext = 0u;  // raw bits; converted at the store below, after the phasor work
       if (tid < kC && t0 + kC + tid < L)
-        bnext = load_beta(a.beta, a.beta_dt, b * a.s_b.b + h * a.s_b.h + (int64_t)(t0 + kC + tid) * a.s_b.t);
+        bnext = load_raw_scalar(a.beta, a.beta_dt, b * a.s_b.b + h * a.s_b.h + (int64_t)(t0 + kC + tid) * a.s_b.t);
 #pragma unroll
       for (int r = 0; r < 2; ++r) {
         const int t = 8 * warp + (lane & 7), sg = ((lane >> 3) + 2 * (lane & 7) + 4 * r) & 7;
@@ -268,7 +268,7 @@ __device__ bool prep_role(const TcArgs &a, uint8_t *smem, Bars *bars, uint32_t t
         }
         *reinterpret_cast<uint4 *>(vb + cm_off(t, 8 * sg, RG_64)) = vraw;
       }
-      if (tid < kC) bs2[(slot ^ 1) * kC + tid] = bnext;
+      if (tid < kC) bs2[(slot ^ 1) * kC + tid] = raw_scalar_to_f32(bnext, a.beta_dt);
     }
     fence_proxy_async_smem();
     group_sync(BAR_PREP, kPrepThreads);

@@ -44,6 +44,19 @@ __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float x) { retu
 template <>
 __device__ __forceinline__ __half from_f32<__half>(float x) { return __float2half_rn(x); }
 
+// Scalar of runtime dtype dt, loaded as raw bits and converted later: a prefetch whose
+// value is needed only after other work must not convert at the load (the conversion
+// would wait for the load).
+__device__ __forceinline__ uint32_t load_raw_scalar(const void *p, int dt, int64_t i) {
+  if (dt == DP_F32) return __ldg(static_cast<const unsigned int *>(p) + i);
+  return __ldg(static_cast<const unsigned short *>(p) + i);
+}
+__device__ __forceinline__ float raw_scalar_to_f32(uint32_t raw, int dt) {
+  if (dt == DP_F32) return __uint_as_float(raw);
+  if (dt == DP_BF16) return __uint_as_float(raw << 16);
+  return __half2float(__ushort_as_half(static_cast<unsigned short>(raw)));
+}
+
 inline bool valid_dtype(int dt) { return dt == DP_F32 || dt == DP_BF16 || dt == DP_F16; }
 inline size_t dtype_size(int dt) { return dt == DP_F32 ? 4 : 2; }
 

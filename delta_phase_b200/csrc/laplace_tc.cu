@@ -32,6 +32,8 @@
 // do not interact, so the two halves run independently.  Phases stream in two chunks ahead
 // with bulk async copies; v, log-decay and beta are prefetched a chunk ahead in registers.
 // Every wait is bounded.
+#include <type_traits>
+
 #include "dp_common.cuh"
 #include "tc_ptx.cuh"
 
@@ -58,7 +60,7 @@ constexpr int STAGE_BYTES = 4 * kC * 128;
 constexpr int RG_KQ = 16 * 128;
 constexpr int RG_32 = 4 * 128;
 constexpr int LDG = 72;   // g, h: [s][m] fp32
-constexpr int LDM = 72;   // channel-major per-(token, channel) arrays: [o][m] fp32
+constexpr int LDM = 68;   // channel-major per-(token, channel) arrays: [o][m] fp32
 constexpr int LDF = 40;   // F: [s][o] fp32
 
 constexpr int OFF_STAGE = 0;                                  // [2]
@@ -70,16 +72,23 @@ constexpr int OFF_H = OFF_G + kC * LDG * 4;                  // h[s][m]
 constexpr int OFF_VF = OFF_H + kC * LDG * 4;                 // v[o][m]
 constexpr int OFF_LAM = OFF_VF + kNo * LDM * 4;              // Lam[o][m]
 constexpr int OFF_EA = OFF_LAM + kNo * LDM * 4;              // e^{Lam[m]-Lref}[o][m]; e[o][m] (exact path)
-constexpr int OFF_BK = OFF_EA + kNo * LDM * 4;               // B0k[o][m]
-constexpr int OFF_BQ = OFF_BK + kNo * LDM * 4;               // B0q[o][m]
+constexpr int OFF_BK = OFF_EA + kNo * LDM * 4;               // B0k[o][m]; R[o][m] (factorised path)
+constexpr int OFF_BT = OFF_BK + kNo * LDM * 4;               // e^{Lref - Lam[m]} beta_m [o][m]
+constexpr int OFF_BQ = OFF_BT + kNo * LDM * 4;               // B0q[o][m]
 constexpr int OFF_F = OFF_BQ + kNo * LDM * 4;                // F[s][o]
 constexpr int OFF_XB = OFF_F + kC * LDF * 4;                 // X of the next block [16][o]
 constexpr int OFF_EREF = OFF_XB + 16 * LDF * 4;              // e^{Lref_b}[b][o]
 constexpr int OFF_RHO = OFF_EREF + 4 * kNo * 4;              // rho_b[b][o]
-constexpr int OFF_BETA = OFF_RHO + 4 * kNo * 4;
+constexpr int OFF_EDEC = OFF_RHO + 4 * kNo * 4;             // e^{Lam[63]}[o]
+constexpr int OFF_WSC = OFF_EDEC + kNo * 4;                // e^{Lam[63] - Lref_b}[b][o]
+constexpr int OFF_BETA = OFF_WSC + 4 * kNo * 4;
 constexpr int OFF_BAR = OFF_BETA + kC * 4;
 constexpr int SMEM_BYTES = OFF_BAR + 64;
 static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
+static_assert(OFF_VF % 16 == 0 && OFF_LAM % 16 == 0 && OFF_EA % 16 == 0 && OFF_BK % 16 == 0 && OFF_BT % 16 == 0 &&
+                  OFF_F % 16 == 0 && OFF_G % 16 == 0 && OFF_BETA % 16 == 0 && (LDM * 4) % 16 == 0 &&
+                  (LDF * 4) % 16 == 0 && (LDG * 4) % 16 == 0,
+              "float4 accesses need 16-byte aligned rows");
 
 constexpr uint32_t COL_S = 0, COL_D1 = 32, COL_D3 = 96, TMEM_COLS = 128;
 
@@ -97,12 +106,6 @@ __device__ __forceinline__ void fast_sincos(float x, float *s, float *c) {
   float r = fmaf(-k, 6.28318548202514648f, x);
   r = fmaf(-k, -1.7484556e-07f, r);
   __sincosf(r, s, c);
-}
-
-__device__ __forceinline__ float load_beta(const void *p, int dt, int64_t i) {
-  if (dt == DP_F32) return static_cast<const float *>(p)[i];
-  if (dt == DP_BF16) return __bfloat162float(static_cast<const __nv_bfloat16 *>(p)[i]);
-  return __half2float(static_cast<const __half *>(p)[i]);
 }
 
 struct LapTcArgs {
@@ -144,18 +147,158 @@ __device__ __forceinline__ void lap_issue_loads(const LapTcArgs &a, int b, int h
 // 8 (tid / 64) .. + 7 of this CTA's half) and beta (threads 0..63).  Past the end: v = 0,
 // log r = 0, beta = 0 -- the reference's padding.
 __device__ __forceinline__ void prefetch_vlr(const LapTcArgs &a, int b, int h, int oh, int c, int tid, uint4 &pv,
-                                             uint4 &pl, float &pb) {
+                                             uint4 &pl, uint32_t &pb) {
   const int tt = tid & 63, q4 = tid >> 6, t = c * kC + tt;
   pv = make_uint4(0, 0, 0, 0);
   pl = pv;
-  pb = 0.f;
+  pb = 0u;
   if (t < a.L) {
     pv = __ldg(reinterpret_cast<const uint4 *>(a.v + b * a.s_v.b + h * a.s_v.h + (int64_t)t * a.s_v.t + kNo * oh + 8 * q4));
     pl = __ldg(reinterpret_cast<const uint4 *>(a.lr + b * a.s_lr.b + h * a.s_lr.h + (int64_t)t * a.s_lr.t + kNo * oh +
                                                8 * q4));
   }
   const int tb = c * kC + tid;
-  if (tid < kC && tb < a.L) pb = load_beta(a.beta, a.beta_dt, b * a.s_b.b + h * a.s_b.h + (int64_t)tb * a.s_b.t);
+  if (tid < kC && tb < a.L) pb = load_raw_scalar(a.beta, a.beta_dt, b * a.s_b.b + h * a.s_b.h + (int64_t)tb * a.s_b.t);
+}
+
+// Phasors of one chunk -> [K; Q] bf16 (rows 0..63 K, 64..127 Q, no-swizzle K-major).
+// Thread: token 8 warp + lane % 8, two 16-feature segments chosen so that the 16-byte
+// stores of a warp hit distinct banks.
+template <bool kMag>
+__device__ __forceinline__ void phasor_rows(const LapTcArgs &a, const uint8_t *stage, uint8_t *kq, int nvalid,
+                                            int warp, int lane) {
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int t = 8 * warp + (lane & 7), sg = ((lane >> 3) + 2 * (lane & 7) + 4 * r) & 7;
+    uint32_t kw[8], qw[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) kw[i] = qw[i] = 0u;
+    if (t < nvalid) {
+      const uint4 kraw = *reinterpret_cast<const uint4 *>(stage + ST_TK + t * 128 + sg * 16);
+      const uint4 qraw = *reinterpret_cast<const uint4 *>(stage + ST_TQ + t * 128 + sg * 16);
+      const uint32_t kr[4] = {kraw.x, kraw.y, kraw.z, kraw.w}, qr[4] = {qraw.x, qraw.y, qraw.z, qraw.w};
+      uint32_t mkr[4] = {0u, 0u, 0u, 0u}, mqr[4] = {0u, 0u, 0u, 0u};
+      if (kMag) {
+        if (a.mk) {
+          const uint4 m = *reinterpret_cast<const uint4 *>(stage + ST_MK + t * 128 + sg * 16);
+          mkr[0] = m.x; mkr[1] = m.y; mkr[2] = m.z; mkr[3] = m.w;
+        }
+        if (a.mq) {
+          const uint4 m = *reinterpret_cast<const uint4 *>(stage + ST_MQ + t * 128 + sg * 16);
+          mqr[0] = m.x; mqr[1] = m.y; mqr[2] = m.z; mqr[3] = m.w;
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float s0, c0, s1, c1;
+        const __nv_bfloat162 k2 = *reinterpret_cast<const __nv_bfloat162 *>(&kr[i]);
+        const __nv_bfloat162 q2 = *reinterpret_cast<const __nv_bfloat162 *>(&qr[i]);
+        fast_sincos(__low2float(k2), &s0, &c0);
+        fast_sincos(__high2float(k2), &s1, &c1);
+        if (kMag) {
+          // bf16 zeros in an absent magnitude tensor give e^0 = 1
+          const float2 mk = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&mkr[i]));
+          const float a0 = __expf(mk.x), a1 = __expf(mk.y);
+          c0 *= a0; s0 *= a0; c1 *= a1; s1 *= a1;
+        }
+        kw[2 * i] = pack_bf16(c0, s0);
+        kw[2 * i + 1] = pack_bf16(c1, s1);
+        fast_sincos(__low2float(q2), &s0, &c0);
+        fast_sincos(__high2float(q2), &s1, &c1);
+        if (kMag) {
+          const float2 mq = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&mqr[i]));
+          const float b0 = __expf(mq.x), b1 = __expf(mq.y);
+          c0 *= b0; s0 *= b0; c1 *= b1; s1 *= b1;
+        }
+        qw[2 * i] = pack_bf16(c0, s0);
+        qw[2 * i + 1] = pack_bf16(c1, s1);
+      }
+    }
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      *reinterpret_cast<uint4 *>(kq + cm_off(t, 16 * sg + 8 * half, RG_KQ)) =
+          make_uint4(kw[4 * half], kw[4 * half + 1], kw[4 * half + 2], kw[4 * half + 3]);
+      *reinterpret_cast<uint4 *>(kq + cm_off(64 + t, 16 * sg + 8 * half, RG_KQ)) =
+          make_uint4(qw[4 * half], qw[4 * half + 1], qw[4 * half + 2], qw[4 * half + 3]);
+    }
+  }
+}
+
+// acc (+)= sum over the 16-token K segments [SEG_LO, SEG_HI) of A_seg F_seg for one 16 x 8
+// tile (rows R0 .. R0 + 15, channels n0 .. n0 + 7), the accumulator rescaled by rho between
+// segments.  A(m, s) = amat[s * LDG + m], masked to s <= m on the diagonal segment.  Two
+// accumulators (k = 0..7 / 8..15 of each segment) halve the MMA dependency chain.
+template <int SEG_LO, int SEG_HI, int R0>
+__device__ __forceinline__ void seg_mma(float (&acc)[4], const float *amat, const float *fv, const float *rho, int n0,
+                                        int g8, int t4) {
+  float a1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int seg = SEG_LO; seg < SEG_HI; ++seg) {
+    if (seg > SEG_LO) {
+      const float ra = rho[(seg - 1) * kNo + n0 + 2 * t4], rb = rho[(seg - 1) * kNo + n0 + 2 * t4 + 1];
+      acc[0] *= ra; acc[1] *= rb; acc[2] *= ra; acc[3] *= rb;
+      a1[0] *= ra; a1[1] *= rb; a1[2] *= ra; a1[3] *= rb;
+    }
+    const bool diag = 16 * seg == R0;
+#pragma unroll
+    for (int k8 = 0; k8 < 2; ++k8) {
+      const int sa = 16 * seg + 8 * k8 + t4, sb = sa + 4, ma = R0 + g8, mb = ma + 8;
+      float x0 = amat[sa * LDG + ma], x1 = amat[sa * LDG + mb], x2 = amat[sb * LDG + ma], x3 = amat[sb * LDG + mb];
+      if (diag) {
+        x0 = sa <= ma ? x0 : 0.f;
+        x1 = sa <= mb ? x1 : 0.f;
+        x2 = sb <= ma ? x2 : 0.f;
+        x3 = sb <= mb ? x3 : 0.f;
+      }
+      const uint32_t af[4] = {to_tf32(x0), to_tf32(x1), to_tf32(x2), to_tf32(x3)};
+      const uint32_t bf[2] = {to_tf32(fv[sa * LDF + n0 + g8]), to_tf32(fv[sb * LDF + n0 + g8])};
+      if (k8 == 0) mma_tf32_m16n8k8(acc, af, bf);
+      else mma_tf32_m16n8k8(a1, af, bf);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) acc[i] += a1[i];
+}
+
+// Forward substitution of block BLK for channel o (one lane per channel):
+//   f[s] = Bt[s] (R[s] - A[s] y[s]),  y[m] += g[s][m] f[s] for m > s,  y starts at X_b,
+// with A[s] = e^{Lam[s-1] - Lref_b} (1 at the block's first token), Bt = e^{Lref_b - Lam[s]} beta_s.
+// Writes F[s][o] = f[s].
+template <int BLK>
+__device__ __forceinline__ void solve_block(int o, const float *gm, const float *rT, const float *eaT,
+                                            const float *btT, const float *xb, float *fv) {
+  constexpr int m0 = 16 * BLK;
+  float R[16], E[16], Bt[16], y[16], f[16];
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const float4 r4 = *reinterpret_cast<const float4 *>(rT + o * LDM + m0 + 4 * c);
+    const float4 e4 = *reinterpret_cast<const float4 *>(eaT + o * LDM + m0 + 4 * c);
+    const float4 b4 = *reinterpret_cast<const float4 *>(btT + o * LDM + m0 + 4 * c);
+    R[4 * c] = r4.x; R[4 * c + 1] = r4.y; R[4 * c + 2] = r4.z; R[4 * c + 3] = r4.w;
+    E[4 * c] = e4.x; E[4 * c + 1] = e4.y; E[4 * c + 2] = e4.z; E[4 * c + 3] = e4.w;
+    Bt[4 * c] = b4.x; Bt[4 * c + 1] = b4.y; Bt[4 * c + 2] = b4.z; Bt[4 * c + 3] = b4.w;
+  }
+#pragma unroll
+  for (int k = 0; k < 16; ++k) y[k] = BLK ? xb[k * LDF + o] : 0.f;
+#pragma unroll
+  for (int s = 0; s < 16; ++s) {
+    const float A = s ? E[s - 1] : 1.f;
+    f[s] = Bt[s] * fmaf(-A, y[s], R[s]);
+    if (s < 15) {
+      const float *grow = gm + (m0 + s) * LDG + m0;
+#pragma unroll
+      for (int c4 = (s + 1) >> 2; c4 < 4; ++c4) {
+        const float4 g4 = *reinterpret_cast<const float4 *>(grow + 4 * c4);
+        const float gv[4] = {g4.x, g4.y, g4.z, g4.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          if (4 * c4 + k > s) y[4 * c4 + k] = fmaf(gv[k], f[s], y[4 * c4 + k]);
+      }
+    }
+  }
+  // stores after the loop: no shared-memory store sits between the g loads of the chain
+#pragma unroll
+  for (int s = 0; s < 16; ++s) fv[(m0 + s) * LDF + o] = f[s];
 }
 
 __global__ void __launch_bounds__(kThreads, 1) laplace_tc_kernel(LapTcArgs a) {
@@ -174,6 +317,9 @@ __global__ void __launch_bounds__(kThreads, 1) laplace_tc_kernel(LapTcArgs a) {
   float *xb = reinterpret_cast<float *>(smem + OFF_XB);
   float *eref = reinterpret_cast<float *>(smem + OFF_EREF);
   float *rho = reinterpret_cast<float *>(smem + OFF_RHO);
+  float *edec = reinterpret_cast<float *>(smem + OFF_EDEC);
+  float *wsc = reinterpret_cast<float *>(smem + OFF_WSC);
+  float *btT = reinterpret_cast<float *>(smem + OFF_BT);
   float *bs = reinterpret_cast<float *>(smem + OFF_BETA);
   uint64_t *mma_bar = reinterpret_cast<uint64_t *>(smem + OFF_BAR);
   uint64_t *load_bar = mma_bar + 1;  // [2]
@@ -206,7 +352,7 @@ __global__ void __launch_bounds__(kThreads, 1) laplace_tc_kernel(LapTcArgs a) {
       lap_issue_loads(a, b, h, c * kC, min(kC, L - c * kC), smem + OFF_STAGE + c * STAGE_BYTES, &load_bar[c], lane);
   }
   uint4 pv, pl;
-  float pb;
+  uint32_t pb;  // raw bits of beta (converted when stored)
   prefetch_vlr(a, b, h, oh, 0, tid, pv, pl, pb);
   // state^T of this CTA's 32 value channels -> TMEM (lane = feature j, column = o)
   const int64_t sbase = (int64_t)unit * kDv * kF;
@@ -240,49 +386,9 @@ __global__ void __launch_bounds__(kThreads, 1) laplace_tc_kernel(LapTcArgs a) {
 
     // ---- L1: phasors (with magnitudes) -> [K; Q] bf16; v, log-decay, beta -> shared
     {
-#pragma unroll
-      for (int r = 0; r < 2; ++r) {
-        const int t = 8 * warp + (lane & 7), sg = ((lane >> 3) + 2 * (lane & 7) + 4 * r) & 7;
-        const bool valid = t < nvalid;
-        uint32_t kw[8], qw[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) kw[i] = qw[i] = 0u;
-        if (valid) {
-          const uint4 kraw = *reinterpret_cast<const uint4 *>(stage + ST_TK + t * 128 + sg * 16);
-          const uint4 qraw = *reinterpret_cast<const uint4 *>(stage + ST_TQ + t * 128 + sg * 16);
-          uint4 mkraw = make_uint4(0, 0, 0, 0), mqraw = mkraw;
-          if (a.mk) mkraw = *reinterpret_cast<const uint4 *>(stage + ST_MK + t * 128 + sg * 16);
-          if (a.mq) mqraw = *reinterpret_cast<const uint4 *>(stage + ST_MQ + t * 128 + sg * 16);
-          const uint32_t kr[4] = {kraw.x, kraw.y, kraw.z, kraw.w}, qr[4] = {qraw.x, qraw.y, qraw.z, qraw.w};
-          const uint32_t mkr[4] = {mkraw.x, mkraw.y, mkraw.z, mkraw.w};
-          const uint32_t mqr[4] = {mqraw.x, mqraw.y, mqraw.z, mqraw.w};
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            float s0_, c0_, s1_, c1_;
-            const __nv_bfloat162 k2 = *reinterpret_cast<const __nv_bfloat162 *>(&kr[i]);
-            const __nv_bfloat162 m2 = *reinterpret_cast<const __nv_bfloat162 *>(&mkr[i]);
-            const float a0 = a.mk ? __expf(__low2float(m2)) : 1.f, a1 = a.mk ? __expf(__high2float(m2)) : 1.f;
-            fast_sincos(__low2float(k2), &s0_, &c0_);
-            fast_sincos(__high2float(k2), &s1_, &c1_);
-            kw[2 * i] = pack_bf16(a0 * c0_, a0 * s0_);
-            kw[2 * i + 1] = pack_bf16(a1 * c1_, a1 * s1_);
-            const __nv_bfloat162 q2 = *reinterpret_cast<const __nv_bfloat162 *>(&qr[i]);
-            const __nv_bfloat162 n2 = *reinterpret_cast<const __nv_bfloat162 *>(&mqr[i]);
-            const float b0 = a.mq ? __expf(__low2float(n2)) : 1.f, b1 = a.mq ? __expf(__high2float(n2)) : 1.f;
-            fast_sincos(__low2float(q2), &s0_, &c0_);
-            fast_sincos(__high2float(q2), &s1_, &c1_);
-            qw[2 * i] = pack_bf16(b0 * c0_, b0 * s0_);
-            qw[2 * i + 1] = pack_bf16(b1 * c1_, b1 * s1_);
-          }
-        }
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          *reinterpret_cast<uint4 *>(kq + cm_off(t, 16 * sg + 8 * half, RG_KQ)) =
-              make_uint4(kw[4 * half], kw[4 * half + 1], kw[4 * half + 2], kw[4 * half + 3]);
-          *reinterpret_cast<uint4 *>(kq + cm_off(64 + t, 16 * sg + 8 * half, RG_KQ)) =
-              make_uint4(qw[4 * half], qw[4 * half + 1], qw[4 * half + 2], qw[4 * half + 3]);
-        }
-      }
+      if (a.mk || a.mq) phasor_rows<true>(a, stage, kq, nvalid, warp, lane);
+      else phasor_rows<false>(a, stage, kq, nvalid, warp, lane);
+      // ---- L1v: v, log-decay (clamped), beta from the prefetch registers -> shared
       {
         const int tt = tid & 63, q4 = tid >> 6;
         const uint32_t vw[4] = {pv.x, pv.y, pv.z, pv.w}, lw[4] = {pl.x, pl.y, pl.z, pl.w};
@@ -295,8 +401,9 @@ __global__ void __launch_bounds__(kThreads, 1) laplace_tc_kernel(LapTcArgs a) {
           lamT[(8 * q4 + 2 * i) * LDM + tt] = fmaxf(ll.x, kLogFloor);
           lamT[(8 * q4 + 2 * i + 1) * LDM + tt] = fmaxf(ll.y, kLogFloor);
         }
-        if (tid < kC) bs[tid] = pb;
+        if (tid < kC) bs[tid] = raw_scalar_to_f32(pb, a.beta_dt);
       }
+      // ---- L1p: prefetch of the next chunk's v, log-decay and beta
       if (c + 1 < nchunks) prefetch_vlr(a, b, h, oh, c + 1, tid, pv, pl, pb);
     }
     // ---- L2: S^T (TMEM fp32) -> bf16 operand (128 x 32), MN-major B of [K;Q] S0^T
@@ -342,6 +449,8 @@ __global__ void __launch_bounds__(kThreads, 1) laplace_tc_kernel(LapTcArgs a) {
       const int o = tid >> 3, p = tid & 7;  // channel o, tokens 8p .. 8p + 7
       float *lo = lamT + o * LDM + 8 * p;
       const float4 x0 = *reinterpret_cast<const float4 *>(lo), x1 = *reinterpret_cast<const float4 *>(lo + 4);
+      const float4 b0 = *reinterpret_cast<const float4 *>(bs + 8 * p), b1 = *reinterpret_cast<const float4 *>(bs + 8 * p + 4);
+      const float bsv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
       float l[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
 #pragma unroll
       for (int i = 1; i < 8; ++i) l[i] += l[i - 1];
@@ -369,6 +478,15 @@ __global__ void __launch_bounds__(kThreads, 1) laplace_tc_kernel(LapTcArgs a) {
       *reinterpret_cast<float4 *>(eo + 4) = make_float4(e[4], e[5], e[6], e[7]);
       if (p & 1) rho[(p >> 1) * kNo + o] = e[7];
       else eref[(p >> 1) * kNo + o] = __expf(lref);
+      if (p == 7) edec[o] = __expf(l[7]);
+      const float l63 = __shfl_sync(0xffffffffu, l[7], (lane & ~7) | 7);
+      if (!(p & 1)) wsc[(p >> 1) * kNo + o] = __expf(l63 - lref);
+      float bt[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) bt[i] = __fdividef(bsv[i], e[i]);
+      float *bo = btT + o * LDM + 8 * p;
+      *reinterpret_cast<float4 *>(bo) = make_float4(bt[0], bt[1], bt[2], bt[3]);
+      *reinterpret_cast<float4 *>(bo + 4) = make_float4(bt[4], bt[5], bt[6], bt[7]);
       bad = !(dev <= kFastRange);
     }
     if (tid == 0) ok = mbar_wait(mma_bar, mma_phase, kTimeoutNs);
@@ -382,6 +500,17 @@ __global__ void __launch_bounds__(kThreads, 1) laplace_tc_kernel(LapTcArgs a) {
     //      (rows 64..127 hold (Q K^T)[m][s]); B0k, B0q channel-major from [K;Q] S0^T.
     {
       const int row = 32 * q + lane, hf = warp >> 2;
+      // operands of R (factorised path, K rows) gathered before any store of this phase
+      float rv[16], ra[16], re[16];
+      if (fast && row < 64) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int o = 16 * hf + i;
+          rv[i] = vfT[o * LDM + row];
+          ra[i] = (row & 15) ? eaT[o * LDM + row - 1] : 1.f;
+          re[i] = eref[(row >> 4) * kNo + o];
+        }
+      }
 #pragma unroll
       for (int u = 0; u < 2; ++u) {
         float d[16];
@@ -400,116 +529,95 @@ __global__ void __launch_bounds__(kThreads, 1) laplace_tc_kernel(LapTcArgs a) {
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
         const int o = 16 * hf + i;
-        if (row < 64) bkT[o * LDM + row] = d[i] * inv_d;
+        if (row < 64) {
+          // factorised path: R[m] = v[m] - e^{Lam[m-1]} B0k[m] (e^{Lam[m-1]} = e^{Lref} A[m])
+          bkT[o * LDM + row] = fast ? fmaf(-re[i] * ra[i], d[i] * inv_d, rv[i]) : d[i] * inv_d;
+        }
         else bqT[o * LDM + (row - 64)] = d[i] * inv_d;
       }
     }
     tc_fence_before();
     __syncthreads();
 
-    const int so = tid >> 3, sj = tid & 7;  // solve layout: channel so, tokens m0 + sj, m0 + 8 + sj
     if (fast) {
-      // ---- L5: factorised blocked solve; W written straight to its bf16 operand
-      const float l63 = lamT[so * LDM + 63];
-      for (int blk = 0; blk < 4; ++blk) {
-        const int m0 = 16 * blk;
-        {
-          const float er = eref[blk * kNo + so];
-          float R[2], A[2], Bt[2], y[2];
-#pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const int m = m0 + 8 * u + sj;
-            const float ap = eaT[so * LDM + m];
-            const float am = (8 * u + sj == 0) ? 1.f : eaT[so * LDM + m - 1];
-            R[u] = fmaf(-er * am, bkT[so * LDM + m], vfT[so * LDM + m]);
-            A[u] = am;
-            Bt[u] = __fdividef(bs[m], ap);
-            y[u] = blk ? xb[(8 * u + sj) * LDF + so] : 0.f;
-          }
-#pragma unroll
-          for (int s8 = 0; s8 < 16; ++s8) {
-            const int uo = s8 >> 3;
-            const float f_own = Bt[uo] * fmaf(-A[uo], y[uo], R[uo]);
-            const float f = __shfl_sync(0xffffffffu, f_own, (lane & ~7) | (s8 & 7));
-#pragma unroll
-            for (int u = 0; u < 2; ++u)
-              if (8 * u + sj > s8) y[u] = fmaf(gm[(m0 + s8) * LDG + m0 + 8 * u + sj], f, y[u]);
-          }
-#pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const int m = m0 + 8 * u + sj;
-            const float e = fmaf(-A[u], y[u], R[u]);
-            fv[m * LDF + so] = Bt[u] * e;
-            const float w = __expf(l63 - lamT[so * LDM + m]) * bs[m] * e;
-            *reinterpret_cast<__nv_bfloat16 *>(wt + cm_off(m, so, RG_32)) = __float2bfloat16_rn(w);
-          }
-        }
-        __syncthreads();
-        if (blk < 3) {
-          // X of the next block: rows 16 (blk + 1) .., warps 0..3 one 8-channel tile each
-          if (warp < 4) {
-            const int n0 = 8 * warp, r0 = m0 + 16;
-            float acc[4] = {0.f, 0.f, 0.f, 0.f};
-            for (int seg = 0; seg <= blk; ++seg) {
-              if (seg > 0) {
-                const float ra = rho[(seg - 1) * kNo + n0 + 2 * t4], rb = rho[(seg - 1) * kNo + n0 + 2 * t4 + 1];
-                acc[0] *= ra; acc[1] *= rb; acc[2] *= ra; acc[3] *= rb;
-              }
-#pragma unroll
-              for (int k8 = 0; k8 < 2; ++k8) {
-                const int k0 = 16 * seg + 8 * k8;
-                const uint32_t af[4] = {to_tf32(gm[(k0 + t4) * LDG + r0 + g8]), to_tf32(gm[(k0 + t4) * LDG + r0 + g8 + 8]),
-                                        to_tf32(gm[(k0 + t4 + 4) * LDG + r0 + g8]),
-                                        to_tf32(gm[(k0 + t4 + 4) * LDG + r0 + g8 + 8])};
-                const uint32_t bf[2] = {to_tf32(fv[(k0 + t4) * LDF + n0 + g8]), to_tf32(fv[(k0 + t4 + 4) * LDF + n0 + g8])};
-                mma_tf32_m16n8k8(acc, af, bf);
-              }
-            }
-            const float ra = rho[blk * kNo + n0 + 2 * t4], rb = rho[blk * kNo + n0 + 2 * t4 + 1];
-            xb[g8 * LDF + n0 + 2 * t4] = acc[0] * ra;
-            xb[g8 * LDF + n0 + 2 * t4 + 1] = acc[1] * rb;
-            xb[(g8 + 8) * LDF + n0 + 2 * t4] = acc[2] * ra;
-            xb[(g8 + 8) * LDF + n0 + 2 * t4 + 1] = acc[3] * rb;
-          }
-          __syncthreads();
-        }
-      }
-      // ---- L5o: outputs, 16 tiles (4 blocks x 4 channel tiles) over 8 warps
-#pragma unroll 1
-      for (int rep = 0; rep < 2; ++rep) {
-        const int blk = rep == 0 ? (warp >> 2) : 3 - (warp >> 2);
-        const int n0 = 8 * (warp & 3), r0 = 16 * blk;
+      // ---- L5: factorised blocked solve.  Warp 0 (lane = channel) runs the forward
+      //      substitution of each block; meanwhile warps 4..7 fold the earlier blocks into X
+      //      of the next block and form the previous block's outputs; after the barrier they
+      //      add the newest block to X.
+      const int n0 = 8 * (warp & 3);
+      float xacc[4];
+      auto outputs = [&](auto bc) {
+        constexpr int OB = decltype(bc)::value;
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
-        for (int seg = 0; seg <= blk; ++seg) {
-          if (seg > 0) {
-            const float ra = rho[(seg - 1) * kNo + n0 + 2 * t4], rb = rho[(seg - 1) * kNo + n0 + 2 * t4 + 1];
-            acc[0] *= ra; acc[1] *= rb; acc[2] *= ra; acc[3] *= rb;
-          }
-#pragma unroll
-          for (int k8 = 0; k8 < 2; ++k8) {
-            const int k0 = 16 * seg + 8 * k8;
-            const int sa = k0 + t4, sb = k0 + t4 + 4, ma = r0 + g8, mb = r0 + g8 + 8;
-            const uint32_t af[4] = {to_tf32(sa <= ma ? hm[sa * LDG + ma] : 0.f), to_tf32(sa <= mb ? hm[sa * LDG + mb] : 0.f),
-                                    to_tf32(sb <= ma ? hm[sb * LDG + ma] : 0.f), to_tf32(sb <= mb ? hm[sb * LDG + mb] : 0.f)};
-            const uint32_t bf[2] = {to_tf32(fv[sa * LDF + n0 + g8]), to_tf32(fv[sb * LDF + n0 + g8])};
-            mma_tf32_m16n8k8(acc, af, bf);
-          }
-        }
+        seg_mma<0, OB + 1, 16 * OB>(acc, hm, fv, rho, n0, g8, t4);
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
-          const int m = r0 + g8 + 8 * hh;
+          const int m = 16 * OB + g8 + 8 * hh;
           if (m < nvalid) {
 #pragma unroll
             for (int cc = 0; cc < 2; ++cc) {
               const int o = n0 + 2 * t4 + cc;
-              const float val = eaT[o * LDM + m] * fmaf(eref[blk * kNo + o], bqT[o * LDM + m], acc[2 * hh + cc]);
-              obase[(int64_t)m * a.s_out.t + o] = val;
+              obase[(int64_t)m * a.s_out.t + o] =
+                  eaT[o * LDM + m] * fmaf(eref[OB * kNo + o], bqT[o * LDM + m], acc[2 * hh + cc]);
             }
           }
+        }
+      };
+      auto block_step = [&](auto bc) {
+        constexpr int BLK = decltype(bc)::value;
+        if (warp == 0) {
+          solve_block<BLK>(lane, gm, bkT, eaT, btT, xb, fv);
+        } else if (warp >= 4) {
+          if constexpr (BLK > 0) outputs(std::integral_constant<int, BLK - 1>{});
+          if constexpr (BLK > 0 && BLK < 3) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) xacc[i] = 0.f;
+            seg_mma<0, BLK, 16 * (BLK + 1)>(xacc, gm, fv, rho, n0, g8, t4);
+            const float ra = rho[(BLK - 1) * kNo + n0 + 2 * t4], rb = rho[(BLK - 1) * kNo + n0 + 2 * t4 + 1];
+            xacc[0] *= ra; xacc[1] *= rb; xacc[2] *= ra; xacc[3] *= rb;
+          }
+        }
+        // ---- L5b: block solved; F of the block visible to all warps after the barrier
+        __syncthreads();
+        if constexpr (BLK < 3) {
+          if (warp >= 4) {
+            if constexpr (BLK == 0) {
+#pragma unroll
+              for (int i = 0; i < 4; ++i) xacc[i] = 0.f;
+            }
+            seg_mma<BLK, BLK + 1, 16 * (BLK + 1)>(xacc, gm, fv, rho, n0, g8, t4);
+            const float ra = rho[BLK * kNo + n0 + 2 * t4], rb = rho[BLK * kNo + n0 + 2 * t4 + 1];
+            xb[g8 * LDF + n0 + 2 * t4] = xacc[0] * ra;
+            xb[g8 * LDF + n0 + 2 * t4 + 1] = xacc[1] * rb;
+            xb[(g8 + 8) * LDF + n0 + 2 * t4] = xacc[2] * ra;
+            xb[(g8 + 8) * LDF + n0 + 2 * t4 + 1] = xacc[3] * rb;
+          }
+          // ---- L5c: X of the next block visible after the barrier
+          __syncthreads();
+        }
+      };
+      block_step(std::integral_constant<int, 0>{});
+      block_step(std::integral_constant<int, 1>{});
+      block_step(std::integral_constant<int, 2>{});
+      block_step(std::integral_constant<int, 3>{});
+      // ---- L5z: last block's outputs (warps 4..7); W = e^{Lam[63] - Lref_b} F -> bf16 (warps 0..3)
+      if (warp >= 4) {
+        outputs(std::integral_constant<int, 3>{});
+      } else {
+        const int s = tid >> 1, o0 = 16 * (tid & 1);
+#pragma unroll
+        for (int hv = 0; hv < 2; ++hv) {
+          const float4 f0 = *reinterpret_cast<const float4 *>(fv + s * LDF + o0 + 8 * hv);
+          const float4 f1 = *reinterpret_cast<const float4 *>(fv + s * LDF + o0 + 8 * hv + 4);
+          const float *ws = wsc + (s >> 4) * kNo + o0 + 8 * hv;
+          *reinterpret_cast<uint4 *>(wt + cm_off(s, o0 + 8 * hv, RG_32)) =
+              make_uint4(pack_bf16(f0.x * ws[0], f0.y * ws[1]), pack_bf16(f0.z * ws[2], f0.w * ws[3]),
+                         pack_bf16(f1.x * ws[4], f1.y * ws[5]), pack_bf16(f1.z * ws[6], f1.w * ws[7]));
         }
       }
     } else {
       // ---- L5x: exact path, every decay ratio formed as exp(difference) <= 1
+      const int so = tid >> 3, sj = tid & 7;  // channel so, tokens m0 + sj, m0 + 8 + sj
       float *ev = eaT;
       const float *lo = lamT + so * LDM;
       for (int blk = 0; blk < 4; ++blk) {
@@ -582,7 +690,7 @@ __global__ void __launch_bounds__(kThreads, 1) laplace_tc_kernel(LapTcArgs a) {
         tmem_ld16(tmem + lane_base + COL_S + 16 * u, sv);
         tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 16; ++i) sv[i] *= __expf(lamT[(16 * u + i) * LDM + 63]);
+        for (int i = 0; i < 16; ++i) sv[i] *= edec[16 * u + i];
         tmem_st16(tmem + lane_base + COL_S + 16 * u, sv);
       }
       tmem_st_wait();
