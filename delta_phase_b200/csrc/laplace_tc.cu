@@ -53,6 +53,8 @@ constexpr int kThreads = 256;
 constexpr uint64_t kTimeoutNs = 2000000000ull;
 constexpr float kLogFloor = -80.0f;
 constexpr float kFastRange = 64.0f;  // max |Lam[m] - Lref_b| for the factorised solve
+constexpr int BAR_SOLVE = 1;   // named barrier of the solve warps 0, 4..7 (160 threads)
+constexpr int BAR_PH = 2;      // named barrier of the phasor warps 1..3 (96 threads)
 
 // stage: theta_k, theta_q, logmag_k, logmag_q rows of a chunk (64 rows x 128 B each)
 constexpr int ST_TK = 0, ST_TQ = kC * 128, ST_MK = 2 * kC * 128, ST_MQ = 3 * kC * 128;
@@ -63,9 +65,10 @@ constexpr int LDG = 72;   // g, h: [s][m] fp32
 constexpr int LDM = 68;   // channel-major per-(token, channel) arrays: [o][m] fp32
 constexpr int LDF = 40;   // F: [s][o] fp32
 
-constexpr int OFF_STAGE = 0;                                  // [2]
-constexpr int OFF_KQ = OFF_STAGE + 2 * STAGE_BYTES;          // [K; Q] bf16 128 x 128
-constexpr int OFF_S0 = OFF_KQ + 16 * RG_KQ;                  // S^T bf16 128 x 32
+constexpr int KQ_BYTES = 16 * RG_KQ;
+constexpr int OFF_STAGE = 0;                                  // phases of the next chunk
+constexpr int OFF_KQ = OFF_STAGE + STAGE_BYTES;              // [K; Q] bf16 128 x 128, [2] (this / next chunk)
+constexpr int OFF_S0 = OFF_KQ + 2 * KQ_BYTES;                // S^T bf16 128 x 32
 constexpr int OFF_W = OFF_S0 + 16 * RG_32;                   // W bf16 64 x 32
 constexpr int OFF_G = OFF_W + 8 * RG_32;                     // g[s][m]
 constexpr int OFF_H = OFF_G + kC * LDG * 4;                  // h[s][m]
@@ -303,7 +306,7 @@ __device__ __forceinline__ void solve_block(int o, const float *gm, const float 
 
 __global__ void __launch_bounds__(kThreads, 1) laplace_tc_kernel(LapTcArgs a) {
   extern __shared__ __align__(1024) uint8_t smem[];
-  uint8_t *kq = smem + OFF_KQ;
+  uint8_t *stage = smem + OFF_STAGE;
   uint8_t *s0 = smem + OFF_S0;
   uint8_t *wt = smem + OFF_W;
   float *gm = reinterpret_cast<float *>(smem + OFF_G);
@@ -322,8 +325,9 @@ __global__ void __launch_bounds__(kThreads, 1) laplace_tc_kernel(LapTcArgs a) {
   float *btT = reinterpret_cast<float *>(smem + OFF_BT);
   float *bs = reinterpret_cast<float *>(smem + OFF_BETA);
   uint64_t *mma_bar = reinterpret_cast<uint64_t *>(smem + OFF_BAR);
-  uint64_t *load_bar = mma_bar + 1;  // [2]
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mma_bar + 3);
+  uint64_t *load_bar = mma_bar + 1;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mma_bar + 2);
+  int *last_issued = reinterpret_cast<int *>(mma_bar + 3);  // chunk of the newest stage load
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int unit = blockIdx.x >> 1, oh = blockIdx.x & 1;
@@ -333,8 +337,8 @@ __global__ void __launch_bounds__(kThreads, 1) laplace_tc_kernel(LapTcArgs a) {
 
   if (tid == 0) {
     mbar_init(mma_bar, 1);
-    mbar_init(&load_bar[0], 1);
-    mbar_init(&load_bar[1], 1);
+    mbar_init(load_bar, 1);
+    *last_issued = -1;
     fence_mbar_init();
   }
   if (warp == 0) {
@@ -347,9 +351,31 @@ __global__ void __launch_bounds__(kThreads, 1) laplace_tc_kernel(LapTcArgs a) {
   const int q = warp & 3;
   const uint32_t lane_base = (uint32_t)(q * 32) << 16;
 
-  if (warp == 0) {
-    for (int c = 0; c < 2 && c < nchunks; ++c)
-      lap_issue_loads(a, b, h, c * kC, min(kC, L - c * kC), smem + OFF_STAGE + c * STAGE_BYTES, &load_bar[c], lane);
+  const bool has_mag = a.mk || a.mq;
+  // Phasors of chunk cn -> its [K; Q] buffer by warps wfirst .. wfirst + nw - 1 (barrier
+  // bar_id over them; 0 = the whole CTA), then the stage load of chunk cn + 1.
+  auto next_phasors = [&](int cn, int wfirst, int nw, int bar_id) -> bool {
+    bool okl = true;
+    if (tid == 32 * wfirst) okl = mbar_wait(load_bar, (uint32_t)(cn & 1), kTimeoutNs);
+    if (bar_id == 0 ? __syncthreads_or(!okl) : group_any(!okl, bar_id, 32 * nw)) return false;
+    uint8_t *dst = smem + OFF_KQ + (cn & 1) * KQ_BYTES;
+    const int nv = min(kC, L - cn * kC);
+    for (int grp = warp - wfirst; grp < 8; grp += nw) {
+      if (has_mag) phasor_rows<true>(a, stage, dst, nv, grp, lane);
+      else phasor_rows<false>(a, stage, dst, nv, grp, lane);
+    }
+    fence_proxy_async_smem();
+    if (bar_id == 0) __syncthreads();
+    else group_sync(bar_id, 32 * nw);
+    if (cn + 1 < nchunks && warp == wfirst) {
+      lap_issue_loads(a, b, h, (cn + 1) * kC, min(kC, L - (cn + 1) * kC), stage, load_bar, lane);
+      if (lane == 0) *last_issued = cn + 1;
+    }
+    return true;
+  };
+  if (warp == 0 && nchunks > 0) {
+    lap_issue_loads(a, b, h, 0, min(kC, L), stage, load_bar, lane);
+    if (lane == 0) *last_issued = 0;
   }
   uint4 pv, pl;
   uint32_t pb;  // raw bits of beta (converted when stored)
@@ -373,22 +399,16 @@ __global__ void __launch_bounds__(kThreads, 1) laplace_tc_kernel(LapTcArgs a) {
 
   uint32_t mma_phase = 0;
   bool ok = true, mma_pending = false;
-  int issued = min(nchunks, 2), consumed = 0;
   const int g8 = lane >> 2, t4 = lane & 3;  // mma.sync fragment coordinates
+  if (nchunks > 0) ok = next_phasors(0, 0, 8, 0);
 
-  for (int c = 0; c < nchunks; ++c) {
-    const int t0 = c * kC, nvalid = min(kC, L - t0), st = c & 1;
-    uint8_t *stage = smem + OFF_STAGE + st * STAGE_BYTES;
+  for (int c = 0; ok && c < nchunks; ++c) {
+    const int t0 = c * kC, nvalid = min(kC, L - t0);
+    uint8_t *kq = smem + OFF_KQ + (c & 1) * KQ_BYTES;  // phasors of this chunk (made a chunk ahead)
     float *obase = a.out + b * a.s_out.b + h * a.s_out.h + (int64_t)t0 * a.s_out.t + kNo * oh;
-    if (tid == 0) ok = mbar_wait(&load_bar[st], (uint32_t)((c >> 1) & 1), kTimeoutNs);
-    if (__syncthreads_or(!ok)) { ok = false; break; }
-    consumed = c + 1;
 
-    // ---- L1: phasors (with magnitudes) -> [K; Q] bf16; v, log-decay, beta -> shared
+    // ---- L1: v, log-decay (clamped), beta from the prefetch registers -> shared
     {
-      if (a.mk || a.mq) phasor_rows<true>(a, stage, kq, nvalid, warp, lane);
-      else phasor_rows<false>(a, stage, kq, nvalid, warp, lane);
-      // ---- L1v: v, log-decay (clamped), beta from the prefetch registers -> shared
       {
         const int tt = tid & 63, q4 = tid >> 6;
         const uint32_t vw[4] = {pv.x, pv.y, pv.z, pv.w}, lw[4] = {pl.x, pl.y, pl.z, pl.w};
@@ -439,10 +459,6 @@ __global__ void __launch_bounds__(kThreads, 1) laplace_tc_kernel(LapTcArgs a) {
       mma_commit(mma_bar);
     }
     mma_pending = true;
-    if (c + 2 < nchunks) {
-      if (warp == 7) lap_issue_loads(a, b, h, t0 + 2 * kC, min(kC, L - t0 - 2 * kC), stage, &load_bar[st], lane);
-      issued = c + 3;
-    }
     // ---- decay: cumulative log-decay, block-relative factors (overlaps the MMAs)
     bool bad;
     {
@@ -539,11 +555,14 @@ __global__ void __launch_bounds__(kThreads, 1) laplace_tc_kernel(LapTcArgs a) {
     tc_fence_before();
     __syncthreads();
 
-    if (fast) {
+    if (fast && warp >= 1 && warp <= 3) {
+      // ---- L5p: warps 1..3 make the next chunk's phasors while the others solve this one
+      if (c + 1 < nchunks && !next_phasors(c + 1, 1, 3, BAR_PH)) ok = false;
+    } else if (fast) {
       // ---- L5: factorised blocked solve.  Warp 0 (lane = channel) runs the forward
       //      substitution of each block; meanwhile warps 4..7 fold the earlier blocks into X
       //      of the next block and form the previous block's outputs; after the barrier they
-      //      add the newest block to X.
+      //      add the newest block to X.  Barriers over these five warps only.
       const int n0 = 8 * (warp & 3);
       float xacc[4];
       auto outputs = [&](auto bc) {
@@ -577,8 +596,8 @@ __global__ void __launch_bounds__(kThreads, 1) laplace_tc_kernel(LapTcArgs a) {
             xacc[0] *= ra; xacc[1] *= rb; xacc[2] *= ra; xacc[3] *= rb;
           }
         }
-        // ---- L5b: block solved; F of the block visible to all warps after the barrier
-        __syncthreads();
+        // ---- L5b: block solved; F of the block visible to the solve warps after the barrier
+        group_sync(BAR_SOLVE, 160);
         if constexpr (BLK < 3) {
           if (warp >= 4) {
             if constexpr (BLK == 0) {
@@ -593,18 +612,17 @@ __global__ void __launch_bounds__(kThreads, 1) laplace_tc_kernel(LapTcArgs a) {
             xb[(g8 + 8) * LDF + n0 + 2 * t4 + 1] = xacc[3] * rb;
           }
           // ---- L5c: X of the next block visible after the barrier
-          __syncthreads();
+          group_sync(BAR_SOLVE, 160);
         }
       };
       block_step(std::integral_constant<int, 0>{});
       block_step(std::integral_constant<int, 1>{});
       block_step(std::integral_constant<int, 2>{});
       block_step(std::integral_constant<int, 3>{});
-      // ---- L5z: last block's outputs (warps 4..7); W = e^{Lam[63] - Lref_b} F -> bf16 (warps 0..3)
+      // ---- L5z: last block's outputs, then W = e^{Lam[63] - Lref_b} F -> bf16 (warps 4..7)
       if (warp >= 4) {
         outputs(std::integral_constant<int, 3>{});
-      } else {
-        const int s = tid >> 1, o0 = 16 * (tid & 1);
+        const int s = (tid - 128) >> 1, o0 = 16 * (tid & 1);
 #pragma unroll
         for (int hv = 0; hv < 2; ++hv) {
           const float4 f0 = *reinterpret_cast<const float4 *>(fv + s * LDF + o0 + 8 * hv);
@@ -681,9 +699,12 @@ __global__ void __launch_bounds__(kThreads, 1) laplace_tc_kernel(LapTcArgs a) {
         *reinterpret_cast<uint4 *>(wt + cm_off(s, o0, RG_32)) =
             make_uint4(pack_bf16(w[0], w[1]), pack_bf16(w[2], w[3]), pack_bf16(w[4], w[5]), pack_bf16(w[6], w[7]));
       }
+      // next chunk's phasors by the whole CTA
+      if (c + 1 < nchunks && !next_phasors(c + 1, 0, 8, 0)) ok = false;
     }
-    // state decay in TMEM:  S^T[j][o] *= exp(Lam[63][o])
-    if (warp < 4) {
+    // state decay in TMEM:  S^T[j][o] *= exp(Lam[63][o])  (warps 4..7 on the factorised
+    // path, 0..3 on the exact one; warp w reaches TMEM lanes 32 (w % 4) ..)
+    if (fast ? warp >= 4 : warp < 4) {
 #pragma unroll
       for (int u = 0; u < 2; ++u) {
         float sv[16];
@@ -697,7 +718,7 @@ __global__ void __launch_bounds__(kThreads, 1) laplace_tc_kernel(LapTcArgs a) {
     }
     fence_proxy_async_smem();
     tc_fence_before();
-    __syncthreads();
+    if (__syncthreads_or(!ok)) { ok = false; break; }
 
     // ---- L6: S^T += K^T W  (M=128, N=32, K=64)
     if (tid == 0) {
@@ -720,7 +741,8 @@ __global__ void __launch_bounds__(kThreads, 1) laplace_tc_kernel(LapTcArgs a) {
   if (!ok) {
     if (tid == 0) {
       atomicCAS(a.err, 0, DP_ERR_TIMEOUT);
-      for (int k = consumed; k < issued; ++k) mbar_wait(&load_bar[k & 1], (uint32_t)((k >> 1) & 1), kTimeoutNs);
+      // a stage load still in flight: its phase completes (waits on a finished phase return at once)
+      if (*last_issued >= 0) mbar_wait(load_bar, (uint32_t)(*last_issued & 1), kTimeoutNs);
       if (mma_pending) mbar_wait(mma_bar, mma_phase, kTimeoutNs);
     }
   } else if (warp < 4) {
