@@ -354,6 +354,60 @@ def run_laplace(args, world, rank, local):
     return line
 
 
+def run_laplace_sp(args, world, rank, local):
+    """Sequence-parallel LaplacePhaseCore: one B=4, H=16, L=32768 sequence split into
+    `world` contiguous segments, boundary states passed rank to rank over NCCL in 4
+    batch micro-groups.  Strong scaling (fixed total work); a step is the whole sequence."""
+    import torch
+    import torch.nn.functional as F
+    from delta_phase_b200.sequence_parallel import laplace_chunkwise_sp
+    dev = torch.device("cuda", local)
+    B, H, L, D = 4, 16, 32768, 64
+    Ls = L // world
+    g = torch.Generator(device=dev).manual_seed(3000 + rank)
+    bf = torch.bfloat16
+    tk = (torch.rand(B, H, Ls, D, device=dev, generator=g) * 2 * np.pi).to(bf)
+    tq = (torch.rand(B, H, Ls, D, device=dev, generator=g) * 2 * np.pi).to(bf)
+    v = torch.randn(B, H, Ls, D, device=dev, generator=g).to(bf)
+    logr = (-F.softplus(torch.randn(B, H, Ls, D, device=dev, generator=g))).to(bf)
+    beta = (2 * torch.sigmoid(torch.randn(B, H, Ls, device=dev, generator=g))).to(bf)
+    out = torch.empty(B, H, Ls, D, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        laplace_chunkwise_sp(tk, None, tq, None, v, logr, beta, 64, None, micro_groups=B, out=out)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    sampler.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    clocks = sampler.stop()
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
+    alg = B * H * L * (4 * D * 2 + 2 + D * 4) + B * H * D * D * 8
+    peaks, _ = load_peaks()
+    line = _line("laplace-core sequence-parallel tokens/s (B=4,H=16,L=32K,d_k=64)", B * L / (ms / 1e3),
+                 "tokens/s", args, world, ms,
+                 {"workload": "LaplacePhaseCore chunk solve, one B=4,H=16,L=32768 sequence split over the GPUs",
+                  "global_batch": B, "seq_len": L,
+                  "parallelism": f"sequence parallel over {world} GPU(s), NCCL send/recv of boundary states, "
+                                 f"{B} micro-groups"},
+                 scaling="strong", clocks=clocks,
+                 roofline={"bound": "hbm", "achieved": alg / (ms / 1e3) / 1e9 / world, "peak": peaks["hbm_gbs"],
+                           "unit": "GB/s", "frac": alg / (ms / 1e3) / 1e9 / world / peaks["hbm_gbs"],
+                           "algorithmic_bytes_per_launch": alg // world})
+    return line
+
+
 def run_ffn(args, world, rank, local):
     """Spectral Lerp FFN on 16 x 4096 tokens, d_model = 1024, nb = 4, bf16 activations."""
     import torch
@@ -495,7 +549,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="core", choices=["core", "laplace", "ffn", "decode", "lm"])
+    ap.add_argument("--workload", default="core", choices=["core", "laplace", "laplace-sp", "ffn", "decode", "lm"])
     ap.add_argument("--decode-steps", type=int, default=256)
     ap.add_argument("--cpu-units", type=int, default=16)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -510,7 +564,7 @@ def main():
             print(json.dumps(line), flush=True)
         return
     world, rank, local = dist_setup(args.gpus)
-    run = {"core": run_core, "laplace": run_laplace, "ffn": run_ffn, "decode": run_decode,
+    run = {"core": run_core, "laplace": run_laplace, "laplace-sp": run_laplace_sp, "ffn": run_ffn, "decode": run_decode,
            "lm": run_lm}[args.workload]
     line = run(args, world, rank, local)
     if rank == 0:
