@@ -106,6 +106,16 @@ __device__ __forceinline__ void poly_sincos(float x, float *s_out, float *c_out)
   *c_out = co;
 }
 
+// sin and cos of x: x reduced by a two-part 2 pi to |r| <= pi, then the hardware
+// approximation (absolute error ~1e-6 for |x| up to a few hundred) -- for values that are
+// rounded to 16 bits or feed a TF32 / bf16 product next.
+__device__ __forceinline__ void sincos_2pi_fast(float x, float *s, float *c) {
+  const float k = rintf(x * 0.15915494309189535f);
+  float r = fmaf(-k, 6.28318548202514648f, x);
+  r = fmaf(-k, -1.7484556e-07f, r);
+  __sincosf(r, s, c);
+}
+
 struct SeqStrides {  // element strides of a (B, H, L, C) tensor with unit channel stride
   int64_t b, h, t;
 };

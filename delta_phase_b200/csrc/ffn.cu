@@ -19,6 +19,7 @@
 #include <array>
 #include <mutex>
 #include <string>
+#include <type_traits>
 
 #include "dp_common.cuh"
 
@@ -143,6 +144,152 @@ ffn_features_kernel(const T *__restrict__ x, const float *__restrict__ hdct, T *
   }
 }
 
+// Warp-per-token features for d = 32 R (256, 512, 1024): the token row lives in registers, lane l
+// holding x[R l .. R l + R).  FWHT butterflies on bits below log2 R run inside a lane,
+// the five higher bits across lanes with shuffles; the reference's recursive Haar takes
+// adjacent-pair differences inside a lane and folds the upper half of the current level
+// onto the lower half with a shuffle down, until one lane holds the last R values.
+// No shared memory and no block barriers; sin / cos through sincos_2pi_fast.
+template <typename T>
+__device__ __forceinline__ void store_pair(T *p, float a, float b) {
+  if constexpr (sizeof(T) == 2) {
+    *reinterpret_cast<__nv_bfloat162 *>(p) = __floats2bfloat162_rn(a, b);
+  } else {
+    *reinterpret_cast<float2 *>(p) = make_float2(a, b);
+  }
+}
+
+// cos and sin of n consecutive values (n even, p 4-byte aligned for bf16 / 8 for float)
+template <typename T, int N>
+__device__ __forceinline__ void store_cos_sin(T *cp, T *sp, const float *vals, float scale) {
+  if constexpr (sizeof(T) == 2 && N % 8 == 0) {
+#pragma unroll
+    for (int c = 0; c < N; c += 8) {
+      uint32_t cw[4], sw[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        float s0, c0, s1, c1;
+        sincos_2pi_fast(vals[c + 2 * k] * scale, &s0, &c0);
+        sincos_2pi_fast(vals[c + 2 * k + 1] * scale, &s1, &c1);
+        __nv_bfloat162 cc = __floats2bfloat162_rn(c0, c1), ss = __floats2bfloat162_rn(s0, s1);
+        cw[k] = *reinterpret_cast<uint32_t *>(&cc);
+        sw[k] = *reinterpret_cast<uint32_t *>(&ss);
+      }
+      *reinterpret_cast<uint4 *>(cp + c) = make_uint4(cw[0], cw[1], cw[2], cw[3]);
+      *reinterpret_cast<uint4 *>(sp + c) = make_uint4(sw[0], sw[1], sw[2], sw[3]);
+    }
+  } else {
+#pragma unroll
+    for (int c = 0; c < N; c += 2) {
+      float s0, c0, s1, c1;
+      sincos_2pi_fast(vals[c] * scale, &s0, &c0);
+      sincos_2pi_fast(vals[c + 1] * scale, &s1, &c1);
+      store_pair(cp + c, c0, c1);
+      store_pair(sp + c, s0, s1);
+    }
+  }
+}
+
+template <typename T, int R>
+__global__ void __launch_bounds__(256)
+ffn_features_warp_kernel(const T *__restrict__ x, const float *__restrict__ hdct, T *__restrict__ z, int tokens) {
+  // R >= 8: the 16-byte loads of x and hdct and the z stores of a lane start on 16-byte
+  // boundaries, and the Haar output runs of a lane have an even length
+  static_assert(R >= 8 && R % 8 == 0, "warp features need d = 256, 512 or 1024");
+  constexpr int d = 32 * R;
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (row >= tokens) return;  // whole warps only: no block barrier in this kernel
+  const float r2 = 0.70710678118654752f;
+  float v[R], hv[R];
+  {
+    const T *xr = x + row * d + R * lane;  // 16-byte aligned (checked by the launcher)
+    if constexpr (sizeof(T) == 2 && R % 8 == 0) {
+#pragma unroll
+      for (int r = 0; r < R; r += 8) {
+        const uint4 q = __ldg(reinterpret_cast<const uint4 *>(xr + r));
+        const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&w[k]));
+          v[r + 2 * k] = hv[r + 2 * k] = f.x;
+          v[r + 2 * k + 1] = hv[r + 2 * k + 1] = f.y;
+        }
+      }
+    } else {
+#pragma unroll
+      for (int r = 0; r < R; ++r) v[r] = hv[r] = to_f32(xr[r]);
+    }
+  }
+  T *zr = z + row * 6 * d;
+  // ---- FWHT (natural Sylvester order), /sqrt(d)
+#pragma unroll
+  for (int len = 1; len < R; len <<= 1) {
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      if (!(r & len)) {
+        const float u = v[r], w = v[r + len];
+        v[r] = u + w;
+        v[r + len] = u - w;
+      }
+    }
+  }
+#pragma unroll
+  for (int m = 1; m < 32; m <<= 1) {
+    const bool hi = lane & m;
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const float p = __shfl_xor_sync(0xffffffffu, v[r], m);
+      v[r] = hi ? p - v[r] : v[r] + p;
+    }
+  }
+  store_cos_sin<T, R>(zr + R * lane, zr + d + R * lane, v, rsqrtf((float)d));
+  // ---- DCT branch: cos / sin of the projections
+  {
+    const float *hr = hdct + row * d + R * lane;
+#pragma unroll
+    for (int r = 0; r < R; r += 4) {
+      const float4 q = *reinterpret_cast<const float4 *>(hr + r);
+      v[r] = q.x; v[r + 1] = q.y; v[r + 2] = q.z; v[r + 3] = q.w;
+    }
+    store_cos_sin<T, R>(zr + 2 * d + R * lane, zr + 3 * d + R * lane, v, 1.f);
+  }
+  // ---- recursive Haar: levels n = 32R .. 2R span nl = n / R lanes
+#pragma unroll
+  for (int nl = 32; nl >= 2; nl >>= 1) {
+    const int half_l = nl >> 1;
+    float hi[R / 2];
+#pragma unroll
+    for (int r = 0; r < R; r += 2) hi[r / 2] = (hv[r] - hv[r + 1]) * r2;
+    if (lane < nl) {
+      const int o = half_l * R + (R / 2) * lane;  // ho[n/2 + i], i = (R lane + r) / 2
+      store_cos_sin<T, R / 2>(zr + 4 * d + o, zr + 5 * d + o, hi, 1.f);
+    }
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const float p = __shfl_down_sync(0xffffffffu, hv[r], half_l);
+      hv[r] = (hv[r] + p) * r2;
+    }
+  }
+  // levels n = R .. 2 inside lane 0, then ho[0]
+  if (lane == 0) {
+    float ho[R];
+#pragma unroll
+    for (int n = R; n > 1; n >>= 1) {
+      const int half = n >> 1;
+#pragma unroll
+      for (int i = 0; i < half; ++i) ho[half + i] = (hv[2 * i] - hv[2 * i + 1]) * r2;
+      float lo[R / 2 > 0 ? R / 2 : 1];
+#pragma unroll
+      for (int i = 0; i < half; ++i) lo[i] = (hv[i] + hv[i + half]) * r2;
+#pragma unroll
+      for (int i = 0; i < half; ++i) hv[i] = lo[i];
+    }
+    ho[0] = hv[0];
+    store_cos_sin<T, R>(zr + 4 * d, zr + 5 * d, ho, 1.f);
+  }
+}
+
 // ---------------------------------------------------------------- cuBLAS handles
 cublasHandle_t handle_for_device(int dev) {
   static thread_local std::array<cublasHandle_t, 64> handles{};
@@ -209,7 +356,25 @@ extern "C" int dp_ffn_fwd(const void *x, int x_dtype, const void *dct, const voi
   const int threads = d >= 256 ? 256 : d;
   cudaFuncSetAttribute(ffn_features_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   cudaFuncSetAttribute(ffn_features_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (bf)
+  const int wgrid = (tokens + 7) / 8;
+  auto warp_features = [&](auto rc) {
+    constexpr int R = decltype(rc)::value;
+    if (bf)
+      ffn_features_warp_kernel<__nv_bfloat16, R><<<wgrid, 256, 0, st>>>(
+          static_cast<const __nv_bfloat16 *>(x), hdct, static_cast<__nv_bfloat16 *>(z), tokens);
+    else
+      ffn_features_warp_kernel<float, R><<<wgrid, 256, 0, st>>>(static_cast<const float *>(x), hdct,
+                                                                 static_cast<float *>(z), tokens);
+  };
+  const bool x16 = (reinterpret_cast<uintptr_t>(x) & 15) == 0;
+  if (!x16) {
+    // unaligned rows: the block-per-token kernel below
+  } else if (d == 1024) warp_features(std::integral_constant<int, 32>{});
+  else if (d == 512) warp_features(std::integral_constant<int, 16>{});
+  else if (d == 256) warp_features(std::integral_constant<int, 8>{});
+  if (x16 && d >= 256 && d <= 1024) {
+    // launched above
+  } else if (bf)
     ffn_features_kernel<__nv_bfloat16><<<tokens, threads, smem, st>>>(
         static_cast<const __nv_bfloat16 *>(x), hdct, static_cast<__nv_bfloat16 *>(z), d, log2d);
   else

@@ -112,3 +112,39 @@ def test_model_prefill_then_decode():
             lt, st = model.step(ids[:, t:t + 1], st)
     assert logits.shape == (2, 40, 500)
     assert rel_l2(lt[:, 0], logits[:, -1]) < TOL_F32
+
+
+@pytest.mark.parametrize("d", [64, 128, 256, 512, 1024, 2048])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_ffn_widths(d, dtype):
+    """Every width of the warp-per-token feature kernel (256..1024) and the block-per-token
+    one (64, 128, 2048), float32 and bf16 activations, against the fp64 oracle."""
+    torch.manual_seed(d)
+    nb, tokens = 4, 77
+    ffn = dp.LearnableSubstrateLerpFFN(d, nb).cuda()
+    with torch.no_grad():
+        for n, p in ffn.named_parameters():
+            p.copy_(torch.randn_like(p) * (1.0 if n == "substrate_logits" else 0.02))
+    x = torch.randn(tokens, d, device="cuda").to(dtype)
+    with torch.no_grad():
+        y = ffn(x)
+    params = {k: v.detach().cpu().numpy() for k, v in ffn.state_dict().items()}
+    ref = ospec.lerp_ffn(x.float().cpu().numpy(), params)
+    assert rel_l2(y.float(), ref) < (TOL_BF16 if dtype == torch.bfloat16 else TOL_F32)
+
+
+def test_ffn_unaligned_rows():
+    """x starting 2 bytes past a 16-byte boundary takes the block-per-token kernel."""
+    torch.manual_seed(3)
+    d, nb, tokens = 256, 4, 40
+    ffn = dp.LearnableSubstrateLerpFFN(d, nb).cuda()
+    with torch.no_grad():
+        for n, p in ffn.named_parameters():
+            p.copy_(torch.randn_like(p) * (1.0 if n == "substrate_logits" else 0.02))
+    buf = torch.randn(tokens * d + 1, device="cuda").to(torch.bfloat16)
+    x = buf[1:].view(tokens, d)
+    with torch.no_grad():
+        y = ffn(x)
+    params = {k: v.detach().cpu().numpy() for k, v in ffn.state_dict().items()}
+    ref = ospec.lerp_ffn(x.float().cpu().numpy(), params)
+    assert rel_l2(y.float(), ref) < TOL_BF16
