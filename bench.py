@@ -315,7 +315,7 @@ def run_laplace(args, world, rank, local):
     import torch.nn.functional as F
     from delta_phase_b200.kernels import laplace_chunkwise
     dev = torch.device("cuda", local)
-    B, H, L, D = 4, 16, 32768, 64
+    B, H, L, D = 4, 16, args.seq_len, 64
     g = torch.Generator(device=dev).manual_seed(2000 + rank)
     bf = torch.bfloat16
     tk = (torch.rand(B, H, L, D, device=dev, generator=g) * 2 * np.pi).to(bf)
@@ -331,7 +331,7 @@ def run_laplace(args, world, rank, local):
     alg = B * H * L * (4 * D * 2 + 2 + D * 4) + B * H * D * D * 8
     peaks, _ = load_peaks()
     line = _line("laplace-core tokens/s (B=4,H=16,L=32K,d_k=64)", world * B * L / (ms / 1e3), "tokens/s",
-                 args, world, ms, {"workload": "LaplacePhaseCore chunk solve, B=4,H=16,L=32768,d_k=64,C=64",
+                 args, world, ms, {"workload": f"LaplacePhaseCore chunk solve, B=4,H=16,L={L},d_k=64,C=64",
                                    "global_batch": B * world, "seq_len": L},
                  roofline={"bound": "hbm", "achieved": alg / (ms / 1e3) / 1e9, "peak": peaks["hbm_gbs"],
                            "unit": "GB/s", "frac": alg / (ms / 1e3) / 1e9 / peaks["hbm_gbs"],
@@ -552,6 +552,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="core", choices=["core", "laplace", "laplace-sp", "ffn", "decode", "lm"])
     ap.add_argument("--decode-steps", type=int, default=256)
+    ap.add_argument("--seq-len", type=int, default=32768,
+                    help="laplace workload only: sequence length (the headline is 32768; smaller for profiling)")
     ap.add_argument("--cpu-units", type=int, default=16)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
