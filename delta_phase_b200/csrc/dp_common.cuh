@@ -110,10 +110,20 @@ __device__ __forceinline__ void poly_sincos(float x, float *s_out, float *c_out)
 // approximation (absolute error ~1e-6 for |x| up to a few hundred) -- for values that are
 // rounded to 16 bits or feed a TF32 / bf16 product next.
 __device__ __forceinline__ void sincos_2pi_fast(float x, float *s, float *c) {
-  const float k = rintf(x * 0.15915494309189535f);
+  // round x / 2 pi to an integer with the 1.5 * 2^23 add (FMA pipe; |x| < 2^22)
+  const float k = fmaf(x, 0.15915494309189535f, 12582912.0f) - 12582912.0f;
   float r = fmaf(-k, 6.28318548202514648f, x);
   r = fmaf(-k, -1.7484556e-07f, r);
   __sincosf(r, s, c);
+}
+
+// Two floats -> packed bf16 pair, round to nearest even, with integer operations
+// (finite inputs; keeps the conversion off the special-function pipe).
+__device__ __forceinline__ uint32_t pack_bf16_rne(float a, float b) {
+  uint32_t ua = __float_as_uint(a), ub = __float_as_uint(b);
+  ua += 0x7FFFu + ((ua >> 16) & 1u);
+  ub += 0x7FFFu + ((ub >> 16) & 1u);
+  return __byte_perm(ua, ub, 0x7632);
 }
 
 struct SeqStrides {  // element strides of a (B, H, L, C) tensor with unit channel stride

@@ -153,7 +153,7 @@ ffn_features_kernel(const T *__restrict__ x, const float *__restrict__ hdct, T *
 template <typename T>
 __device__ __forceinline__ void store_pair(T *p, float a, float b) {
   if constexpr (sizeof(T) == 2) {
-    *reinterpret_cast<__nv_bfloat162 *>(p) = __floats2bfloat162_rn(a, b);
+    *reinterpret_cast<uint32_t *>(p) = pack_bf16_rne(a, b);
   } else {
     *reinterpret_cast<float2 *>(p) = make_float2(a, b);
   }
@@ -171,9 +171,8 @@ __device__ __forceinline__ void store_cos_sin(T *cp, T *sp, const float *vals, f
         float s0, c0, s1, c1;
         sincos_2pi_fast(vals[c + 2 * k] * scale, &s0, &c0);
         sincos_2pi_fast(vals[c + 2 * k + 1] * scale, &s1, &c1);
-        __nv_bfloat162 cc = __floats2bfloat162_rn(c0, c1), ss = __floats2bfloat162_rn(s0, s1);
-        cw[k] = *reinterpret_cast<uint32_t *>(&cc);
-        sw[k] = *reinterpret_cast<uint32_t *>(&ss);
+        cw[k] = pack_bf16_rne(c0, c1);
+        sw[k] = pack_bf16_rne(s0, s1);
       }
       *reinterpret_cast<uint4 *>(cp + c) = make_uint4(cw[0], cw[1], cw[2], cw[3]);
       *reinterpret_cast<uint4 *>(sp + c) = make_uint4(sw[0], sw[1], sw[2], sw[3]);
