@@ -165,6 +165,17 @@ def cpu_core_sample(units=2, L=8192, D=64, C=64, seed=0):
     return time.perf_counter() - t0, units * L
 
 
+def repeat_for(fn, min_seconds=10.0):
+    """Run fn() until at least min_seconds have passed; returns (seconds, repetitions)."""
+    t0, reps = time.perf_counter(), 0
+    while True:
+        fn(reps)
+        reps += 1
+        secs = time.perf_counter() - t0
+        if secs >= min_seconds:
+            return secs, reps
+
+
 def cpu_threads():
     try:
         from threadpoolctl import threadpool_info
@@ -276,10 +287,12 @@ def run_core(args, world, rank, local):
         "library": _capi.version(),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        secs, ht = cpu_core_sample(units=args.cpu_units)
+        parts = []
+        _, reps = repeat_for(lambda i: parts.append(cpu_core_sample(units=args.cpu_units, seed=i)))
+        secs, ht = sum(p[0] for p in parts), sum(p[1] for p in parts)  # timed regions only
         line["cpu_baseline"] = {
             "value": ht / H / secs, "unit": "tokens/s", "cores": cpu_threads(), "kind": "port",
-            "sample": f"{args.cpu_units} (b,h) units x L=8192 of the H=16 workload, numpy float32 "
+            "sample": f"{reps} x {args.cpu_units} (b,h) units x L=8192 of the H=16 workload, numpy float32 "
                       f"port of the reference chunkwise path (oracle.core), {secs:.1f} s; "
                       "tokens/s = head-tokens / 16 / s"}
     return line
@@ -345,12 +358,11 @@ def run_laplace(args, world, rank, local):
         vv = rng.standard_normal((1, u, Ls, D)).astype(np.float32)
         bb = (2 / (1 + np.exp(-rng.standard_normal((1, u, Ls))))).astype(np.float32)
         rr = np.exp(-np.logaddexp(0, rng.standard_normal((1, u, Ls, D)))).astype(np.float32)
-        t0 = time.perf_counter()
-        olap.laplace_chunkwise(K, Q, vv, bb, rr, 64, None, dtype=np.float32)
-        secs = time.perf_counter() - t0
-        line["cpu_baseline"] = {"value": u * Ls / H / secs, "unit": "tokens/s", "cores": cpu_threads(),
-                                "kind": "port", "sample": f"{u} (b,h) units x L={Ls}, numpy float32 port of "
-                                "LaplacePhaseCore.forward's chunk loop; tokens/s = head-tokens / 16 / s"}
+        secs, reps = repeat_for(lambda i: olap.laplace_chunkwise(K, Q, vv, bb, rr, 64, None, dtype=np.float32))
+        line["cpu_baseline"] = {"value": reps * u * Ls / H / secs, "unit": "tokens/s", "cores": cpu_threads(),
+                                "kind": "port", "sample": f"{reps} x {u} (b,h) units x L={Ls}, numpy float32 port "
+                                f"of LaplacePhaseCore.forward's chunk loop, {secs:.1f} s; "
+                                "tokens/s = head-tokens / 16 / s"}
     return line
 
 
@@ -440,11 +452,10 @@ def run_ffn(args, world, rank, local):
         from oracle import spectral as ospec
         params = {k: v.detach().float().cpu().numpy() for k, v in ffn.state_dict().items()}
         xs = x[:512].float().cpu().numpy()
-        t0 = time.perf_counter()
-        ospec.lerp_ffn(xs, params, dtype=np.float32)
-        secs = time.perf_counter() - t0
-        line["cpu_baseline"] = {"value": 512 / secs, "unit": "tokens/s", "cores": cpu_threads(), "kind": "port",
-                                "sample": "512 tokens, numpy float32 port of LearnableSubstrateLerpFFN.forward"}
+        secs, reps = repeat_for(lambda i: ospec.lerp_ffn(xs, params, dtype=np.float32))
+        line["cpu_baseline"] = {"value": reps * 512 / secs, "unit": "tokens/s", "cores": cpu_threads(),
+                                "kind": "port", "sample": f"{reps} x 512 tokens, numpy float32 port of "
+                                f"LearnableSubstrateLerpFFN.forward, {secs:.1f} s"}
     return line
 
 
