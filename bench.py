@@ -517,14 +517,22 @@ def run_lm(args, world, rank, local):
         def dec():
             nonlocal st
             logits, st = model.step(nxt, st)
-        dec_ms = _timed(dec, ndec, 2, stream)
+        dec_eager_ms = _timed(dec, min(ndec, 32), 2, stream)
+    # the whole step as one CUDA graph, state buffers updated in place
+    from delta_phase_b200 import DecodeGraph
+    graph = DecodeGraph(model, B, states=[(None, M) for M in states], autocast_dtype=torch.bfloat16)
+    dec_ms = _timed(lambda: graph.step(nxt), ndec, 3, stream)
+    del graph
     pre_ms = max_over_ranks(pre_ms, world)
     dec_ms = max_over_ranks(dec_ms, world)
+    dec_eager_ms = max_over_ranks(dec_eager_ms, world)
     return _line("LM prefill tokens/s (12x1024, 16 heads, vocab 32000)", world * B * L / (pre_ms / 1e3),
                  "tokens/s", args, world, pre_ms,
                  {"workload": "DeltaPhaseModel prefill B=16 x L=4096 then decode, bf16 autocast",
                   "global_batch": B * world, "seq_len": L, "model": "d1024-h16-l12"},
-                 decode={"ms_per_token": dec_ms, "steps": ndec, "batch": B})
+                 decode={"ms_per_token": dec_ms, "steps": ndec, "batch": B,
+                         "path": "DecodeGraph (one CUDA graph per token step)",
+                         "eager_ms_per_token": dec_eager_ms})
 
 
 def run_reference(args, world, rank):

@@ -21,6 +21,7 @@ from .layers import (
     LearnableSubstrateLerpFFN,
     ShortCausalConv1D,
 )
+from .decode_graph import DecodeGraph
 from .model import DeltaPhaseConfig, DeltaPhaseModel
 from .spectral import create_dct2_matrix, create_haar_matrix, create_hadamard_matrix
 
@@ -28,6 +29,7 @@ __version__ = "0.1.0"
 __all__ = [
     "DeltaPhaseConfig",
     "DeltaPhaseModel",
+    "DecodeGraph",
     "DeltaPhaseHolographicBlock",
     "LearnableSubstrateLerpFFN",
     "ShortCausalConv1D",

@@ -177,6 +177,28 @@ class DeltaPhaseHolographicBlock(nn.Module):
         x = x + self.ffn(self.norm2(x))
         return x, M_state
 
+    def _step_inplace(self, x_t: torch.Tensor, conv_state: torch.Tensor, memory_state: torch.Tensor):
+        """``step`` with the state updated in place: ``conv_state`` (B, d, k-1) and
+        ``memory_state`` (B, H, d_k, d_k) complex64 are overwritten with the new state, so
+        their addresses stay fixed (what a captured CUDA graph needs).  Returns x."""
+        res = x_t
+        normed = self.norm1(x_t)
+        conv_x, new_conv_state = self.causal_conv.step(normed, conv_state=conv_state)
+        conv_state.copy_(new_conv_state)
+        B, L, D = conv_x.shape
+        H, dk = self.n_heads, self.d_k
+        tk = self.w_k(conv_x).view(B, H, dk)
+        tq = self.w_q(conv_x).view(B, H, dk)
+        v = self.w_v(conv_x).view(B, H, dk)
+        beta = self._beta(conv_x).view(B, H)
+        dt = torch.promote_types(torch.promote_types(tk.dtype, tq.dtype), v.dtype)
+        tk, tq, v = tk.to(dt), tq.to(dt), v.to(dt)
+        self.last_beta = beta.detach().unsqueeze(-1)
+        out, _ = decode_step(memory_state, tk, tq, v, beta, state_out=memory_state)
+        retrieved_norm = self.norm_retrieved(out.reshape(B, 1, D))
+        x = res + self.out_proj(retrieved_norm)
+        return x + self.ffn(self.norm2(x))
+
     def step(self, x_t: torch.Tensor, state=None):
         """Single-token step (layers.py:246-291); returns ``(x, (conv_state, M))``."""
         res = x_t
