@@ -110,13 +110,19 @@ class LearnableSubstrateLerpFFN(nn.Module):
             raise TypeError("float64 inputs are not supported by the CUDA path")
         _capi.require_cuda(x, self.mat_dct)
         cdt = torch.bfloat16 if x.dtype == torch.bfloat16 else torch.float32
+        out_dt = x.dtype
+        if cdt == torch.float32 and torch.is_autocast_enabled(x.device.type):
+            # the reference's transforms and combine are matmuls, which autocast runs in
+            # its lower precision: take the bf16 path and return bf16 like they would
+            if torch.get_autocast_dtype(x.device.type) == torch.bfloat16:
+                cdt = out_dt = torch.bfloat16
         x2 = x.reshape(-1, self.d_model).to(cdt).contiguous()
         Fm, dct = self.folded(cdt)
         y = torch.empty_like(x2)
         ws = torch.empty(_capi.ffn_workspace_size(x2.shape[0], self.d_model, cdt),
                          device=x.device, dtype=torch.uint8)
         _capi.ffn_fwd(x2, dct, Fm, y, ws)
-        return y.view(x.shape).to(x.dtype)
+        return y.view(x.shape).to(out_dt)
 
     def get_substrate_probabilities(self):
         probs = F.softmax(self.substrate_logits, dim=0)

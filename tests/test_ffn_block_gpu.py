@@ -148,3 +148,21 @@ def test_ffn_unaligned_rows():
     params = {k: v.detach().cpu().numpy() for k, v in ffn.state_dict().items()}
     ref = ospec.lerp_ffn(x.float().cpu().numpy(), params)
     assert rel_l2(y.float(), ref) < TOL_BF16
+
+
+def test_ffn_follows_bf16_autocast():
+    """float32 activations under bf16 autocast (the LayerNorm in front of the FFN returns
+    float32) take the bf16 path, as the reference's matmuls would, and return bf16."""
+    torch.manual_seed(7)
+    d, nb, tokens = 1024, 4, 64
+    ffn = dp.LearnableSubstrateLerpFFN(d, nb).cuda()
+    with torch.no_grad():
+        for n, p in ffn.named_parameters():
+            p.copy_(torch.randn_like(p) * (1.0 if n == "substrate_logits" else 0.02))
+    x = torch.randn(tokens, d, device="cuda")
+    with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+        y = ffn(x)
+    assert y.dtype == torch.bfloat16
+    params = {k: v.detach().cpu().numpy() for k, v in ffn.state_dict().items()}
+    ref = ospec.lerp_ffn(x.to(torch.bfloat16).float().cpu().numpy(), params)
+    assert rel_l2(y.float(), ref) < TOL_BF16
