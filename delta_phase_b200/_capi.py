@@ -37,6 +37,8 @@ _SIG = {
     "dp_ffn_fwd": (_I, [_P, _I, _P, _P, _P, _I, _I, _P, ctypes.c_size_t, _P]),
     "dp_ffn_fwd_noalloc": (_I, [_P, _I, _P, _P, _P, _I, _I, _P]),
     "dp_ffn_noalloc_max_tokens": (ctypes.c_size_t, [_I, _I]),
+    "dp_ln_conv_silu": (_I, [_P, _I, _P, _P, ctypes.c_float, _P, _P, _P, _I, _I, _I, _I, _I, _P]),
+    "dp_layernorm": (_I, [_P, _I, _P, _P, _P, ctypes.c_float, _P, _P, _I, ctypes.c_int64, _I, _P]),
 }
 
 _lib = None
@@ -255,3 +257,28 @@ def ffn_fwd_noalloc(x, dct, F, y):
 
 def ffn_noalloc_max_tokens(d, dtype):
     return int(lib().dp_ffn_noalloc_max_tokens(d, _DTYPE_CODES[dtype]))
+
+
+def ln_conv_silu(x, ln_w, ln_b, eps, conv_w, conv_b, out):
+    """dp_ln_conv_silu: out = n + SiLU(causal depthwise conv(n)), n = LayerNorm(x); x, out
+    (B, L, d) contiguous; conv_w (d, k) float32."""
+    dev = require_cuda(x, ln_w, ln_b, conv_w, out)
+    B, L, d = x.shape
+    k = conv_w.shape[-1]
+    with torch.cuda.device(dev):
+        rc = lib().dp_ln_conv_silu(ptr(x), dtype_code(x), ptr(ln_w), ptr(ln_b), float(eps), ptr(conv_w),
+                                   ptr(conv_b) if conv_b is not None else None, ptr(out), dtype_code(out),
+                                   B, L, d, k, stream_of(dev))
+    _check("dp_ln_conv_silu", rc)
+
+
+def layernorm(x, ln_w, ln_b, eps, y, residual=None, sum_out=None):
+    """dp_layernorm: s = x (+ residual) (written to sum_out if given); y = LayerNorm(s).
+    x, y, residual, sum_out are (rows, d) contiguous."""
+    dev = require_cuda(x, ln_w, ln_b, y)
+    rows, d = x.shape
+    with torch.cuda.device(dev):
+        rc = lib().dp_layernorm(ptr(x), dtype_code(x), ptr(residual) if residual is not None else None,
+                                ptr(ln_w), ptr(ln_b), float(eps), ptr(sum_out) if sum_out is not None else None,
+                                ptr(y), dtype_code(y), rows, d, stream_of(dev))
+    _check("dp_layernorm", rc)

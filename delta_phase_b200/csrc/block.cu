@@ -1,0 +1,182 @@
+// Fused glue of DeltaPhaseHolographicBlock.forward (delta_phase/layers.py:177-244):
+//   dp_ln_conv_silu : conv_x = n + SiLU(causal_depthwise_conv(n)),  n = LayerNorm(x)
+//                     (norm1 and ShortCausalConv1D.forward, layers.py:60-88,178)
+//   dp_layernorm    : s = x (+ residual);  y = LayerNorm(s)  (norm_retrieved, norm2)
+// Each is one pass over the (tokens, d) activations instead of the separate
+// LayerNorm / transpose / conv / SiLU / add / cast kernels of the module, and each writes
+// its output directly in the dtype of the GEMM that consumes it.  LayerNorm statistics
+// are two-pass in fp32 (mean, then the mean of squared deviations), like torch's.
+#include <string>
+
+#include "dp_common.cuh"
+
+namespace dp {
+namespace {
+
+constexpr int kBlkThreads = 256;
+
+template <typename T>
+__device__ __forceinline__ void store_f32_as(T *p, float v);
+template <>
+__device__ __forceinline__ void store_f32_as<float>(float *p, float v) { *p = v; }
+template <>
+__device__ __forceinline__ void store_f32_as<__nv_bfloat16>(__nv_bfloat16 *p, float v) { *p = __float2bfloat16_rn(v); }
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int m = 16; m > 0; m >>= 1) v += __shfl_xor_sync(0xffffffffu, v, m);
+  return v;
+}
+
+// Grid (ceil(L / T), B); rows t0 - (k - 1) .. t0 + T - 1 of batch b are normalised into
+// shared memory (zeros before the sequence start: the conv's zero padding), then thread
+// c walks column c through the T tokens of the tile.
+template <typename InT, typename OutT>
+__global__ void __launch_bounds__(kBlkThreads)
+ln_conv_silu_kernel(const InT *__restrict__ x, const float *__restrict__ ln_w, const float *__restrict__ ln_b,
+                    float eps, const float *__restrict__ conv_w, const float *__restrict__ conv_b,
+                    OutT *__restrict__ out, int L, int d, int k, int T) {
+  extern __shared__ float nrm[];  // (T + k - 1) x d
+  const int b = blockIdx.y, t0 = blockIdx.x * T;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = kBlkThreads / 32;
+  const int rows = T + k - 1;
+  const float inv_d = 1.0f / (float)d;
+  for (int r = warp; r < rows; r += nwarps) {
+    const int t = t0 - (k - 1) + r;
+    float *nr = nrm + (size_t)r * d;
+    if (t < 0 || t >= L) {
+      for (int c = lane; c < d; c += 32) nr[c] = 0.f;
+      continue;
+    }
+    const InT *xr = x + ((size_t)b * L + t) * d;
+    float s = 0.f;
+    for (int c = lane; c < d; c += 32) {
+      const float v = to_f32(xr[c]);
+      nr[c] = v;
+      s += v;
+    }
+    const float mean = warp_sum(s) * inv_d;
+    float q = 0.f;
+    for (int c = lane; c < d; c += 32) {
+      const float dv = nr[c] - mean;
+      q = fmaf(dv, dv, q);
+    }
+    const float rstd = rsqrtf(warp_sum(q) * inv_d + eps);
+    for (int c = lane; c < d; c += 32) nr[c] = fmaf((nr[c] - mean) * rstd, ln_w[c], ln_b[c]);
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < d; c += kBlkThreads) {
+    float w[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) w[j] = j < k ? conv_w[(size_t)c * k + j] : 0.f;
+    const float cb = conv_b ? conv_b[c] : 0.f;
+    for (int i = 0; i < T && t0 + i < L; ++i) {
+      float acc = cb;
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (j < k) acc = fmaf(w[j], nrm[(size_t)(i + j) * d + c], acc);
+      const float silu = acc / (1.f + __expf(-acc));
+      store_f32_as(out + ((size_t)b * L + t0 + i) * d + c, nrm[(size_t)(i + k - 1) * d + c] + silu);
+    }
+  }
+}
+
+// One warp per row: s = x (+ res); y = LayerNorm(s); the row stays in L1 between passes.
+template <typename InT, typename OutT>
+__global__ void __launch_bounds__(kBlkThreads)
+layernorm_kernel(const InT *__restrict__ x, const float *__restrict__ res, const float *__restrict__ ln_w,
+                 const float *__restrict__ ln_b, float eps, float *__restrict__ sum_out, OutT *__restrict__ y,
+                 int64_t rows, int d) {
+  const int64_t r = (int64_t)blockIdx.x * (kBlkThreads / 32) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (r >= rows) return;
+  const InT *xr = x + r * d;
+  const float *rr = res ? res + r * d : nullptr;
+  const float inv_d = 1.0f / (float)d;
+  float s = 0.f;
+  for (int c = lane; c < d; c += 32) {
+    float v = to_f32(xr[c]);
+    if (rr) v += rr[c];
+    if (sum_out) sum_out[r * d + c] = v;
+    s += v;
+  }
+  const float mean = warp_sum(s) * inv_d;
+  float q = 0.f;
+  for (int c = lane; c < d; c += 32) {
+    float v = to_f32(xr[c]);
+    if (rr) v += rr[c];
+    const float dv = v - mean;
+    q = fmaf(dv, dv, q);
+  }
+  const float rstd = rsqrtf(warp_sum(q) * inv_d + eps);
+  for (int c = lane; c < d; c += 32) {
+    float v = to_f32(xr[c]);
+    if (rr) v += rr[c];
+    store_f32_as(y + r * d + c, fmaf((v - mean) * rstd, ln_w[c], ln_b[c]));
+  }
+}
+
+}  // namespace
+}  // namespace dp
+
+extern "C" int dp_ln_conv_silu(const void *x, int x_dtype, const float *ln_w, const float *ln_b, float eps,
+                               const float *conv_w, const float *conv_b, void *out, int out_dtype, int B, int L,
+                               int d, int k, void *stream) {
+  using namespace dp;
+  DP_REQUIRE(B >= 0 && L >= 0 && d >= 1 && k >= 1, DP_ERR_INVALID_ARGUMENT, "dp_ln_conv_silu: bad sizes");
+  DP_REQUIRE(k <= 8, DP_ERR_UNSUPPORTED, "dp_ln_conv_silu: kernel size must be <= 8");
+  DP_REQUIRE((x_dtype == DP_F32 || x_dtype == DP_BF16) && (out_dtype == DP_F32 || out_dtype == DP_BF16),
+             DP_ERR_INVALID_ARGUMENT, "dp_ln_conv_silu: dtypes must be float32 or bfloat16");
+  if (B == 0 || L == 0) return DP_OK;
+  DP_REQUIRE(x && ln_w && ln_b && conv_w && out, DP_ERR_INVALID_ARGUMENT, "dp_ln_conv_silu: null pointer");
+  int T = 16;
+  while (T > 1 && (size_t)(T + k - 1) * d * sizeof(float) > 200 * 1024) T >>= 1;
+  const size_t smem = (size_t)(T + k - 1) * d * sizeof(float);
+  DP_REQUIRE(smem <= 227 * 1024, DP_ERR_UNSUPPORTED, "dp_ln_conv_silu: d too large");
+  dim3 grid((L + T - 1) / T, B);
+  cudaStream_t st = as_stream(stream);
+  auto launch = [&](auto xt, auto ot) {
+    using XT = decltype(xt);
+    using OT = decltype(ot);
+    cudaFuncSetAttribute(ln_conv_silu_kernel<XT, OT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    ln_conv_silu_kernel<XT, OT><<<grid, kBlkThreads, smem, st>>>(static_cast<const XT *>(x), ln_w, ln_b, eps,
+                                                                 conv_w, conv_b, static_cast<OT *>(out), L, d, k, T);
+  };
+  if (x_dtype == DP_F32) {
+    if (out_dtype == DP_F32) launch(float{}, float{});
+    else launch(float{}, __nv_bfloat16{});
+  } else {
+    if (out_dtype == DP_F32) launch(__nv_bfloat16{}, float{});
+    else launch(__nv_bfloat16{}, __nv_bfloat16{});
+  }
+  return check_launch("ln_conv_silu_kernel");
+}
+
+extern "C" int dp_layernorm(const void *x, int x_dtype, const float *residual, const float *ln_w,
+                            const float *ln_b, float eps, float *sum_out, void *y, int y_dtype, int64_t rows, int d,
+                            void *stream) {
+  using namespace dp;
+  DP_REQUIRE(rows >= 0 && d >= 1, DP_ERR_INVALID_ARGUMENT, "dp_layernorm: bad sizes");
+  DP_REQUIRE((x_dtype == DP_F32 || x_dtype == DP_BF16) && (y_dtype == DP_F32 || y_dtype == DP_BF16),
+             DP_ERR_INVALID_ARGUMENT, "dp_layernorm: dtypes must be float32 or bfloat16");
+  if (rows == 0) return DP_OK;
+  DP_REQUIRE(x && ln_w && ln_b && y, DP_ERR_INVALID_ARGUMENT, "dp_layernorm: null pointer");
+  const int64_t blocks = (rows + kBlkThreads / 32 - 1) / (kBlkThreads / 32);
+  DP_REQUIRE(blocks < (1ll << 31), DP_ERR_UNSUPPORTED, "dp_layernorm: too many rows");
+  cudaStream_t st = as_stream(stream);
+  auto launch = [&](auto xt, auto ot) {
+    using XT = decltype(xt);
+    using OT = decltype(ot);
+    layernorm_kernel<XT, OT><<<(unsigned)blocks, kBlkThreads, 0, st>>>(static_cast<const XT *>(x), residual, ln_w,
+                                                                       ln_b, eps, sum_out, static_cast<OT *>(y),
+                                                                       rows, d);
+  };
+  if (x_dtype == DP_F32) {
+    if (y_dtype == DP_F32) launch(float{}, float{});
+    else launch(float{}, __nv_bfloat16{});
+  } else {
+    if (y_dtype == DP_F32) launch(__nv_bfloat16{}, float{});
+    else launch(__nv_bfloat16{}, __nv_bfloat16{});
+  }
+  return check_launch("layernorm_kernel");
+}

@@ -161,27 +161,69 @@ class DeltaPhaseHolographicBlock(nn.Module):
             beta = torch.ones_like(beta)
         return beta
 
+    def _proj_weights(self, dtype):
+        """[w_k; w_q; w_v; w_beta] weights and biases concatenated in ``dtype`` (one GEMM
+        for the four input projections), rebuilt when any of them changes."""
+        ts = (self.w_k.weight, self.w_q.weight, self.w_v.weight, self.w_beta.weight,
+              self.w_k.bias, self.w_q.bias, self.w_v.bias, self.w_beta.bias)
+        key = (dtype,) + tuple((t.data_ptr(), t._version) for t in ts)
+        if getattr(self, "_proj_key", None) != key:
+            with torch.no_grad():
+                W = torch.cat([t.detach() for t in ts[:4]], 0).to(dtype).contiguous()
+                bvec = torch.cat([t.detach() for t in ts[4:]], 0).to(dtype).contiguous()
+            self._proj_cache = (W, bvec)
+            self._proj_key = key
+        return self._proj_cache
+
     def forward(self, x: torch.Tensor, memory_state=None):
-        res = x
-        conv_x = self.causal_conv(self.norm1(x))
-        B, L, D = conv_x.shape
+        """Block forward (layers.py:177-244) on fused kernels: LayerNorm + causal conv +
+        SiLU + residual in one pass, the four input projections as one GEMM, the
+        delta-rule core, LayerNorm -> output projection, and the residual add fused into
+        norm2.  GEMM operands are bf16 under bf16 autocast (like the reference's autocast
+        matmuls) and float32 otherwise; the residual stream stays float32."""
+        if x.dtype == torch.float64:
+            raise TypeError("float64 inputs are not supported by the CUDA path")
+        _capi.require_cuda(x)
+        B, L, D = x.shape
         H, dk = self.n_heads, self.d_k
-        # (B, L, H, dk) projections viewed as (B, H, L, dk): the kernel reads them in
-        # place, handles the ragged last chunk itself (no padding copy) and writes the
-        # retrieved values straight into the (B, L, H*dk) buffer the norm consumes.
-        tk = self.w_k(conv_x).view(B, L, H, dk).transpose(1, 2)
-        tq = self.w_q(conv_x).view(B, L, H, dk).transpose(1, 2)
-        v = self.w_v(conv_x).view(B, L, H, dk).transpose(1, 2)
-        beta = self._beta(conv_x).transpose(1, 2)
-        dt = torch.promote_types(torch.promote_types(tk.dtype, tq.dtype), v.dtype)
-        tk, tq, v = tk.to(dt), tq.to(dt), v.to(dt)
+        bf16_ac = torch.is_autocast_enabled(x.device.type) and \
+            torch.get_autocast_dtype(x.device.type) == torch.bfloat16
+        gdt = torch.bfloat16 if (bf16_ac or x.dtype == torch.bfloat16) else torch.float32
+        xc = x.contiguous()
+        conv = self.causal_conv.conv
+        conv_x = torch.empty(B, L, D, device=x.device, dtype=gdt)
+        _capi.ln_conv_silu(xc, self.norm1.weight.float(), self.norm1.bias.float(), self.norm1.eps,
+                           conv.weight.detach().float().reshape(D, -1).contiguous(),
+                           None if conv.bias is None else conv.bias.detach().float(), conv_x)
+        W, bvec = self._proj_weights(gdt)
+        with torch.autocast(x.device.type, enabled=False):
+            proj = F.linear(conv_x, W, bvec)                      # (B, L, 3D + H)
+        # (B, L, H, dk) slices of the projection viewed as (B, H, L, dk): the kernel reads
+        # them in place and writes the retrieved values straight into (B, L, D)
+        tk = proj[..., :D].view(B, L, H, dk).transpose(1, 2)
+        tq = proj[..., D:2 * D].view(B, L, H, dk).transpose(1, 2)
+        v = proj[..., 2 * D:3 * D].view(B, L, H, dk).transpose(1, 2)
+        if self.beta_mode == "fixed":
+            beta = torch.ones(B, H, L, device=x.device, dtype=torch.float32)
+        else:
+            beta = (2.0 * torch.sigmoid(proj[..., 3 * D:].float())).transpose(1, 2)
         retrieved = torch.empty(B, L, D, device=x.device, dtype=torch.float32)
         _, M_state = chunkwise_forward(tk, tq, v, beta, self.chunk_size, memory_state,
                                        out=retrieved.view(B, L, H, dk).transpose(1, 2))
         self.last_beta = beta.detach()
-        x = res + self.out_proj(self.norm_retrieved(retrieved))
-        x = x + self.ffn(self.norm2(x))
-        return x, M_state
+        nr = self.norm_retrieved
+        rn = torch.empty(B * L, D, device=x.device, dtype=gdt)
+        _capi.layernorm(retrieved.view(B * L, D), nr.weight.float(), nr.bias.float(), nr.eps, rn)
+        o = self.out_proj(rn)
+        # s = x + out_proj(...) (float32), n2 = norm2(s) in the FFN's operand dtype
+        res = xc.view(B * L, D)
+        res32 = res if res.dtype == torch.float32 else res.float()
+        s_sum = torch.empty(B * L, D, device=x.device, dtype=torch.float32)
+        n2 = torch.empty(B * L, D, device=x.device, dtype=gdt)
+        _capi.layernorm(o.contiguous(), self.norm2.weight.float(), self.norm2.bias.float(), self.norm2.eps, n2,
+                        residual=res32, sum_out=s_sum)
+        out = s_sum.view(B, L, D) + self.ffn(n2.view(B, L, D))
+        return out.to(x.dtype) if x.dtype != torch.float32 else out, M_state
 
     def _step_inplace(self, x_t: torch.Tensor, conv_state: torch.Tensor, memory_state: torch.Tensor):
         """``step`` with the state updated in place: ``conv_state`` (B, d, k-1) and

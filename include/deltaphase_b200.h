@@ -190,6 +190,29 @@ DP_API int dp_ffn_fwd_noalloc(const void *x, int x_dtype, const void *dct, const
 /* Largest token count dp_ffn_fwd_noalloc accepts for width d and dtype x_dtype. */
 DP_API size_t dp_ffn_noalloc_max_tokens(int d, int x_dtype);
 
+/*
+ * Fused block glue: norm1 and ShortCausalConv1D.forward of DeltaPhaseHolographicBlock
+ * (delta_phase/layers.py:60-88,178):  n = LayerNorm(x) (weight ln_w, bias ln_b, eps);
+ * out = n + SiLU(b + sum_j w[c][j] n[t - (k-1) + j][c])  (zero before the sequence start).
+ *   x, out : (B, L, d) contiguous, float32 or bfloat16 (dtype codes)
+ *   conv_w : (d, k) float32 (the depthwise Conv1d weight (d, 1, k));  conv_b : (d) or NULL
+ * Limits: k <= 8; (16 + k - 1) * d * 4 bytes of shared memory at most 227 KB.
+ */
+DP_API int dp_ln_conv_silu(const void *x, int x_dtype, const float *ln_w, const float *ln_b, float eps,
+                           const float *conv_w, const float *conv_b, void *out, int out_dtype, int B, int L,
+                           int d, int k, void *stream);
+
+/*
+ * s = x (+ residual); y = LayerNorm(s) over the last dimension (weight ln_w, bias ln_b, eps).
+ * The block's norm_retrieved and norm2 (delta_phase/layers.py:237-243), with the residual
+ * add of the output projection fused in front of norm2.
+ *   x : (rows, d) float32 or bfloat16;  residual, sum_out : (rows, d) float32 or NULL
+ *   y : (rows, d) float32 or bfloat16 (y_dtype)
+ */
+DP_API int dp_layernorm(const void *x, int x_dtype, const float *residual, const float *ln_w,
+                        const float *ln_b, float eps, float *sum_out, void *y, int y_dtype, int64_t rows,
+                        int d, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -166,3 +166,47 @@ def test_ffn_follows_bf16_autocast():
     params = {k: v.detach().cpu().numpy() for k, v in ffn.state_dict().items()}
     ref = ospec.lerp_ffn(x.to(torch.bfloat16).float().cpu().numpy(), params)
     assert rel_l2(y.float(), ref) < TOL_BF16
+
+
+@pytest.mark.parametrize("L,d,out_dtype", [(37, 256, torch.float32), (70, 1024, torch.bfloat16), (5, 64, torch.float32)])
+def test_ln_conv_silu_kernel(L, d, out_dtype):
+    """dp_ln_conv_silu against torch's LayerNorm -> causal depthwise conv -> SiLU ->
+    residual (tile edges, the first k-1 tokens' zero padding, several sequences)."""
+    from delta_phase_b200 import _capi
+    torch.manual_seed(L)
+    B = 3
+    norm = torch.nn.LayerNorm(d).cuda()
+    conv = dp.ShortCausalConv1D(d).cuda()
+    with torch.no_grad():
+        norm.weight.uniform_(0.5, 1.5)
+        norm.bias.uniform_(-0.2, 0.2)
+        x = torch.randn(B, L, d, device="cuda") * 2 + 0.3
+        ref = conv(norm(x))
+        out = torch.empty(B, L, d, device="cuda", dtype=out_dtype)
+        _capi.ln_conv_silu(x, norm.weight, norm.bias, norm.eps, conv.conv.weight.reshape(d, -1).contiguous(),
+                           conv.conv.bias, out)
+    tol = 1e-5 if out_dtype == torch.float32 else 4e-3
+    assert rel_l2(out.float(), ref) < tol
+
+
+@pytest.mark.parametrize("x_dtype,y_dtype,resid", [(torch.float32, torch.float32, False),
+                                                   (torch.bfloat16, torch.bfloat16, True),
+                                                   (torch.float32, torch.bfloat16, True)])
+def test_layernorm_kernel(x_dtype, y_dtype, resid):
+    from delta_phase_b200 import _capi
+    torch.manual_seed(1)
+    rows, d = 300, 1024
+    norm = torch.nn.LayerNorm(d).cuda()
+    with torch.no_grad():
+        norm.weight.uniform_(0.5, 1.5)
+        norm.bias.uniform_(-0.2, 0.2)
+        x = (torch.randn(rows, d, device="cuda") * 3).to(x_dtype)
+        r = torch.randn(rows, d, device="cuda") if resid else None
+        s_ref = x.float() + (r if resid else 0)
+        y = torch.empty(rows, d, device="cuda", dtype=y_dtype)
+        s = torch.empty(rows, d, device="cuda") if resid else None
+        _capi.layernorm(x, norm.weight, norm.bias, norm.eps, y, residual=r, sum_out=s)
+        ref = norm(s_ref)
+    assert rel_l2(y.float(), ref) < (1e-5 if y_dtype == torch.float32 else 4e-3)
+    if resid:
+        assert rel_l2(s, s_ref) < 1e-7
