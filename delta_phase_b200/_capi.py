@@ -38,6 +38,7 @@ _SIG = {
     "dp_ffn_fwd_noalloc": (_I, [_P, _I, _P, _P, _P, _I, _I, _P]),
     "dp_ffn_noalloc_max_tokens": (ctypes.c_size_t, [_I, _I]),
     "dp_ln_conv_silu": (_I, [_P, _I, _P, _P, ctypes.c_float, _P, _P, _P, _I, _I, _I, _I, _I, _P]),
+    "dp_ln_conv_step": (_I, [_P, _I, _P, _P, ctypes.c_float, _P, _P, _P, _P, _I, _I, _I, _I, _P]),
     "dp_layernorm": (_I, [_P, _I, _P, _P, _P, ctypes.c_float, _P, _P, _I, ctypes.c_int64, _I, _P]),
 }
 
@@ -282,3 +283,19 @@ def layernorm(x, ln_w, ln_b, eps, y, residual=None, sum_out=None):
                                 ptr(ln_w), ptr(ln_b), float(eps), ptr(sum_out) if sum_out is not None else None,
                                 ptr(y), dtype_code(y), rows, d, stream_of(dev))
     _check("dp_layernorm", rc)
+
+
+def ln_conv_step(x, ln_w, ln_b, eps, conv_w, conv_b, conv_state, out):
+    """dp_ln_conv_step: one decode token; x, out (B, d) contiguous; conv_state (B, d, k-1)
+    float32 contiguous, updated in place."""
+    dev = require_cuda(x, ln_w, ln_b, conv_w, conv_state, out)
+    B, d = x.shape
+    k = conv_w.shape[-1]
+    if conv_state.dtype != torch.float32 or not conv_state.is_contiguous() or \
+            tuple(conv_state.shape) != (B, d, k - 1):
+        raise ValueError(f"conv_state must be a contiguous float32 ({B}, {d}, {k - 1}) tensor")
+    with torch.cuda.device(dev):
+        rc = lib().dp_ln_conv_step(ptr(x), dtype_code(x), ptr(ln_w), ptr(ln_b), float(eps), ptr(conv_w),
+                                   ptr(conv_b) if conv_b is not None else None, ptr(conv_state), ptr(out),
+                                   dtype_code(out), B, d, k, stream_of(dev))
+    _check("dp_ln_conv_step", rc)

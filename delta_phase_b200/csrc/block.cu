@@ -1,6 +1,8 @@
 // Fused glue of DeltaPhaseHolographicBlock.forward (delta_phase/layers.py:177-244):
 //   dp_ln_conv_silu : conv_x = n + SiLU(causal_depthwise_conv(n)),  n = LayerNorm(x)
 //                     (norm1 and ShortCausalConv1D.forward, layers.py:60-88,178)
+//   dp_ln_conv_step : the same for one decode token, with the conv's last k-1 inputs
+//                     kept in a (B, d, k-1) state (ShortCausalConv1D.step, layers.py:43-50)
 //   dp_layernorm    : s = x (+ residual);  y = LayerNorm(s)  (norm_retrieved, norm2)
 // Each is one pass over the (tokens, d) activations instead of the separate
 // LayerNorm / transpose / conv / SiLU / add / cast kernels of the module, and each writes
@@ -116,6 +118,59 @@ layernorm_kernel(const InT *__restrict__ x, const float *__restrict__ res, const
   }
 }
 
+// Decode step of norm1 + ShortCausalConv1D.step (layers.py:43-50,182-190): one CTA per
+// sequence.  n = LayerNorm(x_t); out = n + SiLU(b + sum_{j<k-1} w[j] state[j] + w[k-1] n);
+// state (d, k-1) float32 shifts left and takes n (the conv's last k-1 inputs).
+template <typename InT, typename OutT>
+__global__ void __launch_bounds__(kBlkThreads)
+ln_conv_step_kernel(const InT *__restrict__ x, const float *__restrict__ ln_w, const float *__restrict__ ln_b,
+                    float eps, const float *__restrict__ conv_w, const float *__restrict__ conv_b,
+                    float *__restrict__ state, OutT *__restrict__ out, int d, int k) {
+  __shared__ float red[kBlkThreads / 32];
+  __shared__ float stat[2];
+  const int b = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const InT *xr = x + (size_t)b * d;
+  const float inv_d = 1.0f / (float)d;
+  float s = 0.f;
+  for (int c = tid; c < d; c += kBlkThreads) s += to_f32(xr[c]);
+  s = warp_sum(s);
+  if (lane == 0) red[warp] = s;
+  __syncthreads();
+  if (tid == 0) {
+    float t = 0.f;
+    for (int w = 0; w < kBlkThreads / 32; ++w) t += red[w];
+    stat[0] = t * inv_d;
+  }
+  __syncthreads();
+  const float mean = stat[0];
+  float q = 0.f;
+  for (int c = tid; c < d; c += kBlkThreads) {
+    const float dv = to_f32(xr[c]) - mean;
+    q = fmaf(dv, dv, q);
+  }
+  q = warp_sum(q);
+  if (lane == 0) red[warp] = q;
+  __syncthreads();
+  if (tid == 0) {
+    float t = 0.f;
+    for (int w = 0; w < kBlkThreads / 32; ++w) t += red[w];
+    stat[1] = rsqrtf(t * inv_d + eps);
+  }
+  __syncthreads();
+  const float rstd = stat[1];
+  for (int c = tid; c < d; c += kBlkThreads) {
+    const float n = fmaf((to_f32(xr[c]) - mean) * rstd, ln_w[c], ln_b[c]);
+    float *st = state + ((size_t)b * d + c) * (k - 1);
+    const float *w = conv_w + (size_t)c * k;
+    float acc = conv_b ? conv_b[c] : 0.f;
+    for (int j = 0; j < k - 1; ++j) acc = fmaf(w[j], st[j], acc);
+    acc = fmaf(w[k - 1], n, acc);
+    for (int j = 0; j + 1 < k - 1; ++j) st[j] = st[j + 1];
+    if (k > 1) st[k - 2] = n;
+    store_f32_as(out + (size_t)b * d + c, n + acc / (1.f + __expf(-acc)));
+  }
+}
+
 }  // namespace
 }  // namespace dp
 
@@ -179,4 +234,31 @@ extern "C" int dp_layernorm(const void *x, int x_dtype, const float *residual, c
     else launch(__nv_bfloat16{}, __nv_bfloat16{});
   }
   return check_launch("layernorm_kernel");
+}
+
+extern "C" int dp_ln_conv_step(const void *x, int x_dtype, const float *ln_w, const float *ln_b, float eps,
+                               const float *conv_w, const float *conv_b, float *conv_state, void *out,
+                               int out_dtype, int B, int d, int k, void *stream) {
+  using namespace dp;
+  DP_REQUIRE(B >= 0 && d >= 1 && k >= 1, DP_ERR_INVALID_ARGUMENT, "dp_ln_conv_step: bad sizes");
+  DP_REQUIRE((x_dtype == DP_F32 || x_dtype == DP_BF16) && (out_dtype == DP_F32 || out_dtype == DP_BF16),
+             DP_ERR_INVALID_ARGUMENT, "dp_ln_conv_step: dtypes must be float32 or bfloat16");
+  if (B == 0) return DP_OK;
+  DP_REQUIRE(x && ln_w && ln_b && conv_w && out && (k == 1 || conv_state), DP_ERR_INVALID_ARGUMENT,
+             "dp_ln_conv_step: null pointer");
+  cudaStream_t st = as_stream(stream);
+  auto launch = [&](auto xt, auto ot) {
+    using XT = decltype(xt);
+    using OT = decltype(ot);
+    ln_conv_step_kernel<XT, OT><<<B, kBlkThreads, 0, st>>>(static_cast<const XT *>(x), ln_w, ln_b, eps, conv_w,
+                                                           conv_b, conv_state, static_cast<OT *>(out), d, k);
+  };
+  if (x_dtype == DP_F32) {
+    if (out_dtype == DP_F32) launch(float{}, float{});
+    else launch(float{}, __nv_bfloat16{});
+  } else {
+    if (out_dtype == DP_F32) launch(__nv_bfloat16{}, float{});
+    else launch(__nv_bfloat16{}, __nv_bfloat16{});
+  }
+  return check_launch("ln_conv_step_kernel");
 }

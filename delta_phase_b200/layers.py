@@ -225,55 +225,85 @@ class DeltaPhaseHolographicBlock(nn.Module):
         out = s_sum.view(B, L, D) + self.ffn(n2.view(B, L, D))
         return out.to(x.dtype) if x.dtype != torch.float32 else out, M_state
 
+    def _out_proj_weights(self, dtype):
+        """out_proj weight and bias in ``dtype``, rebuilt when either changes."""
+        ts = (self.out_proj.weight, self.out_proj.bias)
+        key = (dtype,) + tuple((t.data_ptr(), t._version) for t in ts)
+        if getattr(self, "_oproj_key", None) != key:
+            with torch.no_grad():
+                self._oproj_cache = tuple(t.detach().to(dtype).contiguous() for t in ts)
+            self._oproj_key = key
+        return self._oproj_cache
+
     def _step_inplace(self, x_t: torch.Tensor, conv_state: torch.Tensor, memory_state: torch.Tensor):
-        """``step`` with the state updated in place: ``conv_state`` (B, d, k-1) and
-        ``memory_state`` (B, H, d_k, d_k) complex64 are overwritten with the new state, so
-        their addresses stay fixed (what a captured CUDA graph needs).  Returns x."""
-        res = x_t
-        normed = self.norm1(x_t)
-        conv_x, new_conv_state = self.causal_conv.step(normed, conv_state=conv_state)
-        conv_state.copy_(new_conv_state)
-        B, L, D = conv_x.shape
+        """One decode token (layers.py:246-291) with the state updated in place:
+        ``conv_state`` (B, d, k-1) float32 and ``memory_state`` (B, H, d_k, d_k) complex64
+        are overwritten, so their addresses stay fixed (what a captured CUDA graph needs).
+        norm1 + the conv step in one kernel, the projections as one GEMM on cached
+        weights (no per-call casts), the fused decode kernel, norm_retrieved, and norm2
+        with the residual add fused in.  Returns x (B, 1, d)."""
+        if x_t.dtype == torch.float64:
+            raise TypeError("float64 inputs are not supported by the CUDA path")
+        B, _, D = x_t.shape
         H, dk = self.n_heads, self.d_k
-        tk = self.w_k(conv_x).view(B, H, dk)
-        tq = self.w_q(conv_x).view(B, H, dk)
-        v = self.w_v(conv_x).view(B, H, dk)
-        beta = self._beta(conv_x).view(B, H)
-        dt = torch.promote_types(torch.promote_types(tk.dtype, tq.dtype), v.dtype)
-        tk, tq, v = tk.to(dt), tq.to(dt), v.to(dt)
-        self.last_beta = beta.detach().unsqueeze(-1)
-        out, _ = decode_step(memory_state, tk, tq, v, beta, state_out=memory_state)
-        retrieved_norm = self.norm_retrieved(out.reshape(B, 1, D))
-        x = res + self.out_proj(retrieved_norm)
-        return x + self.ffn(self.norm2(x))
+        bf16_ac = torch.is_autocast_enabled(x_t.device.type) and \
+            torch.get_autocast_dtype(x_t.device.type) == torch.bfloat16
+        gdt = torch.bfloat16 if (bf16_ac or x_t.dtype == torch.bfloat16) else torch.float32
+        xc = x_t.reshape(B, D).contiguous()
+        conv = self.causal_conv.conv
+        conv_x = torch.empty(B, D, device=x_t.device, dtype=gdt)
+        _capi.ln_conv_step(xc, self.norm1.weight.float(), self.norm1.bias.float(), self.norm1.eps,
+                           conv.weight.detach().float().reshape(D, -1).contiguous(),
+                           None if conv.bias is None else conv.bias.detach().float(), conv_state, conv_x)
+        W, bvec = self._proj_weights(gdt)
+        Wo, bo = self._out_proj_weights(gdt)
+        with torch.autocast(x_t.device.type, enabled=False):
+            proj = F.linear(conv_x, W, bvec)                      # (B, 3D + H)
+            tk = proj[:, :D].view(B, H, dk)
+            tq = proj[:, D:2 * D].view(B, H, dk)
+            v = proj[:, 2 * D:3 * D].view(B, H, dk)
+            if self.beta_mode == "fixed":
+                beta = torch.ones(B, H, device=x_t.device, dtype=torch.float32)
+            else:
+                beta = 2.0 * torch.sigmoid(proj[:, 3 * D:].float())
+            self.last_beta = beta.detach().unsqueeze(-1)
+            out, _ = decode_step(memory_state, tk, tq, v, beta, state_out=memory_state)
+            nr = self.norm_retrieved
+            rn = torch.empty(B, D, device=x_t.device, dtype=gdt)
+            _capi.layernorm(out.view(B, D), nr.weight.float(), nr.bias.float(), nr.eps, rn)
+            o = F.linear(rn, Wo, bo)
+            res32 = xc if xc.dtype == torch.float32 else xc.float()
+            s_sum = torch.empty(B, D, device=x_t.device, dtype=torch.float32)
+            n2 = torch.empty(B, D, device=x_t.device, dtype=gdt)
+            _capi.layernorm(o, self.norm2.weight.float(), self.norm2.bias.float(), self.norm2.eps, n2,
+                            residual=res32, sum_out=s_sum)
+        y = s_sum + self.ffn(n2)
+        y = y.view(B, 1, D)
+        return y.to(x_t.dtype) if x_t.dtype != torch.float32 else y
 
     def step(self, x_t: torch.Tensor, state=None):
-        """Single-token step (layers.py:246-291); returns ``(x, (conv_state, M))``."""
-        res = x_t
-        normed = self.norm1(x_t)
+        """Single-token step (layers.py:246-291); returns ``(x, (conv_state, M))``.
+        The input state is not modified: the new conv state (float32, (B, d, k-1)) and
+        memory state are fresh tensors."""
+        B, _, D = x_t.shape
+        H, dk = self.n_heads, self.d_k
         if state is None:
             conv_state, memory_state = None, None
         elif isinstance(state, tuple):
             conv_state, memory_state = state
         else:
             conv_state, memory_state = None, state
-        conv_x, new_conv_state = self.causal_conv.step(normed, conv_state=conv_state)
-        B, L, D = conv_x.shape
-        H, dk = self.n_heads, self.d_k
-        tk = self.w_k(conv_x).view(B, H, dk)
-        tq = self.w_q(conv_x).view(B, H, dk)
-        v = self.w_v(conv_x).view(B, H, dk)
-        beta = self._beta(conv_x).view(B, H)
-        dt = torch.promote_types(torch.promote_types(tk.dtype, tq.dtype), v.dtype)
-        tk, tq, v = tk.to(dt), tq.to(dt), v.to(dt)
-        self.last_beta = beta.detach().unsqueeze(-1)
+        k = self.causal_conv.kernel_size
+        if conv_state is None:
+            conv_new = torch.zeros(B, D, k - 1, device=x_t.device, dtype=torch.float32)
+        else:
+            conv_new = conv_state.detach().to(torch.float32).clone().contiguous()
         if memory_state is None:
-            memory_state = torch.zeros(B, H, dk, dk, dtype=torch.complex64, device=x_t.device)
-        out, memory_state = decode_step(memory_state, tk, tq, v, beta)
-        retrieved_norm = self.norm_retrieved(out.reshape(B, 1, D))
-        x = res + self.out_proj(retrieved_norm)
-        x = x + self.ffn(self.norm2(x))
-        return x, (new_conv_state, memory_state)
+            mem_new = torch.zeros(B, H, dk, dk, dtype=torch.complex64, device=x_t.device)
+        else:
+            mem_new = memory_state.detach().to(torch.complex64).clone().contiguous()
+        x = self._step_inplace(x_t, conv_new, mem_new)
+        return x, (conv_new, mem_new)
 
 
 class LaplacePhaseCore(nn.Module):

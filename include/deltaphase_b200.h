@@ -203,6 +203,16 @@ DP_API int dp_ln_conv_silu(const void *x, int x_dtype, const float *ln_w, const 
                            int d, int k, void *stream);
 
 /*
+ * Decode step of the same (ShortCausalConv1D.step, delta_phase/layers.py:43-50,182-190):
+ * n = LayerNorm(x_t); out = n + SiLU(b + sum_{j<k-1} w[c][j] state[c][j] + w[c][k-1] n[c]);
+ * then state (B, d, k-1) float32, the conv's last k-1 inputs, shifts left and takes n.
+ *   x, out : (B, d) contiguous, float32 or bfloat16;  conv_w : (d, k);  conv_b : (d) or NULL
+ */
+DP_API int dp_ln_conv_step(const void *x, int x_dtype, const float *ln_w, const float *ln_b, float eps,
+                           const float *conv_w, const float *conv_b, float *conv_state, void *out,
+                           int out_dtype, int B, int d, int k, void *stream);
+
+/*
  * s = x (+ residual); y = LayerNorm(s) over the last dimension (weight ln_w, bias ln_b, eps).
  * The block's norm_retrieved and norm2 (delta_phase/layers.py:237-243), with the residual
  * add of the output projection fused in front of norm2.

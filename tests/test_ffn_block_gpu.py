@@ -210,3 +210,27 @@ def test_layernorm_kernel(x_dtype, y_dtype, resid):
     assert rel_l2(y.float(), ref) < (1e-5 if y_dtype == torch.float32 else 4e-3)
     if resid:
         assert rel_l2(s, s_ref) < 1e-7
+
+
+@pytest.mark.parametrize("out_dtype", [torch.float32, torch.bfloat16])
+def test_ln_conv_step_kernel(out_dtype):
+    """dp_ln_conv_step over 6 tokens against LayerNorm + ShortCausalConv1D.step, the
+    (B, d, k-1) conv state carried through the kernel."""
+    from delta_phase_b200 import _capi
+    torch.manual_seed(4)
+    B, d = 5, 512
+    norm = torch.nn.LayerNorm(d).cuda()
+    conv = dp.ShortCausalConv1D(d).cuda()
+    with torch.no_grad():
+        norm.weight.uniform_(0.5, 1.5)
+        norm.bias.uniform_(-0.2, 0.2)
+        st_ref = torch.randn(B, d, 3, device="cuda")
+        st = st_ref.clone()
+        for _ in range(6):
+            x = torch.randn(B, 1, d, device="cuda") * 2
+            ref, st_ref = conv.step(norm(x), conv_state=st_ref)
+            out = torch.empty(B, d, device="cuda", dtype=out_dtype)
+            _capi.ln_conv_step(x.view(B, d), norm.weight, norm.bias, norm.eps,
+                               conv.conv.weight.reshape(d, -1).contiguous(), conv.conv.bias, st, out)
+            assert rel_l2(out.float(), ref.view(B, d)) < (1e-5 if out_dtype == torch.float32 else 4e-3)
+            assert rel_l2(st, st_ref) < 1e-6
