@@ -55,6 +55,7 @@ constexpr float kLogFloor = -80.0f;
 constexpr float kFastRange = 64.0f;  // max |Lam[m] - Lref_b| for the factorised solve
 constexpr int BAR_SOLVE = 1;   // named barrier of the solve warps 0, 4..7 (160 threads)
 constexpr int BAR_PH = 2;      // named barrier of the phasor warps 1..3 (96 threads)
+constexpr int BAR_L2 = 3;      // named barrier of warps 0..3 (128 threads): state operand ready
 
 // stage: theta_k, theta_q, logmag_k, logmag_q rows of a chunk (64 rows x 128 B each)
 constexpr int ST_TK = 0, ST_TQ = kC * 128, ST_MK = 2 * kC * 128, ST_MQ = 3 * kC * 128;
@@ -426,8 +427,11 @@ __global__ void __launch_bounds__(kThreads, 1) laplace_tc_kernel(LapTcArgs a) {
       // ---- L1p: prefetch of the next chunk's v, log-decay and beta
       if (c + 1 < nchunks) prefetch_vlr(a, b, h, oh, c + 1, tid, pv, pl, pb);
     }
-    // ---- L2: S^T (TMEM fp32) -> bf16 operand (128 x 32), MN-major B of [K;Q] S0^T
+    // L1 -> the decay pass reads the staged log-decay and beta of every thread
+    __syncthreads();
+    bool bad = false;
     if (warp < 4) {
+      // ---- L2: S^T (TMEM fp32) -> bf16 operand (128 x 32), MN-major B of [K;Q] S0^T
       const int j = 32 * q + lane;
 #pragma unroll
       for (int u = 0; u < 2; ++u) {
@@ -441,70 +445,71 @@ __global__ void __launch_bounds__(kThreads, 1) laplace_tc_kernel(LapTcArgs a) {
               make_uint4(pack_bf16(ss[0], ss[1]), pack_bf16(ss[2], ss[3]), pack_bf16(ss[4], ss[5]), pack_bf16(ss[6], ss[7]));
         }
       }
-    }
-    fence_proxy_async_smem();
-    tc_fence_before();
-    __syncthreads();
-
-    // ---- L3: [K;Q] K^T -> D1 (M=128, N=64) and [K;Q] S0^T -> D3 (M=128, N=32)
-    if (tid == 0) {
-      tc_fence_after();
-      const uint32_t sa = smem_u32(kq), ss = smem_u32(s0);
+      fence_proxy_async_smem();
+      tc_fence_before();
+      group_sync(BAR_L2, 128);
+      // ---- L3: [K;Q] K^T -> D1 (M=128, N=64) and [K;Q] S0^T -> D3 (M=128, N=32).  The
+      //      issuing thread is held ~45 cycles per MMA, so warp 0 does no decay work.
+      if (tid == 0) {
+        tc_fence_after();
+        const uint32_t sa = smem_u32(kq), ss = smem_u32(s0);
 #pragma unroll
-      for (int kk = 0; kk < 8; ++kk) {
-        const uint64_t ad = make_desc(sa + kk * 256, 128, RG_KQ);
-        mma_f16_ss(tmem + COL_D1, ad, make_desc(sa + kk * 256, 128, RG_KQ), idesc_bf16(128, 64, false, false), kk > 0);
-        mma_f16_ss(tmem + COL_D3, ad, make_desc(ss + kk * 2 * RG_32, RG_32, 128), idesc_bf16(128, 32, false, true), kk > 0);
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint64_t ad = make_desc(sa + kk * 256, 128, RG_KQ);
+          mma_f16_ss(tmem + COL_D1, ad, make_desc(sa + kk * 256, 128, RG_KQ), idesc_bf16(128, 64, false, false), kk > 0);
+          mma_f16_ss(tmem + COL_D3, ad, make_desc(ss + kk * 2 * RG_32, RG_32, 128), idesc_bf16(128, 32, false, true), kk > 0);
+        }
+        mma_commit(mma_bar);
       }
-      mma_commit(mma_bar);
+    } else {
+      // ---- decay (warps 4..7, overlapping L2 and the MMAs): cumulative log-decay and the
+      //      block-relative factors, 16 channels per pass
+      for (int pass = 0; pass < 2; ++pass) {
+          const int o = 16 * pass + 4 * (warp - 4) + (lane >> 3), p = lane & 7;  // tokens 8p .. 8p + 7
+        float *lo = lamT + o * LDM + 8 * p;
+        const float4 x0 = *reinterpret_cast<const float4 *>(lo), x1 = *reinterpret_cast<const float4 *>(lo + 4);
+        const float4 b0 = *reinterpret_cast<const float4 *>(bs + 8 * p), b1 = *reinterpret_cast<const float4 *>(bs + 8 * p + 4);
+        const float bsv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+        float l[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+  #pragma unroll
+        for (int i = 1; i < 8; ++i) l[i] += l[i - 1];
+        float tot = l[7];
+  #pragma unroll
+        for (int d = 1; d < 8; d <<= 1) {
+          const float n = __shfl_up_sync(0xffffffffu, tot, d, 8);
+          if (p >= d) tot += n;
+        }
+        const float excl = tot - l[7];
+        const float excl_prev = __shfl_up_sync(0xffffffffu, excl, 1, 8);
+        const float lref = (p & 1) ? excl_prev : excl;  // Lam[16 (p / 2) - 1]
+        float e[8], dev = 0.f;
+  #pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          l[i] += excl;
+          const float d = l[i] - lref;
+          e[i] = __expf(d);
+          dev = fmaxf(dev, fabsf(d));
+        }
+        *reinterpret_cast<float4 *>(lo) = make_float4(l[0], l[1], l[2], l[3]);
+        *reinterpret_cast<float4 *>(lo + 4) = make_float4(l[4], l[5], l[6], l[7]);
+        float *eo = eaT + o * LDM + 8 * p;
+        *reinterpret_cast<float4 *>(eo) = make_float4(e[0], e[1], e[2], e[3]);
+        *reinterpret_cast<float4 *>(eo + 4) = make_float4(e[4], e[5], e[6], e[7]);
+        if (p & 1) rho[(p >> 1) * kNo + o] = e[7];
+        else eref[(p >> 1) * kNo + o] = __expf(lref);
+        if (p == 7) edec[o] = __expf(l[7]);
+        const float l63 = __shfl_sync(0xffffffffu, l[7], (lane & ~7) | 7);
+        if (!(p & 1)) wsc[(p >> 1) * kNo + o] = __expf(l63 - lref);
+        float bt[8];
+  #pragma unroll
+        for (int i = 0; i < 8; ++i) bt[i] = __fdividef(bsv[i], e[i]);
+        float *bo = btT + o * LDM + 8 * p;
+        *reinterpret_cast<float4 *>(bo) = make_float4(bt[0], bt[1], bt[2], bt[3]);
+        *reinterpret_cast<float4 *>(bo + 4) = make_float4(bt[4], bt[5], bt[6], bt[7]);
+        bad = bad || !(dev <= kFastRange);
+      }
     }
     mma_pending = true;
-    // ---- decay: cumulative log-decay, block-relative factors (overlaps the MMAs)
-    bool bad;
-    {
-      const int o = tid >> 3, p = tid & 7;  // channel o, tokens 8p .. 8p + 7
-      float *lo = lamT + o * LDM + 8 * p;
-      const float4 x0 = *reinterpret_cast<const float4 *>(lo), x1 = *reinterpret_cast<const float4 *>(lo + 4);
-      const float4 b0 = *reinterpret_cast<const float4 *>(bs + 8 * p), b1 = *reinterpret_cast<const float4 *>(bs + 8 * p + 4);
-      const float bsv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
-      float l[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-#pragma unroll
-      for (int i = 1; i < 8; ++i) l[i] += l[i - 1];
-      float tot = l[7];
-#pragma unroll
-      for (int d = 1; d < 8; d <<= 1) {
-        const float n = __shfl_up_sync(0xffffffffu, tot, d, 8);
-        if (p >= d) tot += n;
-      }
-      const float excl = tot - l[7];
-      const float excl_prev = __shfl_up_sync(0xffffffffu, excl, 1, 8);
-      const float lref = (p & 1) ? excl_prev : excl;  // Lam[16 (p / 2) - 1]
-      float e[8], dev = 0.f;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        l[i] += excl;
-        const float d = l[i] - lref;
-        e[i] = __expf(d);
-        dev = fmaxf(dev, fabsf(d));
-      }
-      *reinterpret_cast<float4 *>(lo) = make_float4(l[0], l[1], l[2], l[3]);
-      *reinterpret_cast<float4 *>(lo + 4) = make_float4(l[4], l[5], l[6], l[7]);
-      float *eo = eaT + o * LDM + 8 * p;
-      *reinterpret_cast<float4 *>(eo) = make_float4(e[0], e[1], e[2], e[3]);
-      *reinterpret_cast<float4 *>(eo + 4) = make_float4(e[4], e[5], e[6], e[7]);
-      if (p & 1) rho[(p >> 1) * kNo + o] = e[7];
-      else eref[(p >> 1) * kNo + o] = __expf(lref);
-      if (p == 7) edec[o] = __expf(l[7]);
-      const float l63 = __shfl_sync(0xffffffffu, l[7], (lane & ~7) | 7);
-      if (!(p & 1)) wsc[(p >> 1) * kNo + o] = __expf(l63 - lref);
-      float bt[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) bt[i] = __fdividef(bsv[i], e[i]);
-      float *bo = btT + o * LDM + 8 * p;
-      *reinterpret_cast<float4 *>(bo) = make_float4(bt[0], bt[1], bt[2], bt[3]);
-      *reinterpret_cast<float4 *>(bo + 4) = make_float4(bt[4], bt[5], bt[6], bt[7]);
-      bad = !(dev <= kFastRange);
-    }
     if (tid == 0) ok = mbar_wait(mma_bar, mma_phase, kTimeoutNs);
     if (__syncthreads_or(!ok)) { ok = false; break; }
     mma_phase ^= 1;
