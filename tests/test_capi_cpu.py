@@ -73,6 +73,23 @@ def test_other_entry_points_validate_arguments():
     assert L.dp_ffn_workspace_size(10, 64, 1) >= 10 * 64 * 4 + 10 * 6 * 64 * 2
 
 
+def test_block_glue_entry_points_validate_arguments():
+    """dp_ln_conv_silu / dp_ln_conv_step / dp_layernorm reject bad sizes, dtypes and null
+    pointers before touching the device; empty batches are no-ops."""
+    L = _capi.lib()
+    # kernel size above 8, float16 x, null pointers, negative sizes
+    assert L.dp_ln_conv_silu(None, 0, None, None, 1e-5, None, None, None, 0, 1, 4, 64, 9, None) == 2
+    assert L.dp_ln_conv_silu(None, 2, None, None, 1e-5, None, None, None, 0, 1, 4, 64, 4, None) == 1
+    assert L.dp_ln_conv_silu(None, 0, None, None, 1e-5, None, None, None, 0, 1, 4, 64, 4, None) == 1
+    assert L.dp_ln_conv_silu(None, 0, None, None, 1e-5, None, None, None, 0, 0, 4, 64, 4, None) == 0
+    assert L.dp_ln_conv_step(None, 0, None, None, 1e-5, None, None, None, None, 0, -1, 64, 4, None) == 1
+    assert L.dp_ln_conv_step(None, 0, None, None, 1e-5, None, None, None, None, 0, 2, 64, 4, None) == 1
+    assert L.dp_ln_conv_step(None, 0, None, None, 1e-5, None, None, None, None, 0, 0, 64, 4, None) == 0
+    assert L.dp_layernorm(None, 0, None, None, None, 1e-5, None, None, 2, 3, 64, None) == 1
+    assert L.dp_layernorm(None, 0, None, None, None, 1e-5, None, None, 0, 3, 64, None) == 1
+    assert L.dp_layernorm(None, 0, None, None, None, 1e-5, None, None, 0, 0, 64, None) == 0
+
+
 def test_python_layer_rejects_cpu_tensors():
     import torch
 
