@@ -7,22 +7,24 @@
 // Real form (see core_simt.cu): per chunk of 64 tokens with key features K (64 x 128,
 // interleaved cos/sin), query features Q, values V, write strengths beta and the state
 // S (64 x 128, fp32, kept transposed in tensor memory for the whole sequence):
-//   A = strict_lower(K K^T / 64) diag(beta),  bT = diag(beta) (I + A)^-1
-//   W = bT K,  Ut = bT V,  P = tril(Q K^T)            (independent of the state)
-//   U = Ut - W S^T / 64;  O = (Q S^T + P U) / 64;  S^T += K^T U   (the state chain)
+//   A = strict_lower(K K^T / 64) diag(beta),  bT = diag(beta) (I + A)^-1,  P = tril(Q K^T)
+//   E = V - K S^T / 64;  U = bT E;  O = (Q S^T + P U) / 64;  S^T += K^T U
+// (U = bT V - (bT K) S^T / 64 of the WY form, with the state correction applied before
+// the triangular factor, so no bT [K | V] product is needed.)
 //
 // Two warp-specialised roles share one CTA per (batch, head):
 //   * prep (8 warps) computes the state-independent work of chunk c+1 while
 //   * chain (4 warps) runs the recurrence of chunk c.
-// Prep: phasors (bf16) from bulk-copied inputs; G1 = [K; Q] K^T (tcgen05, M=128);
-// A and P from the Gram rows; T = (I + A)^-1 in fp32 (16 x 16 diagonal blocks by
-// right-looking substitution, two block-merge levels); G2 = bT [K | V] (M=64); W to
-// shared memory.  Chain: S^T -> bf16; G3 = W S^T and Q S^T (M=64); U; G4 S^T += K^T U
-// (M=128, accumulated in TMEM) and G5 Q S^T += P U (M=64); outputs.  Buffers the
-// chain reads are double-buffered; hand-off uses mbarriers (ready / free per slot).
+// Prep: phasors (bf16) from bulk-copied inputs; G1 = [K; Q] K^T (tcgen05, M=128); A and P
+// from the Gram rows; T = (I + A)^-1 in fp32 (16 x 16 diagonal blocks by right-looking
+// substitution, two block-merge levels on warp-level tf32 MMA); bT to shared memory.
+// Chain: S^T -> bf16; G3 = [K; Q] S^T (M=128); E; G U = bT E (M=64); G4 S^T += K^T U
+// (M=128, accumulated in TMEM) and G5: Q S^T += P U (M=128 with A starting 64 rows before
+// P, so the product lands in the Q rows of G3's accumulator); outputs.  Buffers the chain
+// reads are double-buffered; hand-off uses mbarriers (ready / free per slot).
 // Operand tiles use the SWIZZLE_NONE core-matrix layout (8 rows x 16 bytes), so one
 // buffer is a K-major or MN-major operand by swapping the two descriptor strides: K is
-// read as A and B of G1, B of G2 and A^T of G4 without copies.  M=64 accumulators put
+// read as A and B of G1, A of G3 and A^T of G4 without copies.  M=64 accumulators put
 // row m in TMEM lane (m % 16) + 32 (m / 16).  Every wait is bounded.
 #include "dp_common.cuh"
 #include "tc_ptx.cuh"
@@ -48,14 +50,14 @@ constexpr uint64_t kTimeoutNs = 2000000000ull;  // 2 s per wait
 constexpr int RG_KQ = 16 * 128;
 constexpr int RG_64 = 8 * 128;
 constexpr int KQ_BYTES = 16 * RG_KQ;                 // rows 0..63 K, rows 64..127 Q
-constexpr int W_BYTES = 8 * RG_KQ;
+constexpr int BT_BYTES = 8 * RG_64;                  // bT = diag(beta) (I + A)^-1, bf16
+constexpr int V_BYTES = 8 * RG_64;                   // V, then E = V - K S^T / 64 (chain)
 constexpr int P_BYTES = 8 * RG_64;
 constexpr int OFF_KQ = 0;                            // [2 slots]
-constexpr int OFF_W = OFF_KQ + 2 * KQ_BYTES;         // [2 slots]
-constexpr int OFF_P = OFF_W + 2 * W_BYTES;           // [2 slots]
-constexpr int OFF_V = OFF_P + 2 * P_BYTES;           // prep only
-constexpr int OFF_T = OFF_V + 8 * RG_64;             // bT bf16, prep only
-constexpr int OFF_U = OFF_T + 8 * RG_64;             // chain only
+constexpr int OFF_BT = OFF_KQ + 2 * KQ_BYTES;        // [2 slots]
+constexpr int OFF_VS = OFF_BT + 2 * BT_BYTES;        // [2 slots]
+constexpr int OFF_P = OFF_VS + 2 * V_BYTES;          // [2 slots]; 8 KB of shared memory precede it
+constexpr int OFF_U = OFF_P + 2 * P_BYTES;           // chain only
 constexpr int OFF_S0 = OFF_U + 8 * RG_64;            // S^T bf16 (128 x 64), chain only
 constexpr int OFF_STAGE = OFF_S0 + 16 * RG_64;       // raw theta_k, theta_q, v rows of a chunk
 constexpr int STAGE_BYTES = 3 * kC * 128;
@@ -71,11 +73,9 @@ constexpr int SMEM_BYTES = OFF_BAR + 128;
 // tensor-memory columns (fp32)
 constexpr uint32_t COL_S = 0;      // S^T, M = 128 (lane = feature)
 constexpr uint32_t COL_D1 = 64;    // [K;Q] K^T, M = 128 (prep)
-constexpr uint32_t COL_D2W = 128;  // bT K, M = 64 (prep)
-constexpr uint32_t COL_DU = 256;   // bT V, M = 64, 2 slots (prep writes, chain reads)
-constexpr uint32_t COL_DCA = 384;  // W S^T, M = 64 (chain)
-constexpr uint32_t COL_DCB = 448;  // Q S^T + P U, M = 64 (chain)
-constexpr uint32_t TMEM_COLS = 512;
+constexpr uint32_t COL_R3 = 128;   // [K;Q] S^T, M = 128; rows 64.. then += P U (chain)
+constexpr uint32_t COL_RU = 192;   // U = bT E, M = 64 (chain)
+constexpr uint32_t TMEM_COLS = 256;
 
 __device__ __forceinline__ uint32_t cm_off(int r, int k, int rg) {
   return (uint32_t)((r >> 3) * rg + (k >> 3) * 128 + (r & 7) * 16 + (k & 7) * 2);
@@ -184,8 +184,6 @@ __device__ bool prep_role(const TcArgs &a, uint8_t *smem, Bars *bars, uint32_t t
   const uint32_t lane_base = (uint32_t)(q * 32) << 16;
   const int L = a.L;
   uint8_t *stage = smem + OFF_STAGE;
-  uint8_t *vb = smem + OFF_V;
-  uint8_t *tb = smem + OFF_T;
   float *at = reinterpret_cast<float *>(smem + OFF_AT);
   float *tf = reinterpret_cast<float *>(smem + OFF_TF);
   float *zs = reinterpret_cast<float *>(smem + OFF_Z);
@@ -206,7 +204,8 @@ __device__ bool prep_role(const TcArgs &a, uint8_t *smem, Bars *bars, uint32_t t
   for (int c = 0; c < nchunks; ++c) {
     const int slot = c & 1, t0 = c * kC, nvalid = min(kC, L - t0);
     uint8_t *kq = smem + OFF_KQ + slot * KQ_BYTES;
-    uint8_t *wb = smem + OFF_W + slot * W_BYTES;
+    uint8_t *vb = smem + OFF_VS + slot * V_BYTES;
+    uint8_t *tb = smem + OFF_BT + slot * BT_BYTES;
     uint8_t *pb = smem + OFF_P + slot * P_BYTES;
     const float *bs = bs2 + slot * kC;
 
@@ -409,50 +408,7 @@ __device__ bool prep_role(const TcArgs &a, uint8_t *smem, Bars *bars, uint32_t t
                        pack_bf16(bi * x1.x, bi * x1.y), pack_bf16(bi * x1.z, bi * x1.w));
       }
     }
-    fence_proxy_async_smem();
-    group_sync(BAR_PREP, kPrepThreads);
-
-    // ---- P5: G2 = bT [K | V]  (M=64; N=128 -> D2W, N=64 -> DU[slot])
-    if (tid == 0) {
-      tc_fence_after();
-      const uint32_t sa = smem_u32(tb), sk = smem_u32(kq), sv = smem_u32(vb);
-#pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
-        const uint64_t ad = make_desc(sa + kk * 256, 128, RG_64);
-        mma_f16_ss(tmem + COL_D2W, ad, make_desc(sk + kk * 2 * RG_KQ, RG_KQ, 128),
-                   idesc_bf16(64, 128, false, true), kk > 0);
-        mma_f16_ss(tmem + COL_DU + 64 * slot, ad, make_desc(sv + kk * 2 * RG_64, RG_64, 128),
-                   idesc_bf16(64, 64, false, true), kk > 0);
-      }
-      mma_commit(&bars->prep_mma);
-    }
-    mma_pending = true;
-    if (tid == 0) ok = mbar_wait(&bars->prep_mma, pm_phase, kTimeoutNs);
-    if (group_any(!ok, BAR_PREP, kPrepThreads)) { ok = false; break; }
-    pm_phase ^= 1;
-    mma_pending = false;
-    tc_fence_after();
-
-    // ---- P6: W = bT K (M=64 rows in lanes < 16 of each quarter) -> bf16 tile
-    {
-      const int t = 16 * q + lane;
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        float w[16];
-        const int c0 = 64 * hf + 16 * u;
-        tmem_ld16(tmem + lane_base + COL_D2W + c0, w);
-        tmem_ld_wait();
-        if (lane < 16) {
-#pragma unroll
-          for (int half = 0; half < 2; ++half) {
-            const float *ww = w + 8 * half;
-            *reinterpret_cast<uint4 *>(wb + cm_off(t, c0 + 8 * half, RG_KQ)) =
-                make_uint4(pack_bf16(ww[0], ww[1]), pack_bf16(ww[2], ww[3]), pack_bf16(ww[4], ww[5]),
-                           pack_bf16(ww[6], ww[7]));
-          }
-        }
-      }
-    }
+    // bT, P, V and K, Q of this slot are ready for the chain
     fence_proxy_async_smem();
     tc_fence_before();
     group_sync(BAR_PREP, kPrepThreads);
@@ -498,7 +454,8 @@ __device__ bool chain_role(const TcArgs &a, uint8_t *smem, Bars *bars, uint32_t 
   for (int c = 0; c < nchunks; ++c) {
     const int slot = c & 1, t0 = c * kC, nvalid = min(kC, L - t0);
     uint8_t *kq = smem + OFF_KQ + slot * KQ_BYTES;
-    uint8_t *wb = smem + OFF_W + slot * W_BYTES;
+    uint8_t *tb = smem + OFF_BT + slot * BT_BYTES;
+    uint8_t *vs = smem + OFF_VS + slot * V_BYTES;
     uint8_t *pb = smem + OFF_P + slot * P_BYTES;
 
     if (ctid == 0) ok = mbar_wait(&bars->ready[slot], (uint32_t)((c >> 1) & 1), kTimeoutNs);
@@ -523,16 +480,14 @@ __device__ bool chain_role(const TcArgs &a, uint8_t *smem, Bars *bars, uint32_t 
     tc_fence_before();
     group_sync(BAR_CHAIN, kChainThreads);
 
-    // ---- C2: G3 = W S^T -> DCA and Q S^T -> DCB  (M=64, N=64, K=128)
+    // ---- C2: G3 = [K;Q] S^T -> R3  (M=128, N=64, K=128): rows 0..63 K S^T, 64.. Q S^T
     if (ctid == 0) {
       tc_fence_after();
-      const uint32_t sw = smem_u32(wb), sq = smem_u32(kq) + 8 * RG_KQ, ss = smem_u32(s0);
+      const uint32_t sa = smem_u32(kq), ss = smem_u32(s0);
 #pragma unroll
-      for (int kk = 0; kk < 8; ++kk) {
-        const uint64_t bd = make_desc(ss + kk * 2 * RG_64, RG_64, 128);
-        mma_f16_ss(tmem + COL_DCA, make_desc(sw + kk * 256, 128, RG_KQ), bd, idesc_bf16(64, 64, false, true), kk > 0);
-        mma_f16_ss(tmem + COL_DCB, make_desc(sq + kk * 256, 128, RG_KQ), bd, idesc_bf16(64, 64, false, true), kk > 0);
-      }
+      for (int kk = 0; kk < 8; ++kk)
+        mma_f16_ss(tmem + COL_R3, make_desc(sa + kk * 256, 128, RG_KQ), make_desc(ss + kk * 2 * RG_64, RG_64, 128),
+                   idesc_bf16(128, 64, false, true), kk > 0);
       mma_commit(&bars->chain_mma);
     }
     mma_pending = true;
@@ -542,24 +497,67 @@ __device__ bool chain_role(const TcArgs &a, uint8_t *smem, Bars *bars, uint32_t 
     mma_pending = false;
     tc_fence_after();
 
-    // ---- C3: U = bT V - W S^T / 64 -> bf16 (M=64 rows: lanes < 16 of each quarter)
+    // ---- C3: E = V - K S^T / 64 -> bf16 in place of V (row t = lane of chain warps 0, 1).
+    //      U = bT (V - K S^T / 64) = bT V - (bT K) S^T / 64: the state correction is applied
+    //      before the triangular factor, so the prep role needs no bT [K | V] product.
+    if (cw < 2) {
+      const int t = 32 * cw + lane;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        float ks[16];
+        tmem_ld16(tmem + lane_base + COL_R3 + 16 * u, ks);
+        tmem_ld_wait();
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          uint4 *vp = reinterpret_cast<uint4 *>(vs + cm_off(t, 16 * u + 8 * half, RG_64));
+          const uint4 vr = *vp;
+          const uint32_t vw[4] = {vr.x, vr.y, vr.z, vr.w};
+          uint32_t ew[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float2 vv = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&vw[i]));
+            ew[i] = pack_bf16(vv.x - ks[8 * half + 2 * i] * inv64, vv.y - ks[8 * half + 2 * i + 1] * inv64);
+          }
+          *vp = make_uint4(ew[0], ew[1], ew[2], ew[3]);
+        }
+      }
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    group_sync(BAR_CHAIN, kChainThreads);
+
+    // ---- C3u: U = bT E  (M=64, N=64, K=64) -> RU
+    if (ctid == 0) {
+      tc_fence_after();
+      const uint32_t sb = smem_u32(tb), se = smem_u32(vs);
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk)
+        mma_f16_ss(tmem + COL_RU, make_desc(sb + kk * 256, 128, RG_64), make_desc(se + kk * 2 * RG_64, RG_64, 128),
+                   idesc_bf16(64, 64, false, true), kk > 0);
+      mma_commit(&bars->chain_mma);
+    }
+    mma_pending = true;
+    if (ctid == 0) ok = mbar_wait(&bars->chain_mma, cm_phase, kTimeoutNs);
+    if (group_any(!ok, BAR_CHAIN, kChainThreads)) { ok = false; break; }
+    cm_phase ^= 1;
+    mma_pending = false;
+    tc_fence_after();
+
+    // ---- C3c: U -> bf16 operand tile (M=64 rows: lanes < 16 of each quarter)
     {
       const int t = 16 * cw + lane;
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
-        float ws[16], ut[16];
-        tmem_ld16(tmem + lane_base + COL_DCA + 16 * u, ws);
-        tmem_ld16(tmem + lane_base + COL_DU + 64 * slot + 16 * u, ut);
+        float uv[16];
+        tmem_ld16(tmem + lane_base + COL_RU + 16 * u, uv);
         tmem_ld_wait();
         if (lane < 16) {
 #pragma unroll
           for (int half = 0; half < 2; ++half) {
-            const int o = 8 * half;
-            *reinterpret_cast<uint4 *>(ub + cm_off(t, 16 * u + o, RG_64)) =
-                make_uint4(pack_bf16(ut[o] - ws[o] * inv64, ut[o + 1] - ws[o + 1] * inv64),
-                           pack_bf16(ut[o + 2] - ws[o + 2] * inv64, ut[o + 3] - ws[o + 3] * inv64),
-                           pack_bf16(ut[o + 4] - ws[o + 4] * inv64, ut[o + 5] - ws[o + 5] * inv64),
-                           pack_bf16(ut[o + 6] - ws[o + 6] * inv64, ut[o + 7] - ws[o + 7] * inv64));
+            const float *uu = uv + 8 * half;
+            *reinterpret_cast<uint4 *>(ub + cm_off(t, 16 * u + 8 * half, RG_64)) =
+                make_uint4(pack_bf16(uu[0], uu[1]), pack_bf16(uu[2], uu[3]), pack_bf16(uu[4], uu[5]),
+                           pack_bf16(uu[6], uu[7]));
           }
         }
       }
@@ -568,15 +566,17 @@ __device__ bool chain_role(const TcArgs &a, uint8_t *smem, Bars *bars, uint32_t 
     tc_fence_before();
     group_sync(BAR_CHAIN, kChainThreads);
 
-    // ---- C4: G4 S^T += K^T U (M=128) and G5 DCB += P U (M=64)
+    // ---- C4: G4 S^T += K^T U (M=128) and G5 R3 += [X; P] U (M=128, A starting 8 KB
+    //      before P: rows 64.. of R3 (Q S^T) gain P U; rows 0.. (K S^T, already used) are
+    //      don't-care)
     if (ctid == 0) {
       tc_fence_after();
-      const uint32_t sk = smem_u32(kq), su = smem_u32(ub), sp = smem_u32(pb);
+      const uint32_t sk = smem_u32(kq), su = smem_u32(ub), sp = smem_u32(pb) - 8 * RG_64;
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) {
         const uint64_t ud = make_desc(su + kk * 2 * RG_64, RG_64, 128);
         mma_f16_ss(tmem + COL_S, make_desc(sk + kk * 2 * RG_KQ, RG_KQ, 128), ud, idesc_bf16(128, 64, true, true), 1u);
-        mma_f16_ss(tmem + COL_DCB, make_desc(sp + kk * 256, 128, RG_64), ud, idesc_bf16(64, 64, false, true), 1u);
+        mma_f16_ss(tmem + COL_R3, make_desc(sp + kk * 256, 128, RG_64), ud, idesc_bf16(128, 64, false, true), 1u);
       }
       mma_commit(&bars->chain_mma);
     }
@@ -586,18 +586,18 @@ __device__ bool chain_role(const TcArgs &a, uint8_t *smem, Bars *bars, uint32_t 
     cm_phase ^= 1;
     mma_pending = false;
     tc_fence_after();
-    if (ctid == 0) mbar_arrive(&bars->free_[slot]);  // K, Q, W, P, bT V of this slot are consumed
+    if (ctid == 0) mbar_arrive(&bars->free_[slot]);  // K, Q, bT, E, P of this slot are consumed
 
-    // ---- C5: outputs O = DCB / 64 (M=64 rows: lanes < 16 of each quarter)
-    {
-      const int t = 16 * cw + lane;
+    // ---- C5: outputs O = R3 rows 64.. / 64 (row t = lane of chain warps 2, 3)
+    if (cw >= 2) {
+      const int t = 32 * (cw - 2) + lane;
       float *orow = a.out + b * a.s_out.b + h * a.s_out.h + (int64_t)(t0 + t) * a.s_out.t;
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         float o[16];
-        tmem_ld16(tmem + lane_base + COL_DCB + 16 * u, o);
+        tmem_ld16(tmem + lane_base + COL_R3 + 16 * u, o);
         tmem_ld_wait();
-        if (lane < 16 && t < nvalid) {
+        if (t < nvalid) {
 #pragma unroll
           for (int i = 0; i < 16; i += 4)
             *reinterpret_cast<float4 *>(orow + 16 * u + i) =
