@@ -17,8 +17,9 @@
 //   * chain (4 warps) runs the recurrence of chunk c.
 // Prep: phasors (bf16) from bulk-copied inputs; G1 = [K; Q] K^T (tcgen05, M=128); A and P
 // from the Gram rows; T = (I + A)^-1 in fp32 (16 x 16 diagonal blocks by right-looking
-// substitution, two block-merge levels on warp-level tf32 MMA); bT to shared memory.
-// Chain: S^T -> bf16; G3 = [K; Q] S^T (M=128); E; G U = bT E (M=64); G4 S^T += K^T U
+// substitution, two block-merge levels on warp-level tf32 MMA) into a per-slot buffer.
+// Chain: S^T -> bf16; G3 = [K; Q] S^T (M=128); E and bT = diag(beta) T in bf16 (two warps
+// each); U = bT E (M=64); G4 S^T += K^T U
 // (M=128, accumulated in TMEM) and G5: Q S^T += P U (M=128 with A starting 64 rows before
 // P, so the product lands in the Q rows of G3's accumulator); outputs.  Buffers the chain
 // reads are double-buffered; hand-off uses mbarriers (ready / free per slot).
@@ -63,12 +64,15 @@ constexpr int OFF_STAGE = OFF_S0 + 16 * RG_64;       // raw theta_k, theta_q, v 
 constexpr int STAGE_BYTES = 3 * kC * 128;
 constexpr int LDA = 68;                              // padded fp32 row stride
 constexpr int OFF_AT = OFF_STAGE + STAGE_BYTES;      // A^T fp32: At[k][i] = A[i][k]
-constexpr int OFF_TF = OFF_AT + kC * LDA * 4;        // T = (I + A)^-1 fp32
+constexpr int TF_FLOATS = kC * LDA;
+constexpr int OFF_TF = OFF_AT + kC * LDA * 4;        // T = (I + A)^-1 fp32, [2 slots] (chain forms bT)
 constexpr int LDZ = 36;
-constexpr int OFF_Z = OFF_TF + kC * LDA * 4;         // block-merge scratch fp32 (32 x LDZ)
+constexpr int OFF_Z = OFF_TF + 2 * TF_FLOATS * 4;    // block-merge scratch fp32 (32 x LDZ)
 constexpr int OFF_BETA = OFF_Z + 32 * LDZ * 4;       // beta, 2 chunk slots
-constexpr int OFF_BAR = OFF_BETA + 2 * kC * 4;
+constexpr int OFF_BSLOT = OFF_BETA + 2 * kC * 4;     // beta of the chunk in each slot (chain)
+constexpr int OFF_BAR = OFF_BSLOT + 2 * kC * 4;
 constexpr int SMEM_BYTES = OFF_BAR + 128;
+static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 
 // tensor-memory columns (fp32)
 constexpr uint32_t COL_S = 0;      // S^T, M = 128 (lane = feature)
@@ -185,7 +189,7 @@ __device__ bool prep_role(const TcArgs &a, uint8_t *smem, Bars *bars, uint32_t t
   const int L = a.L;
   uint8_t *stage = smem + OFF_STAGE;
   float *at = reinterpret_cast<float *>(smem + OFF_AT);
-  float *tf = reinterpret_cast<float *>(smem + OFF_TF);
+  float *tf0 = reinterpret_cast<float *>(smem + OFF_TF);
   float *zs = reinterpret_cast<float *>(smem + OFF_Z);
   float *bs2 = reinterpret_cast<float *>(smem + OFF_BETA);
   const float inv64 = 1.0f / 64.0f;
@@ -205,7 +209,7 @@ __device__ bool prep_role(const TcArgs &a, uint8_t *smem, Bars *bars, uint32_t t
     const int slot = c & 1, t0 = c * kC, nvalid = min(kC, L - t0);
     uint8_t *kq = smem + OFF_KQ + slot * KQ_BYTES;
     uint8_t *vb = smem + OFF_VS + slot * V_BYTES;
-    uint8_t *tb = smem + OFF_BT + slot * BT_BYTES;
+    float *tf = tf0 + slot * TF_FLOATS;
     uint8_t *pb = smem + OFF_P + slot * P_BYTES;
     const float *bs = bs2 + slot * kC;
 
@@ -394,21 +398,9 @@ __device__ bool prep_role(const TcArgs &a, uint8_t *smem, Bars *bars, uint32_t t
     }
     group_sync(BAR_PREP, kPrepThreads);
 
-    // ---- P4d: bT = diag(beta) T -> bf16 (row i = tid / 4, columns 16 (tid % 4) .. + 15)
-    {
-      const int i = tid >> 2, c0 = 16 * (tid & 3);
-      const float bi = bs[i];
-      const float *tr = tf + i * LDA + c0;
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        const float4 x0 = *reinterpret_cast<const float4 *>(tr + 8 * half);
-        const float4 x1 = *reinterpret_cast<const float4 *>(tr + 8 * half + 4);
-        *reinterpret_cast<uint4 *>(tb + cm_off(i, c0 + 8 * half, RG_64)) =
-            make_uint4(pack_bf16(bi * x0.x, bi * x0.y), pack_bf16(bi * x0.z, bi * x0.w),
-                       pack_bf16(bi * x1.x, bi * x1.y), pack_bf16(bi * x1.z, bi * x1.w));
-      }
-    }
-    // bT, P, V and K, Q of this slot are ready for the chain
+    // ---- P4d: beta of this chunk next to T for the chain, which forms bT = diag(beta) T
+    if (tid < kC) reinterpret_cast<float *>(smem + OFF_BSLOT)[slot * kC + tid] = bs[tid];
+    // T, beta, P, V and K, Q of this slot are ready for the chain
     fence_proxy_async_smem();
     tc_fence_before();
     group_sync(BAR_PREP, kPrepThreads);
@@ -457,6 +449,8 @@ __device__ bool chain_role(const TcArgs &a, uint8_t *smem, Bars *bars, uint32_t 
     uint8_t *tb = smem + OFF_BT + slot * BT_BYTES;
     uint8_t *vs = smem + OFF_VS + slot * V_BYTES;
     uint8_t *pb = smem + OFF_P + slot * P_BYTES;
+    const float *tfs = reinterpret_cast<const float *>(smem + OFF_TF) + slot * TF_FLOATS;
+    const float *bsl = reinterpret_cast<const float *>(smem + OFF_BSLOT) + slot * kC;
 
     if (ctid == 0) ok = mbar_wait(&bars->ready[slot], (uint32_t)((c >> 1) & 1), kTimeoutNs);
     if (group_any(!ok, BAR_CHAIN, kChainThreads)) { ok = false; break; }
@@ -520,6 +514,19 @@ __device__ bool chain_role(const TcArgs &a, uint8_t *smem, Bars *bars, uint32_t 
           }
           *vp = make_uint4(ew[0], ew[1], ew[2], ew[3]);
         }
+      }
+    } else {
+      // bT = diag(beta) T -> bf16 (row i = lane of chain warps 2, 3), beside E
+      const int i = 32 * (cw - 2) + lane;
+      const float bi = bsl[i];
+      const float *tr = tfs + i * LDA;
+#pragma unroll
+      for (int c8 = 0; c8 < 8; ++c8) {
+        const float4 x0 = *reinterpret_cast<const float4 *>(tr + 8 * c8);
+        const float4 x1 = *reinterpret_cast<const float4 *>(tr + 8 * c8 + 4);
+        *reinterpret_cast<uint4 *>(tb + cm_off(i, 8 * c8, RG_64)) =
+            make_uint4(pack_bf16(bi * x0.x, bi * x0.y), pack_bf16(bi * x0.z, bi * x0.w),
+                       pack_bf16(bi * x1.x, bi * x1.y), pack_bf16(bi * x1.z, bi * x1.w));
       }
     }
     fence_proxy_async_smem();
@@ -586,7 +593,7 @@ __device__ bool chain_role(const TcArgs &a, uint8_t *smem, Bars *bars, uint32_t 
     cm_phase ^= 1;
     mma_pending = false;
     tc_fence_after();
-    if (ctid == 0) mbar_arrive(&bars->free_[slot]);  // K, Q, bT, E, P of this slot are consumed
+    if (ctid == 0) mbar_arrive(&bars->free_[slot]);  // K, Q, T, beta, E, P of this slot are consumed
 
     // ---- C5: outputs O = R3 rows 64.. / 64 (row t = lane of chain warps 2, 3)
     if (cw >= 2) {
@@ -651,8 +658,8 @@ __global__ void __launch_bounds__(kThreads, 1) core_tc_kernel(TcArgs a) {
     tmem_alloc(tmem_slot, TMEM_COLS);
     tmem_relinquish();
   }
-  // T's strictly upper blocks are never written: zero them once
-  for (int i = tid; i < kC * LDA; i += kThreads) tf[i] = 0.f;
+  // T's strictly upper blocks are never written: zero them once (both slots)
+  for (int i = tid; i < 2 * TF_FLOATS; i += kThreads) tf[i] = 0.f;
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
