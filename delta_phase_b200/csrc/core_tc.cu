@@ -17,9 +17,10 @@
 //   * chain (4 warps) runs the recurrence of chunk c.
 // Prep: phasors (bf16) from bulk-copied inputs; G1 = [K; Q] K^T (tcgen05, M=128); A and P
 // from the Gram rows; T = (I + A)^-1 in fp32 (16 x 16 diagonal blocks by right-looking
-// substitution, two block-merge levels on warp-level tf32 MMA) into a per-slot buffer.
-// Chain: S^T -> bf16; G3 = [K; Q] S^T (M=128); E and bT = diag(beta) T in bf16 (two warps
-// each); U = bT E (M=64); G4 S^T += K^T U
+// substitution, the 16 -> 32 block merge on warp-level tf32 MMA) into a per-slot buffer.
+// Chain: S^T -> bf16; G3 = [K; Q] S^T (M=128) and, while it runs, the 32 -> 64 merge of
+// the inverse; E and bT = diag(beta) T in bf16 (two warps each); U = bT E (M=64);
+// G4 S^T += K^T U
 // (M=128, accumulated in TMEM) and G5: Q S^T += P U (M=128 with A starting 64 rows before
 // P, so the product lands in the Q rows of G3's accumulator); outputs.  Buffers the chain
 // reads are double-buffered; hand-off uses mbarriers (ready / free per slot).
@@ -70,7 +71,10 @@ constexpr int LDZ = 36;
 constexpr int OFF_Z = OFF_TF + 2 * TF_FLOATS * 4;    // block-merge scratch fp32 (32 x LDZ)
 constexpr int OFF_BETA = OFF_Z + 32 * LDZ * 4;       // beta, 2 chunk slots
 constexpr int OFF_BSLOT = OFF_BETA + 2 * kC * 4;     // beta of the chunk in each slot (chain)
-constexpr int OFF_BAR = OFF_BSLOT + 2 * kC * 4;
+constexpr int LDA10 = 36;
+constexpr int A10_FLOATS = 32 * LDA10;
+constexpr int OFF_A10 = OFF_BSLOT + 2 * kC * 4;       // A block (rows 32.., cols ..32) for the chain's merge [2]
+constexpr int OFF_BAR = OFF_A10 + 2 * A10_FLOATS * 4;
 constexpr int SMEM_BYTES = OFF_BAR + 128;
 static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 
@@ -345,6 +349,15 @@ __device__ bool prep_role(const TcArgs &a, uint8_t *smem, Bars *bars, uint32_t t
 
     // ---- P4a: 16 x 16 diagonal blocks of (I + A)^-1, right-looking substitution with
     //      the column in registers (threads 0..63: block tid / 16, column tid % 16)
+    if (tid >= 64) {
+      // beside the diagonal solves: the block of A^T the chain's 32 -> 64 merge reads,
+      // a10[k][i] = At[k][32 + i] (k, i < 32), to this slot's buffer
+      float *a10 = reinterpret_cast<float *>(smem + OFF_A10) + slot * A10_FLOATS;
+      for (int e = tid - 64; e < 32 * 8; e += kPrepThreads - 64) {
+        const int k = e >> 3, i4 = 4 * (e & 7);
+        *reinterpret_cast<float4 *>(a10 + k * LDA10 + i4) = *reinterpret_cast<const float4 *>(at + k * LDA + 32 + i4);
+      }
+    }
     if (tid < 64) {
       const int o = 16 * (tid >> 4), col = tid & 15;
       float cl[16];
@@ -378,23 +391,6 @@ __device__ bool prep_role(const TcArgs &a, uint8_t *smem, Bars *bars, uint32_t t
       __syncwarp();
       warp_gemm16<16>(d0, d1, tf + (o + 16) * LDA + o + 16, LDA, 1, zs + 16 * warp * LDZ, LDZ, 1, lane);
       warp_store16(tf + (o + 16) * LDA + o, LDA, d0, d1, -1.f, lane);
-    }
-    group_sync(BAR_PREP, kPrepThreads);
-
-    // ---- P4c: 32 -> 64 merge on warps 0..3 (tf32 mma, one 16 x 16 tile each):
-    //      Y = A[32+i][k] T[k][j] (k < 32), then T[32+i][j] = -T11 Y
-    if (warp < 4) {
-      const int mi = 16 * (warp >> 1), nj = 16 * (warp & 1);
-      float d0[4], d1[4];
-      warp_gemm16<32>(d0, d1, at + 32 + mi, 1, LDA, tf + nj, LDA, 1, lane);
-      warp_store16(zs + mi * LDZ + nj, LDZ, d0, d1, 1.f, lane);
-    }
-    group_sync(BAR_PREP, kPrepThreads);
-    if (warp < 4) {
-      const int mi = 16 * (warp >> 1), nj = 16 * (warp & 1);
-      float d0[4], d1[4];
-      warp_gemm16<32>(d0, d1, tf + (32 + mi) * LDA + 32, LDA, 1, zs + nj, LDZ, 1, lane);
-      warp_store16(tf + (32 + mi) * LDA + nj, LDA, d0, d1, -1.f, lane);
     }
     group_sync(BAR_PREP, kPrepThreads);
 
@@ -449,7 +445,8 @@ __device__ bool chain_role(const TcArgs &a, uint8_t *smem, Bars *bars, uint32_t 
     uint8_t *tb = smem + OFF_BT + slot * BT_BYTES;
     uint8_t *vs = smem + OFF_VS + slot * V_BYTES;
     uint8_t *pb = smem + OFF_P + slot * P_BYTES;
-    const float *tfs = reinterpret_cast<const float *>(smem + OFF_TF) + slot * TF_FLOATS;
+    float *tfs = reinterpret_cast<float *>(smem + OFF_TF) + slot * TF_FLOATS;
+    const float *a10 = reinterpret_cast<const float *>(smem + OFF_A10) + slot * A10_FLOATS;
     const float *bsl = reinterpret_cast<const float *>(smem + OFF_BSLOT) + slot * kC;
 
     if (ctid == 0) ok = mbar_wait(&bars->ready[slot], (uint32_t)((c >> 1) & 1), kTimeoutNs);
@@ -485,6 +482,18 @@ __device__ bool chain_role(const TcArgs &a, uint8_t *smem, Bars *bars, uint32_t 
       mma_commit(&bars->chain_mma);
     }
     mma_pending = true;
+    // ---- C2m: while G3 runs, the last level of the inverse: T[32+i][j] = -T11 (A10 T00)
+    //      (tf32 mma, one 16 x 16 tile per warp; the U tile is the scratch)
+    {
+      float *zc = reinterpret_cast<float *>(ub);
+      const int mi = 16 * (cw >> 1), nj = 16 * (cw & 1);
+      float d0[4], d1[4];
+      warp_gemm16<32>(d0, d1, a10 + mi, 1, LDA10, tfs + nj, LDA, 1, lane);
+      warp_store16(zc + mi * LDZ + nj, LDZ, d0, d1, 1.f, lane);
+      group_sync(BAR_CHAIN, kChainThreads);
+      warp_gemm16<32>(d0, d1, tfs + (32 + mi) * LDA + 32, LDA, 1, zc + nj, LDZ, 1, lane);
+      warp_store16(tfs + (32 + mi) * LDA + nj, LDA, d0, d1, -1.f, lane);
+    }
     if (ctid == 0) ok = mbar_wait(&bars->chain_mma, cm_phase, kTimeoutNs);
     if (group_any(!ok, BAR_CHAIN, kChainThreads)) { ok = false; break; }
     cm_phase ^= 1;
