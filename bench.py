@@ -6,7 +6,7 @@ each GPU (batch x head sharding, weak scaling: global batch = 8 x n_gpus; no
 collective on the data path).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload core|decode|laplace|ffn]
+                    [--workload core|cbeta|decode|laplace|laplace-sp|ffn|lm]
 
 Multi-GPU: launch with torch.distributed.run (one process per GPU); rank 0 prints one
 JSON line.  ``--impl reference`` times the reference algorithm's CPU restatement
@@ -321,6 +321,71 @@ def _line(metric, value, unit, args, world, ms, config, **extra):
     return d
 
 
+def cpu_cbeta_sample(units=2, L=512, D=64, seed=0):
+    """Time the numpy float32 port of the reference's complex-beta token loop
+    (oracle.core.complex_beta_recurrent) on `units` (b, h) units of L tokens."""
+    from oracle import core as ocore
+    rng = np.random.default_rng(seed)
+    tk = rng.uniform(0, 2 * np.pi, (1, units, L, D)).astype(np.float32)
+    tq = rng.uniform(0, 2 * np.pi, (1, units, L, D)).astype(np.float32)
+    v = rng.standard_normal((1, units, L, D)).astype(np.float32)
+    phi = rng.standard_normal((1, units, L)).astype(np.float32)
+    t0 = time.perf_counter()
+    ocore.complex_beta_recurrent(tk, tq, v, phi, None, dtype=np.float32)
+    return time.perf_counter() - t0, units * L
+
+
+def run_cbeta(args, world, rank, local):
+    """Complex-beta (Householder) rule of ComplexBetaDeltaPhaseBlock at the core's
+    shape: B=8, H=16, L=8192, d_k=64, bf16 inputs, phi ~ N(0, 1) (beta = 1 + e^{i phi})."""
+    import torch
+    from delta_phase_b200.kernels import chunkwise_forward
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    B, H, L, D = (CORE[k] for k in ("B", "H", "L", "D"))
+    tk, tq, v, _ = make_core_inputs(dev, 3000 + rank, B, H, L, D)
+    g = torch.Generator(device=dev).manual_seed(4000 + rank)
+    phi = torch.randn(B, H, L, device=dev, generator=g).to(torch.bfloat16)
+    out = torch.empty(B, H, L, D, device=dev, dtype=torch.float32)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        chunkwise_forward(tk, tq, v, phi, 64, None, out=out, complex_beta=True)
+
+    barrier(world)
+    clocks = ClockSampler(local)
+    clocks.start()
+    ms = _timed(step, args.steps, args.warmup, stream)
+    clk = clocks.stop()
+    ms_max = max_over_ranks(ms, world)
+    peaks, src = load_peaks()
+    alg_bytes = core_algorithmic_bytes(B, H, L, D, D)
+    achieved = alg_bytes / (ms / 1e3) / 1e9
+    line = _line("complex-beta delta-core tokens/s (H=16,d_k=64,L=8K)", world * B * L / (ms_max / 1e3),
+                 "tokens/s", args, world, ms_max,
+                 {"workload": "ComplexBetaDeltaPhaseBlock core (beta = 1 + e^{i phi}), chunkwise on fp16 "
+                              "operand tiles, B=8,H=16,L=8192,d_k=64 per GPU, bf16 in / fp32 out",
+                  "global_batch": B * world, "seq_len": L, "heads": H, "d_k": D,
+                  "parallelism": f"batch x head sharding over {world} GPU(s), no collective",
+                  "l2": f"inputs+outputs {alg_bytes / 1e6:.0f} MB per step > 126 MB L2; no flush"},
+                 roofline={"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                           "frac": achieved / peaks["hbm_gbs"], "traffic": None,
+                           "algorithmic_bytes_per_launch": alg_bytes, "peak_source": src,
+                           "kernel": "dp_core_cbeta_fwd (one launch per step)"},
+                 gpu_launches=args.steps, clocks=clk)
+    line["data"] = "synthetic (seeded: theta~U[0,2pi), v~N(0,1), phi~N(0,1))"
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        parts = []
+        _, reps = repeat_for(lambda i: parts.append(cpu_cbeta_sample(seed=i)))
+        secs, ht = sum(p[0] for p in parts), sum(p[1] for p in parts)
+        line["cpu_baseline"] = {
+            "value": ht / H / secs, "unit": "tokens/s", "cores": cpu_threads(), "kind": "port",
+            "sample": f"{reps} x 2 (b,h) units x 512 tokens, numpy float32 port of the reference's "
+                      f"complex-beta token loop (oracle.core.complex_beta_recurrent), {secs:.1f} s; "
+                      "tokens/s = head-tokens / 16 / s"}
+    return line
+
+
 def run_laplace(args, world, rank, local):
     """LaplacePhaseCore chunk solve at B=4, H=16, L=32768, d_k=64 (gated decay:
     log r = -softplus(N(0,1)), unit phasors, bf16 inputs)."""
@@ -569,7 +634,8 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="core", choices=["core", "laplace", "laplace-sp", "ffn", "decode", "lm"])
+    ap.add_argument("--workload", default="core",
+                    choices=["core", "cbeta", "laplace", "laplace-sp", "ffn", "decode", "lm"])
     ap.add_argument("--decode-steps", type=int, default=256)
     ap.add_argument("--seq-len", type=int, default=32768,
                     help="laplace workload only: sequence length (the headline is 32768; smaller for profiling)")
@@ -586,8 +652,8 @@ def main():
             print(json.dumps(line), flush=True)
         return
     world, rank, local = dist_setup(args.gpus)
-    run = {"core": run_core, "laplace": run_laplace, "laplace-sp": run_laplace_sp, "ffn": run_ffn, "decode": run_decode,
-           "lm": run_lm}[args.workload]
+    run = {"core": run_core, "cbeta": run_cbeta, "laplace": run_laplace, "laplace-sp": run_laplace_sp,
+           "ffn": run_ffn, "decode": run_decode, "lm": run_lm}[args.workload]
     line = run(args, world, rank, local)
     if rank == 0:
         print(json.dumps(line), flush=True)

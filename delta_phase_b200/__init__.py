@@ -16,6 +16,7 @@ from .kernels import (
     triton_available,
 )
 from .layers import (
+    ComplexBetaDeltaPhaseBlock,
     DeltaPhaseHolographicBlock,
     LaplacePhaseCore,
     LearnableSubstrateLerpFFN,
@@ -31,6 +32,7 @@ __all__ = [
     "DeltaPhaseModel",
     "DecodeGraph",
     "DeltaPhaseHolographicBlock",
+    "ComplexBetaDeltaPhaseBlock",
     "LearnableSubstrateLerpFFN",
     "ShortCausalConv1D",
     "LaplacePhaseCore",

@@ -28,6 +28,8 @@ _SIG = {
     "dp_device_error": (_I, [_I]),
     "dp_core_fwd": (_I, [_P, _P, _P, _P, _I, _I, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I64P, _P]),
     "dp_core_decode": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _P, _I, _I, _I, _I, _I64P, _P]),
+    "dp_core_cbeta_fwd": (_I, [_P, _P, _P, _P, _I, _I, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I64P, _P]),
+    "dp_core_cbeta_decode": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _P, _I, _I, _I, _I, _I64P, _P]),
     "dp_gram": (_I, [_P, _P, _I, _I, _P, _I, _I, _I, _P]),
     "dp_phasor": (_I, [_P, _I, ctypes.c_int64, _P, _P]),
     "dp_laplace_fwd": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _P, _P, _P, _I, _I, _I, _I, _I,
@@ -148,9 +150,10 @@ def seq_strides(t: torch.Tensor):
     return t.stride(0), t.stride(1), t.stride(2)
 
 
-def core_fwd(theta_k, theta_q, v, beta, chunk_size, state_in, out, state_out):
+def core_fwd(theta_k, theta_q, v, beta, chunk_size, state_in, out, state_out, complex_beta=False):
     """dp_core_fwd on (B,H,L,D) views.  state_in/state_out are float32 views of the
-    interleaved complex64 state (B,H,Dv,D,2), contiguous."""
+    interleaved complex64 state (B,H,Dv,D,2), contiguous.  complex_beta: ``beta`` holds
+    phi of beta = 1 + e^{i phi} (dp_core_cbeta_fwd)."""
     dev = require_cuda(theta_k, theta_q, v, beta, state_in, out, state_out)
     B, H, L, D = theta_k.shape
     Dv = v.shape[-1]
@@ -160,15 +163,17 @@ def core_fwd(theta_k, theta_q, v, beta, chunk_size, state_in, out, state_out):
     st += (beta.stride(0), beta.stride(1), beta.stride(2))
     st += seq_strides(out)
     arr = strides_array(st)
+    name = "dp_core_cbeta_fwd" if complex_beta else "dp_core_fwd"
     with torch.cuda.device(dev):
-        rc = lib().dp_core_fwd(ptr(theta_k), ptr(theta_q), ptr(v), ptr(beta), dtype_code(theta_k),
-                               dtype_code(beta), ptr(state_in), ptr(out), ptr(state_out), B, H, L, D,
-                               Dv, int(chunk_size), arr, stream_of(dev))
-    _check("dp_core_fwd", rc)
+        rc = getattr(lib(), name)(ptr(theta_k), ptr(theta_q), ptr(v), ptr(beta), dtype_code(theta_k),
+                                  dtype_code(beta), ptr(state_in), ptr(out), ptr(state_out), B, H, L, D,
+                                  Dv, int(chunk_size), arr, stream_of(dev))
+    _check(name, rc)
 
 
-def core_decode(state_in, state_out, theta_k, theta_q, v, beta, out):
-    """dp_core_decode; theta_k/theta_q (B,H,D), v (B,H,Dv), beta (B,H), out (B,H,Dv)."""
+def core_decode(state_in, state_out, theta_k, theta_q, v, beta, out, complex_beta=False):
+    """dp_core_decode; theta_k/theta_q (B,H,D), v (B,H,Dv), beta (B,H), out (B,H,Dv).
+    complex_beta: ``beta`` holds phi of beta = 1 + e^{i phi} (dp_core_cbeta_decode)."""
     dev = require_cuda(state_in, state_out, theta_k, theta_q, v, beta, out)
     B, H, D = theta_k.shape
     Dv = v.shape[-1]
@@ -178,11 +183,12 @@ def core_decode(state_in, state_out, theta_k, theta_q, v, beta, out):
     st = []
     for t in (theta_k, theta_q, v, beta, out):
         st += (t.stride(0), t.stride(1))
+    name = "dp_core_cbeta_decode" if complex_beta else "dp_core_decode"
     with torch.cuda.device(dev):
-        rc = lib().dp_core_decode(ptr(state_in), ptr(state_out), ptr(theta_k), ptr(theta_q), ptr(v),
+        rc = getattr(lib(), name)(ptr(state_in), ptr(state_out), ptr(theta_k), ptr(theta_q), ptr(v),
                                   ptr(beta), dtype_code(theta_k), dtype_code(beta), ptr(out), B, H, D,
                                   Dv, strides_array(st), stream_of(dev))
-    _check("dp_core_decode", rc)
+    _check(name, rc)
 
 
 def gram(theta, beta, out):

@@ -62,6 +62,7 @@ const char *dp_status_string(int status) {
     case DP_ERR_CUDA: return "CUDA error";
     case DP_ERR_TIMEOUT: return "device-side wait timed out";
     case DP_ERR_WORKSPACE: return "workspace too small";
+    case DP_ERR_RANGE: return "value outside the range of 16-bit operand tiles";
     default: return "unknown status";
   }
 }

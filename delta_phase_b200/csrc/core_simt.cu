@@ -20,6 +20,13 @@
 // One CTA per (batch, head); the state lives in shared memory for the whole
 // sequence.  This kernel covers every shape (D, Dv <= 128, any L); the tensor-core
 // kernel in core_tc.cu covers the (D = Dv = 64) production shape.
+//
+// Complex beta (ComplexBetaDeltaPhaseBlock, delta_phase/layers.py:294-418; beta_t =
+// 1 + e^{i phi_t}, update M += beta (v - Re(M conj k) / D) k^T): in the real form the
+// update writes along w_t = beta_t k_t = (br c - bi s, br s + bi c) per channel while
+// the read stays along kap_t, so S_t = S_{t-1} + (v_t - S_{t-1} kap_t / D) w_t^T and
+//   A = strict_lower(K W^T / D),  T = (I + A)^-1,  U = T (V - K S^T / D)
+//   O = Q S^T / D + tril(Q W^T / D) U,  S += U^T W.
 #include "dp_common.cuh"
 
 namespace dp {
@@ -34,12 +41,13 @@ __device__ __forceinline__ float load_beta(const void *p, int dt, int64_t i) {
 }
 
 template <int CI>
-__host__ __device__ inline size_t core_simt_smem_floats(int D, int Dv) {
+__host__ __device__ inline size_t core_simt_smem_floats(int D, int Dv, bool cbeta) {
   const int ks = 2 * D + 1;
-  return (size_t)Dv * ks + 2 * (size_t)CI * ks + 3 * (size_t)CI * Dv + 3 * CI * CI + CI;
+  return (size_t)Dv * ks + (cbeta ? 3 : 2) * (size_t)CI * ks + 3 * (size_t)CI * Dv + 3 * CI * CI + CI;
 }
 
-template <typename T, int CI>
+// CB: `beta` holds phi of the complex beta 1 + e^{i phi}.
+template <typename T, int CI, bool CB>
 __global__ void __launch_bounds__(kThreads)
 core_fwd_simt_kernel(const T *__restrict__ tk, const T *__restrict__ tq, const T *__restrict__ v,
                      const void *__restrict__ beta, int beta_dt, const float *state_in,
@@ -57,7 +65,8 @@ core_fwd_simt_kernel(const T *__restrict__ tk, const T *__restrict__ tq, const T
   float *A = Oi + CI * Dv;      // CI x CI     beta-scaled strictly-lower Gram
   float *Tm = A + CI * CI;      // CI x CI     (I + A)^-1
   float *P = Tm + CI * CI;      // CI x CI     tril(Q K^T) / D
-  float *bb = P + CI * CI;      // CI
+  float *bb = P + CI * CI;      // CI          beta (CB: phi)
+  float *wk = bb + CI;          // CI x ks     CB: write keys beta k
 
   const int tid = threadIdx.x;
   const int bh = blockIdx.x;
@@ -96,19 +105,31 @@ core_fwd_simt_kernel(const T *__restrict__ tk, const T *__restrict__ tq, const T
     for (int t = tid; t < CI; t += kThreads)
       bb[t] = (t0 + t < L) ? load_beta(beta, beta_dt, b_bh + (int64_t)(t0 + t) * s_b.t) : 0.f;
     __syncthreads();
+    if (CB) {
+      for (int idx = tid; idx < CI * D; idx += kThreads) {
+        const int t = idx / D, c = idx % D;
+        float sp, cp;
+        sincosf(bb[t], &sp, &cp);
+        const float br = 1.f + cp, c0 = kap[t * ks + 2 * c], s0 = kap[t * ks + 2 * c + 1];
+        wk[t * ks + 2 * c] = fmaf(br, c0, -sp * s0);
+        wk[t * ks + 2 * c + 1] = fmaf(br, s0, sp * c0);
+      }
+      __syncthreads();
+    }
+    const float *wsrc = CB ? wk : kap;  // write keys
 
     // 2. Gram (A), intra-chunk query-key products (P), state reads (R, Oi)
     for (int idx = tid; idx < CI * CI; idx += kThreads) {
       const int t = idx / CI, s = idx % CI;
       float g = 0.f, p = 0.f;
       if (s <= t) {
-        const float *kt = kap + t * ks, *ks_ = kap + s * ks, *qt = xi + t * ks;
+        const float *kt = kap + t * ks, *ks_ = wsrc + s * ks, *qt = xi + t * ks;
         for (int j = 0; j < D2; ++j) {
           g = fmaf(kt[j], ks_[j], g);
           p = fmaf(qt[j], ks_[j], p);
         }
       }
-      A[idx] = (s < t) ? bb[s] * g * inv_d : 0.f;
+      A[idx] = (s < t) ? (CB ? 1.f : bb[s]) * g * inv_d : 0.f;
       P[idx] = (s <= t) ? p * inv_d : 0.f;
     }
     for (int idx = tid; idx < CI * Dv; idx += kThreads) {
@@ -145,7 +166,7 @@ core_fwd_simt_kernel(const T *__restrict__ tk, const T *__restrict__ tq, const T
       const int t = idx / Dv, o = idx % Dv;
       float acc = 0.f;
       for (int s = 0; s <= t; ++s) acc = fmaf(Tm[t * CI + s], R[s * Dv + o], acc);
-      U[idx] = bb[t] * acc;
+      U[idx] = CB ? acc : bb[t] * acc;
     }
     __syncthreads();
 
@@ -162,7 +183,7 @@ core_fwd_simt_kernel(const T *__restrict__ tk, const T *__restrict__ tq, const T
       const int o = idx / D2, j = idx % D2;
       float acc = 0.f;
 #pragma unroll 4
-      for (int t = 0; t < CI; ++t) acc = fmaf(U[t * Dv + o], kap[t * ks + j], acc);
+      for (int t = 0; t < CI; ++t) acc = fmaf(U[t * Dv + o], wsrc[t * ks + j], acc);
       S[o * ks + j] += acc;
     }
   }
@@ -202,11 +223,11 @@ gram_kernel(const T *__restrict__ theta, const void *__restrict__ beta, int beta
 template <int CI>
 int launch_core_simt(const void *tk, const void *tq, const void *v, const void *beta, int in_dt,
                      int beta_dt, const float *state_in, float *out, float *state_out, int B,
-                     int H, int L, int D, int Dv, const SeqStrides *s, cudaStream_t stream) {
-  const size_t smem = core_simt_smem_floats<CI>(D, Dv) * sizeof(float);
+                     int H, int L, int D, int Dv, const SeqStrides *s, cudaStream_t stream, bool cbeta) {
+  const size_t smem = core_simt_smem_floats<CI>(D, Dv, cbeta) * sizeof(float);
   return dispatch_dtype(in_dt, [&](auto tag) -> int {
     using T = decltype(tag);
-    auto kern = core_fwd_simt_kernel<T, CI>;
+    auto kern = cbeta ? core_fwd_simt_kernel<T, CI, true> : core_fwd_simt_kernel<T, CI, false>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return set_error(DP_ERR_CUDA, std::string("core_fwd_simt smem attr: ") + cudaGetErrorString(e));
     kern<<<B * H, kThreads, smem, stream>>>(static_cast<const T *>(tk), static_cast<const T *>(tq),
@@ -218,15 +239,17 @@ int launch_core_simt(const void *tk, const void *tq, const void *v, const void *
 
 }  // namespace
 
-// Entry used by dp_core_fwd for shapes the tensor-core kernel does not cover.
+// Entry used by dp_core_fwd / dp_core_cbeta_fwd for shapes the tensor-core kernel does not cover.
 int core_fwd_simt(const void *tk, const void *tq, const void *v, const void *beta, int in_dt,
                   int beta_dt, const float *state_in, float *out, float *state_out, int B, int H,
-                  int L, int D, int Dv, const SeqStrides *s, cudaStream_t stream) {
-  const size_t limit = 200 * 1024;
-  if (core_simt_smem_floats<32>(D, Dv) * sizeof(float) <= limit)
-    return launch_core_simt<32>(tk, tq, v, beta, in_dt, beta_dt, state_in, out, state_out, B, H, L, D, Dv, s, stream);
-  if (core_simt_smem_floats<16>(D, Dv) * sizeof(float) <= limit)
-    return launch_core_simt<16>(tk, tq, v, beta, in_dt, beta_dt, state_in, out, state_out, B, H, L, D, Dv, s, stream);
+                  int L, int D, int Dv, const SeqStrides *s, cudaStream_t stream, bool cbeta) {
+  const size_t limit = 227 * 1024;
+  if (core_simt_smem_floats<32>(D, Dv, cbeta) * sizeof(float) <= limit)
+    return launch_core_simt<32>(tk, tq, v, beta, in_dt, beta_dt, state_in, out, state_out, B, H, L, D, Dv, s, stream,
+                                cbeta);
+  if (core_simt_smem_floats<16>(D, Dv, cbeta) * sizeof(float) <= limit)
+    return launch_core_simt<16>(tk, tq, v, beta, in_dt, beta_dt, state_in, out, state_out, B, H, L, D, Dv, s, stream,
+                                cbeta);
   return set_error(DP_ERR_UNSUPPORTED, "core_fwd: D/Dv too large for shared memory");
 }
 

@@ -70,13 +70,17 @@ constexpr int OFF_TF = OFF_AT + kC * LDA * 4;        // T = (I + A)^-1 fp32, [2 
 constexpr int LDZ = 36;
 constexpr int OFF_Z = OFF_TF + 2 * TF_FLOATS * 4;    // block-merge scratch fp32 (32 x LDZ)
 constexpr int OFF_BETA = OFF_Z + 32 * LDZ * 4;       // beta, 2 chunk slots
-constexpr int OFF_BSLOT = OFF_BETA + 2 * kC * 4;     // beta of the chunk in each slot (chain)
+constexpr int OFF_BSLOT = OFF_BETA + 2 * kC * 4;     // beta (complex beta: Re) of each slot's chunk (chain)
+constexpr int OFF_BIM = OFF_BSLOT + 2 * kC * 4;      // complex beta: Im(beta) of each slot's chunk (chain)
 constexpr int LDA10 = 36;
 constexpr int A10_FLOATS = 32 * LDA10;
-constexpr int OFF_A10 = OFF_BSLOT + 2 * kC * 4;       // A block (rows 32.., cols ..32) for the chain's merge [2]
+constexpr int OFF_A10 = OFF_BIM + 2 * kC * 4;         // A block (rows 32.., cols ..32) for the chain's merge [2]
 constexpr int OFF_BAR = OFF_A10 + 2 * A10_FLOATS * 4;
 constexpr int SMEM_BYTES = OFF_BAR + 128;
 static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
+// complex beta: the write-key tile W (64 x 128 bf16, RG_KQ row groups) lives in the A^T
+// buffer for the prep role's Gram MMA and in the S^T operand buffer for the chain's update
+static_assert(KQ_BYTES / 2 <= kC * LDA * 4 && KQ_BYTES / 2 <= 16 * RG_64, "W tile fits its aliases");
 
 // tensor-memory columns (fp32)
 constexpr uint32_t COL_S = 0;      // S^T, M = 128 (lane = feature)
@@ -92,6 +96,42 @@ __device__ __forceinline__ uint32_t cm_off(int r, int k, int rg) {
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
   __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
   return *reinterpret_cast<uint32_t *>(&h);
+}
+
+// Operand tiles: bf16 for the real-beta rule; fp16 (F16) for the complex-beta rule, whose
+// update is isometric, so the per-chunk rounding of the tiles is not damped and adds up
+// along the sequence like a random walk (bf16 tiles: 1.3e-2 relative L2 after 1000
+// tokens; fp16 tiles: 1.6e-3).  fp16 operands are kept in range by scaling S and P by
+// 1 / 64 (exact); values past 65504 set `over`, reported as DP_ERR_RANGE.
+template <bool F16>
+__device__ __forceinline__ uint32_t pack_op(float a, float b) {
+  if (F16) {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t *>(&h);
+  }
+  return pack_bf16(a, b);
+}
+template <bool F16>
+__device__ __forceinline__ uint32_t pack_chk(float a, float b, bool &over) {
+  if (F16) over |= !(fabsf(a) <= 65504.f) || !(fabsf(b) <= 65504.f);
+  return pack_op<F16>(a, b);
+}
+template <bool F16>
+__device__ __forceinline__ float2 unpack_op(uint32_t w) {
+  if (F16) return __half22float2(*reinterpret_cast<const __half2 *>(&w));
+  return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&w));
+}
+template <bool F16>
+__host__ __device__ constexpr uint32_t idesc_op(int M, int N, bool a_mn_major, bool b_mn_major) {
+  return F16 ? idesc_f16(M, N, a_mn_major, b_mn_major) : idesc_bf16(M, N, a_mn_major, b_mn_major);
+}
+
+// Complex beta: one (cos, sin) pair of a key phasor (fp16x2) times beta = br + i bi, i.e.
+// the write key (br c - bi s, br s + bi c), rounded to fp16.  The prep and chain roles
+// both form W through this function from the same key words, so they agree bit for bit.
+__device__ __forceinline__ uint32_t rotate_pair(uint32_t cs, float br, float bi) {
+  const float2 f = unpack_op<true>(cs);
+  return pack_op<true>(fmaf(br, f.x, -bi * f.y), fmaf(br, f.y, bi * f.x));
 }
 
 // sin/cos of a phase: reduce to [-pi, pi] (x - 2 pi round(x / 2 pi), with the rounding
@@ -185,6 +225,9 @@ struct Bars {
 
 // ------------------------------------------------------------------------------ prep
 // Returns false if a bounded wait expired (after letting its own copies / MMAs land).
+// CB: complex beta (beta = 1 + e^{i phi}, a.beta holds phi): G1 = [K; Q] W^T with the
+// write key W = beta K, A[i][k] = K_i . W_k / 64 (not symmetric; no beta factor left).
+template <bool CB>
 __device__ bool prep_role(const TcArgs &a, uint8_t *smem, Bars *bars, uint32_t tmem, int b, int h,
                           int nchunks) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -239,6 +282,11 @@ __device__ bool prep_role(const TcArgs &a, uint8_t *smem, Bars *bars, uint32_t t
       for (int r = 0; r < 2; ++r) {
         const int t = 8 * warp + (lane & 7), sg = ((lane >> 3) + 2 * (lane & 7) + 4 * r) & 7;
         const bool valid = t < nvalid;
+        float br = 1.f, bi = 0.f;
+        if (CB) {
+          fast_sincos(bs[t], &bi, &br);
+          br += 1.f;
+        }
         uint4 kraw = make_uint4(0, 0, 0, 0), qraw = kraw, vraw = kraw;
         if (valid) {
           kraw = *reinterpret_cast<const uint4 *>(stage + t * 128 + sg * 16);
@@ -254,13 +302,13 @@ __device__ bool prep_role(const TcArgs &a, uint8_t *smem, Bars *bars, uint32_t t
           const __nv_bfloat162 kk2 = *reinterpret_cast<const __nv_bfloat162 *>(&kr[i]);
           fast_sincos(__low2float(kk2), &s0_, &c0_);
           fast_sincos(__high2float(kk2), &s1_, &c1_);
-          kw[2 * i] = pack_bf16(c0_, s0_);
-          kw[2 * i + 1] = pack_bf16(c1_, s1_);
+          kw[2 * i] = pack_op<CB>(c0_, s0_);
+          kw[2 * i + 1] = pack_op<CB>(c1_, s1_);
           const __nv_bfloat162 qq2 = *reinterpret_cast<const __nv_bfloat162 *>(&qr[i]);
           fast_sincos(__low2float(qq2), &s0_, &c0_);
           fast_sincos(__high2float(qq2), &s1_, &c1_);
-          qw[2 * i] = pack_bf16(c0_, s0_);
-          qw[2 * i + 1] = pack_bf16(c1_, s1_);
+          qw[2 * i] = pack_op<CB>(c0_, s0_);
+          qw[2 * i + 1] = pack_op<CB>(c1_, s1_);
         }
         if (!valid) {
 #pragma unroll
@@ -272,6 +320,10 @@ __device__ bool prep_role(const TcArgs &a, uint8_t *smem, Bars *bars, uint32_t t
               make_uint4(kw[4 * half], kw[4 * half + 1], kw[4 * half + 2], kw[4 * half + 3]);
           *reinterpret_cast<uint4 *>(kq + cm_off(64 + t, 16 * sg + 8 * half, RG_KQ)) =
               make_uint4(qw[4 * half], qw[4 * half + 1], qw[4 * half + 2], qw[4 * half + 3]);
+          if (CB)  // write key W = beta K into the (free) A^T buffer, for G1
+            *reinterpret_cast<uint4 *>(smem + OFF_AT + cm_off(t, 16 * sg + 8 * half, RG_KQ)) =
+                make_uint4(rotate_pair(kw[4 * half], br, bi), rotate_pair(kw[4 * half + 1], br, bi),
+                           rotate_pair(kw[4 * half + 2], br, bi), rotate_pair(kw[4 * half + 3], br, bi));
         }
         *reinterpret_cast<uint4 *>(vb + cm_off(t, 8 * sg, RG_64)) = vraw;
       }
@@ -287,11 +339,11 @@ __device__ bool prep_role(const TcArgs &a, uint8_t *smem, Bars *bars, uint32_t t
     }
     if (tid == 0) {
       tc_fence_after();
-      const uint32_t sa = smem_u32(kq);
+      const uint32_t sa = smem_u32(kq), sb = CB ? smem_u32(smem + OFF_AT) : sa;
 #pragma unroll
       for (int kk = 0; kk < 8; ++kk)
-        mma_f16_ss(tmem + COL_D1, make_desc(sa + kk * 256, 128, RG_KQ), make_desc(sa + kk * 256, 128, RG_KQ),
-                   idesc_bf16(128, 64, false, false), kk > 0);
+        mma_f16_ss(tmem + COL_D1, make_desc(sa + kk * 256, 128, RG_KQ), make_desc(sb + kk * 256, 128, RG_KQ),
+                   idesc_op<CB>(128, 64, false, false), kk > 0);
       mma_commit(&bars->prep_mma);
     }
     mma_pending = true;
@@ -304,7 +356,19 @@ __device__ bool prep_role(const TcArgs &a, uint8_t *smem, Bars *bars, uint32_t t
     // ---- P3: A^T from the (exactly symmetric) Gram rows, At[k][i] = beta_k G[k][i] / 64
     //      for i > k (quarters 0, 1); P = tril(Q K^T) in bf16 (quarters 2, 3).
     //      Warp half hf takes columns 32 hf .. 32 hf + 31.
-    if (q < 2) {
+    if (CB && q < 2) {
+      // row i of K W^T: A[i][k] = G1[i][k] / 64 for k < i, stored as column i of A^T
+      const int i = q * 32 + lane;
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        float g[16];
+        const int c0 = 32 * hf + 16 * u;
+        tmem_ld16(tmem + lane_base + COL_D1 + c0, g);
+        tmem_ld_wait();
+#pragma unroll
+        for (int kk = 0; kk < 16; ++kk) at[(c0 + kk) * LDA + i] = (c0 + kk < i) ? g[kk] * inv64 : 0.f;
+      }
+    } else if (q < 2) {
       const int k = q * 32 + lane;
       const float bk = bs[k] * inv64;
 #pragma unroll
@@ -335,11 +399,12 @@ __device__ bool prep_role(const TcArgs &a, uint8_t *smem, Bars *bars, uint32_t t
         for (int half = 0; half < 2; ++half) {
           const int s = c0 + 8 * half;
           const float *pp = p + 8 * half;
+          const float ps = CB ? inv64 : 1.f;  // fp16 tiles hold P / 64
           uint4 w;
-          w.x = pack_bf16(s + 0 <= t ? pp[0] : 0.f, s + 1 <= t ? pp[1] : 0.f);
-          w.y = pack_bf16(s + 2 <= t ? pp[2] : 0.f, s + 3 <= t ? pp[3] : 0.f);
-          w.z = pack_bf16(s + 4 <= t ? pp[4] : 0.f, s + 5 <= t ? pp[5] : 0.f);
-          w.w = pack_bf16(s + 6 <= t ? pp[6] : 0.f, s + 7 <= t ? pp[7] : 0.f);
+          w.x = pack_op<CB>(s + 0 <= t ? pp[0] * ps : 0.f, s + 1 <= t ? pp[1] * ps : 0.f);
+          w.y = pack_op<CB>(s + 2 <= t ? pp[2] * ps : 0.f, s + 3 <= t ? pp[3] * ps : 0.f);
+          w.z = pack_op<CB>(s + 4 <= t ? pp[4] * ps : 0.f, s + 5 <= t ? pp[5] * ps : 0.f);
+          w.w = pack_op<CB>(s + 6 <= t ? pp[6] * ps : 0.f, s + 7 <= t ? pp[7] * ps : 0.f);
           *reinterpret_cast<uint4 *>(pb + cm_off(t, s, RG_64)) = w;
         }
       }
@@ -395,7 +460,16 @@ __device__ bool prep_role(const TcArgs &a, uint8_t *smem, Bars *bars, uint32_t t
     group_sync(BAR_PREP, kPrepThreads);
 
     // ---- P4d: beta of this chunk next to T for the chain, which forms bT = diag(beta) T
-    if (tid < kC) reinterpret_cast<float *>(smem + OFF_BSLOT)[slot * kC + tid] = bs[tid];
+    if (tid < kC) {
+      if (CB) {
+        float sp, cp;
+        fast_sincos(bs[tid], &sp, &cp);
+        reinterpret_cast<float *>(smem + OFF_BSLOT)[slot * kC + tid] = 1.f + cp;
+        reinterpret_cast<float *>(smem + OFF_BIM)[slot * kC + tid] = sp;
+      } else {
+        reinterpret_cast<float *>(smem + OFF_BSLOT)[slot * kC + tid] = bs[tid];
+      }
+    }
     // T, beta, P, V and K, Q of this slot are ready for the chain
     fence_proxy_async_smem();
     tc_fence_before();
@@ -414,6 +488,9 @@ __device__ bool prep_role(const TcArgs &a, uint8_t *smem, Bars *bars, uint32_t t
 }
 
 // ------------------------------------------------------------------------------ chain
+// CB: complex beta; U = T E (no beta factor) and the state update S^T += W^T U, with W
+// rebuilt from this slot's K tile into the S^T operand buffer while U = T E runs.
+template <bool CB>
 __device__ bool chain_role(const TcArgs &a, uint8_t *smem, Bars *bars, uint32_t tmem, int bh, int b,
                            int h, int nchunks) {
   const int ctid = threadIdx.x - kPrepThreads, cw = ctid >> 5, lane = ctid & 31;
@@ -438,7 +515,8 @@ __device__ bool chain_role(const TcArgs &a, uint8_t *smem, Bars *bars, uint32_t 
   group_sync(BAR_CHAIN, kChainThreads);
 
   uint32_t cm_phase = 0;
-  bool ok = true, mma_pending = false;
+  bool ok = true, mma_pending = false, over = false;
+  const float ss64 = CB ? inv64 : 1.f;  // fp16 tiles hold S^T / 64
   for (int c = 0; c < nchunks; ++c) {
     const int slot = c & 1, t0 = c * kC, nvalid = min(kC, L - t0);
     uint8_t *kq = smem + OFF_KQ + slot * KQ_BYTES;
@@ -463,8 +541,8 @@ __device__ bool chain_role(const TcArgs &a, uint8_t *smem, Bars *bars, uint32_t 
       for (int half = 0; half < 2; ++half) {
         const float *ss = sv + 8 * half;
         *reinterpret_cast<uint4 *>(s0 + cm_off(j, 16 * u + 8 * half, RG_64)) =
-            make_uint4(pack_bf16(ss[0], ss[1]), pack_bf16(ss[2], ss[3]), pack_bf16(ss[4], ss[5]),
-                       pack_bf16(ss[6], ss[7]));
+            make_uint4(pack_chk<CB>(ss[0] * ss64, ss[1] * ss64, over), pack_chk<CB>(ss[2] * ss64, ss[3] * ss64, over),
+                       pack_chk<CB>(ss[4] * ss64, ss[5] * ss64, over), pack_chk<CB>(ss[6] * ss64, ss[7] * ss64, over));
       }
     }
     fence_proxy_async_smem();
@@ -478,7 +556,7 @@ __device__ bool chain_role(const TcArgs &a, uint8_t *smem, Bars *bars, uint32_t 
 #pragma unroll
       for (int kk = 0; kk < 8; ++kk)
         mma_f16_ss(tmem + COL_R3, make_desc(sa + kk * 256, 128, RG_KQ), make_desc(ss + kk * 2 * RG_64, RG_64, 128),
-                   idesc_bf16(128, 64, false, true), kk > 0);
+                   idesc_op<CB>(128, 64, false, true), kk > 0);
       mma_commit(&bars->chain_mma);
     }
     mma_pending = true;
@@ -519,7 +597,10 @@ __device__ bool chain_role(const TcArgs &a, uint8_t *smem, Bars *bars, uint32_t 
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
             const float2 vv = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&vw[i]));
-            ew[i] = pack_bf16(vv.x - ks[8 * half + 2 * i] * inv64, vv.y - ks[8 * half + 2 * i + 1] * inv64);
+            if (CB)  // the state-read rows already carry the 1 / 64
+              ew[i] = pack_chk<true>(vv.x - ks[8 * half + 2 * i], vv.y - ks[8 * half + 2 * i + 1], over);
+            else
+              ew[i] = pack_bf16(vv.x - ks[8 * half + 2 * i] * inv64, vv.y - ks[8 * half + 2 * i + 1] * inv64);
           }
           *vp = make_uint4(ew[0], ew[1], ew[2], ew[3]);
         }
@@ -527,15 +608,15 @@ __device__ bool chain_role(const TcArgs &a, uint8_t *smem, Bars *bars, uint32_t 
     } else {
       // bT = diag(beta) T -> bf16 (row i = lane of chain warps 2, 3), beside E
       const int i = 32 * (cw - 2) + lane;
-      const float bi = bsl[i];
+      const float bi = CB ? 1.f : bsl[i];
       const float *tr = tfs + i * LDA;
 #pragma unroll
       for (int c8 = 0; c8 < 8; ++c8) {
         const float4 x0 = *reinterpret_cast<const float4 *>(tr + 8 * c8);
         const float4 x1 = *reinterpret_cast<const float4 *>(tr + 8 * c8 + 4);
         *reinterpret_cast<uint4 *>(tb + cm_off(i, 8 * c8, RG_64)) =
-            make_uint4(pack_bf16(bi * x0.x, bi * x0.y), pack_bf16(bi * x0.z, bi * x0.w),
-                       pack_bf16(bi * x1.x, bi * x1.y), pack_bf16(bi * x1.z, bi * x1.w));
+            make_uint4(pack_chk<CB>(bi * x0.x, bi * x0.y, over), pack_chk<CB>(bi * x0.z, bi * x0.w, over),
+                       pack_chk<CB>(bi * x1.x, bi * x1.y, over), pack_chk<CB>(bi * x1.z, bi * x1.w, over));
       }
     }
     fence_proxy_async_smem();
@@ -549,10 +630,22 @@ __device__ bool chain_role(const TcArgs &a, uint8_t *smem, Bars *bars, uint32_t 
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk)
         mma_f16_ss(tmem + COL_RU, make_desc(sb + kk * 256, 128, RG_64), make_desc(se + kk * 2 * RG_64, RG_64, 128),
-                   idesc_bf16(64, 64, false, true), kk > 0);
+                   idesc_op<CB>(64, 64, false, true), kk > 0);
       mma_commit(&bars->chain_mma);
     }
     mma_pending = true;
+    if (CB) {
+      // W = beta K of this slot -> the S^T operand buffer (G3, its last reader, is done)
+      const int t = ctid & 63;
+      const float br = bsl[t], bi = reinterpret_cast<const float *>(smem + OFF_BIM)[slot * kC + t];
+#pragma unroll
+      for (int jj = 0; jj < 8; ++jj) {
+        const uint32_t off = cm_off(t, 8 * (2 * jj + (ctid >> 6)), RG_KQ);
+        const uint4 kr = *reinterpret_cast<const uint4 *>(kq + off);
+        *reinterpret_cast<uint4 *>(s0 + off) = make_uint4(rotate_pair(kr.x, br, bi), rotate_pair(kr.y, br, bi),
+                                                          rotate_pair(kr.z, br, bi), rotate_pair(kr.w, br, bi));
+      }
+    }
     if (ctid == 0) ok = mbar_wait(&bars->chain_mma, cm_phase, kTimeoutNs);
     if (group_any(!ok, BAR_CHAIN, kChainThreads)) { ok = false; break; }
     cm_phase ^= 1;
@@ -572,8 +665,8 @@ __device__ bool chain_role(const TcArgs &a, uint8_t *smem, Bars *bars, uint32_t 
           for (int half = 0; half < 2; ++half) {
             const float *uu = uv + 8 * half;
             *reinterpret_cast<uint4 *>(ub + cm_off(t, 16 * u + 8 * half, RG_64)) =
-                make_uint4(pack_bf16(uu[0], uu[1]), pack_bf16(uu[2], uu[3]), pack_bf16(uu[4], uu[5]),
-                           pack_bf16(uu[6], uu[7]));
+                make_uint4(pack_chk<CB>(uu[0], uu[1], over), pack_chk<CB>(uu[2], uu[3], over),
+                           pack_chk<CB>(uu[4], uu[5], over), pack_chk<CB>(uu[6], uu[7], over));
           }
         }
       }
@@ -587,12 +680,12 @@ __device__ bool chain_role(const TcArgs &a, uint8_t *smem, Bars *bars, uint32_t 
     //      don't-care)
     if (ctid == 0) {
       tc_fence_after();
-      const uint32_t sk = smem_u32(kq), su = smem_u32(ub), sp = smem_u32(pb) - 8 * RG_64;
+      const uint32_t sk = CB ? smem_u32(s0) : smem_u32(kq), su = smem_u32(ub), sp = smem_u32(pb) - 8 * RG_64;
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) {
         const uint64_t ud = make_desc(su + kk * 2 * RG_64, RG_64, 128);
-        mma_f16_ss(tmem + COL_S, make_desc(sk + kk * 2 * RG_KQ, RG_KQ, 128), ud, idesc_bf16(128, 64, true, true), 1u);
-        mma_f16_ss(tmem + COL_R3, make_desc(sp + kk * 256, 128, RG_64), ud, idesc_bf16(128, 64, false, true), 1u);
+        mma_f16_ss(tmem + COL_S, make_desc(sk + kk * 2 * RG_KQ, RG_KQ, 128), ud, idesc_op<CB>(128, 64, true, true), 1u);
+        mma_f16_ss(tmem + COL_R3, make_desc(sp + kk * 256, 128, RG_64), ud, idesc_op<CB>(128, 64, false, true), 1u);
       }
       mma_commit(&bars->chain_mma);
     }
@@ -604,8 +697,10 @@ __device__ bool chain_role(const TcArgs &a, uint8_t *smem, Bars *bars, uint32_t 
     tc_fence_after();
     if (ctid == 0) mbar_arrive(&bars->free_[slot]);  // K, Q, T, beta, E, P of this slot are consumed
 
-    // ---- C5: outputs O = R3 rows 64.. / 64 (row t = lane of chain warps 2, 3)
+    // ---- C5: outputs O = R3 rows 64.. / 64 (row t = lane of chain warps 2, 3); the fp16
+    //      tiles (S^T / 64, P / 64) put the 1 / 64 into R3 already
     if (cw >= 2) {
+      const float ss64_out = CB ? 1.f : inv64;
       const int t = 32 * (cw - 2) + lane;
       float *orow = a.out + b * a.s_out.b + h * a.s_out.h + (int64_t)(t0 + t) * a.s_out.t;
 #pragma unroll
@@ -617,7 +712,7 @@ __device__ bool chain_role(const TcArgs &a, uint8_t *smem, Bars *bars, uint32_t 
 #pragma unroll
           for (int i = 0; i < 16; i += 4)
             *reinterpret_cast<float4 *>(orow + 16 * u + i) =
-                make_float4(o[i] * inv64, o[i + 1] * inv64, o[i + 2] * inv64, o[i + 3] * inv64);
+                make_float4(o[i] * ss64_out, o[i + 1] * ss64_out, o[i + 2] * ss64_out, o[i + 3] * ss64_out);
         }
       }
     }
@@ -638,9 +733,11 @@ __device__ bool chain_role(const TcArgs &a, uint8_t *smem, Bars *bars, uint32_t 
   } else if (mma_pending && ctid == 0) {
     mbar_wait(&bars->chain_mma, cm_phase, kTimeoutNs);
   }
+  if (CB && over) atomicCAS(a.err, 0, DP_ERR_RANGE);
   return ok;
 }
 
+template <bool CB>
 __global__ void __launch_bounds__(kThreads, 1) core_tc_kernel(TcArgs a) {
   extern __shared__ __align__(1024) uint8_t smem[];
   Bars *bars = reinterpret_cast<Bars *>(smem + OFF_BAR);
@@ -675,9 +772,9 @@ __global__ void __launch_bounds__(kThreads, 1) core_tc_kernel(TcArgs a) {
 
   bool ok;
   if (tid < kPrepThreads)
-    ok = prep_role(a, smem, bars, tmem, b, h, nchunks);
+    ok = prep_role<CB>(a, smem, bars, tmem, b, h, nchunks);
   else
-    ok = chain_role(a, smem, bars, tmem, bh, b, h, nchunks);
+    ok = chain_role<CB>(a, smem, bars, tmem, bh, b, h, nchunks);
   if (!ok) atomicExch(fail_flag, 1);
 
   tc_fence_before();
@@ -700,9 +797,10 @@ bool core_tc_supported(const void *tk, const void *tq, const void *v, int in_dt,
   return true;
 }
 
+// cbeta: `beta` holds phi of the complex beta 1 + e^{i phi} (ComplexBetaDeltaPhaseBlock).
 int core_fwd_tc(const void *tk, const void *tq, const void *v, const void *beta, int beta_dt,
                 const float *state_in, float *out, float *state_out, int B, int H, int L,
-                const SeqStrides *s, cudaStream_t stream) {
+                const SeqStrides *s, cudaStream_t stream, bool cbeta) {
   TcArgs a;
   a.tk = static_cast<const __nv_bfloat16 *>(tk);
   a.tq = static_cast<const __nv_bfloat16 *>(tq);
@@ -721,9 +819,10 @@ int core_fwd_tc(const void *tk, const void *tq, const void *v, const void *beta,
   a.s_out = s[4];
   a.err = device_error_ptr();
   if (!a.err) return set_error(DP_ERR_CUDA, "core_fwd_tc: device error word unavailable");
-  cudaError_t e = cudaFuncSetAttribute(core_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+  auto kern = cbeta ? core_tc_kernel<true> : core_tc_kernel<false>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
   if (e != cudaSuccess) return set_error(DP_ERR_CUDA, std::string("core_tc smem attr: ") + cudaGetErrorString(e));
-  core_tc_kernel<<<B * H, kThreads, SMEM_BYTES, stream>>>(a);
+  kern<<<B * H, kThreads, SMEM_BYTES, stream>>>(a);
   return check_launch("core_tc_kernel");
 }
 

@@ -6,6 +6,10 @@
 // _triton_streaming_step_kernel (delta_phase/kernels/triton_chunk_delta.py:125-185),
 // but on the interleaved complex64 state, so torch's complex tensor is used as is.
 //
+// Complex beta (ComplexBetaDeltaPhaseBlock.step, layers.py:402-407): beta = 1 + e^{i phi}
+// and M <- M + beta (v - v_old) k^T, i.e. the update writes along the rotated key
+// w = beta k = (br c - bi s) + i (br s + bi c) per channel (template flag CB, `beta` = phi).
+//
 // One CTA per (batch, head); one warp per state row (value channel) at a time.  Each
 // row is read once and written once with 16-byte accesses (two complex entries per
 // lane), so the kernel moves the 2 * Dv * D * 8 bytes of state plus the inputs.
@@ -28,8 +32,8 @@ __device__ __forceinline__ float warp_sum(float x) {
   return x;
 }
 
-// kq: smem (4 x D): cos k, sin k, cos q, sin q.
-template <bool kVec4>
+// kq: smem (4 x D): cos k, sin k, cos q, sin q; CB adds the write key (2 x D).
+template <bool kVec4, bool CB>
 __global__ void __launch_bounds__(kDecThreads)
 decode_kernel(const float *state_in, float *state_out, const void *__restrict__ tk,
               const void *__restrict__ tq, const void *__restrict__ v,
@@ -48,9 +52,24 @@ decode_kernel(const float *state_in, float *state_out, const void *__restrict__ 
     kq[2 * D + c] = co;
     kq[3 * D + c] = s;
   }
-  __syncthreads();
   const float inv_d = 1.0f / (float)D;
-  const float bt = load_any(beta, beta_dt, b * s_b.b + h * s_b.h);
+  float bt = load_any(beta, beta_dt, b * s_b.b + h * s_b.h);
+  // write key: the read key (real beta) or beta k (complex beta, then bt = 1)
+  const float *wc = kq, *ws = kq + D;
+  if (CB) {
+    float sp, cp;
+    sincosf(bt, &sp, &cp);
+    const float br = 1.f + cp;
+    __syncthreads();
+    for (int c = threadIdx.x; c < D; c += kDecThreads) {
+      kq[4 * D + c] = fmaf(br, kq[c], -sp * kq[D + c]);
+      kq[5 * D + c] = fmaf(br, kq[D + c], sp * kq[c]);
+    }
+    wc = kq + 4 * D;
+    ws = kq + 5 * D;
+    bt = 1.f;
+  }
+  __syncthreads();
   const int64_t base = (int64_t)bh * Dv * 2 * D;
   for (int o = warp; o < Dv; o += kDecThreads / 32) {
     const float *row_in = state_in + base + (int64_t)o * 2 * D;
@@ -83,10 +102,10 @@ decode_kernel(const float *state_in, float *state_out, const void *__restrict__ 
         const int p = lane + 32 * it;
         if (it < cnt && p < npair) {
           float4 t = m[it];
-          t.x = fmaf(e, kq[2 * p], t.x);
-          t.y = fmaf(e, kq[D + 2 * p], t.y);
-          t.z = fmaf(e, kq[2 * p + 1], t.z);
-          t.w = fmaf(e, kq[D + 2 * p + 1], t.w);
+          t.x = fmaf(e, wc[2 * p], t.x);
+          t.y = fmaf(e, ws[2 * p], t.y);
+          t.z = fmaf(e, wc[2 * p + 1], t.z);
+          t.w = fmaf(e, ws[2 * p + 1], t.w);
           reinterpret_cast<float4 *>(row_out)[p] = t;
           r += t.x * kq[2 * D + 2 * p] + t.y * kq[3 * D + 2 * p] + t.z * kq[2 * D + 2 * p + 1] +
                t.w * kq[3 * D + 2 * p + 1];
@@ -94,10 +113,10 @@ decode_kernel(const float *state_in, float *state_out, const void *__restrict__ 
       }
       for (int p = lane + 128; p < npair; p += 32) {
         float4 t = reinterpret_cast<const float4 *>(row_in)[p];
-        t.x = fmaf(e, kq[2 * p], t.x);
-        t.y = fmaf(e, kq[D + 2 * p], t.y);
-        t.z = fmaf(e, kq[2 * p + 1], t.z);
-        t.w = fmaf(e, kq[D + 2 * p + 1], t.w);
+        t.x = fmaf(e, wc[2 * p], t.x);
+        t.y = fmaf(e, ws[2 * p], t.y);
+        t.z = fmaf(e, wc[2 * p + 1], t.z);
+        t.w = fmaf(e, ws[2 * p + 1], t.w);
         reinterpret_cast<float4 *>(row_out)[p] = t;
         r += t.x * kq[2 * D + 2 * p] + t.y * kq[3 * D + 2 * p] + t.z * kq[2 * D + 2 * p + 1] +
              t.w * kq[3 * D + 2 * p + 1];
@@ -115,8 +134,8 @@ decode_kernel(const float *state_in, float *state_out, const void *__restrict__ 
       float r = 0.f;
       for (int c = lane; c < D; c += 32) {
         float2 m = reinterpret_cast<const float2 *>(row_in)[c];
-        m.x = fmaf(e, kq[c], m.x);
-        m.y = fmaf(e, kq[D + c], m.y);
+        m.x = fmaf(e, wc[c], m.x);
+        m.y = fmaf(e, ws[c], m.y);
         reinterpret_cast<float2 *>(row_out)[c] = m;
         r += m.x * kq[2 * D + c] + m.y * kq[3 * D + c];
       }
@@ -129,7 +148,7 @@ decode_kernel(const float *state_in, float *state_out, const void *__restrict__ 
 // Fast path for even D <= 64 (one float4 = two complex entries per lane and row) and
 // Dv <= 8 RPW: warp w owns rows w, w + 8, ...; all of its rows are loaded before any
 // reduction, so every lane keeps RPW independent 16-byte loads in flight.
-template <int RPW>
+template <int RPW, bool CB>
 __global__ void __launch_bounds__(kDecThreads)
 decode_rows_kernel(const float *state_in, float *state_out, const void *__restrict__ tk,
                    const void *__restrict__ tq, const void *__restrict__ v,
@@ -149,7 +168,19 @@ decode_rows_kernel(const float *state_in, float *state_out, const void *__restri
     sincosf(load_any(tq, in_dt, b * s_tq.b + h * s_tq.h + 2 * p + 1), &sq1, &cq1);
   }
   const float inv_d = 1.0f / (float)D;
-  const float bt = load_any(beta, beta_dt, b * s_b.b + h * s_b.h);
+  float bt = load_any(beta, beta_dt, b * s_b.b + h * s_b.h);
+  // write key: the read key (real beta) or beta k (complex beta, then bt = 1)
+  float wc0 = ck0, ws0 = sk0, wc1 = ck1, ws1 = sk1;
+  if (CB) {
+    float sp, cp;
+    sincosf(bt, &sp, &cp);
+    const float br = 1.f + cp;
+    wc0 = fmaf(br, ck0, -sp * sk0);
+    ws0 = fmaf(br, sk0, sp * ck0);
+    wc1 = fmaf(br, ck1, -sp * sk1);
+    ws1 = fmaf(br, sk1, sp * ck1);
+    bt = 1.f;
+  }
   const int64_t base = (int64_t)bh * Dv * 2 * D;
   float4 m[RPW];
   float vo[RPW];
@@ -173,10 +204,10 @@ decode_rows_kernel(const float *state_in, float *state_out, const void *__restri
 #pragma unroll
   for (int r = 0; r < RPW; ++r) {
     const float e = bt * (vo[r] - acc[r] * inv_d);
-    m[r].x = fmaf(e, ck0, m[r].x);
-    m[r].y = fmaf(e, sk0, m[r].y);
-    m[r].z = fmaf(e, ck1, m[r].z);
-    m[r].w = fmaf(e, sk1, m[r].w);
+    m[r].x = fmaf(e, wc0, m[r].x);
+    m[r].y = fmaf(e, ws0, m[r].y);
+    m[r].z = fmaf(e, wc1, m[r].z);
+    m[r].w = fmaf(e, ws1, m[r].w);
     const int o = warp + 8 * r;
     if (o < Dv && active) reinterpret_cast<float4 *>(state_out + base + (int64_t)o * 2 * D)[p] = m[r];
     acc[r] = m[r].x * cq0 + m[r].y * sq0 + m[r].z * cq1 + m[r].w * sq1;
@@ -197,35 +228,55 @@ decode_rows_kernel(const float *state_in, float *state_out, const void *__restri
 }  // namespace
 }  // namespace dp
 
-extern "C" int dp_core_decode(const float *state_in, float *state_out, const void *theta_k,
-                              const void *theta_q, const void *v, const void *beta, int in_dtype,
-                              int beta_dtype, float *out, int B, int H, int D, int Dv,
-                              const int64_t *strides, void *stream) {
-  using namespace dp;
-  DP_REQUIRE(B >= 0 && H >= 0 && D >= 1 && Dv >= 1, DP_ERR_INVALID_ARGUMENT,
-             "dp_core_decode: bad sizes");
-  DP_REQUIRE(valid_dtype(in_dtype) && valid_dtype(beta_dtype), DP_ERR_INVALID_ARGUMENT,
-             "dp_core_decode: bad dtype code");
-  DP_REQUIRE(D <= 4096, DP_ERR_UNSUPPORTED, "dp_core_decode: D must be <= 4096");
+namespace dp {
+namespace {
+int decode_entry(const char *name, bool cbeta, const float *state_in, float *state_out, const void *theta_k,
+                 const void *theta_q, const void *v, const void *beta, int in_dtype, int beta_dtype, float *out,
+                 int B, int H, int D, int Dv, const int64_t *strides, void *stream) {
+  const std::string n(name);
+  DP_REQUIRE(B >= 0 && H >= 0 && D >= 1 && Dv >= 1, DP_ERR_INVALID_ARGUMENT, n + ": bad sizes");
+  DP_REQUIRE(valid_dtype(in_dtype) && valid_dtype(beta_dtype), DP_ERR_INVALID_ARGUMENT, n + ": bad dtype code");
+  DP_REQUIRE(D <= 4096, DP_ERR_UNSUPPORTED, n + ": D must be <= 4096");
   if (B == 0 || H == 0) return DP_OK;
   DP_REQUIRE(state_in && state_out && theta_k && theta_q && v && beta && out && strides,
-             DP_ERR_INVALID_ARGUMENT, "dp_core_decode: null pointer");
+             DP_ERR_INVALID_ARGUMENT, n + ": null pointer");
   SeqStrides s[5];
   for (int i = 0; i < 5; ++i) s[i] = SeqStrides{strides[2 * i], strides[2 * i + 1], 0};
   const bool vec4 = (D % 2 == 0) && (reinterpret_cast<uintptr_t>(state_in) % 16 == 0) &&
                     (reinterpret_cast<uintptr_t>(state_out) % 16 == 0);
-  const size_t smem = 4 * (size_t)D * sizeof(float);
+  const size_t smem = (cbeta ? 6 : 4) * (size_t)D * sizeof(float);
   if (vec4 && D <= 64 && Dv <= 128) {
-    auto kern = Dv <= 64 ? decode_rows_kernel<8> : decode_rows_kernel<16>;
+    auto kern = Dv <= 64 ? (cbeta ? decode_rows_kernel<8, true> : decode_rows_kernel<8, false>)
+                         : (cbeta ? decode_rows_kernel<16, true> : decode_rows_kernel<16, false>);
     kern<<<B * H, kDecThreads, 0, as_stream(stream)>>>(state_in, state_out, theta_k, theta_q, v, beta, in_dtype,
                                                        beta_dtype, out, H, D, Dv, s[0], s[1], s[2], s[3], s[4]);
-  } else if (vec4)
-    decode_kernel<true><<<B * H, kDecThreads, smem, as_stream(stream)>>>(
-        state_in, state_out, theta_k, theta_q, v, beta, in_dtype, beta_dtype, out, H, D, Dv, s[0],
-        s[1], s[2], s[3], s[4]);
-  else
-    decode_kernel<false><<<B * H, kDecThreads, smem, as_stream(stream)>>>(
-        state_in, state_out, theta_k, theta_q, v, beta, in_dtype, beta_dtype, out, H, D, Dv, s[0],
-        s[1], s[2], s[3], s[4]);
+  } else {
+    auto kern = vec4 ? (cbeta ? decode_kernel<true, true> : decode_kernel<true, false>)
+                     : (cbeta ? decode_kernel<false, true> : decode_kernel<false, false>);
+    if (smem > 48 * 1024) {
+      const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess) return set_error(DP_ERR_CUDA, n + ": smem attribute: " + cudaGetErrorString(e));
+    }
+    kern<<<B * H, kDecThreads, smem, as_stream(stream)>>>(state_in, state_out, theta_k, theta_q, v, beta, in_dtype,
+                                                          beta_dtype, out, H, D, Dv, s[0], s[1], s[2], s[3], s[4]);
+  }
   return check_launch("decode_kernel");
+}
+}  // namespace
+}  // namespace dp
+
+extern "C" int dp_core_decode(const float *state_in, float *state_out, const void *theta_k,
+                              const void *theta_q, const void *v, const void *beta, int in_dtype,
+                              int beta_dtype, float *out, int B, int H, int D, int Dv,
+                              const int64_t *strides, void *stream) {
+  return dp::decode_entry("dp_core_decode", false, state_in, state_out, theta_k, theta_q, v, beta, in_dtype,
+                          beta_dtype, out, B, H, D, Dv, strides, stream);
+}
+
+extern "C" int dp_core_cbeta_decode(const float *state_in, float *state_out, const void *theta_k,
+                                    const void *theta_q, const void *v, const void *phi, int in_dtype,
+                                    int phi_dtype, float *out, int B, int H, int D, int Dv,
+                                    const int64_t *strides, void *stream) {
+  return dp::decode_entry("dp_core_cbeta_decode", true, state_in, state_out, theta_k, theta_q, v, phi, in_dtype,
+                          phi_dtype, out, B, H, D, Dv, strides, stream);
 }

@@ -3,6 +3,7 @@ from .chunk_delta import (
     DeltaPhaseCudaFunction,
     DeltaPhaseTritonFunction,
     chunkwise_forward,
+    complex_beta_chunkwise,
     cuda_available,
     decode_step,
     delta_phase_chunkwise_fused,
@@ -20,6 +21,7 @@ __all__ = [
     "DeltaPhaseCudaFunction",
     "cuda_available",
     "chunkwise_forward",
+    "complex_beta_chunkwise",
     "decode_step",
     "gram_matrix_cuda",
     "gram_matrix_triton",

@@ -12,6 +12,10 @@ Drop-in for ``delta_phase.kernels.triton_chunk_delta`` (mcarbonell/delta-phase v
 * :func:`gram_matrix_cuda` (alias ``gram_matrix_triton``) -- the strictly-lower phasor
   Gram of the archived Triton kernel (:32-122).
 * :func:`decode_step` -- the fused single-token state update (layers.py:279-285).
+* ``complex_beta=True`` on :func:`chunkwise_forward` / :func:`decode_step` -- the
+  complex-beta rule of ComplexBetaDeltaPhaseBlock (layers.py:294-418), ``beta`` then
+  holding phi of beta = 1 + e^{i phi}; :func:`complex_beta_chunkwise` is its chunkwise
+  form over a sequence (the reference's token loop, layers.py:346-360).
 * :func:`laplace_chunkwise` -- the LaplacePhaseCore chunk solve (layers.py:481-561).
 * :func:`triton_available` -- kept for API compatibility; True when the CUDA library
   is loaded and a GPU is present (the kernels it reported on are replaced here).
@@ -72,11 +76,13 @@ def _complex_state_view(state, B, H, Dv, D, device):
     return torch.view_as_real(state.contiguous())
 
 
-def chunkwise_forward(theta_k, theta_q, v, beta, chunk_size=64, initial_state=None, out=None):
+def chunkwise_forward(theta_k, theta_q, v, beta, chunk_size=64, initial_state=None, out=None,
+                      complex_beta=False):
     """Run the CUDA chunkwise core; ragged L is allowed (tokens past L do not exist).
 
     ``out`` may be a preallocated float32 (B, H, L, Dv) view (any strides with unit
-    channel stride), e.g. a (B, L, H, Dv) buffer transposed.  Returns ``(out, M)``.
+    channel stride), e.g. a (B, L, H, Dv) buffer transposed.  ``complex_beta``: ``beta``
+    holds phi and the write strength is 1 + e^{i phi}.  Returns ``(out, M)``.
     """
     _check_phase_inputs(theta_k, theta_q, v, beta)
     _capi.require_cuda(theta_k, theta_q, v, beta)
@@ -87,8 +93,21 @@ def chunkwise_forward(theta_k, theta_q, v, beta, chunk_size=64, initial_state=No
     if out is None:
         out = torch.empty(B, H, L, Dv, device=dev, dtype=torch.float32)
     M = torch.empty(B, H, Dv, D, device=dev, dtype=torch.complex64)
-    _capi.core_fwd(theta_k, theta_q, v, beta, chunk_size, s_in, out, torch.view_as_real(M))
+    _capi.core_fwd(theta_k, theta_q, v, beta, chunk_size, s_in, out, torch.view_as_real(M),
+                   complex_beta=complex_beta)
     return out, M
+
+
+def complex_beta_chunkwise(theta_k, theta_q, v, phi, initial_state=None):
+    """Complex-beta delta rule over a sequence: the chunkwise (WY) form of the token loop
+    of ComplexBetaDeltaPhaseBlock.forward (layers.py:346-360), beta = 1 + e^{i phi}.
+
+    theta_k, theta_q, v: (B, H, L, D); phi (B, H, L); initial_state (B, H, D, D)
+    complex64 or None (never modified).  Any L.  Returns ``(out (B,H,L,D) float32,
+    M (B,H,D,D) complex64)``.
+    """
+    with torch.no_grad():
+        return chunkwise_forward(theta_k, theta_q, v, phi, 64, initial_state, complex_beta=True)
 
 
 class DeltaPhaseCudaFunction(torch.autograd.Function):
@@ -143,10 +162,12 @@ def gram_matrix_cuda(theta_k: torch.Tensor, beta: torch.Tensor) -> torch.Tensor:
 gram_matrix_triton = gram_matrix_cuda
 
 
-def decode_step(memory_state, theta_k, theta_q, v, beta, out=None, state_out=None):
+def decode_step(memory_state, theta_k, theta_q, v, beta, out=None, state_out=None, complex_beta=False):
     """Fused decode step (layers.py:279-285).  memory_state (B,H,Dv,D) complex64;
     theta_k/theta_q (B,H,D); v (B,H,Dv); beta (B,H).  Returns ``(out (B,H,Dv) float32,
-    new_state)``.  ``state_out=memory_state`` updates the state in place."""
+    new_state)``.  ``state_out=memory_state`` updates the state in place.
+    ``complex_beta``: ``beta`` holds phi, the step of ComplexBetaDeltaPhaseBlock
+    (layers.py:402-407)."""
     B, H, D = theta_k.shape
     Dv = v.shape[-1]
     _capi.require_cuda(memory_state, theta_k, theta_q, v, beta)
@@ -157,7 +178,8 @@ def decode_step(memory_state, theta_k, theta_q, v, beta, out=None, state_out=Non
         raise ValueError("state_out must be a contiguous complex64 tensor")
     if out is None:
         out = torch.empty(B, H, Dv, device=theta_k.device, dtype=torch.float32)
-    _capi.core_decode(s_in, torch.view_as_real(state_out), theta_k, theta_q, v, beta, out)
+    _capi.core_decode(s_in, torch.view_as_real(state_out), theta_k, theta_q, v, beta, out,
+                      complex_beta=complex_beta)
     return out, state_out
 
 

@@ -7,6 +7,7 @@ load in both directions:
 * :class:`ShortCausalConv1D`            -- layers.py:60-88 (torch glue, unchanged math)
 * :class:`LearnableSubstrateLerpFFN`    -- layers.py:90-145 (CUDA: dp_ffn_fold/dp_ffn_fwd)
 * :class:`DeltaPhaseHolographicBlock`   -- layers.py:147-291 (CUDA: dp_core_fwd/dp_core_decode)
+* :class:`ComplexBetaDeltaPhaseBlock`   -- layers.py:294-418 (CUDA: dp_core_cbeta_fwd/dp_core_cbeta_decode)
 * :class:`LaplacePhaseCore`             -- layers.py:422-583 (CUDA: dp_laplace_fwd)
 
 LayerNorms, the causal conv and the projections stay torch (cuBLAS) calls; the
@@ -129,48 +130,37 @@ class LearnableSubstrateLerpFFN(nn.Module):
         return probs[0].item(), probs[1].item(), probs[2].item()
 
 
-class DeltaPhaseHolographicBlock(nn.Module):
-    """Chunkwise complex delta-phase memory block (layers.py:147-291)."""
+class _DeltaRuleBlock(nn.Module):
+    """Forward and step shared by the two delta-rule blocks: LayerNorm -> causal conv ->
+    projections -> the delta-rule core -> norm_retrieved -> out_proj -> norm2 -> FFN.
+    Subclasses name the write-gate projection (``_gate_linear``), map its output to the
+    kernel's gate (``_write_gate``) and to ``last_beta``, and set ``_complex_beta``."""
 
-    def __init__(self, d_model: int, n_heads: int = 8, conv_kernel_size: int = 4,
-                 chunk_size: int = 64, num_banks: int = 4, beta_mode: str = "learned"):
-        super().__init__()
-        if beta_mode not in ("learned", "fixed"):
-            raise ValueError(f"beta_mode must be 'learned' or 'fixed', got {beta_mode!r}")
-        self.d_model = d_model
-        self.n_heads = n_heads
-        self.d_k = d_model // n_heads
-        self.inv_dk = 1.0 / float(self.d_k)
-        self.chunk_size = chunk_size
-        self.beta_mode = beta_mode
-        self.last_beta = None
-        self.norm1 = nn.LayerNorm(d_model)
-        self.norm2 = nn.LayerNorm(d_model)
-        self.norm_retrieved = nn.LayerNorm(d_model)
-        self.causal_conv = ShortCausalConv1D(d_model, kernel_size=conv_kernel_size)
-        self.w_k = nn.Linear(d_model, d_model)
-        self.w_q = nn.Linear(d_model, d_model)
-        self.w_v = nn.Linear(d_model, d_model)
-        self.w_beta = nn.Linear(d_model, n_heads)
-        self.out_proj = nn.Linear(d_model, d_model)
-        self.ffn = LearnableSubstrateLerpFFN(d_model, num_banks=num_banks)
+    _complex_beta = False
 
-    def _beta(self, conv_x):
-        beta = 2.0 * torch.sigmoid(self.w_beta(conv_x))
-        if self.beta_mode == "fixed":
-            beta = torch.ones_like(beta)
-        return beta
+    def _gate_linear(self) -> nn.Linear:
+        raise NotImplementedError
+
+    def _write_gate(self, g: torch.Tensor) -> torch.Tensor:
+        raise NotImplementedError
+
+    def _last_beta(self, gate: torch.Tensor) -> torch.Tensor:
+        return gate.detach()
 
     def _proj_weights(self, dtype):
-        """[w_k; w_q; w_v; w_beta] weights and biases concatenated in ``dtype`` (one GEMM
-        for the four input projections), rebuilt when any of them changes."""
-        ts = (self.w_k.weight, self.w_q.weight, self.w_v.weight, self.w_beta.weight,
-              self.w_k.bias, self.w_q.bias, self.w_v.bias, self.w_beta.bias)
+        """[w_k; w_q; w_v; gate] weights (and biases, when the layers have them)
+        concatenated in ``dtype`` (one GEMM for the four input projections), rebuilt when
+        any of them changes."""
+        lins = (self.w_k, self.w_q, self.w_v, self._gate_linear())
+        biases = [m.bias for m in lins if m.bias is not None]
+        if biases and len(biases) != len(lins):
+            raise ValueError("the input projections must all have biases or none")
+        ts = tuple(m.weight for m in lins) + tuple(biases)
         key = (dtype,) + tuple((t.data_ptr(), t._version) for t in ts)
         if getattr(self, "_proj_key", None) != key:
             with torch.no_grad():
                 W = torch.cat([t.detach() for t in ts[:4]], 0).to(dtype).contiguous()
-                bvec = torch.cat([t.detach() for t in ts[4:]], 0).to(dtype).contiguous()
+                bvec = torch.cat([t.detach() for t in ts[4:]], 0).to(dtype).contiguous() if biases else None
             self._proj_cache = (W, bvec)
             self._proj_key = key
         return self._proj_cache
@@ -203,14 +193,12 @@ class DeltaPhaseHolographicBlock(nn.Module):
         tk = proj[..., :D].view(B, L, H, dk).transpose(1, 2)
         tq = proj[..., D:2 * D].view(B, L, H, dk).transpose(1, 2)
         v = proj[..., 2 * D:3 * D].view(B, L, H, dk).transpose(1, 2)
-        if self.beta_mode == "fixed":
-            beta = torch.ones(B, H, L, device=x.device, dtype=torch.float32)
-        else:
-            beta = (2.0 * torch.sigmoid(proj[..., 3 * D:].float())).transpose(1, 2)
+        beta = self._write_gate(proj[..., 3 * D:]).transpose(1, 2)   # (B, H, L)
         retrieved = torch.empty(B, L, D, device=x.device, dtype=torch.float32)
         _, M_state = chunkwise_forward(tk, tq, v, beta, self.chunk_size, memory_state,
-                                       out=retrieved.view(B, L, H, dk).transpose(1, 2))
-        self.last_beta = beta.detach()
+                                       out=retrieved.view(B, L, H, dk).transpose(1, 2),
+                                       complex_beta=self._complex_beta)
+        self.last_beta = self._last_beta(beta)
         nr = self.norm_retrieved
         rn = torch.empty(B * L, D, device=x.device, dtype=gdt)
         _capi.layernorm(retrieved.view(B * L, D), nr.weight.float(), nr.bias.float(), nr.eps, rn)
@@ -262,12 +250,10 @@ class DeltaPhaseHolographicBlock(nn.Module):
             tk = proj[:, :D].view(B, H, dk)
             tq = proj[:, D:2 * D].view(B, H, dk)
             v = proj[:, 2 * D:3 * D].view(B, H, dk)
-            if self.beta_mode == "fixed":
-                beta = torch.ones(B, H, device=x_t.device, dtype=torch.float32)
-            else:
-                beta = 2.0 * torch.sigmoid(proj[:, 3 * D:].float())
-            self.last_beta = beta.detach().unsqueeze(-1)
-            out, _ = decode_step(memory_state, tk, tq, v, beta, state_out=memory_state)
+            beta = self._write_gate(proj[:, 3 * D:])
+            self.last_beta = self._last_beta(beta.unsqueeze(-1))
+            out, _ = decode_step(memory_state, tk, tq, v, beta, state_out=memory_state,
+                                 complex_beta=self._complex_beta)
             nr = self.norm_retrieved
             rn = torch.empty(B, D, device=x_t.device, dtype=gdt)
             _capi.layernorm(out.view(B, D), nr.weight.float(), nr.bias.float(), nr.eps, rn)
@@ -304,6 +290,92 @@ class DeltaPhaseHolographicBlock(nn.Module):
             mem_new = memory_state.detach().to(torch.complex64).clone().contiguous()
         x = self._step_inplace(x_t, conv_new, mem_new)
         return x, (conv_new, mem_new)
+
+
+class DeltaPhaseHolographicBlock(_DeltaRuleBlock):
+    """Chunkwise complex delta-phase memory block (layers.py:147-291)."""
+
+    def __init__(self, d_model: int, n_heads: int = 8, conv_kernel_size: int = 4,
+                 chunk_size: int = 64, num_banks: int = 4, beta_mode: str = "learned"):
+        super().__init__()
+        if beta_mode not in ("learned", "fixed"):
+            raise ValueError(f"beta_mode must be 'learned' or 'fixed', got {beta_mode!r}")
+        self.d_model = d_model
+        self.n_heads = n_heads
+        self.d_k = d_model // n_heads
+        self.inv_dk = 1.0 / float(self.d_k)
+        self.chunk_size = chunk_size
+        self.beta_mode = beta_mode
+        self.last_beta = None
+        self.norm1 = nn.LayerNorm(d_model)
+        self.norm2 = nn.LayerNorm(d_model)
+        self.norm_retrieved = nn.LayerNorm(d_model)
+        self.causal_conv = ShortCausalConv1D(d_model, kernel_size=conv_kernel_size)
+        self.w_k = nn.Linear(d_model, d_model)
+        self.w_q = nn.Linear(d_model, d_model)
+        self.w_v = nn.Linear(d_model, d_model)
+        self.w_beta = nn.Linear(d_model, n_heads)
+        self.out_proj = nn.Linear(d_model, d_model)
+        self.ffn = LearnableSubstrateLerpFFN(d_model, num_banks=num_banks)
+
+    def _gate_linear(self):
+        return self.w_beta
+
+    def _write_gate(self, g):
+        """beta = 2 sigmoid(w_beta(conv_x)) (layers.py:192-196), or 1 in "fixed" mode."""
+        if self.beta_mode == "fixed":
+            return torch.ones(g.shape, device=g.device, dtype=torch.float32)
+        return 2.0 * torch.sigmoid(g.float())
+
+    def _beta(self, conv_x):
+        beta = 2.0 * torch.sigmoid(self.w_beta(conv_x))
+        if self.beta_mode == "fixed":
+            beta = torch.ones_like(beta)
+        return beta
+
+
+class ComplexBetaDeltaPhaseBlock(_DeltaRuleBlock):
+    """Complex-beta Householder block (layers.py:294-418): beta_t = 1 + e^{i phi_t} with
+    phi = w_phi(conv_x), update M += beta (v - Re(M conj k) / d_k) k^T.  The reference
+    runs a token loop (layers.py:346-360); here the sequence goes through the chunkwise
+    (WY) form of the same recurrence on the tensor-core kernel (dp_core_cbeta_fwd) and
+    ``step`` through dp_core_cbeta_decode.  ``chunk_size`` is kept for the constructor's
+    signature; like the reference's loop, the result does not depend on it."""
+
+    _complex_beta = True
+
+    def __init__(self, d_model: int, n_heads: int = 4, conv_kernel_size: int = 4,
+                 chunk_size: int = 32, num_banks: int = 2):
+        super().__init__()
+        self.d_model = d_model
+        self.n_heads = n_heads
+        self.d_k = d_model // n_heads
+        self.inv_dk = 1.0 / float(self.d_k)
+        self.chunk_size = chunk_size
+        self.beta_mode = "complex"
+        self.norm1 = nn.LayerNorm(d_model)
+        self.norm2 = nn.LayerNorm(d_model)
+        self.norm_retrieved = nn.LayerNorm(d_model)
+        self.causal_conv = ShortCausalConv1D(d_model, kernel_size=conv_kernel_size)
+        self.w_k = nn.Linear(d_model, d_model, bias=False)
+        self.w_q = nn.Linear(d_model, d_model, bias=False)
+        self.w_v = nn.Linear(d_model, d_model, bias=False)
+        self.w_phi = nn.Linear(d_model, n_heads, bias=False)
+        self.out_proj = nn.Linear(d_model, d_model)
+        self.ffn = LearnableSubstrateLerpFFN(d_model, num_banks=num_banks)
+        self.last_beta = None
+
+    def _gate_linear(self):
+        return self.w_phi
+
+    def _write_gate(self, g):
+        """phi (float32); the kernels form beta = 1 + e^{i phi} (layers.py:344, 397)."""
+        return g.float()
+
+    def _last_beta(self, phi):
+        """beta_complex = 1 + polar(1, phi), as the reference records it (layers.py:345, 398)."""
+        with torch.no_grad():
+            return 1.0 + torch.polar(torch.ones_like(phi), phi)
 
 
 class LaplacePhaseCore(nn.Module):

@@ -1,8 +1,8 @@
 """DeltaPhase language model on the B200 blocks (drop-in for delta_phase/model.py:9-140).
 
-Same config fields, module names and weight init, so reference checkpoints load.  The
-``beta_mode="complex"`` Householder variant (ComplexBetaDeltaPhaseBlock) has no fused
-kernel and is not provided.
+Same config fields, module names and weight init, so reference checkpoints load.
+``beta_mode="complex"`` / ``"complex_householder"`` builds ComplexBetaDeltaPhaseBlock
+layers (model.py:38-45 of the reference), the others DeltaPhaseHolographicBlock.
 """
 from __future__ import annotations
 
@@ -12,7 +12,7 @@ from typing import List, Optional, Tuple
 import torch
 import torch.nn as nn
 
-from .layers import DeltaPhaseHolographicBlock
+from .layers import ComplexBetaDeltaPhaseBlock, DeltaPhaseHolographicBlock
 
 
 @dataclass
@@ -35,8 +35,6 @@ class DeltaPhaseModel(nn.Module):
 
     def __init__(self, config: DeltaPhaseConfig):
         super().__init__()
-        if config.beta_mode in ("complex", "complex_householder"):
-            raise NotImplementedError("the complex-beta Householder block has no B200 kernel")
         self.config = config
         if config.emb_dim and config.emb_dim > 0:
             self.embed = nn.Embedding(config.vocab_size, config.emb_dim)
@@ -46,12 +44,15 @@ class DeltaPhaseModel(nn.Module):
             self.embed = nn.Embedding(config.vocab_size, config.dim)
             self.embed_proj = None
             self.use_factorized = False
-        self.blocks = nn.ModuleList([
-            DeltaPhaseHolographicBlock(d_model=config.dim, n_heads=config.n_heads,
-                                       conv_kernel_size=config.conv_kernel_size,
-                                       chunk_size=config.chunk_size, num_banks=config.num_banks,
-                                       beta_mode=config.beta_mode)
-            for _ in range(config.n_layers)])
+        if config.beta_mode in ("complex", "complex_householder"):
+            make = lambda: ComplexBetaDeltaPhaseBlock(  # noqa: E731
+                d_model=config.dim, n_heads=config.n_heads, conv_kernel_size=config.conv_kernel_size,
+                chunk_size=config.chunk_size, num_banks=config.num_banks)
+        else:
+            make = lambda: DeltaPhaseHolographicBlock(  # noqa: E731
+                d_model=config.dim, n_heads=config.n_heads, conv_kernel_size=config.conv_kernel_size,
+                chunk_size=config.chunk_size, num_banks=config.num_banks, beta_mode=config.beta_mode)
+        self.blocks = nn.ModuleList([make() for _ in range(config.n_layers)])
         self.norm_f = nn.LayerNorm(config.dim)
         if self.use_factorized:
             self.head_proj = nn.Linear(config.dim, config.emb_dim, bias=False)

@@ -44,7 +44,9 @@ enum dp_status {
   DP_ERR_MISALIGNED = 3,       /* pointer/stride alignment a kernel requires   */
   DP_ERR_CUDA = 4,             /* launch or runtime error reported by CUDA     */
   DP_ERR_TIMEOUT = 5,          /* a device-side wait exceeded its bound        */
-  DP_ERR_WORKSPACE = 6         /* workspace too small                          */
+  DP_ERR_WORKSPACE = 6,        /* workspace too small                          */
+  DP_ERR_RANGE = 7             /* a value left the range of a kernel's 16-bit
+                                  operand tiles (reported by dp_device_error)   */
 };
 
 /* Library version string, e.g. "deltaphase_b200 0.1.0 (sm_100a)". */
@@ -54,8 +56,9 @@ DP_API const char *dp_last_error(void);
 /* Name of a status code. */
 DP_API const char *dp_status_string(int status);
 /* Synchronises the current device and returns the device-side error word (0, or
- * DP_ERR_TIMEOUT if a kernel's bounded wait expired since the last clear); clears it
- * when `clear` is non-zero.  Returns -1 if the CUDA runtime reports an error. */
+ * DP_ERR_TIMEOUT if a kernel's bounded wait expired, DP_ERR_RANGE if an operand left
+ * the fp16 range of dp_core_cbeta_fwd's tensor-core tiles, since the last clear); clears
+ * it when `clear` is non-zero.  Returns -1 if the CUDA runtime reports an error. */
 DP_API int dp_device_error(int clear);
 
 /*
@@ -106,6 +109,24 @@ DP_API int dp_phasor(const void *theta, int dtype, int64_t n, float *out, void *
 DP_API int dp_core_decode(const float *state_in, float *state_out, const void *theta_k,
                    const void *theta_q, const void *v, const void *beta, int in_dtype,
                    int beta_dtype, float *out, int B, int H, int D, int Dv,
+                   const int64_t *strides, void *stream);
+
+/*
+ * Complex-beta (Householder) variants: beta_t = 1 + e^{i phi_t} per (b, h, t), the
+ * update M += beta (v - Re(M conj(k))/D) k^T of ComplexBetaDeltaPhaseBlock
+ * (delta_phase/layers.py:294-418).  The reference runs it as a token loop
+ * (forward, layers.py:346-360; step, :402-407); dp_core_cbeta_fwd is its chunkwise
+ * (WY) form, dp_core_cbeta_decode one step.  Arguments, layouts, strides and limits are
+ * those of dp_core_fwd / dp_core_decode with `phi` (B, H, L) resp. (B, H) in place of
+ * beta; phi_dtype is its dtype code.
+ */
+DP_API int dp_core_cbeta_fwd(const void *theta_k, const void *theta_q, const void *v, const void *phi,
+                int in_dtype, int phi_dtype, const float *state_in, float *out,
+                float *state_out, int B, int H, int L, int D, int Dv, int chunk_size,
+                const int64_t *strides, void *stream);
+DP_API int dp_core_cbeta_decode(const float *state_in, float *state_out, const void *theta_k,
+                   const void *theta_q, const void *v, const void *phi, int in_dtype,
+                   int phi_dtype, float *out, int B, int H, int D, int Dv,
                    const int64_t *strides, void *stream);
 
 /*

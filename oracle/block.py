@@ -4,6 +4,8 @@ Reference: mcarbonell/delta-phase v1.3.0, delta_phase/layers.py.
 
 * :func:`block_forward` -- ``DeltaPhaseHolographicBlock.forward`` (layers.py:177-244)
 * :func:`block_step`    -- ``DeltaPhaseHolographicBlock.step``    (layers.py:246-291)
+* :func:`cb_block_forward`, :func:`cb_block_step` -- ``ComplexBetaDeltaPhaseBlock``
+  forward / step (layers.py:324-418)
 
 Parameters are a dict keyed by the reference ``state_dict`` names (norm1.weight,
 causal_conv.conv.weight, w_k.weight, ..., ffn.combine.weight, ffn.mat_dct, ...).
@@ -127,6 +129,51 @@ def block_step(x_t, params, n_heads, state=None, beta_mode="learned", dtype=np.f
     if M is None:
         M = np.zeros((B, n_heads, dk, dk), dtype=core._cplx(dtype))
     out, M = core.decode_step(M, tk, tq, v, beta, dtype)
+    rn = layer_norm(out.reshape(B, 1, d), _p(params, "norm_retrieved.weight", dtype),
+                    _p(params, "norm_retrieved.bias", dtype))
+    x1 = x_t + linear(rn, params, "out_proj", dtype)
+    n2 = layer_norm(x1, _p(params, "norm2.weight", dtype), _p(params, "norm2.bias", dtype))
+    return x1 + spectral.lerp_ffn(n2, ffn_params(params), dtype), (new_conv, M)
+
+
+def cb_block_forward(x, params, n_heads, memory_state=None, dtype=np.float64):
+    """``ComplexBetaDeltaPhaseBlock.forward`` (layers.py:324-366): LayerNorm, causal conv,
+    projections, phi = w_phi(conv_x), the complex-beta token loop, output projection and
+    FFN.  Returns ``(x_out, M_state)``."""
+    x = np.asarray(x, dtype=dtype)
+    B, L, d = x.shape
+    dk = d // n_heads
+    normed = layer_norm(x, _p(params, "norm1.weight", dtype), _p(params, "norm1.bias", dtype))
+    conv_x = causal_conv(normed, params, dtype)
+    tk = _heads(linear(conv_x, params, "w_k", dtype), B, L, n_heads, dk)
+    tq = _heads(linear(conv_x, params, "w_q", dtype), B, L, n_heads, dk)
+    v = _heads(linear(conv_x, params, "w_v", dtype), B, L, n_heads, dk)
+    phi = linear(conv_x, params, "w_phi", dtype).transpose(0, 2, 1)     # :336
+    out, M = core.complex_beta_recurrent(tk, tq, v, phi, memory_state, dtype)
+    retrieved = out.transpose(0, 2, 1, 3).reshape(B, L, d)
+    rn = layer_norm(retrieved, _p(params, "norm_retrieved.weight", dtype),
+                    _p(params, "norm_retrieved.bias", dtype))
+    x1 = x + linear(rn, params, "out_proj", dtype)
+    n2 = layer_norm(x1, _p(params, "norm2.weight", dtype), _p(params, "norm2.bias", dtype))
+    return x1 + spectral.lerp_ffn(n2, ffn_params(params), dtype), M
+
+
+def cb_block_step(x_t, params, n_heads, state=None, dtype=np.float64):
+    """``ComplexBetaDeltaPhaseBlock.step`` (layers.py:368-418).  x_t (B, 1, d);
+    state = (conv_state, M) or None.  Returns ``(x_out, (conv_state, M))``."""
+    x_t = np.asarray(x_t, dtype=dtype)
+    B, _, d = x_t.shape
+    dk = d // n_heads
+    conv_state, M = (None, None) if state is None else state
+    normed = layer_norm(x_t, _p(params, "norm1.weight", dtype), _p(params, "norm1.bias", dtype))
+    conv_x, new_conv = causal_conv_step(normed, conv_state, params, dtype)
+    tk = _heads(linear(conv_x, params, "w_k", dtype), B, 1, n_heads, dk)[:, :, 0]
+    tq = _heads(linear(conv_x, params, "w_q", dtype), B, 1, n_heads, dk)[:, :, 0]
+    v = _heads(linear(conv_x, params, "w_v", dtype), B, 1, n_heads, dk)[:, :, 0]
+    phi = linear(conv_x, params, "w_phi", dtype)[:, 0, :]
+    if M is None:
+        M = np.zeros((B, n_heads, dk, dk), dtype=core._cplx(dtype))
+    out, M = core.complex_beta_step(M, tk, tq, v, phi, dtype)
     rn = layer_norm(out.reshape(B, 1, d), _p(params, "norm_retrieved.weight", dtype),
                     _p(params, "norm_retrieved.bias", dtype))
     x1 = x_t + linear(rn, params, "out_proj", dtype)

@@ -10,6 +10,9 @@ Reference: mcarbonell/delta-phase v1.3.0.
   whole sequence; the reference's own definition of correctness
   (tests/test_equivalence.py:18-56).
 * :func:`decode_step`      -- one step of that recurrence (layers.py:279-285).
+* :func:`complex_beta_step`, :func:`complex_beta_recurrent` -- the complex-beta
+  Householder rule of ``ComplexBetaDeltaPhaseBlock`` (delta_phase/layers.py:294-418):
+  one token, and its token loop over a sequence (layers.py:346-360).
 * :func:`gram_matrix`      -- ``gram_matrix_reference``
   (triton_chunk_delta.py:192-208), the contract of the archived Triton Gram
   kernel (triton_chunk_delta.py:32-98).
@@ -150,6 +153,45 @@ def recurrent_delta(theta_k, theta_q, v, beta, initial_state=None, dtype=np.floa
     for t in range(L):
         out[:, :, t], M = decode_step(M, tk[:, :, t], np.asarray(theta_q)[:, :, t],
                                       np.asarray(v)[:, :, t], np.asarray(beta)[:, :, t], dtype)
+    return out, M
+
+
+def complex_beta_step(M, theta_k, theta_q, v, phi, dtype=np.float64):
+    """One token of ``ComplexBetaDeltaPhaseBlock`` (layers.py:402-407; the loop body of
+    its ``forward``, layers.py:354-360): beta = 1 + e^{i phi} (layers.py:344, 397),
+    v_old = Re(M conj(k)) / D, M <- M + beta (v - v_old) k^T, out = Re(M conj(q)) / D.
+
+    M (B,H,Dv,D) complex; theta_k/theta_q (B,H,D); v (B,H,Dv); phi (B,H).
+    Returns ``(out (B,H,Dv), M_new)``; the input state is not modified.
+    """
+    D = np.asarray(theta_k).shape[-1]
+    inv_dk = 1.0 / float(D)
+    cd = _cplx(dtype)
+    k = phasor(theta_k, dtype)
+    q = phasor(theta_q, dtype)
+    vv = np.asarray(v, dtype=dtype)
+    bt = (1.0 + phasor(phi, dtype)).astype(cd)
+    M = np.asarray(M, dtype=cd)
+    v_old = np.real(np.einsum("bhoc,bhc->bho", M, np.conj(k))) * inv_dk
+    err = (vv - v_old).astype(cd)
+    Mn = M + bt[..., None, None] * (err[..., :, None] * k[..., None, :])
+    out = np.real(np.einsum("bhoc,bhc->bho", Mn, np.conj(q))) * inv_dk
+    return out.astype(dtype), Mn
+
+
+def complex_beta_recurrent(theta_k, theta_q, v, phi, initial_state=None, dtype=np.float64):
+    """The token loop of ``ComplexBetaDeltaPhaseBlock.forward`` (layers.py:346-360) over
+    a whole sequence.  theta_k/theta_q/v (B,H,L,D), phi (B,H,L).
+    Returns ``(out (B,H,L,Dv), M (B,H,Dv,D) complex)``."""
+    tk = np.asarray(theta_k, dtype=dtype)
+    B, H, L, D = tk.shape
+    Dv = np.asarray(v).shape[-1]
+    M = (np.zeros((B, H, Dv, D), dtype=_cplx(dtype)) if initial_state is None
+         else np.array(initial_state, dtype=_cplx(dtype), copy=True))
+    out = np.empty((B, H, L, Dv), dtype=dtype)
+    for t in range(L):
+        out[:, :, t], M = complex_beta_step(M, tk[:, :, t], np.asarray(theta_q)[:, :, t],
+                                            np.asarray(v)[:, :, t], np.asarray(phi)[:, :, t], dtype)
     return out, M
 
 

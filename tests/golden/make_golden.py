@@ -4,7 +4,7 @@ Runs the UNMODIFIED reference package (mcarbonell/delta-phase v1.3.0, imported
 read-only from REFERENCE_ROOT, default /root/reference) on small seeded inputs and
 stores inputs + reference outputs as .npz.  The oracle in ``oracle/`` is pinned
 against these files by tests/test_oracle_golden.py; the GPU parity tests reuse
-them.  Usage:  python tests/golden/make_golden.py
+them.  Usage:  python tests/golden/make_golden.py [fixture ...]  (default: all of them)
 """
 from __future__ import annotations
 
@@ -21,7 +21,8 @@ sys.path.insert(0, REF)
 from delta_phase.kernels.triton_chunk_delta import (  # noqa: E402
     _chunkwise_delta_reference, gram_matrix_reference)
 from delta_phase.layers import (  # noqa: E402
-    DeltaPhaseHolographicBlock, LaplacePhaseCore, LearnableSubstrateLerpFFN)
+    ComplexBetaDeltaPhaseBlock, DeltaPhaseHolographicBlock, LaplacePhaseCore,
+    LearnableSubstrateLerpFFN)
 from delta_phase.spectral import (  # noqa: E402
     create_dct2_matrix, create_haar_matrix, create_hadamard_matrix)
 
@@ -225,10 +226,63 @@ def make_block():
     save("block", **arrays)
 
 
+def make_complex_beta():
+    """ComplexBetaDeltaPhaseBlock (layers.py:294-418) in fp64: block forward (from a zero
+    and from a random state) and the step loop.  Forward hooks record what the reference
+    itself feeds its token loop (the w_k / w_q / w_v / w_phi outputs) and what the loop
+    returns (the input of norm_retrieved), so the core is pinned on its own too."""
+    arrays = {}
+    cases = [(37, False, 1.0), (9, True, 3.0), (1, False, 1.0), (64, True, 1.0)]
+    for i, (L, init, phi_scale) in enumerate(cases):
+        torch.manual_seed(90 + i)
+        d, H = 64, 4
+        blk = ComplexBetaDeltaPhaseBlock(d_model=d, n_heads=H).double()
+        blk.eval()
+        with torch.no_grad():
+            blk.w_phi.weight.mul_(phi_scale)
+        x = torch.randn(2, L, d, dtype=torch.float64)
+        M0 = torch.randn(2, H, d // H, d // H, dtype=torch.complex128) if init else None
+        seen = {}
+
+        def keep(name):
+            def hook(mod, inp, out):
+                seen.setdefault(name, out.detach().clone())
+            return hook
+
+        hooks = [getattr(blk, n).register_forward_hook(keep(n)) for n in ("w_k", "w_q", "w_v", "w_phi")]
+        hooks.append(blk.norm_retrieved.register_forward_pre_hook(
+            lambda mod, inp: seen.setdefault("retrieved", inp[0].detach().clone())))
+        with torch.no_grad():
+            out, M = blk(x, memory_state=None if M0 is None else M0.clone())
+        for hk in hooks:
+            hk.remove()
+        with torch.no_grad():
+            st = None if M0 is None else (None, M0.clone())
+            outs = []
+            for t in range(L):
+                o, st = blk.step(x[:, t:t + 1], st)
+                outs.append(o)
+            out_s = torch.cat(outs, 1)
+        heads = lambda y: y.view(2, L, H, d // H).transpose(1, 2).numpy()  # noqa: E731
+        p = f"c{i}_"
+        arrays.update({p + "x": x.numpy(), p + "out": out.numpy(), p + "M": M.numpy(),
+                       p + "out_step": out_s.numpy(), p + "M_step": st[1].numpy(),
+                       p + "conv_state": st[0].numpy(),
+                       p + "theta_k": heads(seen["w_k"]), p + "theta_q": heads(seen["w_q"]),
+                       p + "v": heads(seen["w_v"]), p + "phi": seen["w_phi"].transpose(1, 2).numpy(),
+                       p + "retrieved": seen["retrieved"].view(2, L, H, d // H).transpose(1, 2).numpy()})
+        if M0 is not None:
+            arrays[p + "M0"] = M0.numpy()
+        for k, v in blk.state_dict().items():
+            arrays[p + "p_" + k] = v.numpy()
+    arrays["n_cases"] = len(cases)
+    arrays["n_heads"] = 4
+    save("complex_beta", **arrays)
+
+
+MAKERS = {"core": make_core, "gram": make_gram, "laplace": make_laplace, "spectral": make_spectral,
+          "ffn": make_ffn, "block": make_block, "complex_beta": make_complex_beta}
+
 if __name__ == "__main__":
-    make_core()
-    make_gram()
-    make_laplace()
-    make_spectral()
-    make_ffn()
-    make_block()
+    for name in (sys.argv[1:] or list(MAKERS)):
+        MAKERS[name]()

@@ -123,3 +123,36 @@ def test_block_forward_and_step_match_reference():
         assert ocore.rel_l2(np.concatenate(outs, 1), g[p + "out_step"]) < 1e-10
         assert ocore.rel_l2(st[1], g[p + "M_step"]) < 1e-10
         np.testing.assert_allclose(st[0], g[p + "conv_state"], atol=1e-12)
+
+
+def test_complex_beta_core_matches_reference():
+    """The complex-beta token loop (layers.py:346-360) on the inputs the reference's own
+    forward fed it, against what that loop returned."""
+    g = load("complex_beta")
+    for i in range(int(g["n_cases"])):
+        p = f"c{i}_"
+        M0 = g[p + "M0"] if p + "M0" in g.files else None
+        out, M = ocore.complex_beta_recurrent(g[p + "theta_k"], g[p + "theta_q"], g[p + "v"], g[p + "phi"], M0)
+        assert ocore.rel_l2(out, g[p + "retrieved"]) < 1e-12
+        assert ocore.rel_l2(M, g[p + "M"]) < 1e-12
+
+
+def test_complex_beta_block_forward_and_step_match_reference():
+    g = load("complex_beta")
+    H = int(g["n_heads"])
+    for i in range(int(g["n_cases"])):
+        p = f"c{i}_"
+        params = {k[len(p) + 2:]: g[k] for k in g.files if k.startswith(p + "p_")}
+        M0 = g[p + "M0"] if p + "M0" in g.files else None
+        out, M = oblock.cb_block_forward(g[p + "x"], params, n_heads=H, memory_state=M0)
+        assert ocore.rel_l2(out, g[p + "out"]) < 1e-10
+        assert ocore.rel_l2(M, g[p + "M"]) < 1e-10
+        x = g[p + "x"]
+        st = None if M0 is None else (None, M0)
+        outs = []
+        for t in range(x.shape[1]):
+            o, st = oblock.cb_block_step(x[:, t:t + 1], params, n_heads=H, state=st)
+            outs.append(o)
+        assert ocore.rel_l2(np.concatenate(outs, 1), g[p + "out_step"]) < 1e-10
+        assert ocore.rel_l2(st[1], g[p + "M_step"]) < 1e-10
+        np.testing.assert_allclose(st[0], g[p + "conv_state"], atol=1e-12)
