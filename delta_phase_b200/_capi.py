@@ -30,6 +30,9 @@ _SIG = {
     "dp_core_decode": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _P, _I, _I, _I, _I, _I64P, _P]),
     "dp_core_cbeta_fwd": (_I, [_P, _P, _P, _P, _I, _I, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I64P, _P]),
     "dp_core_cbeta_decode": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _P, _I, _I, _I, _I, _I64P, _P]),
+    "dp_core_bwd_workspace_size": (ctypes.c_size_t, [_I, _I, _I, _I]),
+    "dp_core_bwd": (_I, [_P, _P, _P, _P, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I64P,
+                         _P, ctypes.c_size_t, _P]),
     "dp_gram": (_I, [_P, _P, _I, _I, _P, _I, _I, _I, _P]),
     "dp_phasor": (_I, [_P, _I, ctypes.c_int64, _P, _P]),
     "dp_laplace_fwd": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _P, _P, _P, _I, _I, _I, _I, _I,
@@ -189,6 +192,29 @@ def core_decode(state_in, state_out, theta_k, theta_q, v, beta, out, complex_bet
                                   ptr(beta), dtype_code(theta_k), dtype_code(beta), ptr(out), B, H, D,
                                   Dv, strides_array(st), stream_of(dev))
     _check(name, rc)
+
+
+def core_bwd(theta_k, theta_q, v, beta, state_in, grad_out, grad_state_out, grad_theta_k, grad_theta_q,
+             grad_v, grad_beta, grad_state_in, complex_beta=False):
+    """dp_core_bwd.  theta_k/theta_q/v/beta as core_fwd; state tensors are float32 views of
+    complex64 states (B,H,Dv,D,2) or None; gradient outputs float32 contiguous."""
+    dev = require_cuda(theta_k, theta_q, v, beta, grad_out, grad_theta_k, grad_theta_q, grad_v, grad_beta)
+    B, H, L, D = theta_k.shape
+    Dv = v.shape[-1]
+    for t in (grad_out, grad_theta_k, grad_theta_q, grad_v, grad_beta):
+        if t.dtype != torch.float32 or not t.is_contiguous():
+            raise ValueError("gradient tensors must be contiguous float32")
+    st = []
+    for t in (theta_k, theta_q, v):
+        st += seq_strides(t)
+    st += (beta.stride(0), beta.stride(1), beta.stride(2))
+    ws = torch.empty(max(1, int(lib().dp_core_bwd_workspace_size(B, H, L, Dv))), device=dev, dtype=torch.uint8)
+    with torch.cuda.device(dev):
+        rc = lib().dp_core_bwd(ptr(theta_k), ptr(theta_q), ptr(v), ptr(beta), dtype_code(theta_k), dtype_code(beta),
+                               1 if complex_beta else 0, ptr(state_in), ptr(grad_out), ptr(grad_state_out),
+                               ptr(grad_theta_k), ptr(grad_theta_q), ptr(grad_v), ptr(grad_beta), ptr(grad_state_in),
+                               B, H, L, D, Dv, strides_array(st), ptr(ws), ws.numel(), stream_of(dev))
+    _check("dp_core_bwd", rc)
 
 
 def gram(theta, beta, out):

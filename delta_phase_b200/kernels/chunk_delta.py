@@ -8,7 +8,9 @@ Drop-in for ``delta_phase.kernels.triton_chunk_delta`` (mcarbonell/delta-phase v
   of ``chunk_size`` (the reference's ``view`` raises RuntimeError otherwise);
   ``initial_state`` is never modified.
 * :class:`DeltaPhaseCudaFunction` (alias ``DeltaPhaseTritonFunction``) -- the autograd
-  wrapper; like the reference's (:255-276) it is inference-only and its backward raises.
+  wrapper: forward on the fused kernels, backward on ``dp_core_bwd`` (the reference's
+  Function, :255-276, raises in backward and its dispatcher sends gradient-enabled calls
+  to the PyTorch path instead; here both directions run on the GPU kernels).
 * :func:`gram_matrix_cuda` (alias ``gram_matrix_triton``) -- the strictly-lower phasor
   Gram of the archived Triton kernel (:32-122).
 * :func:`decode_step` -- the fused single-token state update (layers.py:279-285).
@@ -106,22 +108,48 @@ def complex_beta_chunkwise(theta_k, theta_q, v, phi, initial_state=None):
     complex64 or None (never modified).  Any L.  Returns ``(out (B,H,L,D) float32,
     M (B,H,D,D) complex64)``.
     """
+    if torch.is_grad_enabled() and any(
+            t is not None and t.requires_grad for t in (theta_k, theta_q, v, phi, initial_state)):
+        return DeltaPhaseCudaFunction.apply(theta_k, theta_q, v, phi, 64, initial_state, True)
     with torch.no_grad():
         return chunkwise_forward(theta_k, theta_q, v, phi, 64, initial_state, complex_beta=True)
 
 
 class DeltaPhaseCudaFunction(torch.autograd.Function):
-    """Autograd wrapper of the fused forward.  Inference only, like the reference's
-    DeltaPhaseTritonFunction (triton_chunk_delta.py:255-276): backward raises."""
+    """Autograd wrapper of the chunkwise core: forward on dp_core_fwd (dp_core_cbeta_fwd
+    when ``complex_beta``), backward on dp_core_bwd, which returns the gradients of
+    theta_k, theta_q, v, beta (phi) and the initial state in the inputs' dtypes.  Same
+    call signature as the reference's DeltaPhaseTritonFunction (triton_chunk_delta.py:
+    255-276), whose backward raises; ``complex_beta`` is an extra trailing argument."""
 
     @staticmethod
-    def forward(ctx, theta_k, theta_q, v, beta, chunk_size=64, initial_state=None):
-        return chunkwise_forward(theta_k, theta_q, v, beta, chunk_size, initial_state)
+    def forward(ctx, theta_k, theta_q, v, beta, chunk_size=64, initial_state=None, complex_beta=False):
+        out, M = chunkwise_forward(theta_k, theta_q, v, beta, chunk_size, initial_state,
+                                   complex_beta=complex_beta)
+        ctx.save_for_backward(theta_k, theta_q, v, beta, initial_state)
+        ctx.complex_beta = bool(complex_beta)
+        return out, M
 
     @staticmethod
     def backward(ctx, grad_out, grad_final_state):
-        raise NotImplementedError(
-            "The B200 delta-phase kernels are inference-only: no backward pass is built.")
+        tk, tq, v, beta, M0 = ctx.saved_tensors
+        B, H, L, D = tk.shape
+        Dv = v.shape[-1]
+        dev = tk.device
+        go = (torch.zeros(B, H, L, Dv, device=dev, dtype=torch.float32) if grad_out is None
+              else grad_out.to(torch.float32).contiguous())
+        gM = (None if grad_final_state is None
+              else torch.view_as_real(grad_final_state.to(torch.complex64).contiguous()))
+        s_in = None if M0 is None else torch.view_as_real(M0.detach().to(torch.complex64).contiguous())
+        f32 = dict(device=dev, dtype=torch.float32)
+        dtk, dtq = torch.empty(B, H, L, D, **f32), torch.empty(B, H, L, D, **f32)
+        dv, db = torch.empty(B, H, L, Dv, **f32), torch.empty(B, H, L, **f32)
+        need_m0 = M0 is not None and ctx.needs_input_grad[5]
+        dM0 = torch.empty(B, H, Dv, D, device=dev, dtype=torch.complex64) if need_m0 else None
+        _capi.core_bwd(tk, tq, v, beta, s_in, go, gM, dtk, dtq, dv, db,
+                       None if dM0 is None else torch.view_as_real(dM0), complex_beta=ctx.complex_beta)
+        return (dtk.to(tk.dtype), dtq.to(tq.dtype), dv.to(v.dtype), db.to(beta.dtype), None,
+                None if dM0 is None else dM0.to(M0.dtype), None)
 
 
 DeltaPhaseTritonFunction = DeltaPhaseCudaFunction

@@ -10,9 +10,12 @@ load in both directions:
 * :class:`ComplexBetaDeltaPhaseBlock`   -- layers.py:294-418 (CUDA: dp_core_cbeta_fwd/dp_core_cbeta_decode)
 * :class:`LaplacePhaseCore`             -- layers.py:422-583 (CUDA: dp_laplace_fwd)
 
-LayerNorms, the causal conv and the projections stay torch (cuBLAS) calls; the
-delta-rule core, its decode step and the spectral FFN run in the CUDA library, with no
-CPU fallback.  The modules are inference-only: the fused core has no backward.
+The delta-rule core, its decode step, the block glue and the spectral FFN run in the
+CUDA library, with no CPU fallback.  Training: when autograd is recording (grad enabled
+and an input or parameter requires grad -- the reference dispatcher's rule,
+triton_chunk_delta.py:279-291), the two delta-rule blocks run their glue and the FFN as
+differentiable torch ops and the core through DeltaPhaseCudaFunction (backward on the
+dp_core_bwd kernel).  LaplacePhaseCore has no backward.
 """
 from __future__ import annotations
 
@@ -21,10 +24,19 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from . import _capi
-from .kernels.chunk_delta import chunkwise_forward, decode_step, laplace_chunkwise
+from .kernels.chunk_delta import DeltaPhaseCudaFunction, chunkwise_forward, decode_step, laplace_chunkwise
 from .spectral import create_dct2_matrix, create_haar_matrix, create_hadamard_matrix
 
 _BRANCHES = ("fwht", "dct", "haar")
+
+
+def _records_autograd(module: nn.Module, *tensors) -> bool:
+    """True when autograd would record this call: grad enabled and an input or a
+    parameter of ``module`` requires grad."""
+    if not torch.is_grad_enabled():
+        return False
+    return any(t is not None and t.requires_grad for t in tensors) or \
+        any(p.requires_grad for p in module.parameters())
 
 
 class ShortCausalConv1D(nn.Module):
@@ -104,11 +116,27 @@ class LearnableSubstrateLerpFFN(nn.Module):
             self._fold[dtype] = (Fm.to(dtype), dct.to(dtype))
         return self._fold[dtype]
 
+    def _forward_autograd(self, x: torch.Tensor) -> torch.Tensor:
+        """The reference's formula (layers.py:119-141) as differentiable torch ops, for
+        training (the folded CUDA path has no backward)."""
+        weights = F.softmax(self.substrate_logits, dim=0)
+        out = 0.0
+        for i, b in enumerate(_BRANCHES):
+            mat = getattr(self, f"mat_{b}")
+            h = F.linear(x, mat).unsqueeze(-2)
+            a = (torch.cos(h + getattr(self, f"phi1_{b}")) * getattr(self, f"w1_{b}") +
+                 torch.sin(h + getattr(self, f"phi2_{b}")) * getattr(self, f"w2_{b}")).flatten(-2)
+            out = out + weights[i] * F.linear(self.combine(a), mat.t())
+        return out
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         if x.shape[-1] != self.d_model:
             raise ValueError(f"expected last dim {self.d_model}, got {x.shape[-1]}")
         if x.dtype == torch.float64:
             raise TypeError("float64 inputs are not supported by the CUDA path")
+        if _records_autograd(self, x):
+            _capi.require_cuda(x, self.mat_dct)
+            return self._forward_autograd(x)
         _capi.require_cuda(x, self.mat_dct)
         cdt = torch.bfloat16 if x.dtype == torch.bfloat16 else torch.float32
         out_dt = x.dtype
@@ -165,15 +193,38 @@ class _DeltaRuleBlock(nn.Module):
             self._proj_key = key
         return self._proj_cache
 
+    def _forward_autograd(self, x: torch.Tensor, memory_state=None):
+        """Differentiable block forward for training: the reference's sequence of torch
+        ops around the core (layers.py:177-244 / 324-366) with the core through
+        DeltaPhaseCudaFunction (CUDA forward and backward)."""
+        B, L, D = x.shape
+        H, dk = self.n_heads, self.d_k
+        conv_x = self.causal_conv(self.norm1(x))
+        tk = self.w_k(conv_x).view(B, L, H, dk).transpose(1, 2)
+        tq = self.w_q(conv_x).view(B, L, H, dk).transpose(1, 2)
+        v = self.w_v(conv_x).view(B, L, H, dk).transpose(1, 2)
+        beta = self._write_gate(self._gate_linear()(conv_x)).transpose(1, 2)   # (B, H, L)
+        if tk.dtype != tq.dtype or tk.dtype != v.dtype:
+            tq, v = tq.to(tk.dtype), v.to(tk.dtype)
+        out, M_state = DeltaPhaseCudaFunction.apply(tk, tq, v, beta, self.chunk_size, memory_state,
+                                                    self._complex_beta)
+        self.last_beta = self._last_beta(beta)
+        retrieved = out.transpose(1, 2).reshape(B, L, D)
+        x = x + self.out_proj(self.norm_retrieved(retrieved))
+        return x + self.ffn(self.norm2(x)), M_state
+
     def forward(self, x: torch.Tensor, memory_state=None):
         """Block forward (layers.py:177-244) on fused kernels: LayerNorm + causal conv +
         SiLU + residual in one pass, the four input projections as one GEMM, the
         delta-rule core, LayerNorm -> output projection, and the residual add fused into
         norm2.  GEMM operands are bf16 under bf16 autocast (like the reference's autocast
-        matmuls) and float32 otherwise; the residual stream stays float32."""
+        matmuls) and float32 otherwise; the residual stream stays float32.  When autograd
+        records (training), the differentiable path above runs instead."""
         if x.dtype == torch.float64:
             raise TypeError("float64 inputs are not supported by the CUDA path")
         _capi.require_cuda(x)
+        if _records_autograd(self, x, memory_state):
+            return self._forward_autograd(x, memory_state)
         B, L, D = x.shape
         H, dk = self.n_heads, self.d_k
         bf16_ac = torch.is_autocast_enabled(x.device.type) and \

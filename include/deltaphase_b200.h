@@ -85,6 +85,36 @@ DP_API int dp_core_fwd(const void *theta_k, const void *theta_q, const void *v, 
                 const int64_t *strides, void *stream);
 
 /*
+ * Backward of the chunkwise core (training): gradients with respect to theta_k, theta_q,
+ * v, beta and the initial state, given grad_out = dL/d out and grad_state_out = dL/dM
+ * (or NULL = 0).  The reference trains through autograd of its PyTorch chunkwise path
+ * (delta_phase/kernels/triton_chunk_delta.py:211-252, dispatched at :279-291; its
+ * DeltaPhaseTritonFunction.backward, :271-276, raises) and of the complex-beta token loop
+ * (delta_phase/layers.py:346-360); this is the adjoint of the same recurrence, in fp32.
+ *
+ *   theta_k, theta_q, v, beta : as dp_core_fwd (complex_beta != 0: beta holds phi, the
+ *                               gradient written is d phi)
+ *   state_in                  : (B, H, Dv, D) complex64 initial state or NULL (= zero)
+ *   grad_out                  : (B, H, L, Dv) float32, contiguous
+ *   grad_state_out            : (B, H, Dv, D) complex64 (as interleaved floats) or NULL
+ *   grad_theta_k, grad_theta_q: (B, H, L, D) float32, contiguous
+ *   grad_v                    : (B, H, L, Dv) float32, contiguous
+ *   grad_beta                 : (B, H, L) float32, contiguous
+ *   grad_state_in             : (B, H, Dv, D) complex64 (as floats) or NULL
+ *   strides[12]               : {sb, sh, st} of theta_k, theta_q, v, beta
+ *   workspace                 : dp_core_bwd_workspace_size(B, H, L, Dv) bytes
+ * Complex gradients follow PyTorch's convention (dL/dRe + i dL/dIm).  Limits:
+ * 1 <= D, Dv <= 64.
+ */
+DP_API size_t dp_core_bwd_workspace_size(int B, int H, int L, int Dv);
+DP_API int dp_core_bwd(const void *theta_k, const void *theta_q, const void *v, const void *beta,
+                int in_dtype, int beta_dtype, int complex_beta, const float *state_in,
+                const float *grad_out, const float *grad_state_out, float *grad_theta_k,
+                float *grad_theta_q, float *grad_v, float *grad_beta, float *grad_state_in,
+                int B, int H, int L, int D, int Dv, const int64_t *strides, void *workspace,
+                size_t workspace_bytes, void *stream);
+
+/*
  * Phasors e^{i theta} = cos theta + i sin theta of n phases, written as interleaved
  * complex64 (out[2i] = cos, out[2i+1] = sin).  The elementwise step of
  * DeltaPhaseHolographicBlock.forward/step (delta_phase/layers.py:203-206, 275-278) and

@@ -280,8 +280,95 @@ def make_complex_beta():
     save("complex_beta", **arrays)
 
 
+def make_grad():
+    """Gradients, as the reference trains: autograd (float64) of _chunkwise_delta_reference
+    (triton_chunk_delta.py:211-252) for the real beta, and of the two blocks for a seeded
+    loss sum(out * R) + Re sum(conj(dM) M) -- with forward hooks recording the core's
+    inputs, their gradients and the gradient reaching the core's output (the input of
+    norm_retrieved), plus every parameter's gradient."""
+    arrays = {}
+    cases = [(1, 2, 64, 16, 16, True, True), (2, 1, 96, 32, 32, False, False), (1, 1, 8, 8, 8, True, True)]
+    for i, (B, H, L, D, C, init, with_dM) in enumerate(cases):
+        rng = np.random.default_rng(300 + i)
+        tk, tq, v, beta = core_inputs(rng, B, H, L, D)
+        dout = rng.standard_normal((B, H, L, D))
+        M0 = (rng.standard_normal((B, H, D, D)) + 1j * rng.standard_normal((B, H, D, D))) if init else None
+        dM = (rng.standard_normal((B, H, D, D)) + 1j * rng.standard_normal((B, H, D, D))) if with_dM else None
+        t = [torch.from_numpy(np.asarray(a, np.float64)).requires_grad_(True) for a in (tk, tq, v, beta)]
+        m0 = None if M0 is None else torch.from_numpy(M0).requires_grad_(True)
+        out, M = _chunkwise_delta_reference(*t, C, m0)
+        outs, gos = [out], [torch.from_numpy(dout)]
+        if dM is not None:
+            outs.append(M)
+            gos.append(torch.from_numpy(dM))
+        grads = torch.autograd.grad(outs, t + ([m0] if m0 is not None else []), gos)
+        p = f"c{i}_"
+        arrays.update({p + "theta_k": tk, p + "theta_q": tq, p + "v": v, p + "beta": beta, p + "dout": dout,
+                       p + "C": C, p + "d_theta_k": grads[0].numpy(), p + "d_theta_q": grads[1].numpy(),
+                       p + "d_v": grads[2].numpy(), p + "d_beta": grads[3].numpy()})
+        if M0 is not None:
+            arrays[p + "M0"] = M0
+            arrays[p + "d_M0"] = grads[4].numpy()
+        if dM is not None:
+            arrays[p + "dM"] = dM
+    arrays["n_cases"] = len(cases)
+
+    # the two blocks: parameter gradients and the core's own view of them
+    for name, make in (("hb", lambda: DeltaPhaseHolographicBlock(d_model=32, n_heads=2, chunk_size=8)),
+                       ("cb", lambda: ComplexBetaDeltaPhaseBlock(d_model=32, n_heads=2))):
+        torch.manual_seed(77)
+        blk = make().double()
+        blk.train()
+        H, dk, L = 2, 16, 20
+        x = torch.randn(2, L, 32, dtype=torch.float64)
+        R = torch.randn(2, L, 32, dtype=torch.float64)
+        M0 = torch.randn(2, H, dk, dk, dtype=torch.complex128).requires_grad_(True)
+        dM = torch.randn(2, H, dk, dk, dtype=torch.complex128)
+        seen = {}
+
+        def keep(nm):
+            def hook(mod, inp, out):
+                out.retain_grad()
+                seen.setdefault(nm, out)
+            return hook
+
+        def keep_in(mod, inp):
+            inp[0].retain_grad()
+            seen.setdefault("retrieved", inp[0])
+
+        gate = "w_beta" if name == "hb" else "w_phi"
+        hooks = [getattr(blk, n).register_forward_hook(keep(n)) for n in ("w_k", "w_q", "w_v", gate)]
+        hooks.append(blk.norm_retrieved.register_forward_pre_hook(keep_in))
+        out, M = blk(x, memory_state=M0)
+        loss = (out * R).sum() + (torch.conj(dM) * M).real.sum()
+        loss.backward()
+        for hk in hooks:
+            hk.remove()
+        Lp = seen["w_k"].shape[1]  # the holographic block pads L to a chunk multiple (layers.py:185-190)
+        heads = lambda y: y.view(2, Lp, H, dk).transpose(1, 2).detach().numpy()  # noqa: E731
+        dret = seen["retrieved"].grad.view(2, L, H, dk).transpose(1, 2).numpy()
+        dout = np.zeros((2, H, Lp, dk))
+        dout[:, :, :L] = dret
+        p = name + "_"
+        arrays.update({p + "x": x.numpy(), p + "R": R.numpy(), p + "M0": M0.detach().numpy(), p + "dM": dM.numpy(),
+                       p + "out": out.detach().numpy(), p + "M": M.detach().numpy(),
+                       p + "d_M0": M0.grad.numpy(),
+                       p + "theta_k": heads(seen["w_k"]), p + "theta_q": heads(seen["w_q"]),
+                       p + "v": heads(seen["w_v"]),
+                       p + "d_theta_k": heads(seen["w_k"].grad), p + "d_theta_q": heads(seen["w_q"].grad),
+                       p + "d_v": heads(seen["w_v"].grad),
+                       p + "gate_raw": seen[gate].transpose(1, 2).detach().numpy(),
+                       p + "d_gate_raw": seen[gate].grad.transpose(1, 2).numpy(),
+                       p + "dout": dout, p + "L": L})
+        for k, v in blk.state_dict().items():
+            arrays[p + "p_" + k] = v.numpy()
+        for k, prm in blk.named_parameters():
+            arrays[p + "g_" + k] = prm.grad.numpy()
+    save("grad", **arrays)
+
+
 MAKERS = {"core": make_core, "gram": make_gram, "laplace": make_laplace, "spectral": make_spectral,
-          "ffn": make_ffn, "block": make_block, "complex_beta": make_complex_beta}
+          "ffn": make_ffn, "block": make_block, "complex_beta": make_complex_beta, "grad": make_grad}
 
 if __name__ == "__main__":
     for name in (sys.argv[1:] or list(MAKERS)):

@@ -156,3 +156,42 @@ def test_complex_beta_block_forward_and_step_match_reference():
         assert ocore.rel_l2(np.concatenate(outs, 1), g[p + "out_step"]) < 1e-10
         assert ocore.rel_l2(st[1], g[p + "M_step"]) < 1e-10
         np.testing.assert_allclose(st[0], g[p + "conv_state"], atol=1e-12)
+
+
+def _beta_from_raw(raw, L):
+    """beta as the holographic block feeds its core: 2 sigmoid(w_beta(conv_x)), 0 on the
+    padded tail (layers.py:192-201); and d beta / d raw."""
+    sig = 1.0 / (1.0 + np.exp(-raw))
+    beta, dbeta = 2.0 * sig, 2.0 * sig * (1.0 - sig)
+    beta[:, :, L:] = 0.0
+    dbeta[:, :, L:] = 0.0
+    return beta, dbeta
+
+
+def test_autograd_oracle_matches_reference_gradients():
+    """oracle.autograd (token recurrences under torch autograd) against the gradients the
+    reference itself produced (chunkwise path and both blocks)."""
+    from oracle import autograd as oag
+    g = load("grad")
+    for i in range(int(g["n_cases"])):
+        p = f"c{i}_"
+        M0 = g[p + "M0"] if p + "M0" in g.files else None
+        dM = g[p + "dM"] if p + "dM" in g.files else None
+        d = oag.core_grads(g[p + "theta_k"], g[p + "theta_q"], g[p + "v"], g[p + "beta"], g[p + "dout"], dM, M0)
+        for k, name in enumerate(("d_theta_k", "d_theta_q", "d_v", "d_beta")):
+            assert ocore.rel_l2(d[k], g[p + name]) < 1e-10, (i, name)
+        if M0 is not None:
+            assert ocore.rel_l2(d[4], g[p + "d_M0"]) < 1e-10
+    # holographic block: beta = 2 sigmoid(raw) with the pad masked
+    beta, dbeta = _beta_from_raw(g["hb_gate_raw"], int(g["hb_L"]))
+    d = oag.core_grads(g["hb_theta_k"], g["hb_theta_q"], g["hb_v"], beta, g["hb_dout"], g["hb_dM"], g["hb_M0"])
+    for k, name in enumerate(("d_theta_k", "d_theta_q", "d_v")):
+        assert ocore.rel_l2(d[k], g["hb_" + name]) < 1e-10, name
+    assert ocore.rel_l2(d[3] * dbeta, g["hb_d_gate_raw"]) < 1e-10
+    assert ocore.rel_l2(d[4], g["hb_d_M0"]) < 1e-10
+    # complex-beta block: phi is the raw gate
+    d = oag.complex_beta_grads(g["cb_theta_k"], g["cb_theta_q"], g["cb_v"], g["cb_gate_raw"], g["cb_dout"],
+                               g["cb_dM"], g["cb_M0"])
+    for k, name in enumerate(("d_theta_k", "d_theta_q", "d_v", "d_gate_raw")):
+        assert ocore.rel_l2(d[k], g["cb_" + name]) < 1e-10, name
+    assert ocore.rel_l2(d[4], g["cb_d_M0"]) < 1e-10
