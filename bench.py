@@ -6,7 +6,7 @@ each GPU (batch x head sharding, weak scaling: global batch = 8 x n_gpus; no
 collective on the data path).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload core|cbeta|decode|laplace|laplace-sp|ffn|lm]
+                    [--workload core|cbeta|train|decode|laplace|laplace-sp|ffn|lm]
 
 Multi-GPU: launch with torch.distributed.run (one process per GPU); rank 0 prints one
 JSON line.  ``--impl reference`` times the reference algorithm's CPU restatement
@@ -386,6 +386,42 @@ def run_cbeta(args, world, rank, local):
     return line
 
 
+def run_train(args, world, rank, local):
+    """Training step of the chunkwise core at config 2 (B=8, H=16, L=8192, d_k=64, bf16
+    phases/values): forward (tensor-core kernel) and backward (dp_core_bwd) through
+    DeltaPhaseCudaFunction, gradients of theta_k, theta_q, v and beta."""
+    import torch
+    from delta_phase_b200.kernels import DeltaPhaseCudaFunction
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    B, H, L, D = (CORE[k] for k in ("B", "H", "L", "D"))
+    tk, tq, v, beta = make_core_inputs(dev, 5000 + rank, B, H, L, D)
+    ins = [t.requires_grad_(True) for t in (tk, tq, v, beta)]
+    g = torch.Generator(device=dev).manual_seed(6000 + rank)
+    dout = torch.randn(B, H, L, D, device=dev, generator=g)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        out, _ = DeltaPhaseCudaFunction.apply(*ins, 64, None, False)
+        torch.autograd.grad(out, ins, dout)
+
+    barrier(world)
+    clocks = ClockSampler(local)
+    clocks.start()
+    ms = _timed(step, args.steps, args.warmup, stream)
+    clk = clocks.stop()
+    ms_max = max_over_ranks(ms, world)
+    line = _line("delta-core training step tokens/s (fwd+bwd, H=16,d_k=64,L=8K)", world * B * L / (ms_max / 1e3),
+                 "tokens/s", args, world, ms_max,
+                 {"workload": "chunkwise core forward + backward (dp_core_fwd + dp_core_bwd), B=8,H=16,L=8192,"
+                              "d_k=64 per GPU, bf16 in, fp32 gradients",
+                  "global_batch": B * world, "seq_len": L, "heads": H, "d_k": D,
+                  "parallelism": f"batch x head sharding over {world} GPU(s), no collective"},
+                 gpu_launches=2 * args.steps, clocks=clk)
+    line["roofline"] = None
+    return line
+
+
 def run_laplace(args, world, rank, local):
     """LaplacePhaseCore chunk solve at B=4, H=16, L=32768, d_k=64 (gated decay:
     log r = -softplus(N(0,1)), unit phasors, bf16 inputs)."""
@@ -635,7 +671,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="core",
-                    choices=["core", "cbeta", "laplace", "laplace-sp", "ffn", "decode", "lm"])
+                    choices=["core", "cbeta", "train", "laplace", "laplace-sp", "ffn", "decode", "lm"])
     ap.add_argument("--decode-steps", type=int, default=256)
     ap.add_argument("--seq-len", type=int, default=32768,
                     help="laplace workload only: sequence length (the headline is 32768; smaller for profiling)")
@@ -652,7 +688,7 @@ def main():
             print(json.dumps(line), flush=True)
         return
     world, rank, local = dist_setup(args.gpus)
-    run = {"core": run_core, "cbeta": run_cbeta, "laplace": run_laplace, "laplace-sp": run_laplace_sp,
+    run = {"core": run_core, "cbeta": run_cbeta, "train": run_train, "laplace": run_laplace, "laplace-sp": run_laplace_sp,
            "ffn": run_ffn, "decode": run_decode, "lm": run_lm}[args.workload]
     line = run(args, world, rank, local)
     if rank == 0:
