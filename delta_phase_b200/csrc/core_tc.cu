@@ -359,46 +359,36 @@ __device__ bool prep_role(const TcArgs &a, uint8_t *smem, Bars *bars, uint32_t t
     if (CB && q < 2) {
       // row i of K W^T: A[i][k] = G1[i][k] / 64 for k < i, stored as column i of A^T
       const int i = q * 32 + lane;
+      float g[32];
+      tmem_ld32_sync(tmem + lane_base + COL_D1 + 32 * hf, g);
 #pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        float g[16];
-        const int c0 = 32 * hf + 16 * u;
-        tmem_ld16(tmem + lane_base + COL_D1 + c0, g);
-        tmem_ld_wait();
-#pragma unroll
-        for (int kk = 0; kk < 16; ++kk) at[(c0 + kk) * LDA + i] = (c0 + kk < i) ? g[kk] * inv64 : 0.f;
-      }
+      for (int kk = 0; kk < 32; ++kk) at[(32 * hf + kk) * LDA + i] = (32 * hf + kk < i) ? g[kk] * inv64 : 0.f;
     } else if (q < 2) {
       const int k = q * 32 + lane;
       const float bk = bs[k] * inv64;
+      float g[32];
+      tmem_ld32_sync(tmem + lane_base + COL_D1 + 32 * hf, g);
 #pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        float g[16];
-        const int c0 = 32 * hf + 16 * u;
-        tmem_ld16(tmem + lane_base + COL_D1 + c0, g);
-        tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 16; i += 4) {
-          float4 w;
-          w.x = (c0 + i + 0 > k) ? g[i + 0] * bk : 0.f;
-          w.y = (c0 + i + 1 > k) ? g[i + 1] * bk : 0.f;
-          w.z = (c0 + i + 2 > k) ? g[i + 2] * bk : 0.f;
-          w.w = (c0 + i + 3 > k) ? g[i + 3] * bk : 0.f;
-          *reinterpret_cast<float4 *>(at + k * LDA + c0 + i) = w;
-        }
+      for (int i = 0; i < 32; i += 4) {
+        const int c0 = 32 * hf;
+        float4 w;
+        w.x = (c0 + i + 0 > k) ? g[i + 0] * bk : 0.f;
+        w.y = (c0 + i + 1 > k) ? g[i + 1] * bk : 0.f;
+        w.z = (c0 + i + 2 > k) ? g[i + 2] * bk : 0.f;
+        w.w = (c0 + i + 3 > k) ? g[i + 3] * bk : 0.f;
+        *reinterpret_cast<float4 *>(at + k * LDA + c0 + i) = w;
       }
     } else {
       const int t = (q - 2) * 32 + lane;
+      float p[32];
+      tmem_ld32_sync(tmem + lane_base + COL_D1 + 32 * hf, p);
 #pragma unroll
       for (int u = 0; u < 2; ++u) {
-        float p[16];
         const int c0 = 32 * hf + 16 * u;
-        tmem_ld16(tmem + lane_base + COL_D1 + c0, p);
-        tmem_ld_wait();
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
           const int s = c0 + 8 * half;
-          const float *pp = p + 8 * half;
+          const float *pp = p + 16 * u + 8 * half;
           const float ps = CB ? inv64 : 1.f;  // fp16 tiles hold P / 64
           uint4 w;
           w.x = pack_op<CB>(s + 0 <= t ? pp[0] * ps : 0.f, s + 1 <= t ? pp[1] * ps : 0.f);
@@ -408,6 +398,7 @@ __device__ bool prep_role(const TcArgs &a, uint8_t *smem, Bars *bars, uint32_t t
           *reinterpret_cast<uint4 *>(pb + cm_off(t, s, RG_64)) = w;
         }
       }
+      fence_proxy_async_smem();  // P is an MMA operand of the chain (G5)
     }
     tc_fence_before();
     group_sync(BAR_PREP, kPrepThreads);
@@ -470,8 +461,8 @@ __device__ bool prep_role(const TcArgs &a, uint8_t *smem, Bars *bars, uint32_t t
         reinterpret_cast<float *>(smem + OFF_BSLOT)[slot * kC + tid] = bs[tid];
       }
     }
-    // T, beta, P, V and K, Q of this slot are ready for the chain
-    fence_proxy_async_smem();
+    // T, beta, P, V and K, Q of this slot are ready for the chain (the tiles that MMAs read
+    // were fenced for the async proxy where they were written)
     tc_fence_before();
     group_sync(BAR_PREP, kPrepThreads);
     if (tid == 0) mbar_arrive(&bars->ready[slot]);
@@ -532,15 +523,13 @@ __device__ bool chain_role(const TcArgs &a, uint8_t *smem, Bars *bars, uint32_t 
     tc_fence_after();
 
     // ---- C1: S^T (fp32, TMEM) -> bf16 operand tile
+    {
+      float sv[64];
+      tmem_ld64_sync(tmem + lane_base + COL_S, sv);
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      float sv[16];
-      tmem_ld16(tmem + lane_base + COL_S + 16 * u, sv);
-      tmem_ld_wait();
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        const float *ss = sv + 8 * half;
-        *reinterpret_cast<uint4 *>(s0 + cm_off(j, 16 * u + 8 * half, RG_64)) =
+      for (int u8 = 0; u8 < 8; ++u8) {
+        const float *ss = sv + 8 * u8;
+        *reinterpret_cast<uint4 *>(s0 + cm_off(j, 8 * u8, RG_64)) =
             make_uint4(pack_chk<CB>(ss[0] * ss64, ss[1] * ss64, over), pack_chk<CB>(ss[2] * ss64, ss[3] * ss64, over),
                        pack_chk<CB>(ss[4] * ss64, ss[5] * ss64, over), pack_chk<CB>(ss[6] * ss64, ss[7] * ss64, over));
       }
@@ -583,27 +572,23 @@ __device__ bool chain_role(const TcArgs &a, uint8_t *smem, Bars *bars, uint32_t 
     //      before the triangular factor, so the prep role needs no bT [K | V] product.
     if (cw < 2) {
       const int t = 32 * cw + lane;
+      float ks[64];
+      tmem_ld64_sync(tmem + lane_base + COL_R3, ks);
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        float ks[16];
-        tmem_ld16(tmem + lane_base + COL_R3 + 16 * u, ks);
-        tmem_ld_wait();
+      for (int u8 = 0; u8 < 8; ++u8) {
+        uint4 *vp = reinterpret_cast<uint4 *>(vs + cm_off(t, 8 * u8, RG_64));
+        const uint4 vr = *vp;
+        const uint32_t vw[4] = {vr.x, vr.y, vr.z, vr.w};
+        uint32_t ew[4];
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          uint4 *vp = reinterpret_cast<uint4 *>(vs + cm_off(t, 16 * u + 8 * half, RG_64));
-          const uint4 vr = *vp;
-          const uint32_t vw[4] = {vr.x, vr.y, vr.z, vr.w};
-          uint32_t ew[4];
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const float2 vv = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&vw[i]));
-            if (CB)  // the state-read rows already carry the 1 / 64
-              ew[i] = pack_chk<true>(vv.x - ks[8 * half + 2 * i], vv.y - ks[8 * half + 2 * i + 1], over);
-            else
-              ew[i] = pack_bf16(vv.x - ks[8 * half + 2 * i] * inv64, vv.y - ks[8 * half + 2 * i + 1] * inv64);
-          }
-          *vp = make_uint4(ew[0], ew[1], ew[2], ew[3]);
+        for (int i = 0; i < 4; ++i) {
+          const float2 vv = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&vw[i]));
+          if (CB)  // the state-read rows already carry the 1 / 64
+            ew[i] = pack_chk<true>(vv.x - ks[8 * u8 + 2 * i], vv.y - ks[8 * u8 + 2 * i + 1], over);
+          else
+            ew[i] = pack_bf16(vv.x - ks[8 * u8 + 2 * i] * inv64, vv.y - ks[8 * u8 + 2 * i + 1] * inv64);
         }
+        *vp = make_uint4(ew[0], ew[1], ew[2], ew[3]);
       }
     } else {
       // bT = diag(beta) T -> bf16 (row i = lane of chain warps 2, 3), beside E
@@ -655,19 +640,15 @@ __device__ bool chain_role(const TcArgs &a, uint8_t *smem, Bars *bars, uint32_t 
     // ---- C3c: U -> bf16 operand tile (M=64 rows: lanes < 16 of each quarter)
     {
       const int t = 16 * cw + lane;
+      float uv[64];
+      tmem_ld64_sync(tmem + lane_base + COL_RU, uv);
+      if (lane < 16) {
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        float uv[16];
-        tmem_ld16(tmem + lane_base + COL_RU + 16 * u, uv);
-        tmem_ld_wait();
-        if (lane < 16) {
-#pragma unroll
-          for (int half = 0; half < 2; ++half) {
-            const float *uu = uv + 8 * half;
-            *reinterpret_cast<uint4 *>(ub + cm_off(t, 16 * u + 8 * half, RG_64)) =
-                make_uint4(pack_chk<CB>(uu[0], uu[1], over), pack_chk<CB>(uu[2], uu[3], over),
-                           pack_chk<CB>(uu[4], uu[5], over), pack_chk<CB>(uu[6], uu[7], over));
-          }
+        for (int u8 = 0; u8 < 8; ++u8) {
+          const float *uu = uv + 8 * u8;
+          *reinterpret_cast<uint4 *>(ub + cm_off(t, 8 * u8, RG_64)) =
+              make_uint4(pack_chk<CB>(uu[0], uu[1], over), pack_chk<CB>(uu[2], uu[3], over),
+                         pack_chk<CB>(uu[4], uu[5], over), pack_chk<CB>(uu[6], uu[7], over));
         }
       }
     }
@@ -703,17 +684,13 @@ __device__ bool chain_role(const TcArgs &a, uint8_t *smem, Bars *bars, uint32_t 
       const float ss64_out = CB ? 1.f : inv64;
       const int t = 32 * (cw - 2) + lane;
       float *orow = a.out + b * a.s_out.b + h * a.s_out.h + (int64_t)(t0 + t) * a.s_out.t;
+      float o[64];
+      tmem_ld64_sync(tmem + lane_base + COL_R3, o);
+      if (t < nvalid) {
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        float o[16];
-        tmem_ld16(tmem + lane_base + COL_R3 + 16 * u, o);
-        tmem_ld_wait();
-        if (t < nvalid) {
-#pragma unroll
-          for (int i = 0; i < 16; i += 4)
-            *reinterpret_cast<float4 *>(orow + 16 * u + i) =
-                make_float4(o[i] * ss64_out, o[i + 1] * ss64_out, o[i + 2] * ss64_out, o[i + 3] * ss64_out);
-        }
+        for (int i = 0; i < 64; i += 4)
+          *reinterpret_cast<float4 *>(orow + i) =
+              make_float4(o[i] * ss64_out, o[i + 1] * ss64_out, o[i + 2] * ss64_out, o[i + 3] * ss64_out);
       }
     }
     tc_fence_before();
