@@ -5,34 +5,74 @@
 // The reference trains through PyTorch autograd of its chunkwise path
 // (_chunkwise_delta_reference, delta_phase/kernels/triton_chunk_delta.py:211-252, via the
 // dispatcher at :279-291; DeltaPhaseTritonFunction.backward at :271-276 raises) and of the
-// complex-beta token loop (delta_phase/layers.py:346-360).  Both compute the token
-// recurrence, per value row o (real form, see core_simt.cu):
-//   e_t = v_t - S_{t-1} kap_t / D,  u_t = g_t e_t,  S_t = S_{t-1} + u_t w_t^T,
-//   o_t = S_t xi_t / D
-// with g = beta, w = kap (real beta) or g = 1, w = beta kap = (br c - bi s, br s + bi c)
-// (complex beta, br = 1 + cos phi, bi = sin phi).  Its adjoint, backwards in t with
-// dS = dL/dS_t:
-//   dS += dO_t xi_t^T / D;  dxi_t = S_t^T dO_t / D;  du_t = dS w_t;  dw_t = dS^T u_t;
-//   dg_t = du_t . e_t;  de_t = g_t du_t = dv_t;  S_{t-1} = S_t - u_t w_t^T;
-//   dS -= de_t kap_t^T / D;  dkap_t = -S_{t-1}^T de_t / D (+ dw_t through w),
-// and dtheta = -sin dkap_cos + cos dkap_sin.  The states S_{t-1} are not stored: the
-// kernel runs the recurrence forward once (fp32, keeping u_t in the workspace) and then
-// undoes one rank-1 update per token on the way back, which is exact up to fp32
-// rounding (no factor multiplies S, so rounding errors only add).  e_t comes back from
-// S_t kap_t = S_{t-1} kap_t + u_t (w_t . kap_t), w . kap = D (real) or br D (complex).
+// complex-beta token loop (delta_phase/layers.py:346-360).  Both compute, in the real form
+// of core_simt.cu, the recurrence S_t = S_{t-1} + g_t (v_t - S_{t-1} kap_t / D) w_t^T,
+// o_t = S_t xi_t / D, with g = beta, w = kap (real beta) or g = 1, w = beta kap =
+// (br c - bi s, br s + bi c) (complex beta, br = 1 + cos phi, bi = sin phi).
 //
-// One CTA of 256 threads per (b, h): warp w holds rows 32 (w / 4) .. +31 of column
-// 32 (w % 4) + lane of S and dS in registers (D <= 64, Dv <= 64).  Row sums (S kap,
-// dS w) are warp reduce-scatters plus a 4-way shared-memory sum; column sums (the key /
-// query gradients) pair the two row halves through shared memory one token later.  One
-// block barrier per token.
+// Chunked adjoint (C = 32 tokens; rows = tokens; K, W, Q the key / write-key / query
+// phasor rows, S^T the state at the sub-chunk start, dS^T the gradient of the state at
+// its end):
+//   forward again:  G = K W^T,  A = strict_lower(G) diag(g) / D,  T = (I + A)^-1,
+//                   P = tril(Q W^T),  E = V - K S^T / D,  Y = T E,  U = diag(g) Y
+//   dU = W dS^T + P^T dO / D;   dg += rowsum(dU o Y);   dY = diag(g) dU;   dE = T^T dY = dV
+//   dA = -strict_lower(dE Y^T);  dG = dA diag(g) / D;  dg += colsum(dA o G) / D
+//   dP = tril(dO U^T) / D
+//   dK (read) = dG W - dE S / D;   dW = U dS + dP^T Q + dG^T K;   dQ = dO S / D + dP W
+//   dS^T <- dS^T + Q^T dO / D - K^T dE / D
+// then dK += dW (real beta) or R^T dW and dphi from dW (complex beta), and
+// dtheta = -sin dkap_cos + cos dkap_sin.  Pass 1 runs the chunked forward and keeps the
+// state at every sub-chunk start in the workspace; pass 2 walks the sub-chunks backwards.
+//
+// One CTA of 256 threads per (b, h); every product is a warp-level tf32 tensor-core MMA
+// (mma.sync m16n8k8) on fp32 shared-memory operands; the ones that carry the state and
+// its gradient across sub-chunks are split in high and low tf32 parts (three products:
+// hi hi + hi lo + lo hi), which keeps fp32 accuracy there (see mma16).  The 32 x 32
+// triangular inverse is a forward substitution by one warp (a lane per column) while the
+// other warps form E.  Limits: D <= 64, Dv <= 64.
 #include "dp_common.cuh"
+#include "tc_ptx.cuh"
 
 namespace dp {
 namespace {
 
+using namespace ptx;
+
 constexpr int kBwdThreads = 256;
-constexpr int TB = 32;  // tokens staged per block
+constexpr int kC = 32;      // tokens per sub-chunk
+constexpr int kF = 128;     // key features (2 D) at most
+constexpr int kDv = 64;     // value channels at most
+constexpr int LD_S = 68;    // state (F x Dv), transposed
+constexpr int LD_F = 132;   // C x F phasor rows
+constexpr int LD_V = 68;    // C x Dv
+constexpr int LD_C = 36;    // C x C
+constexpr int S_FLOATS = kF * LD_S;
+constexpr int F_FLOATS = kC * LD_F;
+constexpr int V_FLOATS = kC * LD_V;
+constexpr int C_FLOATS = kC * LD_C;
+// float offsets
+constexpr int O_DST = 0;
+constexpr int O_ST = O_DST + S_FLOATS;
+constexpr int O_K = O_ST + S_FLOATS;
+constexpr int O_Q = O_K + F_FLOATS;
+constexpr int O_W = O_Q + F_FLOATS;     // complex beta only
+constexpr int O_V = O_W + F_FLOATS;     // V, then U
+constexpr int O_DO = O_V + V_FLOATS;
+constexpr int O_Y = O_DO + V_FLOATS;
+constexpr int O_DU = O_Y + V_FLOATS;    // U (pass 1); dU, then dY (pass 2)
+constexpr int O_DE = O_DU + V_FLOATS;   // E, then dE
+constexpr int O_T = O_DE + V_FLOATS;
+constexpr int O_G = O_T + C_FLOATS;
+constexpr int O_P = O_G + C_FLOATS;
+constexpr int O_DA = O_P + C_FLOATS;    // dG = dA diag(g) / D
+constexpr int O_DP = O_DA + C_FLOATS;
+constexpr int O_GV = O_DP + C_FLOATS;   // g per token (beta, or 1)
+constexpr int O_BR = O_GV + kC;         // complex beta: br, bi per token
+constexpr int O_BI = O_BR + kC;
+constexpr int O_DG = O_BI + kC;         // d beta / d phi per token
+constexpr int SMEM_FLOATS = O_DG + kC;
+constexpr size_t SMEM_BYTES = SMEM_FLOATS * sizeof(float);
+static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 
 struct BwdArgs {
   const void *tk, *tq, *v, *g;  // g: beta or phi
@@ -40,14 +80,8 @@ struct BwdArgs {
   SeqStrides s_tk, s_tq, s_v, s_g;
   const float *state_in, *dout, *dstate_out;  // dout (B,H,L,Dv) contiguous; others may be null
   float *dtk, *dtq, *dv, *dg, *dstate_in;     // dtk/dtq (B,H,L,D), dv (B,H,L,Dv), dg (B,H,L)
-  float *ws_u;                                // (B,H,L,Dv)
+  float *ckpt;                                // (B, H, NSC, F, Dv) states at sub-chunk starts
   int H, L, D, Dv;
-};
-
-struct Stage {
-  float tk[TB][64], tq[TB][64];
-  float v[TB][64], dout[TB][64], u[TB][64];
-  float g[TB];
 };
 
 __device__ __forceinline__ float load_any(const void *p, int dt, int64_t i) {
@@ -56,245 +90,467 @@ __device__ __forceinline__ float load_any(const void *p, int dt, int64_t i) {
   return __half2float(static_cast<const __half *>(p)[i]);
 }
 
-// Lane l returns the sum over the warp's lanes of x[l] (reduce-scatter of 32 values).
-__device__ __forceinline__ float warp_reduce_scatter32(float (&x)[32], int lane) {
+// d (a 16 x 16 tile as two m16n8 fragments) += X Y, X(i, k) = x[i * x_si + k * x_sk]
+// (16 x K), Y(k, j) = y[k * y_sk + j * y_sj] (K x 16); tf32 products, split in high and
+// low parts (hi hi + hi lo + lo hi) when SPLIT.  Unsplit products (relative error ~5e-4)
+// serve the products whose result is a gradient of this sub-chunk only (dK, dQ, dA, dP,
+// Y); everything that feeds the state or its gradient across sub-chunks is split (an
+// error there would add up along the sequence).
+template <int K, bool SPLIT = true>
+__device__ __forceinline__ void mma16(float (&d)[2][4], const float *x, int x_si, int x_sk, const float *y, int y_sk,
+                                      int y_sj, int lane) {
+  const int g = lane >> 2, c = lane & 3;
+  // the high-high products accumulate in d, the two cross products in e: four independent
+  // accumulation chains per call instead of two
+  float e[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll 4
+  for (int k0 = 0; k0 < K; k0 += 8) {
+    const float xv[4] = {x[g * x_si + (k0 + c) * x_sk], x[(g + 8) * x_si + (k0 + c) * x_sk],
+                         x[g * x_si + (k0 + c + 4) * x_sk], x[(g + 8) * x_si + (k0 + c + 4) * x_sk]};
+    uint32_t xh[4], xl[4];
 #pragma unroll
-  for (int k = 16; k >= 1; k >>= 1) {
-    const bool upper = (lane & k) != 0;
+    for (int i = 0; i < 4; ++i) {
+      xh[i] = to_tf32(xv[i]);
+      xl[i] = to_tf32(xv[i] - __uint_as_float(xh[i]));
+    }
 #pragma unroll
-    for (int i = 0; i < k; ++i) {
-      const float send = upper ? x[i] : x[i + k];
-      const float keep = upper ? x[i + k] : x[i];
-      x[i] = keep + __shfl_xor_sync(0xffffffffu, send, k);
-    }
-  }
-  return x[0];
-}
-
-// Stages tokens [t0, t0 + n) of this (b, h): phases, values (and output gradients and
-// u_t in the backward pass), the write gate.  Rows / channels past Dv / D are zero.
-__device__ void stage_tokens(const BwdArgs &a, Stage &st, int b, int h, int t0, int n, bool bwd, int64_t row_base) {
-  const int tid = threadIdx.x;
-  for (int idx = tid; idx < TB * 64; idx += kBwdThreads) {
-    const int r = idx >> 6, c = idx & 63, t = t0 + r;
-    const bool ok = r < n;
-    float xk = 0.f, xq = 0.f, xv = 0.f, xo = 0.f, xu = 0.f;
-    if (ok && c < a.D) {
-      xk = load_any(a.tk, a.in_dt, b * a.s_tk.b + h * a.s_tk.h + (int64_t)t * a.s_tk.t + c);
-      xq = load_any(a.tq, a.in_dt, b * a.s_tq.b + h * a.s_tq.h + (int64_t)t * a.s_tq.t + c);
-    }
-    if (ok && c < a.Dv) {
-      xv = load_any(a.v, a.in_dt, b * a.s_v.b + h * a.s_v.h + (int64_t)t * a.s_v.t + c);
-      if (bwd) {
-        xo = a.dout[row_base + (int64_t)t * a.Dv + c];
-        xu = a.ws_u[row_base + (int64_t)t * a.Dv + c];
+    for (int n = 0; n < 2; ++n) {
+      const float y0 = y[(k0 + c) * y_sk + (g + 8 * n) * y_sj], y1 = y[(k0 + c + 4) * y_sk + (g + 8 * n) * y_sj];
+      const uint32_t yh[2] = {to_tf32(y0), to_tf32(y1)};
+      const uint32_t yl[2] = {to_tf32(y0 - __uint_as_float(yh[0])), to_tf32(y1 - __uint_as_float(yh[1]))};
+      mma_tf32_m16n8k8(d[n], xh, yh);
+      if (SPLIT) {
+        mma_tf32_m16n8k8(e[n], xh, yl);
+        mma_tf32_m16n8k8(e[n], xl, yh);
       }
     }
-    st.tk[r][c] = xk;
-    st.tq[r][c] = xq;
-    st.v[r][c] = xv;
-    st.dout[r][c] = xo;
-    st.u[r][c] = xu;
   }
-  for (int r = tid; r < TB; r += kBwdThreads)
-    st.g[r] = r < n ? load_any(a.g, a.g_dt, b * a.s_g.b + h * a.s_g.h + (int64_t)(t0 + r) * a.s_g.t) : 0.f;
+#pragma unroll
+  for (int n = 0; n < 2; ++n)
+#pragma unroll
+    for (int r = 0; r < 4; ++r) d[n][r] += e[n][r];
 }
 
-// Column sums of one token -> d theta_k, d theta_q (and d phi).  Called by whole warps
-// (the four column warps of row half 0); lane pairs (2c, 2c + 1) hold channel c.
-// pend = {sin, cos of theta_k, sin, cos of theta_q, br, bi} of that token.
-template <bool CB>
-__device__ __forceinline__ void finish_token(const BwdArgs &a, const float (*cb_)[3][128], int j, int lane,
-                                             bool col_ok, int64_t gi_base, int t, const float (&pend)[6],
-                                             float invD) {
-  const float qk = cb_[0][0][j] + cb_[1][0][j];  // d kap through the read (per column)
-  const float qq = cb_[0][1][j] + cb_[1][1][j];  // D * d xi
-  const float qw = cb_[0][2][j] + cb_[1][2][j];  // d w
-  const float ok_ = __shfl_xor_sync(0xffffffffu, qk, 1), oq = __shfl_xor_sync(0xffffffffu, qq, 1),
-              ow = __shfl_xor_sync(0xffffffffu, qw, 1);
-  const float sk = pend[0], ck = pend[1], sq = pend[2], cq = pend[3], br = pend[4], bi = pend[5];
-  float dphi = 0.f;
-  if (!(j & 1) && col_ok) {  // even lane: channel j / 2, own = cos column, partner = sin column
-    float dkc = qk, dks = ok_;
-    if (CB) {
-      dkc += br * qw + bi * ow;
-      dks += -bi * qw + br * ow;
-      const float dbr = -bi, dbi = br - 1.f;
-      dphi = qw * (dbr * ck - dbi * sk) + ow * (dbr * sk + dbi * ck);
-    } else {
-      dkc += qw;
-      dks += ow;
-    }
-    const int64_t gi = gi_base + (j >> 1);
-    a.dtk[gi] = -sk * dkc + ck * dks;
-    a.dtq[gi] = (-sq * qq + cq * oq) * invD;
-  }
-  if (CB) {
+__device__ __forceinline__ void zero16(float (&d)[2][4]) {
 #pragma unroll
-    for (int o2 = 1; o2 < 32; o2 <<= 1) dphi += __shfl_xor_sync(0xffffffffu, dphi, o2);
-    if (lane == 0) atomicAdd(&a.dg[t], dphi);
+  for (int n = 0; n < 2; ++n)
+#pragma unroll
+    for (int r = 0; r < 4; ++r) d[n][r] = 0.f;
+}
+
+// Row / column of fragment element (n, r) inside its 16 x 16 tile.
+__device__ __forceinline__ int frow(int lane, int r) { return (lane >> 2) + (r >= 2 ? 8 : 0); }
+__device__ __forceinline__ int fcol(int lane, int n, int r) { return 8 * n + 2 * (lane & 3) + (r & 1); }
+
+// T = (I + A)^-1 for the strictly lower A (row stride LD_C): lane = column, forward
+// substitution with four partial sums per row (a quarter of the dependency chain).
+__device__ __forceinline__ void solve_T(float *Tb, const float *Ab, int lane) {
+  float col[kC];
+#pragma unroll
+  for (int i = 0; i < kC; ++i) {
+    float acc[4] = {(i == lane) ? 1.f : 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int k = 0; k < i; ++k) acc[k & 3] = fmaf(-Ab[i * LD_C + k], col[k], acc[k & 3]);
+    col[i] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
   }
+#pragma unroll
+  for (int i = 0; i < kC; ++i) Tb[i * LD_C + lane] = col[i];
+}
+
+// Sub-chunk inputs: key / query phasors (and write keys), values, output gradients, gates.
+// Rows past n and channels past D / Dv are zero.
+template <bool CB>
+__device__ void load_sub_chunk(const BwdArgs &a, float *sm, int b, int h, int t0, int n, bool with_q, bool with_do,
+                               int64_t row_base) {
+  constexpr int kPer = kC * 64 / kBwdThreads;  // elements per thread
+  const int tid = threadIdx.x;
+  float *gv = sm + O_GV, *br = sm + O_BR, *bi = sm + O_BI;
+  // every global load of this thread first, then the arithmetic and the shared stores
+  float xk[kPer], xq[kPer], xv[kPer], xo[kPer];
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int idx = tid + i * kBwdThreads, r = idx >> 6, c = idx & 63, t = t0 + r;
+    const bool ok = r < n;
+    xk[i] = xq[i] = xv[i] = xo[i] = 0.f;
+    if (ok && c < a.D) {
+      xk[i] = load_any(a.tk, a.in_dt, b * a.s_tk.b + h * a.s_tk.h + (int64_t)t * a.s_tk.t + c);
+      if (with_q) xq[i] = load_any(a.tq, a.in_dt, b * a.s_tq.b + h * a.s_tq.h + (int64_t)t * a.s_tq.t + c);
+    }
+    if (ok && c < a.Dv) {
+      xv[i] = load_any(a.v, a.in_dt, b * a.s_v.b + h * a.s_v.h + (int64_t)t * a.s_v.t + c);
+      if (with_do) xo[i] = a.dout[row_base + (int64_t)t * a.Dv + c];
+    }
+  }
+  if (tid < kC) {
+    const float g = tid < n ? load_any(a.g, a.g_dt, b * a.s_g.b + h * a.s_g.h + (int64_t)(t0 + tid) * a.s_g.t) : 0.f;
+    if (CB) {
+      float sp, cp;
+      sincosf(g, &sp, &cp);
+      br[tid] = tid < n ? 1.f + cp : 0.f;
+      bi[tid] = tid < n ? sp : 0.f;
+      gv[tid] = tid < n ? 1.f : 0.f;
+    } else {
+      gv[tid] = g;
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int idx = tid + i * kBwdThreads, r = idx >> 6, c = idx & 63;
+    float ck = 0.f, sk = 0.f, cq = 0.f, sq = 0.f;
+    if (r < n && c < a.D) {
+      sincos_2pi_fast(xk[i], &sk, &ck);
+      if (with_q) sincos_2pi_fast(xq[i], &sq, &cq);
+    }
+    *reinterpret_cast<float2 *>(sm + O_K + r * LD_F + 2 * c) = make_float2(ck, sk);
+    if (with_q) *reinterpret_cast<float2 *>(sm + O_Q + r * LD_F + 2 * c) = make_float2(cq, sq);
+    if (CB)
+      *reinterpret_cast<float2 *>(sm + O_W + r * LD_F + 2 * c) =
+          make_float2(fmaf(br[r], ck, -bi[r] * sk), fmaf(br[r], sk, bi[r] * ck));
+    sm[O_V + r * LD_V + c] = xv[i];
+    if (with_do) sm[O_DO + r * LD_V + c] = xo[i];
+  }
+}
+
+// State^T (F x Dv, dense in global) <-> shared memory (row stride LD_S), 16-byte accesses,
+// all loads of a thread issued before its stores.
+__device__ __forceinline__ void state_to_smem(float *dst, const float *src) {
+  constexpr int kPer = kF * kDv / 4 / kBwdThreads;
+  float4 x[kPer];
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) x[i] = reinterpret_cast<const float4 *>(src)[threadIdx.x + i * kBwdThreads];
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int q = threadIdx.x + i * kBwdThreads, j = q / (kDv / 4), o4 = q % (kDv / 4);
+    *reinterpret_cast<float4 *>(dst + j * LD_S + 4 * o4) = x[i];
+  }
+}
+__device__ __forceinline__ void state_to_global(float *dst, const float *src) {
+  constexpr int kPer = kF * kDv / 4 / kBwdThreads;
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int q = threadIdx.x + i * kBwdThreads, j = q / (kDv / 4), o4 = q % (kDv / 4);
+    reinterpret_cast<float4 *>(dst)[q] = *reinterpret_cast<const float4 *>(src + j * LD_S + 4 * o4);
+  }
+}
+
+// G = K W^T (C x C) into Gb and A = strict_lower(G) diag(g) / D into the dA buffer (free
+// until the dA phase): tiles 0..3 (2 x 2 of 16 x 16).
+__device__ __forceinline__ void gram_tile(float *sm, const float *Wb, int tile, float invD, int lane) {
+  const int rb = tile >> 1, cb = tile & 1;
+  float d[2][4];
+  zero16(d);
+  mma16<kF>(d, sm + O_K + rb * 16 * LD_F, LD_F, 1, Wb + cb * 16 * LD_F, 1, LD_F, lane);
+#pragma unroll
+  for (int n = 0; n < 2; ++n)
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int t = rb * 16 + frow(lane, r), s2 = cb * 16 + fcol(lane, n, r);
+      sm[O_G + t * LD_C + s2] = d[n][r];
+      sm[O_DA + t * LD_C + s2] = s2 < t ? d[n][r] * sm[O_GV + s2] * invD : 0.f;
+    }
+}
+
+// E = V - K S^T / D (C x Dv) into the dE buffer: tiles 0..7 (2 x 4).
+__device__ __forceinline__ void e_tile(float *sm, int tile, float invD, int lane) {
+  const int rb = tile >> 2, cb = tile & 3;
+  float d[2][4];
+  zero16(d);
+  mma16<kF>(d, sm + O_K + rb * 16 * LD_F, LD_F, 1, sm + O_ST + cb * 16, LD_S, 1, lane);
+#pragma unroll
+  for (int n = 0; n < 2; ++n)
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int i = (rb * 16 + frow(lane, r)) * LD_V + cb * 16 + fcol(lane, n, r);
+      sm[O_DE + i] = sm[O_V + i] - d[n][r] * invD;
+    }
+}
+
+// Y = T E (C x Dv) into Yb; with U = diag(g) Y into `u_out` (a C x Dv buffer) when given.
+template <bool SPLIT>
+__device__ __forceinline__ void y_tile(float *sm, int tile, float *u_out, int lane) {
+  const int rb = tile >> 2, cb = tile & 3;
+  float d[2][4];
+  zero16(d);
+  mma16<kC, SPLIT>(d, sm + O_T + rb * 16 * LD_C, LD_C, 1, sm + O_DE + cb * 16, LD_V, 1, lane);
+#pragma unroll
+  for (int n = 0; n < 2; ++n)
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int row = rb * 16 + frow(lane, r);
+      const int i = row * LD_V + cb * 16 + fcol(lane, n, r);
+      sm[O_Y + i] = d[n][r];
+      if (u_out) u_out[i] = sm[O_GV + row] * d[n][r];
+    }
 }
 
 template <bool CB>
 __global__ void __launch_bounds__(kBwdThreads, 1) core_bwd_kernel(BwdArgs a) {
-  extern __shared__ __align__(16) uint8_t smem_raw[];
-  Stage &st = *reinterpret_cast<Stage *>(smem_raw);
-  float(*red)[2][4][64] = reinterpret_cast<float(*)[2][4][64]>(smem_raw + sizeof(Stage));  // [parity][which][cb][row]
-  float(*colb)[2][3][128] =
-      reinterpret_cast<float(*)[2][3][128]>(smem_raw + sizeof(Stage) + sizeof(float) * 2 * 2 * 4 * 64);  // [par][rh][q][j]
-
+  extern __shared__ __align__(16) float sm[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int rh = warp >> 2, cb = warp & 3, j = 32 * cb + lane, row0 = 32 * rh;
   const int bh = blockIdx.x, b = bh / a.H, h = bh % a.H;
-  const int L = a.L, D = a.D, Dv = a.Dv, c_idx = j >> 1;
-  const bool col_ok = j < 2 * D;
+  const int L = a.L, D = a.D, Dv = a.Dv, F = 2 * D;
   const float invD = 1.0f / (float)D;
-  const int64_t row_base = (int64_t)bh * L * Dv;  // (B,H,L,Dv) contiguous
-  const int64_t st_base = (int64_t)bh * Dv * 2 * D;
+  const int nsc = (L + kC - 1) / kC;
+  const int64_t row_base = (int64_t)bh * L * Dv;
+  const int64_t st_base = (int64_t)bh * Dv * F;
+  float *ckpt = a.ckpt + (int64_t)bh * nsc * kF * kDv;
+  const float *Wb = CB ? sm + O_W : sm + O_K;
 
-  float S[32], dS[32];
-#pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    const int o = row0 + i;
-    S[i] = (a.state_in && col_ok && o < Dv) ? a.state_in[st_base + (int64_t)o * 2 * D + j] : 0.f;
+  // state^T from the complex state (row o, interleaved column j)
+  for (int idx = tid; idx < kF * kDv; idx += kBwdThreads) {
+    const int j = idx / kDv, o = idx % kDv;
+    sm[O_ST + j * LD_S + o] = (a.state_in && j < F && o < Dv) ? a.state_in[st_base + (int64_t)o * F + j] : 0.f;
   }
 
-  // ---- pass 1: the recurrence forward, u_t to the workspace
-  int par = 0;
-  for (int t0 = 0; t0 < L; t0 += TB) {
-    const int n = min(TB, L - t0);
+  // ---- pass 1: the chunked forward, keeping the state at every sub-chunk start
+  for (int sc = 0; sc < nsc; ++sc) {
+    const int t0 = sc * kC, n = min(kC, L - t0);
     __syncthreads();
-    stage_tokens(a, st, b, h, t0, n, false, row_base);
+    state_to_global(ckpt + (int64_t)sc * kF * kDv, sm + O_ST);
+    load_sub_chunk<CB>(a, sm, b, h, t0, n, false, false, row_base);
     __syncthreads();
-    for (int r = 0; r < n; ++r, par ^= 1) {
-      float sk, ck;
-      __sincosf(st.tk[r][c_idx & 63], &sk, &ck);
-      const float kap = col_ok ? ((j & 1) ? sk : ck) : 0.f;
-      float wj = kap;
-      const float g = st.g[r];
-      float br = 1.f, bi = 0.f;
-      if (CB) {
-        float sp, cp;
-        __sincosf(g, &sp, &cp);
-        br = 1.f + cp;
-        bi = sp;
-        wj = col_ok ? ((j & 1) ? fmaf(br, sk, bi * ck) : fmaf(br, ck, -bi * sk)) : 0.f;
-      }
-      float x[32];
+    if (warp < 4) gram_tile(sm, Wb, warp, invD, lane);
+    __syncthreads();
+    if (warp == 0)
+      solve_T(sm + O_T, sm + O_DA, lane);
+    else
+      for (int tile = warp - 1; tile < 8; tile += 7) e_tile(sm, tile, invD, lane);
+    __syncthreads();
+    y_tile<true>(sm, warp, sm + O_DU, lane);  // U into the dU buffer
+    __syncthreads();
+    // S^T += W^T U  (F x Dv: 8 x 4 tiles, 4 per warp)
+    for (int tile = warp; tile < 32; tile += 8) {
+      const int rb = tile >> 2, cb = tile & 3;
+      float d[2][4];
 #pragma unroll
-      for (int i = 0; i < 32; ++i) x[i] = S[i] * kap;
-      const float part = warp_reduce_scatter32(x, lane);
-      red[par][0][cb][row0 + lane] = part;
-      __syncthreads();
-      const int o = row0 + lane;
-      const float sk_row = red[par][0][0][o] + red[par][0][1][o] + red[par][0][2][o] + red[par][0][3][o];
-      const float e = st.v[r][o & 63] - sk_row * invD;
-      const float u = CB ? e : g * e;
-      if (cb == 0 && o < Dv) a.ws_u[row_base + (int64_t)(t0 + r) * Dv + o] = u;
+      for (int nn = 0; nn < 2; ++nn)
 #pragma unroll
-      for (int i = 0; i < 32; ++i) S[i] = fmaf(__shfl_sync(0xffffffffu, u, i), wj, S[i]);
+        for (int r = 0; r < 4; ++r) d[nn][r] = sm[O_ST + (rb * 16 + frow(lane, r)) * LD_S + cb * 16 + fcol(lane, nn, r)];
+      mma16<kC>(d, Wb + rb * 16, 1, LD_F, sm + O_DU + cb * 16, LD_V, 1, lane);
+#pragma unroll
+      for (int nn = 0; nn < 2; ++nn)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) sm[O_ST + (rb * 16 + frow(lane, r)) * LD_S + cb * 16 + fcol(lane, nn, r)] = d[nn][r];
     }
   }
 
-  // ---- pass 2: backwards in t
-#pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    const int o = row0 + i;
-    dS[i] = (a.dstate_out && col_ok && o < Dv) ? a.dstate_out[st_base + (int64_t)o * 2 * D + j] : 0.f;
+  // ---- pass 2: backwards over the sub-chunks
+  __syncthreads();
+  for (int idx = tid; idx < kF * kDv; idx += kBwdThreads) {
+    const int j = idx / kDv, o = idx % kDv;
+    sm[O_DST + j * LD_S + o] =
+        (a.dstate_out && j < F && o < Dv) ? a.dstate_out[st_base + (int64_t)o * F + j] : 0.f;
   }
-  __syncthreads();  // pass 1's reads of the stage are done
-  int pend_t = -1;  // token whose column sums wait in colb[pend_par]
-  int pend_par = 0;
-  float pend[6] = {0.f, 1.f, 0.f, 1.f, 1.f, 0.f};
-  const int nblk = (L + TB - 1) / TB;
-  for (int blk = nblk - 1; blk >= 0; --blk) {
-    const int t0 = blk * TB, n = min(TB, L - t0);
+  for (int sc = nsc - 1; sc >= 0; --sc) {
+    const int t0 = sc * kC, n = min(kC, L - t0);
     __syncthreads();
-    stage_tokens(a, st, b, h, t0, n, true, row_base);
+    state_to_smem(sm + O_ST, ckpt + (int64_t)sc * kF * kDv);
+    if (tid < kC) sm[O_DG + tid] = 0.f;
+    load_sub_chunk<CB>(a, sm, b, h, t0, n, true, true, row_base);
     __syncthreads();
-    for (int r = n - 1; r >= 0; --r, par ^= 1) {
-      const int t = t0 + r;
-      float sk, ck, sq, cq;
-      __sincosf(st.tk[r][c_idx & 63], &sk, &ck);
-      __sincosf(st.tq[r][c_idx & 63], &sq, &cq);
-      const float kap = col_ok ? ((j & 1) ? sk : ck) : 0.f;
-      const float xi = col_ok ? ((j & 1) ? sq : cq) : 0.f;
-      const float g = st.g[r];
-      float br = 1.f, bi = 0.f, wj = kap;
-      if (CB) {
-        float sp, cp;
-        __sincosf(g, &sp, &cp);
-        br = 1.f + cp;
-        bi = sp;
-        wj = col_ok ? ((j & 1) ? fmaf(br, sk, bi * ck) : fmaf(br, ck, -bi * sk)) : 0.f;
-      }
-      // A1: output term, column partials, row products
-      float pq = 0.f, pw = 0.f, x1[32], x2[32];
+    // G = K W^T (warps 0..3), P = tril(Q W^T) (warps 4..7)
+    if (warp < 4) {
+      gram_tile(sm, Wb, warp, invD, lane);
+    } else {
+      const int tile = warp - 4, rb = tile >> 1, cb = tile & 1;
+      float d[2][4];
+      zero16(d);
+      mma16<kF>(d, sm + O_Q + rb * 16 * LD_F, LD_F, 1, Wb + cb * 16 * LD_F, 1, LD_F, lane);
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const float dO = st.dout[r][row0 + i];
-        const float uu = st.u[r][row0 + i];
-        dS[i] = fmaf(dO * invD, xi, dS[i]);
-        pq = fmaf(S[i], dO, pq);
-        pw = fmaf(dS[i], uu, pw);
-        x1[i] = dS[i] * wj;
-        x2[i] = S[i] * kap;
-      }
-      red[par][0][cb][row0 + lane] = warp_reduce_scatter32(x1, lane);
-      red[par][1][cb][row0 + lane] = warp_reduce_scatter32(x2, lane);
-      __syncthreads();
-      // the previous (later) token's column sums: both row halves are in colb now
-      if (pend_t >= 0 && rh == 0)
-        finish_token<CB>(a, colb[pend_par], j, lane, col_ok, (int64_t)bh * L * D + (int64_t)pend_t * D,
-                         bh * L + pend_t, pend, invD);
-      // A2: row sums -> du, e; dg, dv
-      const int o = row0 + lane;
-      const float du = red[par][0][0][o] + red[par][0][1][o] + red[par][0][2][o] + red[par][0][3][o];
-      const float skr = red[par][1][0][o] + red[par][1][1][o] + red[par][1][2][o] + red[par][1][3][o];
-      const float u_o = st.u[r][o & 63];
-      const float wk = CB ? br * (float)D : (float)D;  // w . kap
-      const float e = st.v[r][o & 63] - (skr - u_o * wk) * invD;
-      const float de = CB ? du : g * du;
-      if (cb == 0 && o < Dv) a.dv[row_base + (int64_t)t * Dv + o] = de;
-      if (!CB && cb == 0) {
-        float p = (o < Dv) ? du * e : 0.f;
+      for (int nn = 0; nn < 2; ++nn)
 #pragma unroll
-        for (int o2 = 16; o2 >= 1; o2 >>= 1) p += __shfl_xor_sync(0xffffffffu, p, o2);
-        if (lane == 0) atomicAdd(&a.dg[(int64_t)bh * L + t], p);
-      }
-      // A3: undo the update, propagate dS, read-key partial
-      float pk = 0.f;
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const float de_i = __shfl_sync(0xffffffffu, de, i);
-        const float uu = st.u[r][row0 + i];
-        S[i] = fmaf(-uu, wj, S[i]);
-        dS[i] = fmaf(-de_i * invD, kap, dS[i]);
-        pk = fmaf(S[i], de_i, pk);
-      }
-      colb[par][rh][0][j] = -pk * invD;
-      colb[par][rh][1][j] = pq;
-      colb[par][rh][2][j] = pw;
-      pend_t = t;
-      pend_par = par;
-      pend[0] = sk;
-      pend[1] = ck;
-      pend[2] = sq;
-      pend[3] = cq;
-      pend[4] = br;
-      pend[5] = bi;
+        for (int r = 0; r < 4; ++r) {
+          const int t = rb * 16 + frow(lane, r), s = cb * 16 + fcol(lane, nn, r);
+          sm[O_P + t * LD_C + s] = s <= t ? d[nn][r] : 0.f;
+        }
     }
+    __syncthreads();
+    // warp 0: T; the others: E and dU = W dS^T + P^T dO / D (neither needs T)
+    if (warp == 0) {
+      solve_T(sm + O_T, sm + O_DA, lane);
+    } else {
+      for (int tile = warp - 1; tile < 16; tile += 7) {
+        if (tile < 8) {
+          e_tile(sm, tile, invD, lane);
+        } else {
+          const int rb = (tile - 8) >> 2, cb = (tile - 8) & 3;
+          float d1[2][4], d2[2][4];
+          zero16(d1);
+          zero16(d2);
+          mma16<kF>(d1, Wb + rb * 16 * LD_F, LD_F, 1, sm + O_DST + cb * 16, LD_S, 1, lane);
+          mma16<kC>(d2, sm + O_P + rb * 16, 1, LD_C, sm + O_DO + cb * 16, LD_V, 1, lane);
+#pragma unroll
+          for (int nn = 0; nn < 2; ++nn)
+#pragma unroll
+            for (int r = 0; r < 4; ++r)
+              sm[O_DU + (rb * 16 + frow(lane, r)) * LD_V + cb * 16 + fcol(lane, nn, r)] = d1[nn][r] + d2[nn][r] * invD;
+        }
+      }
+    }
+    __syncthreads();
+    y_tile<false>(sm, warp, sm + O_V, lane);  // Y, and U into the V buffer
+    __syncthreads();
+    // dg += rowsum(dU o Y) (real beta); dY = diag(g) dU in place (a warp per 4 rows)
+#pragma unroll
+    for (int rr = 0; rr < 4; ++rr) {
+      const int row = 4 * warp + rr;
+      const float gr = sm[O_GV + row];
+      float rs = 0.f;
+#pragma unroll
+      for (int oo = 0; oo < kDv; oo += 32) {
+        const int i = row * LD_V + oo + lane;
+        const float du = sm[O_DU + i];
+        rs = fmaf(du, sm[O_Y + i], rs);
+        sm[O_DU + i] = gr * du;
+      }
+      if (!CB) {
+#pragma unroll
+        for (int o2 = 16; o2 >= 1; o2 >>= 1) rs += __shfl_xor_sync(0xffffffffu, rs, o2);
+        if (lane == 0) sm[O_DG + row] += rs;
+      }
+    }
+    __syncthreads();
+    // dE = T^T dY
+    {
+      const int rb = warp >> 2, cb = warp & 3;
+      float d[2][4];
+      zero16(d);
+      mma16<kC>(d, sm + O_T + rb * 16, 1, LD_C, sm + O_DU + cb * 16, LD_V, 1, lane);
+#pragma unroll
+      for (int nn = 0; nn < 2; ++nn)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) sm[O_DE + (rb * 16 + frow(lane, r)) * LD_V + cb * 16 + fcol(lane, nn, r)] = d[nn][r];
+    }
+    __syncthreads();
+    if (warp < 4) {
+      // dA = -strict_lower(dE Y^T); dG = dA diag(g) / D; dg += colsum(dA o G) / D
+      const int rb = warp >> 1, cb = warp & 1;
+      float d[2][4];
+      zero16(d);
+      mma16<kDv, false>(d, sm + O_DE + rb * 16 * LD_V, LD_V, 1, sm + O_Y + cb * 16 * LD_V, 1, LD_V, lane);
+      float cs[2][2] = {{0.f, 0.f}, {0.f, 0.f}};  // [n][col parity]
+#pragma unroll
+      for (int nn = 0; nn < 2; ++nn)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          const int t = rb * 16 + frow(lane, r), s = cb * 16 + fcol(lane, nn, r);
+          const float da = s < t ? -d[nn][r] : 0.f;
+          sm[O_DA + t * LD_C + s] = da * sm[O_GV + s] * invD;
+          cs[nn][r & 1] = fmaf(da, sm[O_G + t * LD_C + s], cs[nn][r & 1]);
+        }
+      if (!CB) {
+#pragma unroll
+        for (int nn = 0; nn < 2; ++nn)
+#pragma unroll
+          for (int p = 0; p < 2; ++p) {
+            float v2 = cs[nn][p];
+#pragma unroll
+            for (int o2 = 4; o2 < 32; o2 <<= 1) v2 += __shfl_xor_sync(0xffffffffu, v2, o2);
+            if (lane < 4) atomicAdd(&sm[O_DG + cb * 16 + 8 * nn + 2 * lane + p], v2 * invD);
+          }
+      }
+    } else {
+      // dP = tril(dO U^T) / D  (U in the V buffer)
+      const int tile = warp - 4, rb = tile >> 1, cb = tile & 1;
+      float d[2][4];
+      zero16(d);
+      mma16<kDv, false>(d, sm + O_DO + rb * 16 * LD_V, LD_V, 1, sm + O_V + cb * 16 * LD_V, 1, LD_V, lane);
+#pragma unroll
+      for (int nn = 0; nn < 2; ++nn)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          const int t = rb * 16 + frow(lane, r), s = cb * 16 + fcol(lane, nn, r);
+          sm[O_DP + t * LD_C + s] = s <= t ? d[nn][r] * invD : 0.f;
+        }
+    }
+    __syncthreads();
+    // dK, dQ (32 x F: 2 x 8 tiles, 2 per warp) -> d theta_k, d theta_q; dphi (complex beta)
+    for (int tile = warp; tile < 16; tile += 8) {
+      const int rb = tile >> 3, cb = tile & 7;
+      if (cb * 16 >= F) continue;  // columns past 2D (warp-uniform)
+      float kr[2][4], ks[2][4], kw[2][4], q1[2][4], q2[2][4];
+      zero16(kr);
+      zero16(ks);
+      zero16(kw);
+      zero16(q1);
+      zero16(q2);
+      // dG W, dG^T K, U dS, dP^T Q, -dE S / D
+      mma16<kC, false>(kr, sm + O_DA + rb * 16 * LD_C, LD_C, 1, Wb + cb * 16, LD_F, 1, lane);
+      mma16<kC, false>(kw, sm + O_DA + rb * 16, 1, LD_C, sm + O_K + cb * 16, LD_F, 1, lane);
+      mma16<kDv, false>(kw, sm + O_V + rb * 16 * LD_V, LD_V, 1, sm + O_DST + cb * 16 * LD_S, 1, LD_S, lane);
+      mma16<kC, false>(kw, sm + O_DP + rb * 16, 1, LD_C, sm + O_Q + cb * 16, LD_F, 1, lane);
+      mma16<kDv, false>(ks, sm + O_DE + rb * 16 * LD_V, LD_V, 1, sm + O_ST + cb * 16 * LD_S, 1, LD_S, lane);
+      // dO S / D, dP W
+      mma16<kDv, false>(q1, sm + O_DO + rb * 16 * LD_V, LD_V, 1, sm + O_ST + cb * 16 * LD_S, 1, LD_S, lane);
+      mma16<kC, false>(q2, sm + O_DP + rb * 16 * LD_C, LD_C, 1, Wb + cb * 16, LD_F, 1, lane);
+      float dphi[2] = {0.f, 0.f};
+#pragma unroll
+      for (int nn = 0; nn < 2; ++nn)
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const int t = rb * 16 + frow(lane, 2 * hh), j = cb * 16 + fcol(lane, nn, 0), ch = j >> 1;
+          const float kc = sm[O_K + t * LD_F + j], ksn = sm[O_K + t * LD_F + j + 1];
+          float dkc = kr[nn][2 * hh] - ks[nn][2 * hh] * invD, dks = kr[nn][2 * hh + 1] - ks[nn][2 * hh + 1] * invD;
+          const float dwc = kw[nn][2 * hh], dws = kw[nn][2 * hh + 1];
+          if (CB) {
+            const float brt = sm[O_BR + t], bit = sm[O_BI + t];
+            dkc += brt * dwc + bit * dws;
+            dks += -bit * dwc + brt * dws;
+            const float dbr = -bit, dbi = brt - 1.f;
+            dphi[hh] += dwc * (dbr * kc - dbi * ksn) + dws * (dbr * ksn + dbi * kc);
+          } else {
+            dkc += dwc;
+            dks += dws;
+          }
+          const float qc = sm[O_Q + t * LD_F + j], qs = sm[O_Q + t * LD_F + j + 1];
+          const float dqc = q1[nn][2 * hh] * invD + q2[nn][2 * hh], dqs = q1[nn][2 * hh + 1] * invD + q2[nn][2 * hh + 1];
+          if (t < n && ch < D) {
+            const int64_t gi = ((int64_t)bh * L + t0 + t) * D + ch;
+            a.dtk[gi] = -ksn * dkc + kc * dks;
+            a.dtq[gi] = -qs * dqc + qc * dqs;
+          }
+        }
+      if (CB) {
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          dphi[hh] += __shfl_xor_sync(0xffffffffu, dphi[hh], 1);
+          dphi[hh] += __shfl_xor_sync(0xffffffffu, dphi[hh], 2);
+        }
+        if ((lane & 3) == 0) {
+          atomicAdd(&sm[O_DG + rb * 16 + (lane >> 2)], dphi[0]);
+          atomicAdd(&sm[O_DG + rb * 16 + (lane >> 2) + 8], dphi[1]);
+        }
+      }
+    }
+    __syncthreads();
+    // dS^T += Q^T dO / D - K^T dE / D  (F x Dv: 8 x 4 tiles, 4 per warp); dv, dg out
+    for (int tile = warp; tile < 32; tile += 8) {
+      const int rb = tile >> 2, cb = tile & 3;
+      float dq[2][4], dk[2][4];
+      zero16(dq);
+      zero16(dk);
+      mma16<kC>(dq, sm + O_Q + rb * 16, 1, LD_F, sm + O_DO + cb * 16, LD_V, 1, lane);
+      mma16<kC>(dk, sm + O_K + rb * 16, 1, LD_F, sm + O_DE + cb * 16, LD_V, 1, lane);
+#pragma unroll
+      for (int nn = 0; nn < 2; ++nn)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          const int i = (rb * 16 + frow(lane, r)) * LD_S + cb * 16 + fcol(lane, nn, r);
+          sm[O_DST + i] += (dq[nn][r] - dk[nn][r]) * invD;
+        }
+    }
+    for (int idx = tid; idx < kC * kDv; idx += kBwdThreads) {
+      const int r = idx / kDv, o = idx % kDv;
+      if (r < n && o < Dv) a.dv[row_base + (int64_t)(t0 + r) * Dv + o] = sm[O_DE + r * LD_V + o];
+    }
+    if (tid < n) a.dg[(int64_t)bh * L + t0 + tid] = sm[O_DG + tid];
   }
   __syncthreads();
-  if (pend_t >= 0 && rh == 0)
-    finish_token<CB>(a, colb[pend_par], j, lane, col_ok, (int64_t)bh * L * D + (int64_t)pend_t * D, bh * L + pend_t,
-                     pend, invD);
   if (a.dstate_in) {
-#pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      const int o = row0 + i;
-      if (col_ok && o < Dv) a.dstate_in[st_base + (int64_t)o * 2 * D + j] = dS[i];
+    for (int idx = tid; idx < Dv * F; idx += kBwdThreads) {
+      const int o = idx / F, j = idx % F;
+      a.dstate_in[st_base + idx] = sm[O_DST + j * LD_S + o];
     }
   }
 }
@@ -303,8 +559,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1) core_bwd_kernel(BwdArgs a) {
 }  // namespace dp
 
 extern "C" size_t dp_core_bwd_workspace_size(int B, int H, int L, int Dv) {
-  if (B <= 0 || H <= 0 || L <= 0 || Dv <= 0) return 0;
-  return (size_t)B * H * L * Dv * sizeof(float);
+  (void)Dv;
+  if (B <= 0 || H <= 0 || L <= 0) return 0;
+  const size_t nsc = ((size_t)L + dp::kC - 1) / dp::kC;
+  return (size_t)B * H * nsc * dp::kF * dp::kDv * sizeof(float);
 }
 
 extern "C" int dp_core_bwd(const void *theta_k, const void *theta_q, const void *v, const void *beta,
@@ -326,12 +584,6 @@ extern "C" int dp_core_bwd(const void *theta_k, const void *theta_q, const void 
     DP_REQUIRE(workspace && workspace_bytes >= dp_core_bwd_workspace_size(B, H, L, Dv), DP_ERR_WORKSPACE,
                "dp_core_bwd: workspace too small (dp_core_bwd_workspace_size)");
   }
-  cudaStream_t s = as_stream(stream);
-  if (L > 0) {
-    // beta / phi gradients are accumulated with atomics
-    cudaError_t e = cudaMemsetAsync(grad_beta, 0, (size_t)B * H * L * sizeof(float), s);
-    if (e != cudaSuccess) return set_error(DP_ERR_CUDA, std::string("dp_core_bwd: memset: ") + cudaGetErrorString(e));
-  }
   BwdArgs a;
   a.tk = theta_k;
   a.tq = theta_q;
@@ -351,15 +603,14 @@ extern "C" int dp_core_bwd(const void *theta_k, const void *theta_q, const void 
   a.dv = grad_v;
   a.dg = grad_beta;
   a.dstate_in = grad_state_in;
-  a.ws_u = static_cast<float *>(workspace);
+  a.ckpt = static_cast<float *>(workspace);
   a.H = H;
   a.L = L;
   a.D = D;
   a.Dv = Dv;
-  const size_t smem = sizeof(Stage) + sizeof(float) * (2 * 2 * 4 * 64 + 2 * 2 * 3 * 128);
   auto kern = complex_beta ? core_bwd_kernel<true> : core_bwd_kernel<false>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
   if (e != cudaSuccess) return set_error(DP_ERR_CUDA, std::string("dp_core_bwd smem attr: ") + cudaGetErrorString(e));
-  kern<<<B * H, kBwdThreads, smem, s>>>(a);
+  kern<<<B * H, kBwdThreads, SMEM_BYTES, as_stream(stream)>>>(a);
   return check_launch("core_bwd_kernel");
 }
