@@ -201,7 +201,7 @@ def make_core_inputs(dev, seed, B, H, L, D):
 def run_core(args, world, rank, local):
     import torch
     from delta_phase_b200 import _capi
-    from delta_phase_b200.kernels import chunkwise_forward, delta_phase_chunkwise_fused
+    from delta_phase_b200.kernels import chunkwise_forward
 
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
@@ -233,32 +233,55 @@ def run_core(args, world, rank, local):
     tokens = world * B * L
     value = tokens / (ms_max / 1e3)
 
-    # e2e: through the public API from pinned host buffers, result read back to host
+    # e2e: through the public API from pinned host buffers, result read back to host, every
+    # step.  Steps are pipelined the way a streaming caller would run them: the inputs of
+    # step i + 1 go up (copy stream) while step i computes and its outputs come down
+    # (second copy stream); device buffers are double-buffered and ordered by events.
     host = [t.cpu().pin_memory() for t in (tk, tq, v, beta)]
-    out_h = torch.empty(B, H, L, D, dtype=torch.float32).pin_memory()
-    M_h = torch.empty(B, H, D, D, dtype=torch.complex64).pin_memory()
-    dev_in = [torch.empty_like(t) for t in (tk, tq, v, beta)]
+    out_h = [torch.empty(B, H, L, D, dtype=torch.float32).pin_memory() for _ in range(2)]
+    M_h = [torch.empty(B, H, D, D, dtype=torch.complex64).pin_memory() for _ in range(2)]
+    dev_in = [[torch.empty_like(t) for t in (tk, tq, v, beta)] for _ in range(2)]
+    dev_out = [torch.empty(B, H, L, D, device=dev, dtype=torch.float32) for _ in range(2)]
+    s_up, s_down = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_done = [torch.cuda.Event() for _ in range(2)]
+    ev_read = [torch.cuda.Event() for _ in range(2)]
+    for e in ev_done + ev_read:
+        e.record(stream)
 
-    def e2e_step():
-        for d_, h_ in zip(dev_in, host):
-            d_.copy_(h_, non_blocking=True)
-        o, M = delta_phase_chunkwise_fused(*dev_in, chunk_size=C)
-        out_h.copy_(o, non_blocking=True)
-        M_h.copy_(M, non_blocking=True)
+    def e2e_step(i):
+        k = i & 1
+        with torch.cuda.stream(s_up):
+            s_up.wait_event(ev_done[k])  # step i - 2 is done reading this input slot
+            for d_, h_ in zip(dev_in[k], host):
+                d_.copy_(h_, non_blocking=True)
+            ev_in[k].record(s_up)
+        stream.wait_event(ev_in[k])
+        stream.wait_event(ev_read[k])  # step i - 2's outputs have left this slot
+        _, M = chunkwise_forward(*dev_in[k], C, None, out=dev_out[k])
+        ev_done[k].record(stream)
+        with torch.cuda.stream(s_down):
+            s_down.wait_event(ev_done[k])
+            out_h[k].copy_(dev_out[k], non_blocking=True)
+            M_h[k].copy_(M, non_blocking=True)
+            M.record_stream(s_down)
+            ev_read[k].record(s_down)
 
-    e2e_steps = max(1, min(args.steps, 5))
-    for _ in range(2):
-        e2e_step()
+    e2e_steps = max(4, min(args.steps, 10))
+    for i in range(2):
+        e2e_step(i)
     torch.cuda.synchronize()
     barrier(world)
     ev0.record(stream)
-    for _ in range(e2e_steps):
-        e2e_step()
+    for i in range(e2e_steps):
+        e2e_step(i)
+    stream.wait_stream(s_up)
+    stream.wait_stream(s_down)
     ev1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(ev0.elapsed_time(ev1) / e2e_steps, world)
     h2d = sum(t.numel() * t.element_size() for t in host)
-    d2h = out_h.numel() * 4 + M_h.numel() * 8
+    d2h = out_h[0].numel() * 4 + M_h[0].numel() * 8
 
     peaks, src = load_peaks()
     alg_bytes = core_algorithmic_bytes(B, H, L, D, D)
@@ -281,14 +304,16 @@ def run_core(args, world, rank, local):
                      "kernel": "dp_core_fwd (one launch per step)"},
         "e2e": {"value": tokens / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
-                "path": "delta_phase_chunkwise_fused from pinned host buffers, out+M read back"},
+                "path": "kernels.chunkwise_forward from pinned host buffers, out + M read back every step; "
+                        "steps pipelined over two copy streams (inputs of step i+1 up while step i "
+                        "computes and its outputs come down)"},
         "gpu_launches": args.steps,
         "clocks": clk,
         "library": _capi.version(),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         parts = []
-        _, reps = repeat_for(lambda i: parts.append(cpu_core_sample(units=args.cpu_units, seed=i)))
+        _, reps = repeat_for(lambda i: parts.append(cpu_core_sample(units=args.cpu_units, seed=i)), min_seconds=13.0)
         secs, ht = sum(p[0] for p in parts), sum(p[1] for p in parts)  # timed regions only
         line["cpu_baseline"] = {
             "value": ht / H / secs, "unit": "tokens/s", "cores": cpu_threads(), "kind": "port",
