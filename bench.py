@@ -298,7 +298,7 @@ def run_core(args, world, rank, local):
                    "l2": f"inputs+outputs {alg_bytes / 1e6:.0f} MB per step > 126 MB L2; no flush"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": achieved / peaks["hbm_gbs"],
-                     "traffic": read_profile_traffic("core_tc_kernel_config2_ncu_full.md"),
+                     "traffic": read_profile_traffic("core_tc_kernel_b8h16l8192_ncu_full.md"),
                      "algorithmic_bytes_per_launch": alg_bytes,
                      "peak_source": f"{src} (MEASURED_PEAKS.json hbm_gbs)" if src == "measured" else src,
                      "kernel": "dp_core_fwd (one launch per step)"},
@@ -412,7 +412,7 @@ def run_cbeta(args, world, rank, local):
 
 
 def run_train(args, world, rank, local):
-    """Training step of the chunkwise core at config 2 (B=8, H=16, L=8192, d_k=64, bf16
+    """Training step of the chunkwise core at B=8, H=16, L=8192, d_k=64 (bf16
     phases/values): forward (tensor-core kernel) and backward (dp_core_bwd) through
     DeltaPhaseCudaFunction, gradients of theta_k, theta_q, v and beta."""
     import torch

@@ -191,3 +191,31 @@ def test_model_training_step():
         opt.step()
         losses.append(float(loss.detach()))
     assert losses[-1] < losses[0]
+
+
+@pytest.mark.parametrize("kind", ["hb", "cb"])
+def test_block_training_under_bf16_autocast(kind):
+    """As the reference's AMP test (tests/test_amp_dtypes.py:31-97): forward and backward
+    under bf16 autocast stay finite, and the forward agrees with the float32 step loop
+    (the projections run in bf16 there, the core on its tensor-core kernel)."""
+    torch.manual_seed(5)
+    if kind == "hb":
+        blk = dp.DeltaPhaseHolographicBlock(d_model=512, n_heads=8, chunk_size=64)
+    else:
+        blk = dp.ComplexBetaDeltaPhaseBlock(d_model=512, n_heads=8)
+    blk = blk.cuda().train()
+    x = torch.randn(2, 130, 512, device="cuda", requires_grad=True)
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        out, M = blk(x)
+        loss = out.float().pow(2).mean() + M.abs().pow(2).mean()
+    loss.backward()
+    assert torch.isfinite(out.float()).all() and torch.isfinite(x.grad).all()
+    for name, prm in blk.named_parameters():
+        assert prm.grad is not None and torch.isfinite(prm.grad).all(), name
+    with torch.no_grad():
+        st = None
+        outs = []
+        for t in range(x.shape[1]):
+            o, st = blk.step(x[:, t:t + 1].detach(), st)
+            outs.append(o)
+    assert rel_l2(out.float(), torch.cat(outs, 1)) < 5e-2

@@ -120,7 +120,7 @@ def test_dispatcher_contract():
     assert x.grad is not None and x.grad.shape == x.shape and torch.isfinite(x.grad).all()
 
 
-def test_config2_slice_parity_bf16():
+def test_full_length_slice_parity_bf16():
     """Full-length (L = 8192, d_k = 64) units of the B=8, H=16 workload vs the fp64 oracle."""
     tk, tq, v, beta = core_inputs(0, 1, 2, 8192, 64)
     tk, tq, v, beta = (round_bf16(a) for a in (tk, tq, v, beta))
@@ -131,7 +131,7 @@ def test_config2_slice_parity_bf16():
     assert rel_l2(M, ref_M) < TOL_BF16
 
 
-def _config2_inputs(seed=0, B=8, H=16, L=8192, D=64):
+def _b8h16_l8192_inputs(seed=0, B=8, H=16, L=8192, D=64):
     g = torch.Generator(device="cuda").manual_seed(seed)
     tk = (torch.rand(B, H, L, D, device="cuda", generator=g) * 2 * np.pi).to(torch.bfloat16)
     tq = (torch.rand(B, H, L, D, device="cuda", generator=g) * 2 * np.pi).to(torch.bfloat16)
@@ -140,11 +140,11 @@ def _config2_inputs(seed=0, B=8, H=16, L=8192, D=64):
     return tk, tq, v, beta
 
 
-def test_config2_full_size_properties():
+def test_b8h16_l8192_properties():
     """Size-independent checks at the full B=8, H=16, L=8192, d_k=64 workload:
     (b, h) units are independent, the result is linear in v (zero initial state), and
     a split sequence with state hand-off equals the single pass."""
-    tk, tq, v, beta = _config2_inputs()
+    tk, tq, v, beta = _b8h16_l8192_inputs()
     out, M = chunkwise_forward(tk, tq, v, beta, 64)
     assert torch.isfinite(out).all() and torch.isfinite(torch.view_as_real(M)).all()
     for (b, h) in [(0, 0), (3, 7), (7, 15)]:
