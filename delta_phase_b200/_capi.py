@@ -37,6 +37,8 @@ _SIG = {
     "dp_phasor": (_I, [_P, _I, ctypes.c_int64, _P, _P]),
     "dp_laplace_fwd": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _P, _P, _P, _I, _I, _I, _I, _I,
                             _I, _I64P, _P]),
+    "dp_laplace_bwd_workspace_size": (ctypes.c_size_t, [_I, _I, _I, _I, _I]),
+    "dp_laplace_bwd": (_I, [_P] * 7 + [_I, _I] + [_P] * 11 + [_I] * 5 + [_I64P, _P, ctypes.c_size_t, _P]),
     "dp_ffn_fold": (_I, [_P, _P, _P, _P, _P, _I, _I, _P]),
     "dp_ffn_workspace_size": (ctypes.c_size_t, [_I, _I, _I]),
     "dp_ffn_fwd": (_I, [_P, _I, _P, _P, _P, _I, _I, _P, ctypes.c_size_t, _P]),
@@ -253,6 +255,30 @@ def laplace_fwd(theta_k, logmag_k, theta_q, logmag_q, v, log_decay, beta, chunk_
                                   ptr(state_in), ptr(out), ptr(state_out), B, H, L, D, Dv,
                                   int(chunk_size), strides_array(st), stream_of(dev))
     _check("dp_laplace_fwd", rc)
+
+
+def laplace_bwd(theta_k, logmag_k, theta_q, logmag_q, v, log_decay, beta, state_in, grad_out, grad_state_out,
+                grads, grad_state_in):
+    """dp_laplace_bwd.  ``grads`` = (theta_k, logmag_k, theta_q, logmag_q, v, log_decay, beta)
+    gradient outputs, float32 contiguous; state tensors are float32 views of complex64
+    states or None."""
+    dev = require_cuda(theta_k, theta_q, v, log_decay, beta, grad_out, *grads)
+    B, H, L, D = theta_k.shape
+    Dv = v.shape[-1]
+    for t in (grad_out,) + tuple(grads):
+        if t.dtype != torch.float32 or not t.is_contiguous():
+            raise ValueError("gradient tensors must be contiguous float32")
+    st = []
+    for t in (theta_k, logmag_k, theta_q, logmag_q, v, log_decay):
+        st += (0, 0, 0) if t is None else seq_strides(t)
+    st += (beta.stride(0), beta.stride(1), beta.stride(2))
+    ws = torch.empty(max(1, int(lib().dp_laplace_bwd_workspace_size(B, H, L, D, Dv))), device=dev, dtype=torch.uint8)
+    with torch.cuda.device(dev):
+        rc = lib().dp_laplace_bwd(ptr(theta_k), ptr(logmag_k), ptr(theta_q), ptr(logmag_q), ptr(v), ptr(log_decay),
+                                  ptr(beta), dtype_code(theta_k), dtype_code(beta), ptr(state_in), ptr(grad_out),
+                                  ptr(grad_state_out), *[ptr(g) for g in grads], ptr(grad_state_in), B, H, L, D, Dv,
+                                  strides_array(st), ptr(ws), ws.numel(), stream_of(dev))
+    _check("dp_laplace_bwd", rc)
 
 
 def ffn_fold(logits, mats, banks, combine, F, d, nb):

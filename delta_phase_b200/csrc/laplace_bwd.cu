@@ -1,0 +1,379 @@
+// Backward of the LaplacePhaseCore recurrence (training path): gradients with respect to
+// theta_k, log|k|, theta_q, log|q|, v, log r (the per-row decay), beta and the initial state.
+//
+// The reference trains LaplacePhaseCore through PyTorch autograd of its chunk loop
+// (delta_phase/layers.py:481-561; its tests check the gradient flow through the solve,
+// tests/test_laplace_chunkwise.py).  The recurrence, per value row o (real form,
+// kap = |k| [cos theta_k, sin theta_k] interleaved, xi likewise for q):
+//   e_t = v_t - S_{t-1} kap_t / D,  S_t = diag(r_t) S_{t-1} + beta_t e_t kap_t^T,
+//   o_t = S_t xi_t / D,  r_t = exp(max(log r_t, -80))  (layers.py:512)
+// and its adjoint, backwards in t with dS = dL/dS_t:
+//   dS += dO_t xi_t^T / D;  dxi_t = S_t^T dO_t / D;  du_t = dS kap_t;  dkap_t = dS^T u_t;
+//   dr_t = rowsum(dS o S_{t-1});  dbeta_t = du_t . e_t;  de_t = beta_t du_t = dv_t;
+//   dS <- diag(r_t) dS - de_t kap_t^T / D;  dkap_t -= S_{t-1}^T de_t / D;
+//   d log r = r dr (0 where the clamp is active), d theta = -kap_s dkap_c + kap_c dkap_s,
+//   d log|k| = kap_c dkap_c + kap_s dkap_s (and the same for q).
+// A strong decay (r down to e^-80) makes S_{t-1} unrecoverable from S_t, so nothing is
+// undone: pass 1 runs the recurrence forward and keeps the state at every 32-token
+// sub-chunk start; pass 2 takes the sub-chunks backwards, recomputes the sub-chunk's
+// states from its checkpoint into a per-unit scratch (32 KB per token at D = Dv = 64,
+// L2-resident) and then walks back through them.
+//
+// One CTA of 256 threads per (b, h): warp w holds rows 32 (w / 4) .. +31 of column
+// 32 (w % 4) + lane of S and dS in registers (D <= 64, Dv <= 64).  Row sums are warp
+// reduce-scatters plus a 4-way shared-memory sum; the column sums of the two row halves
+// are paired through shared memory one token later.
+#include "dp_common.cuh"
+
+namespace dp {
+namespace {
+
+constexpr int kLT = 256;     // threads
+constexpr int kLC = 32;      // tokens per sub-chunk
+constexpr int kLF = 128;     // key features (2 D) at most
+constexpr int kLDv = 64;     // value rows at most
+constexpr float kLogFloor = -80.f;
+
+struct LapBwdArgs {
+  const void *tk, *mk, *tq, *mq, *v, *ld, *beta;  // mk, mq may be null (unit magnitudes)
+  int in_dt, beta_dt;
+  SeqStrides s_tk, s_mk, s_tq, s_mq, s_v, s_ld, s_b;
+  const float *state_in, *dout, *dstate_out;  // dout (B,H,L,Dv) contiguous; the others may be null
+  float *dtk, *dmk, *dtq, *dmq;               // (B,H,L,D)
+  float *dv, *dld;                            // (B,H,L,Dv)
+  float *dbeta;                               // (B,H,L), accumulated: zeroed by the entry point
+  float *dstate_in;                           // may be null
+  float *ckpt;                                // (B*H, NSC, Dv, F) states at sub-chunk starts
+  float *scratch;                             // (B*H, kLC + 1, Dv, F) states inside a sub-chunk
+  int H, L, D, Dv;
+};
+
+struct LapStage {
+  float kc[kLC][64], ks[kLC][64];  // key features |k| cos, |k| sin per channel
+  float qc[kLC][64], qs[kLC][64];
+  float v[kLC][64], r[kLC][64], rg[kLC][64];  // rg = r where log r > -80, else 0 (clamp gradient)
+  float dout[kLC][64], u[kLC][64], e[kLC][64];
+  float beta[kLC];
+};
+
+__device__ __forceinline__ float load_any(const void *p, int dt, int64_t i) {
+  if (dt == DP_F32) return static_cast<const float *>(p)[i];
+  if (dt == DP_BF16) return __bfloat162float(static_cast<const __nv_bfloat16 *>(p)[i]);
+  return __half2float(static_cast<const __half *>(p)[i]);
+}
+
+// Lane l returns the sum over the warp's lanes of x[l] (reduce-scatter of 32 values).
+__device__ __forceinline__ float reduce_scatter32(float (&x)[32], int lane) {
+#pragma unroll
+  for (int k = 16; k >= 1; k >>= 1) {
+    const bool upper = (lane & k) != 0;
+#pragma unroll
+    for (int i = 0; i < k; ++i) {
+      const float send = upper ? x[i] : x[i + k];
+      const float keep = upper ? x[i + k] : x[i];
+      x[i] = keep + __shfl_xor_sync(0xffffffffu, send, k);
+    }
+  }
+  return x[0];
+}
+
+// Tokens [t0, t0 + n) of this (b, h) into the stage; every global load of a thread is
+// issued before its arithmetic and shared stores.  Rows / channels past n, D, Dv are zero
+// (decay 1 for the absent tokens, so a partial sub-chunk leaves the state alone).
+__device__ void lap_stage(const LapBwdArgs &a, LapStage &st, int b, int h, int t0, int n, bool bwd, int64_t row_base) {
+  constexpr int kPer = kLC * 64 / kLT;
+  const int tid = threadIdx.x;
+  float xk[kPer], xmk[kPer], xq[kPer], xmq[kPer], xv[kPer], xl[kPer], xo[kPer];
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int idx = tid + i * kLT, r = idx >> 6, c = idx & 63, t = t0 + r;
+    const bool ok = r < n;
+    xk[i] = xmk[i] = xq[i] = xmq[i] = xv[i] = xo[i] = 0.f;
+    xl[i] = 0.f;
+    if (ok && c < a.D) {
+      xk[i] = load_any(a.tk, a.in_dt, b * a.s_tk.b + h * a.s_tk.h + (int64_t)t * a.s_tk.t + c);
+      if (a.mk) xmk[i] = load_any(a.mk, a.in_dt, b * a.s_mk.b + h * a.s_mk.h + (int64_t)t * a.s_mk.t + c);
+      if (bwd) {
+        xq[i] = load_any(a.tq, a.in_dt, b * a.s_tq.b + h * a.s_tq.h + (int64_t)t * a.s_tq.t + c);
+        if (a.mq) xmq[i] = load_any(a.mq, a.in_dt, b * a.s_mq.b + h * a.s_mq.h + (int64_t)t * a.s_mq.t + c);
+      }
+    }
+    if (ok && c < a.Dv) {
+      xv[i] = load_any(a.v, a.in_dt, b * a.s_v.b + h * a.s_v.h + (int64_t)t * a.s_v.t + c);
+      xl[i] = load_any(a.ld, a.in_dt, b * a.s_ld.b + h * a.s_ld.h + (int64_t)t * a.s_ld.t + c);
+      if (bwd) xo[i] = a.dout[row_base + (int64_t)t * a.Dv + c];
+    }
+  }
+  float xb = 0.f;
+  if (tid < kLC && tid < n) xb = load_any(a.beta, a.beta_dt, b * a.s_b.b + h * a.s_b.h + (int64_t)(t0 + tid) * a.s_b.t);
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int idx = tid + i * kLT, r = idx >> 6, c = idx & 63;
+    const bool ok = r < n;
+    float s, co, mag = __expf(xmk[i]);
+    sincosf(xk[i], &s, &co);
+    st.kc[r][c] = (ok && c < a.D) ? mag * co : 0.f;
+    st.ks[r][c] = (ok && c < a.D) ? mag * s : 0.f;
+    if (bwd) {
+      mag = __expf(xmq[i]);
+      sincosf(xq[i], &s, &co);
+      st.qc[r][c] = (ok && c < a.D) ? mag * co : 0.f;
+      st.qs[r][c] = (ok && c < a.D) ? mag * s : 0.f;
+      st.dout[r][c] = xo[i];
+    }
+    st.v[r][c] = xv[i];
+    const bool live = ok && c < a.Dv;
+    const float r_ = live ? __expf(fmaxf(xl[i], kLogFloor)) : 1.f;
+    st.r[r][c] = r_;
+    st.rg[r][c] = (live && xl[i] > kLogFloor) ? r_ : 0.f;
+  }
+  if (tid < kLC) st.beta[tid] = xb;
+}
+
+// One forward token (row o = row0 + lane of this warp): e, u = beta e, S = diag(r) S + u kap^T.
+// Returns u for this lane's row and e through *e_out.
+__device__ __forceinline__ float lap_fwd_token(float (&S)[32], float (*red)[4][64], const LapStage &st, int r, int j,
+                                               int cb, int row0, int lane, float invD, float *e_out) {
+  const float kap = (j & 1) ? st.ks[r][j >> 1] : st.kc[r][j >> 1];
+  float x[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) x[i] = S[i] * kap;
+  red[0][cb][row0 + lane] = reduce_scatter32(x, lane);
+  __syncthreads();
+  const int o = row0 + lane;
+  const float skr = red[0][0][o] + red[0][1][o] + red[0][2][o] + red[0][3][o];
+  const float e = st.v[r][o] - skr * invD;
+  const float u = st.beta[r] * e;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) S[i] = fmaf(__shfl_sync(0xffffffffu, u, i), kap, st.r[r][row0 + i] * S[i]);
+  *e_out = e;
+  return u;
+}
+
+__global__ void __launch_bounds__(kLT, 1) laplace_bwd_kernel(LapBwdArgs a) {
+  extern __shared__ __align__(16) uint8_t lsm[];
+  LapStage &st = *reinterpret_cast<LapStage *>(lsm);
+  float(*red)[2][4][64] = reinterpret_cast<float(*)[2][4][64]>(lsm + sizeof(LapStage));   // [par][which][cb][row]
+  float(*colb)[2][2][128] =
+      reinterpret_cast<float(*)[2][2][128]>(lsm + sizeof(LapStage) + sizeof(float) * 2 * 2 * 4 * 64);  // [par][rh][q][j]
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int rh = warp >> 2, cb = warp & 3, j = 32 * cb + lane, row0 = 32 * rh;
+  const int bh = blockIdx.x, b = bh / a.H, h = bh % a.H;
+  const int L = a.L, D = a.D, Dv = a.Dv, F = 2 * D;
+  const bool col_ok = j < F;
+  const float invD = 1.0f / (float)D;
+  const int nsc = (L + kLC - 1) / kLC;
+  const int64_t row_base = (int64_t)bh * L * Dv;
+  const int64_t st_base = (int64_t)bh * Dv * F;
+  float *ckpt = a.ckpt + (int64_t)bh * nsc * Dv * F;
+  float *scr = a.scratch + (int64_t)bh * (kLC + 1) * Dv * F;
+
+  float S[32], dS[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const int o = row0 + i;
+    S[i] = (a.state_in && col_ok && o < Dv) ? a.state_in[st_base + (int64_t)o * F + j] : 0.f;
+  }
+
+  // ---- pass 1: forward, state at every sub-chunk start to the checkpoints
+  int par = 0;
+  for (int sc = 0; sc < nsc; ++sc) {
+    const int t0 = sc * kLC, n = min(kLC, L - t0);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const int o = row0 + i;
+      if (col_ok && o < Dv) ckpt[((int64_t)sc * Dv + o) * F + j] = S[i];
+    }
+    __syncthreads();
+    lap_stage(a, st, b, h, t0, n, false, row_base);
+    __syncthreads();
+    for (int r = 0; r < n; ++r, par ^= 1) {
+      float e;
+      lap_fwd_token(S, red[par], st, r, j, cb, row0, lane, invD, &e);
+    }
+  }
+
+  // ---- pass 2: sub-chunks backwards
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const int o = row0 + i;
+    dS[i] = (a.dstate_out && col_ok && o < Dv) ? a.dstate_out[st_base + (int64_t)o * F + j] : 0.f;
+  }
+  int pend_t = -1, pend_par = 0;
+  float pend_kc = 0.f, pend_ks = 0.f, pend_qc = 0.f, pend_qs = 0.f;
+  auto finish = [&](int t, int pp, float kc, float ks, float qc, float qs) {
+    // even lane: channel j / 2 (own = cos column, partner = sin column)
+    const float dk = colb[pp][0][0][j] + colb[pp][1][0][j];
+    const float dq = (colb[pp][0][1][j] + colb[pp][1][1][j]) * invD;
+    const float dk2 = __shfl_xor_sync(0xffffffffu, dk, 1), dq2 = __shfl_xor_sync(0xffffffffu, dq, 1);
+    if (!(j & 1) && col_ok) {
+      const int64_t gi = ((int64_t)bh * L + t) * D + (j >> 1);
+      a.dtk[gi] = -ks * dk + kc * dk2;
+      a.dmk[gi] = kc * dk + ks * dk2;
+      a.dtq[gi] = -qs * dq + qc * dq2;
+      a.dmq[gi] = qc * dq + qs * dq2;
+    }
+  };
+  for (int sc = nsc - 1; sc >= 0; --sc) {
+    const int t0 = sc * kLC, n = min(kLC, L - t0);
+    // the sub-chunk's states: checkpoint -> scratch slot 0, S_t -> slot r + 1
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const int o = row0 + i;
+      S[i] = (col_ok && o < Dv) ? ckpt[((int64_t)sc * Dv + o) * F + j] : 0.f;
+      if (col_ok && o < Dv) scr[(int64_t)o * F + j] = S[i];
+    }
+    __syncthreads();
+    lap_stage(a, st, b, h, t0, n, true, row_base);
+    __syncthreads();
+    for (int r = 0; r < n; ++r, par ^= 1) {
+      float e;
+      const float u = lap_fwd_token(S, red[par], st, r, j, cb, row0, lane, invD, &e);
+      if (cb == 0) {
+        st.u[r][row0 + lane] = u;
+        st.e[r][row0 + lane] = e;
+      }
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int o = row0 + i;
+        if (col_ok && o < Dv) scr[((int64_t)(r + 1) * Dv + o) * F + j] = S[i];
+      }
+    }
+    __syncthreads();  // u, e of the sub-chunk are in the stage
+    for (int r = n - 1; r >= 0; --r, par ^= 1) {
+      const int t = t0 + r;
+      float Sp[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int o = row0 + i;
+        Sp[i] = (col_ok && o < Dv) ? scr[((int64_t)r * Dv + o) * F + j] : 0.f;
+      }
+      const float kap = (j & 1) ? st.ks[r][j >> 1] : st.kc[r][j >> 1];
+      const float xi = (j & 1) ? st.qs[r][j >> 1] : st.qc[r][j >> 1];
+      float pq = 0.f, pw = 0.f, x1[32], x2[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const float dO = st.dout[r][row0 + i];
+        dS[i] = fmaf(dO * invD, xi, dS[i]);
+        pq = fmaf(S[i], dO, pq);
+        pw = fmaf(dS[i], st.u[r][row0 + i], pw);
+        x1[i] = dS[i] * kap;
+        x2[i] = dS[i] * Sp[i];
+      }
+      red[par][0][cb][row0 + lane] = reduce_scatter32(x1, lane);
+      red[par][1][cb][row0 + lane] = reduce_scatter32(x2, lane);
+      __syncthreads();
+      if (pend_t >= 0 && rh == 0) finish(pend_t, pend_par, pend_kc, pend_ks, pend_qc, pend_qs);
+      const int o = row0 + lane;
+      const float du = red[par][0][0][o] + red[par][0][1][o] + red[par][0][2][o] + red[par][0][3][o];
+      const float dr = red[par][1][0][o] + red[par][1][1][o] + red[par][1][2][o] + red[par][1][3][o];
+      const float de = st.beta[r] * du;
+      if (cb == 0) {
+        if (o < Dv) {
+          a.dv[row_base + (int64_t)t * Dv + o] = de;
+          a.dld[row_base + (int64_t)t * Dv + o] = dr * st.rg[r][o];
+        }
+        float p = (o < Dv) ? du * st.e[r][o] : 0.f;
+#pragma unroll
+        for (int o2 = 16; o2 >= 1; o2 >>= 1) p += __shfl_xor_sync(0xffffffffu, p, o2);
+        if (lane == 0) atomicAdd(&a.dbeta[(int64_t)bh * L + t], p);
+      }
+      float pk = 0.f;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const float de_i = __shfl_sync(0xffffffffu, de, i);
+        dS[i] = fmaf(-de_i * invD, kap, st.r[r][row0 + i] * dS[i]);
+        pk = fmaf(Sp[i], de_i, pk);
+        S[i] = Sp[i];
+      }
+      colb[par][rh][0][j] = pw - pk * invD;
+      colb[par][rh][1][j] = pq;
+      pend_t = t;
+      pend_par = par;
+      pend_kc = st.kc[r][j >> 1];
+      pend_ks = st.ks[r][j >> 1];
+      pend_qc = st.qc[r][j >> 1];
+      pend_qs = st.qs[r][j >> 1];
+    }
+    __syncthreads();  // the stage is reloaded next
+  }
+  if (pend_t >= 0 && rh == 0) finish(pend_t, pend_par, pend_kc, pend_ks, pend_qc, pend_qs);
+  if (a.dstate_in) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const int o = row0 + i;
+      if (col_ok && o < Dv) a.dstate_in[st_base + (int64_t)o * F + j] = dS[i];
+    }
+  }
+}
+
+}  // namespace
+}  // namespace dp
+
+extern "C" size_t dp_laplace_bwd_workspace_size(int B, int H, int L, int D, int Dv) {
+  if (B <= 0 || H <= 0 || L <= 0 || D <= 0 || Dv <= 0) return 0;
+  const size_t nsc = ((size_t)L + dp::kLC - 1) / dp::kLC;
+  return (size_t)B * H * (nsc + dp::kLC + 1) * Dv * 2 * D * sizeof(float);
+}
+
+extern "C" int dp_laplace_bwd(const void *theta_k, const void *logmag_k, const void *theta_q, const void *logmag_q,
+                              const void *v, const void *log_decay, const void *beta, int in_dtype, int beta_dtype,
+                              const float *state_in, const float *grad_out, const float *grad_state_out,
+                              float *grad_theta_k, float *grad_logmag_k, float *grad_theta_q, float *grad_logmag_q,
+                              float *grad_v, float *grad_log_decay, float *grad_beta, float *grad_state_in, int B,
+                              int H, int L, int D, int Dv, const int64_t *strides, void *workspace,
+                              size_t workspace_bytes, void *stream) {
+  using namespace dp;
+  DP_REQUIRE(B >= 0 && H >= 0 && L >= 0, DP_ERR_INVALID_ARGUMENT, "dp_laplace_bwd: negative size");
+  DP_REQUIRE(D >= 1 && Dv >= 1, DP_ERR_INVALID_ARGUMENT, "dp_laplace_bwd: D and Dv must be >= 1");
+  DP_REQUIRE(D <= 64 && Dv <= 64, DP_ERR_UNSUPPORTED, "dp_laplace_bwd: D and Dv must be <= 64");
+  DP_REQUIRE(valid_dtype(in_dtype) && valid_dtype(beta_dtype), DP_ERR_INVALID_ARGUMENT,
+             "dp_laplace_bwd: bad dtype code");
+  if (B == 0 || H == 0) return DP_OK;
+  DP_REQUIRE(strides, DP_ERR_INVALID_ARGUMENT, "dp_laplace_bwd: null strides");
+  if (L > 0) {
+    DP_REQUIRE(theta_k && theta_q && v && log_decay && beta && grad_out && grad_theta_k && grad_logmag_k &&
+                   grad_theta_q && grad_logmag_q && grad_v && grad_log_decay && grad_beta,
+               DP_ERR_INVALID_ARGUMENT, "dp_laplace_bwd: null pointer");
+    DP_REQUIRE(workspace && workspace_bytes >= dp_laplace_bwd_workspace_size(B, H, L, D, Dv), DP_ERR_WORKSPACE,
+               "dp_laplace_bwd: workspace too small (dp_laplace_bwd_workspace_size)");
+    const cudaError_t e = cudaMemsetAsync(grad_beta, 0, (size_t)B * H * L * sizeof(float), as_stream(stream));
+    if (e != cudaSuccess) return set_error(DP_ERR_CUDA, std::string("dp_laplace_bwd: memset: ") + cudaGetErrorString(e));
+  }
+  LapBwdArgs a;
+  a.tk = theta_k;
+  a.mk = logmag_k;
+  a.tq = theta_q;
+  a.mq = logmag_q;
+  a.v = v;
+  a.ld = log_decay;
+  a.beta = beta;
+  a.in_dt = in_dtype;
+  a.beta_dt = beta_dtype;
+  SeqStrides *ss[7] = {&a.s_tk, &a.s_mk, &a.s_tq, &a.s_mq, &a.s_v, &a.s_ld, &a.s_b};
+  for (int i = 0; i < 7; ++i) *ss[i] = SeqStrides{strides[3 * i], strides[3 * i + 1], strides[3 * i + 2]};
+  a.state_in = state_in;
+  a.dout = grad_out;
+  a.dstate_out = grad_state_out;
+  a.dtk = grad_theta_k;
+  a.dmk = grad_logmag_k;
+  a.dtq = grad_theta_q;
+  a.dmq = grad_logmag_q;
+  a.dv = grad_v;
+  a.dld = grad_log_decay;
+  a.dbeta = grad_beta;
+  a.dstate_in = grad_state_in;
+  const size_t nsc = ((size_t)L + kLC - 1) / kLC;
+  a.ckpt = static_cast<float *>(workspace);
+  a.scratch = a.ckpt + (size_t)B * H * nsc * Dv * 2 * D;
+  a.H = H;
+  a.L = L;
+  a.D = D;
+  a.Dv = Dv;
+  const size_t smem = sizeof(LapStage) + sizeof(float) * (2 * 2 * 4 * 64 + 2 * 2 * 2 * 128);
+  cudaError_t e = cudaFuncSetAttribute(laplace_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return set_error(DP_ERR_CUDA, std::string("dp_laplace_bwd smem attr: ") + cudaGetErrorString(e));
+  laplace_bwd_kernel<<<B * H, kLT, smem, as_stream(stream)>>>(a);
+  return check_launch("laplace_bwd_kernel");
+}

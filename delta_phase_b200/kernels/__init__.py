@@ -2,6 +2,7 @@
 from .chunk_delta import (
     DeltaPhaseCudaFunction,
     DeltaPhaseTritonFunction,
+    LaplaceCudaFunction,
     chunkwise_forward,
     complex_beta_chunkwise,
     cuda_available,
@@ -19,6 +20,7 @@ __all__ = [
     "triton_available",
     "DeltaPhaseTritonFunction",
     "DeltaPhaseCudaFunction",
+    "LaplaceCudaFunction",
     "cuda_available",
     "chunkwise_forward",
     "complex_beta_chunkwise",

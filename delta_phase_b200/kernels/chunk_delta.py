@@ -18,7 +18,8 @@ Drop-in for ``delta_phase.kernels.triton_chunk_delta`` (mcarbonell/delta-phase v
   complex-beta rule of ComplexBetaDeltaPhaseBlock (layers.py:294-418), ``beta`` then
   holding phi of beta = 1 + e^{i phi}; :func:`complex_beta_chunkwise` is its chunkwise
   form over a sequence (the reference's token loop, layers.py:346-360).
-* :func:`laplace_chunkwise` -- the LaplacePhaseCore chunk solve (layers.py:481-561).
+* :func:`laplace_chunkwise` -- the LaplacePhaseCore chunk solve (layers.py:481-561);
+  differentiable through :class:`LaplaceCudaFunction` (backward on ``dp_laplace_bwd``).
 * :func:`triton_available` -- kept for API compatibility; True when the CUDA library
   is loaded and a GPU is present (the kernels it reported on are replaced here).
 """
@@ -211,6 +212,41 @@ def decode_step(memory_state, theta_k, theta_q, v, beta, out=None, state_out=Non
     return out, state_out
 
 
+class LaplaceCudaFunction(torch.autograd.Function):
+    """Autograd wrapper of the Laplace core: forward on dp_laplace_fwd, backward on
+    dp_laplace_bwd (gradients of every input in its own dtype; None for absent
+    log-magnitudes)."""
+
+    @staticmethod
+    def forward(ctx, theta_k, logmag_k, theta_q, logmag_q, v, log_decay, beta, chunk_size=32, initial_state=None):
+        out, M = _laplace_forward(theta_k, logmag_k, theta_q, logmag_q, v, log_decay, beta, chunk_size,
+                                  initial_state, None)
+        ctx.save_for_backward(theta_k, logmag_k, theta_q, logmag_q, v, log_decay, beta, initial_state)
+        return out, M
+
+    @staticmethod
+    def backward(ctx, grad_out, grad_final_state):
+        tk, mk, tq, mq, v, ld, beta, M0 = ctx.saved_tensors
+        B, H, L, D = tk.shape
+        Dv = v.shape[-1]
+        dev = tk.device
+        f32 = dict(device=dev, dtype=torch.float32)
+        go = (torch.zeros(B, H, L, Dv, **f32) if grad_out is None else grad_out.to(torch.float32).contiguous())
+        gM = (None if grad_final_state is None
+              else torch.view_as_real(grad_final_state.to(torch.complex64).contiguous()))
+        s_in = None if M0 is None else torch.view_as_real(M0.detach().to(torch.complex64).contiguous())
+        grads = (torch.empty(B, H, L, D, **f32), torch.empty(B, H, L, D, **f32), torch.empty(B, H, L, D, **f32),
+                 torch.empty(B, H, L, D, **f32), torch.empty(B, H, L, Dv, **f32), torch.empty(B, H, L, Dv, **f32),
+                 torch.empty(B, H, L, **f32))
+        need_m0 = M0 is not None and ctx.needs_input_grad[8]
+        dM0 = torch.empty(B, H, Dv, D, device=dev, dtype=torch.complex64) if need_m0 else None
+        _capi.laplace_bwd(tk, mk, tq, mq, v, ld, beta, s_in, go, gM, grads,
+                          None if dM0 is None else torch.view_as_real(dM0))
+        like = (tk, mk, tq, mq, v, ld, beta)
+        res = [None if x is None else g.to(x.dtype) for g, x in zip(grads, like)]
+        return (*res, None, None if dM0 is None else dM0.to(M0.dtype))
+
+
 def laplace_chunkwise(theta_k, logmag_k, theta_q, logmag_q, v, log_decay, beta, chunk_size=32,
                       initial_state=None, out=None):
     """LaplacePhaseCore chunk solve (layers.py:481-561) on the CUDA kernel.
@@ -218,8 +254,21 @@ def laplace_chunkwise(theta_k, logmag_k, theta_q, logmag_q, v, log_decay, beta, 
     K = exp(logmag_k) e^{i theta_k}, Q = exp(logmag_q) e^{i theta_q} ((B,H,L,D); the
     log-magnitudes may be None = unit phasors); log_decay (B,H,L,Dv) is log r per value
     channel (clamped at -80 per step like the reference); beta (B,H,L).
-    Returns ``(out (B,H,L,Dv) float32, M (B,H,Dv,D) complex64)``.
+    Returns ``(out (B,H,L,Dv) float32, M (B,H,Dv,D) complex64)``.  Differentiable (through
+    LaplaceCudaFunction) when autograd records and an input requires grad; ``out`` must
+    then be None.
     """
+    if torch.is_grad_enabled() and any(t is not None and t.requires_grad for t in (
+            theta_k, logmag_k, theta_q, logmag_q, v, log_decay, beta, initial_state)):
+        if out is not None:
+            raise ValueError("out= is not supported when gradients are recorded")
+        return LaplaceCudaFunction.apply(theta_k, logmag_k, theta_q, logmag_q, v, log_decay, beta, chunk_size,
+                                         initial_state)
+    return _laplace_forward(theta_k, logmag_k, theta_q, logmag_q, v, log_decay, beta, chunk_size, initial_state,
+                            out)
+
+
+def _laplace_forward(theta_k, logmag_k, theta_q, logmag_q, v, log_decay, beta, chunk_size, initial_state, out):
     B, H, L, D = theta_k.shape
     Dv = v.shape[-1]
     _capi.require_cuda(theta_k, theta_q, v, log_decay, beta)

@@ -15,7 +15,7 @@ CUDA library, with no CPU fallback.  Training: when autograd is recording (grad 
 and an input or parameter requires grad -- the reference dispatcher's rule,
 triton_chunk_delta.py:279-291), the two delta-rule blocks run their glue and the FFN as
 differentiable torch ops and the core through DeltaPhaseCudaFunction (backward on the
-dp_core_bwd kernel).  LaplacePhaseCore has no backward.
+dp_core_bwd kernel); LaplacePhaseCore through LaplaceCudaFunction (dp_laplace_bwd).
 """
 from __future__ import annotations
 
@@ -479,6 +479,12 @@ class LaplacePhaseCore(nn.Module):
     def forward(self, x: torch.Tensor, memory_state=None, time_scale: float = 1.0):
         theta_k, sigma_k, theta_q, sigma_q, v, beta = self._proj(x, time_scale)
         B, H, L, dk = theta_k.shape
+        if _records_autograd(self, x, memory_state):
+            # training: sigma_k is both the key's log-magnitude and the row decay; autograd
+            # adds the two gradients
+            out, M = laplace_chunkwise(theta_k, sigma_k, theta_q, sigma_q, v, sigma_k, beta, self.chunk_size,
+                                       memory_state)
+            return out.transpose(1, 2).reshape(B, L, H * dk), M
         retrieved = torch.empty(B, L, H * dk, device=x.device, dtype=torch.float32)
         _, M = laplace_chunkwise(theta_k, sigma_k, theta_q, sigma_q, v, sigma_k, beta,
                                  self.chunk_size, memory_state,

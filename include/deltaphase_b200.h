@@ -192,6 +192,30 @@ DP_API int dp_laplace_fwd(const void *theta_k, const void *logmag_k, const void 
                    int chunk_size, const int64_t *strides, void *stream);
 
 /*
+ * Backward of dp_laplace_fwd (training): gradients with respect to theta_k, logmag_k,
+ * theta_q, logmag_q, v, log_decay, beta and the initial state, given grad_out = dL/d out
+ * and grad_state_out = dL/dM (or NULL = 0).  The reference trains LaplacePhaseCore through
+ * autograd of its chunk loop (delta_phase/layers.py:481-561); this is the adjoint of the
+ * same recurrence in fp32 (log r clamped at -80 like the forward, zero gradient there).
+ *   inputs, dtypes, strides[21] : as dp_laplace_fwd without `out` ({sb, sh, st} of
+ *                                 theta_k, logmag_k, theta_q, logmag_q, v, log_decay, beta)
+ *   grad_out                    : (B, H, L, Dv) float32, contiguous
+ *   grad_theta_k/logmag_k/theta_q/logmag_q : (B, H, L, D) float32, contiguous
+ *   grad_v, grad_log_decay      : (B, H, L, Dv) float32;  grad_beta : (B, H, L) float32
+ *   grad_state_in               : (B, H, Dv, D) complex64 as floats, or NULL
+ *   workspace                   : dp_laplace_bwd_workspace_size(B, H, L, D, Dv) bytes
+ * Limits: 1 <= D, Dv <= 64.
+ */
+DP_API size_t dp_laplace_bwd_workspace_size(int B, int H, int L, int D, int Dv);
+DP_API int dp_laplace_bwd(const void *theta_k, const void *logmag_k, const void *theta_q,
+                   const void *logmag_q, const void *v, const void *log_decay, const void *beta,
+                   int in_dtype, int beta_dtype, const float *state_in, const float *grad_out,
+                   const float *grad_state_out, float *grad_theta_k, float *grad_logmag_k,
+                   float *grad_theta_q, float *grad_logmag_q, float *grad_v, float *grad_log_decay,
+                   float *grad_beta, float *grad_state_in, int B, int H, int L, int D, int Dv,
+                   const int64_t *strides, void *workspace, size_t workspace_bytes, void *stream);
+
+/*
  * Fold the spectral Lerp FFN parameters into one (6d x d) matrix.
  * With a_b = cos(h_b + phi1_b) w1_b + sin(h_b + phi2_b) w2_b
  *           = cos(h_b) alpha_b + sin(h_b) gamma_b   (angle addition), the FFN of

@@ -367,8 +367,75 @@ def make_grad():
     save("grad", **arrays)
 
 
+def make_laplace_grad():
+    """LaplacePhaseCore gradients as the reference trains it: autograd (float64) of its
+    chunk loop (layers.py:481-561).  Core level: `_project` patched to build K, Q, v, beta
+    and r from leaf tensors (theta_k, log|k|, theta_q, log|q|, v, log r, beta), so the
+    gradients of exactly those inputs are recorded.  Module level: every parameter's
+    gradient for a seeded loss sum(out * R) + Re sum(conj(dM) M)."""
+    arrays = {}
+    cases = [(2, 2, 40, 8, 8, True), (1, 2, 33, 16, 32, False), (2, 1, 64, 16, 16, True)]
+    for i, (B, H, L, D, C, init) in enumerate(cases):
+        rng = np.random.default_rng(500 + i)
+        core = LaplacePhaseCore(d_model=H * D, n_heads=H, d_k=D, chunk_size=C).double()
+        leaves = {
+            "theta_k": rng.uniform(0, 2 * np.pi, (B, H, L, D)), "logmag_k": -0.5 * rng.random((B, H, L, D)),
+            "theta_q": rng.uniform(0, 2 * np.pi, (B, H, L, D)), "logmag_q": -0.5 * rng.random((B, H, L, D)),
+            "v": rng.standard_normal((B, H, L, D)), "log_decay": -np.log1p(np.exp(rng.standard_normal((B, H, L, D)))),
+            "beta": 2.0 / (1.0 + np.exp(-rng.standard_normal((B, H, L))))}
+        T = {k: torch.from_numpy(a).requires_grad_(True) for k, a in leaves.items()}
+
+        def project(x, ts, T=T):
+            K = torch.complex(torch.exp(T["logmag_k"]) * torch.cos(T["theta_k"]),
+                              torch.exp(T["logmag_k"]) * torch.sin(T["theta_k"]))
+            Q = torch.complex(torch.exp(T["logmag_q"]) * torch.cos(T["theta_q"]),
+                              torch.exp(T["logmag_q"]) * torch.sin(T["theta_q"]))
+            return K, Q, T["v"], T["beta"], torch.exp(T["log_decay"])
+
+        core._project = project
+        M0 = torch.from_numpy(rng.standard_normal((B, H, D, D)) + 1j * rng.standard_normal((B, H, D, D))) if init else None
+        if M0 is not None:
+            M0.requires_grad_(True)
+        dout = rng.standard_normal((B, L, H * D))
+        dM = rng.standard_normal((B, H, D, D)) + 1j * rng.standard_normal((B, H, D, D))
+        x = torch.zeros(B, L, H * D, dtype=torch.float64)
+        out, M = core(x, memory_state=M0)
+        loss = (out * torch.from_numpy(dout)).sum() + (torch.conj(torch.from_numpy(dM)) * M).real.sum()
+        loss.backward()
+        p = f"c{i}_"
+        for k, a in leaves.items():
+            arrays[p + k] = a
+            arrays[p + "d_" + k] = T[k].grad.numpy()
+        arrays.update({p + "C": C, p + "dM": dM, p + "out": out.detach().view(B, L, H, D).transpose(1, 2).numpy(),
+                       p + "M": M.detach().numpy(),
+                       p + "dout": dout.reshape(B, L, H, D).transpose(0, 2, 1, 3)})
+        if M0 is not None:
+            arrays[p + "M0"] = M0.detach().numpy()
+            arrays[p + "d_M0"] = M0.grad.numpy()
+    arrays["n_cases"] = len(cases)
+    # module level
+    torch.manual_seed(61)
+    core = LaplacePhaseCore(d_model=32, n_heads=2, d_k=16, chunk_size=8).double()
+    with torch.no_grad():
+        core.w_sigma_k.weight.mul_(3.0)
+    x = torch.randn(2, 29, 32, dtype=torch.float64)
+    R = torch.randn(2, 29, 32, dtype=torch.float64)
+    M0 = torch.randn(2, 2, 16, 16, dtype=torch.complex128).requires_grad_(True)
+    dM = torch.randn(2, 2, 16, 16, dtype=torch.complex128)
+    out, M = core(x, memory_state=M0)
+    ((out * R).sum() + (torch.conj(dM) * M).real.sum()).backward()
+    arrays.update({"mod_x": x.numpy(), "mod_R": R.numpy(), "mod_M0": M0.detach().numpy(), "mod_dM": dM.numpy(),
+                   "mod_out": out.detach().numpy(), "mod_M": M.detach().numpy(), "mod_d_M0": M0.grad.numpy()})
+    for k, v in core.state_dict().items():
+        arrays["mod_p_" + k] = v.numpy()
+    for k, prm in core.named_parameters():
+        arrays["mod_g_" + k] = prm.grad.numpy()
+    save("laplace_grad", **arrays)
+
+
 MAKERS = {"core": make_core, "gram": make_gram, "laplace": make_laplace, "spectral": make_spectral,
-          "ffn": make_ffn, "block": make_block, "complex_beta": make_complex_beta, "grad": make_grad}
+          "ffn": make_ffn, "block": make_block, "complex_beta": make_complex_beta, "grad": make_grad,
+          "laplace_grad": make_laplace_grad}
 
 if __name__ == "__main__":
     for name in (sys.argv[1:] or list(MAKERS)):

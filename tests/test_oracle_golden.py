@@ -195,3 +195,17 @@ def test_autograd_oracle_matches_reference_gradients():
     for k, name in enumerate(("d_theta_k", "d_theta_q", "d_v", "d_gate_raw")):
         assert ocore.rel_l2(d[k], g["cb_" + name]) < 1e-10, name
     assert ocore.rel_l2(d[4], g["cb_d_M0"]) < 1e-10
+
+
+def test_laplace_autograd_oracle_matches_reference_gradients():
+    from oracle import autograd as oag
+    g = load("laplace_grad")
+    names = ("theta_k", "logmag_k", "theta_q", "logmag_q", "v", "log_decay", "beta")
+    for i in range(int(g["n_cases"])):
+        p = f"c{i}_"
+        M0 = g[p + "M0"] if p + "M0" in g.files else None
+        d = oag.laplace_grads(*(g[p + n] for n in names), g[p + "dout"], g[p + "dM"], M0)
+        for k, n in enumerate(names):
+            assert ocore.rel_l2(d[k], g[p + "d_" + n]) < 1e-10, (i, n)
+        if M0 is not None:
+            assert ocore.rel_l2(d[7], g[p + "d_M0"]) < 1e-10
