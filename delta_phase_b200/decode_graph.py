@@ -9,7 +9,7 @@ states and the per-layer memory states in static buffers that the step updates i
 place, and replays it per token.
 
 The arithmetic is exactly ``DeltaPhaseModel.step``'s (the same module calls, through
-``DeltaPhaseHolographicBlock._step_inplace``).  The buffers belong to the graph: the
+the blocks' ``_step_inplace``, for both block kinds).  The buffers belong to the graph: the
 states returned by :meth:`states` alias them and change on the next :meth:`step`.
 """
 from __future__ import annotations

@@ -378,12 +378,6 @@ class DeltaPhaseHolographicBlock(_DeltaRuleBlock):
             return torch.ones(g.shape, device=g.device, dtype=torch.float32)
         return 2.0 * torch.sigmoid(g.float())
 
-    def _beta(self, conv_x):
-        beta = 2.0 * torch.sigmoid(self.w_beta(conv_x))
-        if self.beta_mode == "fixed":
-            beta = torch.ones_like(beta)
-        return beta
-
 
 class ComplexBetaDeltaPhaseBlock(_DeltaRuleBlock):
     """Complex-beta Householder block (layers.py:294-418): beta_t = 1 + e^{i phi_t} with
