@@ -20,7 +20,8 @@
 // L2-resident) and then walks back through them.
 //
 // One CTA of 256 threads per (b, h): warp w holds rows 32 (w / 4) .. +31 of column
-// 32 (w % 4) + lane of S and dS in registers (D <= 64, Dv <= 64).  Row sums are warp
+// 32 (w % 4) + lane of S and dS in registers (D <= 64, Dv <= 64); heads with 2 D <= 32
+// and Dv <= 32 take a one-warp-per-unit kernel instead (end of this file).  Row sums are warp
 // reduce-scatters plus a 4-way shared-memory sum; the column sums of the two row halves
 // are paired through shared memory one token later.
 #include "dp_common.cuh"
@@ -308,12 +309,226 @@ __global__ void __launch_bounds__(kLT, 1) laplace_bwd_kernel(LapBwdArgs a) {
   }
 }
 
+
+// ---- small heads (2 D <= 32 key features, Dv <= 32 rows): one warp per (b, h) unit.
+// Lane j holds column j of S and dS for all ROWS rows in registers, so the column sums
+// (the key / query gradients) are complete in each lane and the row sums are warp
+// reduce-scatters: no block barrier, no atomics, eight units per CTA.
+// still spread over many SMs.  The reference
+// module's default head (d_k = 16) runs here; the CTA kernel above would leave seven of
+// its eight warps on padding at that size.
+constexpr int kWarpUnits = 8;
+constexpr unsigned kFull = 0xffffffffu;
+
+// Lane l returns the warp sum of x[l % ROWS] (ROWS = 16 or 32).
+template <int ROWS>
+__device__ __forceinline__ float rs_rows(float (&x)[ROWS], int lane) {
+  if (ROWS == 16) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) x[i] += __shfl_xor_sync(kFull, x[i], 16);
+  }
+#pragma unroll
+  for (int k = ROWS / 2; k >= 1; k >>= 1) {
+    const bool upper = (lane & k) != 0;
+#pragma unroll
+    for (int i = 0; i < k; ++i) {
+      const float send = upper ? x[i] : x[i + k];
+      const float keep = upper ? x[i + k] : x[i];
+      x[i] = keep + __shfl_xor_sync(kFull, send, k);
+    }
+  }
+  return x[0];
+}
+
+// Raw per-token values of one lane: its key (and query) channel, its row's v and log r,
+// beta.  Loaded a token ahead of their use.
+struct LapTok {
+  float tk, mk, tq, mq, v, ld, beta, dout;
+};
+
+__device__ __forceinline__ LapTok lap_tok_load(const LapBwdArgs &a, int b, int h, int t, int c, bool col_ok,
+                                              int ro, bool row_ok, bool bwd, int64_t row_base) {
+  LapTok x{0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  if (col_ok) {
+    x.tk = load_any(a.tk, a.in_dt, b * a.s_tk.b + h * a.s_tk.h + (int64_t)t * a.s_tk.t + c);
+    if (a.mk) x.mk = load_any(a.mk, a.in_dt, b * a.s_mk.b + h * a.s_mk.h + (int64_t)t * a.s_mk.t + c);
+    if (bwd) {
+      x.tq = load_any(a.tq, a.in_dt, b * a.s_tq.b + h * a.s_tq.h + (int64_t)t * a.s_tq.t + c);
+      if (a.mq) x.mq = load_any(a.mq, a.in_dt, b * a.s_mq.b + h * a.s_mq.h + (int64_t)t * a.s_mq.t + c);
+    }
+  }
+  if (row_ok) {
+    x.v = load_any(a.v, a.in_dt, b * a.s_v.b + h * a.s_v.h + (int64_t)t * a.s_v.t + ro);
+    x.ld = load_any(a.ld, a.in_dt, b * a.s_ld.b + h * a.s_ld.h + (int64_t)t * a.s_ld.t + ro);
+    if (bwd) x.dout = a.dout[row_base + (int64_t)t * a.Dv + ro];
+  }
+  x.beta = load_any(a.beta, a.beta_dt, b * a.s_b.b + h * a.s_b.h + (int64_t)t * a.s_b.t);
+  return x;
+}
+
+// |k| (cos, sin) of the lane's channel.
+__device__ __forceinline__ void lap_phasor(float th, float lm, bool col_ok, float *pc, float *ps) {
+  float sn, cs;
+  sincosf(th, &sn, &cs);
+  const float mag = __expf(lm);
+  *pc = col_ok ? mag * cs : 0.f;
+  *ps = col_ok ? mag * sn : 0.f;
+}
+
+// Per unit: checkpoints (NSC states), the sub-chunk's states (kLC + 1), and its u, e.
+template <int ROWS>
+__host__ __device__ constexpr size_t lap_warp_unit_floats(size_t nsc) {
+  return (nsc + kLC + 1) * (size_t)ROWS * 32 + 2 * kLC * 32;
+}
+
+template <int ROWS>
+__global__ void __launch_bounds__(32 * kWarpUnits) laplace_bwd_warp_kernel(LapBwdArgs a, int units) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bh = blockIdx.x * kWarpUnits + warp;
+  if (bh >= units) return;  // the whole warp: nothing below synchronises the block
+  const int b = bh / a.H, h = bh % a.H;
+  const int L = a.L, D = a.D, Dv = a.Dv, F = 2 * D;
+  const int j = lane, c = j >> 1, ro = lane & (ROWS - 1);
+  const bool col_ok = j < F, row_ok = ro < Dv, row_lane = lane < ROWS && row_ok;
+  const float invD = 1.0f / (float)D;
+  const int nsc = (L + kLC - 1) / kLC;
+  const int64_t row_base = (int64_t)bh * L * Dv;
+  const int64_t st_base = (int64_t)bh * Dv * F;
+  constexpr int SS = ROWS * 32;
+  float *ckpt = a.ckpt + (int64_t)bh * lap_warp_unit_floats<ROWS>(nsc);
+  float *scr = ckpt + (int64_t)nsc * SS;
+  float *ue = scr + (int64_t)(kLC + 1) * SS;  // u: [r][32], e: [kLC + r][32]
+
+  float S[ROWS], dS[ROWS];
+#pragma unroll
+  for (int i = 0; i < ROWS; ++i) S[i] = (a.state_in && col_ok && i < Dv) ? a.state_in[st_base + (int64_t)i * F + j] : 0.f;
+
+  // one forward token: returns u and e of row ro
+  auto fwd = [&](const LapTok &x, float kap, float *e_out) {
+    float xx[ROWS];
+#pragma unroll
+    for (int i = 0; i < ROWS; ++i) xx[i] = S[i] * kap;
+    const float skr = rs_rows<ROWS>(xx, lane);
+    const float e = x.v - skr * invD;
+    const float u = x.beta * e;
+    const float r = row_ok ? __expf(fmaxf(x.ld, kLogFloor)) : 1.f;
+#pragma unroll
+    for (int i = 0; i < ROWS; ++i) S[i] = fmaf(__shfl_sync(kFull, u, i), kap, __shfl_sync(kFull, r, i) * S[i]);
+    *e_out = e;
+    return u;
+  };
+
+  // ---- pass 1: forward, checkpoints at sub-chunk starts
+  LapTok nx = L > 0 ? lap_tok_load(a, b, h, 0, c, col_ok, ro, row_ok, false, row_base) : LapTok{};
+  for (int t = 0; t < L; ++t) {
+    const LapTok x = nx;
+    if (t + 1 < L) nx = lap_tok_load(a, b, h, t + 1, c, col_ok, ro, row_ok, false, row_base);
+    if (t % kLC == 0) {
+#pragma unroll
+      for (int i = 0; i < ROWS; ++i) ckpt[(int64_t)(t / kLC) * SS + i * 32 + lane] = S[i];
+    }
+    float kc, ks, e;
+    lap_phasor(x.tk, x.mk, col_ok, &kc, &ks);
+    fwd(x, (j & 1) ? ks : kc, &e);
+  }
+
+  // ---- pass 2: sub-chunks backwards
+#pragma unroll
+  for (int i = 0; i < ROWS; ++i)
+    dS[i] = (a.dstate_out && col_ok && i < Dv) ? a.dstate_out[st_base + (int64_t)i * F + j] : 0.f;
+  for (int sc = nsc - 1; sc >= 0; --sc) {
+    const int t0 = sc * kLC, n = min(kLC, L - t0);
+#pragma unroll
+    for (int i = 0; i < ROWS; ++i) {
+      S[i] = ckpt[(int64_t)sc * SS + i * 32 + lane];
+      scr[i * 32 + lane] = S[i];
+    }
+    nx = lap_tok_load(a, b, h, t0, c, col_ok, ro, row_ok, false, row_base);
+    for (int r = 0; r < n; ++r) {
+      const LapTok x = nx;
+      if (r + 1 < n) nx = lap_tok_load(a, b, h, t0 + r + 1, c, col_ok, ro, row_ok, false, row_base);
+      float kc, ks, e;
+      lap_phasor(x.tk, x.mk, col_ok, &kc, &ks);
+      const float u = fwd(x, (j & 1) ? ks : kc, &e);
+      if (lane < ROWS) {
+        ue[r * 32 + lane] = u;
+        ue[(kLC + r) * 32 + lane] = e;
+      }
+#pragma unroll
+      for (int i = 0; i < ROWS; ++i) scr[(int64_t)(r + 1) * SS + i * 32 + lane] = S[i];
+    }
+    nx = lap_tok_load(a, b, h, t0 + n - 1, c, col_ok, ro, row_ok, true, row_base);
+    for (int r = n - 1; r >= 0; --r) {
+      const int t = t0 + r;
+      const LapTok x = nx;
+      if (r > 0) nx = lap_tok_load(a, b, h, t - 1, c, col_ok, ro, row_ok, true, row_base);
+      float Sp[ROWS];
+#pragma unroll
+      for (int i = 0; i < ROWS; ++i) Sp[i] = scr[(int64_t)r * SS + i * 32 + lane];
+      float kc, ks, qc, qs;
+      lap_phasor(x.tk, x.mk, col_ok, &kc, &ks);
+      lap_phasor(x.tq, x.mq, col_ok, &qc, &qs);
+      const float kap = (j & 1) ? ks : kc, xi = (j & 1) ? qs : qc;
+      const float u_r = ue[r * 32 + ro], e_r = ue[(kLC + r) * 32 + ro];
+      const float rr = row_ok ? __expf(fmaxf(x.ld, kLogFloor)) : 1.f;
+      const float rg = (row_ok && x.ld > kLogFloor) ? rr : 0.f;
+      float pq = 0.f, pw = 0.f, x1[ROWS], x2[ROWS];
+#pragma unroll
+      for (int i = 0; i < ROWS; ++i) {
+        const float dO = __shfl_sync(kFull, x.dout, i);
+        dS[i] = fmaf(dO * invD, xi, dS[i]);
+        pq = fmaf(S[i], dO, pq);
+        pw = fmaf(dS[i], __shfl_sync(kFull, u_r, i), pw);
+        x1[i] = dS[i] * kap;
+        x2[i] = dS[i] * Sp[i];
+      }
+      const float du = rs_rows<ROWS>(x1, lane);
+      const float dr = rs_rows<ROWS>(x2, lane);
+      const float de = x.beta * du;
+      if (row_lane) {
+        a.dv[row_base + (int64_t)t * Dv + ro] = de;
+        a.dld[row_base + (int64_t)t * Dv + ro] = dr * rg;
+      }
+      float p = row_lane ? du * e_r : 0.f;
+#pragma unroll
+      for (int o2 = 16; o2 >= 1; o2 >>= 1) p += __shfl_xor_sync(kFull, p, o2);
+      if (lane == 0) a.dbeta[(int64_t)bh * L + t] = p;
+      float pk = 0.f;
+#pragma unroll
+      for (int i = 0; i < ROWS; ++i) {
+        const float de_i = __shfl_sync(kFull, de, i);
+        dS[i] = fmaf(-de_i * invD, kap, __shfl_sync(kFull, rr, i) * dS[i]);
+        pk = fmaf(Sp[i], de_i, pk);
+        S[i] = Sp[i];
+      }
+      // column sums are complete: this lane's channel (pair with the neighbouring lane)
+      const float dk = pw - pk * invD, dq = pq * invD;
+      const float dk2 = __shfl_xor_sync(kFull, dk, 1), dq2 = __shfl_xor_sync(kFull, dq, 1);
+      if (!(j & 1) && col_ok) {
+        const int64_t gi = ((int64_t)bh * L + t) * D + c;
+        a.dtk[gi] = -ks * dk + kc * dk2;
+        a.dmk[gi] = kc * dk + ks * dk2;
+        a.dtq[gi] = -qs * dq + qc * dq2;
+        a.dmq[gi] = qc * dq + qs * dq2;
+      }
+    }
+  }
+  if (a.dstate_in) {
+#pragma unroll
+    for (int i = 0; i < ROWS; ++i)
+      if (col_ok && i < Dv) a.dstate_in[st_base + (int64_t)i * F + j] = dS[i];
+  }
+}
+
 }  // namespace
 }  // namespace dp
 
 extern "C" size_t dp_laplace_bwd_workspace_size(int B, int H, int L, int D, int Dv) {
   if (B <= 0 || H <= 0 || L <= 0 || D <= 0 || Dv <= 0) return 0;
   const size_t nsc = ((size_t)L + dp::kLC - 1) / dp::kLC;
+  if (2 * D <= 32 && Dv <= 32)  // one warp per unit
+    return (size_t)B * H * (Dv <= 16 ? dp::lap_warp_unit_floats<16>(nsc) : dp::lap_warp_unit_floats<32>(nsc)) *
+           sizeof(float);
   return (size_t)B * H * (nsc + dp::kLC + 1) * Dv * 2 * D * sizeof(float);
 }
 
@@ -341,7 +556,7 @@ extern "C" int dp_laplace_bwd(const void *theta_k, const void *logmag_k, const v
     const cudaError_t e = cudaMemsetAsync(grad_beta, 0, (size_t)B * H * L * sizeof(float), as_stream(stream));
     if (e != cudaSuccess) return set_error(DP_ERR_CUDA, std::string("dp_laplace_bwd: memset: ") + cudaGetErrorString(e));
   }
-  LapBwdArgs a;
+  LapBwdArgs a{};
   a.tk = theta_k;
   a.mk = logmag_k;
   a.tq = theta_q;
@@ -371,6 +586,12 @@ extern "C" int dp_laplace_bwd(const void *theta_k, const void *logmag_k, const v
   a.L = L;
   a.D = D;
   a.Dv = Dv;
+  if (2 * D <= 32 && Dv <= 32) {  // small heads: one warp per unit
+    const int units = B * H;
+    auto kern = Dv <= 16 ? laplace_bwd_warp_kernel<16> : laplace_bwd_warp_kernel<32>;
+    kern<<<(units + kWarpUnits - 1) / kWarpUnits, 32 * kWarpUnits, 0, as_stream(stream)>>>(a, units);
+    return check_launch("laplace_bwd_warp_kernel");
+  }
   const size_t smem = sizeof(LapStage) + sizeof(float) * (2 * 2 * 4 * 64 + 2 * 2 * 2 * 128);
   cudaError_t e = cudaFuncSetAttribute(laplace_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return set_error(DP_ERR_CUDA, std::string("dp_laplace_bwd smem attr: ") + cudaGetErrorString(e));
