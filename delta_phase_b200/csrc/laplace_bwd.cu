@@ -313,11 +313,11 @@ __global__ void __launch_bounds__(kLT, 1) laplace_bwd_kernel(LapBwdArgs a) {
 // ---- small heads (2 D <= 32 key features, Dv <= 32 rows): one warp per (b, h) unit.
 // Lane j holds column j of S and dS for all ROWS rows in registers, so the column sums
 // (the key / query gradients) are complete in each lane and the row sums are warp
-// reduce-scatters: no block barrier, no atomics, eight units per CTA.
+// reduce-scatters: no block barrier, no atomics; two units per CTA, so that few units
 // still spread over many SMs.  The reference
 // module's default head (d_k = 16) runs here; the CTA kernel above would leave seven of
 // its eight warps on padding at that size.
-constexpr int kWarpUnits = 8;
+constexpr int kWarpUnits = 2;
 constexpr unsigned kFull = 0xffffffffu;
 
 // Lane l returns the warp sum of x[l % ROWS] (ROWS = 16 or 32).
