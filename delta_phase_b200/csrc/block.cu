@@ -118,6 +118,88 @@ layernorm_kernel(const InT *__restrict__ x, const float *__restrict__ res, const
   }
 }
 
+// Eight consecutive values <-> float: 16-byte (bf16) or two 16-byte (float) accesses.
+__device__ __forceinline__ void load8(const float *p, float (&v)[8]) {
+  const float4 a = reinterpret_cast<const float4 *>(p)[0], b = reinterpret_cast<const float4 *>(p)[1];
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+__device__ __forceinline__ void load8(const __nv_bfloat16 *p, float (&v)[8]) {
+  const uint4 a = *reinterpret_cast<const uint4 *>(p);
+  const uint32_t w[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&w[i]));
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+__device__ __forceinline__ void store8(float *p, const float (&v)[8]) {
+  reinterpret_cast<float4 *>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
+  reinterpret_cast<float4 *>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
+}
+__device__ __forceinline__ void store8(__nv_bfloat16 *p, const float (&v)[8]) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+    w[i] = *reinterpret_cast<uint32_t *>(&h);
+  }
+  *reinterpret_cast<uint4 *>(p) = make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// The same LayerNorm with the row held in registers: one warp per row, lane l holds the
+// eight-value groups l, l + 32, ... (NG groups, d = 256 NG), every global access 16 bytes
+// wide and issued before the reductions.  The row is read once, not three times, and at
+// the few rows of a decode step the load latency is paid once per row.
+template <typename InT, typename OutT, int NG>
+__global__ void __launch_bounds__(128)
+layernorm_reg_kernel(const InT *__restrict__ x, const float *__restrict__ res, const float *__restrict__ ln_w,
+                     const float *__restrict__ ln_b, float eps, float *__restrict__ sum_out, OutT *__restrict__ y,
+                     int64_t rows) {
+  constexpr int d = 256 * NG;
+  const int64_t r = (int64_t)blockIdx.x * 4 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (r >= rows) return;
+  float v[NG][8];
+#pragma unroll
+  for (int g = 0; g < NG; ++g) {
+    const int c0 = 8 * (lane + 32 * g);
+    load8(x + r * d + c0, v[g]);
+    if (res) {
+      float rv[8];
+      load8(res + r * d + c0, rv);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[g][i] += rv[i];
+    }
+  }
+  float s = 0.f;
+#pragma unroll
+  for (int g = 0; g < NG; ++g)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) s += v[g][i];
+  const float mean = warp_sum(s) * (1.0f / d);
+  float q = 0.f;
+#pragma unroll
+  for (int g = 0; g < NG; ++g)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float dv = v[g][i] - mean;
+      q = fmaf(dv, dv, q);
+    }
+  const float rstd = rsqrtf(warp_sum(q) * (1.0f / d) + eps);
+#pragma unroll
+  for (int g = 0; g < NG; ++g) {
+    const int c0 = 8 * (lane + 32 * g);
+    if (sum_out) store8(sum_out + r * d + c0, v[g]);
+    float w[8], bb[8], o[8];
+    load8(ln_w + c0, w);
+    load8(ln_b + c0, bb);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i] = fmaf((v[g][i] - mean) * rstd, w[i], bb[i]);
+    store8(y + r * d + c0, o);
+  }
+}
+
 // Decode step of norm1 + ShortCausalConv1D.step (layers.py:43-50,182-190): one CTA per
 // sequence.  n = LayerNorm(x_t); out = n + SiLU(b + sum_{j<k-1} w[j] state[j] + w[k-1] n);
 // state (d, k-1) float32 shifts left and takes n (the conv's last k-1 inputs).
@@ -219,6 +301,32 @@ extern "C" int dp_layernorm(const void *x, int x_dtype, const float *residual, c
   const int64_t blocks = (rows + kBlkThreads / 32 - 1) / (kBlkThreads / 32);
   DP_REQUIRE(blocks < (1ll << 31), DP_ERR_UNSUPPORTED, "dp_layernorm: too many rows");
   cudaStream_t st = as_stream(stream);
+  auto al16 = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  if (d % 256 == 0 && d <= 1024 && al16(x) && al16(residual) && al16(ln_w) && al16(ln_b) && al16(sum_out) &&
+      al16(y) && (rows + 3) / 4 < (1ll << 31)) {
+    // row in registers (d = 256, 512, 768, 1024), four rows per CTA
+    const unsigned rb = (unsigned)((rows + 3) / 4);
+    auto launch_reg = [&](auto xt, auto ot) {
+      using XT = decltype(xt);
+      using OT = decltype(ot);
+      const XT *xp = static_cast<const XT *>(x);
+      OT *yp = static_cast<OT *>(y);
+      switch (d / 256) {
+        case 1: layernorm_reg_kernel<XT, OT, 1><<<rb, 128, 0, st>>>(xp, residual, ln_w, ln_b, eps, sum_out, yp, rows); break;
+        case 2: layernorm_reg_kernel<XT, OT, 2><<<rb, 128, 0, st>>>(xp, residual, ln_w, ln_b, eps, sum_out, yp, rows); break;
+        case 3: layernorm_reg_kernel<XT, OT, 3><<<rb, 128, 0, st>>>(xp, residual, ln_w, ln_b, eps, sum_out, yp, rows); break;
+        default: layernorm_reg_kernel<XT, OT, 4><<<rb, 128, 0, st>>>(xp, residual, ln_w, ln_b, eps, sum_out, yp, rows);
+      }
+    };
+    if (x_dtype == DP_F32) {
+      if (y_dtype == DP_F32) launch_reg(float{}, float{});
+      else launch_reg(float{}, __nv_bfloat16{});
+    } else {
+      if (y_dtype == DP_F32) launch_reg(__nv_bfloat16{}, float{});
+      else launch_reg(__nv_bfloat16{}, __nv_bfloat16{});
+    }
+    return check_launch("layernorm_reg_kernel");
+  }
   auto launch = [&](auto xt, auto ot) {
     using XT = decltype(xt);
     using OT = decltype(ot);

@@ -64,7 +64,7 @@ class DecodeGraph:
                                              enabled=self.autocast_dtype is not None):
             h = m._embed(self.ids)
             for blk, conv, mem in zip(m.blocks, self.conv, self.mem):
-                h = blk._step_inplace(h, conv, mem)
+                h = blk._step_inplace(h, conv, mem, keep_fp32=True)
             return m._head(h)
 
     def step(self, input_id_t: torch.Tensor) -> torch.Tensor:

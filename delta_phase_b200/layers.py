@@ -274,7 +274,8 @@ class _DeltaRuleBlock(nn.Module):
             self._oproj_key = key
         return self._oproj_cache
 
-    def _step_inplace(self, x_t: torch.Tensor, conv_state: torch.Tensor, memory_state: torch.Tensor):
+    def _step_inplace(self, x_t: torch.Tensor, conv_state: torch.Tensor, memory_state: torch.Tensor,
+                      keep_fp32: bool = False):
         """One decode token (layers.py:246-291) with the state updated in place:
         ``conv_state`` (B, d, k-1) float32 and ``memory_state`` (B, H, d_k, d_k) complex64
         are overwritten, so their addresses stay fixed (what a captured CUDA graph needs).
@@ -316,12 +317,18 @@ class _DeltaRuleBlock(nn.Module):
                             residual=res32, sum_out=s_sum)
         y = s_sum + self.ffn(n2)
         y = y.view(B, 1, D)
-        return y.to(x_t.dtype) if x_t.dtype != torch.float32 else y
+        return y if (keep_fp32 or x_t.dtype == torch.float32) else y.to(x_t.dtype)
 
     def step(self, x_t: torch.Tensor, state=None):
         """Single-token step (layers.py:246-291); returns ``(x, (conv_state, M))``.
         The input state is not modified: the new conv state (float32, (B, d, k-1)) and
         memory state are fresh tensors."""
+        return self._step_fresh(x_t, state)
+
+    def _step_fresh(self, x_t: torch.Tensor, state=None, keep_fp32: bool = False):
+        """``step`` on fresh state tensors; ``keep_fp32`` returns the float32 residual
+        stream instead of casting it back to x_t's dtype (the model's decode loop passes it
+        between blocks that way)."""
         B, _, D = x_t.shape
         H, dk = self.n_heads, self.d_k
         if state is None:
@@ -339,7 +346,7 @@ class _DeltaRuleBlock(nn.Module):
             mem_new = torch.zeros(B, H, dk, dk, dtype=torch.complex64, device=x_t.device)
         else:
             mem_new = memory_state.detach().to(torch.complex64).clone().contiguous()
-        x = self._step_inplace(x_t, conv_new, mem_new)
+        x = self._step_inplace(x_t, conv_new, mem_new, keep_fp32=keep_fp32)
         return x, (conv_new, mem_new)
 
 

@@ -110,7 +110,8 @@ class DeltaPhaseModel(nn.Module):
             states = [None] * len(self.blocks)
         new_states = []
         for i, block in enumerate(self.blocks):
-            h, s = block.step(h, states[i])
+            # the residual stream stays float32 between blocks (no bf16 round trip per layer)
+            h, s = block._step_fresh(h, states[i], keep_fp32=True)
             new_states.append(s)
         return self._head(h), new_states
 
