@@ -30,6 +30,7 @@ _SIG = {
     "dp_core_decode": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _P, _I, _I, _I, _I, _I64P, _P]),
     "dp_core_cbeta_fwd": (_I, [_P, _P, _P, _P, _I, _I, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I64P, _P]),
     "dp_core_cbeta_decode": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _P, _I, _I, _I, _I, _I64P, _P]),
+    "dp_core_decode_gated": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _P, _I, _I, _I, _I, _I64P, _P]),
     "dp_core_bwd_workspace_size": (ctypes.c_size_t, [_I, _I, _I, _I]),
     "dp_core_bwd": (_I, [_P, _P, _P, _P, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I64P,
                          _P, ctypes.c_size_t, _P]),
@@ -42,6 +43,7 @@ _SIG = {
     "dp_ffn_fold": (_I, [_P, _P, _P, _P, _P, _I, _I, _P]),
     "dp_ffn_workspace_size": (ctypes.c_size_t, [_I, _I, _I]),
     "dp_ffn_fwd": (_I, [_P, _I, _P, _P, _P, _I, _I, _P, ctypes.c_size_t, _P]),
+    "dp_ffn_fwd_residual": (_I, [_P, _I, _P, _P, _P, _I, _I, _P, ctypes.c_size_t, _P]),
     "dp_ffn_fwd_noalloc": (_I, [_P, _I, _P, _P, _P, _I, _I, _P]),
     "dp_ffn_noalloc_max_tokens": (ctypes.c_size_t, [_I, _I]),
     "dp_ln_conv_silu": (_I, [_P, _I, _P, _P, ctypes.c_float, _P, _P, _P, _I, _I, _I, _I, _I, _P]),
@@ -176,9 +178,14 @@ def core_fwd(theta_k, theta_q, v, beta, chunk_size, state_in, out, state_out, co
     _check(name, rc)
 
 
-def core_decode(state_in, state_out, theta_k, theta_q, v, beta, out, complex_beta=False):
+DP_GATE_BETA, DP_GATE_SIGMOID2, DP_GATE_ONE, DP_GATE_PHI = 0, 1, 2, 3
+
+
+def core_decode(state_in, state_out, theta_k, theta_q, v, beta, out, complex_beta=False, gate_mode=None):
     """dp_core_decode; theta_k/theta_q (B,H,D), v (B,H,Dv), beta (B,H), out (B,H,Dv).
-    complex_beta: ``beta`` holds phi of beta = 1 + e^{i phi} (dp_core_cbeta_decode)."""
+    complex_beta: ``beta`` holds phi of beta = 1 + e^{i phi} (dp_core_cbeta_decode).
+    gate_mode (one of DP_GATE_*): ``beta`` is the raw gate that dp_core_decode_gated maps
+    to the write strength itself."""
     dev = require_cuda(state_in, state_out, theta_k, theta_q, v, beta, out)
     B, H, D = theta_k.shape
     Dv = v.shape[-1]
@@ -188,11 +195,17 @@ def core_decode(state_in, state_out, theta_k, theta_q, v, beta, out, complex_bet
     st = []
     for t in (theta_k, theta_q, v, beta, out):
         st += (t.stride(0), t.stride(1))
-    name = "dp_core_cbeta_decode" if complex_beta else "dp_core_decode"
     with torch.cuda.device(dev):
-        rc = getattr(lib(), name)(ptr(state_in), ptr(state_out), ptr(theta_k), ptr(theta_q), ptr(v),
-                                  ptr(beta), dtype_code(theta_k), dtype_code(beta), ptr(out), B, H, D,
-                                  Dv, strides_array(st), stream_of(dev))
+        if gate_mode is not None:
+            name = "dp_core_decode_gated"
+            rc = lib().dp_core_decode_gated(ptr(state_in), ptr(state_out), ptr(theta_k), ptr(theta_q), ptr(v),
+                                            ptr(beta), dtype_code(theta_k), dtype_code(beta), int(gate_mode),
+                                            ptr(out), B, H, D, Dv, strides_array(st), stream_of(dev))
+        else:
+            name = "dp_core_cbeta_decode" if complex_beta else "dp_core_decode"
+            rc = getattr(lib(), name)(ptr(state_in), ptr(state_out), ptr(theta_k), ptr(theta_q), ptr(v),
+                                      ptr(beta), dtype_code(theta_k), dtype_code(beta), ptr(out), B, H, D,
+                                      Dv, strides_array(st), stream_of(dev))
     _check(name, rc)
 
 
@@ -301,6 +314,19 @@ def ffn_fwd(x, dct, F, y, workspace):
                               ptr(workspace), workspace.numel() * workspace.element_size(),
                               stream_of(dev))
     _check("dp_ffn_fwd", rc)
+
+
+def ffn_fwd_residual(x, dct, F, y, workspace):
+    """dp_ffn_fwd_residual: y (tokens, d) float32 += FFN(x)."""
+    dev = require_cuda(x, dct, F, y, workspace)
+    tokens, d = x.shape
+    if y.dtype != torch.float32 or not y.is_contiguous() or tuple(y.shape) != (tokens, d):
+        raise ValueError("y must be a contiguous float32 (tokens, d) tensor")
+    with torch.cuda.device(dev):
+        rc = lib().dp_ffn_fwd_residual(ptr(x), dtype_code(x), ptr(dct), ptr(F), ptr(y), tokens, d,
+                                       ptr(workspace), workspace.numel() * workspace.element_size(),
+                                       stream_of(dev))
+    _check("dp_ffn_fwd_residual", rc)
 
 
 def ffn_fwd_noalloc(x, dct, F, y):

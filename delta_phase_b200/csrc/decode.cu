@@ -32,13 +32,19 @@ __device__ __forceinline__ float warp_sum(float x) {
   return x;
 }
 
+// The write gate from its raw value: 2 sigmoid(g) for DP_GATE_SIGMOID2 (layers.py:265),
+// the value itself otherwise (beta, phi, or the 1 the caller loaded for DP_GATE_ONE).
+__device__ __forceinline__ float gate_beta(float g, int gate_mode) {
+  return gate_mode == DP_GATE_SIGMOID2 ? 2.f / (1.f + expf(-g)) : g;
+}
+
 // kq: smem (4 x D): cos k, sin k, cos q, sin q; CB adds the write key (2 x D).
 template <bool kVec4, bool CB>
 __global__ void __launch_bounds__(kDecThreads)
 decode_kernel(const float *state_in, float *state_out, const void *__restrict__ tk,
               const void *__restrict__ tq, const void *__restrict__ v,
-              const void *__restrict__ beta, int in_dt, int beta_dt, float *__restrict__ out,
-              int H, int D, int Dv, SeqStrides s_tk, SeqStrides s_tq, SeqStrides s_v,
+              const void *__restrict__ beta, int in_dt, int beta_dt, int gate_mode,
+              float *__restrict__ out, int H, int D, int Dv, SeqStrides s_tk, SeqStrides s_tq, SeqStrides s_v,
               SeqStrides s_b, SeqStrides s_out) {
   extern __shared__ float kq[];
   const int bh = blockIdx.x, b = bh / H, h = bh % H;
@@ -53,7 +59,8 @@ decode_kernel(const float *state_in, float *state_out, const void *__restrict__ 
     kq[3 * D + c] = s;
   }
   const float inv_d = 1.0f / (float)D;
-  float bt = load_any(beta, beta_dt, b * s_b.b + h * s_b.h);
+  const float bt_raw = gate_mode == DP_GATE_ONE ? 1.f : load_any(beta, beta_dt, b * s_b.b + h * s_b.h);
+  float bt = gate_beta(bt_raw, gate_mode);
   // write key: the read key (real beta) or beta k (complex beta, then bt = 1)
   const float *wc = kq, *ws = kq + D;
   if (CB) {
@@ -152,8 +159,8 @@ template <int RPW, bool CB>
 __global__ void __launch_bounds__(kDecThreads)
 decode_rows_kernel(const float *state_in, float *state_out, const void *__restrict__ tk,
                    const void *__restrict__ tq, const void *__restrict__ v,
-                   const void *__restrict__ beta, int in_dt, int beta_dt, float *__restrict__ out,
-                   int H, int D, int Dv, SeqStrides s_tk, SeqStrides s_tq, SeqStrides s_v, SeqStrides s_b,
+                   const void *__restrict__ beta, int in_dt, int beta_dt, int gate_mode,
+                   float *__restrict__ out, int H, int D, int Dv, SeqStrides s_tk, SeqStrides s_tq, SeqStrides s_v, SeqStrides s_b,
                    SeqStrides s_out) {
   const int bh = blockIdx.x, b = bh / H, h = bh % H;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -168,7 +175,8 @@ decode_rows_kernel(const float *state_in, float *state_out, const void *__restri
     sincosf(load_any(tq, in_dt, b * s_tq.b + h * s_tq.h + 2 * p + 1), &sq1, &cq1);
   }
   const float inv_d = 1.0f / (float)D;
-  float bt = load_any(beta, beta_dt, b * s_b.b + h * s_b.h);
+  const float bt_raw = gate_mode == DP_GATE_ONE ? 1.f : load_any(beta, beta_dt, b * s_b.b + h * s_b.h);
+  float bt = gate_beta(bt_raw, gate_mode);
   // write key: the read key (real beta) or beta k (complex beta, then bt = 1)
   float wc0 = ck0, ws0 = sk0, wc1 = ck1, ws1 = sk1;
   if (CB) {
@@ -230,16 +238,21 @@ decode_rows_kernel(const float *state_in, float *state_out, const void *__restri
 
 namespace dp {
 namespace {
-int decode_entry(const char *name, bool cbeta, const float *state_in, float *state_out, const void *theta_k,
+int decode_entry(const char *name, int gate_mode, const float *state_in, float *state_out, const void *theta_k,
                  const void *theta_q, const void *v, const void *beta, int in_dtype, int beta_dtype, float *out,
                  int B, int H, int D, int Dv, const int64_t *strides, void *stream) {
   const std::string n(name);
   DP_REQUIRE(B >= 0 && H >= 0 && D >= 1 && Dv >= 1, DP_ERR_INVALID_ARGUMENT, n + ": bad sizes");
-  DP_REQUIRE(valid_dtype(in_dtype) && valid_dtype(beta_dtype), DP_ERR_INVALID_ARGUMENT, n + ": bad dtype code");
+  DP_REQUIRE(gate_mode >= DP_GATE_BETA && gate_mode <= DP_GATE_PHI, DP_ERR_INVALID_ARGUMENT,
+             n + ": bad gate mode");
+  const bool gate_read = gate_mode != DP_GATE_ONE;
+  DP_REQUIRE(valid_dtype(in_dtype) && (!gate_read || valid_dtype(beta_dtype)), DP_ERR_INVALID_ARGUMENT,
+             n + ": bad dtype code");
   DP_REQUIRE(D <= 4096, DP_ERR_UNSUPPORTED, n + ": D must be <= 4096");
   if (B == 0 || H == 0) return DP_OK;
-  DP_REQUIRE(state_in && state_out && theta_k && theta_q && v && beta && out && strides,
+  DP_REQUIRE(state_in && state_out && theta_k && theta_q && v && (beta || !gate_read) && out && strides,
              DP_ERR_INVALID_ARGUMENT, n + ": null pointer");
+  const bool cbeta = gate_mode == DP_GATE_PHI;
   SeqStrides s[5];
   for (int i = 0; i < 5; ++i) s[i] = SeqStrides{strides[2 * i], strides[2 * i + 1], 0};
   const bool vec4 = (D % 2 == 0) && (reinterpret_cast<uintptr_t>(state_in) % 16 == 0) &&
@@ -249,7 +262,7 @@ int decode_entry(const char *name, bool cbeta, const float *state_in, float *sta
     auto kern = Dv <= 64 ? (cbeta ? decode_rows_kernel<8, true> : decode_rows_kernel<8, false>)
                          : (cbeta ? decode_rows_kernel<16, true> : decode_rows_kernel<16, false>);
     kern<<<B * H, kDecThreads, 0, as_stream(stream)>>>(state_in, state_out, theta_k, theta_q, v, beta, in_dtype,
-                                                       beta_dtype, out, H, D, Dv, s[0], s[1], s[2], s[3], s[4]);
+                                                       beta_dtype, gate_mode, out, H, D, Dv, s[0], s[1], s[2], s[3], s[4]);
   } else {
     auto kern = vec4 ? (cbeta ? decode_kernel<true, true> : decode_kernel<true, false>)
                      : (cbeta ? decode_kernel<false, true> : decode_kernel<false, false>);
@@ -258,7 +271,7 @@ int decode_entry(const char *name, bool cbeta, const float *state_in, float *sta
       if (e != cudaSuccess) return set_error(DP_ERR_CUDA, n + ": smem attribute: " + cudaGetErrorString(e));
     }
     kern<<<B * H, kDecThreads, smem, as_stream(stream)>>>(state_in, state_out, theta_k, theta_q, v, beta, in_dtype,
-                                                          beta_dtype, out, H, D, Dv, s[0], s[1], s[2], s[3], s[4]);
+                                                          beta_dtype, gate_mode, out, H, D, Dv, s[0], s[1], s[2], s[3], s[4]);
   }
   return check_launch("decode_kernel");
 }
@@ -269,7 +282,7 @@ extern "C" int dp_core_decode(const float *state_in, float *state_out, const voi
                               const void *theta_q, const void *v, const void *beta, int in_dtype,
                               int beta_dtype, float *out, int B, int H, int D, int Dv,
                               const int64_t *strides, void *stream) {
-  return dp::decode_entry("dp_core_decode", false, state_in, state_out, theta_k, theta_q, v, beta, in_dtype,
+  return dp::decode_entry("dp_core_decode", DP_GATE_BETA, state_in, state_out, theta_k, theta_q, v, beta, in_dtype,
                           beta_dtype, out, B, H, D, Dv, strides, stream);
 }
 
@@ -277,6 +290,14 @@ extern "C" int dp_core_cbeta_decode(const float *state_in, float *state_out, con
                                     const void *theta_q, const void *v, const void *phi, int in_dtype,
                                     int phi_dtype, float *out, int B, int H, int D, int Dv,
                                     const int64_t *strides, void *stream) {
-  return dp::decode_entry("dp_core_cbeta_decode", true, state_in, state_out, theta_k, theta_q, v, phi, in_dtype,
+  return dp::decode_entry("dp_core_cbeta_decode", DP_GATE_PHI, state_in, state_out, theta_k, theta_q, v, phi, in_dtype,
                           phi_dtype, out, B, H, D, Dv, strides, stream);
+}
+
+extern "C" int dp_core_decode_gated(const float *state_in, float *state_out, const void *theta_k,
+                                    const void *theta_q, const void *v, const void *gate, int in_dtype,
+                                    int gate_dtype, int gate_mode, float *out, int B, int H, int D, int Dv,
+                                    const int64_t *strides, void *stream) {
+  return dp::decode_entry("dp_core_decode_gated", gate_mode, state_in, state_out, theta_k, theta_q, v, gate,
+                          in_dtype, gate_dtype, out, B, H, D, Dv, strides, stream);
 }

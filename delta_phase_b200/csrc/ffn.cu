@@ -319,9 +319,12 @@ extern "C" size_t dp_ffn_workspace_size(int tokens, int d, int x_dtype) {
   return (size_t)tokens * d * sizeof(float) + (size_t)tokens * 6 * d * es + 256;
 }
 
-extern "C" int dp_ffn_fwd(const void *x, int x_dtype, const void *dct, const void *F, void *y,
-                          int tokens, int d, void *workspace, size_t workspace_bytes, void *stream) {
-  using namespace dp;
+namespace dp {
+namespace {
+// dp_ffn_fwd (accumulate = false: y = z F in x's dtype) and dp_ffn_fwd_residual
+// (accumulate = true: y float32, y += z F in the combine GEMM's epilogue).
+int ffn_fwd_impl(const void *x, int x_dtype, const void *dct, const void *F, void *y, int tokens, int d,
+                 void *workspace, size_t workspace_bytes, void *stream, bool accumulate) {
   DP_REQUIRE(tokens >= 0 && d >= 1, DP_ERR_INVALID_ARGUMENT, "dp_ffn_fwd: bad sizes");
   DP_REQUIRE(x_dtype == DP_F32 || x_dtype == DP_BF16, DP_ERR_INVALID_ARGUMENT,
              "dp_ffn_fwd: x dtype must be float32 or bfloat16");
@@ -383,9 +386,21 @@ extern "C" int dp_ffn_fwd(const void *x, int x_dtype, const void *dct, const voi
   if (rc != DP_OK) return rc;
   // Y (tokens x d) = Z (tokens x 6d) F (6d x d)  <=>  Y^T = F^T Z^T in column-major
   cs = cublasGemmEx(hdl, CUBLAS_OP_N, CUBLAS_OP_N, d, tokens, 6 * d, &one, F, ab, d, z, ab, 6 * d,
-                    &zero, y, ab, d, ct, CUBLAS_GEMM_DEFAULT);
+                    accumulate ? &one : &zero, y, accumulate ? CUDA_R_32F : ab, d, ct, CUBLAS_GEMM_DEFAULT);
   DP_REQUIRE(cs == CUBLAS_STATUS_SUCCESS, DP_ERR_CUDA, "dp_ffn_fwd: combine GEMM failed");
   return DP_OK;
+}
+}  // namespace
+}  // namespace dp
+
+extern "C" int dp_ffn_fwd(const void *x, int x_dtype, const void *dct, const void *F, void *y,
+                          int tokens, int d, void *workspace, size_t workspace_bytes, void *stream) {
+  return dp::ffn_fwd_impl(x, x_dtype, dct, F, y, tokens, d, workspace, workspace_bytes, stream, false);
+}
+
+extern "C" int dp_ffn_fwd_residual(const void *x, int x_dtype, const void *dct, const void *F, float *y,
+                                   int tokens, int d, void *workspace, size_t workspace_bytes, void *stream) {
+  return dp::ffn_fwd_impl(x, x_dtype, dct, F, y, tokens, d, workspace, workspace_bytes, stream, true);
 }
 
 // ---------------------------------------------------------------------------------

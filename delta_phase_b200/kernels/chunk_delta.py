@@ -191,12 +191,15 @@ def gram_matrix_cuda(theta_k: torch.Tensor, beta: torch.Tensor) -> torch.Tensor:
 gram_matrix_triton = gram_matrix_cuda
 
 
-def decode_step(memory_state, theta_k, theta_q, v, beta, out=None, state_out=None, complex_beta=False):
+def decode_step(memory_state, theta_k, theta_q, v, beta, out=None, state_out=None, complex_beta=False,
+                gate_mode=None):
     """Fused decode step (layers.py:279-285).  memory_state (B,H,Dv,D) complex64;
     theta_k/theta_q (B,H,D); v (B,H,Dv); beta (B,H).  Returns ``(out (B,H,Dv) float32,
     new_state)``.  ``state_out=memory_state`` updates the state in place.
     ``complex_beta``: ``beta`` holds phi, the step of ComplexBetaDeltaPhaseBlock
-    (layers.py:402-407)."""
+    (layers.py:402-407).  ``gate_mode`` (``_capi.DP_GATE_*``): ``beta`` is the write
+    gate's raw projection and the kernel forms beta from it (2 sigmoid(g), 1, or
+    1 + e^{i g})."""
     B, H, D = theta_k.shape
     Dv = v.shape[-1]
     _capi.require_cuda(memory_state, theta_k, theta_q, v, beta)
@@ -208,7 +211,7 @@ def decode_step(memory_state, theta_k, theta_q, v, beta, out=None, state_out=Non
     if out is None:
         out = torch.empty(B, H, Dv, device=theta_k.device, dtype=torch.float32)
     _capi.core_decode(s_in, torch.view_as_real(state_out), theta_k, theta_q, v, beta, out,
-                      complex_beta=complex_beta)
+                      complex_beta=complex_beta, gate_mode=gate_mode)
     return out, state_out
 
 

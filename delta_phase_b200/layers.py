@@ -129,6 +129,17 @@ class LearnableSubstrateLerpFFN(nn.Module):
             out = out + weights[i] * F.linear(self.combine(a), mat.t())
         return out
 
+    def _compute_dtype(self, x: torch.Tensor):
+        """(GEMM operand dtype, output dtype) of the CUDA path for input ``x``."""
+        cdt = torch.bfloat16 if x.dtype == torch.bfloat16 else torch.float32
+        out_dt = x.dtype
+        if cdt == torch.float32 and torch.is_autocast_enabled(x.device.type):
+            # the reference's transforms and combine are matmuls, which autocast runs in
+            # its lower precision: take the bf16 path and return bf16 like they would
+            if torch.get_autocast_dtype(x.device.type) == torch.bfloat16:
+                cdt = out_dt = torch.bfloat16
+        return cdt, out_dt
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         if x.shape[-1] != self.d_model:
             raise ValueError(f"expected last dim {self.d_model}, got {x.shape[-1]}")
@@ -138,13 +149,7 @@ class LearnableSubstrateLerpFFN(nn.Module):
             _capi.require_cuda(x, self.mat_dct)
             return self._forward_autograd(x)
         _capi.require_cuda(x, self.mat_dct)
-        cdt = torch.bfloat16 if x.dtype == torch.bfloat16 else torch.float32
-        out_dt = x.dtype
-        if cdt == torch.float32 and torch.is_autocast_enabled(x.device.type):
-            # the reference's transforms and combine are matmuls, which autocast runs in
-            # its lower precision: take the bf16 path and return bf16 like they would
-            if torch.get_autocast_dtype(x.device.type) == torch.bfloat16:
-                cdt = out_dt = torch.bfloat16
+        cdt, out_dt = self._compute_dtype(x)
         x2 = x.reshape(-1, self.d_model).to(cdt).contiguous()
         Fm, dct = self.folded(cdt)
         y = torch.empty_like(x2)
@@ -152,6 +157,19 @@ class LearnableSubstrateLerpFFN(nn.Module):
                          device=x.device, dtype=torch.uint8)
         _capi.ffn_fwd(x2, dct, Fm, y, ws)
         return y.view(x.shape).to(out_dt)
+
+    def add_to(self, residual: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
+        """``residual += ffn(x)`` in place for a contiguous float32 ``residual`` shaped like
+        ``x``, the block's ``x + self.ffn(self.norm2(x))`` (layers.py:243, 290) with the add
+        in the combine GEMM's epilogue (dp_ffn_fwd_residual).  Inference path only."""
+        _capi.require_cuda(x, residual, self.mat_dct)
+        cdt, _ = self._compute_dtype(x)
+        x2 = x.reshape(-1, self.d_model).to(cdt).contiguous()
+        Fm, dct = self.folded(cdt)
+        ws = torch.empty(_capi.ffn_workspace_size(x2.shape[0], self.d_model, cdt),
+                         device=x.device, dtype=torch.uint8)
+        _capi.ffn_fwd_residual(x2, dct, Fm, residual.view(-1, self.d_model), ws)
+        return residual
 
     def get_substrate_probabilities(self):
         probs = F.softmax(self.substrate_logits, dim=0)
@@ -174,6 +192,26 @@ class _DeltaRuleBlock(nn.Module):
 
     def _last_beta(self, gate: torch.Tensor) -> torch.Tensor:
         return gate.detach()
+
+    def _decode_gate_mode(self) -> int:
+        """How dp_core_decode_gated forms beta from the raw gate projection."""
+        raise NotImplementedError
+
+    @property
+    def last_beta(self):
+        """The write strengths of the last forward or step, as the reference records them
+        (layers.py:240, 268, 346, 400).  After a step it is formed on access from the raw
+        gate the decode kernel read, so the step launches no gate kernels of its own."""
+        raw = self.__dict__.get("_last_gate_raw")
+        if raw is not None:
+            with torch.no_grad():
+                return self._last_beta(self._write_gate(raw).unsqueeze(-1))
+        return self.__dict__.get("_last_beta_value")
+
+    @last_beta.setter
+    def last_beta(self, value):
+        self.__dict__["_last_beta_value"] = value
+        self.__dict__["_last_gate_raw"] = None
 
     def _proj_weights(self, dtype):
         """[w_k; w_q; w_v; gate] weights (and biases, when the layers have them)
@@ -261,7 +299,7 @@ class _DeltaRuleBlock(nn.Module):
         n2 = torch.empty(B * L, D, device=x.device, dtype=gdt)
         _capi.layernorm(o.contiguous(), self.norm2.weight.float(), self.norm2.bias.float(), self.norm2.eps, n2,
                         residual=res32, sum_out=s_sum)
-        out = s_sum.view(B, L, D) + self.ffn(n2.view(B, L, D))
+        out = self.ffn.add_to(s_sum, n2).view(B, L, D)
         return out.to(x.dtype) if x.dtype != torch.float32 else out, M_state
 
     def _out_proj_weights(self, dtype):
@@ -280,8 +318,9 @@ class _DeltaRuleBlock(nn.Module):
         ``conv_state`` (B, d, k-1) float32 and ``memory_state`` (B, H, d_k, d_k) complex64
         are overwritten, so their addresses stay fixed (what a captured CUDA graph needs).
         norm1 + the conv step in one kernel, the projections as one GEMM on cached
-        weights (no per-call casts), the fused decode kernel, norm_retrieved, and norm2
-        with the residual add fused in.  Returns x (B, 1, d)."""
+        weights (no per-call casts), the fused decode kernel (which forms the write gate
+        from its raw projection), norm_retrieved, and norm2 with the residual add fused
+        in.  Returns x (B, 1, d)."""
         if x_t.dtype == torch.float64:
             raise TypeError("float64 inputs are not supported by the CUDA path")
         B, _, D = x_t.shape
@@ -302,10 +341,11 @@ class _DeltaRuleBlock(nn.Module):
             tk = proj[:, :D].view(B, H, dk)
             tq = proj[:, D:2 * D].view(B, H, dk)
             v = proj[:, 2 * D:3 * D].view(B, H, dk)
-            beta = self._write_gate(proj[:, 3 * D:])
-            self.last_beta = self._last_beta(beta.unsqueeze(-1))
-            out, _ = decode_step(memory_state, tk, tq, v, beta, state_out=memory_state,
-                                 complex_beta=self._complex_beta)
+            gate = proj[:, 3 * D:]                                 # raw (B, H) gate
+            self.last_beta = None
+            self.__dict__["_last_gate_raw"] = gate
+            out, _ = decode_step(memory_state, tk, tq, v, gate, state_out=memory_state,
+                                 gate_mode=self._decode_gate_mode())
             nr = self.norm_retrieved
             rn = torch.empty(B, D, device=x_t.device, dtype=gdt)
             _capi.layernorm(out.view(B, D), nr.weight.float(), nr.bias.float(), nr.eps, rn)
@@ -315,8 +355,7 @@ class _DeltaRuleBlock(nn.Module):
             n2 = torch.empty(B, D, device=x_t.device, dtype=gdt)
             _capi.layernorm(o, self.norm2.weight.float(), self.norm2.bias.float(), self.norm2.eps, n2,
                             residual=res32, sum_out=s_sum)
-        y = s_sum + self.ffn(n2)
-        y = y.view(B, 1, D)
+        y = self.ffn.add_to(s_sum, n2).view(B, 1, D)
         return y if (keep_fp32 or x_t.dtype == torch.float32) else y.to(x_t.dtype)
 
     def step(self, x_t: torch.Tensor, state=None):
@@ -380,10 +419,13 @@ class DeltaPhaseHolographicBlock(_DeltaRuleBlock):
         return self.w_beta
 
     def _write_gate(self, g):
-        """beta = 2 sigmoid(w_beta(conv_x)) (layers.py:192-196), or 1 in "fixed" mode."""
+        """beta = 2 sigmoid(w_beta(conv_x)) (layers.py:195), or 1 in "fixed" mode (:196-197)."""
         if self.beta_mode == "fixed":
             return torch.ones(g.shape, device=g.device, dtype=torch.float32)
         return 2.0 * torch.sigmoid(g.float())
+
+    def _decode_gate_mode(self):
+        return _capi.DP_GATE_ONE if self.beta_mode == "fixed" else _capi.DP_GATE_SIGMOID2
 
 
 class ComplexBetaDeltaPhaseBlock(_DeltaRuleBlock):
@@ -425,9 +467,12 @@ class ComplexBetaDeltaPhaseBlock(_DeltaRuleBlock):
         return g.float()
 
     def _last_beta(self, phi):
-        """beta_complex = 1 + polar(1, phi), as the reference records it (layers.py:345, 398)."""
+        """beta_complex = 1 + polar(1, phi), as the reference records it (layers.py:346, 400)."""
         with torch.no_grad():
             return 1.0 + torch.polar(torch.ones_like(phi), phi)
+
+    def _decode_gate_mode(self):
+        return _capi.DP_GATE_PHI
 
 
 class LaplacePhaseCore(nn.Module):

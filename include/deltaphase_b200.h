@@ -160,6 +160,21 @@ DP_API int dp_core_cbeta_decode(const float *state_in, float *state_out, const v
                    const int64_t *strides, void *stream);
 
 /*
+ * Decode step that reads the write gate's raw projection and forms the gate itself,
+ * so a block's step needs no separate gate kernels:
+ *   DP_GATE_BETA     beta = gate                 (dp_core_decode)
+ *   DP_GATE_SIGMOID2 beta = 2 sigmoid(gate)      (w_beta gate, delta_phase/layers.py:195, 265)
+ *   DP_GATE_ONE      beta = 1, gate not read (may be NULL)  (beta_mode "fixed", layers.py:196-197, 266-267)
+ *   DP_GATE_PHI      beta = 1 + e^{i gate}       (dp_core_cbeta_decode, layers.py:397-398)
+ * Arguments otherwise as dp_core_decode; gate_dtype is the gate's dtype code.
+ */
+enum dp_gate_mode { DP_GATE_BETA = 0, DP_GATE_SIGMOID2 = 1, DP_GATE_ONE = 2, DP_GATE_PHI = 3 };
+DP_API int dp_core_decode_gated(const float *state_in, float *state_out, const void *theta_k,
+                   const void *theta_q, const void *v, const void *gate, int in_dtype,
+                   int gate_dtype, int gate_mode, float *out, int B, int H, int D, int Dv,
+                   const int64_t *strides, void *stream);
+
+/*
  * Strictly-lower, row-beta-scaled phasor Gram of N chunks:
  *   G[n, m, j] = beta[n, m] * sum_d cos(theta[n,m,d] - theta[n,j,d]) / D  (m > j), else 0.
  * Replaces gram_matrix_triton / _triton_fused_phase_gram_kernel
@@ -246,6 +261,16 @@ DP_API size_t dp_ffn_workspace_size(int tokens, int d, int x_dtype);
  */
 DP_API int dp_ffn_fwd(const void *x, int x_dtype, const void *dct, const void *F, void *y, int tokens,
                int d, void *workspace, size_t workspace_bytes, void *stream);
+
+/*
+ * The FFN with the block's residual add: y += FFN(x), y (tokens, d) float32, added in
+ * the combine GEMM's epilogue.  The block output x + ffn(norm2(x)) of
+ * DeltaPhaseHolographicBlock.forward/step (delta_phase/layers.py:243, 290) and of
+ * ComplexBetaDeltaPhaseBlock (layers.py:368, 417) with y holding the residual stream.
+ * Other arguments and limits as dp_ffn_fwd (same workspace size).
+ */
+DP_API int dp_ffn_fwd_residual(const void *x, int x_dtype, const void *dct, const void *F, float *y,
+               int tokens, int d, void *workspace, size_t workspace_bytes, void *stream);
 
 /*
  * Allocation-free variant of dp_ffn_fwd.  It has no counterpart in the reference.

@@ -62,3 +62,29 @@ def test_decode_loop_matches_chunkwise():
         outs.append(o)
     assert rel_l2(torch.stack(outs, 2), full[:, :, L0:]) < TOL_F32
     assert rel_l2(M, Mfull) < TOL_F32
+
+
+@pytest.mark.parametrize("mode", ["sigmoid2", "one", "phi", "beta"])
+@pytest.mark.parametrize("D,gdt", [(64, torch.float32), (33, torch.float32), (128, torch.bfloat16),
+                                   (32, torch.bfloat16)])
+def test_decode_gated(mode, D, gdt):
+    """dp_core_decode_gated reads the raw gate from a strided (B, H) slice of the block's
+    projection row and forms beta itself: 2 sigmoid(g) (layers.py:265), 1 (beta_mode
+    "fixed", :266-267), 1 + e^{i g} (layers.py:397-398), or g as given."""
+    B, H = 3, 4
+    M, k, q, v, _ = _inputs(D + 7, B, H, D)
+    rng = np.random.default_rng(D)
+    proj = rng.standard_normal((B, 3 * H * D + H)).astype(np.float32) * 2.0
+    proj = round_bf16(proj) if gdt == torch.bfloat16 else proj
+    g = proj[:, 3 * H * D:]
+    gate = to_dev(proj, gdt)[:, 3 * H * D:]
+    code = {"beta": dp._capi.DP_GATE_BETA, "sigmoid2": dp._capi.DP_GATE_SIGMOID2,
+            "one": dp._capi.DP_GATE_ONE, "phi": dp._capi.DP_GATE_PHI}[mode]
+    out, Mn = dp.decode_step(to_dev(M), to_dev(k), to_dev(q), to_dev(v), gate, gate_mode=code)
+    if mode == "phi":
+        ro, rM = ocore.complex_beta_step(M, k, q, v, g)
+    else:
+        b = {"beta": g, "sigmoid2": 2.0 / (1.0 + np.exp(-g.astype(np.float64))), "one": np.ones_like(g)}[mode]
+        ro, rM = ocore.decode_step(M, k, q, v, b)
+    assert rel_l2(out, ro) < TOL_F32
+    assert rel_l2(Mn, rM) < TOL_F32

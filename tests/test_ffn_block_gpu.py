@@ -133,6 +133,28 @@ def test_ffn_widths(d, dtype):
     assert rel_l2(y.float(), ref) < (TOL_BF16 if dtype == torch.bfloat16 else TOL_F32)
 
 
+@pytest.mark.parametrize("d,dtype", [(1024, torch.bfloat16), (256, torch.float32), (64, torch.bfloat16)])
+def test_ffn_residual_accumulate(d, dtype):
+    """dp_ffn_fwd_residual (through LearnableSubstrateLerpFFN.add_to): r += FFN(x) in
+    float32, the block's x + ffn(norm2(x)) (layers.py:243, 290), against the fp64 oracle."""
+    torch.manual_seed(d + 1)
+    nb, tokens = 4, 16
+    ffn = dp.LearnableSubstrateLerpFFN(d, nb).cuda()
+    with torch.no_grad():
+        for n, p in ffn.named_parameters():
+            p.copy_(torch.randn_like(p) * (1.0 if n == "substrate_logits" else 0.02))
+    x = torch.randn(tokens, d, device="cuda").to(dtype)
+    r0 = torch.randn(tokens, d, device="cuda")
+    r = r0.clone()
+    with torch.no_grad():
+        out = ffn.add_to(r, x)
+    assert out.data_ptr() == r.data_ptr()
+    params = {k: v.detach().cpu().numpy() for k, v in ffn.state_dict().items()}
+    ref = ospec.lerp_ffn(x.float().cpu().numpy(), params)
+    tol = TOL_BF16 if dtype == torch.bfloat16 else TOL_F32
+    assert rel_l2(r - r0, ref) < tol
+
+
 def test_ffn_unaligned_rows():
     """x starting 2 bytes past a 16-byte boundary takes the block-per-token kernel."""
     torch.manual_seed(3)
