@@ -28,6 +28,9 @@ namespace {
 
 // ---------------------------------------------------------------- fold
 constexpr int kFoldTile = 32;
+// token counts up to which dp_ffn_fwd computes the three feature branches of a token on
+// three warps (decode batches) instead of one
+constexpr int kFeatSplitTokens = 512;
 
 // grid (d/32, d/32, 6): z = 2*branch + s.  One thread per output, float64 accumulation.
 __global__ void __launch_bounds__(kFoldTile * 8)
@@ -189,39 +192,32 @@ __device__ __forceinline__ void store_cos_sin(T *cp, T *sp, const float *vals, f
   }
 }
 
+// lane l's R consecutive values of the token row (16-byte loads; aligned by the launcher)
 template <typename T, int R>
-__global__ void __launch_bounds__(256)
-ffn_features_warp_kernel(const T *__restrict__ x, const float *__restrict__ hdct, T *__restrict__ z, int tokens) {
-  // R >= 8: the 16-byte loads of x and hdct and the z stores of a lane start on 16-byte
-  // boundaries, and the Haar output runs of a lane have an even length
-  static_assert(R >= 8 && R % 8 == 0, "warp features need d = 256, 512 or 1024");
-  constexpr int d = 32 * R;
-  const int lane = threadIdx.x & 31;
-  const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
-  if (row >= tokens) return;  // whole warps only: no block barrier in this kernel
-  const float r2 = 0.70710678118654752f;
-  float v[R], hv[R];
-  {
-    const T *xr = x + row * d + R * lane;  // 16-byte aligned (checked by the launcher)
-    if constexpr (sizeof(T) == 2 && R % 8 == 0) {
+__device__ __forceinline__ void load_row_part(const T *__restrict__ xr, float (&v)[R]) {
+  if constexpr (sizeof(T) == 2 && R % 8 == 0) {
 #pragma unroll
-      for (int r = 0; r < R; r += 8) {
-        const uint4 q = __ldg(reinterpret_cast<const uint4 *>(xr + r));
-        const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+    for (int r = 0; r < R; r += 8) {
+      const uint4 q = __ldg(reinterpret_cast<const uint4 *>(xr + r));
+      const uint32_t w[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&w[k]));
-          v[r + 2 * k] = hv[r + 2 * k] = f.x;
-          v[r + 2 * k + 1] = hv[r + 2 * k + 1] = f.y;
-        }
+      for (int k = 0; k < 4; ++k) {
+        const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&w[k]));
+        v[r + 2 * k] = f.x;
+        v[r + 2 * k + 1] = f.y;
       }
-    } else {
-#pragma unroll
-      for (int r = 0; r < R; ++r) v[r] = hv[r] = to_f32(xr[r]);
     }
+  } else {
+#pragma unroll
+    for (int r = 0; r < R; ++r) v[r] = to_f32(xr[r]);
   }
-  T *zr = z + row * 6 * d;
-  // ---- FWHT (natural Sylvester order), /sqrt(d)
+}
+
+// FWHT branch (natural Sylvester order, / sqrt(d)): cos / sin into z[0:d], z[d:2d].
+// v holds lane l's values x[R l .. R l + R) and is overwritten.
+template <typename T, int R>
+__device__ __forceinline__ void features_fwht(float (&v)[R], T *__restrict__ zr, int lane) {
+  constexpr int d = 32 * R;
 #pragma unroll
   for (int len = 1; len < R; len <<= 1) {
 #pragma unroll
@@ -243,17 +239,29 @@ ffn_features_warp_kernel(const T *__restrict__ x, const float *__restrict__ hdct
     }
   }
   store_cos_sin<T, R>(zr + R * lane, zr + d + R * lane, v, rsqrtf((float)d));
-  // ---- DCT branch: cos / sin of the projections
-  {
-    const float *hr = hdct + row * d + R * lane;
+}
+
+// DCT branch: cos / sin of the projections hdct into z[2d:3d], z[3d:4d].
+template <typename T, int R>
+__device__ __forceinline__ void features_dct(const float *__restrict__ hrow, T *__restrict__ zr, int lane) {
+  constexpr int d = 32 * R;
+  float v[R];
+  const float *hr = hrow + R * lane;
 #pragma unroll
-    for (int r = 0; r < R; r += 4) {
-      const float4 q = *reinterpret_cast<const float4 *>(hr + r);
-      v[r] = q.x; v[r + 1] = q.y; v[r + 2] = q.z; v[r + 3] = q.w;
-    }
-    store_cos_sin<T, R>(zr + 2 * d + R * lane, zr + 3 * d + R * lane, v, 1.f);
+  for (int r = 0; r < R; r += 4) {
+    const float4 q = *reinterpret_cast<const float4 *>(hr + r);
+    v[r] = q.x; v[r + 1] = q.y; v[r + 2] = q.z; v[r + 3] = q.w;
   }
-  // ---- recursive Haar: levels n = 32R .. 2R span nl = n / R lanes
+  store_cos_sin<T, R>(zr + 2 * d + R * lane, zr + 3 * d + R * lane, v, 1.f);
+}
+
+// Recursive Haar branch into z[4d:5d], z[5d:6d]; hv holds lane l's values of x and is
+// overwritten.
+template <typename T, int R>
+__device__ __forceinline__ void features_haar(float (&hv)[R], T *__restrict__ zr, int lane) {
+  constexpr int d = 32 * R;
+  const float r2 = 0.70710678118654752f;
+  // levels n = 32R .. 2R span nl = n / R lanes
 #pragma unroll
   for (int nl = 32; nl >= 2; nl >>= 1) {
     const int half_l = nl >> 1;
@@ -287,6 +295,49 @@ ffn_features_warp_kernel(const T *__restrict__ x, const float *__restrict__ hdct
     ho[0] = hv[0];
     store_cos_sin<T, R>(zr + 4 * d, zr + 5 * d, ho, 1.f);
   }
+}
+
+template <typename T, int R>
+__global__ void __launch_bounds__(256)
+ffn_features_warp_kernel(const T *__restrict__ x, const float *__restrict__ hdct, T *__restrict__ z, int tokens) {
+  // R >= 8: the 16-byte loads of x and hdct and the z stores of a lane start on 16-byte
+  // boundaries, and the Haar output runs of a lane have an even length
+  static_assert(R >= 8 && R % 8 == 0, "warp features need d = 256, 512 or 1024");
+  constexpr int d = 32 * R;
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (row >= tokens) return;  // whole warps only: no block barrier in this kernel
+  float v[R], hv[R];
+  load_row_part<T, R>(x + row * d + R * lane, v);
+#pragma unroll
+  for (int r = 0; r < R; ++r) hv[r] = v[r];
+  T *zr = z + row * 6 * d;
+  features_fwht<T, R>(v, zr, lane);
+  features_dct<T, R>(hdct + row * d, zr, lane);
+  features_haar<T, R>(hv, zr, lane);
+}
+
+// Few tokens (decode): one CTA of three warps per token, warp w computing branch w
+// (FWHT, DCT, Haar) of the warp kernel above, so a token's features take a third of
+// the serial time.
+template <typename T, int R>
+__global__ void __launch_bounds__(96)
+ffn_features_split_kernel(const T *__restrict__ x, const float *__restrict__ hdct, T *__restrict__ z) {
+  static_assert(R >= 8 && R % 8 == 0, "warp features need d = 256, 512 or 1024");
+  constexpr int d = 32 * R;
+  const int lane = threadIdx.x & 31, part = threadIdx.x >> 5;
+  const int64_t row = blockIdx.x;
+  T *zr = z + row * 6 * d;
+  if (part == 1) {
+    features_dct<T, R>(hdct + row * d, zr, lane);
+    return;
+  }
+  float v[R];
+  load_row_part<T, R>(x + row * d + R * lane, v);
+  if (part == 0)
+    features_fwht<T, R>(v, zr, lane);
+  else
+    features_haar<T, R>(v, zr, lane);
 }
 
 // ---------------------------------------------------------------- cuBLAS handles
@@ -359,9 +410,18 @@ int ffn_fwd_impl(const void *x, int x_dtype, const void *dct, const void *F, voi
   cudaFuncSetAttribute(ffn_features_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   cudaFuncSetAttribute(ffn_features_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   const int wgrid = (tokens + 7) / 8;
+  // below about one warp per SM sub-partition the three branches of a token run on
+  // three warps (ffn_features_split_kernel); above, one warp per token
+  const bool split = tokens <= kFeatSplitTokens;
   auto warp_features = [&](auto rc) {
     constexpr int R = decltype(rc)::value;
-    if (bf)
+    if (bf && split)
+      ffn_features_split_kernel<__nv_bfloat16, R><<<tokens, 96, 0, st>>>(
+          static_cast<const __nv_bfloat16 *>(x), hdct, static_cast<__nv_bfloat16 *>(z));
+    else if (split)
+      ffn_features_split_kernel<float, R><<<tokens, 96, 0, st>>>(static_cast<const float *>(x), hdct,
+                                                                  static_cast<float *>(z));
+    else if (bf)
       ffn_features_warp_kernel<__nv_bfloat16, R><<<wgrid, 256, 0, st>>>(
           static_cast<const __nv_bfloat16 *>(x), hdct, static_cast<__nv_bfloat16 *>(z), tokens);
     else

@@ -116,11 +116,13 @@ def test_model_prefill_then_decode():
 
 @pytest.mark.parametrize("d", [64, 128, 256, 512, 1024, 2048])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-def test_ffn_widths(d, dtype):
-    """Every width of the warp-per-token feature kernel (256..1024) and the block-per-token
-    one (64, 128, 2048), float32 and bf16 activations, against the fp64 oracle."""
+@pytest.mark.parametrize("tokens", [77, 700])
+def test_ffn_widths(d, dtype, tokens):
+    """Every width of the warp feature kernels (256..1024: three warps per token up to 512
+    tokens, one warp per token above) and of the block-per-token one (64, 128, 2048),
+    float32 and bf16 activations, against the fp64 oracle."""
     torch.manual_seed(d)
-    nb, tokens = 4, 77
+    nb = 4
     ffn = dp.LearnableSubstrateLerpFFN(d, nb).cuda()
     with torch.no_grad():
         for n, p in ffn.named_parameters():
