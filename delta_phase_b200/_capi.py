@@ -44,6 +44,8 @@ _SIG = {
     "dp_ffn_workspace_size": (ctypes.c_size_t, [_I, _I, _I]),
     "dp_ffn_fwd": (_I, [_P, _I, _P, _P, _P, _I, _I, _P, ctypes.c_size_t, _P]),
     "dp_ffn_fwd_residual": (_I, [_P, _I, _P, _P, _P, _I, _I, _P, ctypes.c_size_t, _P]),
+    "dp_ffn_features": (_I, [_P, _I, _P, _P, _I, _I, _P]),
+    "dp_gemm_skinny": (_I, [_P, ctypes.c_int64, _P, _P, _I, _P, _I, ctypes.c_int64, _I, _I, _I, _I, _P]),
     "dp_ffn_fwd_noalloc": (_I, [_P, _I, _P, _P, _P, _I, _I, _P]),
     "dp_ffn_noalloc_max_tokens": (ctypes.c_size_t, [_I, _I]),
     "dp_ln_conv_silu": (_I, [_P, _I, _P, _P, ctypes.c_float, _P, _P, _P, _I, _I, _I, _I, _I, _P]),
@@ -327,6 +329,39 @@ def ffn_fwd_residual(x, dct, F, y, workspace):
                                        ptr(workspace), workspace.numel() * workspace.element_size(),
                                        stream_of(dev))
     _check("dp_ffn_fwd_residual", rc)
+
+
+def ffn_features(x, hdct, z):
+    """dp_ffn_features: z (tokens, 6d) from x (tokens, d) and hdct = x mat_dct^T (float32)."""
+    dev = require_cuda(x, hdct, z)
+    tokens, d = x.shape
+    for t in (x, hdct, z):
+        if not t.is_contiguous():
+            raise ValueError("dp_ffn_features takes contiguous tensors")
+    if hdct.dtype != torch.float32 or z.dtype != x.dtype or tuple(z.shape) != (tokens, 6 * d):
+        raise ValueError("hdct must be float32 (tokens, d) and z (tokens, 6d) of x's dtype")
+    with torch.cuda.device(dev):
+        rc = lib().dp_ffn_features(ptr(x), dtype_code(x), ptr(hdct), ptr(z), tokens, d, stream_of(dev))
+    _check("dp_ffn_features", rc)
+
+
+SKINNY_MAX_ROWS = 16
+
+
+def gemm_skinny(x, w, bias, y, accumulate=False):
+    """dp_gemm_skinny: y (M, N) = x (M, K) w^T (+ bias) (+ y); x, w bf16, M <= 16."""
+    dev = require_cuda(x, w, y)
+    M, K = x.shape
+    N = w.shape[0]
+    if x.dtype != torch.bfloat16 or w.dtype != torch.bfloat16:
+        raise ValueError("dp_gemm_skinny takes bf16 x and w")
+    if x.stride(1) != 1 or not w.is_contiguous() or y.stride(1) != 1 or tuple(y.shape) != (M, N):
+        raise ValueError("x, y need unit column stride, w must be contiguous (N, K)")
+    with torch.cuda.device(dev):
+        rc = lib().dp_gemm_skinny(ptr(x), x.stride(0), ptr(w), None if bias is None else ptr(bias),
+                                  DP_F32 if bias is None else dtype_code(bias), ptr(y), dtype_code(y),
+                                  y.stride(0), int(bool(accumulate)), M, N, K, stream_of(dev))
+    _check("dp_gemm_skinny", rc)
 
 
 def ffn_fwd_noalloc(x, dct, F, y):

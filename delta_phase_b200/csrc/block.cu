@@ -86,9 +86,11 @@ ln_conv_silu_kernel(const InT *__restrict__ x, const float *__restrict__ ln_w, c
 // One warp per row: s = x (+ res); y = LayerNorm(s); the row stays in L1 between passes.
 template <typename InT, typename OutT>
 __global__ void __launch_bounds__(kBlkThreads)
-layernorm_kernel(const InT *__restrict__ x, const float *__restrict__ res, const float *__restrict__ ln_w,
+layernorm_kernel(const InT *x, const float *res, const float *__restrict__ ln_w,
                  const float *__restrict__ ln_b, float eps, float *__restrict__ sum_out, OutT *__restrict__ y,
                  int64_t rows, int d) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t r = (int64_t)blockIdx.x * (kBlkThreads / 32) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (r >= rows) return;
@@ -153,10 +155,12 @@ __device__ __forceinline__ void store8(__nv_bfloat16 *p, const float (&v)[8]) {
 // the few rows of a decode step the load latency is paid once per row.
 template <typename InT, typename OutT, int NG>
 __global__ void __launch_bounds__(128)
-layernorm_reg_kernel(const InT *__restrict__ x, const float *__restrict__ res, const float *__restrict__ ln_w,
+layernorm_reg_kernel(const InT *x, const float *res, const float *__restrict__ ln_w,
                      const float *__restrict__ ln_b, float eps, float *__restrict__ sum_out, OutT *__restrict__ y,
                      int64_t rows) {
   constexpr int d = 256 * NG;
+  pdl_wait();
+  pdl_trigger();
   const int64_t r = (int64_t)blockIdx.x * 4 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (r >= rows) return;
@@ -205,11 +209,13 @@ layernorm_reg_kernel(const InT *__restrict__ x, const float *__restrict__ res, c
 // state (d, k-1) float32 shifts left and takes n (the conv's last k-1 inputs).
 template <typename InT, typename OutT>
 __global__ void __launch_bounds__(kBlkThreads)
-ln_conv_step_kernel(const InT *__restrict__ x, const float *__restrict__ ln_w, const float *__restrict__ ln_b,
+ln_conv_step_kernel(const InT *x, const float *__restrict__ ln_w, const float *__restrict__ ln_b,
                     float eps, const float *__restrict__ conv_w, const float *__restrict__ conv_b,
                     float *__restrict__ state, OutT *__restrict__ out, int d, int k) {
   __shared__ float red[kBlkThreads / 32];
   __shared__ float stat[2];
+  pdl_wait();
+  pdl_trigger();
   const int b = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const InT *xr = x + (size_t)b * d;
   const float inv_d = 1.0f / (float)d;
@@ -311,37 +317,31 @@ extern "C" int dp_layernorm(const void *x, int x_dtype, const float *residual, c
       using OT = decltype(ot);
       const XT *xp = static_cast<const XT *>(x);
       OT *yp = static_cast<OT *>(y);
-      switch (d / 256) {
-        case 1: layernorm_reg_kernel<XT, OT, 1><<<rb, 128, 0, st>>>(xp, residual, ln_w, ln_b, eps, sum_out, yp, rows); break;
-        case 2: layernorm_reg_kernel<XT, OT, 2><<<rb, 128, 0, st>>>(xp, residual, ln_w, ln_b, eps, sum_out, yp, rows); break;
-        case 3: layernorm_reg_kernel<XT, OT, 3><<<rb, 128, 0, st>>>(xp, residual, ln_w, ln_b, eps, sum_out, yp, rows); break;
-        default: layernorm_reg_kernel<XT, OT, 4><<<rb, 128, 0, st>>>(xp, residual, ln_w, ln_b, eps, sum_out, yp, rows);
-      }
+      auto kern = d == 256 ? layernorm_reg_kernel<XT, OT, 1>
+                  : d == 512 ? layernorm_reg_kernel<XT, OT, 2>
+                  : d == 768 ? layernorm_reg_kernel<XT, OT, 3>
+                             : layernorm_reg_kernel<XT, OT, 4>;
+      return launch_pdl(kern, dim3(rb), dim3(128), 0, st, xp, residual, ln_w, ln_b, eps, sum_out, yp, rows);
     };
-    if (x_dtype == DP_F32) {
-      if (y_dtype == DP_F32) launch_reg(float{}, float{});
-      else launch_reg(float{}, __nv_bfloat16{});
-    } else {
-      if (y_dtype == DP_F32) launch_reg(__nv_bfloat16{}, float{});
-      else launch_reg(__nv_bfloat16{}, __nv_bfloat16{});
-    }
-    return check_launch("layernorm_reg_kernel");
+    cudaError_t e;
+    if (x_dtype == DP_F32)
+      e = y_dtype == DP_F32 ? launch_reg(float{}, float{}) : launch_reg(float{}, __nv_bfloat16{});
+    else
+      e = y_dtype == DP_F32 ? launch_reg(__nv_bfloat16{}, float{}) : launch_reg(__nv_bfloat16{}, __nv_bfloat16{});
+    return pdl_status(e, "layernorm_reg_kernel");
   }
   auto launch = [&](auto xt, auto ot) {
     using XT = decltype(xt);
     using OT = decltype(ot);
-    layernorm_kernel<XT, OT><<<(unsigned)blocks, kBlkThreads, 0, st>>>(static_cast<const XT *>(x), residual, ln_w,
-                                                                       ln_b, eps, sum_out, static_cast<OT *>(y),
-                                                                       rows, d);
+    return launch_pdl(layernorm_kernel<XT, OT>, dim3((unsigned)blocks), dim3(kBlkThreads), 0, st,
+                      static_cast<const XT *>(x), residual, ln_w, ln_b, eps, sum_out, static_cast<OT *>(y), rows, d);
   };
-  if (x_dtype == DP_F32) {
-    if (y_dtype == DP_F32) launch(float{}, float{});
-    else launch(float{}, __nv_bfloat16{});
-  } else {
-    if (y_dtype == DP_F32) launch(__nv_bfloat16{}, float{});
-    else launch(__nv_bfloat16{}, __nv_bfloat16{});
-  }
-  return check_launch("layernorm_kernel");
+  cudaError_t e;
+  if (x_dtype == DP_F32)
+    e = y_dtype == DP_F32 ? launch(float{}, float{}) : launch(float{}, __nv_bfloat16{});
+  else
+    e = y_dtype == DP_F32 ? launch(__nv_bfloat16{}, float{}) : launch(__nv_bfloat16{}, __nv_bfloat16{});
+  return pdl_status(e, "layernorm_kernel");
 }
 
 extern "C" int dp_ln_conv_step(const void *x, int x_dtype, const float *ln_w, const float *ln_b, float eps,
@@ -358,15 +358,13 @@ extern "C" int dp_ln_conv_step(const void *x, int x_dtype, const float *ln_w, co
   auto launch = [&](auto xt, auto ot) {
     using XT = decltype(xt);
     using OT = decltype(ot);
-    ln_conv_step_kernel<XT, OT><<<B, kBlkThreads, 0, st>>>(static_cast<const XT *>(x), ln_w, ln_b, eps, conv_w,
-                                                           conv_b, conv_state, static_cast<OT *>(out), d, k);
+    return launch_pdl(ln_conv_step_kernel<XT, OT>, dim3(B), dim3(kBlkThreads), 0, st, static_cast<const XT *>(x),
+                      ln_w, ln_b, eps, conv_w, conv_b, conv_state, static_cast<OT *>(out), d, k);
   };
-  if (x_dtype == DP_F32) {
-    if (out_dtype == DP_F32) launch(float{}, float{});
-    else launch(float{}, __nv_bfloat16{});
-  } else {
-    if (out_dtype == DP_F32) launch(__nv_bfloat16{}, float{});
-    else launch(__nv_bfloat16{}, __nv_bfloat16{});
-  }
-  return check_launch("ln_conv_step_kernel");
+  cudaError_t e;
+  if (x_dtype == DP_F32)
+    e = out_dtype == DP_F32 ? launch(float{}, float{}) : launch(float{}, __nv_bfloat16{});
+  else
+    e = out_dtype == DP_F32 ? launch(__nv_bfloat16{}, float{}) : launch(__nv_bfloat16{}, __nv_bfloat16{});
+  return pdl_status(e, "ln_conv_step_kernel");
 }

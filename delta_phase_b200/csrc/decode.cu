@@ -41,12 +41,14 @@ __device__ __forceinline__ float gate_beta(float g, int gate_mode) {
 // kq: smem (4 x D): cos k, sin k, cos q, sin q; CB adds the write key (2 x D).
 template <bool kVec4, bool CB>
 __global__ void __launch_bounds__(kDecThreads)
-decode_kernel(const float *state_in, float *state_out, const void *__restrict__ tk,
-              const void *__restrict__ tq, const void *__restrict__ v,
-              const void *__restrict__ beta, int in_dt, int beta_dt, int gate_mode,
+decode_kernel(const float *state_in, float *state_out, const void *tk,
+              const void *tq, const void *v,
+              const void *beta, int in_dt, int beta_dt, int gate_mode,
               float *__restrict__ out, int H, int D, int Dv, SeqStrides s_tk, SeqStrides s_tq, SeqStrides s_v,
               SeqStrides s_b, SeqStrides s_out) {
   extern __shared__ float kq[];
+  pdl_wait();
+  pdl_trigger();
   const int bh = blockIdx.x, b = bh / H, h = bh % H;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   for (int c = tid; c < D; c += kDecThreads) {
@@ -157,11 +159,13 @@ decode_kernel(const float *state_in, float *state_out, const void *__restrict__ 
 // reduction, so every lane keeps RPW independent 16-byte loads in flight.
 template <int RPW, bool CB>
 __global__ void __launch_bounds__(kDecThreads)
-decode_rows_kernel(const float *state_in, float *state_out, const void *__restrict__ tk,
-                   const void *__restrict__ tq, const void *__restrict__ v,
-                   const void *__restrict__ beta, int in_dt, int beta_dt, int gate_mode,
+decode_rows_kernel(const float *state_in, float *state_out, const void *tk,
+                   const void *tq, const void *v,
+                   const void *beta, int in_dt, int beta_dt, int gate_mode,
                    float *__restrict__ out, int H, int D, int Dv, SeqStrides s_tk, SeqStrides s_tq, SeqStrides s_v, SeqStrides s_b,
                    SeqStrides s_out) {
+  pdl_wait();
+  pdl_trigger();
   const int bh = blockIdx.x, b = bh / H, h = bh % H;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int npair = D >> 1, p = lane;
@@ -261,8 +265,10 @@ int decode_entry(const char *name, int gate_mode, const float *state_in, float *
   if (vec4 && D <= 64 && Dv <= 128) {
     auto kern = Dv <= 64 ? (cbeta ? decode_rows_kernel<8, true> : decode_rows_kernel<8, false>)
                          : (cbeta ? decode_rows_kernel<16, true> : decode_rows_kernel<16, false>);
-    kern<<<B * H, kDecThreads, 0, as_stream(stream)>>>(state_in, state_out, theta_k, theta_q, v, beta, in_dtype,
-                                                       beta_dtype, gate_mode, out, H, D, Dv, s[0], s[1], s[2], s[3], s[4]);
+    return pdl_status(launch_pdl(kern, dim3(B * H), dim3(kDecThreads), 0, as_stream(stream), state_in, state_out,
+                                 theta_k, theta_q, v, beta, in_dtype, beta_dtype, gate_mode, out, H, D, Dv, s[0],
+                                 s[1], s[2], s[3], s[4]),
+                      "decode_rows_kernel");
   } else {
     auto kern = vec4 ? (cbeta ? decode_kernel<true, true> : decode_kernel<true, false>)
                      : (cbeta ? decode_kernel<false, true> : decode_kernel<false, false>);
@@ -270,10 +276,11 @@ int decode_entry(const char *name, int gate_mode, const float *state_in, float *
       const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       if (e != cudaSuccess) return set_error(DP_ERR_CUDA, n + ": smem attribute: " + cudaGetErrorString(e));
     }
-    kern<<<B * H, kDecThreads, smem, as_stream(stream)>>>(state_in, state_out, theta_k, theta_q, v, beta, in_dtype,
-                                                          beta_dtype, gate_mode, out, H, D, Dv, s[0], s[1], s[2], s[3], s[4]);
+    return pdl_status(launch_pdl(kern, dim3(B * H), dim3(kDecThreads), smem, as_stream(stream), state_in,
+                                 state_out, theta_k, theta_q, v, beta, in_dtype, beta_dtype, gate_mode, out, H, D,
+                                 Dv, s[0], s[1], s[2], s[3], s[4]),
+                      "decode_kernel");
   }
-  return check_launch("decode_kernel");
 }
 }  // namespace
 }  // namespace dp

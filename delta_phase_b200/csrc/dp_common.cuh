@@ -25,6 +25,47 @@ int check_launch(const char *what);
 
 inline cudaStream_t as_stream(void *s) { return reinterpret_cast<cudaStream_t>(s); }
 
+// ---------------------------------------------------------------- dependent launch
+// The token-step kernels run back to back, each a few microseconds long, so the gap
+// between two launches is a large part of a step.  They are launched with programmatic
+// dependent launch: a kernel may start while its predecessor in the stream still runs,
+// and waits in pdl_wait() (griddepcontrol.wait: until the predecessor grid has completed
+// and its writes are visible) before it touches memory that earlier kernels write, or
+// writes memory they read.  Right after its wait it lets its own successor start
+// (pdl_trigger).  Without the launch attribute both instructions do nothing.
+// Data written by earlier kernels is read with coherent loads in these kernels (no
+// __ldg, no const __restrict__ on those pointers): the read-only path assumes memory that
+// stays fixed for the kernel's lifetime, which a kernel started early does not see.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
+
+// kern<<<grid, block, smem, st>>>(args...) with the programmatic-dependent-launch
+// attribute; returns the launch status.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
+// Status of a launch_pdl call (DP_OK, or DP_ERR_CUDA with the message recorded).
+inline int pdl_status(cudaError_t e, const char *what) {
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return set_error(DP_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+  }
+  return check_launch(what);
+}
+
 // ---------------------------------------------------------------- dtypes
 template <typename T>
 __device__ __forceinline__ float to_f32(T x);

@@ -194,11 +194,11 @@ __device__ __forceinline__ void store_cos_sin(T *cp, T *sp, const float *vals, f
 
 // lane l's R consecutive values of the token row (16-byte loads; aligned by the launcher)
 template <typename T, int R>
-__device__ __forceinline__ void load_row_part(const T *__restrict__ xr, float (&v)[R]) {
+__device__ __forceinline__ void load_row_part(const T *xr, float (&v)[R]) {
   if constexpr (sizeof(T) == 2 && R % 8 == 0) {
 #pragma unroll
     for (int r = 0; r < R; r += 8) {
-      const uint4 q = __ldg(reinterpret_cast<const uint4 *>(xr + r));
+      const uint4 q = *reinterpret_cast<const uint4 *>(xr + r);
       const uint32_t w[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
@@ -243,7 +243,7 @@ __device__ __forceinline__ void features_fwht(float (&v)[R], T *__restrict__ zr,
 
 // DCT branch: cos / sin of the projections hdct into z[2d:3d], z[3d:4d].
 template <typename T, int R>
-__device__ __forceinline__ void features_dct(const float *__restrict__ hrow, T *__restrict__ zr, int lane) {
+__device__ __forceinline__ void features_dct(const float *hrow, T *__restrict__ zr, int lane) {
   constexpr int d = 32 * R;
   float v[R];
   const float *hr = hrow + R * lane;
@@ -322,9 +322,11 @@ ffn_features_warp_kernel(const T *__restrict__ x, const float *__restrict__ hdct
 // the serial time.
 template <typename T, int R>
 __global__ void __launch_bounds__(96)
-ffn_features_split_kernel(const T *__restrict__ x, const float *__restrict__ hdct, T *__restrict__ z) {
+ffn_features_split_kernel(const T *x, const float *hdct, T *__restrict__ z) {
   static_assert(R >= 8 && R % 8 == 0, "warp features need d = 256, 512 or 1024");
   constexpr int d = 32 * R;
+  pdl_wait();
+  pdl_trigger();
   const int lane = threadIdx.x & 31, part = threadIdx.x >> 5;
   const int64_t row = blockIdx.x;
   T *zr = z + row * 6 * d;
@@ -372,6 +374,52 @@ extern "C" size_t dp_ffn_workspace_size(int tokens, int d, int x_dtype) {
 
 namespace dp {
 namespace {
+// z (tokens, 6d) = the sin / cos features of x given its DCT projections hdct (tokens, d)
+// float32; x, z of dtype bf16 (bf = true) or float32, hdct and z 16-byte aligned.
+int launch_features(const void *x, bool bf, const float *hdct, void *z, int tokens, int d, cudaStream_t st) {
+  int log2d = 0;
+  while ((1 << log2d) < d) ++log2d;
+  const size_t smem = 4 * (size_t)d * sizeof(float);
+  const int threads = d >= 256 ? 256 : d;
+  cudaFuncSetAttribute(ffn_features_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaFuncSetAttribute(ffn_features_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  const int wgrid = (tokens + 7) / 8;
+  // below about one warp per SM sub-partition the three branches of a token run on
+  // three warps (ffn_features_split_kernel); above, one warp per token
+  const bool split = tokens <= kFeatSplitTokens;
+  cudaError_t le = cudaSuccess;
+  auto warp_features = [&](auto rc) {
+    constexpr int R = decltype(rc)::value;
+    if (bf && split)
+      le = launch_pdl(ffn_features_split_kernel<__nv_bfloat16, R>, dim3(tokens), dim3(96), 0, st,
+                      static_cast<const __nv_bfloat16 *>(x), hdct, static_cast<__nv_bfloat16 *>(z));
+    else if (split)
+      le = launch_pdl(ffn_features_split_kernel<float, R>, dim3(tokens), dim3(96), 0, st,
+                      static_cast<const float *>(x), hdct, static_cast<float *>(z));
+    else if (bf)
+      ffn_features_warp_kernel<__nv_bfloat16, R><<<wgrid, 256, 0, st>>>(
+          static_cast<const __nv_bfloat16 *>(x), hdct, static_cast<__nv_bfloat16 *>(z), tokens);
+    else
+      ffn_features_warp_kernel<float, R><<<wgrid, 256, 0, st>>>(static_cast<const float *>(x), hdct,
+                                                                 static_cast<float *>(z), tokens);
+  };
+  const bool x16 = (reinterpret_cast<uintptr_t>(x) & 15) == 0;
+  if (!x16) {
+    // unaligned rows: the block-per-token kernel below
+  } else if (d == 1024) warp_features(std::integral_constant<int, 32>{});
+  else if (d == 512) warp_features(std::integral_constant<int, 16>{});
+  else if (d == 256) warp_features(std::integral_constant<int, 8>{});
+  if (x16 && d >= 256 && d <= 1024) {
+    // launched above
+  } else if (bf)
+    ffn_features_kernel<__nv_bfloat16><<<tokens, threads, smem, st>>>(
+        static_cast<const __nv_bfloat16 *>(x), hdct, static_cast<__nv_bfloat16 *>(z), d, log2d);
+  else
+    ffn_features_kernel<float><<<tokens, threads, smem, st>>>(static_cast<const float *>(x), hdct,
+                                                               static_cast<float *>(z), d, log2d);
+  return pdl_status(le, "ffn_features_kernel");
+}
+
 // dp_ffn_fwd (accumulate = false: y = z F in x's dtype) and dp_ffn_fwd_residual
 // (accumulate = true: y float32, y += z F in the combine GEMM's epilogue).
 int ffn_fwd_impl(const void *x, int x_dtype, const void *dct, const void *F, void *y, int tokens, int d,
@@ -403,46 +451,7 @@ int ffn_fwd_impl(const void *x, int x_dtype, const void *dct, const void *F, voi
   cublasStatus_t cs = cublasGemmEx(hdl, CUBLAS_OP_T, CUBLAS_OP_N, d, tokens, d, &one, dct, ab, d, x,
                                    ab, d, &zero, hdct, CUDA_R_32F, d, ct, CUBLAS_GEMM_DEFAULT);
   DP_REQUIRE(cs == CUBLAS_STATUS_SUCCESS, DP_ERR_CUDA, "dp_ffn_fwd: DCT GEMM failed");
-  int log2d = 0;
-  while ((1 << log2d) < d) ++log2d;
-  const size_t smem = 4 * (size_t)d * sizeof(float);
-  const int threads = d >= 256 ? 256 : d;
-  cudaFuncSetAttribute(ffn_features_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  cudaFuncSetAttribute(ffn_features_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  const int wgrid = (tokens + 7) / 8;
-  // below about one warp per SM sub-partition the three branches of a token run on
-  // three warps (ffn_features_split_kernel); above, one warp per token
-  const bool split = tokens <= kFeatSplitTokens;
-  auto warp_features = [&](auto rc) {
-    constexpr int R = decltype(rc)::value;
-    if (bf && split)
-      ffn_features_split_kernel<__nv_bfloat16, R><<<tokens, 96, 0, st>>>(
-          static_cast<const __nv_bfloat16 *>(x), hdct, static_cast<__nv_bfloat16 *>(z));
-    else if (split)
-      ffn_features_split_kernel<float, R><<<tokens, 96, 0, st>>>(static_cast<const float *>(x), hdct,
-                                                                  static_cast<float *>(z));
-    else if (bf)
-      ffn_features_warp_kernel<__nv_bfloat16, R><<<wgrid, 256, 0, st>>>(
-          static_cast<const __nv_bfloat16 *>(x), hdct, static_cast<__nv_bfloat16 *>(z), tokens);
-    else
-      ffn_features_warp_kernel<float, R><<<wgrid, 256, 0, st>>>(static_cast<const float *>(x), hdct,
-                                                                 static_cast<float *>(z), tokens);
-  };
-  const bool x16 = (reinterpret_cast<uintptr_t>(x) & 15) == 0;
-  if (!x16) {
-    // unaligned rows: the block-per-token kernel below
-  } else if (d == 1024) warp_features(std::integral_constant<int, 32>{});
-  else if (d == 512) warp_features(std::integral_constant<int, 16>{});
-  else if (d == 256) warp_features(std::integral_constant<int, 8>{});
-  if (x16 && d >= 256 && d <= 1024) {
-    // launched above
-  } else if (bf)
-    ffn_features_kernel<__nv_bfloat16><<<tokens, threads, smem, st>>>(
-        static_cast<const __nv_bfloat16 *>(x), hdct, static_cast<__nv_bfloat16 *>(z), d, log2d);
-  else
-    ffn_features_kernel<float><<<tokens, threads, smem, st>>>(static_cast<const float *>(x), hdct,
-                                                               static_cast<float *>(z), d, log2d);
-  int rc = check_launch("ffn_features_kernel");
+  int rc = launch_features(x, bf, hdct, z, tokens, d, st);
   if (rc != DP_OK) return rc;
   // Y (tokens x d) = Z (tokens x 6d) F (6d x d)  <=>  Y^T = F^T Z^T in column-major
   cs = cublasGemmEx(hdl, CUBLAS_OP_N, CUBLAS_OP_N, d, tokens, 6 * d, &one, F, ab, d, z, ab, 6 * d,
@@ -616,4 +625,19 @@ extern "C" int dp_ffn_fwd_noalloc(const void *x, int x_dtype, const void *dct, c
                                  d, sp, st);
   return ffn_fwd_noalloc_typed(static_cast<const float *>(x), static_cast<const float *>(dct),
                                static_cast<const float *>(F), static_cast<float *>(y), tokens, d, sp, st);
+}
+
+extern "C" int dp_ffn_features(const void *x, int x_dtype, const float *hdct, void *z, int tokens, int d,
+                               void *stream) {
+  using namespace dp;
+  DP_REQUIRE(tokens >= 0 && d >= 1, DP_ERR_INVALID_ARGUMENT, "dp_ffn_features: bad sizes");
+  DP_REQUIRE(x_dtype == DP_F32 || x_dtype == DP_BF16, DP_ERR_INVALID_ARGUMENT,
+             "dp_ffn_features: x dtype must be float32 or bfloat16");
+  DP_REQUIRE((d & (d - 1)) == 0 && d >= 8 && d <= 4096, DP_ERR_UNSUPPORTED,
+             "dp_ffn_features: d must be a power of two in [8, 4096]");
+  if (tokens == 0) return DP_OK;
+  DP_REQUIRE(x && hdct && z, DP_ERR_INVALID_ARGUMENT, "dp_ffn_features: null pointer");
+  DP_REQUIRE(reinterpret_cast<uintptr_t>(hdct) % 16 == 0 && reinterpret_cast<uintptr_t>(z) % 16 == 0,
+             DP_ERR_MISALIGNED, "dp_ffn_features: hdct and z must be 16-byte aligned");
+  return launch_features(x, x_dtype == DP_BF16, hdct, z, tokens, d, as_stream(stream));
 }

@@ -116,6 +116,15 @@ class LearnableSubstrateLerpFFN(nn.Module):
             self._fold[dtype] = (Fm.to(dtype), dct.to(dtype))
         return self._fold[dtype]
 
+    @torch.no_grad()
+    def folded_t(self):
+        """F^T (d x 6d) in bf16, contiguous: the combine matrix in nn.Linear layout for
+        dp_gemm_skinny, cached with the fold."""
+        Fm, _ = self.folded(torch.bfloat16)
+        if self._fold.get("t") is None or self._fold["t"][0] is not Fm:
+            self._fold["t"] = (Fm, Fm.t().contiguous())
+        return self._fold["t"][1]
+
     def _forward_autograd(self, x: torch.Tensor) -> torch.Tensor:
         """The reference's formula (layers.py:119-141) as differentiable torch ops, for
         training (the folded CUDA path has no backward)."""
@@ -166,8 +175,17 @@ class LearnableSubstrateLerpFFN(nn.Module):
         cdt, _ = self._compute_dtype(x)
         x2 = x.reshape(-1, self.d_model).to(cdt).contiguous()
         Fm, dct = self.folded(cdt)
-        ws = torch.empty(_capi.ffn_workspace_size(x2.shape[0], self.d_model, cdt),
-                         device=x.device, dtype=torch.uint8)
+        tokens, d = x2.shape
+        ws = torch.empty(_capi.ffn_workspace_size(tokens, d, cdt), device=x.device, dtype=torch.uint8)
+        if cdt == torch.bfloat16 and tokens <= _capi.SKINNY_MAX_ROWS and d % 32 == 0:
+            # decode batch: DCT projection and folded combine through dp_gemm_skinny (F^T
+            # is the (d, 6d) weight in nn.Linear layout), features in between
+            hdct = ws[:tokens * d * 4].view(torch.float32).view(tokens, d)
+            z = ws[tokens * d * 4:tokens * d * 16].view(torch.bfloat16).view(tokens, 6 * d)
+            _capi.gemm_skinny(x2, dct, None, hdct)
+            _capi.ffn_features(x2, hdct, z)
+            _capi.gemm_skinny(z, self.folded_t(), None, residual.view(-1, d), accumulate=True)
+            return residual
         _capi.ffn_fwd_residual(x2, dct, Fm, residual.view(-1, self.d_model), ws)
         return residual
 
@@ -336,8 +354,14 @@ class _DeltaRuleBlock(nn.Module):
                            None if conv.bias is None else conv.bias.detach().float(), conv_state, conv_x)
         W, bvec = self._proj_weights(gdt)
         Wo, bo = self._out_proj_weights(gdt)
+        # decode batches of bf16 rows: the weights stream through dp_gemm_skinny
+        skinny = gdt == torch.bfloat16 and B <= _capi.SKINNY_MAX_ROWS and D % 32 == 0
         with torch.autocast(x_t.device.type, enabled=False):
-            proj = F.linear(conv_x, W, bvec)                      # (B, 3D + H)
+            if skinny:
+                proj = torch.empty(B, W.shape[0], device=x_t.device, dtype=gdt)
+                _capi.gemm_skinny(conv_x, W, bvec, proj)
+            else:
+                proj = F.linear(conv_x, W, bvec)                  # (B, 3D + H)
             tk = proj[:, :D].view(B, H, dk)
             tq = proj[:, D:2 * D].view(B, H, dk)
             v = proj[:, 2 * D:3 * D].view(B, H, dk)
@@ -349,7 +373,11 @@ class _DeltaRuleBlock(nn.Module):
             nr = self.norm_retrieved
             rn = torch.empty(B, D, device=x_t.device, dtype=gdt)
             _capi.layernorm(out.view(B, D), nr.weight.float(), nr.bias.float(), nr.eps, rn)
-            o = F.linear(rn, Wo, bo)
+            if skinny:
+                o = torch.empty(B, D, device=x_t.device, dtype=gdt)
+                _capi.gemm_skinny(rn, Wo, bo, o)
+            else:
+                o = F.linear(rn, Wo, bo)
             res32 = xc if xc.dtype == torch.float32 else xc.float()
             s_sum = torch.empty(B, D, device=x_t.device, dtype=torch.float32)
             n2 = torch.empty(B, D, device=x_t.device, dtype=gdt)

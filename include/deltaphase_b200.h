@@ -273,6 +273,29 @@ DP_API int dp_ffn_fwd_residual(const void *x, int x_dtype, const void *dct, cons
                int tokens, int d, void *workspace, size_t workspace_bytes, void *stream);
 
 /*
+ * The middle step of dp_ffn_fwd on its own: z (tokens, 6d) = [cos h_b, sin h_b] for the
+ * three branches of LearnableSubstrateLerpFFN.forward (delta_phase/layers.py:119-141),
+ * FWHT and Haar from x, the DCT branch from its projections hdct = x mat_dct^T
+ * (tokens, d) float32.  x and z of dtype x_dtype (float32 or bf16), contiguous; hdct
+ * and z 16-byte aligned.  Lets a caller run the two GEMMs around it with its own GEMM
+ * (dp_gemm_skinny for decode batches).
+ */
+DP_API int dp_ffn_features(const void *x, int x_dtype, const float *hdct, void *z, int tokens, int d,
+               void *stream);
+
+/*
+ * Skinny GEMM for decode batches: y (M, N) = x (M, K) W^T (+ bias) (+ y if accumulate),
+ * the token-step projections of the blocks (delta_phase/layers.py:262-290; nn.Linear with
+ * M = batch rows) and the FFN's two matrix products.
+ *   x (M, K) bf16, row stride ldx (a multiple of 8); W (N, K) bf16, contiguous
+ *   (nn.Linear weight layout); both 16-byte aligned.  bias (N) of bias_dtype or NULL.
+ *   y (M, N) of y_dtype, row stride ldy.  1 <= M <= 16; K a multiple of 32.
+ * fp32 accumulation; deterministic (the K split is summed in a fixed order).
+ */
+DP_API int dp_gemm_skinny(const void *x, int64_t ldx, const void *w, const void *bias, int bias_dtype,
+               void *y, int y_dtype, int64_t ldy, int accumulate, int M, int N, int K, void *stream);
+
+/*
  * Allocation-free variant of dp_ffn_fwd.  It has no counterpart in the reference.
  * For callers that cannot allocate device memory where they run the FFN: code being
  * captured into a CUDA graph (cudaMalloc cannot be captured), runtimes whose own
