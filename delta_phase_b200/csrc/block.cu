@@ -214,6 +214,8 @@ ln_conv_step_kernel(const InT *x, const float *__restrict__ ln_w, const float *_
                     float *__restrict__ state, OutT *__restrict__ out, int d, int k) {
   __shared__ float red[kBlkThreads / 32];
   __shared__ float stat[2];
+  if (threadIdx.x == 0 && k > 1)  // this row's conv state, into L2 before the wait
+    prefetch_l2_span(state + (size_t)blockIdx.x * d * (k - 1), (size_t)d * (k - 1) * 4);
   pdl_wait();
   pdl_trigger();
   const int b = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;

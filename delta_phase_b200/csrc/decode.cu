@@ -164,6 +164,9 @@ decode_rows_kernel(const float *state_in, float *state_out, const void *tk,
                    const void *beta, int in_dt, int beta_dt, int gate_mode,
                    float *__restrict__ out, int H, int D, int Dv, SeqStrides s_tk, SeqStrides s_tq, SeqStrides s_v, SeqStrides s_b,
                    SeqStrides s_out) {
+  // this (b, h)'s state does not come from the kernels this one overlaps: fetch it into
+  // L2 while the predecessor finishes (the loads themselves follow the wait)
+  if (threadIdx.x == 0) prefetch_l2_span(state_in + (int64_t)blockIdx.x * Dv * 2 * D, (size_t)Dv * 2 * D * 4);
   pdl_wait();
   pdl_trigger();
   const int bh = blockIdx.x, b = bh / H, h = bh % H;

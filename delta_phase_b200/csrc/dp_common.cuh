@@ -57,6 +57,20 @@ inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, siz
   return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
 }
 
+// Ask the L2 to fetch `bytes` (a multiple of 16) from p (16-byte aligned): a TMA bulk
+// prefetch, which needs no registers and no completion wait.  Safe before pdl_wait: it
+// returns no data to the thread, and the L2 is coherent with the writes of other kernels.
+__device__ __forceinline__ void prefetch_l2_bulk(const void *p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// The same for an arbitrary span: the 16-byte aligned interior of [p, p + bytes).
+__device__ __forceinline__ void prefetch_l2_span(const void *p, size_t bytes) {
+  const uintptr_t a = (reinterpret_cast<uintptr_t>(p) + 15) & ~uintptr_t(15);
+  const uintptr_t e = (reinterpret_cast<uintptr_t>(p) + bytes) & ~uintptr_t(15);
+  if (e > a) prefetch_l2_bulk(reinterpret_cast<const void *>(a), (uint32_t)(e - a));
+}
+
 // Status of a launch_pdl call (DP_OK, or DP_ERR_CUDA with the message recorded).
 inline int pdl_status(cudaError_t e, const char *what) {
   if (e != cudaSuccess) {

@@ -58,12 +58,6 @@ __device__ __forceinline__ void store_scalar(void *p, int dt, int64_t i, float v
     static_cast<__half *>(p)[i] = __float2half_rn(v);
 }
 
-// Ask the L2 to fetch `bytes` (a multiple of 16) from p (16-byte aligned): a TMA bulk
-// prefetch, which needs no registers and no completion wait.
-__device__ __forceinline__ void prefetch_l2_bulk(const void *p, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(p), "r"(bytes) : "memory");
-}
-
 // One 32-wide K step of a warp: x rows g, g + 8 and W row n, 8 consecutive k per lane.
 struct SkStep {
   uint4 a, b, w;

@@ -62,10 +62,10 @@ class DecodeGraph:
         m = self.model
         with torch.no_grad(), torch.autocast("cuda", dtype=self.autocast_dtype or torch.float32,
                                              enabled=self.autocast_dtype is not None):
-            h = m._embed(self.ids)
+            h = m._embed_step(self.ids)
             for blk, conv, mem in zip(m.blocks, self.conv, self.mem):
                 h = blk._step_inplace(h, conv, mem, keep_fp32=True)
-            return m._head(h)
+            return m._head_step(h)
 
     def step(self, input_id_t: torch.Tensor) -> torch.Tensor:
         """One token per sequence, ids (B, 1); returns the logits (a static buffer)."""

@@ -11,7 +11,9 @@ from typing import List, Optional, Tuple
 
 import torch
 import torch.nn as nn
+import torch.nn.functional as F
 
+from . import _capi
 from .layers import ComplexBetaDeltaPhaseBlock, DeltaPhaseHolographicBlock
 
 
@@ -83,6 +85,63 @@ class DeltaPhaseModel(nn.Module):
             h = self.head_proj(h)
         return self.head(h)
 
+    # ---- decode step: embedding and head of a few bf16 rows on the library's kernels
+    def _bf16_weight(self, lin):
+        """bf16 copy of a Linear's / Embedding's weight, rebuilt when it changes."""
+        cache = self.__dict__.setdefault("_bf16_cache", {})
+        w = lin.weight
+        key = (w.data_ptr(), w._version, w.device)
+        hit = cache.get(id(w))  # per parameter: the tied embedding / head share one copy
+        if hit is None or hit[0] != key:
+            with torch.no_grad():
+                hit = (key, w.detach().to(torch.bfloat16).contiguous())
+            cache[id(w)] = hit
+        return hit[1]
+
+    def _step_fast(self, rows: int, dev) -> bool:
+        """Decode rows under bf16 autocast go through dp_layernorm / dp_gemm_skinny with
+        cached bf16 weights (no per-token weight casts)."""
+        if not (dev.type == "cuda" and torch.is_autocast_enabled("cuda")
+                and torch.get_autocast_dtype("cuda") == torch.bfloat16):
+            return False
+        if rows > _capi.SKINNY_MAX_ROWS or torch.is_grad_enabled():
+            return False
+        dims = [self.config.dim] + ([self.config.emb_dim] if self.use_factorized else [])
+        return all(d % 32 == 0 for d in dims) and self.head.bias is None and \
+            (self.embed_proj is None or self.embed_proj.bias is None) and \
+            (self.head_proj is None or self.head_proj.bias is None)
+
+    def _embed_step(self, ids):
+        """_embed for one token per sequence; (B, 1, dim), float32 on the fast path."""
+        B = ids.shape[0]
+        if not self._step_fast(B, ids.device):
+            return self._embed(ids)
+        e = F.embedding(ids.reshape(B), self._bf16_weight(self.embed))
+        if not self.use_factorized:
+            return e.view(B, 1, -1)
+        h = torch.empty(B, self.config.dim, device=ids.device, dtype=torch.float32)
+        _capi.gemm_skinny(e, self._bf16_weight(self.embed_proj), None, h)
+        return h.view(B, 1, -1)
+
+    def _head_step(self, h):
+        """_head for one token per sequence; bf16 logits on the fast path, like the
+        autocast matmul of the reference's head."""
+        B = h.shape[0]
+        if not self._step_fast(B, h.device):
+            return self._head(h)
+        d = self.config.dim
+        x = h.reshape(B, d)
+        n = torch.empty(B, d, device=h.device, dtype=torch.bfloat16)
+        nf = self.norm_f
+        _capi.layernorm(x.contiguous(), nf.weight.float(), nf.bias.float(), nf.eps, n)
+        if self.head_proj is not None:
+            p = torch.empty(B, self.config.emb_dim, device=h.device, dtype=torch.bfloat16)
+            _capi.gemm_skinny(n, self._bf16_weight(self.head_proj), None, p)
+            n = p
+        out = torch.empty(B, self.config.vocab_size, device=h.device, dtype=torch.bfloat16)
+        _capi.gemm_skinny(n, self._bf16_weight(self.head), None, out)
+        return out.view(B, 1, -1)
+
     def forward(self, input_ids: torch.Tensor, states: Optional[List[torch.Tensor]] = None):
         """Prefill over a whole sequence (model.py:82-103); returns logits."""
         h = self._embed(input_ids)
@@ -105,7 +164,7 @@ class DeltaPhaseModel(nn.Module):
 
     def step(self, input_id_t: torch.Tensor, states=None) -> Tuple[torch.Tensor, list]:
         """One decode step (model.py:105-128); returns (logits, new_states)."""
-        h = self._embed(input_id_t)
+        h = self._embed_step(input_id_t)
         if states is None:
             states = [None] * len(self.blocks)
         new_states = []
@@ -113,7 +172,7 @@ class DeltaPhaseModel(nn.Module):
             # the residual stream stays float32 between blocks (no bf16 round trip per layer)
             h, s = block._step_fresh(h, states[i], keep_fp32=True)
             new_states.append(s)
-        return self._head(h), new_states
+        return self._head_step(h), new_states
 
     def print_substrate_report(self):
         print("=" * 72)

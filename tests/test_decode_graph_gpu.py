@@ -47,3 +47,23 @@ def test_graph_decode_reproduces_prefill():
     for t in range(L):
         lt = g.step(ids[:, t:t + 1])
     assert rel_l2(lt[:, 0], logits[:, -1]) < TOL_F32
+
+
+def test_step_fast_embedding_and_head(monkeypatch):
+    """Under bf16 autocast, model.step's embedding and head run on dp_gemm_skinny /
+    dp_layernorm with cached bf16 weights; they agree with the module path (torch
+    embedding, nn.LayerNorm, autocast matmuls) to bf16 precision."""
+    model = _model(dim=256, heads=4, layers=2, vocab=300, seed=3)
+    B = 5
+    ids = torch.randint(0, 300, (B, 6), device="cuda")
+    outs = {}
+    for fast in (True, False):
+        if not fast:
+            monkeypatch.setattr(type(model), "_step_fast", lambda self, rows, dev: False)
+        st = None
+        with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+            for t in range(6):
+                lg, st = model.step(ids[:, t:t + 1], st)
+        outs[fast] = lg.float()
+    assert outs[True].shape == (B, 1, 300)
+    assert rel_l2(outs[True], outs[False]) < 2e-2
