@@ -261,6 +261,75 @@ ln_conv_step_kernel(const InT *x, const float *__restrict__ ln_w, const float *_
   }
 }
 
+// The same step for the usual shapes (conv kernel size 4, d = 256 CPT <= 1024): thread t
+// owns channels t + 256 j; every load of the row -- x, the LayerNorm and conv parameters,
+// the three state values -- is issued right after the wait, before the two reductions,
+// so the step pays one memory round trip instead of three.
+template <typename InT, typename OutT, int CPT>
+__global__ void __launch_bounds__(kBlkThreads)
+ln_conv_step_reg_kernel(const InT *x, const float *__restrict__ ln_w, const float *__restrict__ ln_b, float eps,
+                        const float *__restrict__ conv_w, const float *__restrict__ conv_b, float *state,
+                        OutT *__restrict__ out) {
+  constexpr int d = kBlkThreads * CPT;
+  __shared__ float red[2][kBlkThreads / 32];
+  const int b = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  float *st = state + (size_t)b * d * 3;
+  if (tid == 0) prefetch_l2_span(st, (size_t)d * 3 * 4);  // before the wait: see the kernel above
+  pdl_wait();
+  pdl_trigger();
+  float xv[CPT], w[CPT], bb[CPT], cb[CPT], s0[CPT], s1[CPT], s2[CPT];
+  float4 cw[CPT];
+#pragma unroll
+  for (int j = 0; j < CPT; ++j) {
+    const int c = tid + kBlkThreads * j;
+    xv[j] = to_f32(x[(size_t)b * d + c]);
+    w[j] = ln_w[c];
+    bb[j] = ln_b[c];
+    cb[j] = conv_b ? conv_b[c] : 0.f;
+    cw[j] = reinterpret_cast<const float4 *>(conv_w)[c];  // w[c][0..3], 16-byte aligned rows
+    s0[j] = st[c * 3];
+    s1[j] = st[c * 3 + 1];
+    s2[j] = st[c * 3 + 2];
+  }
+  float s = 0.f;
+#pragma unroll
+  for (int j = 0; j < CPT; ++j) s += xv[j];
+  s = warp_sum(s);
+  if (lane == 0) red[0][warp] = s;
+  __syncthreads();
+  float t = 0.f;
+#pragma unroll
+  for (int i = 0; i < kBlkThreads / 32; ++i) t += red[0][i];
+  const float mean = t * (1.0f / d);
+  float q = 0.f;
+#pragma unroll
+  for (int j = 0; j < CPT; ++j) {
+    const float dv = xv[j] - mean;
+    q = fmaf(dv, dv, q);
+  }
+  q = warp_sum(q);
+  if (lane == 0) red[1][warp] = q;
+  __syncthreads();
+  t = 0.f;
+#pragma unroll
+  for (int i = 0; i < kBlkThreads / 32; ++i) t += red[1][i];
+  const float rstd = rsqrtf(t * (1.0f / d) + eps);
+#pragma unroll
+  for (int j = 0; j < CPT; ++j) {
+    const int c = tid + kBlkThreads * j;
+    const float n = fmaf((xv[j] - mean) * rstd, w[j], bb[j]);
+    float acc = cb[j];
+    acc = fmaf(cw[j].x, s0[j], acc);
+    acc = fmaf(cw[j].y, s1[j], acc);
+    acc = fmaf(cw[j].z, s2[j], acc);
+    acc = fmaf(cw[j].w, n, acc);
+    st[c * 3] = s1[j];
+    st[c * 3 + 1] = s2[j];
+    st[c * 3 + 2] = n;
+    store_f32_as(out + (size_t)b * d + c, n + acc / (1.f + __expf(-acc)));
+  }
+}
+
 }  // namespace
 }  // namespace dp
 
@@ -357,9 +426,19 @@ extern "C" int dp_ln_conv_step(const void *x, int x_dtype, const float *ln_w, co
   DP_REQUIRE(x && ln_w && ln_b && conv_w && out && (k == 1 || conv_state), DP_ERR_INVALID_ARGUMENT,
              "dp_ln_conv_step: null pointer");
   cudaStream_t st = as_stream(stream);
+  const bool reg = k == 4 && d % kBlkThreads == 0 && d <= 4 * kBlkThreads &&
+                   (reinterpret_cast<uintptr_t>(conv_w) & 15) == 0;
   auto launch = [&](auto xt, auto ot) {
     using XT = decltype(xt);
     using OT = decltype(ot);
+    if (reg) {
+      auto kern = d == 256 ? ln_conv_step_reg_kernel<XT, OT, 1>
+                  : d == 512 ? ln_conv_step_reg_kernel<XT, OT, 2>
+                  : d == 768 ? ln_conv_step_reg_kernel<XT, OT, 3>
+                             : ln_conv_step_reg_kernel<XT, OT, 4>;
+      return launch_pdl(kern, dim3(B), dim3(kBlkThreads), 0, st, static_cast<const XT *>(x), ln_w, ln_b, eps,
+                        conv_w, conv_b, conv_state, static_cast<OT *>(out));
+    }
     return launch_pdl(ln_conv_step_kernel<XT, OT>, dim3(B), dim3(kBlkThreads), 0, st, static_cast<const XT *>(x),
                       ln_w, ln_b, eps, conv_w, conv_b, conv_state, static_cast<OT *>(out), d, k);
   };

@@ -173,6 +173,20 @@ decode_rows_kernel(const float *state_in, float *state_out, const void *tk,
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int npair = D >> 1, p = lane;
   const bool active = p < npair;
+  // the state rows and values first (the long loads), then phases and gate
+  const int64_t base = (int64_t)bh * Dv * 2 * D;
+  float4 m[RPW];
+  float vo[RPW];
+#pragma unroll
+  for (int r = 0; r < RPW; ++r) {
+    const int o = warp + 8 * r;
+    m[r] = make_float4(0.f, 0.f, 0.f, 0.f);
+    vo[r] = 0.f;
+    if (o < Dv) {
+      if (active) m[r] = reinterpret_cast<const float4 *>(state_in + base + (int64_t)o * 2 * D)[p];
+      vo[r] = load_any(v, in_dt, b * s_v.b + h * s_v.h + o);
+    }
+  }
   // this lane's two key / query channels (2p, 2p+1)
   float ck0 = 0.f, sk0 = 0.f, ck1 = 0.f, sk1 = 0.f, cq0 = 0.f, sq0 = 0.f, cq1 = 0.f, sq1 = 0.f;
   if (active) {
@@ -195,19 +209,6 @@ decode_rows_kernel(const float *state_in, float *state_out, const void *tk,
     wc1 = fmaf(br, ck1, -sp * sk1);
     ws1 = fmaf(br, sk1, sp * ck1);
     bt = 1.f;
-  }
-  const int64_t base = (int64_t)bh * Dv * 2 * D;
-  float4 m[RPW];
-  float vo[RPW];
-#pragma unroll
-  for (int r = 0; r < RPW; ++r) {
-    const int o = warp + 8 * r;
-    m[r] = make_float4(0.f, 0.f, 0.f, 0.f);
-    vo[r] = 0.f;
-    if (o < Dv) {
-      if (active) m[r] = reinterpret_cast<const float4 *>(state_in + base + (int64_t)o * 2 * D)[p];
-      vo[r] = load_any(v, in_dt, b * s_v.b + h * s_v.h + o);
-    }
   }
   float acc[RPW];
 #pragma unroll

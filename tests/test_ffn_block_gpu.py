@@ -237,12 +237,14 @@ def test_layernorm_kernel(x_dtype, y_dtype, resid):
 
 
 @pytest.mark.parametrize("out_dtype", [torch.float32, torch.bfloat16])
-def test_ln_conv_step_kernel(out_dtype):
+@pytest.mark.parametrize("d", [512, 1024, 320])
+def test_ln_conv_step_kernel(out_dtype, d):
     """dp_ln_conv_step over 6 tokens against LayerNorm + ShortCausalConv1D.step, the
-    (B, d, k-1) conv state carried through the kernel."""
+    (B, d, k-1) conv state carried through the kernel (d = 256 j on the register-resident
+    kernel, others on the general one)."""
     from delta_phase_b200 import _capi
     torch.manual_seed(4)
-    B, d = 5, 512
+    B = 5
     norm = torch.nn.LayerNorm(d).cuda()
     conv = dp.ShortCausalConv1D(d).cuda()
     with torch.no_grad():
