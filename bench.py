@@ -647,7 +647,9 @@ def run_lm(args, world, rank, local):
     # the whole step as one CUDA graph, state buffers updated in place
     from delta_phase_b200 import DecodeGraph
     graph = DecodeGraph(model, B, states=[(None, M) for M in states], autocast_dtype=torch.bfloat16)
+    torch.cuda.nvtx.range_push("lm_decode_graph")  # lets a profiler select the decode replays
     dec_ms = _timed(lambda: graph.step(nxt), ndec, 3, stream)
+    torch.cuda.nvtx.range_pop()
     del graph
     pre_ms = max_over_ranks(pre_ms, world)
     dec_ms = max_over_ranks(dec_ms, world)
