@@ -635,7 +635,9 @@ def run_lm(args, world, rank, local):
     ids = torch.randint(0, 32000, (B, L), device=dev)
     stream = torch.cuda.current_stream(dev)
     with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+        torch.cuda.nvtx.range_push("lm_prefill")  # lets a profiler select the prefill passes
         pre_ms = _timed(lambda: model(ids), max(1, args.steps // 4), 1, stream)
+        torch.cuda.nvtx.range_pop()
         _, states = model.forward_with_states(ids)
         st = [(None, M) for M in states]
         nxt = ids[:, -1:]

@@ -204,6 +204,80 @@ layernorm_reg_kernel(const InT *x, const float *res, const float *__restrict__ l
   }
 }
 
+// The same pass for the usual shapes (conv kernel size 4, d = 256 NG <= 1024, 16-byte
+// aligned rows), at HBM speed: a CTA takes 32 tokens of one sequence; first each warp
+// computes the LayerNorm statistics of rows t0 - 3 .. t0 + 31 from registers (one
+// 16-byte-wide read of the row), then thread t walks channels t + 256 j down the 35 rows,
+// normalising on the fly and keeping the three previous normalised values in registers
+// for the depthwise conv.  Shared memory holds only the 2 x 35 statistics (the kernel
+// above stages the normalised rows, 77 KB, and runs at a fraction of the bandwidth).
+constexpr int kConvRowsT = 32;
+
+template <typename InT, typename OutT, int NG>
+__global__ void __launch_bounds__(kBlkThreads)
+ln_conv_silu_rows_kernel(const InT *x, const float *__restrict__ ln_w, const float *__restrict__ ln_b, float eps,
+                         const float *__restrict__ conv_w, const float *__restrict__ conv_b,
+                         OutT *__restrict__ out, int L) {
+  constexpr int d = 256 * NG, K = 4, R = kConvRowsT + K - 1;
+  __shared__ float s_mean[R], s_rstd[R];
+  const int b = blockIdx.y, t0 = blockIdx.x * kConvRowsT;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int r = warp; r < R; r += kBlkThreads / 32) {
+    const int t = t0 - (K - 1) + r;
+    if (t < 0 || t >= L) {  // the conv's zero padding (t < 0); rows past L are not used
+      if (lane == 0) s_mean[r] = s_rstd[r] = 0.f;
+      continue;
+    }
+    const InT *xr = x + ((size_t)b * L + t) * d;
+    float v[NG][8];
+#pragma unroll
+    for (int g = 0; g < NG; ++g) load8(xr + 8 * (lane + 32 * g), v[g]);
+    float s = 0.f;
+#pragma unroll
+    for (int g = 0; g < NG; ++g)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) s += v[g][i];
+    const float mean = warp_sum(s) * (1.0f / d);
+    float q = 0.f;
+#pragma unroll
+    for (int g = 0; g < NG; ++g)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float dv = v[g][i] - mean;
+        q = fmaf(dv, dv, q);
+      }
+    const float rstd = rsqrtf(warp_sum(q) * (1.0f / d) + eps);
+    if (lane == 0) {
+      s_mean[r] = mean;
+      s_rstd[r] = rstd;
+    }
+  }
+  __syncthreads();
+#pragma unroll 1
+  for (int j = 0; j < NG; ++j) {
+    const int c = threadIdx.x + kBlkThreads * j;
+    const float4 w = reinterpret_cast<const float4 *>(conv_w)[c];  // taps of channel c
+    const float lw = ln_w[c], lb = ln_b[c], cb = conv_b ? conv_b[c] : 0.f;
+    float n0 = 0.f, n1 = 0.f, n2 = 0.f;  // normalised inputs of the three previous tokens
+#pragma unroll 5
+    for (int r = 0; r < R; ++r) {
+      const int t = t0 - (K - 1) + r;
+      float n = 0.f;
+      if (t >= 0 && t < L) n = fmaf((to_f32(x[((size_t)b * L + t) * d + c]) - s_mean[r]) * s_rstd[r], lw, lb);
+      if (r >= K - 1 && t < L) {
+        float acc = fmaf(w.x, n0, cb);
+        acc = fmaf(w.y, n1, acc);
+        acc = fmaf(w.z, n2, acc);
+        acc = fmaf(w.w, n, acc);
+        store_f32_as(out + ((size_t)b * L + t) * d + c, n + acc / (1.f + __expf(-acc)));
+      }
+      n0 = n1;
+      n1 = n2;
+      n2 = n;
+    }
+  }
+}
+
 // Decode step of norm1 + ShortCausalConv1D.step (layers.py:43-50,182-190): one CTA per
 // sequence.  n = LayerNorm(x_t); out = n + SiLU(b + sum_{j<k-1} w[j] state[j] + w[k-1] n);
 // state (d, k-1) float32 shifts left and takes n (the conv's last k-1 inputs).
@@ -343,6 +417,29 @@ extern "C" int dp_ln_conv_silu(const void *x, int x_dtype, const float *ln_w, co
              DP_ERR_INVALID_ARGUMENT, "dp_ln_conv_silu: dtypes must be float32 or bfloat16");
   if (B == 0 || L == 0) return DP_OK;
   DP_REQUIRE(x && ln_w && ln_b && conv_w && out, DP_ERR_INVALID_ARGUMENT, "dp_ln_conv_silu: null pointer");
+  cudaStream_t st0 = as_stream(stream);
+  if (k == 4 && d % kBlkThreads == 0 && d <= 4 * kBlkThreads && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
+      (reinterpret_cast<uintptr_t>(conv_w) & 15) == 0 && (L + kConvRowsT - 1) / kConvRowsT < (1 << 30)) {
+    const dim3 grid((L + kConvRowsT - 1) / kConvRowsT, B);
+    auto launch = [&](auto xt, auto ot) {
+      using XT = decltype(xt);
+      using OT = decltype(ot);
+      auto kern = d == 256 ? ln_conv_silu_rows_kernel<XT, OT, 1>
+                  : d == 512 ? ln_conv_silu_rows_kernel<XT, OT, 2>
+                  : d == 768 ? ln_conv_silu_rows_kernel<XT, OT, 3>
+                             : ln_conv_silu_rows_kernel<XT, OT, 4>;
+      kern<<<grid, kBlkThreads, 0, st0>>>(static_cast<const XT *>(x), ln_w, ln_b, eps, conv_w, conv_b,
+                                           static_cast<OT *>(out), L);
+    };
+    if (x_dtype == DP_F32) {
+      if (out_dtype == DP_F32) launch(float{}, float{});
+      else launch(float{}, __nv_bfloat16{});
+    } else {
+      if (out_dtype == DP_F32) launch(__nv_bfloat16{}, float{});
+      else launch(__nv_bfloat16{}, __nv_bfloat16{});
+    }
+    return check_launch("ln_conv_silu_rows_kernel");
+  }
   int T = 16;
   while (T > 1 && (size_t)(T + k - 1) * d * sizeof(float) > 200 * 1024) T >>= 1;
   const size_t smem = (size_t)(T + k - 1) * d * sizeof(float);

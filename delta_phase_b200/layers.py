@@ -270,12 +270,18 @@ class _DeltaRuleBlock(nn.Module):
         return x + self.ffn(self.norm2(x)), M_state
 
     def forward(self, x: torch.Tensor, memory_state=None):
+        """Block forward (layers.py:177-244); see ``_forward``."""
+        return self._forward(x, memory_state)
+
+    def _forward(self, x: torch.Tensor, memory_state=None, keep_fp32: bool = False):
         """Block forward (layers.py:177-244) on fused kernels: LayerNorm + causal conv +
         SiLU + residual in one pass, the four input projections as one GEMM, the
         delta-rule core, LayerNorm -> output projection, and the residual add fused into
         norm2.  GEMM operands are bf16 under bf16 autocast (like the reference's autocast
         matmuls) and float32 otherwise; the residual stream stays float32.  When autograd
-        records (training), the differentiable path above runs instead."""
+        records (training), the differentiable path above runs instead.  ``keep_fp32``
+        returns the float32 residual stream instead of casting it back to x's dtype (the
+        model's layer loop passes it between blocks that way)."""
         if x.dtype == torch.float64:
             raise TypeError("float64 inputs are not supported by the CUDA path")
         _capi.require_cuda(x)
@@ -318,7 +324,7 @@ class _DeltaRuleBlock(nn.Module):
         _capi.layernorm(o.contiguous(), self.norm2.weight.float(), self.norm2.bias.float(), self.norm2.eps, n2,
                         residual=res32, sum_out=s_sum)
         out = self.ffn.add_to(s_sum, n2).view(B, L, D)
-        return out.to(x.dtype) if x.dtype != torch.float32 else out, M_state
+        return (out if (keep_fp32 or x.dtype == torch.float32) else out.to(x.dtype)), M_state
 
     def _out_proj_weights(self, dtype):
         """out_proj weight and bias in ``dtype``, rebuilt when either changes."""

@@ -148,7 +148,8 @@ class DeltaPhaseModel(nn.Module):
         if states is None:
             states = [None] * len(self.blocks)
         for i, block in enumerate(self.blocks):
-            h, _ = block(h, states[i])
+            # the residual stream stays float32 between blocks (no bf16 round trip per layer)
+            h, _ = block._forward(h, states[i], keep_fp32=True)
         return self._head(h)
 
     def forward_with_states(self, input_ids: torch.Tensor, states=None):
@@ -158,7 +159,7 @@ class DeltaPhaseModel(nn.Module):
             states = [None] * len(self.blocks)
         out_states = []
         for i, block in enumerate(self.blocks):
-            h, M = block(h, states[i])
+            h, M = block._forward(h, states[i], keep_fp32=True)
             out_states.append(M)
         return self._head(h), out_states
 

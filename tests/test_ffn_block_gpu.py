@@ -192,10 +192,12 @@ def test_ffn_follows_bf16_autocast():
     assert rel_l2(y.float(), ref) < TOL_BF16
 
 
-@pytest.mark.parametrize("L,d,out_dtype", [(37, 256, torch.float32), (70, 1024, torch.bfloat16), (5, 64, torch.float32)])
+@pytest.mark.parametrize("L,d,out_dtype", [(37, 256, torch.float32), (70, 1024, torch.bfloat16), (5, 64, torch.float32),
+                                           (100, 512, torch.float32), (2, 768, torch.bfloat16), (33, 320, torch.float32)])
 def test_ln_conv_silu_kernel(L, d, out_dtype):
     """dp_ln_conv_silu against torch's LayerNorm -> causal depthwise conv -> SiLU ->
-    residual (tile edges, the first k-1 tokens' zero padding, several sequences)."""
+    residual (tile edges, the first k-1 tokens' zero padding, several sequences; d = 256 j
+    on the statistics-then-channels kernel, other widths on the staged one)."""
     from delta_phase_b200 import _capi
     torch.manual_seed(L)
     B = 3
