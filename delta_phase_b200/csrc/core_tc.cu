@@ -28,6 +28,10 @@
 // buffer is a K-major or MN-major operand by swapping the two descriptor strides: K is
 // read as A and B of G1, A of G3 and A^T of G4 without copies.  M=64 accumulators put
 // row m in TMEM lane (m % 16) + 32 (m / 16).  Every wait is bounded.
+#include <cuda.h>  // CUtensorMap and cuTensorMapEncodeTiled's types (called through the runtime)
+
+#include <cstring>
+
 #include "dp_common.cuh"
 #include "tc_ptx.cuh"
 
@@ -196,12 +200,30 @@ struct TcArgs {
   int H, L;
   SeqStrides s_tk, s_tq, s_v, s_b, s_out;
   int *err;
+  int use_tmap;  // inputs are strided views: load chunks through the tensor maps below
 };
 
-// Bulk copies of chunk rows [c0, c0 + n) of one (b, h) into the stage (one full warp;
-// lane 0 registers the expected bytes first).
-__device__ __forceinline__ void issue_chunk_loads(const TcArgs &a, int b, int h, int c0, int n,
+// Tensor maps of theta_k, theta_q, v as 4-d tensors (channel, head, token, batch) with a
+// (64, 1, 64, 1) box: one chunk of one (b, h) per copy.
+struct alignas(64) TcMaps {
+  CUtensorMap m[3];
+};
+
+// Copies of chunk rows [c0, c0 + n) of one (b, h) into the stage (one full warp; lane 0
+// registers the expected bytes first).  Strided inputs (the (B, L, H, d_k) projection
+// views of a block) go through the tensor maps, one tiled copy per tensor (rows past L
+// arrive as zeros and are not used); otherwise contiguous rows are one bulk copy per
+// tensor and other layouts one bulk copy per row.
+__device__ __forceinline__ void issue_chunk_loads(const TcArgs &a, const TcMaps &maps, int b, int h, int c0, int n,
                                                   uint8_t *stage, uint64_t *bar, int lane) {
+  if (a.use_tmap) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(bar, (uint32_t)(3 * kC * 128));
+#pragma unroll
+      for (int x = 0; x < 3; ++x) tma_load_4d(stage + x * kC * 128, &maps.m[x], 0, h, c0, b, bar);
+    }
+    return;
+  }
   if (lane == 0) mbar_arrive_expect_tx(bar, (uint32_t)(3 * n * 128));
   __syncwarp();
   const __nv_bfloat16 *src[3] = {a.tk + b * a.s_tk.b + h * a.s_tk.h + (int64_t)c0 * a.s_tk.t,
@@ -228,7 +250,7 @@ struct Bars {
 // CB: complex beta (beta = 1 + e^{i phi}, a.beta holds phi): G1 = [K; Q] W^T with the
 // write key W = beta K, A[i][k] = K_i . W_k / 64 (not symmetric; no beta factor left).
 template <bool CB>
-__device__ bool prep_role(const TcArgs &a, uint8_t *smem, Bars *bars, uint32_t tmem, int b, int h,
+__device__ bool prep_role(const TcArgs &a, const TcMaps &maps, uint8_t *smem, Bars *bars, uint32_t tmem, int b, int h,
                           int nchunks) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int q = warp & 3, hf = warp >> 2;  // TMEM lane quarter, column half
@@ -245,7 +267,7 @@ __device__ bool prep_role(const TcArgs &a, uint8_t *smem, Bars *bars, uint32_t t
   uint32_t pm_phase = 0;
   bool mma_pending = false, ok = true;
   if (nchunks > 0) {
-    if (warp == 0) issue_chunk_loads(a, b, h, 0, min(kC, L), stage, &bars->load, lane);
+    if (warp == 0) issue_chunk_loads(a, maps, b, h, 0, min(kC, L), stage, &bars->load, lane);
     issued = 1;
   }
   if (tid < kC)
@@ -334,7 +356,7 @@ __device__ bool prep_role(const TcArgs &a, uint8_t *smem, Bars *bars, uint32_t t
 
     // ---- P2: the stage is free -> next chunk's loads; G1 = [K; Q] K^T  (M=128, N=64)
     if (c + 1 < nchunks) {
-      if (warp == 0) issue_chunk_loads(a, b, h, t0 + kC, min(kC, L - t0 - kC), stage, &bars->load, lane);
+      if (warp == 0) issue_chunk_loads(a, maps, b, h, t0 + kC, min(kC, L - t0 - kC), stage, &bars->load, lane);
       issued = c + 2;
     }
     if (tid == 0) {
@@ -715,7 +737,8 @@ __device__ bool chain_role(const TcArgs &a, uint8_t *smem, Bars *bars, uint32_t 
 }
 
 template <bool CB>
-__global__ void __launch_bounds__(kThreads, 1) core_tc_kernel(TcArgs a) {
+__global__ void __launch_bounds__(kThreads, 1) core_tc_kernel(const __grid_constant__ TcArgs a,
+                                                               const __grid_constant__ TcMaps maps) {
   extern __shared__ __align__(1024) uint8_t smem[];
   Bars *bars = reinterpret_cast<Bars *>(smem + OFF_BAR);
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 1);
@@ -749,7 +772,7 @@ __global__ void __launch_bounds__(kThreads, 1) core_tc_kernel(TcArgs a) {
 
   bool ok;
   if (tid < kPrepThreads)
-    ok = prep_role<CB>(a, smem, bars, tmem, b, h, nchunks);
+    ok = prep_role<CB>(a, maps, smem, bars, tmem, b, h, nchunks);
   else
     ok = chain_role<CB>(a, smem, bars, tmem, bh, b, h, nchunks);
   if (!ok) atomicExch(fail_flag, 1);
@@ -771,6 +794,44 @@ bool core_tc_supported(const void *tk, const void *tq, const void *v, int in_dt,
   for (int i = 0; i < 3; ++i)
     if ((s[i].b % 8) || (s[i].h % 8) || (s[i].t % 8)) return false;
   if ((s[4].b % 4) || (s[4].h % 4) || (s[4].t % 4)) return false;
+  return true;
+}
+
+// cuTensorMapEncodeTiled, fetched through the runtime (no link against the driver library).
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_tiled_fn() {
+  static EncodeTiledFn fn = [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return static_cast<EncodeTiledFn>(nullptr);
+    return reinterpret_cast<EncodeTiledFn>(p);
+  }();
+  return fn;
+}
+
+// Tensor maps of the three bf16 inputs as (channel 64, head H, token L, batch B) with
+// element strides s[i].h, s[i].t, s[i].b (multiples of 8, checked by tc_supported) and a
+// (64, 1, 64, 1) box.  Returns false (bulk copies are used) if the driver rejects a map.
+bool encode_input_maps(TcMaps &maps, const void *tk, const void *tq, const void *v, int B, int H, int L,
+                       const SeqStrides *s) {
+  EncodeTiledFn enc = encode_tiled_fn();
+  if (!enc) return false;
+  const void *base[3] = {tk, tq, v};
+  for (int x = 0; x < 3; ++x) {
+    const cuuint64_t dims[4] = {64, (cuuint64_t)H, (cuuint64_t)L, (cuuint64_t)B};
+    const cuuint64_t strides[3] = {(cuuint64_t)s[x].h * 2, (cuuint64_t)s[x].t * 2, (cuuint64_t)s[x].b * 2};
+    const cuuint32_t box[4] = {64, 1, (cuuint32_t)kC, 1};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    const CUresult r = enc(&maps.m[x], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void *>(base[x]), dims,
+                           strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return false;
+  }
   return true;
 }
 
@@ -796,10 +857,14 @@ int core_fwd_tc(const void *tk, const void *tq, const void *v, const void *beta,
   a.s_out = s[4];
   a.err = device_error_ptr();
   if (!a.err) return set_error(DP_ERR_CUDA, "core_fwd_tc: device error word unavailable");
+  TcMaps maps;
+  memset(&maps, 0, sizeof(maps));
+  a.use_tmap = (s[0].t != 64 && s[1].t != 64 && s[2].t != 64 && L >= kC) &&
+               encode_input_maps(maps, tk, tq, v, B, H, L, s);
   auto kern = cbeta ? core_tc_kernel<true> : core_tc_kernel<false>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
   if (e != cudaSuccess) return set_error(DP_ERR_CUDA, std::string("core_tc smem attr: ") + cudaGetErrorString(e));
-  kern<<<B * H, kThreads, SMEM_BYTES, stream>>>(a);
+  kern<<<B * H, kThreads, SMEM_BYTES, stream>>>(a, maps);
   return check_launch("core_tc_kernel");
 }
 

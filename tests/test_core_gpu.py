@@ -104,6 +104,26 @@ def test_strided_block_layout():
     assert rel_l2(buf.view(B, L, H, D).transpose(1, 2), ref) < TOL_F32
 
 
+@pytest.mark.parametrize("L", [64, 200, 256])
+def test_strided_projection_views_tensor_core(L):
+    """bf16 d_k = 64 inputs as column slices of one (B, L, 3 H 64 + H) projection (the
+    block's layout): the tensor-core kernel loads them through TMA tensor maps; the result
+    equals the same inputs made contiguous (identical arithmetic) and the oracle."""
+    B, H, D = 2, 8, 64  # row width 3 H 64 + H = 1544: token stride a multiple of 8 (tensor-core path)
+    rng = np.random.default_rng(L)
+    proj = np.concatenate([rng.uniform(0, 6.28, (B, L, 2 * H * D)), rng.standard_normal((B, L, H * D)),
+                           rng.standard_normal((B, L, H))], -1)
+    proj = round_bf16(proj.astype(np.float32))
+    pd = to_dev(proj, torch.bfloat16)
+    views = [pd[..., i * H * D:(i + 1) * H * D].view(B, L, H, D).transpose(1, 2) for i in range(3)]
+    beta = to_dev(rng.uniform(0, 2, (B, H, L)).astype(np.float32))
+    out_s, M_s = chunkwise_forward(*views, beta, 64)
+    out_c, M_c = chunkwise_forward(*[t.contiguous() for t in views], beta, 64)
+    assert torch.equal(out_s, out_c) and torch.equal(M_s, M_c)
+    ref, _ = ocore.recurrent_delta(*[t.float().cpu().numpy() for t in views], beta.cpu().numpy())
+    assert rel_l2(out_s, ref) < TOL_BF16
+
+
 def test_dispatcher_contract():
     tk, tq, v, beta = core_inputs(1, 1, 2, 30, 8)
     with pytest.raises(RuntimeError):  # L not a multiple of chunk_size, as in the reference
