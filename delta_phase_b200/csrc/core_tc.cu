@@ -200,27 +200,37 @@ struct TcArgs {
   int H, L;
   SeqStrides s_tk, s_tq, s_v, s_b, s_out;
   int *err;
-  int use_tmap;  // inputs are strided views: load chunks through the tensor maps below
+  int use_tmap;  // load chunks through the tensor maps below
+  // per input: the tensor-map dimension (1..3) of token, head and batch
+  int8_t dim_t[3], dim_h[3], dim_b[3];
 };
 
-// Tensor maps of theta_k, theta_q, v as 4-d tensors (channel, head, token, batch) with a
-// (64, 1, 64, 1) box: one chunk of one (b, h) per copy.
+// Tensor maps of theta_k, theta_q, v as 4-d tensors: the channel innermost, then token,
+// head and batch in the order of their strides, with a box of 64 channels x 64 tokens:
+// one chunk of one (b, h) per copy.
 struct alignas(64) TcMaps {
   CUtensorMap m[3];
 };
 
 // Copies of chunk rows [c0, c0 + n) of one (b, h) into the stage (one full warp; lane 0
-// registers the expected bytes first).  Strided inputs (the (B, L, H, d_k) projection
-// views of a block) go through the tensor maps, one tiled copy per tensor (rows past L
-// arrive as zeros and are not used); otherwise contiguous rows are one bulk copy per
-// tensor and other layouts one bulk copy per row.
+// registers the expected bytes first).  With tensor maps (L >= 64): one tiled copy per
+// tensor (rows past L arrive as zeros and are not used) -- measured faster than both
+// alternatives, for contiguous inputs and for the (B, L, H, d_k) projection views of a
+// block; otherwise contiguous rows are one bulk copy per tensor, other layouts one bulk
+// copy per row.
 __device__ __forceinline__ void issue_chunk_loads(const TcArgs &a, const TcMaps &maps, int b, int h, int c0, int n,
                                                   uint8_t *stage, uint64_t *bar, int lane) {
   if (a.use_tmap) {
     if (lane == 0) {
       mbar_arrive_expect_tx(bar, (uint32_t)(3 * kC * 128));
 #pragma unroll
-      for (int x = 0; x < 3; ++x) tma_load_4d(stage + x * kC * 128, &maps.m[x], 0, h, c0, b, bar);
+      for (int x = 0; x < 3; ++x) {
+        const int dt = a.dim_t[x], dh = a.dim_h[x];  // the batch takes the remaining dimension
+        const int c1 = dt == 1 ? c0 : dh == 1 ? h : b;
+        const int c2 = dt == 2 ? c0 : dh == 2 ? h : b;
+        const int c3 = dt == 3 ? c0 : dh == 3 ? h : b;
+        tma_load_4d(stage + x * kC * 128, &maps.m[x], 0, c1, c2, c3, bar);
+      }
     }
     return;
   }
@@ -814,18 +824,42 @@ EncodeTiledFn encode_tiled_fn() {
   return fn;
 }
 
-// Tensor maps of the three bf16 inputs as (channel 64, head H, token L, batch B) with
-// element strides s[i].h, s[i].t, s[i].b (multiples of 8, checked by tc_supported) and a
-// (64, 1, 64, 1) box.  Returns false (bulk copies are used) if the driver rejects a map.
-bool encode_input_maps(TcMaps &maps, const void *tk, const void *tq, const void *v, int B, int H, int L,
+// Tensor maps of the three bf16 inputs: channel (64) innermost, then token (L), head (H)
+// and batch (B) sorted by element stride (s[i].t, .h, .b: multiples of 8, checked by
+// tc_supported), a box of 64 channels x 64 tokens.  Records each input's dimension order
+// in `a`.  Returns false (bulk copies are used) if the driver rejects a map.
+bool encode_input_maps(TcMaps &maps, TcArgs &a, const void *tk, const void *tq, const void *v, int B, int H, int L,
                        const SeqStrides *s) {
   EncodeTiledFn enc = encode_tiled_fn();
   if (!enc) return false;
   const void *base[3] = {tk, tq, v};
   for (int x = 0; x < 3; ++x) {
-    const cuuint64_t dims[4] = {64, (cuuint64_t)H, (cuuint64_t)L, (cuuint64_t)B};
-    const cuuint64_t strides[3] = {(cuuint64_t)s[x].h * 2, (cuuint64_t)s[x].t * 2, (cuuint64_t)s[x].b * 2};
-    const cuuint32_t box[4] = {64, 1, (cuuint32_t)kC, 1};
+    // (stride, extent, which) of token (0), head (1), batch (2), sorted by stride
+    int64_t st[3] = {s[x].t, s[x].h, s[x].b};
+    int64_t ext[3] = {L, H, B};
+    int ord[3] = {0, 1, 2};
+    for (int i = 0; i < 3; ++i)
+      for (int j = i + 1; j < 3; ++j)
+        if (st[ord[j]] < st[ord[i]]) {
+          const int tmp = ord[i];
+          ord[i] = ord[j];
+          ord[j] = tmp;
+        }
+    cuuint64_t dims[4] = {64, 0, 0, 0};
+    cuuint64_t strides[3];
+    cuuint32_t box[4] = {64, 1, 1, 1};
+    for (int i = 0; i < 3; ++i) {
+      dims[i + 1] = (cuuint64_t)ext[ord[i]];
+      strides[i] = (cuuint64_t)st[ord[i]] * 2;
+      if (ord[i] == 0) {
+        box[i + 1] = (cuuint32_t)kC;
+        a.dim_t[x] = (int8_t)(i + 1);
+      } else if (ord[i] == 1) {
+        a.dim_h[x] = (int8_t)(i + 1);
+      } else {
+        a.dim_b[x] = (int8_t)(i + 1);
+      }
+    }
     const cuuint32_t estr[4] = {1, 1, 1, 1};
     const CUresult r = enc(&maps.m[x], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void *>(base[x]), dims,
                            strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
@@ -859,8 +893,7 @@ int core_fwd_tc(const void *tk, const void *tq, const void *v, const void *beta,
   if (!a.err) return set_error(DP_ERR_CUDA, "core_fwd_tc: device error word unavailable");
   TcMaps maps;
   memset(&maps, 0, sizeof(maps));
-  a.use_tmap = (s[0].t != 64 && s[1].t != 64 && s[2].t != 64 && L >= kC) &&
-               encode_input_maps(maps, tk, tq, v, B, H, L, s);
+  a.use_tmap = L >= kC && encode_input_maps(maps, a, tk, tq, v, B, H, L, s);
   auto kern = cbeta ? core_tc_kernel<true> : core_tc_kernel<false>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
   if (e != cudaSuccess) return set_error(DP_ERR_CUDA, std::string("core_tc smem attr: ") + cudaGetErrorString(e));
