@@ -28,12 +28,11 @@
 // buffer is a K-major or MN-major operand by swapping the two descriptor strides: K is
 // read as A and B of G1, A of G3 and A^T of G4 without copies.  M=64 accumulators put
 // row m in TMEM lane (m % 16) + 32 (m / 16).  Every wait is bounded.
-#include <cuda.h>  // CUtensorMap and cuTensorMapEncodeTiled's types (called through the runtime)
-
 #include <cstring>
 
 #include "dp_common.cuh"
 #include "tc_ptx.cuh"
+#include "tmap.cuh"
 
 namespace dp {
 
@@ -200,14 +199,11 @@ struct TcArgs {
   int H, L;
   SeqStrides s_tk, s_tq, s_v, s_b, s_out;
   int *err;
-  int use_tmap;  // load chunks through the tensor maps below
-  // per input: the tensor-map dimension (1..3) of token, head and batch
-  int8_t dim_t[3], dim_h[3], dim_b[3];
+  int use_tmap;            // load chunks through the tensor maps below
+  ChunkMapDims mdims[3];   // per input: the map dimension of token, head and batch
 };
 
-// Tensor maps of theta_k, theta_q, v as 4-d tensors: the channel innermost, then token,
-// head and batch in the order of their strides, with a box of 64 channels x 64 tokens:
-// one chunk of one (b, h) per copy.
+// Tensor maps of theta_k, theta_q, v (tmap.cuh): one chunk of one (b, h) per copy.
 struct alignas(64) TcMaps {
   CUtensorMap m[3];
 };
@@ -224,13 +220,7 @@ __device__ __forceinline__ void issue_chunk_loads(const TcArgs &a, const TcMaps 
     if (lane == 0) {
       mbar_arrive_expect_tx(bar, (uint32_t)(3 * kC * 128));
 #pragma unroll
-      for (int x = 0; x < 3; ++x) {
-        const int dt = a.dim_t[x], dh = a.dim_h[x];  // the batch takes the remaining dimension
-        const int c1 = dt == 1 ? c0 : dh == 1 ? h : b;
-        const int c2 = dt == 2 ? c0 : dh == 2 ? h : b;
-        const int c3 = dt == 3 ? c0 : dh == 3 ? h : b;
-        tma_load_4d(stage + x * kC * 128, &maps.m[x], 0, c1, c2, c3, bar);
-      }
+      for (int x = 0; x < 3; ++x) tma_load_chunk(stage + x * kC * 128, &maps.m[x], a.mdims[x], c0, h, b, bar);
     }
     return;
   }
@@ -807,68 +797,6 @@ bool core_tc_supported(const void *tk, const void *tq, const void *v, int in_dt,
   return true;
 }
 
-// cuTensorMapEncodeTiled, fetched through the runtime (no link against the driver library).
-using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
-                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
-                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_tiled_fn() {
-  static EncodeTiledFn fn = [] {
-    void *p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
-        q != cudaDriverEntryPointSuccess)
-      return static_cast<EncodeTiledFn>(nullptr);
-    return reinterpret_cast<EncodeTiledFn>(p);
-  }();
-  return fn;
-}
-
-// Tensor maps of the three bf16 inputs: channel (64) innermost, then token (L), head (H)
-// and batch (B) sorted by element stride (s[i].t, .h, .b: multiples of 8, checked by
-// tc_supported), a box of 64 channels x 64 tokens.  Records each input's dimension order
-// in `a`.  Returns false (bulk copies are used) if the driver rejects a map.
-bool encode_input_maps(TcMaps &maps, TcArgs &a, const void *tk, const void *tq, const void *v, int B, int H, int L,
-                       const SeqStrides *s) {
-  EncodeTiledFn enc = encode_tiled_fn();
-  if (!enc) return false;
-  const void *base[3] = {tk, tq, v};
-  for (int x = 0; x < 3; ++x) {
-    // (stride, extent, which) of token (0), head (1), batch (2), sorted by stride
-    int64_t st[3] = {s[x].t, s[x].h, s[x].b};
-    int64_t ext[3] = {L, H, B};
-    int ord[3] = {0, 1, 2};
-    for (int i = 0; i < 3; ++i)
-      for (int j = i + 1; j < 3; ++j)
-        if (st[ord[j]] < st[ord[i]]) {
-          const int tmp = ord[i];
-          ord[i] = ord[j];
-          ord[j] = tmp;
-        }
-    cuuint64_t dims[4] = {64, 0, 0, 0};
-    cuuint64_t strides[3];
-    cuuint32_t box[4] = {64, 1, 1, 1};
-    for (int i = 0; i < 3; ++i) {
-      dims[i + 1] = (cuuint64_t)ext[ord[i]];
-      strides[i] = (cuuint64_t)st[ord[i]] * 2;
-      if (ord[i] == 0) {
-        box[i + 1] = (cuuint32_t)kC;
-        a.dim_t[x] = (int8_t)(i + 1);
-      } else if (ord[i] == 1) {
-        a.dim_h[x] = (int8_t)(i + 1);
-      } else {
-        a.dim_b[x] = (int8_t)(i + 1);
-      }
-    }
-    const cuuint32_t estr[4] = {1, 1, 1, 1};
-    const CUresult r = enc(&maps.m[x], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void *>(base[x]), dims,
-                           strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                           CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) return false;
-  }
-  return true;
-}
-
 // cbeta: `beta` holds phi of the complex beta 1 + e^{i phi} (ComplexBetaDeltaPhaseBlock).
 int core_fwd_tc(const void *tk, const void *tq, const void *v, const void *beta, int beta_dt,
                 const float *state_in, float *out, float *state_out, int B, int H, int L,
@@ -893,7 +821,10 @@ int core_fwd_tc(const void *tk, const void *tq, const void *v, const void *beta,
   if (!a.err) return set_error(DP_ERR_CUDA, "core_fwd_tc: device error word unavailable");
   TcMaps maps;
   memset(&maps, 0, sizeof(maps));
-  a.use_tmap = L >= kC && encode_input_maps(maps, a, tk, tq, v, B, H, L, s);
+  const void *base[3] = {tk, tq, v};
+  a.use_tmap = L >= kC;
+  for (int x = 0; x < 3 && a.use_tmap; ++x)
+    a.use_tmap = encode_chunk_map(&maps.m[x], &a.mdims[x], base[x], B, H, L, s[x]);
   auto kern = cbeta ? core_tc_kernel<true> : core_tc_kernel<false>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
   if (e != cudaSuccess) return set_error(DP_ERR_CUDA, std::string("core_tc smem attr: ") + cudaGetErrorString(e));

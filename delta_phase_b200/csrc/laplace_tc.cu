@@ -34,8 +34,11 @@
 // Every wait is bounded.
 #include <type_traits>
 
+#include <cstring>
+
 #include "dp_common.cuh"
 #include "tc_ptx.cuh"
+#include "tmap.cuh"
 
 namespace dp {
 
@@ -121,12 +124,32 @@ struct LapTcArgs {
   int H, L;
   SeqStrides s_tk, s_mk, s_tq, s_mq, s_v, s_lr, s_b, s_out;
   int *err;
+  int use_tmap;           // load the stage through the tensor maps below
+  ChunkMapDims mdims[4];  // theta_k, theta_q, logmag_k, logmag_q
 };
 
-// Bulk copies of the phase / log-magnitude rows [c0, c0 + n) into a stage (one warp).
-__device__ __forceinline__ void lap_issue_loads(const LapTcArgs &a, int b, int h, int c0, int n, uint8_t *stage,
-                                                uint64_t *bar, int lane) {
+// Tensor maps of theta_k, theta_q, logmag_k, logmag_q (tmap.cuh; absent log-magnitudes
+// have none): one chunk of one (b, h) per copy.
+struct alignas(64) LapMaps {
+  CUtensorMap m[4];
+};
+
+// Copies of the phase / log-magnitude rows [c0, c0 + n) into a stage (one warp): one
+// tiled TMA copy per tensor through the maps (L >= 64; rows past L arrive as zeros and
+// are not used), else bulk copies (one per tensor for contiguous rows, one per row).
+__device__ __forceinline__ void lap_issue_loads(const LapTcArgs &a, const LapMaps &maps, int b, int h, int c0, int n,
+                                                uint8_t *stage, uint64_t *bar, int lane) {
   const bool has_mk = a.mk != nullptr, has_mq = a.mq != nullptr;
+  if (a.use_tmap) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(bar, (uint32_t)kC * 128u * (2 + has_mk + has_mq));
+      tma_load_chunk(stage + ST_TK, &maps.m[0], a.mdims[0], c0, h, b, bar);
+      tma_load_chunk(stage + ST_TQ, &maps.m[1], a.mdims[1], c0, h, b, bar);
+      if (has_mk) tma_load_chunk(stage + ST_MK, &maps.m[2], a.mdims[2], c0, h, b, bar);
+      if (has_mq) tma_load_chunk(stage + ST_MQ, &maps.m[3], a.mdims[3], c0, h, b, bar);
+    }
+    return;
+  }
   const uint32_t bytes = (uint32_t)n * 128u * (2 + has_mk + has_mq);
   if (lane == 0) mbar_arrive_expect_tx(bar, bytes);
   __syncwarp();
@@ -306,7 +329,8 @@ __device__ __noinline__ void solve_block(int o, int BLK, const float *gm, const 
   for (int s = 0; s < 16; ++s) fv[(m0 + s) * LDF + o] = f[s];
 }
 
-__global__ void __launch_bounds__(kThreads, 1) laplace_tc_kernel(LapTcArgs a) {
+__global__ void __launch_bounds__(kThreads, 1) laplace_tc_kernel(const __grid_constant__ LapTcArgs a,
+                                                                  const __grid_constant__ LapMaps maps) {
   extern __shared__ __align__(1024) uint8_t smem[];
   uint8_t *stage = smem + OFF_STAGE;
   uint8_t *s0 = smem + OFF_S0;
@@ -370,13 +394,13 @@ __global__ void __launch_bounds__(kThreads, 1) laplace_tc_kernel(LapTcArgs a) {
     if (bar_id == 0) __syncthreads();
     else group_sync(bar_id, 32 * nw);
     if (cn + 1 < nchunks && warp == wfirst) {
-      lap_issue_loads(a, b, h, (cn + 1) * kC, min(kC, L - (cn + 1) * kC), stage, load_bar, lane);
+      lap_issue_loads(a, maps, b, h, (cn + 1) * kC, min(kC, L - (cn + 1) * kC), stage, load_bar, lane);
       if (lane == 0) *last_issued = cn + 1;
     }
     return true;
   };
   if (warp == 0 && nchunks > 0) {
-    lap_issue_loads(a, b, h, 0, min(kC, L), stage, load_bar, lane);
+    lap_issue_loads(a, maps, b, h, 0, min(kC, L), stage, load_bar, lane);
     if (lane == 0) *last_issued = 0;
   }
   uint4 pv, pl;
@@ -814,7 +838,20 @@ int laplace_fwd_tc(const void *const *ptrs, const void *beta, int beta_dt, const
   if (!a.err) return set_error(DP_ERR_CUDA, "laplace_fwd_tc: device error word unavailable");
   cudaError_t e = cudaFuncSetAttribute(laplace_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
   if (e != cudaSuccess) return set_error(DP_ERR_CUDA, std::string("laplace_tc smem attr: ") + cudaGetErrorString(e));
-  laplace_tc_kernel<<<2 * B * H, kThreads, SMEM_BYTES, stream>>>(a);
+  LapMaps maps;
+  memset(&maps, 0, sizeof(maps));
+  {
+    const void *base[4] = {a.tk, a.tq, a.mk, a.mq};
+    const SeqStrides *st[4] = {&a.s_tk, &a.s_tq, &a.s_mk, &a.s_mq};
+    auto al16 = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+    a.use_tmap = L >= kC;
+    for (int x = 0; x < 4 && a.use_tmap; ++x) {
+      if (!base[x]) continue;
+      a.use_tmap = al16(base[x]) && st[x]->t % 8 == 0 && st[x]->h % 8 == 0 && st[x]->b % 8 == 0 &&
+                   encode_chunk_map(&maps.m[x], &a.mdims[x], base[x], B, H, L, *st[x]);
+    }
+  }
+  laplace_tc_kernel<<<2 * B * H, kThreads, SMEM_BYTES, stream>>>(a, maps);
   return check_launch("laplace_tc_kernel");
 }
 

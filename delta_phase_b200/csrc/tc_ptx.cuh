@@ -68,19 +68,6 @@ __device__ __forceinline__ void bulk_g2s(void *dst_smem, const void *src_gmem, u
       : "memory");
 }
 
-// Tiled TMA load of a 4-d box (no multicast): coordinates innermost first; the box lands
-// in shared memory row-major, completion counted in bytes on `bar`.  The tensor map lives
-// in kernel-parameter space (__grid_constant__).  c0 (the innermost coordinate) is 0 at
-// every call site, so the innermost offset is 16-byte aligned.
-__device__ __forceinline__ void tma_load_4d(void *dst_smem, const void *tmap, int c0, int c1, int c2, int c3,
-                                            uint64_t *bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, "
-      "%5}], [%6];" ::"r"(smem_u32(dst_smem)),
-      "l"(tmap), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
-      : "memory");
-}
-
 // Generic-proxy shared-memory writes -> visible to the async proxy (tcgen05.mma operands).
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");

@@ -1,0 +1,92 @@
+// TMA tensor maps for the chunk inputs of the tensor-core kernels (core_tc.cu,
+// laplace_tc.cu): a bf16 input of d_k = 64 channels viewed as (B, H, L, 64) with element
+// strides (s.b, s.h, s.t) becomes a 4-d map with the channel innermost, then token, head
+// and batch in the order of their strides, and a box of 64 channels x 64 tokens, so one
+// tiled copy (`cp.async.bulk.tensor.4d`, no multicast) fetches one chunk of one (b, h).
+// Tokens past L arrive as zeros.
+#pragma once
+
+#include <cuda.h>  // CUtensorMap and cuTensorMapEncodeTiled's types (called through the runtime)
+
+#include "dp_common.cuh"
+
+namespace dp {
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link against the
+// driver library); null if unavailable.
+inline EncodeTiledFn encode_tiled_fn() {
+  static EncodeTiledFn fn = [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return static_cast<EncodeTiledFn>(nullptr);
+    return reinterpret_cast<EncodeTiledFn>(p);
+  }();
+  return fn;
+}
+
+// Dimension (1..3) of the map that holds token, head and batch.
+struct ChunkMapDims {
+  int8_t t, h, b;
+};
+
+// Encodes the map of one input (base 16-byte aligned, strides multiples of 8 elements, L
+// >= 64: the callers check these); returns false if the driver rejects it.
+inline bool encode_chunk_map(CUtensorMap *m, ChunkMapDims *dims_out, const void *base, int B, int H, int L,
+                             const SeqStrides &s) {
+  EncodeTiledFn enc = encode_tiled_fn();
+  if (!enc) return false;
+  const int64_t st[3] = {s.t, s.h, s.b};
+  const int64_t ext[3] = {L, H, B};
+  int ord[3] = {0, 1, 2};  // token, head, batch sorted by stride
+  for (int i = 0; i < 3; ++i)
+    for (int j = i + 1; j < 3; ++j)
+      if (st[ord[j]] < st[ord[i]]) {
+        const int tmp = ord[i];
+        ord[i] = ord[j];
+        ord[j] = tmp;
+      }
+  cuuint64_t dims[4] = {64, 0, 0, 0};
+  cuuint64_t strides[3];
+  cuuint32_t box[4] = {64, 1, 1, 1};
+  for (int i = 0; i < 3; ++i) {
+    dims[i + 1] = (cuuint64_t)ext[ord[i]];
+    strides[i] = (cuuint64_t)st[ord[i]] * 2;
+    if (ord[i] == 0) {
+      box[i + 1] = 64;
+      dims_out->t = (int8_t)(i + 1);
+    } else if (ord[i] == 1) {
+      dims_out->h = (int8_t)(i + 1);
+    } else {
+      dims_out->b = (int8_t)(i + 1);
+    }
+  }
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void *>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// One chunk (tokens t0 .. t0 + 63) of head h, batch b into 64 rows x 128 bytes of shared
+// memory; completion counted in bytes on `bar` (8192 per call).  The channel coordinate is
+// 0, so the innermost offset is 16-byte aligned.
+__device__ __forceinline__ void tma_load_chunk(void *dst_smem, const CUtensorMap *m, ChunkMapDims d, int t0, int h,
+                                               int b, uint64_t *bar) {
+  const int c1 = d.t == 1 ? t0 : d.h == 1 ? h : b;
+  const int c2 = d.t == 2 ? t0 : d.h == 2 ? h : b;
+  const int c3 = d.t == 3 ? t0 : d.h == 3 ? h : b;
+  const uint32_t dst = static_cast<uint32_t>(__cvta_generic_to_shared(dst_smem));
+  const uint32_t mb = static_cast<uint32_t>(__cvta_generic_to_shared(bar));
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, "
+      "%5}], [%6];" ::"r"(dst),
+      "l"(m), "r"(0), "r"(c1), "r"(c2), "r"(c3), "r"(mb)
+      : "memory");
+}
+
+}  // namespace dp
