@@ -204,12 +204,31 @@ layernorm_reg_kernel(const InT *x, const float *res, const float *__restrict__ l
   }
 }
 
+__device__ __forceinline__ void load4(const float *p, float (&v)[4]) {
+  const float4 a = *reinterpret_cast<const float4 *>(p);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+}
+__device__ __forceinline__ void load4(const __nv_bfloat16 *p, float (&v)[4]) {
+  const uint2 a = *reinterpret_cast<const uint2 *>(p);
+  const float2 f0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&a.x));
+  const float2 f1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&a.y));
+  v[0] = f0.x; v[1] = f0.y; v[2] = f1.x; v[3] = f1.y;
+}
+__device__ __forceinline__ void store4(float *p, const float (&v)[4]) {
+  *reinterpret_cast<float4 *>(p) = make_float4(v[0], v[1], v[2], v[3]);
+}
+__device__ __forceinline__ void store4(__nv_bfloat16 *p, const float (&v)[4]) {
+  __nv_bfloat162 h0 = __floats2bfloat162_rn(v[0], v[1]), h1 = __floats2bfloat162_rn(v[2], v[3]);
+  *reinterpret_cast<uint2 *>(p) = make_uint2(*reinterpret_cast<uint32_t *>(&h0), *reinterpret_cast<uint32_t *>(&h1));
+}
+
 // The same pass for the usual shapes (conv kernel size 4, d = 256 NG <= 1024, 16-byte
 // aligned rows), at HBM speed: a CTA takes 32 tokens of one sequence; first each warp
 // computes the LayerNorm statistics of rows t0 - 3 .. t0 + 31 from registers (one
 // 16-byte-wide read of the row), then thread t walks channels t + 256 j down the 35 rows,
 // normalising on the fly and keeping the three previous normalised values in registers
-// for the depthwise conv.  Shared memory holds only the 2 x 35 statistics (the kernel
+// for the depthwise conv (four consecutive channels per thread, 16-byte loads).  Shared
+// memory holds only the 2 x 35 statistics (the kernel
 // above stages the normalised rows, 77 KB, and runs at a fraction of the bandwidth).
 constexpr int kConvRowsT = 32;
 
@@ -253,27 +272,47 @@ ln_conv_silu_rows_kernel(const InT *x, const float *__restrict__ ln_w, const flo
     }
   }
   __syncthreads();
+  // four consecutive channels per thread: 16-byte loads of x and the parameters
 #pragma unroll 1
-  for (int j = 0; j < NG; ++j) {
-    const int c = threadIdx.x + kBlkThreads * j;
-    const float4 w = reinterpret_cast<const float4 *>(conv_w)[c];  // taps of channel c
-    const float lw = ln_w[c], lb = ln_b[c], cb = conv_b ? conv_b[c] : 0.f;
-    float n0 = 0.f, n1 = 0.f, n2 = 0.f;  // normalised inputs of the three previous tokens
-#pragma unroll 5
+  for (int g = threadIdx.x; g < d / 4; g += kBlkThreads) {
+    const int c = 4 * g;
+    float4 w[4];  // taps of channels c .. c + 3
+#pragma unroll
+    for (int i = 0; i < 4; ++i) w[i] = reinterpret_cast<const float4 *>(conv_w)[c + i];
+    const float4 lw = *reinterpret_cast<const float4 *>(ln_w + c), lb = *reinterpret_cast<const float4 *>(ln_b + c);
+    const float4 cb = conv_b ? *reinterpret_cast<const float4 *>(conv_b + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+    const float lwv[4] = {lw.x, lw.y, lw.z, lw.w}, lbv[4] = {lb.x, lb.y, lb.z, lb.w};
+    const float cbv[4] = {cb.x, cb.y, cb.z, cb.w};
+    float n0[4] = {0.f, 0.f, 0.f, 0.f}, n1[4] = {0.f, 0.f, 0.f, 0.f}, n2[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
     for (int r = 0; r < R; ++r) {
       const int t = t0 - (K - 1) + r;
-      float n = 0.f;
-      if (t >= 0 && t < L) n = fmaf((to_f32(x[((size_t)b * L + t) * d + c]) - s_mean[r]) * s_rstd[r], lw, lb);
-      if (r >= K - 1 && t < L) {
-        float acc = fmaf(w.x, n0, cb);
-        acc = fmaf(w.y, n1, acc);
-        acc = fmaf(w.z, n2, acc);
-        acc = fmaf(w.w, n, acc);
-        store_f32_as(out + ((size_t)b * L + t) * d + c, n + acc / (1.f + __expf(-acc)));
+      float n[4] = {0.f, 0.f, 0.f, 0.f};
+      if (t >= 0 && t < L) {
+        float xv[4];
+        load4(x + ((size_t)b * L + t) * d + c, xv);
+        const float mu = s_mean[r], rs = s_rstd[r];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) n[i] = fmaf((xv[i] - mu) * rs, lwv[i], lbv[i]);
       }
-      n0 = n1;
-      n1 = n2;
-      n2 = n;
+      if (r >= K - 1 && t < L) {
+        float o[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          float acc = fmaf(w[i].x, n0[i], cbv[i]);
+          acc = fmaf(w[i].y, n1[i], acc);
+          acc = fmaf(w[i].z, n2[i], acc);
+          acc = fmaf(w[i].w, n[i], acc);
+          o[i] = n[i] + acc / (1.f + __expf(-acc));
+        }
+        store4(out + ((size_t)b * L + t) * d + c, o);
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        n0[i] = n1[i];
+        n1[i] = n2[i];
+        n2[i] = n[i];
+      }
     }
   }
 }
@@ -418,8 +457,9 @@ extern "C" int dp_ln_conv_silu(const void *x, int x_dtype, const float *ln_w, co
   if (B == 0 || L == 0) return DP_OK;
   DP_REQUIRE(x && ln_w && ln_b && conv_w && out, DP_ERR_INVALID_ARGUMENT, "dp_ln_conv_silu: null pointer");
   cudaStream_t st0 = as_stream(stream);
-  if (k == 4 && d % kBlkThreads == 0 && d <= 4 * kBlkThreads && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
-      (reinterpret_cast<uintptr_t>(conv_w) & 15) == 0 && (L + kConvRowsT - 1) / kConvRowsT < (1 << 30)) {
+  auto al16 = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  if (k == 4 && d % kBlkThreads == 0 && d <= 4 * kBlkThreads && al16(x) && al16(conv_w) && al16(ln_w) &&
+      al16(ln_b) && al16(conv_b) && al16(out) && (L + kConvRowsT - 1) / kConvRowsT < (1 << 30)) {
     const dim3 grid((L + kConvRowsT - 1) / kConvRowsT, B);
     auto launch = [&](auto xt, auto ot) {
       using XT = decltype(xt);
