@@ -24,10 +24,11 @@
 // dtheta = -sin dkap_cos + cos dkap_sin.  Pass 1 runs the chunked forward and keeps the
 // state at every sub-chunk start in the workspace; pass 2 walks the sub-chunks backwards.
 //
-// One CTA of 256 threads per (b, h); every product is a warp-level tf32 tensor-core MMA
-// (mma.sync m16n8k8) on fp32 shared-memory operands; the ones that carry the state and
-// its gradient across sub-chunks are split in high and low tf32 parts (three products:
-// hi hi + hi lo + lo hi), which keeps fp32 accuracy there (see mma16).  The 32 x 32
+// One CTA of 256 threads per (b, h); every product is a warp-level tensor-core MMA on
+// fp32 shared-memory operands: the ones that carry the state and its gradient across
+// sub-chunks split both operands in high and low bf16 parts (three m16n8k16 products:
+// hi hi + hi lo + lo hi, 16 significant bits per operand), the sub-chunk-local gradients
+// use one tf32 m16n8k8 product (see mma16).  The 32 x 32
 // triangular inverse is a forward substitution by one warp (a lane per column) while the
 // other warps form E.  Limits: D <= 64, Dv <= 64.
 #include "dp_common.cuh"
@@ -96,10 +97,51 @@ __device__ __forceinline__ float load_any(const void *p, int dt, int64_t i) {
 // serve the products whose result is a gradient of this sub-chunk only (dK, dQ, dA, dP,
 // Y); everything that feeds the state or its gradient across sub-chunks is split (an
 // error there would add up along the sequence).
+// Split operand pairs in bf16: v = hi + lo with hi = bf16(v), lo = bf16(v - hi) (16
+// significant bits); packs two values' parts into bf16x2 words (first value low).
+__device__ __forceinline__ void split_bf16x2(float v0, float v1, uint32_t &hi, uint32_t &lo) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(v0, v1);
+  const float2 hf = __bfloat1622float2(h);
+  const __nv_bfloat162 l = __floats2bfloat162_rn(v0 - hf.x, v1 - hf.y);
+  hi = *reinterpret_cast<const uint32_t *>(&h);
+  lo = *reinterpret_cast<const uint32_t *>(&l);
+}
+
 template <int K, bool SPLIT = true>
 __device__ __forceinline__ void mma16(float (&d)[2][4], const float *x, int x_si, int x_sk, const float *y, int y_sk,
                                       int y_sj, int lane) {
   const int g = lane >> 2, c = lane & 3;
+  if (SPLIT) {
+    // hi hi + hi lo + lo hi on bf16 m16n8k16 (half the MMAs of the tf32 m16n8k8 form per
+    // k; dropped lo lo term ~2^-16 relative).  A: rows g / g + 8, k pairs (2c, 2c+1) and
+    // (2c+8, 2c+9); B: the same k pairs, column g.
+    static_assert(K % 16 == 0, "split products step K by 16");
+    float e[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll 2
+    for (int k0 = 0; k0 < K; k0 += 16) {
+      const int ka = k0 + 2 * c, kb = k0 + 2 * c + 8;
+      uint32_t ah[4], al[4];
+      split_bf16x2(x[g * x_si + ka * x_sk], x[g * x_si + (ka + 1) * x_sk], ah[0], al[0]);
+      split_bf16x2(x[(g + 8) * x_si + ka * x_sk], x[(g + 8) * x_si + (ka + 1) * x_sk], ah[1], al[1]);
+      split_bf16x2(x[g * x_si + kb * x_sk], x[g * x_si + (kb + 1) * x_sk], ah[2], al[2]);
+      split_bf16x2(x[(g + 8) * x_si + kb * x_sk], x[(g + 8) * x_si + (kb + 1) * x_sk], ah[3], al[3]);
+#pragma unroll
+      for (int n = 0; n < 2; ++n) {
+        const int j = (g + 8 * n) * y_sj;
+        uint32_t bh[2], bl[2];
+        split_bf16x2(y[ka * y_sk + j], y[(ka + 1) * y_sk + j], bh[0], bl[0]);
+        split_bf16x2(y[kb * y_sk + j], y[(kb + 1) * y_sk + j], bh[1], bl[1]);
+        mma_bf16_m16n8k16(d[n], ah, bh);
+        mma_bf16_m16n8k16(e[n], ah, bl);
+        mma_bf16_m16n8k16(e[n], al, bh);
+      }
+    }
+#pragma unroll
+    for (int n = 0; n < 2; ++n)
+#pragma unroll
+      for (int r = 0; r < 4; ++r) d[n][r] += e[n][r];
+    return;
+  }
   // the high-high products accumulate in d, the two cross products in e: four independent
   // accumulation chains per call instead of two
   float e[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
