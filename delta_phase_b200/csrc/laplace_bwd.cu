@@ -19,17 +19,20 @@
 // states from its checkpoint into a per-unit scratch (32 KB per token at D = Dv = 64,
 // L2-resident) and then walks back through them.
 //
-// One CTA of 256 threads per (b, h): warp w holds rows 32 (w / 4) .. +31 of column
-// 32 (w % 4) + lane of S and dS in registers (D <= 64, Dv <= 64); heads with 2 D <= 32
-// and Dv <= 32 take a one-warp-per-unit kernel instead (end of this file).  Row sums are warp
-// reduce-scatters plus a 4-way shared-memory sum; the column sums of the two row halves
-// are paired through shared memory one token later.
+// Rows of the state never interact (each value row has its own decay), so one CTA of 128
+// threads takes one (b, h) and one half of its value rows (two CTAs per unit when
+// Dv > 32): warp w holds rows 32 rh .. +31 of column 32 w + lane of S and dS in registers
+// (D <= 64, Dv <= 64); heads with 2 D <= 32 and Dv <= 32 take a one-warp-per-unit kernel
+// instead (end of this file).  Row sums are warp reduce-scatters plus a 4-way
+// shared-memory sum.  The only sums across rows -- the key / query gradients and d beta --
+// are outputs: each half adds its part into the zeroed outputs (with two halves the two
+// additions onto zero commute exactly, so the result does not depend on their order).
 #include "dp_common.cuh"
 
 namespace dp {
 namespace {
 
-constexpr int kLT = 256;     // threads
+constexpr int kLT = 128;     // threads
 constexpr int kLC = 32;      // tokens per sub-chunk
 constexpr int kLF = 128;     // key features (2 D) at most
 constexpr int kLDv = 64;     // value rows at most
@@ -47,6 +50,7 @@ struct LapBwdArgs {
   float *ckpt;                                // (B*H, NSC, Dv, F) states at sub-chunk starts
   float *scratch;                             // (B*H, kLC + 1, Dv, F) states inside a sub-chunk
   int H, L, D, Dv;
+  int nhalf;  // CTAs per unit (value-row halves)
 };
 
 struct LapStage {
@@ -82,12 +86,16 @@ __device__ __forceinline__ float reduce_scatter32(float (&x)[32], int lane) {
 // issued before its arithmetic and shared stores.  Rows / channels past n, D, Dv are zero
 // (decay 1 for the absent tokens, so a partial sub-chunk leaves the state alone).
 __device__ void lap_stage(const LapBwdArgs &a, LapStage &st, int b, int h, int t0, int n, bool bwd, int64_t row_base) {
-  constexpr int kPer = kLC * 64 / kLT;
+  constexpr int kPer = 8, kRounds = kLC * 64 / (kLT * kPer);
   const int tid = threadIdx.x;
+  float xb = 0.f;
+  if (tid < kLC && tid < n) xb = load_any(a.beta, a.beta_dt, b * a.s_b.b + h * a.s_b.h + (int64_t)(t0 + tid) * a.s_b.t);
+#pragma unroll 1
+  for (int rd = 0; rd < kRounds; ++rd) {
   float xk[kPer], xmk[kPer], xq[kPer], xmq[kPer], xv[kPer], xl[kPer], xo[kPer];
 #pragma unroll
   for (int i = 0; i < kPer; ++i) {
-    const int idx = tid + i * kLT, r = idx >> 6, c = idx & 63, t = t0 + r;
+    const int idx = tid + (rd * kPer + i) * kLT, r = idx >> 6, c = idx & 63, t = t0 + r;
     const bool ok = r < n;
     xk[i] = xmk[i] = xq[i] = xmq[i] = xv[i] = xo[i] = 0.f;
     xl[i] = 0.f;
@@ -105,11 +113,9 @@ __device__ void lap_stage(const LapBwdArgs &a, LapStage &st, int b, int h, int t
       if (bwd) xo[i] = a.dout[row_base + (int64_t)t * a.Dv + c];
     }
   }
-  float xb = 0.f;
-  if (tid < kLC && tid < n) xb = load_any(a.beta, a.beta_dt, b * a.s_b.b + h * a.s_b.h + (int64_t)(t0 + tid) * a.s_b.t);
 #pragma unroll
   for (int i = 0; i < kPer; ++i) {
-    const int idx = tid + i * kLT, r = idx >> 6, c = idx & 63;
+    const int idx = tid + (rd * kPer + i) * kLT, r = idx >> 6, c = idx & 63;
     const bool ok = r < n;
     float s, co, mag = __expf(xmk[i]);
     sincosf(xk[i], &s, &co);
@@ -127,6 +133,7 @@ __device__ void lap_stage(const LapBwdArgs &a, LapStage &st, int b, int h, int t
     const float r_ = live ? __expf(fmaxf(xl[i], kLogFloor)) : 1.f;
     st.r[r][c] = r_;
     st.rg[r][c] = (live && xl[i] > kLogFloor) ? r_ : 0.f;
+  }
   }
   if (tid < kLC) st.beta[tid] = xb;
 }
@@ -155,12 +162,12 @@ __global__ void __launch_bounds__(kLT, 1) laplace_bwd_kernel(LapBwdArgs a) {
   extern __shared__ __align__(16) uint8_t lsm[];
   LapStage &st = *reinterpret_cast<LapStage *>(lsm);
   float(*red)[2][4][64] = reinterpret_cast<float(*)[2][4][64]>(lsm + sizeof(LapStage));   // [par][which][cb][row]
-  float(*colb)[2][2][128] =
-      reinterpret_cast<float(*)[2][2][128]>(lsm + sizeof(LapStage) + sizeof(float) * 2 * 2 * 4 * 64);  // [par][rh][q][j]
+  float(*colb)[2][128] =
+      reinterpret_cast<float(*)[2][128]>(lsm + sizeof(LapStage) + sizeof(float) * 2 * 2 * 4 * 64);  // [par][q][j]
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int rh = warp >> 2, cb = warp & 3, j = 32 * cb + lane, row0 = 32 * rh;
-  const int bh = blockIdx.x, b = bh / a.H, h = bh % a.H;
+  const int rh = blockIdx.x % a.nhalf, cb = warp, j = 32 * cb + lane, row0 = 32 * rh;
+  const int bh = blockIdx.x / a.nhalf, b = bh / a.H, h = bh % a.H;
   const int L = a.L, D = a.D, Dv = a.Dv, F = 2 * D;
   const bool col_ok = j < F;
   const float invD = 1.0f / (float)D;
@@ -204,16 +211,17 @@ __global__ void __launch_bounds__(kLT, 1) laplace_bwd_kernel(LapBwdArgs a) {
   int pend_t = -1, pend_par = 0;
   float pend_kc = 0.f, pend_ks = 0.f, pend_qc = 0.f, pend_qs = 0.f;
   auto finish = [&](int t, int pp, float kc, float ks, float qc, float qs) {
-    // even lane: channel j / 2 (own = cos column, partner = sin column)
-    const float dk = colb[pp][0][0][j] + colb[pp][1][0][j];
-    const float dq = (colb[pp][0][1][j] + colb[pp][1][1][j]) * invD;
+    // even lane: channel j / 2 (own = cos column, partner = sin column); this row half's
+    // part of the gradients (outputs zeroed by the entry point)
+    const float dk = colb[pp][0][j];
+    const float dq = colb[pp][1][j] * invD;
     const float dk2 = __shfl_xor_sync(0xffffffffu, dk, 1), dq2 = __shfl_xor_sync(0xffffffffu, dq, 1);
     if (!(j & 1) && col_ok) {
       const int64_t gi = ((int64_t)bh * L + t) * D + (j >> 1);
-      a.dtk[gi] = -ks * dk + kc * dk2;
-      a.dmk[gi] = kc * dk + ks * dk2;
-      a.dtq[gi] = -qs * dq + qc * dq2;
-      a.dmq[gi] = qc * dq + qs * dq2;
+      atomicAdd(a.dtk + gi, -ks * dk + kc * dk2);
+      atomicAdd(a.dmk + gi, kc * dk + ks * dk2);
+      atomicAdd(a.dtq + gi, -qs * dq + qc * dq2);
+      atomicAdd(a.dmq + gi, qc * dq + qs * dq2);
     }
   };
   for (int sc = nsc - 1; sc >= 0; --sc) {
@@ -265,7 +273,7 @@ __global__ void __launch_bounds__(kLT, 1) laplace_bwd_kernel(LapBwdArgs a) {
       red[par][0][cb][row0 + lane] = reduce_scatter32(x1, lane);
       red[par][1][cb][row0 + lane] = reduce_scatter32(x2, lane);
       __syncthreads();
-      if (pend_t >= 0 && rh == 0) finish(pend_t, pend_par, pend_kc, pend_ks, pend_qc, pend_qs);
+      if (pend_t >= 0) finish(pend_t, pend_par, pend_kc, pend_ks, pend_qc, pend_qs);
       const int o = row0 + lane;
       const float du = red[par][0][0][o] + red[par][0][1][o] + red[par][0][2][o] + red[par][0][3][o];
       const float dr = red[par][1][0][o] + red[par][1][1][o] + red[par][1][2][o] + red[par][1][3][o];
@@ -288,8 +296,8 @@ __global__ void __launch_bounds__(kLT, 1) laplace_bwd_kernel(LapBwdArgs a) {
         pk = fmaf(Sp[i], de_i, pk);
         S[i] = Sp[i];
       }
-      colb[par][rh][0][j] = pw - pk * invD;
-      colb[par][rh][1][j] = pq;
+      colb[par][0][j] = pw - pk * invD;
+      colb[par][1][j] = pq;
       pend_t = t;
       pend_par = par;
       pend_kc = st.kc[r][j >> 1];
@@ -299,7 +307,7 @@ __global__ void __launch_bounds__(kLT, 1) laplace_bwd_kernel(LapBwdArgs a) {
     }
     __syncthreads();  // the stage is reloaded next
   }
-  if (pend_t >= 0 && rh == 0) finish(pend_t, pend_par, pend_kc, pend_ks, pend_qc, pend_qs);
+  if (pend_t >= 0) finish(pend_t, pend_par, pend_kc, pend_ks, pend_qc, pend_qs);
   if (a.dstate_in) {
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
@@ -592,9 +600,19 @@ extern "C" int dp_laplace_bwd(const void *theta_k, const void *logmag_k, const v
     kern<<<(units + kWarpUnits - 1) / kWarpUnits, 32 * kWarpUnits, 0, as_stream(stream)>>>(a, units);
     return check_launch("laplace_bwd_warp_kernel");
   }
-  const size_t smem = sizeof(LapStage) + sizeof(float) * (2 * 2 * 4 * 64 + 2 * 2 * 2 * 128);
+  // the key / query gradients are sums over the row halves: zeroed first
+  if (L > 0) {
+    float *zero[4] = {grad_theta_k, grad_logmag_k, grad_theta_q, grad_logmag_q};
+    for (float *p : zero) {
+      const cudaError_t e = cudaMemsetAsync(p, 0, (size_t)B * H * L * D * sizeof(float), as_stream(stream));
+      if (e != cudaSuccess)
+        return set_error(DP_ERR_CUDA, std::string("dp_laplace_bwd: memset: ") + cudaGetErrorString(e));
+    }
+  }
+  a.nhalf = Dv > 32 ? 2 : 1;
+  const size_t smem = sizeof(LapStage) + sizeof(float) * (2 * 2 * 4 * 64 + 2 * 2 * 128);
   cudaError_t e = cudaFuncSetAttribute(laplace_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return set_error(DP_ERR_CUDA, std::string("dp_laplace_bwd smem attr: ") + cudaGetErrorString(e));
-  laplace_bwd_kernel<<<B * H, kLT, smem, as_stream(stream)>>>(a);
+  laplace_bwd_kernel<<<B * H * a.nhalf, kLT, smem, as_stream(stream)>>>(a);
   return check_launch("laplace_bwd_kernel");
 }
