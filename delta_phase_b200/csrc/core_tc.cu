@@ -15,7 +15,7 @@
 // Two warp-specialised roles share one CTA per (batch, head):
 //   * prep (8 warps) computes the state-independent work of chunk c+1 while
 //   * chain (4 warps) runs the recurrence of chunk c.
-// Prep: phasors (bf16) from bulk-copied inputs; G1 = [K; Q] K^T (tcgen05, M=128); A and P
+// Prep: phasors (bf16) from TMA-loaded inputs; G1 = [K; Q] K^T (tcgen05, M=128); A and P
 // from the Gram rows; T = (I + A)^-1 in fp32 (16 x 16 diagonal blocks by right-looking
 // substitution, the 16 -> 32 block merge on warp-level tf32 MMA) into a per-slot buffer.
 // Chain: S^T -> bf16; G3 = [K; Q] S^T (M=128) and, while it runs, the 32 -> 64 merge of

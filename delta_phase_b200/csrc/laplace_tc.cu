@@ -29,8 +29,9 @@
 // forms every decay ratio as exp(difference) <= 1.
 //
 // One CTA of 256 threads per (batch, head, half of the value channels): rows of the state
-// do not interact, so the two halves run independently.  Phases stream in two chunks ahead
-// with bulk async copies; v, log-decay and beta are prefetched a chunk ahead in registers.
+// do not interact, so the two halves run independently.  Phases and log-magnitudes
+// stream a chunk ahead through TMA tensor maps (tmap.cuh); v, log-decay and beta are
+// prefetched a chunk ahead in registers.
 // Every wait is bounded.
 #include <type_traits>
 
