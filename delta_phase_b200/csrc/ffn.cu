@@ -257,7 +257,7 @@ __device__ __forceinline__ void features_dct(const float *hrow, T *__restrict__ 
 
 // Recursive Haar branch into z[4d:5d], z[5d:6d]; hv holds lane l's values of x and is
 // overwritten.
-template <typename T, int R>
+template <typename T, int R, bool kSpread>
 __device__ __forceinline__ void features_haar(float (&hv)[R], T *__restrict__ zr, int lane) {
   constexpr int d = 32 * R;
   const float r2 = 0.70710678118654752f;
@@ -278,8 +278,11 @@ __device__ __forceinline__ void features_haar(float (&hv)[R], T *__restrict__ zr
       hv[r] = (hv[r] + p) * r2;
     }
   }
-  // levels n = R .. 2 inside lane 0, then ho[0]
-  if (lane == 0) {
+  // levels n = R .. 2 on lane 0's values, then ho[0].  kSpread (few tokens, where the
+  // tail is on the critical path): every lane runs them (only lane 0's are the row's) and
+  // the R outputs' sin / cos are spread over the lanes; otherwise lane 0 alone (fewer
+  // instructions in total, which counts when many tokens share the SMs).
+  if (kSpread || lane == 0) {
     float ho[R];
 #pragma unroll
     for (int n = R; n > 1; n >>= 1) {
@@ -293,7 +296,22 @@ __device__ __forceinline__ void features_haar(float (&hv)[R], T *__restrict__ zr
       for (int i = 0; i < half; ++i) hv[i] = lo[i];
     }
     ho[0] = hv[0];
-    store_cos_sin<T, R>(zr + 4 * d, zr + 5 * d, ho, 1.f);
+    if constexpr (kSpread) {
+      float mine = 0.f;
+#pragma unroll
+      for (int i = 0; i < R; ++i) {
+        const float vi = __shfl_sync(0xffffffffu, ho[i], 0);
+        if (lane == i) mine = vi;
+      }
+      if (lane < R) {
+        float sv, cv;
+        sincos_2pi_fast(mine, &sv, &cv);
+        zr[4 * d + lane] = from_f32<T>(cv);
+        zr[5 * d + lane] = from_f32<T>(sv);
+      }
+    } else {
+      store_cos_sin<T, R>(zr + 4 * d, zr + 5 * d, ho, 1.f);
+    }
   }
 }
 
@@ -314,7 +332,7 @@ ffn_features_warp_kernel(const T *__restrict__ x, const float *__restrict__ hdct
   T *zr = z + row * 6 * d;
   features_fwht<T, R>(v, zr, lane);
   features_dct<T, R>(hdct + row * d, zr, lane);
-  features_haar<T, R>(hv, zr, lane);
+  features_haar<T, R, false>(hv, zr, lane);
 }
 
 // Few tokens (decode): one CTA of three warps per token, warp w computing branch w
@@ -339,7 +357,7 @@ ffn_features_split_kernel(const T *x, const float *hdct, T *__restrict__ z) {
   if (part == 0)
     features_fwht<T, R>(v, zr, lane);
   else
-    features_haar<T, R>(v, zr, lane);
+    features_haar<T, R, true>(v, zr, lane);
 }
 
 // ---------------------------------------------------------------- cuBLAS handles
