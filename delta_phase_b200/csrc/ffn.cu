@@ -256,9 +256,13 @@ __device__ __forceinline__ void features_dct(const float *hrow, T *__restrict__ 
 }
 
 // Recursive Haar branch into z[4d:5d], z[5d:6d]; hv holds lane l's values of x and is
-// overwritten.
-template <typename T, int R, bool kSpread>
-__device__ __forceinline__ void features_haar(float (&hv)[R], T *__restrict__ zr, int lane) {
+// overwritten.  buf == nullptr: each level's outputs get their sin / cos on the lanes that
+// hold the level (lane 0 also takes the last R alone), the fewest instructions in total
+// (many tokens).  buf (d floats of shared memory): the outputs are staged there and every
+// lane then takes R consecutive ones, so no lane computes more sin / cos than the other
+// branches' lanes (few tokens: the branch's serial time is the critical path).
+template <typename T, int R>
+__device__ __forceinline__ void features_haar(float (&hv)[R], T *__restrict__ zr, int lane, float *buf) {
   constexpr int d = 32 * R;
   const float r2 = 0.70710678118654752f;
   // levels n = 32R .. 2R span nl = n / R lanes
@@ -270,7 +274,13 @@ __device__ __forceinline__ void features_haar(float (&hv)[R], T *__restrict__ zr
     for (int r = 0; r < R; r += 2) hi[r / 2] = (hv[r] - hv[r + 1]) * r2;
     if (lane < nl) {
       const int o = half_l * R + (R / 2) * lane;  // ho[n/2 + i], i = (R lane + r) / 2
-      store_cos_sin<T, R / 2>(zr + 4 * d + o, zr + 5 * d + o, hi, 1.f);
+      if (buf) {
+#pragma unroll
+        for (int i = 0; i < R / 2; i += 4)
+          *reinterpret_cast<float4 *>(buf + o + i) = make_float4(hi[i], hi[i + 1], hi[i + 2], hi[i + 3]);
+      } else {
+        store_cos_sin<T, R / 2>(zr + 4 * d + o, zr + 5 * d + o, hi, 1.f);
+      }
     }
 #pragma unroll
     for (int r = 0; r < R; ++r) {
@@ -278,11 +288,8 @@ __device__ __forceinline__ void features_haar(float (&hv)[R], T *__restrict__ zr
       hv[r] = (hv[r] + p) * r2;
     }
   }
-  // levels n = R .. 2 on lane 0's values, then ho[0].  kSpread (few tokens, where the
-  // tail is on the critical path): every lane runs them (only lane 0's are the row's) and
-  // the R outputs' sin / cos are spread over the lanes; otherwise lane 0 alone (fewer
-  // instructions in total, which counts when many tokens share the SMs).
-  if (kSpread || lane == 0) {
+  // levels n = R .. 2 inside lane 0, then ho[0]
+  if (lane == 0) {
     float ho[R];
 #pragma unroll
     for (int n = R; n > 1; n >>= 1) {
@@ -296,22 +303,22 @@ __device__ __forceinline__ void features_haar(float (&hv)[R], T *__restrict__ zr
       for (int i = 0; i < half; ++i) hv[i] = lo[i];
     }
     ho[0] = hv[0];
-    if constexpr (kSpread) {
-      float mine = 0.f;
+    if (buf) {
 #pragma unroll
-      for (int i = 0; i < R; ++i) {
-        const float vi = __shfl_sync(0xffffffffu, ho[i], 0);
-        if (lane == i) mine = vi;
-      }
-      if (lane < R) {
-        float sv, cv;
-        sincos_2pi_fast(mine, &sv, &cv);
-        zr[4 * d + lane] = from_f32<T>(cv);
-        zr[5 * d + lane] = from_f32<T>(sv);
-      }
+      for (int i = 0; i < R; i += 4) *reinterpret_cast<float4 *>(buf + i) = make_float4(ho[i], ho[i + 1], ho[i + 2], ho[i + 3]);
     } else {
       store_cos_sin<T, R>(zr + 4 * d, zr + 5 * d, ho, 1.f);
     }
+  }
+  if (buf) {
+    __syncwarp();
+    float vals[R];
+#pragma unroll
+    for (int i = 0; i < R; i += 4) {
+      const float4 q = *reinterpret_cast<const float4 *>(buf + R * lane + i);
+      vals[i] = q.x; vals[i + 1] = q.y; vals[i + 2] = q.z; vals[i + 3] = q.w;
+    }
+    store_cos_sin<T, R>(zr + 4 * d + R * lane, zr + 5 * d + R * lane, vals, 1.f);
   }
 }
 
@@ -332,7 +339,7 @@ ffn_features_warp_kernel(const T *__restrict__ x, const float *__restrict__ hdct
   T *zr = z + row * 6 * d;
   features_fwht<T, R>(v, zr, lane);
   features_dct<T, R>(hdct + row * d, zr, lane);
-  features_haar<T, R, false>(hv, zr, lane);
+  features_haar<T, R>(hv, zr, lane, nullptr);
 }
 
 // Few tokens (decode): one CTA of three warps per token, warp w computing branch w
@@ -352,12 +359,13 @@ ffn_features_split_kernel(const T *x, const float *hdct, T *__restrict__ z) {
     features_dct<T, R>(hdct + row * d, zr, lane);
     return;
   }
+  __shared__ __align__(16) float haar_out[d];  // the Haar warp's staged outputs
   float v[R];
   load_row_part<T, R>(x + row * d + R * lane, v);
   if (part == 0)
     features_fwht<T, R>(v, zr, lane);
   else
-    features_haar<T, R, true>(v, zr, lane);
+    features_haar<T, R>(v, zr, lane, haar_out);
 }
 
 // ---------------------------------------------------------------- cuBLAS handles
