@@ -78,6 +78,7 @@ class ClockSampler:
         self.samples = []
         self.reasons = set()
         self._stop = threading.Event()
+        self._first = threading.Event()
         self._t = None
         self.max_mhz = None
 
@@ -95,6 +96,7 @@ class ClockSampler:
             return
         self._t = threading.Thread(target=self._run, daemon=True)
         self._t.start()
+        self._first.wait(timeout=1.0)  # sampling is running before the timed region starts
 
     def _run(self):
         nv = self._nv
@@ -107,6 +109,7 @@ class ClockSampler:
                         self.reasons.add(name)
             except Exception:
                 pass
+            self._first.set()
             time.sleep(self.period)
 
     def stop(self):
