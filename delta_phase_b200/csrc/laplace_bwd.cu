@@ -19,20 +19,22 @@
 // states from its checkpoint into a per-unit scratch (32 KB per token at D = Dv = 64,
 // L2-resident) and then walks back through them.
 //
-// Rows of the state never interact (each value row has its own decay), so one CTA of 128
+// Rows of the state never interact (each value row has its own decay), so one CTA of 256
 // threads takes one (b, h) and one half of its value rows (two CTAs per unit when
-// Dv > 32): warp w holds rows 32 rh .. +31 of column 32 w + lane of S and dS in registers
-// (D <= 64, Dv <= 64); heads with 2 D <= 32 and Dv <= 32 take a one-warp-per-unit kernel
-// instead (end of this file).  Row sums are warp reduce-scatters plus a 4-way
+// Dv > 32): warp w holds rows 32 rh + 16 (w / 4) .. +15 of column 32 (w % 4) + lane of S
+// and dS in registers (D <= 64, Dv <= 64; two warps per scheduler); heads with 2 D <= 32
+// and Dv <= 32 take a one-warp-per-unit kernel instead (end of this file).  Row sums are warp reduce-scatters plus a 4-way
 // shared-memory sum.  The only sums across rows -- the key / query gradients and d beta --
-// are outputs: each half adds its part into the zeroed outputs (with two halves the two
-// additions onto zero commute exactly, so the result does not depend on their order).
+// are outputs: a CTA sums its two row groups in shared memory in a fixed order, and each
+// half adds its part into the zeroed outputs (with two halves the two additions onto zero
+// commute exactly, so the result does not depend on their order).
 #include "dp_common.cuh"
 
 namespace dp {
 namespace {
 
-constexpr int kLT = 128;     // threads
+constexpr int kLT = 256;     // threads: 2 row groups x 4 column blocks
+constexpr int kRW = 16;      // state rows per warp
 constexpr int kLC = 32;      // tokens per sub-chunk
 constexpr int kLF = 128;     // key features (2 D) at most
 constexpr int kLDv = 64;     // value rows at most
@@ -71,6 +73,26 @@ __device__ __forceinline__ float load_any(const void *p, int dt, int64_t i) {
 __device__ __forceinline__ float reduce_scatter32(float (&x)[32], int lane) {
 #pragma unroll
   for (int k = 16; k >= 1; k >>= 1) {
+    const bool upper = (lane & k) != 0;
+#pragma unroll
+    for (int i = 0; i < k; ++i) {
+      const float send = upper ? x[i] : x[i + k];
+      const float keep = upper ? x[i + k] : x[i];
+      x[i] = keep + __shfl_xor_sync(0xffffffffu, send, k);
+    }
+  }
+  return x[0];
+}
+
+// Lane l returns the warp sum of x[l % ROWS] (ROWS = 16 or 32).
+template <int ROWS>
+__device__ __forceinline__ float rs_rows(float (&x)[ROWS], int lane) {
+  if (ROWS == 16) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) x[i] += __shfl_xor_sync(0xffffffffu, x[i], 16);
+  }
+#pragma unroll
+  for (int k = ROWS / 2; k >= 1; k >>= 1) {
     const bool upper = (lane & k) != 0;
 #pragma unroll
     for (int i = 0; i < k; ++i) {
@@ -138,22 +160,24 @@ __device__ void lap_stage(const LapBwdArgs &a, LapStage &st, int b, int h, int t
   if (tid < kLC) st.beta[tid] = xb;
 }
 
-// One forward token (row o = row0 + lane of this warp): e, u = beta e, S = diag(r) S + u kap^T.
-// Returns u for this lane's row and e through *e_out.
-__device__ __forceinline__ float lap_fwd_token(float (&S)[32], float (*red)[4][64], const LapStage &st, int r, int j,
-                                               int cb, int row0, int lane, float invD, float *e_out) {
+// One forward token (rows row0 .. row0 + 15 of this warp; lane l stands for row
+// row0 + l % 16): e, u = beta e, S = diag(r) S + u kap^T.  Returns u for this lane's row
+// and e through *e_out.
+__device__ __forceinline__ float lap_fwd_token(float (&S)[kRW], float (*red)[4][64], const LapStage &st, int r,
+                                               int j, int cb, int row0, int lane, float invD, float *e_out) {
   const float kap = (j & 1) ? st.ks[r][j >> 1] : st.kc[r][j >> 1];
-  float x[32];
+  float x[kRW];
 #pragma unroll
-  for (int i = 0; i < 32; ++i) x[i] = S[i] * kap;
-  red[0][cb][row0 + lane] = reduce_scatter32(x, lane);
+  for (int i = 0; i < kRW; ++i) x[i] = S[i] * kap;
+  const float rsum = rs_rows<kRW>(x, lane);
+  const int o = row0 + (lane & (kRW - 1));
+  if (lane < kRW) red[0][cb][o] = rsum;
   __syncthreads();
-  const int o = row0 + lane;
   const float skr = red[0][0][o] + red[0][1][o] + red[0][2][o] + red[0][3][o];
   const float e = st.v[r][o] - skr * invD;
   const float u = st.beta[r] * e;
 #pragma unroll
-  for (int i = 0; i < 32; ++i) S[i] = fmaf(__shfl_sync(0xffffffffu, u, i), kap, st.r[r][row0 + i] * S[i]);
+  for (int i = 0; i < kRW; ++i) S[i] = fmaf(__shfl_sync(0xffffffffu, u, i), kap, st.r[r][row0 + i] * S[i]);
   *e_out = e;
   return u;
 }
@@ -162,11 +186,14 @@ __global__ void __launch_bounds__(kLT, 1) laplace_bwd_kernel(LapBwdArgs a) {
   extern __shared__ __align__(16) uint8_t lsm[];
   LapStage &st = *reinterpret_cast<LapStage *>(lsm);
   float(*red)[2][4][64] = reinterpret_cast<float(*)[2][4][64]>(lsm + sizeof(LapStage));   // [par][which][cb][row]
-  float(*colb)[2][128] =
-      reinterpret_cast<float(*)[2][128]>(lsm + sizeof(LapStage) + sizeof(float) * 2 * 2 * 4 * 64);  // [par][q][j]
+  float(*colb)[2][2][128] = reinterpret_cast<float(*)[2][2][128]>(
+      lsm + sizeof(LapStage) + sizeof(float) * 2 * 2 * 4 * 64);  // [par][row group][q][j]
+  float(*pbeta)[2] = reinterpret_cast<float(*)[2]>(
+      lsm + sizeof(LapStage) + sizeof(float) * (2 * 2 * 4 * 64 + 2 * 2 * 2 * 128));  // [par][row group]
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int rh = blockIdx.x % a.nhalf, cb = warp, j = 32 * cb + lane, row0 = 32 * rh;
+  const int rh = blockIdx.x % a.nhalf, rg = warp >> 2, cb = warp & 3, j = 32 * cb + lane;
+  const int row0 = 32 * rh + kRW * rg;
   const int bh = blockIdx.x / a.nhalf, b = bh / a.H, h = bh % a.H;
   const int L = a.L, D = a.D, Dv = a.Dv, F = 2 * D;
   const bool col_ok = j < F;
@@ -177,9 +204,9 @@ __global__ void __launch_bounds__(kLT, 1) laplace_bwd_kernel(LapBwdArgs a) {
   float *ckpt = a.ckpt + (int64_t)bh * nsc * Dv * F;
   float *scr = a.scratch + (int64_t)bh * (kLC + 1) * Dv * F;
 
-  float S[32], dS[32];
+  float S[kRW], dS[kRW];
 #pragma unroll
-  for (int i = 0; i < 32; ++i) {
+  for (int i = 0; i < kRW; ++i) {
     const int o = row0 + i;
     S[i] = (a.state_in && col_ok && o < Dv) ? a.state_in[st_base + (int64_t)o * F + j] : 0.f;
   }
@@ -189,7 +216,7 @@ __global__ void __launch_bounds__(kLT, 1) laplace_bwd_kernel(LapBwdArgs a) {
   for (int sc = 0; sc < nsc; ++sc) {
     const int t0 = sc * kLC, n = min(kLC, L - t0);
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
+    for (int i = 0; i < kRW; ++i) {
       const int o = row0 + i;
       if (col_ok && o < Dv) ckpt[((int64_t)sc * Dv + o) * F + j] = S[i];
     }
@@ -204,7 +231,7 @@ __global__ void __launch_bounds__(kLT, 1) laplace_bwd_kernel(LapBwdArgs a) {
 
   // ---- pass 2: sub-chunks backwards
 #pragma unroll
-  for (int i = 0; i < 32; ++i) {
+  for (int i = 0; i < kRW; ++i) {
     const int o = row0 + i;
     dS[i] = (a.dstate_out && col_ok && o < Dv) ? a.dstate_out[st_base + (int64_t)o * F + j] : 0.f;
   }
@@ -212,23 +239,25 @@ __global__ void __launch_bounds__(kLT, 1) laplace_bwd_kernel(LapBwdArgs a) {
   float pend_kc = 0.f, pend_ks = 0.f, pend_qc = 0.f, pend_qs = 0.f;
   auto finish = [&](int t, int pp, float kc, float ks, float qc, float qs) {
     // even lane: channel j / 2 (own = cos column, partner = sin column); this row half's
-    // part of the gradients (outputs zeroed by the entry point)
-    const float dk = colb[pp][0][j];
-    const float dq = colb[pp][1][j] * invD;
+    // part of the gradients (its two row groups summed in order; outputs zeroed by the
+    // entry point, so the two halves' additions commute exactly)
+    const float dk = colb[pp][0][0][j] + colb[pp][1][0][j];
+    const float dq = (colb[pp][0][1][j] + colb[pp][1][1][j]) * invD;
     const float dk2 = __shfl_xor_sync(0xffffffffu, dk, 1), dq2 = __shfl_xor_sync(0xffffffffu, dq, 1);
-    if (!(j & 1) && col_ok) {
+    if (rg == 0 && !(j & 1) && col_ok) {  // one row group writes the CTA's sums
       const int64_t gi = ((int64_t)bh * L + t) * D + (j >> 1);
       atomicAdd(a.dtk + gi, -ks * dk + kc * dk2);
       atomicAdd(a.dmk + gi, kc * dk + ks * dk2);
       atomicAdd(a.dtq + gi, -qs * dq + qc * dq2);
       atomicAdd(a.dmq + gi, qc * dq + qs * dq2);
     }
+    if (tid == 32 * 4) atomicAdd(&a.dbeta[(int64_t)bh * L + t], pbeta[pp][0] + pbeta[pp][1]);
   };
   for (int sc = nsc - 1; sc >= 0; --sc) {
     const int t0 = sc * kLC, n = min(kLC, L - t0);
     // the sub-chunk's states: checkpoint -> scratch slot 0, S_t -> slot r + 1
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
+    for (int i = 0; i < kRW; ++i) {
       const int o = row0 + i;
       S[i] = (col_ok && o < Dv) ? ckpt[((int64_t)sc * Dv + o) * F + j] : 0.f;
       if (col_ok && o < Dv) scr[(int64_t)o * F + j] = S[i];
@@ -239,12 +268,12 @@ __global__ void __launch_bounds__(kLT, 1) laplace_bwd_kernel(LapBwdArgs a) {
     for (int r = 0; r < n; ++r, par ^= 1) {
       float e;
       const float u = lap_fwd_token(S, red[par], st, r, j, cb, row0, lane, invD, &e);
-      if (cb == 0) {
+      if (cb == 0 && lane < kRW) {
         st.u[r][row0 + lane] = u;
         st.e[r][row0 + lane] = e;
       }
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
+      for (int i = 0; i < kRW; ++i) {
         const int o = row0 + i;
         if (col_ok && o < Dv) scr[((int64_t)(r + 1) * Dv + o) * F + j] = S[i];
       }
@@ -252,17 +281,17 @@ __global__ void __launch_bounds__(kLT, 1) laplace_bwd_kernel(LapBwdArgs a) {
     __syncthreads();  // u, e of the sub-chunk are in the stage
     for (int r = n - 1; r >= 0; --r, par ^= 1) {
       const int t = t0 + r;
-      float Sp[32];
+      float Sp[kRW];
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
+      for (int i = 0; i < kRW; ++i) {
         const int o = row0 + i;
         Sp[i] = (col_ok && o < Dv) ? scr[((int64_t)r * Dv + o) * F + j] : 0.f;
       }
       const float kap = (j & 1) ? st.ks[r][j >> 1] : st.kc[r][j >> 1];
       const float xi = (j & 1) ? st.qs[r][j >> 1] : st.qc[r][j >> 1];
-      float pq = 0.f, pw = 0.f, x1[32], x2[32];
+      float pq = 0.f, pw = 0.f, x1[kRW], x2[kRW];
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
+      for (int i = 0; i < kRW; ++i) {
         const float dO = st.dout[r][row0 + i];
         dS[i] = fmaf(dO * invD, xi, dS[i]);
         pq = fmaf(S[i], dO, pq);
@@ -270,34 +299,37 @@ __global__ void __launch_bounds__(kLT, 1) laplace_bwd_kernel(LapBwdArgs a) {
         x1[i] = dS[i] * kap;
         x2[i] = dS[i] * Sp[i];
       }
-      red[par][0][cb][row0 + lane] = reduce_scatter32(x1, lane);
-      red[par][1][cb][row0 + lane] = reduce_scatter32(x2, lane);
+      const float s1 = rs_rows<kRW>(x1, lane), s2 = rs_rows<kRW>(x2, lane);
+      const int o = row0 + (lane & (kRW - 1));
+      if (lane < kRW) {
+        red[par][0][cb][o] = s1;
+        red[par][1][cb][o] = s2;
+      }
       __syncthreads();
       if (pend_t >= 0) finish(pend_t, pend_par, pend_kc, pend_ks, pend_qc, pend_qs);
-      const int o = row0 + lane;
       const float du = red[par][0][0][o] + red[par][0][1][o] + red[par][0][2][o] + red[par][0][3][o];
       const float dr = red[par][1][0][o] + red[par][1][1][o] + red[par][1][2][o] + red[par][1][3][o];
       const float de = st.beta[r] * du;
       if (cb == 0) {
-        if (o < Dv) {
+        if (lane < kRW && o < Dv) {
           a.dv[row_base + (int64_t)t * Dv + o] = de;
           a.dld[row_base + (int64_t)t * Dv + o] = dr * st.rg[r][o];
         }
-        float p = (o < Dv) ? du * st.e[r][o] : 0.f;
+        float p = (lane < kRW && o < Dv) ? du * st.e[r][o] : 0.f;
 #pragma unroll
         for (int o2 = 16; o2 >= 1; o2 >>= 1) p += __shfl_xor_sync(0xffffffffu, p, o2);
-        if (lane == 0) atomicAdd(&a.dbeta[(int64_t)bh * L + t], p);
+        if (lane == 0) pbeta[par][rg] = p;  // summed over the row groups by finish
       }
       float pk = 0.f;
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
+      for (int i = 0; i < kRW; ++i) {
         const float de_i = __shfl_sync(0xffffffffu, de, i);
         dS[i] = fmaf(-de_i * invD, kap, st.r[r][row0 + i] * dS[i]);
         pk = fmaf(Sp[i], de_i, pk);
         S[i] = Sp[i];
       }
-      colb[par][0][j] = pw - pk * invD;
-      colb[par][1][j] = pq;
+      colb[par][rg][0][j] = pw - pk * invD;
+      colb[par][rg][1][j] = pq;
       pend_t = t;
       pend_par = par;
       pend_kc = st.kc[r][j >> 1];
@@ -310,7 +342,7 @@ __global__ void __launch_bounds__(kLT, 1) laplace_bwd_kernel(LapBwdArgs a) {
   if (pend_t >= 0) finish(pend_t, pend_par, pend_kc, pend_ks, pend_qc, pend_qs);
   if (a.dstate_in) {
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
+    for (int i = 0; i < kRW; ++i) {
       const int o = row0 + i;
       if (col_ok && o < Dv) a.dstate_in[st_base + (int64_t)o * F + j] = dS[i];
     }
@@ -328,25 +360,6 @@ __global__ void __launch_bounds__(kLT, 1) laplace_bwd_kernel(LapBwdArgs a) {
 constexpr int kWarpUnits = 2;
 constexpr unsigned kFull = 0xffffffffu;
 
-// Lane l returns the warp sum of x[l % ROWS] (ROWS = 16 or 32).
-template <int ROWS>
-__device__ __forceinline__ float rs_rows(float (&x)[ROWS], int lane) {
-  if (ROWS == 16) {
-#pragma unroll
-    for (int i = 0; i < 16; ++i) x[i] += __shfl_xor_sync(kFull, x[i], 16);
-  }
-#pragma unroll
-  for (int k = ROWS / 2; k >= 1; k >>= 1) {
-    const bool upper = (lane & k) != 0;
-#pragma unroll
-    for (int i = 0; i < k; ++i) {
-      const float send = upper ? x[i] : x[i + k];
-      const float keep = upper ? x[i + k] : x[i];
-      x[i] = keep + __shfl_xor_sync(kFull, send, k);
-    }
-  }
-  return x[0];
-}
 
 // Raw per-token values of one lane: its key (and query) channel, its row's v and log r,
 // beta.  Loaded a token ahead of their use.
@@ -610,7 +623,7 @@ extern "C" int dp_laplace_bwd(const void *theta_k, const void *logmag_k, const v
     }
   }
   a.nhalf = Dv > 32 ? 2 : 1;
-  const size_t smem = sizeof(LapStage) + sizeof(float) * (2 * 2 * 4 * 64 + 2 * 2 * 128);
+  const size_t smem = sizeof(LapStage) + sizeof(float) * (2 * 2 * 4 * 64 + 2 * 2 * 2 * 128 + 2 * 2);
   cudaError_t e = cudaFuncSetAttribute(laplace_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return set_error(DP_ERR_CUDA, std::string("dp_laplace_bwd smem attr: ") + cudaGetErrorString(e));
   laplace_bwd_kernel<<<B * H * a.nhalf, kLT, smem, as_stream(stream)>>>(a);
