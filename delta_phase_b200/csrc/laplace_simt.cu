@@ -133,14 +133,35 @@ laplace_simt_kernel(LapPtrs p, int in_dt, int beta_dt, const float *state_in, fl
     }
     __syncthreads();
 
-    // per-channel forward substitution (one thread per value channel)
-    for (int o = tid; o < Dv; o += kLapThreads) {
-      for (int m = 0; m < CI; ++m) {
-        const float lprev = m > 0 ? Lc[(m - 1) * vs + o] : 0.f;
-        float e = E[m * vs + o] - expf(lprev) * B0k[m * vs + o];
-        for (int s = 0; s < m; ++s)
-          e -= expf(lprev - Lc[s * vs + o]) * bb[s] * g[s * CI + m] * E[s * vs + o];
-        E[m * vs + o] = e;
+    // per-channel forward substitution
+    if (Dv <= 32) {
+      // few channels (small heads): one warp per channel, lane s forms the term of token
+      // s < m and a warp sum gives e_m, so the serial depth is CI sums, not CI^2 / 2 terms
+      const int lane = tid & 31, warp = tid >> 5;
+      for (int o = warp; o < Dv; o += kLapThreads / 32) {
+        const float lo = lane < CI ? Lc[lane * vs + o] : 0.f;
+        const float bo = lane < CI ? bb[lane] : 0.f;
+        float e_lane = 0.f;  // e of token `lane` once solved
+        for (int m = 0; m < CI; ++m) {
+          const float lprev = m > 0 ? Lc[(m - 1) * vs + o] : 0.f;
+          float term = lane < m ? expf(lprev - lo) * bo * g[lane * CI + m] * e_lane : 0.f;
+#pragma unroll
+          for (int off = 16; off > 0; off >>= 1) term += __shfl_xor_sync(0xffffffffu, term, off);
+          const float e = E[m * vs + o] - expf(lprev) * B0k[m * vs + o] - term;
+          if (lane == m) e_lane = e;
+        }
+        if (lane < CI) E[lane * vs + o] = e_lane;
+      }
+    } else {
+      // one thread per value channel
+      for (int o = tid; o < Dv; o += kLapThreads) {
+        for (int m = 0; m < CI; ++m) {
+          const float lprev = m > 0 ? Lc[(m - 1) * vs + o] : 0.f;
+          float e = E[m * vs + o] - expf(lprev) * B0k[m * vs + o];
+          for (int s = 0; s < m; ++s)
+            e -= expf(lprev - Lc[s * vs + o]) * bb[s] * g[s * CI + m] * E[s * vs + o];
+          E[m * vs + o] = e;
+        }
       }
     }
     __syncthreads();
