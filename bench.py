@@ -9,8 +9,11 @@ collective on the data path).
                     [--workload core|cbeta|train|decode|laplace|laplace-sp|ffn|lm]
 
 Multi-GPU: launch with torch.distributed.run (one process per GPU); rank 0 prints one
-JSON line.  ``--impl reference`` times the reference algorithm's CPU restatement
-(numpy port of the reference's chunkwise path) on the host cores.
+JSON line.  ``--impl reference`` times the reference's own chunkwise path on the host
+cores: its public ``delta_phase_chunkwise_fused`` (torch, float32, no_grad) from the
+unmodified install in ``baseline/_ref``, or, when that install is absent, the numpy port
+of the same path.  On one GPU the headline line also carries a ``secondary`` object with
+the other workloads (Laplace, FFN, decode step, LM prefill and decode), a few steps each.
 """
 from __future__ import annotations
 
@@ -131,6 +134,11 @@ def dist_setup(n_gpus):
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if world > 1:
         import torch.distributed as dist
+        # NCCL's communicator set-up lines (nranks, ranks, devices) go to stderr, so a reader
+        # can check the communicator spans every GPU of the run
+        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
@@ -141,6 +149,18 @@ def barrier(world):
     if world > 1:
         import torch.distributed as dist
         dist.barrier()
+
+
+def gather_over_ranks(x, world):
+    """Every rank's value of x (a float), in rank order."""
+    if world == 1:
+        return [x]
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    out = [torch.empty_like(t) for _ in range(world)]
+    dist.all_gather(out, t)
+    return [float(o.item()) for o in out]
 
 
 def max_over_ranks(x, world):
@@ -166,6 +186,54 @@ def cpu_core_sample(units=2, L=8192, D=64, C=64, seed=0):
     t0 = time.perf_counter()
     ocore.chunkwise_delta(tk, tq, v, beta, C, None, dtype=np.float32)
     return time.perf_counter() - t0, units * L
+
+
+REF_DIR = os.path.join(ROOT, "baseline", "_ref")
+
+
+def reference_chunkwise():
+    """The reference's own public entry point, ``delta_phase.kernels.delta_phase_chunkwise_fused``
+    (delta_phase/kernels/triton_chunk_delta.py:278-291), imported from the unmodified install
+    in baseline/_ref; None when that install is absent."""
+    if not os.path.isdir(os.path.join(REF_DIR, "delta_phase")):
+        return None
+    if REF_DIR not in sys.path:
+        sys.path.insert(0, REF_DIR)
+    try:
+        from delta_phase.kernels import delta_phase_chunkwise_fused
+    except Exception:
+        return None
+    return delta_phase_chunkwise_fused
+
+
+def ref_core_sample(fn, units=16, L=8192, D=64, C=64, seed=0):
+    """Time the reference's chunkwise forward (its own PyTorch path on CPU, float32, under
+    no_grad: the inference dispatch of delta_phase_chunkwise_fused) on `units` (b, h) units
+    of length L.  Returns (seconds, head_tokens)."""
+    import torch
+    torch.set_num_threads(os.cpu_count() or 1)
+    g = torch.Generator().manual_seed(seed)
+    tk = torch.rand(1, units, L, D, generator=g) * (2 * np.pi)
+    tq = torch.rand(1, units, L, D, generator=g) * (2 * np.pi)
+    v = torch.randn(1, units, L, D, generator=g)
+    beta = 2 * torch.sigmoid(torch.randn(1, units, L, generator=g))
+    with torch.no_grad():
+        t0 = time.perf_counter()
+        fn(tk, tq, v, beta, C, None)
+        return time.perf_counter() - t0, units * L
+
+
+def cpu_core_baseline(units, L=8192):
+    """One bounded CPU sample of the core workload: the reference's own code when it is
+    installed (kind "reference"), else the numpy port (kind "port").
+    Returns (seconds, head_tokens, kind, description)."""
+    fn = reference_chunkwise()
+    if fn is not None:
+        s, ht = ref_core_sample(fn, units=units, L=L)
+        return s, ht, "reference", ("reference delta_phase_chunkwise_fused (torch fp32 CPU, no_grad; "
+                                    "unmodified install in baseline/_ref)")
+    s, ht = cpu_core_sample(units=units, L=L)
+    return s, ht, "port", "numpy float32 port of the reference chunkwise path (oracle.core)"
 
 
 def repeat_for(fn, min_seconds=10.0):
@@ -282,7 +350,9 @@ def run_core(args, world, rank, local):
     stream.wait_stream(s_down)
     ev1.record(stream)
     torch.cuda.synchronize()
-    e2e_ms = max_over_ranks(ev0.elapsed_time(ev1) / e2e_steps, world)
+    e2e_rank_ms = ev0.elapsed_time(ev1) / e2e_steps
+    e2e_per_rank = gather_over_ranks(e2e_rank_ms, world)
+    e2e_ms = max(e2e_per_rank)
     h2d = sum(t.numel() * t.element_size() for t in host)
     d2h = out_h[0].numel() * 4 + M_h[0].numel() * 8
 
@@ -309,20 +379,22 @@ def run_core(args, world, rank, local):
                 "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
                 "path": "kernels.chunkwise_forward from pinned host buffers, out + M read back every step; "
                         "steps pipelined over two copy streams (inputs of step i+1 up while step i "
-                        "computes and its outputs come down)"},
+                        "computes and its outputs come down)",
+                "per_rank_ms_per_step": e2e_per_rank,
+                "per_rank_host_link_gbs": [(h2d + d2h) / (m / 1e3) / 1e9 for m in e2e_per_rank]},
         "gpu_launches": args.steps,
         "clocks": clk,
         "library": _capi.version(),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         parts = []
-        _, reps = repeat_for(lambda i: parts.append(cpu_core_sample(units=args.cpu_units, seed=i)), min_seconds=13.0)
+        _, reps = repeat_for(lambda i: parts.append(cpu_core_baseline(args.cpu_units)), min_seconds=10.0)
         secs, ht = sum(p[0] for p in parts), sum(p[1] for p in parts)  # timed regions only
         line["cpu_baseline"] = {
-            "value": ht / H / secs, "unit": "tokens/s", "cores": cpu_threads(), "kind": "port",
-            "sample": f"{reps} x {args.cpu_units} (b,h) units x L=8192 of the H=16 workload, numpy float32 "
-                      f"port of the reference chunkwise path (oracle.core), {secs:.1f} s; "
-                      "tokens/s = head-tokens / 16 / s"}
+            "value": ht / H / secs, "unit": "tokens/s", "cores": os.cpu_count() if parts[0][2] == "reference"
+            else cpu_threads(), "kind": parts[0][2],
+            "sample": f"{reps} x {args.cpu_units} (b,h) units x L=8192 of the H=16 workload, {parts[0][3]}, "
+                      f"{secs:.1f} s; tokens/s = head-tokens / 16 / s"}
     return line
 
 
@@ -339,6 +411,18 @@ def _timed(step, steps, warmup, stream):
     e1.record(stream)
     torch.cuda.synchronize()
     return e0.elapsed_time(e1) / steps
+
+
+def _timed_clk(step, steps, warmup, stream, local):
+    """_timed with the SM clocks and throttle reasons sampled during the timed steps."""
+    import torch
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    sampler.start()
+    ms = _timed(step, steps, 0, stream)
+    return ms, sampler.stop()
 
 
 def _line(metric, value, unit, args, world, ms, config, **extra):
@@ -467,8 +551,8 @@ def run_laplace(args, world, rank, local):
     beta = (2 * torch.sigmoid(torch.randn(B, H, L, device=dev, generator=g))).to(bf)
     out = torch.empty(B, H, L, D, device=dev)
     stream = torch.cuda.current_stream(dev)
-    ms = _timed(lambda: laplace_chunkwise(tk, None, tq, None, v, logr, beta, 64, None, out),
-                args.steps, args.warmup, stream)
+    ms, clk = _timed_clk(lambda: laplace_chunkwise(tk, None, tq, None, v, logr, beta, 64, None, out),
+                         args.steps, args.warmup, stream, local)
     ms = max_over_ranks(ms, world)
     alg = B * H * L * (4 * D * 2 + 2 + D * 4) + B * H * D * D * 8
     peaks, _ = load_peaks()
@@ -477,7 +561,7 @@ def run_laplace(args, world, rank, local):
                                    "global_batch": B * world, "seq_len": L},
                  roofline={"bound": "hbm", "achieved": alg / (ms / 1e3) / 1e9, "peak": peaks["hbm_gbs"],
                            "unit": "GB/s", "frac": alg / (ms / 1e3) / 1e9 / peaks["hbm_gbs"],
-                           "algorithmic_bytes_per_launch": alg})
+                           "algorithmic_bytes_per_launch": alg}, clocks=clk, gpu_launches=args.steps)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         from oracle import laplace as olap
         rng = np.random.default_rng(0)
@@ -564,7 +648,7 @@ def run_ffn(args, world, rank, local):
     x = torch.randn(tokens, d, device=dev).to(torch.bfloat16)
     stream = torch.cuda.current_stream(dev)
     with torch.no_grad():
-        ms = _timed(lambda: ffn(x), args.steps, args.warmup, stream)
+        ms, clk = _timed_clk(lambda: ffn(x), args.steps, args.warmup, stream, local)
     ms = max_over_ranks(ms, world)
     flops = tokens * (2 * 6 * d * d + 2 * d * d)  # folded combine GEMM + DCT-II GEMM
     peaks, _ = load_peaks()
@@ -576,7 +660,7 @@ def run_ffn(args, world, rank, local):
                            "frac": flops / (ms / 1e3) / 1e12 / peaks["bf16_tflops"],
                            "flops_per_launch": flops,
                            "note": "folded algorithm: 2*6d^2 + 2d^2 FLOP/token (the reference's own "
-                                   "algorithm needs 6*nb*d^2 + 12 d^2 = 37.7 MFLOP/token)"})
+                                   "algorithm needs 6*nb*d^2 + 12 d^2 = 37.7 MFLOP/token)"}, clocks=clk)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         from oracle import spectral as ospec
         params = {k: v.detach().float().cpu().numpy() for k, v in ffn.state_dict().items()}
@@ -612,14 +696,14 @@ def run_decode(args, world, rank, local, B=64, H=16, D=64):
                 decode_step(M, tk[t], tq[t], v[t], beta[t], out=out, state_out=M)
     torch.cuda.synchronize()
     stream = torch.cuda.current_stream(dev)
-    ms = _timed(graph.replay, args.steps, args.warmup, stream) / n
-    ms = max_over_ranks(ms, world)
+    ms, clk = _timed_clk(graph.replay, args.steps, args.warmup, stream, local)
+    ms = max_over_ranks(ms / n, world)
     byt = B * H * (2 * D * D * 8 + 3 * D * 4 + 4 + D * 4)
     peaks, _ = load_peaks()
     return _line("decode step latency (B*H=%d, d_k=64)" % (B * H), ms, "ms/step", args, world, ms,
                  {"workload": f"decode step, state ({B},{H},64,64) complex64, fp32 inputs, "
                               f"{n} steps per CUDA graph", "global_batch": B * world},
-                 higher_is_better=False, gpu_launches=n * args.steps,
+                 higher_is_better=False, gpu_launches=n * args.steps, clocks=clk,
                  roofline={"bound": "hbm", "achieved": byt / (ms / 1e3) / 1e9, "peak": peaks["hbm_gbs"],
                            "unit": "GB/s", "frac": byt / (ms / 1e3) / 1e9 / peaks["hbm_gbs"],
                            "algorithmic_bytes_per_launch": byt})
@@ -639,7 +723,7 @@ def run_lm(args, world, rank, local):
     stream = torch.cuda.current_stream(dev)
     with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
         torch.cuda.nvtx.range_push("lm_prefill")  # lets a profiler select the prefill passes
-        pre_ms = _timed(lambda: model(ids), max(1, args.steps // 4), 1, stream)
+        pre_ms, pre_clk = _timed_clk(lambda: model(ids), max(1, args.steps // 4), 1, stream, local)
         torch.cuda.nvtx.range_pop()
         _, states = model.forward_with_states(ids)
         st = [(None, M) for M in states]
@@ -653,7 +737,7 @@ def run_lm(args, world, rank, local):
     from delta_phase_b200 import DecodeGraph
     graph = DecodeGraph(model, B, states=[(None, M) for M in states], autocast_dtype=torch.bfloat16)
     torch.cuda.nvtx.range_push("lm_decode_graph")  # lets a profiler select the decode replays
-    dec_ms = _timed(lambda: graph.step(nxt), ndec, 3, stream)
+    dec_ms, dec_clk = _timed_clk(lambda: graph.step(nxt), ndec, 3, stream, local)
     torch.cuda.nvtx.range_pop()
     del graph
     pre_ms = max_over_ranks(pre_ms, world)
@@ -665,19 +749,21 @@ def run_lm(args, world, rank, local):
                   "global_batch": B * world, "seq_len": L, "model": "d1024-h16-l12"},
                  decode={"ms_per_token": dec_ms, "steps": ndec, "batch": B,
                          "path": "DecodeGraph (one CUDA graph per token step)",
-                         "eager_ms_per_token": dec_eager_ms})
+                         "eager_ms_per_token": dec_eager_ms, "clocks": dec_clk},
+                 clocks=pre_clk)
 
 
 def run_reference(args, world, rank):
-    """CPU arm: the numpy port of the reference chunkwise path on the host cores."""
+    """CPU arm: the reference's own chunkwise path (its public delta_phase_chunkwise_fused,
+    torch on the host cores) when installed in baseline/_ref, else the numpy port."""
     if rank != 0:
         return None
     B, H, L, D, C = (CORE[k] for k in ("B", "H", "L", "D", "C"))
     for _ in range(args.warmup):
-        cpu_core_sample(units=1, L=1024)
-    times, ht = [], 0
+        cpu_core_baseline(1, L=1024)
+    times, ht, kind, desc = [], 0, "port", ""
     for _ in range(args.steps):
-        s, ht = cpu_core_sample(units=args.cpu_units)
+        s, ht, kind, desc = cpu_core_baseline(args.cpu_units)
         times.append(s)
     secs = statistics.median(times)
     value = ht / H / secs
@@ -689,11 +775,40 @@ def run_reference(args, world, rank):
         "config": {"workload": "chunkwise complex delta-rule forward, B=8,H=16,L=8192,d_k=64,C=64 "
                                "(timed on a bounded sample of (b,h) units)",
                    "global_batch": B * world, "seq_len": L},
-        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cpu_threads(), "kind": "port",
-                         "sample": f"{args.cpu_units} (b,h) units x L=8192 per step, numpy float32 "
-                                   "port of the reference chunkwise path; tokens/s = head-tokens/16/s"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s",
+                         "cores": os.cpu_count() if kind == "reference" else cpu_threads(), "kind": kind,
+                         "sample": f"{args.cpu_units} (b,h) units x L=8192 per step (median of {args.steps}), "
+                                   f"{desc}; tokens/s = head-tokens/16/s"},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+
+
+def run_secondary(args, world, rank, local):
+    """The other workloads, each a few steps, for the headline line's `secondary` object:
+    Laplace (B=4, H=16, L=32768), the Lerp FFN (65536 x 1024), the decode step
+    (B*H = 1024) and the 12-layer LM (prefill 16 x 4096, decode B=16)."""
+    import copy
+
+    import torch
+    sub = copy.copy(args)
+    sub.no_cpu_baseline = True
+    sub.warmup = 3
+    out = {}
+    keep = ("metric", "value", "unit", "ms_per_step", "higher_is_better", "config", "roofline", "clocks",
+            "decode", "gpu_launches")
+    for name, fn, steps in (("laplace", run_laplace, 10), ("ffn", run_ffn, 10), ("decode", run_decode, 4),
+                            ("lm", run_lm, 8)):
+        sub.steps = steps
+        sub.seq_len = 32768
+        sub.decode_steps = 64
+        try:
+            line = fn(sub, world, rank, local)
+            out[name] = {k: line[k] for k in keep if k in line}
+        except Exception as e:  # a failing secondary must not hide the headline number
+            out[name] = {"error": f"{type(e).__name__}: {e}"[:300]}
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+    return out
 
 
 def main():
@@ -709,6 +824,8 @@ def main():
                     help="laplace workload only: sequence length (the headline is 32768; smaller for profiling)")
     ap.add_argument("--cpu-units", type=int, default=16)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--secondary", default="auto", choices=["auto", "on", "off"],
+                    help="core workload: also run the other workloads briefly (auto: on one GPU only)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -723,6 +840,8 @@ def main():
     run = {"core": run_core, "cbeta": run_cbeta, "train": run_train, "laplace": run_laplace, "laplace-sp": run_laplace_sp,
            "ffn": run_ffn, "decode": run_decode, "lm": run_lm}[args.workload]
     line = run(args, world, rank, local)
+    if args.workload == "core" and (args.secondary == "on" or (args.secondary == "auto" and world == 1)):
+        line["secondary"] = run_secondary(args, world, rank, local)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:

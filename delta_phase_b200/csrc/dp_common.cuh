@@ -126,9 +126,9 @@ int dispatch_dtype(int dt, F &&f) {
   }
 }
 
-// Phase -> (cos, sin).  float inputs use the accurate sincosf; 16-bit inputs use
-// the hardware approximation, whose error (~1e-6 on [-pi, pi] after CUDA's own
-// reduction) is far below the 16-bit input quantisation.
+// Phase -> (cos, sin) with CUDA's accurate sincosf, for every input type (the CUDA-core
+// kernels; the tensor-core kernels reduce the phase themselves and use the hardware
+// approximation, see fast_sincos below).
 template <typename T>
 __device__ __forceinline__ void phase_sincos(T th, float *s, float *c) {
   sincosf(to_f32(th), s, c);

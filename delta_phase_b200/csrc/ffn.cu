@@ -407,8 +407,11 @@ int launch_features(const void *x, bool bf, const float *hdct, void *z, int toke
   while ((1 << log2d) < d) ++log2d;
   const size_t smem = 4 * (size_t)d * sizeof(float);
   const int threads = d >= 256 ? 256 : d;
-  cudaFuncSetAttribute(ffn_features_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  cudaFuncSetAttribute(ffn_features_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  for (cudaError_t e : {cudaFuncSetAttribute(ffn_features_kernel<__nv_bfloat16>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                        cudaFuncSetAttribute(ffn_features_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)smem)})
+    if (e != cudaSuccess) return set_error(DP_ERR_CUDA, std::string("ffn features smem attr: ") + cudaGetErrorString(e));
   const int wgrid = (tokens + 7) / 8;
   // below about one warp per SM sub-partition the three branches of a token run on
   // three warps (ffn_features_split_kernel); above, one warp per token
@@ -572,25 +575,45 @@ small_gemm_kernel(const TA *__restrict__ A, int lda, const TB *__restrict__ B, i
     }
 }
 
-// Device address of g_ffn_scratch on the current device.  Looked up once per device,
-// with that device current, and cached; the lookup is the only set-up step.
+// Device address of g_ffn_scratch on the current device, looked up on every call with
+// that device current (the lookup allocates nothing; not caching it keeps it right after
+// a device reset, which can move the array).  The first call on a device also loads
+// every kernel this entry point can launch, for both dtypes: CUDA loads kernel code
+// lazily on first launch, and loading is itself a device allocation, so after this
+// first call no later call loads anything.
 int ffn_scratch_address(void **out) {
   static std::mutex mu;
-  static void *addr[64] = {nullptr};
+  static bool loaded[64] = {false};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return set_error(DP_ERR_CUDA, std::string("dp_ffn_fwd_noalloc: ") + cudaGetErrorString(e));
   if (dev < 0 || dev >= 64) return set_error(DP_ERR_UNSUPPORTED, "dp_ffn_fwd_noalloc: device ordinal >= 64");
-  std::lock_guard<std::mutex> lock(mu);
-  if (!addr[dev]) {
-    void *p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_ffn_scratch);
-    if (e != cudaSuccess || p == nullptr)
-      return set_error(DP_ERR_CUDA, std::string("dp_ffn_fwd_noalloc: cudaGetSymbolAddress failed: ") +
-                                        cudaGetErrorString(e));
-    addr[dev] = p;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (!loaded[dev]) {
+      const void *kernels[6] = {
+          reinterpret_cast<const void *>(small_gemm_kernel<float, float, float, true>),
+          reinterpret_cast<const void *>(small_gemm_kernel<float, float, float, false>),
+          reinterpret_cast<const void *>(small_gemm_kernel<__nv_bfloat16, __nv_bfloat16, float, true>),
+          reinterpret_cast<const void *>(small_gemm_kernel<__nv_bfloat16, __nv_bfloat16, __nv_bfloat16, false>),
+          reinterpret_cast<const void *>(ffn_features_kernel<float>),
+          reinterpret_cast<const void *>(ffn_features_kernel<__nv_bfloat16>)};
+      for (const void *k : kernels) {
+        cudaFuncAttributes attr;
+        e = cudaFuncGetAttributes(&attr, k);
+        if (e != cudaSuccess)
+          return set_error(DP_ERR_CUDA, std::string("dp_ffn_fwd_noalloc: kernel load failed: ") +
+                                            cudaGetErrorString(e));
+      }
+      loaded[dev] = true;
+    }
   }
-  *out = addr[dev];
+  void *p = nullptr;
+  e = cudaGetSymbolAddress(&p, g_ffn_scratch);
+  if (e != cudaSuccess || p == nullptr)
+    return set_error(DP_ERR_CUDA, std::string("dp_ffn_fwd_noalloc: cudaGetSymbolAddress failed: ") +
+                                      cudaGetErrorString(e));
+  *out = p;
   return DP_OK;
 }
 
@@ -606,7 +629,9 @@ int ffn_fwd_noalloc_typed(const T *x, const T *dct, const T *F, T *y, int tokens
   int log2d = 0;
   while ((1 << log2d) < d) ++log2d;
   const size_t smem = 4 * (size_t)d * sizeof(float);
-  cudaFuncSetAttribute(ffn_features_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaError_t e = cudaFuncSetAttribute(ffn_features_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess)
+    return set_error(DP_ERR_CUDA, std::string("ffn features smem attr: ") + cudaGetErrorString(e));
   ffn_features_kernel<T><<<tokens, d >= 256 ? 256 : d, smem, st>>>(x, hdct, z, d, log2d);
   rc = check_launch("ffn_features_kernel");
   if (rc != DP_OK) return rc;

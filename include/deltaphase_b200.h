@@ -304,9 +304,11 @@ DP_API int dp_gemm_skinny(const void *x, int64_t ldx, const void *w, const void 
  * scratch is a fixed 8 MiB array in the library's device image (held on every GPU that
  * loads the library until exit), and the GEMMs run on CUDA cores instead of cuBLAS.
  * Limit: tokens <= dp_ffn_noalloc_max_tokens(d, x_dtype) (511 at d = 1024 with bf16 x);
- * larger calls fail with DP_ERR_WORKSPACE.  The first call on a device looks up the
- * array's device address (cudaGetSymbolAddress), so make it before any stream capture.
- * Calls share the array: calls that overlap on the GPU race and must be serialised.
+ * larger calls fail with DP_ERR_WORKSPACE.  Every call looks up the array's device
+ * address (cudaGetSymbolAddress, no allocation); the first call on a device also loads the
+ * kernels of both dtypes (CUDA's lazy loading would otherwise load them on first launch),
+ * so make that first call before any stream capture.  Calls share the array and it keeps
+ * the last call's contents: calls that overlap on the GPU race and must be serialised.
  */
 DP_API int dp_ffn_fwd_noalloc(const void *x, int x_dtype, const void *dct, const void *F, void *y,
                               int tokens, int d, void *stream);

@@ -1,10 +1,12 @@
 """Generate the golden vectors in this directory from the reference itself.
 
 Runs the UNMODIFIED reference package (mcarbonell/delta-phase v1.3.0, imported
-read-only from REFERENCE_ROOT, default /root/reference) on small seeded inputs and
-stores inputs + reference outputs as .npz.  The oracle in ``oracle/`` is pinned
-against these files by tests/test_oracle_golden.py; the GPU parity tests reuse
-them.  Usage:  python tests/golden/make_golden.py [fixture ...]  (default: all of them)
+read-only from the directory given by the REFERENCE_ROOT environment variable, which
+is required) on small seeded inputs and stores inputs + reference outputs as .npz.  The
+oracle in ``oracle/`` is pinned against these files by tests/test_oracle_golden.py; the
+GPU parity tests reuse them.
+Usage:  REFERENCE_ROOT=<reference checkout> python tests/golden/make_golden.py [fixture ...]
+(default: all of them)
 """
 from __future__ import annotations
 
@@ -15,7 +17,10 @@ import numpy as np
 import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = os.environ.get("REFERENCE_ROOT", "/root/reference")
+REF = os.environ.get("REFERENCE_ROOT")
+if not REF or not os.path.isdir(os.path.join(REF, "delta_phase")):
+    sys.exit("make_golden.py: set REFERENCE_ROOT to a checkout of mcarbonell/delta-phase v1.3.0 "
+             "(the directory that holds the delta_phase package)")
 sys.path.insert(0, REF)
 
 from delta_phase.kernels.triton_chunk_delta import (  # noqa: E402

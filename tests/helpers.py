@@ -44,6 +44,12 @@ def rel_l2(a, b):
     return float(np.linalg.norm((a - b).ravel()) / (den if den > 0 else 1.0))
 
 
+def report(name, **errs):
+    """Prints the measured errors of a parity case (``pytest -s`` shows them), so the
+    margin against the tolerance is on record, not only pass / fail."""
+    print("PARITY %s %s" % (name, " ".join("%s=%.3e" % kv for kv in errs.items())), flush=True)
+
+
 # Tolerances of the specification: relative L2 against the reference's fp64 path.
 TOL_F32 = 2e-3   # float32 inputs, fp32 accumulation
 TOL_BF16 = 1e-2  # bfloat16 inputs, fp32 accumulation

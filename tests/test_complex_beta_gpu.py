@@ -17,7 +17,7 @@ from delta_phase_b200.kernels import chunkwise_forward, complex_beta_chunkwise, 
 from oracle import block as oblock
 from oracle import core as ocore
 
-from helpers import TOL_BF16, TOL_F32, load_golden, rel_l2, round_bf16, to_dev
+from helpers import TOL_BF16, TOL_F32, load_golden, rel_l2, report, round_bf16, to_dev
 
 pytestmark = pytest.mark.gpu
 
@@ -69,6 +69,21 @@ def test_tensor_core_bf16(L, init):
     ref_out, ref_M = ocore.complex_beta_recurrent(tk, tq, v, phi, M0)
     assert rel_l2(out, ref_out) < TOL_BF16
     assert rel_l2(M, ref_M) < TOL_BF16
+
+
+def test_tensor_core_bf16_full_length():
+    """One (b, h) unit at the headline length (L = 8192, d_k = 64, bf16, phi ~ N(0, 1) as in
+    the block) against the fp64 token loop (layers.py:346-360).  The isometric update lets
+    rounding errors add up along the sequence, so this is the longest-path check."""
+    B, H, L, D = 1, 1, 8192, 64
+    tk, tq, v, phi = (round_bf16(a) for a in cb_inputs(8192, B, H, L, D, phi_scale=1.0))
+    out, M = chunkwise_forward(to_dev(tk, torch.bfloat16), to_dev(tq, torch.bfloat16), to_dev(v, torch.bfloat16),
+                               to_dev(phi), 64, None, complex_beta=True)
+    ref_out, ref_M = ocore.complex_beta_recurrent(tk, tq, v, phi)
+    e_out, e_M = rel_l2(out, ref_out), rel_l2(M, ref_M)
+    report("cbeta_bf16_L8192", out=e_out, M=e_M)
+    assert e_out < TOL_BF16
+    assert e_M < TOL_BF16
 
 
 def test_tensor_core_bf16_phi():

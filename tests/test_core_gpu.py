@@ -12,7 +12,7 @@ import delta_phase_b200 as dp
 from delta_phase_b200.kernels import chunkwise_forward
 from oracle import core as ocore
 
-from helpers import TOL_BF16, TOL_F32, core_inputs, load_golden, rel_l2, round_bf16, to_dev
+from helpers import TOL_BF16, TOL_F32, core_inputs, load_golden, rel_l2, report, round_bf16, to_dev
 
 pytestmark = pytest.mark.gpu
 
@@ -147,8 +147,10 @@ def test_full_length_slice_parity_bf16():
     out, M = chunkwise_forward(to_dev(tk, torch.bfloat16), to_dev(tq, torch.bfloat16),
                                to_dev(v, torch.bfloat16), to_dev(beta, torch.bfloat16), 64)
     ref_out, ref_M = ocore.chunkwise_delta(tk, tq, v, beta, 64)
-    assert rel_l2(out, ref_out) < TOL_BF16
-    assert rel_l2(M, ref_M) < TOL_BF16
+    e_out, e_M = rel_l2(out, ref_out), rel_l2(M, ref_M)
+    report("core_bf16_L8192", out=e_out, M=e_M)
+    assert e_out < TOL_BF16
+    assert e_M < TOL_BF16
 
 
 def _b8h16_l8192_inputs(seed=0, B=8, H=16, L=8192, D=64):

@@ -9,7 +9,7 @@ import delta_phase_b200 as dp
 from delta_phase_b200 import _capi
 from oracle import laplace as olap
 
-from helpers import TOL_BF16, TOL_F32, load_golden, rel_l2, round_bf16, to_dev
+from helpers import TOL_BF16, TOL_F32, load_golden, rel_l2, report, round_bf16, to_dev
 
 pytestmark = pytest.mark.gpu
 
@@ -178,3 +178,28 @@ def test_tensor_core_large_factors_and_mixed_paths(fill):
     assert torch.isfinite(out).all()
     assert rel_l2(out, ref_out) < TOL_BF16
     assert rel_l2(M, ref_M) < TOL_BF16
+
+
+def test_tensor_core_full_length_config3():
+    """Two (b, h) units of the Laplace workload at full length: L = 32,768 (512 chunks of
+    compounding decay), d_k = d_v = 64, bf16, log r = -softplus(N(0, 1)), unit phasors,
+    against the fp64 chunkwise oracle (layers.py:481-561); the first 4096 tokens also
+    against the fp64 token loop (layers.py:563-583)."""
+    B, H, L, D = 1, 2, 32768, 64
+    tk, mk, tq, mq, v, logr, beta = _lap_bf16_inputs(32768, B, H, L, D, False)
+    out, M = dp.laplace_chunkwise(*[to_dev(a, torch.bfloat16) if a is not None else None
+                                    for a in (tk, mk, tq, mq, v, logr, beta)], 64)
+    K = np.exp(1j * tk.astype(np.float64))
+    Q = np.exp(1j * tq.astype(np.float64))
+    ref_out, ref_M = olap.laplace_chunkwise(K, Q, v, beta, np.exp(logr.astype(np.float64)), 64)
+    e_out, e_M = rel_l2(out, ref_out), rel_l2(M, ref_M)
+    n = 4096
+    seq_out, _ = olap.laplace_sequential(K[:, :, :n], Q[:, :, :n], v[:, :, :n], beta[:, :, :n],
+                                         np.exp(logr[:, :, :n].astype(np.float64)))
+    e_seq = rel_l2(out[:, :, :n], seq_out)
+    report("laplace_bf16_L32768", out=e_out, M=e_M, out_seq4096=e_seq)
+    assert torch.isfinite(out).all()
+    assert e_out < TOL_BF16
+    assert e_M < TOL_BF16
+    assert e_seq < TOL_BF16
+    assert _capi.device_error(clear=True) == 0

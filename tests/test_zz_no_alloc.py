@@ -59,3 +59,20 @@ def test_noalloc_rejects_sizes_beyond_its_scratch():
     dct = torch.zeros(d, d, device="cuda", dtype=torch.bfloat16)
     with pytest.raises(_capi.DeltaPhaseCudaError, match="static scratch"):
         _capi.ffn_fwd_noalloc(x, dct, F, torch.empty_like(x))
+
+
+@pytest.mark.parametrize("dtype,d,tol", [(torch.bfloat16, 1024, TOL_BF16), (torch.float32, 4096, TOL_F32)])
+def test_noalloc_at_its_token_limit(dtype, d, tol):
+    """Exactly dp_ffn_noalloc_max_tokens tokens: the largest call, where the features
+    (placed after the DCT projections at the next 256-byte boundary) reach closest to the
+    end of the fixed scratch."""
+    ffn = _ffn(d, 2, 5)
+    F, dct = ffn.folded(dtype)
+    tokens = _capi.ffn_noalloc_max_tokens(d, dtype)
+    for _ in range(2):
+        x = torch.randn(tokens, d, device="cuda").to(dtype)
+        ref = _workspace_ref(x, dct, F)
+        y = torch.empty_like(x)
+        _capi.ffn_fwd_noalloc(x, dct, F, y)
+        torch.cuda.synchronize()
+        assert rel_l2(y.float(), ref.float()) < tol
