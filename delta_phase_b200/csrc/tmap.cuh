@@ -36,9 +36,14 @@ struct ChunkMapDims {
 };
 
 // Encodes the map of one input (base 16-byte aligned, strides multiples of 8 elements, L
-// >= 64: the callers check these); returns false if the driver rejects it.
+// >= 64: the callers check these); returns false if the driver rejects it.  The box is
+// `box_channels` channels (64: a whole token row; 8: one 16-byte column group, for loads
+// straight into the core-matrix layout of an MMA operand) by 64 tokens.
+// With swizzle128 (box_channels = 64 only) the 16-byte chunk c of a token row r lands at
+// chunk c ^ (r % 8) of that row: threads that each read one row read conflict-free
+// (the destination must be 1024-byte aligned).
 inline bool encode_chunk_map(CUtensorMap *m, ChunkMapDims *dims_out, const void *base, int B, int H, int L,
-                             const SeqStrides &s) {
+                             const SeqStrides &s, int box_channels = 64, bool swizzle128 = false) {
   EncodeTiledFn enc = encode_tiled_fn();
   if (!enc) return false;
   const int64_t st[3] = {s.t, s.h, s.b};
@@ -53,7 +58,7 @@ inline bool encode_chunk_map(CUtensorMap *m, ChunkMapDims *dims_out, const void 
       }
   cuuint64_t dims[4] = {64, 0, 0, 0};
   cuuint64_t strides[3];
-  cuuint32_t box[4] = {64, 1, 1, 1};
+  cuuint32_t box[4] = {(cuuint32_t)box_channels, 1, 1, 1};
   for (int i = 0; i < 3; ++i) {
     dims[i + 1] = (cuuint64_t)ext[ord[i]];
     strides[i] = (cuuint64_t)st[ord[i]] * 2;
@@ -68,7 +73,8 @@ inline bool encode_chunk_map(CUtensorMap *m, ChunkMapDims *dims_out, const void 
   }
   const cuuint32_t estr[4] = {1, 1, 1, 1};
   return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void *>(base), dims, strides, box, estr,
-             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -86,6 +92,23 @@ __device__ __forceinline__ void tma_load_chunk(void *dst_smem, const CUtensorMap
       "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, "
       "%5}], [%6];" ::"r"(dst),
       "l"(m), "r"(0), "r"(c1), "r"(c2), "r"(c3), "r"(mb)
+      : "memory");
+}
+
+// Channels x0 .. x0 + 7 (x0 a multiple of 8: a 16-byte aligned start) of tokens t0 ..
+// t0 + 63 of head h, batch b, through a map encoded with box_channels = 8: 64 rows of 16
+// bytes, contiguous in shared memory; 1024 bytes counted on `bar`.
+__device__ __forceinline__ void tma_load_colgroup(void *dst_smem, const CUtensorMap *m, ChunkMapDims d, int x0, int t0,
+                                                  int h, int b, uint64_t *bar) {
+  const int c1 = d.t == 1 ? t0 : d.h == 1 ? h : b;
+  const int c2 = d.t == 2 ? t0 : d.h == 2 ? h : b;
+  const int c3 = d.t == 3 ? t0 : d.h == 3 ? h : b;
+  const uint32_t dst = static_cast<uint32_t>(__cvta_generic_to_shared(dst_smem));
+  const uint32_t mb = static_cast<uint32_t>(__cvta_generic_to_shared(bar));
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, "
+      "%5}], [%6];" ::"r"(dst),
+      "l"(m), "r"(x0), "r"(c1), "r"(c2), "r"(c3), "r"(mb)
       : "memory");
 }
 
