@@ -4,7 +4,7 @@
 
 Each ``csrc/*.cu`` file is compiled by nvcc in parallel and linked into one shared
 library with a plain C ABI (``include/deltaphase_b200.h``).  No torch headers are
-used: the library depends only on the CUDA runtime and cuBLAS.
+used: the library depends only on the CUDA runtime.
 """
 from __future__ import annotations
 
@@ -61,7 +61,7 @@ def build(verbose=False, extra=()):
                 print(log, file=sys.stderr)
     out = lib_path()
     tmp = out + ".tmp"
-    cmd = [nvcc(), *ARCH, "-shared", "-cudart", "shared", *objs, "-o", tmp, "-lcublas",
+    cmd = [nvcc(), *ARCH, "-shared", "-cudart", "shared", *objs, "-o", tmp,
            "-Xlinker", "-rpath,/usr/local/cuda/lib64"]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:

@@ -11,15 +11,15 @@
 //
 // The work of a chunk is split over three warp-specialised roles that run three chunks at
 // once, so the per-chunk latencies of the roles overlap instead of adding up:
-//   * phasor role (warps 0-3), chunk c + 2: one thread per row of [K; Q] computes its 64
-//     phasors from the TMA-loaded phases and stores the row straight into tensor memory
+//   * phasor role (warps 0-7), chunk c + 2: two threads per row of [K; Q] compute its 64
+//     phasors from the TMA-loaded phases and store the row straight into tensor memory
 //     (the A operand of G1 and G3: no shared-memory traffic for Q at all), the K rows also
 //     into a shared-memory tile (B of G1, A^T of G4); then G1 = [K; Q] K^T (tcgen05,
 //     M = 128, A from tensor memory);
-//   * inverse role (warps 4-7), chunk c + 1: A and P from the G1 rows, T = (I + A)^-1 in
+//   * inverse role (warps 8-11), chunk c + 1: A and P from the G1 rows, T = (I + A)^-1 in
 //     fp32 (16 x 16 diagonal blocks by forward substitution with the next row prefetched,
 //     the 16 -> 32 and 32 -> 64 block merges on warp-level tf32 MMA), bT in bf16;
-//   * chain role (warps 8-15), chunk c: the state recurrence.  S^T -> bf16; G3 = [K; Q] S^T
+//   * chain role (warps 12-19), chunk c: the state recurrence.  S^T -> bf16; G3 = [K; Q] S^T
 //     (M = 128, A from tensor memory); E; U = bT E (M = 64); G4: S^T += K^T U and
 //     G5: Q S^T += P U (M = 128, A starting 64 rows before P); the outputs of chunk c are
 //     read out of TMEM while the G3 of chunk c + 1 runs (two accumulator slots).
@@ -49,9 +49,9 @@ using namespace ptx;
 constexpr int kC = 64;   // tokens per chunk
 constexpr int kF = 128;  // key features (2 * d_k)
 constexpr int kDv = 64;  // value channels
-constexpr int kPhThreads = 128;   // warps 0-3
-constexpr int kInvThreads = 128;  // warps 4-7
-constexpr int kChThreads = 256;   // warps 8-15
+constexpr int kPhThreads = 256;   // warps 0-7
+constexpr int kInvThreads = 128;  // warps 8-11
+constexpr int kChThreads = 256;   // warps 12-19
 constexpr int kInvBase = kPhThreads, kChBase = kPhThreads + kInvThreads;
 constexpr int kThreads = kChBase + kChThreads;
 constexpr int BAR_PH = 1, BAR_INV = 2, BAR_CH = 3;
@@ -113,6 +113,15 @@ __device__ __forceinline__ void fast_sincos(float x, float *s, float *c) {
   float r = fmaf(-k, 6.28318548202514648f, x);
   r = fmaf(-k, -1.7484556e-07f, r);
   __sincosf(r, s, c);
+}
+
+// The bf16 pair (cos theta, sin theta) of a bf16 phase given as raw bits.  (Measured
+// alternatives, all slower on this kernel: the FMA-pipe polynomial poly_sincos for all or
+// half of the phases, and a shared-memory table of the bf16 phases.)
+__device__ __forceinline__ uint32_t phasor_word(uint32_t bits) {
+  float s, c;
+  fast_sincos(__uint_as_float(bits << 16), &s, &c);
+  return pack_bf16(c, s);
 }
 
 // One warp: D[16 x 16] = X[16 x K] Y[K x 16], X(i, k) = x[i * xs_i + k * xs_k],
@@ -193,16 +202,16 @@ __device__ __forceinline__ void issue_v_loads(const PipeMaps &m, const PipeArgs 
 }
 
 // ------------------------------------------------------------------------ phasor role
-// Thread r (warp r / 32 = its TMEM lane quarter) computes row r of [K; Q]: K row r for
-// r < 64, Q row r - 64 otherwise, from stage row r (theta_k rows, then theta_q rows).  The
-// stage is written by TMA with the 128-byte swizzle, so the 32 rows a warp reads at once
-// fall on distinct bank groups.
+// Warp w computes half w / 4 (channels 32 (w / 4) ..) of rows 32 (w % 4) .. + 31 of
+// [K; Q] (its TMEM lane quarter): row r is K row r for r < 64, Q row r - 64 otherwise,
+// from stage row r (theta_k rows, then theta_q rows).  The stage is written by TMA with
+// the 128-byte swizzle, so the 32 rows a warp reads at once fall on distinct bank groups.
 __device__ bool phasor_role(const PipeArgs &a, const PipeMaps &maps, uint8_t *smem, PipeBars *bars, uint32_t tmem,
                             int b, int h, int nchunks) {
-  const int tid = threadIdx.x, warp = tid >> 5;
-  const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+  const int tid = threadIdx.x, warp = tid >> 5, h2 = warp >> 2;
+  const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
   const int L = a.L;
-  const int r = tid, t = r & 63;
+  const int r = (warp & 3) * 32 + (tid & 31), t = r & 63;
   const bool is_k = r < kC;
   uint8_t *stage = smem + OFF_STAGE;
   const uint8_t *srow = stage + r * 128;
@@ -220,8 +229,7 @@ __device__ bool phasor_role(const PipeArgs &a, const PipeMaps &maps, uint8_t *sm
     if (group_any(!ok, BAR_PH, kPhThreads)) { ok = false; break; }
     consumed = c + 1;
     const bool valid = t < nvalid;
-#pragma unroll
-    for (int h2 = 0; h2 < 2; ++h2) {
+    {
       uint32_t w[32];
 #pragma unroll
       for (int s4 = 0; s4 < 4; ++s4) {
@@ -230,12 +238,8 @@ __device__ bool phasor_role(const PipeArgs &a, const PipeMaps &maps, uint8_t *sm
         const uint32_t rw[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          float s0_, c0_, s1_, c1_;
-          const __nv_bfloat162 th = *reinterpret_cast<const __nv_bfloat162 *>(&rw[i]);
-          fast_sincos(__low2float(th), &s0_, &c0_);
-          fast_sincos(__high2float(th), &s1_, &c1_);
-          w[8 * s4 + 2 * i] = valid ? pack_bf16(c0_, s0_) : 0u;
-          w[8 * s4 + 2 * i + 1] = valid ? pack_bf16(c1_, s1_) : 0u;
+          w[8 * s4 + 2 * i] = valid ? phasor_word(rw[i] & 0xFFFFu) : 0u;
+          w[8 * s4 + 2 * i + 1] = valid ? phasor_word(rw[i] >> 16) : 0u;
         }
       }
       tmem_st32(tmem + lane_base + COL_KQ + 64 * ks + 32 * h2, w);

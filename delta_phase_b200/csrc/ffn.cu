@@ -14,8 +14,6 @@
 // then needs 6d sincos and one (tokens x 6d) x (6d x d) GEMM per call -- half the
 // multiply-adds of the reference's three (tokens x nb d) x (nb d x d) combines at nb = 4,
 // and none of its six dense d x d transform GEMMs except the DCT.
-#include <cublas_v2.h>
-
 #include <array>
 #include <mutex>
 #include <string>
@@ -24,6 +22,11 @@
 #include "dp_common.cuh"
 
 namespace dp {
+
+bool gemm_tc_supported(int es, const void *A, const void *B, int M, int N, int K, int64_t lda, int64_t ldb);
+int gemm_tc(int es, const void *A, int64_t lda, const void *B, int64_t ldb, void *C, int64_t ldc, int M, int N, int K,
+            int epi, cudaStream_t stream, int64_t sin_off = 0);
+
 namespace {
 
 // ---------------------------------------------------------------- fold
@@ -132,15 +135,17 @@ ffn_features_kernel(const T *__restrict__ x, const float *__restrict__ hdct, T *
   __syncthreads();
   const float inv_sqrt_d = rsqrtf((float)d);
   T *zr = z + row * 6 * d;
-  const float *hd = hdct + row * d;
+  const float *hd = hdct ? hdct + row * d : nullptr;
   for (int i = tid; i < d; i += nt) {
     float s, c;
     sincosf(a[i] * inv_sqrt_d, &s, &c);
     zr[i] = from_f32<T>(c);
     zr[d + i] = from_f32<T>(s);
-    sincosf(hd[i], &s, &c);
-    zr[2 * d + i] = from_f32<T>(c);
-    zr[3 * d + i] = from_f32<T>(s);
+    if (hd) {
+      sincosf(hd[i], &s, &c);
+      zr[2 * d + i] = from_f32<T>(c);
+      zr[3 * d + i] = from_f32<T>(s);
+    }
     sincosf(ho[i], &s, &c);
     zr[4 * d + i] = from_f32<T>(c);
     zr[5 * d + i] = from_f32<T>(s);
@@ -338,7 +343,7 @@ ffn_features_warp_kernel(const T *__restrict__ x, const float *__restrict__ hdct
   for (int r = 0; r < R; ++r) hv[r] = v[r];
   T *zr = z + row * 6 * d;
   features_fwht<T, R>(v, zr, lane);
-  features_dct<T, R>(hdct + row * d, zr, lane);
+  if (hdct) features_dct<T, R>(hdct + row * d, zr, lane);
   features_haar<T, R>(hv, zr, lane, nullptr);
 }
 
@@ -356,7 +361,7 @@ ffn_features_split_kernel(const T *x, const float *hdct, T *__restrict__ z) {
   const int64_t row = blockIdx.x;
   T *zr = z + row * 6 * d;
   if (part == 1) {
-    features_dct<T, R>(hdct + row * d, zr, lane);
+    if (hdct) features_dct<T, R>(hdct + row * d, zr, lane);
     return;
   }
   __shared__ __align__(16) float haar_out[d];  // the Haar warp's staged outputs
@@ -368,14 +373,73 @@ ffn_features_split_kernel(const T *x, const float *hdct, T *__restrict__ z) {
     features_haar<T, R>(v, zr, lane, haar_out);
 }
 
-// ---------------------------------------------------------------- cuBLAS handles
-cublasHandle_t handle_for_device(int dev) {
-  static thread_local std::array<cublasHandle_t, 64> handles{};
-  if (dev < 0 || dev >= 64) return nullptr;
-  if (!handles[dev]) {
-    if (cublasCreate(&handles[dev]) != CUBLAS_STATUS_SUCCESS) handles[dev] = nullptr;
+// ---------------------------------------------------------------- GEMM helpers
+template <typename T>
+__device__ __forceinline__ float ld_f32(const T *p, int64_t i) { return to_f32(p[i]); }
+
+// C[m][n] (+)= sum_k A[m][k] B(k, n), B(k, n) = B[k ldb + n] or, if B_TRANS, B[n ldb + k]
+// (ACC: added to C).  64 x 64 output tile per CTA, 4 x 4 per thread, fp32 accumulation:
+// the CUDA-core GEMM for widths the tensor-core kernel does not take, and for the
+// allocation-free entry point.
+template <typename TA, typename TB, typename TC, bool B_TRANS, bool ACC = false>
+__global__ void __launch_bounds__(256)
+small_gemm_kernel(const TA *__restrict__ A, int lda, const TB *__restrict__ B, int ldb,
+                  TC *__restrict__ C, int ldc, int M, int N, int K) {
+  __shared__ float As[16][64 + 4];
+  __shared__ float Bs[16][64 + 4];
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  const int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
+  float acc[4][4] = {};
+  for (int k0 = 0; k0 < K; k0 += 16) {
+    for (int i = threadIdx.x; i < 64 * 16; i += 256) {
+      const int m = i >> 4, k = i & 15;
+      As[k][m] = (m0 + m < M && k0 + k < K) ? ld_f32(A, (int64_t)(m0 + m) * lda + k0 + k) : 0.f;
+      int n, kb;
+      if (B_TRANS) { n = i >> 4; kb = i & 15; } else { kb = i >> 6; n = i & 63; }
+      float bv = 0.f;
+      if (n0 + n < N && k0 + kb < K)
+        bv = B_TRANS ? ld_f32(B, (int64_t)(n0 + n) * ldb + k0 + kb) : ld_f32(B, (int64_t)(k0 + kb) * ldb + n0 + n);
+      Bs[kb][n] = bv;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      float a[4], b[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        a[i] = As[k][ty * 4 + i];
+        b[i] = Bs[k][tx * 4 + i];
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    }
+    __syncthreads();
   }
-  return handles[dev];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int m = m0 + ty * 4 + i, n = n0 + tx * 4 + j;
+      if (m < M && n < N) {
+        const float prev = ACC ? to_f32(C[(int64_t)m * ldc + n]) : 0.f;
+        C[(int64_t)m * ldc + n] = from_f32<TC>(prev + acc[i][j]);
+      }
+    }
+}
+
+// Ft (cols x rows) = F^T for F (rows x cols) row-major: 32 x 32 tiles through shared memory.
+template <typename T>
+__global__ void __launch_bounds__(256) transpose_kernel(const T *__restrict__ F, T *__restrict__ Ft, int rows,
+                                                        int cols) {
+  __shared__ T tile[32][33];
+  const int r0 = blockIdx.y * 32, c0 = blockIdx.x * 32, tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  for (int i = ty; i < 32; i += 8)
+    if (r0 + i < rows && c0 + tx < cols) tile[i][tx] = F[(int64_t)(r0 + i) * cols + c0 + tx];
+  __syncthreads();
+  for (int i = ty; i < 32; i += 8)
+    if (c0 + i < cols && r0 + tx < rows) Ft[(int64_t)(c0 + i) * rows + r0 + tx] = tile[tx][i];
 }
 
 }  // namespace
@@ -392,16 +456,36 @@ extern "C" int dp_ffn_fold(const float *logits, const float *mats, const float *
   return check_launch("ffn_fold_kernel");
 }
 
+namespace dp {
+namespace {
+// Workspace of dp_ffn_fwd: the DCT projections (tokens x d fp32), the features z
+// (tokens x 6d, x's dtype) and F^T (d x 6d, x's dtype; the tensor-core GEMM reads both of
+// its operands along K), each at a 256-byte boundary.
+struct FfnWorkspace {
+  size_t z_off, ft_off, total;
+};
+FfnWorkspace ffn_workspace_layout(int tokens, int d, int x_dtype) {
+  const size_t es = dtype_size(x_dtype);
+  auto up = [](size_t v) { return (v + 255) & ~(size_t)255; };
+  FfnWorkspace w;
+  w.z_off = up((size_t)tokens * d * sizeof(float));
+  w.ft_off = w.z_off + up((size_t)tokens * 6 * d * es);
+  w.total = w.ft_off + up((size_t)6 * d * d * es);
+  return w;
+}
+}  // namespace
+}  // namespace dp
+
 extern "C" size_t dp_ffn_workspace_size(int tokens, int d, int x_dtype) {
   if (tokens <= 0 || d <= 0) return 0;
-  const size_t es = dp::dtype_size(x_dtype);
-  return (size_t)tokens * d * sizeof(float) + (size_t)tokens * 6 * d * es + 256;
+  return dp::ffn_workspace_layout(tokens, d, x_dtype).total;
 }
 
 namespace dp {
 namespace {
 // z (tokens, 6d) = the sin / cos features of x given its DCT projections hdct (tokens, d)
-// float32; x, z of dtype bf16 (bf = true) or float32, hdct and z 16-byte aligned.
+// float32; x, z of dtype bf16 (bf = true) or float32, hdct and z 16-byte aligned.  With
+// hdct null the DCT branch's features are left alone (the DCT GEMM wrote them).
 int launch_features(const void *x, bool bf, const float *hdct, void *z, int tokens, int d, cudaStream_t st) {
   int log2d = 0;
   while ((1 << log2d) < d) ++log2d;
@@ -465,28 +549,76 @@ int ffn_fwd_impl(const void *x, int x_dtype, const void *dct, const void *F, voi
   DP_REQUIRE(reinterpret_cast<uintptr_t>(workspace) % 256 == 0, DP_ERR_MISALIGNED,
              "dp_ffn_fwd: workspace must be 256-byte aligned");
   cudaStream_t st = as_stream(stream);
-  int dev = 0;
-  cudaGetDevice(&dev);
-  cublasHandle_t hdl = handle_for_device(dev);
-  DP_REQUIRE(hdl != nullptr, DP_ERR_CUDA, "dp_ffn_fwd: cublasCreate failed");
-  cublasSetStream(hdl, st);
+  const FfnWorkspace wl = ffn_workspace_layout(tokens, d, x_dtype);
   float *hdct = static_cast<float *>(workspace);
-  void *z = static_cast<char *>(workspace) + (size_t)tokens * d * sizeof(float);
+  void *z = static_cast<char *>(workspace) + wl.z_off;
+  void *Ft = static_cast<char *>(workspace) + wl.ft_off;
   const bool bf = x_dtype == DP_BF16;
-  const cudaDataType_t ab = bf ? CUDA_R_16BF : CUDA_R_32F;
-  const cublasComputeType_t ct = bf ? CUBLAS_COMPUTE_32F : CUBLAS_COMPUTE_32F_FAST_TF32;
-  const float one = 1.f, zero = 0.f;
-  // Hdct (tokens x d, row-major) = X Cdct^T  <=>  col-major Hdct^T (d x tokens) = Cdct^T(d x d) X^T
-  cublasStatus_t cs = cublasGemmEx(hdl, CUBLAS_OP_T, CUBLAS_OP_N, d, tokens, d, &one, dct, ab, d, x,
-                                   ab, d, &zero, hdct, CUDA_R_32F, d, ct, CUBLAS_GEMM_DEFAULT);
-  DP_REQUIRE(cs == CUBLAS_STATUS_SUCCESS, DP_ERR_CUDA, "dp_ffn_fwd: DCT GEMM failed");
-  int rc = launch_features(x, bf, hdct, z, tokens, d, st);
+  const int es = bf ? 2 : 4;
+  // z and F^T sit at 256-byte boundaries of the workspace; x and dct must be 16-byte aligned
+  const bool tc = gemm_tc_supported(es, x, dct, tokens, d, d, d, d) &&
+                  gemm_tc_supported(es, workspace, workspace, tokens, d, 6 * d, 6 * d, 6 * d);
+  if (tc) {
+    // tcgen05 GEMMs (bf16, or fp32 read as tf32): Hdct = X Cdct^T, then Y (+)= Z F with F^T
+    // formed in the workspace.  For bf16 the DCT GEMM's epilogue writes the DCT branch's
+    // cos / sin into z itself (blocks 2 and 3 of each row), so the projections never reach
+    // HBM and the feature kernel computes the FWHT and Haar branches only.
+    int rc;
+    if (bf) {
+      rc = gemm_tc(es, x, d, dct, d, static_cast<__nv_bfloat16 *>(z) + 2 * d, 6 * d, tokens, d, d, 3, st, d);
+      if (rc != DP_OK) return rc;
+      rc = launch_features(x, bf, nullptr, z, tokens, d, st);
+    } else {
+      rc = gemm_tc(es, x, d, dct, d, hdct, d, tokens, d, d, 0, st);
+      if (rc != DP_OK) return rc;
+      rc = launch_features(x, bf, hdct, z, tokens, d, st);
+    }
+    if (rc != DP_OK) return rc;
+    dim3 tg((d + 31) / 32, (6 * d + 31) / 32);
+    if (bf)
+      transpose_kernel<__nv_bfloat16><<<tg, 256, 0, st>>>(static_cast<const __nv_bfloat16 *>(F),
+                                                          static_cast<__nv_bfloat16 *>(Ft), 6 * d, d);
+    else
+      transpose_kernel<float><<<tg, 256, 0, st>>>(static_cast<const float *>(F), static_cast<float *>(Ft), 6 * d, d);
+    rc = check_launch("transpose_kernel");
+    if (rc != DP_OK) return rc;
+    return gemm_tc(es, z, 6 * d, Ft, 6 * d, y, d, tokens, d, 6 * d, accumulate ? 2 : (bf ? 1 : 0), st);
+  }
+  // widths the tensor-core kernel does not take (d < 64): the CUDA-core GEMM
+  dim3 g1((d + 63) / 64, (tokens + 63) / 64);
+  dim3 g2((d + 63) / 64, (tokens + 63) / 64);
+  int rc;
+  if (bf) {
+    small_gemm_kernel<__nv_bfloat16, __nv_bfloat16, float, true><<<g1, 256, 0, st>>>(
+        static_cast<const __nv_bfloat16 *>(x), d, static_cast<const __nv_bfloat16 *>(dct), d, hdct, d, tokens, d, d);
+  } else {
+    small_gemm_kernel<float, float, float, true><<<g1, 256, 0, st>>>(static_cast<const float *>(x), d,
+                                                                      static_cast<const float *>(dct), d, hdct, d,
+                                                                      tokens, d, d);
+  }
+  rc = check_launch("small_gemm_kernel (DCT)");
   if (rc != DP_OK) return rc;
-  // Y (tokens x d) = Z (tokens x 6d) F (6d x d)  <=>  Y^T = F^T Z^T in column-major
-  cs = cublasGemmEx(hdl, CUBLAS_OP_N, CUBLAS_OP_N, d, tokens, 6 * d, &one, F, ab, d, z, ab, 6 * d,
-                    accumulate ? &one : &zero, y, accumulate ? CUDA_R_32F : ab, d, ct, CUBLAS_GEMM_DEFAULT);
-  DP_REQUIRE(cs == CUBLAS_STATUS_SUCCESS, DP_ERR_CUDA, "dp_ffn_fwd: combine GEMM failed");
-  return DP_OK;
+  rc = launch_features(x, bf, hdct, z, tokens, d, st);
+  if (rc != DP_OK) return rc;
+  if (accumulate) {
+    if (bf)
+      small_gemm_kernel<__nv_bfloat16, __nv_bfloat16, float, false, true><<<g2, 256, 0, st>>>(
+          static_cast<const __nv_bfloat16 *>(z), 6 * d, static_cast<const __nv_bfloat16 *>(F), d,
+          static_cast<float *>(y), d, tokens, d, 6 * d);
+    else
+      small_gemm_kernel<float, float, float, false, true><<<g2, 256, 0, st>>>(
+          static_cast<const float *>(z), 6 * d, static_cast<const float *>(F), d, static_cast<float *>(y), d, tokens,
+          d, 6 * d);
+  } else if (bf) {
+    small_gemm_kernel<__nv_bfloat16, __nv_bfloat16, __nv_bfloat16, false><<<g2, 256, 0, st>>>(
+        static_cast<const __nv_bfloat16 *>(z), 6 * d, static_cast<const __nv_bfloat16 *>(F), d,
+        static_cast<__nv_bfloat16 *>(y), d, tokens, d, 6 * d);
+  } else {
+    small_gemm_kernel<float, float, float, false><<<g2, 256, 0, st>>>(
+        static_cast<const float *>(z), 6 * d, static_cast<const float *>(F), d, static_cast<float *>(y), d, tokens,
+        d, 6 * d);
+  }
+  return check_launch("small_gemm_kernel (combine)");
 }
 }  // namespace
 }  // namespace dp
@@ -511,7 +643,7 @@ extern "C" int dp_ffn_fwd_residual(const void *x, int x_dtype, const void *dct, 
 // allocator.  This entry point takes its scratch -- the DCT projections and the
 // sin/cos features of the tokens -- from the fixed array below, which lives in the
 // library's device image, and it runs its two GEMMs with a CUDA-core kernel of this
-// file instead of cuBLAS (creating a cuBLAS handle allocates).
+// file (the tensor-core path of dp_ffn_fwd needs workspace for F^T).
 //
 // The array is kFfnScratchBytes on every GPU that loads the library, held until the
 // process exits.  All calls share it and it keeps the last call's contents; nothing in
@@ -524,56 +656,6 @@ namespace dp {
 namespace {
 
 constexpr size_t kFfnScratchBytes = 8u << 20;
-
-template <typename T>
-__device__ __forceinline__ float ld_f32(const T *p, int64_t i) { return to_f32(p[i]); }
-
-// C[m][n] = sum_k A[m][k] B(k, n), B(k, n) = B[k ldb + n] or, if B_TRANS, B[n ldb + k].
-// 64 x 64 output tile per CTA, 4 x 4 per thread, fp32 accumulation.
-template <typename TA, typename TB, typename TC, bool B_TRANS>
-__global__ void __launch_bounds__(256)
-small_gemm_kernel(const TA *__restrict__ A, int lda, const TB *__restrict__ B, int ldb,
-                  TC *__restrict__ C, int ldc, int M, int N, int K) {
-  __shared__ float As[16][64 + 4];
-  __shared__ float Bs[16][64 + 4];
-  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
-  const int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
-  float acc[4][4] = {};
-  for (int k0 = 0; k0 < K; k0 += 16) {
-    for (int i = threadIdx.x; i < 64 * 16; i += 256) {
-      const int m = i >> 4, k = i & 15;
-      As[k][m] = (m0 + m < M && k0 + k < K) ? ld_f32(A, (int64_t)(m0 + m) * lda + k0 + k) : 0.f;
-      int n, kb;
-      if (B_TRANS) { n = i >> 4; kb = i & 15; } else { kb = i >> 6; n = i & 63; }
-      float bv = 0.f;
-      if (n0 + n < N && k0 + kb < K)
-        bv = B_TRANS ? ld_f32(B, (int64_t)(n0 + n) * ldb + k0 + kb) : ld_f32(B, (int64_t)(k0 + kb) * ldb + n0 + n);
-      Bs[kb][n] = bv;
-    }
-    __syncthreads();
-#pragma unroll
-    for (int k = 0; k < 16; ++k) {
-      float a[4], b[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        a[i] = As[k][ty * 4 + i];
-        b[i] = Bs[k][tx * 4 + i];
-      }
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
-    }
-    __syncthreads();
-  }
-#pragma unroll
-  for (int i = 0; i < 4; ++i)
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int m = m0 + ty * 4 + i, n = n0 + tx * 4 + j;
-      if (m < M && n < N) C[(int64_t)m * ldc + n] = from_f32<TC>(acc[i][j]);
-    }
-}
 
 // Device address of g_ffn_scratch on the current device, looked up on every call with
 // that device current (the lookup allocates nothing; not caching it keeps it right after

@@ -256,6 +256,8 @@ DP_API size_t dp_ffn_workspace_size(int tokens, int d, int x_dtype);
  * dense bases of delta_phase/spectral.py:4-35.
  *   x, y (tokens, d), dct (d, d) = mat_dct, F (6d, d): all contiguous and of dtype
  *   x_dtype (DP_F32: TF32 tensor-core GEMMs; DP_BF16: bf16 GEMMs), fp32 accumulation.
+ *   Both GEMMs run on the library's own tcgen05 kernel for d >= 64 (bf16) or d >= 32
+ *   (float32), on a CUDA-core kernel below that; no library GEMM and no handle.
  *   d a power of two, 8 <= d <= 4096.  workspace >= dp_ffn_workspace_size() bytes,
  *   256-byte aligned.
  */
@@ -302,7 +304,8 @@ DP_API int dp_gemm_skinny(const void *x, int64_t ldx, const void *w, const void 
  * allocator owns the device heap, and decode loops that must not block on the
  * driver's allocator.  Same arguments and results as dp_ffn_fwd, but no workspace: the
  * scratch is a fixed 8 MiB array in the library's device image (held on every GPU that
- * loads the library until exit), and the GEMMs run on CUDA cores instead of cuBLAS.
+ * loads the library until exit), and the GEMMs run on CUDA cores (the tensor-core path
+ * of dp_ffn_fwd keeps F^T in its workspace).
  * Limit: tokens <= dp_ffn_noalloc_max_tokens(d, x_dtype) (511 at d = 1024 with bf16 x);
  * larger calls fail with DP_ERR_WORKSPACE.  Every call looks up the array's device
  * address (cudaGetSymbolAddress, no allocation); the first call on a device also loads the
