@@ -23,9 +23,10 @@
 
 namespace dp {
 
-bool gemm_tc_supported(int es, const void *A, const void *B, int M, int N, int K, int64_t lda, int64_t ldb);
+bool gemm_tc_supported(int es, const void *A, const void *B, int M, int N, int K, int64_t lda, int64_t ldb,
+                       int bn_max = 256);
 int gemm_tc(int es, const void *A, int64_t lda, const void *B, int64_t ldb, void *C, int64_t ldc, int M, int N, int K,
-            int epi, cudaStream_t stream, int64_t sin_off = 0);
+            int epi, cudaStream_t stream, int64_t sin_off = 0, int bn_max = 256);
 
 namespace {
 
@@ -556,7 +557,7 @@ int ffn_fwd_impl(const void *x, int x_dtype, const void *dct, const void *F, voi
   const bool bf = x_dtype == DP_BF16;
   const int es = bf ? 2 : 4;
   // z and F^T sit at 256-byte boundaries of the workspace; x and dct must be 16-byte aligned
-  const bool tc = gemm_tc_supported(es, x, dct, tokens, d, d, d, d) &&
+  const bool tc = gemm_tc_supported(es, x, dct, tokens, d, d, d, d, 128) &&
                   gemm_tc_supported(es, workspace, workspace, tokens, d, 6 * d, 6 * d, 6 * d);
   if (tc) {
     // tcgen05 GEMMs (bf16, or fp32 read as tf32): Hdct = X Cdct^T, then Y (+)= Z F with F^T
@@ -565,7 +566,7 @@ int ffn_fwd_impl(const void *x, int x_dtype, const void *dct, const void *F, voi
     // HBM and the feature kernel computes the FWHT and Haar branches only.
     int rc;
     if (bf) {
-      rc = gemm_tc(es, x, d, dct, d, static_cast<__nv_bfloat16 *>(z) + 2 * d, 6 * d, tokens, d, d, 3, st, d);
+      rc = gemm_tc(es, x, d, dct, d, static_cast<__nv_bfloat16 *>(z) + 2 * d, 6 * d, tokens, d, d, 3, st, d, 128);
       if (rc != DP_OK) return rc;
       rc = launch_features(x, bf, nullptr, z, tokens, d, st);
     } else {

@@ -16,8 +16,9 @@
 // three-stage ring through TMA (128-byte swizzle, one tiled copy per operand and slab, no
 // multicast); warp 1 issues the MMAs (two M = 128 halves sharing B, N = BN, one 32-byte K
 // step each, both operands K-major from shared memory) into the two halves of tensor
-// memory; warps 2-9 drain them (tcgen05.ld, one row per thread) while the producer
-// already streams the next tile's first slabs.  A 256-row tile halves the B traffic per
+// memory; warps 2-9 drain them (tcgen05.ld, one row per thread).  Tiles up to 128 wide
+// have two accumulators (the epilogue of one tile runs under the MMAs of the next); 256-wide
+// tiles one, the producer streaming the next tile's first slabs meanwhile.  A 256-row tile halves the B traffic per
 // output of a 128-row one (the operands come from L2 at about 9 TB/s at full MMA rate).
 // All waits are bounded: on expiry the kernel records DP_ERR_TIMEOUT, lets its copies and
 // MMAs land and frees tensor memory.
@@ -56,7 +57,9 @@ struct GemmArgs {
   int64_t ldc;
   int64_t sin_off;  // SINCOS_BF16: elements from a cos output to its sin
   int M, N, K;
-  int BN;           // tile width (a multiple of 16, <= 256, divides N)
+  int BN;           // tile width (a multiple of 32, <= 256, divides N)
+  int nbuf;         // accumulators: 2 if BN <= 128, else 1
+  int acc_cols;     // TMEM columns of one accumulator half (128 or 256)
   int n_tiles_n;    // N / BN
   int num_tiles;    // ceil(M / 256) * n_tiles_n
   int *err;
@@ -68,7 +71,7 @@ struct alignas(64) GemmMaps {
 
 struct GemmBars {
   uint64_t full[kStages], empty[kStages];
-  uint64_t acc_full, acc_empty;
+  uint64_t acc_full[2], acc_empty[2];
   uint32_t tmem_base;
   int fail;
 };
@@ -116,7 +119,8 @@ __device__ bool gemm_producer(const GemmArgs &g, const GemmMaps &maps, uint8_t *
 }
 
 // ------------------------------------------------------------------ MMA issuer (warp 1)
-// Rows 0..127 of a tile accumulate in TMEM columns 0..BN-1, rows 128..255 in 256..256+BN-1.
+// Accumulator b of a tile: rows 0..127 in TMEM columns (2 b) acc_cols .., rows 128..255 in
+// (2 b + 1) acc_cols ...
 template <typename T>
 __device__ bool gemm_mma(const GemmArgs &g, uint8_t *ops, GemmBars *bars, uint32_t tmem) {
   constexpr bool kTf32 = sizeof(T) == 4;
@@ -125,14 +129,18 @@ __device__ bool gemm_mma(const GemmArgs &g, uint8_t *ops, GemmBars *bars, uint32
   const uint32_t idesc = kTf32 ? idesc_tf32(128, g.BN, false, false) : idesc_bf16(128, g.BN, false, false);
   int it = 0, lt = 0;
   for (int tile = blockIdx.x; tile < g.num_tiles; tile += gridDim.x, ++lt) {
-    // the epilogue must have drained the accumulator (tile lt - 1)
-    if (lt >= 1 && !mbar_wait(&bars->acc_empty, (uint32_t)((lt - 1) & 1), kTimeoutNs)) return false;
+    const int buf = lt % g.nbuf;
+    // the epilogue must have drained this accumulator (tile lt - nbuf)
+    if (lt >= g.nbuf && !mbar_wait(&bars->acc_empty[buf], (uint32_t)((lt / g.nbuf - 1) & 1), kTimeoutNs)) {
+      if (lt > 0) mbar_wait(&bars->acc_full[(lt - 1) % g.nbuf], (uint32_t)(((lt - 1) / g.nbuf) & 1), kTimeoutNs);
+      return false;
+    }
     tc_fence_after();
     for (int ks = 0; ks < kslabs; ++ks, ++it) {
       const int s = it % kStages;
       if (!mbar_wait(&bars->full[s], (uint32_t)((it / kStages) & 1), kTimeoutNs)) {
-        mma_commit(&bars->acc_full);  // let the issued MMAs land before returning
-        mbar_wait(&bars->acc_full, (uint32_t)(lt & 1), kTimeoutNs);
+        mma_commit(&bars->acc_full[buf]);  // let the issued MMAs land before returning
+        mbar_wait(&bars->acc_full[buf], (uint32_t)((lt / g.nbuf) & 1), kTimeoutNs);
         return false;
       }
       tc_fence_after();
@@ -143,7 +151,7 @@ __device__ bool gemm_mma(const GemmArgs &g, uint8_t *ops, GemmBars *bars, uint32
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
           const uint64_t ad = desc_sw128(sa + half * (128 * kSlabBytes) + kk * 32);
-          const uint32_t d = tmem + (uint32_t)(half * kMaxBN);
+          const uint32_t d = tmem + (uint32_t)((2 * buf + half) * g.acc_cols);
           if (kTf32)
             mma_tf32_ss(d, ad, bd, idesc, (ks | kk) != 0);
           else
@@ -152,7 +160,7 @@ __device__ bool gemm_mma(const GemmArgs &g, uint8_t *ops, GemmBars *bars, uint32
       }
       mma_commit(&bars->empty[s]);  // the slab's buffers are free once these MMAs have read them
     }
-    mma_commit(&bars->acc_full);
+    mma_commit(&bars->acc_full[buf]);
   }
   return true;
 }
@@ -160,18 +168,20 @@ __device__ bool gemm_mma(const GemmArgs &g, uint8_t *ops, GemmBars *bars, uint32
 // ------------------------------------------------------------------ epilogue (warps 2-5)
 // Warp w (2..9): lane quarter q = w % 4 and tile half hh = (w - 2) / 4; thread l owns row
 // 128 hh + 32 q + l of every tile; 32 columns per tcgen05.ld, written as 16-byte stores.
+// (Sixteen epilogue warps measured slower.)
 template <int EPI>
 __device__ bool gemm_epilogue(const GemmArgs &g, GemmBars *bars, uint32_t tmem) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, q = warp & 3, hh = (warp - 2) >> 2;
   const uint32_t lane_base = (uint32_t)(q * 32) << 16;
   int lt = 0;
   for (int tile = blockIdx.x; tile < g.num_tiles; tile += gridDim.x, ++lt) {
+    const int buf = lt % g.nbuf;
     const int m = (tile / g.n_tiles_n) * kBM + 128 * hh + q * 32 + lane, n0 = (tile % g.n_tiles_n) * g.BN;
-    if (!mbar_wait(&bars->acc_full, (uint32_t)(lt & 1), kTimeoutNs)) return false;
+    if (!mbar_wait(&bars->acc_full[buf], (uint32_t)((lt / g.nbuf) & 1), kTimeoutNs)) return false;
     tc_fence_after();
     for (int j0 = 0; j0 < g.BN; j0 += 32) {
       float v[32];
-      tmem_ld32_sync(tmem + lane_base + (uint32_t)(hh * kMaxBN + j0), v);
+      tmem_ld32_sync(tmem + lane_base + (uint32_t)((2 * buf + hh) * g.acc_cols + j0), v);
       if (m < g.M) {
         if (EPI == SINCOS_BF16) {
           __nv_bfloat16 *row = static_cast<__nv_bfloat16 *>(g.c) + (int64_t)m * g.ldc + n0 + j0;
@@ -220,7 +230,7 @@ __device__ bool gemm_epilogue(const GemmArgs &g, GemmBars *bars, uint32_t tmem) 
       }
     }
     tc_fence_before();
-    mbar_arrive(&bars->acc_empty);
+    mbar_arrive(&bars->acc_empty[buf]);
   }
   return true;
 }
@@ -238,8 +248,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
       mbar_init(&bars->full[i], 1);
       mbar_init(&bars->empty[i], 1);
     }
-    mbar_init(&bars->acc_full, 1);
-    mbar_init(&bars->acc_empty, kThreads - kEpiBase);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars->acc_full[i], 1);
+      mbar_init(&bars->acc_empty[i], kThreads - kEpiBase);
+    }
     bars->fail = 0;
     fence_mbar_init();
   }
@@ -295,20 +307,24 @@ int sm_count() {
 // True if gemm_tc takes these sizes for elements of es bytes (2: bf16, 4: fp32 as tf32):
 // N a multiple of 32 up to 256 or of 256 beyond, K a multiple of the 128-byte slab, A, B
 // and their rows 16-byte aligned (TMA).
-bool gemm_tc_supported(int es, const void *A, const void *B, int M, int N, int K, int64_t lda, int64_t ldb) {
+bool gemm_tc_supported(int es, const void *A, const void *B, int M, int N, int K, int64_t lda, int64_t ldb,
+                       int bn_max) {
   const int bk = kSlabBytes / es;
   if (M <= 0 || N < 32 || K < bk || K % bk) return false;
   if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B)) & 15) return false;
-  if (N > kMaxBN ? N % kMaxBN : N % 32) return false;
+  if (bn_max != 128 && bn_max != 256) return false;
+  if (N > bn_max ? N % bn_max : N % 32) return false;
   return (lda * es) % 16 == 0 && (ldb * es) % 16 == 0;
 }
 
 // C (M x N) (epi) = A (M x K) B (N x K)^T, A and B row-major along K (strides lda, ldb
 // elements, 16-byte aligned), bf16 (es = 2) or fp32 read as tf32 (es = 4).  epi: 0 store
 // fp32, 1 store bf16, 2 add into fp32, 3 (bf16 only) cos to C and sin to C + sin_off.
+// bn_max (128 or 256): the widest tile; 128 double-buffers the accumulator (for epilogues
+// heavy enough to hide under the next tile's MMAs).
 int gemm_tc(int es, const void *A, int64_t lda, const void *B, int64_t ldb, void *C, int64_t ldc, int M, int N, int K,
-            int epi, cudaStream_t stream, int64_t sin_off) {
-  if (!gemm_tc_supported(es, A, B, M, N, K, lda, ldb))
+            int epi, cudaStream_t stream, int64_t sin_off, int bn_max) {
+  if (!gemm_tc_supported(es, A, B, M, N, K, lda, ldb, bn_max))
     return set_error(DP_ERR_UNSUPPORTED, "gemm_tc: unsupported sizes or alignment");
   GemmArgs g;
   memset(&g, 0, sizeof(g));
@@ -318,7 +334,9 @@ int gemm_tc(int es, const void *A, int64_t lda, const void *B, int64_t ldb, void
   g.M = M;
   g.N = N;
   g.K = K;
-  g.BN = N > kMaxBN ? kMaxBN : N;
+  g.BN = N > bn_max ? bn_max : N;
+  g.nbuf = g.BN <= 128 ? 2 : 1;
+  g.acc_cols = g.nbuf == 2 ? 128 : 256;
   g.n_tiles_n = N / g.BN;
   g.num_tiles = ((M + kBM - 1) / kBM) * g.n_tiles_n;
   g.err = device_error_ptr();
