@@ -54,7 +54,7 @@ constexpr int kInvThreads = 128;  // warps 8-11
 constexpr int kChThreads = 256;   // warps 12-19
 constexpr int kInvBase = kPhThreads, kChBase = kPhThreads + kInvThreads;
 constexpr int kThreads = kChBase + kChThreads;
-constexpr int BAR_PH = 1, BAR_INV = 2, BAR_CH = 3;
+constexpr int BAR_PH = 1, BAR_INV = 2, BAR_CH = 3, BAR_OUT = 4;
 constexpr int NKQ = 3;                           // K / Q tile ring
 constexpr uint64_t kTimeoutNs = 2000000000ull;   // 2 s per wait
 
@@ -65,16 +65,19 @@ constexpr int RG_64 = 8 * 128;
 constexpr int K_BYTES = 8 * RG_KQ;                   // K tile: 64 rows x 128 features
 constexpr int T64_BYTES = 8 * RG_64;                 // one 64 x 64 bf16 tile
 constexpr int OFF_K = 0;                             // [NKQ]
-constexpr int OFF_STAGE = OFF_K + NKQ * K_BYTES;     // theta_k rows 0..63, theta_q rows 64..127 (128-byte swizzle)
+constexpr int OFF_STAGE = OFF_K + NKQ * K_BYTES;     // [2] theta_k rows 0..63, theta_q rows 64..127 (128-byte swizzle)
 constexpr int STAGE_BYTES = 2 * kC * 128;
-static_assert(OFF_STAGE % 1024 == 0, "the swizzled stage must be 1024-byte aligned");
-constexpr int OFF_V = OFF_STAGE + STAGE_BYTES;       // [2] V, then E (column-group-major layout)
+static_assert(OFF_STAGE % 1024 == 0 && STAGE_BYTES % 1024 == 0, "the swizzled stages must be 1024-byte aligned");
+constexpr int OFF_V = OFF_STAGE + 2 * STAGE_BYTES;   // [2] V, then E (column-group-major layout)
 constexpr int OFF_BT = OFF_V + 2 * T64_BYTES;        // [2] bT = diag(beta) T, bf16
 constexpr int OFF_P = OFF_BT + 2 * T64_BYTES;        // [2] P; 8 KB of shared memory precede each slot
 constexpr int OFF_U = OFF_P + 2 * T64_BYTES;         // chain: U bf16
 constexpr int OFF_S0 = OFF_U + T64_BYTES;            // chain: S^T bf16 (128 x 64)
+constexpr int OFF_OUT = OFF_S0 + 16 * RG_64;         // chain: outputs of a chunk, two 64 x 32 fp32 boxes (128-byte swizzle)
+constexpr int OUT_BYTES = 2 * kC * 128;
+static_assert(OFF_OUT % 1024 == 0, "the swizzled output tile must be 1024-byte aligned");
 constexpr int LDA = 68;                              // padded fp32 row stride
-constexpr int OFF_AT = OFF_S0 + 16 * RG_64;          // inverse role: A^T fp32, At[k][i] = A[i][k]
+constexpr int OFF_AT = OFF_OUT + OUT_BYTES;          // inverse role: A^T fp32, At[k][i] = A[i][k]
 constexpr int OFF_TF = OFF_AT + kC * LDA * 4;        // inverse role: T = (I + A)^-1 fp32
 constexpr int LDZ = 36;
 constexpr int OFF_Z = OFF_TF + kC * LDA * 4;         // inverse role: block-merge scratch (32 x LDZ)
@@ -165,16 +168,18 @@ struct PipeArgs {
   int H, L;
   SeqStrides s_b, s_out;
   int *err;
-  ChunkMapDims dk, dq, dv;  // map dimension of token, head and batch of each input
+  ChunkMapDims dk, dq, dv, dout;  // map dimension of token, head and batch of each tensor
+  int out_tma;                    // outputs by bulk tensor stores through maps.out
 };
 
-// theta_k and theta_q with a 64 x 64 box; v with an 8 x 64 box (one column group).
+// theta_k and theta_q with a 64 x 64 box; v with an 8 x 64 box (one column group); out
+// with a 32 x 64 box.
 struct alignas(64) PipeMaps {
-  CUtensorMap tk, tq, v8;
+  CUtensorMap tk, tq, v8, out;
 };
 
 struct PipeBars {
-  uint64_t stage;            // theta stage loaded (phasor role)
+  uint64_t stage[2];         // theta stage loaded (phasor role)
   uint64_t g1_done;          // G1 complete (MMA commit) -> inverse role
   uint64_t g1_free;          // inverse role done with the G1 accumulator -> phasor role
   uint64_t kq_free[NKQ];     // chain MMAs done with a K / Q slot -> phasor role
@@ -182,6 +187,7 @@ struct PipeBars {
   uint64_t bt_free[2];       // chain MMAs done with a bT / P slot -> inverse role
   uint64_t v_full[2];        // V of a chunk loaded -> chain
   uint64_t chain_mma;        // chain MMA completion
+  uint64_t out_empty[2];     // outputs of an R3 slot read out of tensor memory -> chain
   uint32_t tmem_base;
   int fail;
 };
@@ -201,11 +207,49 @@ __device__ __forceinline__ void issue_v_loads(const PipeMaps &m, const PipeArgs 
   for (int g = 0; g < 8; ++g) tma_load_colgroup(vt + g * 1024, &m.v8, a.dv, 8 * g, c0, h, b, bar);
 }
 
+// Outputs of chunk cc (row t = token, columns 32 hc .. + 31 of the 64 value channels) from
+// R3 slot cc & 1 of tensor memory: into the output tile, then two bulk tensor stores issued
+// by `lead` (tokens past L are not written); with no output map, straight from registers.
+// Run by the four phasor warps of TMEM lane quarters 2 and 3 (barrier BAR_OUT); `lead`
+// frees the slot (out_empty) as soon as all four warps hold their rows in registers.
+__device__ __noinline__ void pipe_store_out(const PipeArgs &a, const PipeMaps &maps, uint8_t *smem, PipeBars *bars,
+                                            uint32_t taddr, int t, int hc, bool lead, int cc, int h, int b) {
+  const float inv64 = 1.0f / 64.0f;
+  const int tt = cc * kC + t;
+  float o[32];
+  tmem_ld32_sync(taddr, o);
+  tc_fence_before();
+  if (lead) bulk_wait_read_all();  // the previous chunk's stores have read the tile
+  group_sync(BAR_OUT, 128);
+  if (lead) mbar_arrive(&bars->out_empty[cc & 1]);
+  if (a.out_tma) {
+    uint8_t *orow = smem + OFF_OUT + hc * (kC * 128) + t * 128;
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      *reinterpret_cast<float4 *>(orow + ((i ^ (t & 7)) << 4)) =
+          make_float4(o[4 * i] * inv64, o[4 * i + 1] * inv64, o[4 * i + 2] * inv64, o[4 * i + 3] * inv64);
+    fence_proxy_async_smem();
+    group_sync(BAR_OUT, 128);
+    if (lead) {
+      tma_store_chunk(&maps.out, a.dout, smem + OFF_OUT, 0, cc * kC, h, b);
+      tma_store_chunk(&maps.out, a.dout, smem + OFF_OUT + kC * 128, 32, cc * kC, h, b);
+      bulk_commit_group();
+    }
+  } else if (tt < a.L) {
+    float *orow = a.out + b * a.s_out.b + h * a.s_out.h + (int64_t)tt * a.s_out.t + 32 * hc;
+#pragma unroll
+    for (int i = 0; i < 32; i += 4)
+      *reinterpret_cast<float4 *>(orow + i) =
+          make_float4(o[i] * inv64, o[i + 1] * inv64, o[i + 2] * inv64, o[i + 3] * inv64);
+  }
+}
+
 // ------------------------------------------------------------------------ phasor role
 // Warp w computes half w / 4 (channels 32 (w / 4) ..) of rows 32 (w % 4) .. + 31 of
 // [K; Q] (its TMEM lane quarter): row r is K row r for r < 64, Q row r - 64 otherwise,
 // from stage row r (theta_k rows, then theta_q rows).  The stage is written by TMA with
 // the 128-byte swizzle, so the 32 rows a warp reads at once fall on distinct bank groups.
+// Two stages: the phases of chunk c + 1 are in flight while chunk c's are used.
 __device__ bool phasor_role(const PipeArgs &a, const PipeMaps &maps, uint8_t *smem, PipeBars *bars, uint32_t tmem,
                             int b, int h, int nchunks) {
   const int tid = threadIdx.x, warp = tid >> 5, h2 = warp >> 2;
@@ -213,22 +257,37 @@ __device__ bool phasor_role(const PipeArgs &a, const PipeMaps &maps, uint8_t *sm
   const int L = a.L;
   const int r = (warp & 3) * 32 + (tid & 31), t = r & 63;
   const bool is_k = r < kC;
-  uint8_t *stage = smem + OFF_STAGE;
-  const uint8_t *srow = stage + r * 128;
   int issued = 0, consumed = 0, g1_issued = 0;
   bool ok = true;
-  if (tid == 0) issue_theta_loads(maps, a, stage, &bars->stage, 0, h, b);
-  issued = 1;
-  for (int c = 0; c < nchunks; ++c) {
-    const int ks = c % NKQ, t0 = c * kC, nvalid = min(kC, L - t0);
+  for (int k = 0; k < 2 && k < nchunks; ++k) {
+    if (tid == 0) issue_theta_loads(maps, a, smem + OFF_STAGE + k * STAGE_BYTES, &bars->stage[k], k * kC, h, b);
+    issued = k + 1;
+  }
+  // Iteration c makes the phasors of chunk c and, once the chain has finished chunk
+  // c - NKQ (kq_free: its last MMA, G5, has completed), stores that chunk's outputs; NKQ
+  // more iterations after the last chunk store the remaining outputs.
+  for (int c = 0; c < nchunks + NKQ; ++c) {
+    const int ks = c % NKQ, t0 = c * kC, nvalid = min(kC, L - t0), sb = c & 1;
     uint8_t *kt = smem + OFF_K + ks * K_BYTES;
+    uint8_t *stage = smem + OFF_STAGE + sb * STAGE_BYTES;
+    const uint8_t *srow = stage + r * 128;
+    const bool work = c < nchunks;
     if (tid == 0) {
       if (c >= NKQ) ok = mbar_wait(&bars->kq_free[ks], (uint32_t)((c / NKQ - 1) & 1), kTimeoutNs);
-      if (ok) ok = mbar_wait(&bars->stage, (uint32_t)(c & 1), kTimeoutNs);
+      if (ok && work) ok = mbar_wait(&bars->stage[sb], (uint32_t)((c >> 1) & 1), kTimeoutNs);
     }
     if (group_any(!ok, BAR_PH, kPhThreads)) { ok = false; break; }
+    if (c >= NKQ && (warp & 3) >= 2) {
+      const int cc = c - NKQ;
+      pipe_store_out(a, maps, smem, bars, tmem + lane_base + COL_R3 + 64 * (cc & 1) + 32 * h2,
+                     ((warp & 3) - 2) * 32 + (tid & 31), h2, tid == 64, cc, h, b);
+    }
+    if (!work) continue;
     consumed = c + 1;
-    const bool valid = t < nvalid;
+    // rows past L hold zero phasors.  The phasors are computed unconditionally and masked
+    // afterwards: a per-phasor select around the sincos makes the compiler branch around
+    // each one, which serialises them (twice the time of this loop, measured).
+    const uint32_t vmask = t < nvalid ? 0xFFFFFFFFu : 0u;
     {
       uint32_t w[32];
 #pragma unroll
@@ -238,8 +297,8 @@ __device__ bool phasor_role(const PipeArgs &a, const PipeMaps &maps, uint8_t *sm
         const uint32_t rw[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          w[8 * s4 + 2 * i] = valid ? phasor_word(rw[i] & 0xFFFFu) : 0u;
-          w[8 * s4 + 2 * i + 1] = valid ? phasor_word(rw[i] >> 16) : 0u;
+          w[8 * s4 + 2 * i] = phasor_word(rw[i] & 0xFFFFu) & vmask;
+          w[8 * s4 + 2 * i + 1] = phasor_word(rw[i] >> 16) & vmask;
         }
       }
       tmem_st32(tmem + lane_base + COL_KQ + 64 * ks + 32 * h2, w);
@@ -256,10 +315,10 @@ __device__ bool phasor_role(const PipeArgs &a, const PipeMaps &maps, uint8_t *sm
     tc_fence_before();
     group_sync(BAR_PH, kPhThreads);
     if (tid == 0) {
-      // the stage is free: the next chunk's phases; then G1 = [K; Q] K^T (A from TMEM)
-      if (c + 1 < nchunks) {
-        issue_theta_loads(maps, a, stage, &bars->stage, t0 + kC, h, b);
-        issued = c + 2;
+      // the stage is free: the phases of chunk c + 2; then G1 = [K; Q] K^T (A from TMEM)
+      if (c + 2 < nchunks) {
+        issue_theta_loads(maps, a, stage, &bars->stage[sb], t0 + 2 * kC, h, b);
+        issued = c + 3;
       }
       if (c >= 1) ok = mbar_wait(&bars->g1_free, (uint32_t)((c - 1) & 1), kTimeoutNs);
       if (ok) {
@@ -277,9 +336,10 @@ __device__ bool phasor_role(const PipeArgs &a, const PipeMaps &maps, uint8_t *sm
   }
   if (!ok && tid == 0) {
     // let this role's own copies and MMAs land before shared / tensor memory is released
-    for (int k = consumed; k < issued; ++k) mbar_wait(&bars->stage, (uint32_t)(k & 1), kTimeoutNs);
+    for (int k = consumed; k < issued; ++k) mbar_wait(&bars->stage[k & 1], (uint32_t)((k >> 1) & 1), kTimeoutNs);
     if (g1_issued > 0) mbar_wait(&bars->g1_done, (uint32_t)((g1_issued - 1) & 1), kTimeoutNs);
   }
+  if (tid == 64 && a.out_tma) bulk_wait_all();  // the output stores are complete
   return ok;
 }
 
@@ -318,7 +378,7 @@ __device__ bool inverse_role(const PipeArgs &a, uint8_t *smem, PipeBars *bars, u
     if (iw < 2) {
       const int k = iw * 32 + lane;
       const float bk = bs[k] * inv64;
-#pragma unroll
+#pragma unroll 1
       for (int hf = 0; hf < 2; ++hf) {
         float g[32];
         tmem_ld32_sync(tmem + lane_base + COL_G1 + 32 * hf, g);
@@ -335,7 +395,7 @@ __device__ bool inverse_role(const PipeArgs &a, uint8_t *smem, PipeBars *bars, u
       }
     } else {
       const int t = (iw - 2) * 32 + lane;
-#pragma unroll
+#pragma unroll 1
       for (int hf = 0; hf < 2; ++hf) {
         float p[32];
         tmem_ld32_sync(tmem + lane_base + COL_G1 + 32 * hf, p);
@@ -447,7 +507,6 @@ __device__ bool chain_role(const PipeArgs &a, const PipeMaps &maps, uint8_t *sme
   const int ctid = threadIdx.x - kChBase, cw = ctid >> 5, lane = ctid & 31;
   const int q = cw & 3, hc = cw >> 2;
   const uint32_t lane_base = (uint32_t)(q * 32) << 16;
-  const int L = a.L;
   uint8_t *ub = smem + OFF_U;
   uint8_t *s0 = smem + OFF_S0;
   const float inv64 = 1.0f / 64.0f;
@@ -467,26 +526,36 @@ __device__ bool chain_role(const PipeArgs &a, const PipeMaps &maps, uint8_t *sme
   }
   tmem_st_wait();
   tc_fence_before();
-  if (ctid == 0 && nchunks > 0) issue_v_loads(maps, a, smem + OFF_V, &bars->v_full[0], 0, h, b);
   group_sync(BAR_CH, kChThreads);
 
+  // Thread 32 (warp 1) is the role's input thread: it issues the V loads and waits for the
+  // next chunk's bT / P and V while thread 0 issues and waits for this chunk's state MMAs,
+  // so the chain never starts a chunk with those waits.
+  const bool in_thread = ctid == 32;
   uint32_t cm_phase = 0;
-  int v_issued = nchunks > 0 ? 1 : 0, v_consumed = 0;
-  bool ok = true, mma_pending = false;
-
-  // outputs of chunk cc from R3 slot cc & 1, rows 64.. (quarters 2, 3)
-  auto store_out = [&](int cc) {
-    if (q < 2) return;
-    const int t = (q - 2) * 32 + lane, tt = cc * kC + t;
-    float o[32];
-    tmem_ld32_sync(tmem + lane_base + COL_R3 + 64 * (cc & 1) + 32 * hc, o);
-    if (tt < L) {
-      float *orow = a.out + b * a.s_out.b + h * a.s_out.h + (int64_t)tt * a.s_out.t + 32 * hc;
-#pragma unroll
-      for (int i = 0; i < 32; i += 4)
-        *reinterpret_cast<float4 *>(orow + i) =
-            make_float4(o[i] * inv64, o[i + 1] * inv64, o[i + 2] * inv64, o[i + 3] * inv64);
+  int v_issued = 0, v_consumed = 0, cm_pending = 0;
+  bool ok = true;
+  if (in_thread) {
+    for (int k = 0; k < 2 && k < nchunks; ++k) {
+      issue_v_loads(maps, a, smem + OFF_V + k * T64_BYTES, &bars->v_full[k], k * kC, h, b);
+      v_issued = k + 1;
     }
+    if (nchunks > 0) {
+      ok = mbar_wait(&bars->bt_full[0], 0u, kTimeoutNs);
+      if (ok) ok = mbar_wait(&bars->v_full[0], 0u, kTimeoutNs);
+    }
+  }
+
+  // thread 0: commit the MMAs issued so far on chain_mma and wait for them
+  auto mma_sync = [&]() {
+    mma_commit(&bars->chain_mma);
+    ++cm_pending;
+    const bool r = mbar_wait(&bars->chain_mma, cm_phase, kTimeoutNs);
+    if (r) {
+      cm_phase ^= 1;
+      --cm_pending;
+    }
+    return r;
   };
 
   for (int c = 0; c < nchunks; ++c) {
@@ -497,15 +566,7 @@ __device__ bool chain_role(const PipeArgs &a, const PipeMaps &maps, uint8_t *sme
     uint8_t *pb = smem + OFF_P + gs * T64_BYTES;
     const uint32_t r3 = COL_R3 + 64 * gs;
 
-    if (ctid == 0) {
-      // V of the next chunk into the other slot (its last reader, U of chunk c - 1, is done)
-      if (c + 1 < nchunks) {
-        issue_v_loads(maps, a, smem + OFF_V + (gs ^ 1) * T64_BYTES, &bars->v_full[gs ^ 1], (c + 1) * kC, h, b);
-        v_issued = c + 2;
-      }
-      ok = mbar_wait(&bars->bt_full[gs], (uint32_t)((c >> 1) & 1), kTimeoutNs);
-      if (ok) ok = mbar_wait(&bars->v_full[gs], (uint32_t)((c >> 1) & 1), kTimeoutNs);
-    }
+    // bT / P and V of chunk c are present; S^T holds the state at its start
     if (group_any(!ok, BAR_CH, kChThreads)) { ok = false; break; }
     v_consumed = c + 1;
     tc_fence_after();
@@ -534,15 +595,9 @@ __device__ bool chain_role(const PipeArgs &a, const PipeMaps &maps, uint8_t *sme
       for (int kk = 0; kk < 8; ++kk)
         mma_f16_ts(tmem + r3, tmem + COL_KQ + 64 * ks + 8 * kk, make_desc(ss + kk * 2 * RG_64, RG_64, 128),
                    idesc_bf16(128, 64, false, true), kk > 0);
-      mma_commit(&bars->chain_mma);
+      ok = mma_sync();
     }
-    mma_pending = true;
-    // ---- while G3 runs: the outputs of the previous chunk (its G5 completed)
-    if (c > 0) store_out(c - 1);
-    if (ctid == 0) ok = mbar_wait(&bars->chain_mma, cm_phase, kTimeoutNs);
     if (group_any(!ok, BAR_CH, kChThreads)) { ok = false; break; }
-    cm_phase ^= 1;
-    mma_pending = false;
     tc_fence_after();
 
     // ---- C3: E = V - K S^T / 64 -> bf16 in place of V (row t = lane of quarters 0, 1)
@@ -563,8 +618,8 @@ __device__ bool chain_role(const PipeArgs &a, const PipeMaps &maps, uint8_t *sme
         }
         *vp = make_uint4(ew[0], ew[1], ew[2], ew[3]);
       }
+      fence_proxy_async_smem();
     }
-    fence_proxy_async_smem();
     tc_fence_before();
     group_sync(BAR_CH, kChThreads);
 
@@ -577,13 +632,9 @@ __device__ bool chain_role(const PipeArgs &a, const PipeMaps &maps, uint8_t *sme
       for (int kk = 0; kk < 4; ++kk)
         mma_f16_ss(tmem + COL_RU, make_desc(sb + kk * 256, 128, RG_64), make_desc(se + kk * 256, 128, 1024),
                    idesc_bf16(64, 64, false, true), kk > 0);
-      mma_commit(&bars->chain_mma);
+      ok = mma_sync();
     }
-    mma_pending = true;
-    if (ctid == 0) ok = mbar_wait(&bars->chain_mma, cm_phase, kTimeoutNs);
     if (group_any(!ok, BAR_CH, kChThreads)) { ok = false; break; }
-    cm_phase ^= 1;
-    mma_pending = false;
     tc_fence_after();
 
     // ---- C3c: U -> bf16 operand tile (M = 64 rows: row 16 q + lane in lanes < 16)
@@ -605,32 +656,52 @@ __device__ bool chain_role(const PipeArgs &a, const PipeMaps &maps, uint8_t *sme
     tc_fence_before();
     group_sync(BAR_CH, kChThreads);
 
-    // ---- C4: G4 S^T += K^T U (M = 128) and G5 R3 += [X; P] U (M = 128, A starting 8 KB
-    //      before P: rows 64.. of R3 (Q S^T) gain P U, rows 0.. (K S^T, used) are
-    //      don't-care).  The commits also free this chunk's K / Q and bT / P slots.
+    // ---- C4: G4 S^T += K^T U (M = 128), committed and waited for on its own (the next chunk
+    //      needs only the state), then G5 R3 += [X; P] U (M = 128, A starting 8 KB before P:
+    //      rows 64.. of R3 (Q S^T) gain P U, rows 0.. (K S^T, used) are don't-care).  The
+    //      commits after G5 free this chunk's K / Q and bT / P slots.
     if (ctid == 0) {
       tc_fence_after();
       const uint32_t sk = smem_u32(kt), su = smem_u32(ub), sp = smem_u32(pb) - 8 * RG_64;
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
-        const uint64_t ud = make_desc(su + kk * 2 * RG_64, RG_64, 128);
-        mma_f16_ss(tmem + COL_S, make_desc(sk + kk * 2 * RG_KQ, RG_KQ, 128), ud, idesc_bf16(128, 64, true, true), 1u);
-        mma_f16_ss(tmem + r3, make_desc(sp + kk * 256, 128, RG_64), ud, idesc_bf16(128, 64, false, true), 1u);
-      }
+      for (int kk = 0; kk < 4; ++kk)
+        mma_f16_ss(tmem + COL_S, make_desc(sk + kk * 2 * RG_KQ, RG_KQ, 128), make_desc(su + kk * 2 * RG_64, RG_64, 128),
+                   idesc_bf16(128, 64, true, true), 1u);
       mma_commit(&bars->chain_mma);
+      ++cm_pending;
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk)
+        mma_f16_ss(tmem + r3, make_desc(sp + kk * 256, 128, RG_64), make_desc(su + kk * 2 * RG_64, RG_64, 128),
+                   idesc_bf16(128, 64, false, true), 1u);
       mma_commit(&bars->kq_free[ks]);
       mma_commit(&bars->bt_free[gs]);
+      ok = mbar_wait(&bars->chain_mma, cm_phase, kTimeoutNs);
+      if (ok) {
+        cm_phase ^= 1;
+        --cm_pending;
+      }
+    } else if (in_thread) {
+      // V of chunk c + 2 into this chunk's slot (its last reader, U of chunk c, is done);
+      // then the inputs of chunk c + 1
+      if (c + 2 < nchunks) {
+        issue_v_loads(maps, a, vt, &bars->v_full[gs], (c + 2) * kC, h, b);
+        v_issued = c + 3;
+      }
+      if (c + 1 < nchunks) {
+        ok = mbar_wait(&bars->bt_full[gs ^ 1], (uint32_t)(((c + 1) >> 1) & 1), kTimeoutNs);
+        if (ok) ok = mbar_wait(&bars->v_full[gs ^ 1], (uint32_t)(((c + 1) >> 1) & 1), kTimeoutNs);
+        // R3 slot of chunk c + 1: the outputs of chunk c - 1 have been read out of it
+        if (ok && c >= 1) ok = mbar_wait(&bars->out_empty[gs ^ 1], (uint32_t)(((c - 1) >> 1) & 1), kTimeoutNs);
+      }
     }
-    mma_pending = true;
-    if (ctid == 0) ok = mbar_wait(&bars->chain_mma, cm_phase, kTimeoutNs);
-    if (group_any(!ok, BAR_CH, kChThreads)) { ok = false; break; }
-    cm_phase ^= 1;
-    mma_pending = false;
-    tc_fence_after();
   }
 
   if (ok) {
-    if (nchunks > 0) store_out(nchunks - 1);
+    // the last chunk's state update (G4) has completed (thread 0's wait)
+    if (group_any(!ok, BAR_CH, kChThreads)) ok = false;
+    tc_fence_after();
+  }
+  if (ok) {
     // final state: TMEM S^T -> complex64 state (row o, interleaved column j)
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
@@ -641,7 +712,13 @@ __device__ bool chain_role(const PipeArgs &a, const PipeMaps &maps, uint8_t *sme
       for (int i = 0; i < 16; ++i) a.state_out[sbase + (int64_t)(32 * hc + 16 * u + i) * kF + j] = sv[i];
     }
   } else if (ctid == 0) {
-    if (mma_pending) mbar_wait(&bars->chain_mma, cm_phase, kTimeoutNs);
+    // let this role's MMAs finish before shared and tensor memory are released
+    mma_commit(&bars->chain_mma);  // arrives once every MMA issued so far has completed
+    for (int k = 0; k <= cm_pending; ++k) {
+      if (!mbar_wait(&bars->chain_mma, cm_phase, kTimeoutNs)) break;
+      cm_phase ^= 1;
+    }
+  } else if (in_thread) {
     for (int k = v_consumed; k < v_issued; ++k) mbar_wait(&bars->v_full[k & 1], (uint32_t)((k >> 1) & 1), kTimeoutNs);
   }
   return ok;
@@ -657,7 +734,8 @@ __global__ void __launch_bounds__(kThreads, 1) core_pipe_kernel(const __grid_con
   const int nchunks = (a.L + kC - 1) / kC;
 
   if (tid == 0) {
-    mbar_init(&bars->stage, 1);
+    mbar_init(&bars->stage[0], 1);
+    mbar_init(&bars->stage[1], 1);
     mbar_init(&bars->g1_done, 1);
     mbar_init(&bars->g1_free, 1);
     for (int i = 0; i < 2; ++i) {
@@ -667,6 +745,8 @@ __global__ void __launch_bounds__(kThreads, 1) core_pipe_kernel(const __grid_con
     }
     for (int i = 0; i < NKQ; ++i) mbar_init(&bars->kq_free[i], 1);
     mbar_init(&bars->chain_mma, 1);
+    mbar_init(&bars->out_empty[0], 1);
+    mbar_init(&bars->out_empty[1], 1);
     bars->fail = 0;
     fence_mbar_init();
   }
@@ -725,6 +805,7 @@ bool core_fwd_pipe(const void *tk, const void *tq, const void *v, const void *be
       !encode_chunk_map(&maps.tq, &a.dq, tq, B, H, L, s[1], 64, true) ||
       !encode_chunk_map(&maps.v8, &a.dv, v, B, H, L, s[2], 8))
     return false;
+  a.out_tma = encode_out_map(&maps.out, &a.dout, out, B, H, L, s[4]) ? 1 : 0;
   cudaError_t e = cudaFuncSetAttribute(core_pipe_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
   if (e != cudaSuccess) {
     *rc = set_error(DP_ERR_CUDA, std::string("core_pipe smem attr: ") + cudaGetErrorString(e));

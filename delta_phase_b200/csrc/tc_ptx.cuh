@@ -46,14 +46,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Waits for the phase of `parity` to complete; false after `timeout_ns`.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint64_t timeout_ns) {
-  if (mbar_try_wait(bar, parity)) return true;
+// The polling loop of mbar_wait, out of line: kernels with many wait sites keep their
+// instruction footprint small.
+static __device__ __noinline__ bool mbar_wait_loop(uint64_t *bar, uint32_t parity, uint64_t timeout_ns) {
   const uint64_t t0 = globaltimer();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if (globaltimer() - t0 > timeout_ns) return false;
   }
+}
+
+// Waits for the phase of `parity` to complete; false after `timeout_ns`.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint64_t timeout_ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  return mbar_wait_loop(bar, parity, timeout_ns);
 }
 
 // ---------------------------------------------------------------- bulk copies
@@ -214,6 +220,13 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) 
       "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
       "r"(__float_as_uint(v[15]))
       : "memory");
+}
+
+// 32 lanes x 32 bits, 8 consecutive columns per thread (raw 32-bit words).
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&v)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(v[0]),
+               "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+               : "memory");
 }
 
 // 32 lanes x 32 bits, 32 consecutive columns per thread (raw 32-bit words).

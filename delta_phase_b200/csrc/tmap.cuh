@@ -35,15 +35,13 @@ struct ChunkMapDims {
   int8_t t, h, b;
 };
 
-// Encodes the map of one input (base 16-byte aligned, strides multiples of 8 elements, L
-// >= 64: the callers check these); returns false if the driver rejects it.  The box is
-// `box_channels` channels (64: a whole token row; 8: one 16-byte column group, for loads
-// straight into the core-matrix layout of an MMA operand) by 64 tokens.
-// With swizzle128 (box_channels = 64 only) the 16-byte chunk c of a token row r lands at
-// chunk c ^ (r % 8) of that row: threads that each read one row read conflict-free
-// (the destination must be 1024-byte aligned).
-inline bool encode_chunk_map(CUtensorMap *m, ChunkMapDims *dims_out, const void *base, int B, int H, int L,
-                             const SeqStrides &s, int box_channels = 64, bool swizzle128 = false) {
+// Encodes a 4-d map of a (B, H, L, C) tensor with unit channel stride: the channel
+// innermost, then token, head and batch in the order of their strides, and a box of
+// `box_channels` channels by 64 tokens.  Returns false if the driver rejects it (base not
+// 16-byte aligned, a stride not a multiple of 16 bytes, ...).
+inline bool encode_bhlc_map(CUtensorMap *m, ChunkMapDims *dims_out, const void *base, int B, int H, int L, int C,
+                            const SeqStrides &s, CUtensorMapDataType dtype, int elem_bytes, int box_channels,
+                            CUtensorMapSwizzle swizzle) {
   EncodeTiledFn enc = encode_tiled_fn();
   if (!enc) return false;
   const int64_t st[3] = {s.t, s.h, s.b};
@@ -56,12 +54,12 @@ inline bool encode_chunk_map(CUtensorMap *m, ChunkMapDims *dims_out, const void 
         ord[i] = ord[j];
         ord[j] = tmp;
       }
-  cuuint64_t dims[4] = {64, 0, 0, 0};
+  cuuint64_t dims[4] = {(cuuint64_t)C, 0, 0, 0};
   cuuint64_t strides[3];
   cuuint32_t box[4] = {(cuuint32_t)box_channels, 1, 1, 1};
   for (int i = 0; i < 3; ++i) {
     dims[i + 1] = (cuuint64_t)ext[ord[i]];
-    strides[i] = (cuuint64_t)st[ord[i]] * 2;
+    strides[i] = (cuuint64_t)st[ord[i]] * elem_bytes;
     if (ord[i] == 0) {
       box[i + 1] = 64;
       dims_out->t = (int8_t)(i + 1);
@@ -72,10 +70,30 @@ inline bool encode_chunk_map(CUtensorMap *m, ChunkMapDims *dims_out, const void 
     }
   }
   const cuuint32_t estr[4] = {1, 1, 1, 1};
-  return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void *>(base), dims, strides, box, estr,
-             CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
-             CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
-             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  return enc(m, dtype, 4, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Encodes the map of one bf16 input of 64 channels (base 16-byte aligned, strides
+// multiples of 8 elements, L >= 64: the callers check these); returns false if the driver
+// rejects it.  The box is `box_channels` channels (64: a whole token row; 8: one 16-byte
+// column group, for loads straight into the core-matrix layout of an MMA operand) by 64
+// tokens.  With swizzle128 (box_channels = 64 only) the 16-byte chunk c of a token row r
+// lands at chunk c ^ (r % 8) of that row: threads that each read one row read
+// conflict-free (the destination must be 1024-byte aligned).
+inline bool encode_chunk_map(CUtensorMap *m, ChunkMapDims *dims_out, const void *base, int B, int H, int L,
+                             const SeqStrides &s, int box_channels = 64, bool swizzle128 = false) {
+  return encode_bhlc_map(m, dims_out, base, B, H, L, 64, s, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, box_channels,
+                         swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
+// The map of a float32 output of 64 channels for bulk tensor stores: a box of 32 channels
+// (128 bytes) by 64 tokens with the 128-byte swizzle (16-byte chunk c of token row r at
+// chunk c ^ (r % 8) in shared memory, 1024-byte aligned); tokens past L are not written.
+inline bool encode_out_map(CUtensorMap *m, ChunkMapDims *dims_out, const float *base, int B, int H, int L,
+                           const SeqStrides &s) {
+  return encode_bhlc_map(m, dims_out, base, B, H, L, 64, s, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, 32,
+                         CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 // One chunk (tokens t0 .. t0 + 63) of head h, batch b into 64 rows x 128 bytes of shared
@@ -111,5 +129,27 @@ __device__ __forceinline__ void tma_load_colgroup(void *dst_smem, const CUtensor
       "l"(m), "r"(x0), "r"(c1), "r"(c2), "r"(c3), "r"(mb)
       : "memory");
 }
+
+// Bulk tensor store of channels x0 .. x0 + 31 of tokens t0 .. t0 + 63 of head h, batch b
+// from shared memory (a map of encode_out_map; x0 = 0 or 32), in the issuing thread's
+// bulk-async group.
+__device__ __forceinline__ void tma_store_chunk(const CUtensorMap *m, ChunkMapDims d, const void *src_smem, int x0,
+                                                int t0, int h, int b) {
+  const int c1 = d.t == 1 ? t0 : d.h == 1 ? h : b;
+  const int c2 = d.t == 2 ? t0 : d.h == 2 ? h : b;
+  const int c3 = d.t == 3 ? t0 : d.h == 3 ? h : b;
+  const uint32_t src = static_cast<uint32_t>(__cvta_generic_to_shared(src_smem));
+  asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.tile.bulk_group [%0, {%1, %2, %3, %4}], [%5];" ::"l"(m),
+               "r"(x0), "r"(c1), "r"(c2), "r"(c3), "r"(src)
+               : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+
+// The issuing thread's bulk stores have finished reading their shared-memory source.
+__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+
+// The issuing thread's bulk stores are complete.
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 }  // namespace dp
