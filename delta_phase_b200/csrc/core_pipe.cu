@@ -314,21 +314,27 @@ __device__ bool phasor_role(const PipeArgs &a, const PipeMaps &maps, uint8_t *sm
     fence_proxy_async_smem();
     tc_fence_before();
     group_sync(BAR_PH, kPhThreads);
-    if (tid == 0) {
+    if (warp == 0) {
       // the stage is free: the phases of chunk c + 2; then G1 = [K; Q] K^T (A from TMEM)
-      if (c + 2 < nchunks) {
-        issue_theta_loads(maps, a, stage, &bars->stage[sb], t0 + 2 * kC, h, b);
-        issued = c + 3;
+      if (tid == 0) {
+        if (c + 2 < nchunks) {
+          issue_theta_loads(maps, a, stage, &bars->stage[sb], t0 + 2 * kC, h, b);
+          issued = c + 3;
+        }
+        if (c >= 1) ok = mbar_wait(&bars->g1_free, (uint32_t)((c - 1) & 1), kTimeoutNs);
       }
-      if (c >= 1) ok = mbar_wait(&bars->g1_free, (uint32_t)((c - 1) & 1), kTimeoutNs);
+      ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
       if (ok) {
         tc_fence_after();
         const uint32_t sk = smem_u32(kt);
+        if (elect_one()) {
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          mma_f16_ts(tmem + COL_G1, tmem + COL_KQ + 64 * ks + 8 * kk, make_desc(sk + kk * 256, 128, RG_KQ),
-                     idesc_bf16(128, 64, false, false), kk > 0);
-        mma_commit(&bars->g1_done);
+          for (int kk = 0; kk < 8; ++kk)
+            mma_f16_ts(tmem + COL_G1, tmem + COL_KQ + 64 * ks + 8 * kk, make_desc(sk + kk * 256, 128, RG_KQ),
+                       idesc_bf16(128, 64, false, false), kk > 0);
+          mma_commit(&bars->g1_done);
+        }
+        __syncwarp();
         g1_issued = c + 1;
       }
     }
@@ -546,9 +552,8 @@ __device__ bool chain_role(const PipeArgs &a, const PipeMaps &maps, uint8_t *sme
     }
   }
 
-  // thread 0: commit the MMAs issued so far on chain_mma and wait for them
-  auto mma_sync = [&]() {
-    mma_commit(&bars->chain_mma);
+  // thread 0 (the lane elect_one picks in warp 0): wait for the MMAs committed last
+  auto mma_wait = [&]() {
     ++cm_pending;
     const bool r = mbar_wait(&bars->chain_mma, cm_phase, kTimeoutNs);
     if (r) {
@@ -588,14 +593,18 @@ __device__ bool chain_role(const PipeArgs &a, const PipeMaps &maps, uint8_t *sme
     group_sync(BAR_CH, kChThreads);
 
     // ---- C2: G3 = [K; Q] S^T -> R3 slot (M = 128, N = 64, K = 128)
-    if (ctid == 0) {
+    if (cw == 0) {
       tc_fence_after();
       const uint32_t ss = smem_u32(s0);
+      if (elect_one()) {
 #pragma unroll
-      for (int kk = 0; kk < 8; ++kk)
-        mma_f16_ts(tmem + r3, tmem + COL_KQ + 64 * ks + 8 * kk, make_desc(ss + kk * 2 * RG_64, RG_64, 128),
-                   idesc_bf16(128, 64, false, true), kk > 0);
-      ok = mma_sync();
+        for (int kk = 0; kk < 8; ++kk)
+          mma_f16_ts(tmem + r3, tmem + COL_KQ + 64 * ks + 8 * kk, make_desc(ss + kk * 2 * RG_64, RG_64, 128),
+                     idesc_bf16(128, 64, false, true), kk > 0);
+        mma_commit(&bars->chain_mma);
+      }
+      __syncwarp();
+      if (lane == 0) ok = mma_wait();
     }
     if (group_any(!ok, BAR_CH, kChThreads)) { ok = false; break; }
     tc_fence_after();
@@ -625,14 +634,18 @@ __device__ bool chain_role(const PipeArgs &a, const PipeMaps &maps, uint8_t *sme
 
     // ---- C3u: U = bT E (M = 64, N = 64, K = 64) -> RU.  E's tile is column-group-major:
     //      along K (tokens) 8-row core matrices are 128 bytes apart, along N 1 KB.
-    if (ctid == 0) {
+    if (cw == 0) {
       tc_fence_after();
       const uint32_t sb = smem_u32(btb), se = smem_u32(vt);
+      if (elect_one()) {
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk)
-        mma_f16_ss(tmem + COL_RU, make_desc(sb + kk * 256, 128, RG_64), make_desc(se + kk * 256, 128, 1024),
-                   idesc_bf16(64, 64, false, true), kk > 0);
-      ok = mma_sync();
+        for (int kk = 0; kk < 4; ++kk)
+          mma_f16_ss(tmem + COL_RU, make_desc(sb + kk * 256, 128, RG_64), make_desc(se + kk * 256, 128, 1024),
+                     idesc_bf16(64, 64, false, true), kk > 0);
+        mma_commit(&bars->chain_mma);
+      }
+      __syncwarp();
+      if (lane == 0) ok = mma_wait();
     }
     if (group_any(!ok, BAR_CH, kChThreads)) { ok = false; break; }
     tc_fence_after();
@@ -660,26 +673,24 @@ __device__ bool chain_role(const PipeArgs &a, const PipeMaps &maps, uint8_t *sme
     //      needs only the state), then G5 R3 += [X; P] U (M = 128, A starting 8 KB before P:
     //      rows 64.. of R3 (Q S^T) gain P U, rows 0.. (K S^T, used) are don't-care).  The
     //      commits after G5 free this chunk's K / Q and bT / P slots.
-    if (ctid == 0) {
+    if (cw == 0) {
       tc_fence_after();
       const uint32_t sk = smem_u32(kt), su = smem_u32(ub), sp = smem_u32(pb) - 8 * RG_64;
+      if (elect_one()) {
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk)
-        mma_f16_ss(tmem + COL_S, make_desc(sk + kk * 2 * RG_KQ, RG_KQ, 128), make_desc(su + kk * 2 * RG_64, RG_64, 128),
-                   idesc_bf16(128, 64, true, true), 1u);
-      mma_commit(&bars->chain_mma);
-      ++cm_pending;
+        for (int kk = 0; kk < 4; ++kk)
+          mma_f16_ss(tmem + COL_S, make_desc(sk + kk * 2 * RG_KQ, RG_KQ, 128),
+                     make_desc(su + kk * 2 * RG_64, RG_64, 128), idesc_bf16(128, 64, true, true), 1u);
+        mma_commit(&bars->chain_mma);
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk)
-        mma_f16_ss(tmem + r3, make_desc(sp + kk * 256, 128, RG_64), make_desc(su + kk * 2 * RG_64, RG_64, 128),
-                   idesc_bf16(128, 64, false, true), 1u);
-      mma_commit(&bars->kq_free[ks]);
-      mma_commit(&bars->bt_free[gs]);
-      ok = mbar_wait(&bars->chain_mma, cm_phase, kTimeoutNs);
-      if (ok) {
-        cm_phase ^= 1;
-        --cm_pending;
+        for (int kk = 0; kk < 4; ++kk)
+          mma_f16_ss(tmem + r3, make_desc(sp + kk * 256, 128, RG_64), make_desc(su + kk * 2 * RG_64, RG_64, 128),
+                     idesc_bf16(128, 64, false, true), 1u);
+        mma_commit(&bars->kq_free[ks]);
+        mma_commit(&bars->bt_free[gs]);
       }
+      __syncwarp();
+      if (lane == 0) ok = mma_wait();
     } else if (in_thread) {
       // V of chunk c + 2 into this chunk's slot (its last reader, U of chunk c, is done);
       // then the inputs of chunk c + 1
