@@ -474,18 +474,24 @@ __global__ void __launch_bounds__(kThreads, 1) laplace_tc_kernel(const __grid_co
       fence_proxy_async_smem();
       tc_fence_before();
       group_sync(BAR_L2, 128);
-      // ---- L3: [K;Q] K^T -> D1 (M=128, N=64) and [K;Q] S0^T -> D3 (M=128, N=32).  The
-      //      issuing thread is held ~45 cycles per MMA, so warp 0 does no decay work.
-      if (tid == 0) {
+      // ---- L3: [K;Q] K^T -> D1 (M=128, N=64) and [K;Q] S0^T -> D3 (M=128, N=32), issued
+      //      by one elected lane of warp 0 (the issuing thread is held for each MMA, so warp 0
+      //      does no decay work)
+      if (warp == 0) {
         tc_fence_after();
         const uint32_t sa = smem_u32(kq), ss = smem_u32(s0);
+        if (elect_one()) {
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint64_t ad = make_desc(sa + kk * 256, 128, RG_KQ);
-          mma_f16_ss(tmem + COL_D1, ad, make_desc(sa + kk * 256, 128, RG_KQ), idesc_bf16(128, 64, false, false), kk > 0);
-          mma_f16_ss(tmem + COL_D3, ad, make_desc(ss + kk * 2 * RG_32, RG_32, 128), idesc_bf16(128, 32, false, true), kk > 0);
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint64_t ad = make_desc(sa + kk * 256, 128, RG_KQ);
+            mma_f16_ss(tmem + COL_D1, ad, make_desc(sa + kk * 256, 128, RG_KQ), idesc_bf16(128, 64, false, false),
+                       kk > 0);
+            mma_f16_ss(tmem + COL_D3, ad, make_desc(ss + kk * 2 * RG_32, RG_32, 128), idesc_bf16(128, 32, false, true),
+                       kk > 0);
+          }
+          mma_commit(mma_bar);
         }
-        mma_commit(mma_bar);
+        __syncwarp();
       }
     } else {
       // ---- decay (warps 4..7, overlapping L2 and the MMAs): cumulative log-decay and the
@@ -752,14 +758,17 @@ __global__ void __launch_bounds__(kThreads, 1) laplace_tc_kernel(const __grid_co
     if (__syncthreads_or(!ok)) { ok = false; break; }
 
     // ---- L6: S^T += K^T W  (M=128, N=32, K=64)
-    if (tid == 0) {
+    if (warp == 0) {
       tc_fence_after();
       const uint32_t sk = smem_u32(kq), sw = smem_u32(wt);
+      if (elect_one()) {
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk)
-        mma_f16_ss(tmem + COL_S, make_desc(sk + kk * 2 * RG_KQ, RG_KQ, 128),
-                   make_desc(sw + kk * 2 * RG_32, RG_32, 128), idesc_bf16(128, 32, true, true), 1u);
-      mma_commit(mma_bar);
+        for (int kk = 0; kk < 4; ++kk)
+          mma_f16_ss(tmem + COL_S, make_desc(sk + kk * 2 * RG_KQ, RG_KQ, 128),
+                     make_desc(sw + kk * 2 * RG_32, RG_32, 128), idesc_bf16(128, 32, true, true), 1u);
+        mma_commit(mma_bar);
+      }
+      __syncwarp();
     }
     mma_pending = true;
     if (tid == 0) ok = mbar_wait(mma_bar, mma_phase, kTimeoutNs);
