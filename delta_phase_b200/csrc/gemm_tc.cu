@@ -120,7 +120,8 @@ __device__ bool gemm_producer(const GemmArgs &g, const GemmMaps &maps, uint8_t *
 
 // ------------------------------------------------------------------ MMA issuer (warp 1)
 // Accumulator b of a tile: rows 0..127 in TMEM columns (2 b) acc_cols .., rows 128..255 in
-// (2 b + 1) acc_cols ...
+// (2 b + 1) acc_cols ....  Run by the whole warp: the waits by every lane, the MMAs and
+// commits by one elected lane (warp-uniform operands issue faster than from a lane-0 branch).
 template <typename T>
 __device__ bool gemm_mma(const GemmArgs &g, uint8_t *ops, GemmBars *bars, uint32_t tmem) {
   constexpr bool kTf32 = sizeof(T) == 4;
@@ -131,36 +132,43 @@ __device__ bool gemm_mma(const GemmArgs &g, uint8_t *ops, GemmBars *bars, uint32
   for (int tile = blockIdx.x; tile < g.num_tiles; tile += gridDim.x, ++lt) {
     const int buf = lt % g.nbuf;
     // the epilogue must have drained this accumulator (tile lt - nbuf)
-    if (lt >= g.nbuf && !mbar_wait(&bars->acc_empty[buf], (uint32_t)((lt / g.nbuf - 1) & 1), kTimeoutNs)) {
+    bool okw = lt < g.nbuf || mbar_wait(&bars->acc_empty[buf], (uint32_t)((lt / g.nbuf - 1) & 1), kTimeoutNs);
+    if (!__all_sync(0xFFFFFFFFu, okw)) {
       if (lt > 0) mbar_wait(&bars->acc_full[(lt - 1) % g.nbuf], (uint32_t)(((lt - 1) / g.nbuf) & 1), kTimeoutNs);
       return false;
     }
     tc_fence_after();
     for (int ks = 0; ks < kslabs; ++ks, ++it) {
       const int s = it % kStages;
-      if (!mbar_wait(&bars->full[s], (uint32_t)((it / kStages) & 1), kTimeoutNs)) {
-        mma_commit(&bars->acc_full[buf]);  // let the issued MMAs land before returning
+      okw = mbar_wait(&bars->full[s], (uint32_t)((it / kStages) & 1), kTimeoutNs);
+      if (!__all_sync(0xFFFFFFFFu, okw)) {
+        if (elect_one()) mma_commit(&bars->acc_full[buf]);  // let the issued MMAs land before returning
+        __syncwarp();
         mbar_wait(&bars->acc_full[buf], (uint32_t)((lt / g.nbuf) & 1), kTimeoutNs);
         return false;
       }
       tc_fence_after();
       const uint32_t sa = smem_u32(ops + OFF_A + s * A_STAGE), sb = smem_u32(ops + OFF_B + s * B_STAGE);
+      if (elect_one()) {
 #pragma unroll
-      for (int kk = 0; kk < kSlabBytes / 32; ++kk) {
-        const uint64_t bd = desc_sw128(sb + kk * 32);
+        for (int kk = 0; kk < kSlabBytes / 32; ++kk) {
+          const uint64_t bd = desc_sw128(sb + kk * 32);
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          const uint64_t ad = desc_sw128(sa + half * (128 * kSlabBytes) + kk * 32);
-          const uint32_t d = tmem + (uint32_t)((2 * buf + half) * g.acc_cols);
-          if (kTf32)
-            mma_tf32_ss(d, ad, bd, idesc, (ks | kk) != 0);
-          else
-            mma_f16_ss(d, ad, bd, idesc, (ks | kk) != 0);
+          for (int half = 0; half < 2; ++half) {
+            const uint64_t ad = desc_sw128(sa + half * (128 * kSlabBytes) + kk * 32);
+            const uint32_t d = tmem + (uint32_t)((2 * buf + half) * g.acc_cols);
+            if (kTf32)
+              mma_tf32_ss(d, ad, bd, idesc, (ks | kk) != 0);
+            else
+              mma_f16_ss(d, ad, bd, idesc, (ks | kk) != 0);
+          }
         }
+        mma_commit(&bars->empty[s]);  // the slab's buffers are free once these MMAs have read them
       }
-      mma_commit(&bars->empty[s]);  // the slab's buffers are free once these MMAs have read them
+      __syncwarp();
     }
-    mma_commit(&bars->acc_full[buf]);
+    if (elect_one()) mma_commit(&bars->acc_full[buf]);
+    __syncwarp();
   }
   return true;
 }
@@ -266,7 +274,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
   if (warp == 0) {
     if (lane == 0) ok = gemm_producer<T>(g, maps, ops, bars);
   } else if (warp == 1) {
-    if (lane == 0) ok = gemm_mma<T>(g, ops, bars, tmem);
+    ok = gemm_mma<T>(g, ops, bars, tmem);
   } else {
     ok = gemm_epilogue<EPI>(g, bars, tmem);
   }
