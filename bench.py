@@ -371,7 +371,7 @@ def run_core(args, world, rank, local):
                    "l2": f"inputs+outputs {alg_bytes / 1e6:.0f} MB per step > 126 MB L2; no flush"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": achieved / peaks["hbm_gbs"],
-                     "traffic": read_profile_traffic("core_tc_kernel_b8h16l8192_ncu_full.md"),
+                     "traffic": read_profile_traffic("core_pipe_kernel_b8h16l8192_ncu_full.md"),
                      "algorithmic_bytes_per_launch": alg_bytes,
                      "peak_source": f"{src} (MEASURED_PEAKS.json hbm_gbs)" if src == "measured" else src,
                      "kernel": "dp_core_fwd (one launch per step)"},
