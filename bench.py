@@ -128,17 +128,19 @@ class ClockSampler:
 
 # ------------------------------------------------------------------ distributed plumbing
 def dist_setup(n_gpus):
-    import torch
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if world > 1:
-        import torch.distributed as dist
         # NCCL's communicator set-up lines (nranks, ranks, devices) go to stderr, so a reader
-        # can check the communicator spans every GPU of the run
+        # can check the communicator spans every GPU of the run.  NCCL reads these once, when
+        # it first initialises, so they are set before torch (and NCCL) are imported.
         os.environ.setdefault("NCCL_DEBUG", "INFO")
         os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
         os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
+    import torch
+    if world > 1:
+        import torch.distributed as dist
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
