@@ -124,6 +124,37 @@ def test_strided_projection_views_tensor_core(L):
     assert rel_l2(out_s, ref) < TOL_BF16
 
 
+@pytest.mark.parametrize("L", [64, 200, 1000])
+def test_tensor_core_output_layouts(L):
+    """The pipelined tensor-core kernel (real beta, d_k = 64, bf16) writes its outputs with
+    bulk tensor stores (tokens past L clipped by the tensor map): a transposed (B, L, H, Dv)
+    output and one with padded rows give the same bits as a contiguous output, with a random
+    initial state, and leave the padding alone; an output whose rows are not 16-byte
+    multiples goes to the CUDA-core kernel.  All match the oracle."""
+    B, H, D = 2, 3, 64
+    rng = np.random.default_rng(100 + L)
+    tk, tq, v, beta = core_inputs(40 + L, B, H, L, D)
+    tk, tq, v, beta = (round_bf16(a) for a in (tk, tq, v, beta))
+    M0 = (0.3 * (rng.standard_normal((B, H, D, D)) + 1j * rng.standard_normal((B, H, D, D)))).astype(np.complex64)
+    args = [to_dev(a, torch.bfloat16) for a in (tk, tq, v)] + [to_dev(beta)]
+    out_c, M_c = chunkwise_forward(*args, 64, to_dev(M0))
+    # (B, L, H, Dv) buffer viewed as (B, H, L, Dv): token stride H * 64 floats (tensor map)
+    buf = torch.empty(B, L, H, D, device="cuda")
+    out_t, M_t = chunkwise_forward(*args, 64, to_dev(M0), out=buf.transpose(1, 2))
+    # token stride 68 floats: padded rows, still a tensor map; the padding is never written
+    pad = torch.full((B, H, L, D + 4), float("nan"), device="cuda")
+    out_p, M_p = chunkwise_forward(*args, 64, to_dev(M0), out=pad[..., :D])
+    # token stride 65 floats (not 16-byte rows): the CUDA-core kernel takes the call
+    odd = torch.full((B, H, L, D + 1), float("nan"), device="cuda")
+    out_o, M_o = chunkwise_forward(*args, 64, to_dev(M0), out=odd[..., :D])
+    assert torch.equal(out_t, out_c) and torch.equal(M_t, M_c)
+    assert torch.equal(out_p, out_c) and torch.equal(M_p, M_c)
+    assert torch.isnan(pad[..., D:]).all() and torch.isnan(odd[..., D]).all()
+    ref_out, ref_M = ocore.recurrent_delta(tk, tq, v, beta, M0)
+    for o, m in ((out_c, M_c), (out_o, M_o)):
+        assert rel_l2(o, ref_out) < TOL_BF16 and rel_l2(m, ref_M) < TOL_BF16
+
+
 def test_dispatcher_contract():
     tk, tq, v, beta = core_inputs(1, 1, 2, 30, 8)
     with pytest.raises(RuntimeError):  # L not a multiple of chunk_size, as in the reference
