@@ -486,10 +486,12 @@ extern "C" int dp_ln_conv_silu(const void *x, int x_dtype, const float *ln_w, co
   DP_REQUIRE(smem <= 227 * 1024, DP_ERR_UNSUPPORTED, "dp_ln_conv_silu: d too large");
   dim3 grid((L + T - 1) / T, B);
   cudaStream_t st = as_stream(stream);
+  cudaError_t attr_err = cudaSuccess;
   auto launch = [&](auto xt, auto ot) {
     using XT = decltype(xt);
     using OT = decltype(ot);
-    cudaFuncSetAttribute(ln_conv_silu_kernel<XT, OT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    attr_err = cudaFuncSetAttribute(ln_conv_silu_kernel<XT, OT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (attr_err != cudaSuccess) return;
     ln_conv_silu_kernel<XT, OT><<<grid, kBlkThreads, smem, st>>>(static_cast<const XT *>(x), ln_w, ln_b, eps,
                                                                  conv_w, conv_b, static_cast<OT *>(out), L, d, k, T);
   };
@@ -500,6 +502,8 @@ extern "C" int dp_ln_conv_silu(const void *x, int x_dtype, const float *ln_w, co
     if (out_dtype == DP_F32) launch(__nv_bfloat16{}, float{});
     else launch(__nv_bfloat16{}, __nv_bfloat16{});
   }
+  if (attr_err != cudaSuccess)
+    return set_error(DP_ERR_CUDA, std::string("ln_conv_silu smem attr: ") + cudaGetErrorString(attr_err));
   return check_launch("ln_conv_silu_kernel");
 }
 

@@ -268,7 +268,8 @@ extern "C" int dp_gram(const void *theta, const void *beta, int in_dtype, int be
   return dispatch_dtype(in_dtype, [&](auto tag) -> int {
     using T = decltype(tag);
     auto kern = gram_kernel<T>;
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return set_error(DP_ERR_CUDA, std::string("gram smem attr: ") + cudaGetErrorString(e));
     kern<<<N, kThreads, smem, as_stream(stream)>>>(static_cast<const T *>(theta), beta, beta_dtype,
                                                    out, C, D);
     return check_launch("gram_kernel");
