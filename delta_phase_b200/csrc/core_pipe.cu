@@ -12,26 +12,29 @@
 // The work of a chunk is split over three warp-specialised roles that run three chunks at
 // once, so the per-chunk latencies of the roles overlap instead of adding up:
 //   * phasor role (warps 0-7), chunk c + 2: two threads per row of [K; Q] compute its 64
-//     phasors from the TMA-loaded phases and store the row straight into tensor memory
-//     (the A operand of G1 and G3: no shared-memory traffic for Q at all), the K rows also
-//     into a shared-memory tile (B of G1, A^T of G4); then G1 = [K; Q] K^T (tcgen05,
-//     M = 128, A from tensor memory);
+//     phasors from the TMA-loaded phases (two stages: the next chunk's phases are in flight)
+//     and store the row straight into tensor memory (the A operand of G1 and G3: no
+//     shared-memory traffic for Q at all), the K rows also into a shared-memory tile (B of
+//     G1, A^T of G4); then G1 = [K; Q] K^T (tcgen05, M = 128, A from tensor memory).  Its
+//     warps of TMEM lane quarters 2 and 3 also store the outputs of chunk c - 1 (read out of
+//     tensor memory into a swizzled tile, then two bulk tensor stores) and free the chain's
+//     accumulator slot;
 //   * inverse role (warps 8-11), chunk c + 1: A and P from the G1 rows, T = (I + A)^-1 in
 //     fp32 (16 x 16 diagonal blocks by forward substitution with the next row prefetched,
 //     the 16 -> 32 and 32 -> 64 block merges on warp-level tf32 MMA), bT in bf16;
 //   * chain role (warps 12-19), chunk c: the state recurrence.  S^T -> bf16; G3 = [K; Q] S^T
-//     (M = 128, A from tensor memory); E; U = bT E (M = 64); G4: S^T += K^T U and
-//     G5: Q S^T += P U (M = 128, A starting 64 rows before P); the outputs of chunk c are
-//     read out of TMEM while the G3 of chunk c + 1 runs (two accumulator slots).
-// V reaches its MMA operand tile by TMA directly (eight 16-byte column groups per chunk),
-// a chunk ahead, issued by the chain role.  Hand-offs between roles are mbarriers only
+//     (M = 128, A from tensor memory); E; U = bT E (M = 64); G4: S^T += K^T U, waited for on
+//     its own, and G5: Q S^T += P U (M = 128, A starting 64 rows before P) behind it.  A
+//     second thread of the role issues the V loads (TMA straight into the operand tile,
+//     eight 16-byte column groups per chunk, two chunks ahead) and waits for the next
+//     chunk's inputs while thread 0 waits for this chunk's MMAs.
+// Every MMA is issued by one lane that elect.sync picks in warp-uniform code (a plain lane-0
+// branch measured about twice as slow per MMA).  Hand-offs between roles are mbarriers only
 // (the chain's MMA commits arrive on the barriers that free the phasor and inverse roles'
 // slots); K and Q live in a ring of three slots (written two chunks ahead of the chain),
-// the inverse role's outputs and V in rings of two.  Shared-memory bandwidth is the
-// scarce resource here (the small MMAs read their operands from it), which is what the
-// tensor-memory A operands and the bank-conflict-free layouts below are for.  Every wait
-// is bounded: on expiry the kernel records DP_ERR_TIMEOUT, lets its own copies and MMAs
-// land and frees its tensor memory.
+// the inverse role's outputs, V and the G3 accumulator in rings of two.  Every wait is
+// bounded: on expiry the kernel records DP_ERR_TIMEOUT, lets its own copies and MMAs land
+// and frees its tensor memory.
 #include <cstring>
 
 #include "dp_common.cuh"
