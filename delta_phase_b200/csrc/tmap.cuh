@@ -1,9 +1,9 @@
-// TMA tensor maps for the chunk inputs of the tensor-core kernels (core_tc.cu,
-// laplace_tc.cu): a bf16 input of d_k = 64 channels viewed as (B, H, L, 64) with element
-// strides (s.b, s.h, s.t) becomes a 4-d map with the channel innermost, then token, head
-// and batch in the order of their strides, and a box of 64 channels x 64 tokens, so one
-// tiled copy (`cp.async.bulk.tensor.4d`, no multicast) fetches one chunk of one (b, h).
-// Tokens past L arrive as zeros.
+// TMA tensor maps for the chunk inputs and outputs of the tensor-core kernels (core_tc.cu,
+// core_pipe.cu, laplace_tc.cu): a (B, H, L, 64) tensor with element strides (s.b, s.h, s.t)
+// and unit channel stride becomes a 4-d map with the channel innermost, then token, head
+// and batch in the order of their strides, so one tiled copy (`cp.async.bulk.tensor.4d`, no
+// multicast) moves one 64-token chunk of one (b, h).  Loads: tokens past L arrive as zeros.
+// Stores (the float32 outputs of core_pipe.cu): tokens past L are not written.
 #pragma once
 
 #include <cuda.h>  // CUtensorMap and cuTensorMapEncodeTiled's types (called through the runtime)
