@@ -121,13 +121,40 @@ __device__ __forceinline__ void fast_sincos(float x, float *s, float *c) {
   __sincosf(r, s, c);
 }
 
+// 16-bit operand pairs: bf16 (real beta) or fp16 (complex beta, CB: the isometric update
+// does not damp rounding errors, so its tiles keep 10 mantissa bits; the tiles that could
+// grow are range-checked, values past 65504 set `over`, reported as DP_ERR_RANGE).
+template <bool F16>
+__device__ __forceinline__ uint32_t pack_op(float a, float b) {
+  if (F16) {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t *>(&h);
+  }
+  return pack_bf16(a, b);
+}
+template <bool F16>
+__device__ __forceinline__ uint32_t pack_chk(float a, float b, bool &over) {
+  if (F16) over |= !(fabsf(a) <= 65504.f) || !(fabsf(b) <= 65504.f);
+  return pack_op<F16>(a, b);
+}
+template <bool F16>
+__host__ __device__ constexpr uint32_t idesc_op(int M, int N, bool a_mn_major, bool b_mn_major) {
+  return F16 ? idesc_f16(M, N, a_mn_major, b_mn_major) : idesc_bf16(M, N, a_mn_major, b_mn_major);
+}
+// The write key of one fp16 (cos, sin) pair: beta kappa = (br c - bi s, br s + bi c).
+__device__ __forceinline__ uint32_t rotate_pair(uint32_t cs, float br, float bi) {
+  const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&cs));
+  return pack_op<true>(fmaf(br, f.x, -bi * f.y), fmaf(br, f.y, bi * f.x));
+}
+
 // The bf16 pair (cos theta, sin theta) of a bf16 phase given as raw bits.  (Measured
 // alternatives, all slower on this kernel: the FMA-pipe polynomial poly_sincos for all or
 // half of the phases, and a shared-memory table of the bf16 phases.)
+template <bool CB>
 __device__ __forceinline__ uint32_t phasor_word(uint32_t bits) {
   float s, c;
   fast_sincos(__uint_as_float(bits << 16), &s, &c);
-  return pack_bf16(c, s);
+  return pack_op<CB>(c, s);
 }
 
 // One warp: D[16 x 16] = X[16 x K] Y[K x 16], X(i, k) = x[i * xs_i + k * xs_k],
@@ -193,6 +220,7 @@ struct PipeBars {
   uint64_t out_empty[2];     // outputs of an R3 slot read out of tensor memory -> chain
   uint32_t tmem_base;
   int fail;
+  int range;  // a 16-bit tile value out of range (complex beta)
 };
 static_assert(sizeof(PipeBars) <= 256, "barrier block");
 
@@ -215,9 +243,10 @@ __device__ __forceinline__ void issue_v_loads(const PipeMaps &m, const PipeArgs 
 // by `lead` (tokens past L are not written); with no output map, straight from registers.
 // Run by the four phasor warps of TMEM lane quarters 2 and 3 (barrier BAR_OUT); `lead`
 // frees the slot (out_empty) as soon as all four warps hold their rows in registers.
+template <bool CB>
 __device__ __noinline__ void pipe_store_out(const PipeArgs &a, const PipeMaps &maps, uint8_t *smem, PipeBars *bars,
                                             uint32_t taddr, int t, int hc, bool lead, int cc, int h, int b) {
-  const float inv64 = 1.0f / 64.0f;
+  const float inv64 = CB ? 1.0f : 1.0f / 64.0f;  // complex beta: the accumulator holds O already
   const int tt = cc * kC + t;
   float o[32];
   tmem_ld32_sync(taddr, o);
@@ -253,6 +282,7 @@ __device__ __noinline__ void pipe_store_out(const PipeArgs &a, const PipeMaps &m
 // from stage row r (theta_k rows, then theta_q rows).  The stage is written by TMA with
 // the 128-byte swizzle, so the 32 rows a warp reads at once fall on distinct bank groups.
 // Two stages: the phases of chunk c + 1 are in flight while chunk c's are used.
+template <bool CB>
 __device__ bool phasor_role(const PipeArgs &a, const PipeMaps &maps, uint8_t *smem, PipeBars *bars, uint32_t tmem,
                             int b, int h, int nchunks) {
   const int tid = threadIdx.x, warp = tid >> 5, h2 = warp >> 2;
@@ -262,6 +292,10 @@ __device__ bool phasor_role(const PipeArgs &a, const PipeMaps &maps, uint8_t *sm
   const bool is_k = r < kC;
   int issued = 0, consumed = 0, g1_issued = 0;
   bool ok = true;
+  // complex beta: phi of this thread's K row, a chunk ahead (raw bits)
+  const int64_t pbase = b * a.s_b.b + h * a.s_b.h;
+  uint32_t phi_next = 0u;
+  if (CB && is_k && t < L) phi_next = load_raw_scalar(a.beta, a.beta_dt, pbase + (int64_t)t * a.s_b.t);
   for (int k = 0; k < 2 && k < nchunks; ++k) {
     if (tid == 0) issue_theta_loads(maps, a, smem + OFF_STAGE + k * STAGE_BYTES, &bars->stage[k], k * kC, h, b);
     issued = k + 1;
@@ -282,7 +316,7 @@ __device__ bool phasor_role(const PipeArgs &a, const PipeMaps &maps, uint8_t *sm
     if (group_any(!ok, BAR_PH, kPhThreads)) { ok = false; break; }
     if (c >= NKQ && (warp & 3) >= 2) {
       const int cc = c - NKQ;
-      pipe_store_out(a, maps, smem, bars, tmem + lane_base + COL_R3 + 64 * (cc & 1) + 32 * h2,
+      pipe_store_out<CB>(a, maps, smem, bars, tmem + lane_base + COL_R3 + 64 * (cc & 1) + 32 * h2,
                      ((warp & 3) - 2) * 32 + (tid & 31), h2, tid == 64, cc, h, b);
     }
     if (!work) continue;
@@ -291,6 +325,14 @@ __device__ bool phasor_role(const PipeArgs &a, const PipeMaps &maps, uint8_t *sm
     // afterwards: a per-phasor select around the sincos makes the compiler branch around
     // each one, which serialises them (twice the time of this loop, measured).
     const uint32_t vmask = t < nvalid ? 0xFFFFFFFFu : 0u;
+    float br = 1.f, bi = 0.f;  // complex beta of this K row: 1 + e^{i phi}
+    if (CB) {
+      const uint32_t phi_cur = phi_next;
+      phi_next = 0u;
+      if (is_k && t0 + kC + t < L) phi_next = load_raw_scalar(a.beta, a.beta_dt, pbase + (int64_t)(t0 + kC + t) * a.s_b.t);
+      fast_sincos(raw_scalar_to_f32(phi_cur, a.beta_dt), &bi, &br);
+      br += 1.f;
+    }
     {
       uint32_t w[32];
 #pragma unroll
@@ -300,17 +342,22 @@ __device__ bool phasor_role(const PipeArgs &a, const PipeMaps &maps, uint8_t *sm
         const uint32_t rw[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          w[8 * s4 + 2 * i] = phasor_word(rw[i] & 0xFFFFu) & vmask;
-          w[8 * s4 + 2 * i + 1] = phasor_word(rw[i] >> 16) & vmask;
+          w[8 * s4 + 2 * i] = phasor_word<CB>(rw[i] & 0xFFFFu) & vmask;
+          w[8 * s4 + 2 * i + 1] = phasor_word<CB>(rw[i] >> 16) & vmask;
         }
       }
       tmem_st32(tmem + lane_base + COL_KQ + 64 * ks + 32 * h2, w);
       if (is_k) {
-        // the K row also into the shared-memory tile: features 64 h2 + 8 g .. (4 channels)
+        // the K row (complex beta: the write key W = beta K) also into the shared-memory
+        // tile: features 64 h2 + 8 g .. (4 channels)
 #pragma unroll
-        for (int g = 0; g < 8; ++g)
-          *reinterpret_cast<uint4 *>(kt + cm_off(t, 64 * h2 + 8 * g, RG_KQ)) =
-              make_uint4(w[4 * g], w[4 * g + 1], w[4 * g + 2], w[4 * g + 3]);
+        for (int g = 0; g < 8; ++g) {
+          uint4 x = make_uint4(w[4 * g], w[4 * g + 1], w[4 * g + 2], w[4 * g + 3]);
+          if (CB)
+            x = make_uint4(rotate_pair(x.x, br, bi), rotate_pair(x.y, br, bi), rotate_pair(x.z, br, bi),
+                           rotate_pair(x.w, br, bi));
+          *reinterpret_cast<uint4 *>(kt + cm_off(t, 64 * h2 + 8 * g, RG_KQ)) = x;
+        }
       }
     }
     tmem_st_wait();
@@ -334,7 +381,7 @@ __device__ bool phasor_role(const PipeArgs &a, const PipeMaps &maps, uint8_t *sm
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk)
             mma_f16_ts(tmem + COL_G1, tmem + COL_KQ + 64 * ks + 8 * kk, make_desc(sk + kk * 256, 128, RG_KQ),
-                       idesc_bf16(128, 64, false, false), kk > 0);
+                       idesc_op<CB>(128, 64, false, false), kk > 0);
           mma_commit(&bars->g1_done);
         }
         __syncwarp();
@@ -353,6 +400,7 @@ __device__ bool phasor_role(const PipeArgs &a, const PipeMaps &maps, uint8_t *sm
 }
 
 // ----------------------------------------------------------------------- inverse role
+template <bool CB>
 __device__ bool inverse_role(const PipeArgs &a, uint8_t *smem, PipeBars *bars, uint32_t tmem, int b, int h,
                              int nchunks) {
   const int itid = threadIdx.x - kInvBase, iw = itid >> 5, lane = itid & 31;  // iw = TMEM lane quarter
@@ -364,16 +412,16 @@ __device__ bool inverse_role(const PipeArgs &a, uint8_t *smem, PipeBars *bars, u
   float *bs = reinterpret_cast<float *>(smem + OFF_BETA);
   const float inv64 = 1.0f / 64.0f;
   const int64_t bbase = b * a.s_b.b + h * a.s_b.h;
-  bool ok = true;
+  bool ok = true, over = false;
   uint32_t bnext = 0u;  // raw bits of the next chunk's beta (converted when used)
-  if (itid < kC && itid < L) bnext = load_raw_scalar(a.beta, a.beta_dt, bbase + (int64_t)itid * a.s_b.t);
+  if (!CB && itid < kC && itid < L) bnext = load_raw_scalar(a.beta, a.beta_dt, bbase + (int64_t)itid * a.s_b.t);
   for (int c = 0; c < nchunks; ++c) {
     const int gs = c & 1, t0 = c * kC;
     uint8_t *pb = smem + OFF_P + gs * T64_BYTES;
     uint8_t *btb = smem + OFF_BT + gs * T64_BYTES;
     if (itid < kC) bs[itid] = raw_scalar_to_f32(bnext, a.beta_dt);
     bnext = 0u;
-    if (itid < kC && t0 + kC + itid < L)
+    if (!CB && itid < kC && t0 + kC + itid < L)
       bnext = load_raw_scalar(a.beta, a.beta_dt, bbase + (int64_t)(t0 + kC + itid) * a.s_b.t);
     if (itid == 0) {
       ok = mbar_wait(&bars->g1_done, (uint32_t)(c & 1), kTimeoutNs);
@@ -384,7 +432,18 @@ __device__ bool inverse_role(const PipeArgs &a, uint8_t *smem, PipeBars *bars, u
 
     // ---- A^T from the (exactly symmetric) Gram rows, At[k][i] = beta_k G[k][i] / 64 for
     //      i > k (quarters 0, 1); P = tril(Q K^T) in bf16 (quarters 2, 3)
-    if (iw < 2) {
+    if (CB && iw < 2) {
+      // row i of K W^T: A[i][k] = G1[i][k] / 64 for k < i (not symmetric), stored as column
+      // i of A^T
+      const int i = iw * 32 + lane;
+#pragma unroll 1
+      for (int hf = 0; hf < 2; ++hf) {
+        float g[32];
+        tmem_ld32_sync(tmem + lane_base + COL_G1 + 32 * hf, g);
+#pragma unroll
+        for (int kk = 0; kk < 32; ++kk) at[(32 * hf + kk) * LDA + i] = (32 * hf + kk < i) ? g[kk] * inv64 : 0.f;
+      }
+    } else if (iw < 2) {
       const int k = iw * 32 + lane;
       const float bk = bs[k] * inv64;
 #pragma unroll 1
@@ -413,10 +472,11 @@ __device__ bool inverse_role(const PipeArgs &a, uint8_t *smem, PipeBars *bars, u
           const int s = 32 * hf + 8 * u;
           const float *pp = p + 8 * u;
           uint4 w;
-          w.x = pack_bf16(s + 0 <= t ? pp[0] : 0.f, s + 1 <= t ? pp[1] : 0.f);
-          w.y = pack_bf16(s + 2 <= t ? pp[2] : 0.f, s + 3 <= t ? pp[3] : 0.f);
-          w.z = pack_bf16(s + 4 <= t ? pp[4] : 0.f, s + 5 <= t ? pp[5] : 0.f);
-          w.w = pack_bf16(s + 6 <= t ? pp[6] : 0.f, s + 7 <= t ? pp[7] : 0.f);
+          const float ps = CB ? inv64 : 1.f;  // fp16 tiles hold P / 64
+          w.x = pack_op<CB>(s + 0 <= t ? pp[0] * ps : 0.f, s + 1 <= t ? pp[1] * ps : 0.f);
+          w.y = pack_op<CB>(s + 2 <= t ? pp[2] * ps : 0.f, s + 3 <= t ? pp[3] * ps : 0.f);
+          w.z = pack_op<CB>(s + 4 <= t ? pp[4] * ps : 0.f, s + 5 <= t ? pp[5] * ps : 0.f);
+          w.w = pack_op<CB>(s + 6 <= t ? pp[6] * ps : 0.f, s + 7 <= t ? pp[7] * ps : 0.f);
           *reinterpret_cast<uint4 *>(pb + cm_off(t, s, RG_64)) = w;
         }
       }
@@ -491,26 +551,28 @@ __device__ bool inverse_role(const PipeArgs &a, uint8_t *smem, PipeBars *bars, u
     //      consecutive rows per quarter warp, so the row loads and tile stores do not conflict)
     {
       const int i = itid & 63, c0 = 32 * (itid >> 6);
-      const float bi = bs[i];
+      const float bi = CB ? 1.f : bs[i];  // complex beta: U = T E
       const float *tr = tf + i * LDA + c0;
 #pragma unroll
       for (int c8 = 0; c8 < 4; ++c8) {
         const float4 x0 = *reinterpret_cast<const float4 *>(tr + 8 * c8);
         const float4 x1 = *reinterpret_cast<const float4 *>(tr + 8 * c8 + 4);
         *reinterpret_cast<uint4 *>(btb + cm_off(i, c0 + 8 * c8, RG_64)) =
-            make_uint4(pack_bf16(bi * x0.x, bi * x0.y), pack_bf16(bi * x0.z, bi * x0.w),
-                       pack_bf16(bi * x1.x, bi * x1.y), pack_bf16(bi * x1.z, bi * x1.w));
+            make_uint4(pack_chk<CB>(bi * x0.x, bi * x0.y, over), pack_chk<CB>(bi * x0.z, bi * x0.w, over),
+                       pack_chk<CB>(bi * x1.x, bi * x1.y, over), pack_chk<CB>(bi * x1.z, bi * x1.w, over));
       }
     }
     fence_proxy_async_smem();
     group_sync(BAR_INV, kInvThreads);
     if (itid == 0) mbar_arrive(&bars->bt_full[gs]);
   }
+  if (CB && over) atomicOr(&bars->range, 1);
   return ok;
 }
 
 // ------------------------------------------------------------------------- chain role
 // Warp cw (0..7) of the role: TMEM lane quarter q = cw % 4, column half hc = cw / 4.
+template <bool CB>
 __device__ bool chain_role(const PipeArgs &a, const PipeMaps &maps, uint8_t *smem, PipeBars *bars, uint32_t tmem,
                            int bh, int b, int h, int nchunks) {
   const int ctid = threadIdx.x - kChBase, cw = ctid >> 5, lane = ctid & 31;
@@ -543,7 +605,9 @@ __device__ bool chain_role(const PipeArgs &a, const PipeMaps &maps, uint8_t *sme
   const bool in_thread = ctid == 32;
   uint32_t cm_phase = 0;
   int v_issued = 0, v_consumed = 0, cm_pending = 0;
-  bool ok = true;
+  bool ok = true, over = false;
+  // complex beta: the S^T operand holds S^T / 64 (fp16 range), so G3 yields K S^T / 64
+  const float ss64 = CB ? 1.0f / 64.0f : 1.0f;
   if (in_thread) {
     for (int k = 0; k < 2 && k < nchunks; ++k) {
       issue_v_loads(maps, a, smem + OFF_V + k * T64_BYTES, &bars->v_full[k], k * kC, h, b);
@@ -587,8 +651,8 @@ __device__ bool chain_role(const PipeArgs &a, const PipeMaps &maps, uint8_t *sme
       for (int u = 0; u < 4; ++u) {
         const float *ss = sv + 8 * u;
         *reinterpret_cast<uint4 *>(s0 + cm_off(j, 32 * hc + 8 * u, RG_64)) =
-            make_uint4(pack_bf16(ss[0], ss[1]), pack_bf16(ss[2], ss[3]), pack_bf16(ss[4], ss[5]),
-                       pack_bf16(ss[6], ss[7]));
+            make_uint4(pack_chk<CB>(ss[0] * ss64, ss[1] * ss64, over), pack_chk<CB>(ss[2] * ss64, ss[3] * ss64, over),
+                       pack_chk<CB>(ss[4] * ss64, ss[5] * ss64, over), pack_chk<CB>(ss[6] * ss64, ss[7] * ss64, over));
       }
     }
     fence_proxy_async_smem();
@@ -603,7 +667,7 @@ __device__ bool chain_role(const PipeArgs &a, const PipeMaps &maps, uint8_t *sme
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
           mma_f16_ts(tmem + r3, tmem + COL_KQ + 64 * ks + 8 * kk, make_desc(ss + kk * 2 * RG_64, RG_64, 128),
-                     idesc_bf16(128, 64, false, true), kk > 0);
+                     idesc_op<CB>(128, 64, false, true), kk > 0);
         mma_commit(&bars->chain_mma);
       }
       __syncwarp();
@@ -626,7 +690,10 @@ __device__ bool chain_role(const PipeArgs &a, const PipeMaps &maps, uint8_t *sme
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const float2 vv = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&vw[i]));
-          ew[i] = pack_bf16(vv.x - ks[8 * u + 2 * i] * inv64, vv.y - ks[8 * u + 2 * i + 1] * inv64);
+          if (CB)  // the state-read rows already carry the 1 / 64
+            ew[i] = pack_chk<true>(vv.x - ks[8 * u + 2 * i], vv.y - ks[8 * u + 2 * i + 1], over);
+          else
+            ew[i] = pack_bf16(vv.x - ks[8 * u + 2 * i] * inv64, vv.y - ks[8 * u + 2 * i + 1] * inv64);
         }
         *vp = make_uint4(ew[0], ew[1], ew[2], ew[3]);
       }
@@ -644,7 +711,7 @@ __device__ bool chain_role(const PipeArgs &a, const PipeMaps &maps, uint8_t *sme
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
           mma_f16_ss(tmem + COL_RU, make_desc(sb + kk * 256, 128, RG_64), make_desc(se + kk * 256, 128, 1024),
-                     idesc_bf16(64, 64, false, true), kk > 0);
+                     idesc_op<CB>(64, 64, false, true), kk > 0);
         mma_commit(&bars->chain_mma);
       }
       __syncwarp();
@@ -663,8 +730,8 @@ __device__ bool chain_role(const PipeArgs &a, const PipeMaps &maps, uint8_t *sme
         for (int u = 0; u < 4; ++u) {
           const float *uu = uv + 8 * u;
           *reinterpret_cast<uint4 *>(ub + cm_off(t, 32 * hc + 8 * u, RG_64)) =
-              make_uint4(pack_bf16(uu[0], uu[1]), pack_bf16(uu[2], uu[3]), pack_bf16(uu[4], uu[5]),
-                         pack_bf16(uu[6], uu[7]));
+              make_uint4(pack_chk<CB>(uu[0], uu[1], over), pack_chk<CB>(uu[2], uu[3], over),
+                         pack_chk<CB>(uu[4], uu[5], over), pack_chk<CB>(uu[6], uu[7], over));
         }
       }
     }
@@ -683,12 +750,12 @@ __device__ bool chain_role(const PipeArgs &a, const PipeMaps &maps, uint8_t *sme
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
           mma_f16_ss(tmem + COL_S, make_desc(sk + kk * 2 * RG_KQ, RG_KQ, 128),
-                     make_desc(su + kk * 2 * RG_64, RG_64, 128), idesc_bf16(128, 64, true, true), 1u);
+                     make_desc(su + kk * 2 * RG_64, RG_64, 128), idesc_op<CB>(128, 64, true, true), 1u);
         mma_commit(&bars->chain_mma);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
           mma_f16_ss(tmem + r3, make_desc(sp + kk * 256, 128, RG_64), make_desc(su + kk * 2 * RG_64, RG_64, 128),
-                     idesc_bf16(128, 64, false, true), 1u);
+                     idesc_op<CB>(128, 64, false, true), 1u);
         mma_commit(&bars->kq_free[ks]);
         mma_commit(&bars->bt_free[gs]);
       }
@@ -735,9 +802,11 @@ __device__ bool chain_role(const PipeArgs &a, const PipeMaps &maps, uint8_t *sme
   } else if (in_thread) {
     for (int k = v_consumed; k < v_issued; ++k) mbar_wait(&bars->v_full[k & 1], (uint32_t)((k >> 1) & 1), kTimeoutNs);
   }
+  if (CB && over) atomicOr(&bars->range, 1);
   return ok;
 }
 
+template <bool CB>
 __global__ void __launch_bounds__(kThreads, 1) core_pipe_kernel(const __grid_constant__ PipeArgs a,
                                                                  const __grid_constant__ PipeMaps maps) {
   extern __shared__ __align__(1024) uint8_t smem[];
@@ -762,6 +831,7 @@ __global__ void __launch_bounds__(kThreads, 1) core_pipe_kernel(const __grid_con
     mbar_init(&bars->out_empty[0], 1);
     mbar_init(&bars->out_empty[1], 1);
     bars->fail = 0;
+    bars->range = 0;
     fence_mbar_init();
   }
   if (warp == 0) {
@@ -776,26 +846,28 @@ __global__ void __launch_bounds__(kThreads, 1) core_pipe_kernel(const __grid_con
 
   bool ok;
   if (tid < kInvBase)
-    ok = phasor_role(a, maps, smem, bars, tmem, b, h, nchunks);
+    ok = phasor_role<CB>(a, maps, smem, bars, tmem, b, h, nchunks);
   else if (tid < kChBase)
-    ok = inverse_role(a, smem, bars, tmem, b, h, nchunks);
+    ok = inverse_role<CB>(a, smem, bars, tmem, b, h, nchunks);
   else
-    ok = chain_role(a, maps, smem, bars, tmem, bh, b, h, nchunks);
+    ok = chain_role<CB>(a, maps, smem, bars, tmem, bh, b, h, nchunks);
   if (!ok) atomicExch(&bars->fail, 1);
 
   tc_fence_before();
   __syncthreads();
   if (tid == 0 && bars->fail) atomicCAS(a.err, 0, DP_ERR_TIMEOUT);
+  if (CB && tid == 0 && bars->range) atomicCAS(a.err, 0, DP_ERR_RANGE);
   if (warp == 0) tmem_dealloc(tmem, TMEM_COLS);
 }
 
 }  // namespace
 
-// The pipelined kernel for dp_core_fwd (real beta) when its tensor maps encode (L >= 64);
+// The pipelined kernel for dp_core_fwd (real beta) and dp_core_cbeta_fwd (cbeta: `beta`
+// holds phi of the complex beta 1 + e^{i phi}) when its tensor maps encode (L >= 64);
 // returns false without launching otherwise (the caller then runs core_fwd_tc).
 bool core_fwd_pipe(const void *tk, const void *tq, const void *v, const void *beta, int beta_dt,
                    const float *state_in, float *out, float *state_out, int B, int H, int L, const SeqStrides *s,
-                   cudaStream_t stream, int *rc) {
+                   cudaStream_t stream, bool cbeta, int *rc) {
   if (L < kC) return false;
   PipeArgs a;
   memset(&a, 0, sizeof(a));
@@ -820,12 +892,13 @@ bool core_fwd_pipe(const void *tk, const void *tq, const void *v, const void *be
       !encode_chunk_map(&maps.v8, &a.dv, v, B, H, L, s[2], 8))
     return false;
   a.out_tma = encode_out_map(&maps.out, &a.dout, out, B, H, L, s[4]) ? 1 : 0;
-  cudaError_t e = cudaFuncSetAttribute(core_pipe_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+  auto kern = cbeta ? core_pipe_kernel<true> : core_pipe_kernel<false>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
   if (e != cudaSuccess) {
     *rc = set_error(DP_ERR_CUDA, std::string("core_pipe smem attr: ") + cudaGetErrorString(e));
     return true;
   }
-  core_pipe_kernel<<<B * H, kThreads, SMEM_BYTES, stream>>>(a, maps);
+  kern<<<B * H, kThreads, SMEM_BYTES, stream>>>(a, maps);
   *rc = check_launch("core_pipe_kernel");
   return true;
 }

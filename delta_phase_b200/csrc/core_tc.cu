@@ -799,17 +799,17 @@ bool core_tc_supported(const void *tk, const void *tq, const void *v, int in_dt,
 
 bool core_fwd_pipe(const void *tk, const void *tq, const void *v, const void *beta, int beta_dt,
                    const float *state_in, float *out, float *state_out, int B, int H, int L, const SeqStrides *s,
-                   cudaStream_t stream, int *rc);
+                   cudaStream_t stream, bool cbeta, int *rc);
 
 // cbeta: `beta` holds phi of the complex beta 1 + e^{i phi} (ComplexBetaDeltaPhaseBlock).
-// Real beta with L >= 64 runs the pipelined kernel of core_pipe.cu; the kernel below takes
-// complex beta and short sequences.
+// L >= 64 runs the pipelined kernel of core_pipe.cu (both modes); the kernel below takes
+// shorter sequences.
 int core_fwd_tc(const void *tk, const void *tq, const void *v, const void *beta, int beta_dt,
                 const float *state_in, float *out, float *state_out, int B, int H, int L,
                 const SeqStrides *s, cudaStream_t stream, bool cbeta) {
-  if (!cbeta) {
+  {
     int rc = DP_OK;
-    if (core_fwd_pipe(tk, tq, v, beta, beta_dt, state_in, out, state_out, B, H, L, s, stream, &rc)) return rc;
+    if (core_fwd_pipe(tk, tq, v, beta, beta_dt, state_in, out, state_out, B, H, L, s, stream, cbeta, &rc)) return rc;
   }
   TcArgs a;
   a.tk = static_cast<const __nv_bfloat16 *>(tk);
