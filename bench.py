@@ -788,7 +788,8 @@ def run_reference(args, world, rank):
 def run_secondary(args, world, rank, local):
     """The other workloads, each a few steps, for the headline line's `secondary` object:
     Laplace (B=4, H=16, L=32768), the Lerp FFN (65536 x 1024), the decode step
-    (B*H = 1024) and the 12-layer LM (prefill 16 x 4096, decode B=16)."""
+    (B*H = 1024), the complex-beta core (the headline shape) and the 12-layer LM (prefill
+    16 x 4096, decode B=16)."""
     import copy
 
     import torch
@@ -799,7 +800,7 @@ def run_secondary(args, world, rank, local):
     keep = ("metric", "value", "unit", "ms_per_step", "higher_is_better", "config", "roofline", "clocks",
             "decode", "gpu_launches")
     for name, fn, steps in (("laplace", run_laplace, 10), ("ffn", run_ffn, 10), ("decode", run_decode, 4),
-                            ("lm", run_lm, 8)):
+                            ("cbeta", run_cbeta, 10), ("lm", run_lm, 8)):
         sub.steps = steps
         sub.seq_len = 32768
         sub.decode_steps = 64
