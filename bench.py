@@ -13,7 +13,8 @@ JSON line.  ``--impl reference`` times the reference's own chunkwise path on the
 cores: its public ``delta_phase_chunkwise_fused`` (torch, float32, no_grad) from the
 unmodified install in ``baseline/_ref``, or, when that install is absent, the numpy port
 of the same path.  On one GPU the headline line also carries a ``secondary`` object with
-the other workloads (Laplace, FFN, decode step, LM prefill and decode), a few steps each.
+the other workloads (Laplace, FFN, decode step, complex-beta core, LM prefill and decode),
+a few steps each.
 """
 from __future__ import annotations
 
