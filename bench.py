@@ -145,6 +145,10 @@ def dist_setup(n_gpus):
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
+        # the process group as torch sees it (stderr; NCCL's own INIT lines come with it)
+        print(f"bench.py: process group backend={dist.get_backend()} rank={dist.get_rank()} "
+              f"world_size={dist.get_world_size()} device=cuda:{local} "
+              f"nccl={'.'.join(str(x) for x in torch.cuda.nccl.version())}", file=sys.stderr, flush=True)
     return world, rank, local
 
 
