@@ -146,9 +146,13 @@ def dist_setup(n_gpus):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
         # the process group as torch sees it (stderr; NCCL's own INIT lines come with it)
+        try:
+            v = torch.cuda.nccl.version()
+            nccl_v = ".".join(str(x) for x in v) if isinstance(v, (tuple, list)) else str(v)
+        except Exception:  # the report must not stop the benchmark
+            nccl_v = "unknown"
         print(f"bench.py: process group backend={dist.get_backend()} rank={dist.get_rank()} "
-              f"world_size={dist.get_world_size()} device=cuda:{local} "
-              f"nccl={'.'.join(str(x) for x in torch.cuda.nccl.version())}", file=sys.stderr, flush=True)
+              f"world_size={dist.get_world_size()} device=cuda:{local} nccl={nccl_v}", file=sys.stderr, flush=True)
     return world, rank, local
 
 
