@@ -246,7 +246,8 @@ __device__ __forceinline__ void issue_v_loads(const PipeMaps &m, const PipeArgs 
 template <bool CB>
 __device__ __noinline__ void pipe_store_out(const PipeArgs &a, const PipeMaps &maps, uint8_t *smem, PipeBars *bars,
                                             uint32_t taddr, int t, int hc, bool lead, int cc, int h, int b) {
-  const float inv64 = CB ? 1.0f : 1.0f / 64.0f;  // complex beta: the accumulator holds O already
+  // real beta: the accumulator holds 64 O; complex beta: O (its tiles carry the 1 / 64)
+  const float scale = CB ? 1.0f : 1.0f / 64.0f;
   const int tt = cc * kC + t;
   float o[32];
   tmem_ld32_sync(taddr, o);
@@ -259,7 +260,7 @@ __device__ __noinline__ void pipe_store_out(const PipeArgs &a, const PipeMaps &m
 #pragma unroll
     for (int i = 0; i < 8; ++i)
       *reinterpret_cast<float4 *>(orow + ((i ^ (t & 7)) << 4)) =
-          make_float4(o[4 * i] * inv64, o[4 * i + 1] * inv64, o[4 * i + 2] * inv64, o[4 * i + 3] * inv64);
+          make_float4(o[4 * i] * scale, o[4 * i + 1] * scale, o[4 * i + 2] * scale, o[4 * i + 3] * scale);
     fence_proxy_async_smem();
     group_sync(BAR_OUT, 128);
     if (lead) {
@@ -272,7 +273,7 @@ __device__ __noinline__ void pipe_store_out(const PipeArgs &a, const PipeMaps &m
 #pragma unroll
     for (int i = 0; i < 32; i += 4)
       *reinterpret_cast<float4 *>(orow + i) =
-          make_float4(o[i] * inv64, o[i + 1] * inv64, o[i + 2] * inv64, o[i + 3] * inv64);
+          make_float4(o[i] * scale, o[i + 1] * scale, o[i + 2] * scale, o[i + 3] * scale);
   }
 }
 
