@@ -25,6 +25,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import threading
 import time
 
@@ -128,23 +129,54 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------ distributed plumbing
+def nccl_debug_env(world, env):
+    """NCCL's communicator set-up lines (nranks, ranks, devices) for a multi-rank run, so a
+    reader can check the communicator spans every GPU of the run.
+
+    A caller that sets NCCL_DEBUG itself keeps its own setting and destination.  Otherwise
+    NCCL logs its INIT lines to a file of this process (NCCL opens the file for writing,
+    which would truncate a log that stderr is redirected to, and its default destination,
+    stdout, carries the result line); echo_nccl_log copies them to stderr once the
+    communicator exists.  NCCL reads these variables when it initialises, so they are set
+    before torch is imported.  Returns the file's path, or None when nothing was set."""
+    if world <= 1 or "NCCL_DEBUG" in env:
+        return None
+    path = os.path.join(tempfile.gettempdir(), f"bench_nccl_{os.getpid()}.log")
+    env["NCCL_DEBUG"] = "INFO"
+    env.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+    env["NCCL_DEBUG_FILE"] = path
+    return path
+
+
+def echo_nccl_log(path, out):
+    """Copy NCCL's log file (nccl_debug_env) to `out` and remove it; NCCL keeps writing its
+    later lines (tear-down) to the unlinked file."""
+    if path is None:
+        return
+    try:
+        with open(path, "r", errors="replace") as f:
+            text = f.read()
+        os.unlink(path)
+    except OSError:  # no log written: the report line below still names the process group
+        return
+    if text:
+        out.write(text if text.endswith("\n") else text + "\n")
+        out.flush()
+
+
 def dist_setup(n_gpus):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    if world > 1:
-        # NCCL's communicator set-up lines (nranks, ranks, devices) go to stderr, so a reader
-        # can check the communicator spans every GPU of the run.  NCCL reads these once, when
-        # it first initialises, so they are set before torch (and NCCL) are imported.
-        os.environ.setdefault("NCCL_DEBUG", "INFO")
-        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
-        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
+    nccl_log = nccl_debug_env(world, os.environ)
     import torch
     if world > 1:
         import torch.distributed as dist
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
+        dist.barrier()  # the communicator exists on every rank: its set-up lines are written
+        echo_nccl_log(nccl_log, sys.stderr)
         # the process group as torch sees it (stderr; NCCL's own INIT lines come with it)
         try:
             v = torch.cuda.nccl.version()
